@@ -1,0 +1,325 @@
+"""Benchmark of the B200 hot path of wan-dit-lab's Wan-5B DiT block forward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload linear]
+
+Workload "linear" (the W4A4 QKV linear): X bf16 [1392, 3072] N(0,1) with 1% outlier
+channels x20, W [9216, 3072] N(0, 0.02) quantized to INT4 groups of 64 with float16 scales; one step = one
+w4a4 linear call (activation quantizer + tcgen05 kind::i8 GEMM) on inputs resident in HBM. Inputs are
+synthetic and seeded (the reference publishes no dataset for this path).
+
+Timing: W warm-up steps, then K timed steps. Every timed step is bracketed by CUDA events on the launching
+stream; between steps (outside the events) a 512 MiB buffer is written to flush the 126 MB L2, so each step
+starts cold. Under torchrun every rank runs its own replica (this path shards into independent streams: no
+collective on the data path); the time is the max over ranks, the value the sum of the ranks' work over it.
+
+One JSON line (rank 0): metric/value/unit, e2e (the same call from pinned host buffers, copies included),
+roofline of the GEMM kernel (algorithmic int ops / its CUDA-event time vs the measured INT8 peak), the CPU
+baseline (the CPU oracle on the host cores, a bounded sample), clocks sampled by nvidia-smi while timing.
+`--impl reference` times the reference arithmetic on the host CPU (the oracle port in oracle/, since the
+reference's own W4A4 kernels are third-party sm_89 CUDA that neither runs on the CPU nor ships in its tree).
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "wan-dit-lab_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "W4A4 GEMM TOPS vs INT8 peak"
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+INT8_NOMINAL_TOPS = 4500.0
+CODES = "e4m3"  # operand code format of the W4A4 GEMM (--codes)
+
+
+def seeded(shape, seed, scale=1.0, outliers=0.0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(*shape, generator=g) * scale
+    if outliers:
+        cols = torch.randperm(shape[-1], generator=g)[: max(1, int(outliers * shape[-1]))]
+        x[..., cols] *= 20
+    return x
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms in a background process while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=lambda: self.lines.extend(self.proc.stdout), daemon=True)
+            self.reader.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+            self.reader.join(timeout=2)
+
+    def summary(self):
+        sm, sm_max, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                sm_max = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": sm_max,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def int8_peak_tops(device):
+    """Dense INT8 peak measured here: cuBLASLt int8 GEMM (torch._int_mm) 8192^3, best of 10. Falls back to 2x the
+    measured bf16 peak of MEASURED_PEAKS.json (B200's dense INT8 rate is twice its BF16 rate)."""
+    try:
+        a = torch.randint(-8, 8, (8192, 8192), dtype=torch.int8, device=device)
+        b = torch.randint(-8, 8, (8192, 8192), dtype=torch.int8, device=device).t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = float("inf")
+        for _ in range(10):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch._int_mm(a, b)
+            e.record()
+            e.synchronize()
+            best = min(best, s.elapsed_time(e) / 1e3)
+        del a, b
+        return 2 * 8192 ** 3 / best / 1e12, "measured here: cuBLASLt int8 GEMM (torch._int_mm) 8192^3, best of 10"
+    except Exception as error:  # noqa: BLE001 - a missing int8 GEMM falls back to the documented ratio
+        peaks = json.loads(PEAKS_FILE.read_text()) if PEAKS_FILE.exists() else {}
+        bf16 = peaks.get("bf16_tflops", 1590.0)
+        return 2 * bf16, f"2 x bf16 peak of MEASURED_PEAKS.json ({type(error).__name__} measuring int8)"
+
+
+def flush_l2(buf):
+    buf.add_(1)
+
+
+def timed_steps(run, steps, flush, stream):
+    """Per-step CUDA-event times (seconds) of `run`, the L2 flushed before each step outside the events."""
+    times = []
+    for _ in range(steps):
+        flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        run()
+        e.record(stream)
+        e.synchronize()
+        times.append(s.elapsed_time(e) / 1e3)
+    return times
+
+
+def linear_workload(device):
+    from wan_dit_lab_b200 import _native
+    from wan_dit_lab_b200.quantization import w4a4
+    M, K, N = 1392, 3072, 9216
+    x = seeded((M, K), 0, outliers=0.01).to(torch.bfloat16)
+    W = seeded((N, K), 1, scale=0.02)
+    parts = w4a4.quantize(W.to(device), rank=0, scale_dtype=torch.float16)
+    layer = w4a4.PreparedW4A4(*(parts[p] for p in w4a4.PARTS), code_format=CODES)
+    xd = x.to(device)
+    lib = _native.lib()
+    work = torch.empty(lib.wdl_w4a4_linear_workspace(M, K), dtype=torch.uint8, device=device)
+    codes = work[: M * K].view(torch.int8)
+    scales = work[(M * K + 255) // 256 * 256:].view(torch.float32)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+    st = _native.stream(device)
+
+    fmt = layer.code_format
+
+    def step():  # the public entry point: quantizer + GEMM (2 kernels)
+        _native.check(lib.wdl_w4a4_linear(xd.data_ptr(), K, M, K, None, _native.F16, layer.codes.data_ptr(),
+                                          layer.scales.data_ptr(), fmt, None, N, y.data_ptr(), N, work.data_ptr(),
+                                          work.numel(), st))
+
+    def gemm_only():  # the dominant kernel alone, on the activation codes the quantizer left in the workspace
+        _native.check(lib.wdl_w4a4_gemm(codes.data_ptr(), scales.data_ptr(), layer.codes.data_ptr(),
+                                         layer.scales.data_ptr(), fmt, None, M, N, K, y.data_ptr(), N, st))
+
+    x_host = x.pin_memory()
+    y_host = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():  # host -> device copy of X, the call, device -> host copy of Y
+        xd.copy_(x_host, non_blocking=True)
+        step()
+        y_host.copy_(y, non_blocking=True)
+
+    ops = 2 * M * N * K
+    return dict(step=step, kernel=gemm_only, e2e=e2e_step, ops=ops, launches_per_step=2,
+                h2d=x.numel() * 2, d2h=M * N * 2,
+                config={"workload": "BASELINE config 1: W4A4 QKV linear X[1392,3072] x W[9216,3072]^T",
+                        "M": M, "N": N, "K": K, "group": 64, "scale_dtype": "float16", "codes": CODES,
+                        "l2": "flushed between steps"},
+                algorithmic={"int_ops_per_launch": ops, "bytes_per_launch": M * K + N * K + M * N * 2 + (K // 64) * (M + N) * 4},
+                cpu=lambda: cpu_linear_sample(x, W), dtype="int4 x int4 -> int32 (int8 tensor cores), fp32 promote")
+
+
+def cpu_linear_sample(x, W, rows=256):
+    """The oracle's W4A4 linear on `rows` tokens of the workload (quantize, exact group partials in fp32 BLAS,
+    scaled sum), single process with all host threads. Returns (seconds, int ops)."""
+    from oracle import w4a4 as ow
+    torch.set_num_threads(os.cpu_count())
+    wq, _, sw = ow.weight(W.numpy(), "float16")
+    xs = x[:rows].float().numpy()
+    t0 = time.perf_counter()
+    ow.linear(xs, wq, sw, None, None, "float16")
+    dt = time.perf_counter() - t0
+    return dt, 2 * rows * W.shape[0] * W.shape[1], f"{rows} of 1392 tokens, full N and K (oracle port, numpy)"
+
+
+WORKLOADS = {"linear": linear_workload}
+
+
+def reference_arm(args, rank, world):
+    """The reference's arithmetic on the host CPU: the oracle port, each step a bounded sample."""
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count())
+    x = seeded((1392, 3072), 0, outliers=0.01).to(torch.bfloat16)
+    W = seeded((9216, 3072), 1, scale=0.02)
+    for _ in range(args.warmup):
+        cpu_linear_sample(x, W, rows=64)
+    times, ops = [], 0
+    for _ in range(args.steps):
+        dt, ops, sample = cpu_linear_sample(x, W, rows=128)
+        times.append(dt)
+    t = statistics.mean(times)
+    value = ops / t / 1e12
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4 x int4 (fp32 emulation)", "data": "synthetic",
+            "config": {"workload": "BASELINE config 1: W4A4 QKV linear X[1392,3072] x W[9216,3072]^T",
+                       "sample": "128 of 1392 tokens per step"},
+            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    parser.add_argument("--workload", default="linear", choices=sorted(WORKLOADS))
+    parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
+    parser.add_argument("--codes", default="e4m3", choices=("e4m3", "int8"),
+                        help="operand code format of the W4A4 GEMM: e4m3 (kind::f8f6f4) or int8 (kind::i8)")
+    args = parser.parse_args()
+    global CODES
+    CODES = args.codes
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    args.warmup = max(args.warmup, 3)
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    wl = WORKLOADS[args.workload](device)
+    stream = torch.cuda.current_stream(device)
+    flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+    flush = lambda: flush_l2(flush_buf)  # noqa: E731
+
+    for _ in range(args.warmup):
+        wl["step"]()
+    torch.cuda.synchronize()
+    peak, peak_source = int8_peak_tops(device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # main timed region: K steps through the public entry point, inputs resident in HBM
+    barrier()
+    with Clocks(local) as clocks:
+        times = timed_steps(wl["step"], args.steps, flush, stream)
+    barrier()
+    step_s = sum(times) / len(times)
+    # dominant kernel alone, same discipline
+    kernel_times = timed_steps(wl["kernel"], args.steps, flush, stream)
+    kernel_s = sum(kernel_times) / len(kernel_times)
+    # end to end from pinned host buffers
+    for _ in range(2):
+        wl["e2e"]()
+    e2e_times = timed_steps(wl["e2e"], args.steps, flush, stream)
+    e2e_s = sum(e2e_times) / len(e2e_times)
+
+    total = torch.tensor([step_s, e2e_s], device=device, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    step_max, e2e_max = total.tolist()
+    ops = wl["ops"]
+    value = world * ops / step_max / 1e12
+    e2e_value = world * ops / e2e_max / 1e12
+    achieved = ops / kernel_s / 1e12
+
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        dt, cpu_ops, sample = wl["cpu"]()
+        cpu = {"value": cpu_ops / dt / 1e12, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_max * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": wl["dtype"] if CODES == "int8" else wl["dtype"].replace("int8 tensor cores", "e4m3-coded integers on fp8 tensor cores, exact"), "data": "synthetic (seeded, BASELINE shapes)",
+            "config": {**wl["config"], "parallelism": f"replicas{world}" if world > 1 else "single"},
+            "e2e": {"value": e2e_value, "unit": "TOPS", "ms_per_step": e2e_max * 1e3,
+                    "h2d_bytes_per_step": wl["h2d"], "d2h_bytes_per_step": wl["d2h"]},
+            "gpu_launches": wl["launches_per_step"] * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "w4a4_gemm_kernel", "achieved": achieved,
+                         "peak": peak, "unit": "TOPS", "frac": achieved / peak, "peak_source": peak_source,
+                         "frac_of_nominal_int8": achieved / INT8_NOMINAL_TOPS, "kernel_ms": kernel_s * 1e3,
+                         "algorithmic": wl["algorithmic"], "traffic": None},
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

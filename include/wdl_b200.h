@@ -1,0 +1,110 @@
+/* wdl_b200.h — C ABI of the B200 (sm_100a) kernels for the Wan-5B DiT block forward of wan-dit-lab.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (cudaStream_t passed as void*),
+ * launches asynchronously on that stream and returns a status: WDL_OK, or a nonzero code whose message
+ * wdl_last_error() returns (per calling thread). Arguments are validated before anything is launched or
+ * written; invalid arguments return WDL_ERR_ARGUMENT and touch no buffer. Outputs and scratch are allocated by
+ * the caller. The functions hold no state between calls apart from the per-device error word that bounded
+ * device-side waits report into (wdl_device_error).
+ *
+ * Dtype codes: WDL_BF16 = 0, WDL_F16 = 1, WDL_F32 = 2.
+ *
+ * Each declaration names the reference interface it replaces, by file:line of the wan-dit-lab repository.
+ */
+#ifndef WDL_B200_H
+#define WDL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WDL_OK 0
+#define WDL_ERR_ARGUMENT 1 /* invalid shape, dtype, stride, alignment or bounds: nothing was launched */
+#define WDL_ERR_UNSUPPORTED 2 /* valid for the reference but outside what this build implements */
+#define WDL_ERR_CUDA 3 /* a CUDA runtime call failed (launch, attribute, tensor map) */
+#define WDL_ERR_DEVICE 4 /* a kernel reported a device-side error (see wdl_device_error) */
+
+#define WDL_BF16 0
+#define WDL_F16 1
+#define WDL_F32 2
+
+/* How the W4A4 GEMM's operands hold their 4-bit integer codes, one code per byte. Both are exact for codes in
+ * [-8, 15]. WDL_CODES_E4M3 (the default of the Python layer) holds the code's value as an FP8 E4M3 number: the
+ * tensor cores (tcgen05 kind::f8f6f4) then leave float32 group partials - exact integers - that need no
+ * conversion before the scale promotion. WDL_CODES_INT8 holds two's complement int8 (tcgen05 kind::i8, int32
+ * partials); signed codes only. */
+#define WDL_CODES_INT8 0
+#define WDL_CODES_E4M3 1
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* wdl_last_error(void);
+
+/* Version string of the library build. */
+const char* wdl_version(void);
+
+/* Synchronises `stream`, then reads and clears the device error word of the current device: *code = 0 when no
+ * kernel gave up a bounded wait since the last call, else the first code recorded. Returns WDL_OK, or
+ * WDL_ERR_DEVICE when *code != 0. No reference counterpart (the reference has no device-side waits). */
+int wdl_device_error(void* stream, uint32_t* code);
+
+/* ---- W4A4 (SVDQuant INT4 weights and activations, groups of 64 input channels) --------------------------- */
+
+/* Quantizes rows of x [M, K] (bf16 or f32, row stride ldx elements) to symmetric INT4 groups of 64 along K:
+ * scale = max(max|x_g|, 1e-8) / 7 in fp32, code = round-half-even(x / scale) clamped to [-8, 7]. With smooth
+ * ([K] bf16, nullable) x is divided by it first, in fp32. Writes codes [M, K] int8 (one code per byte), scales
+ * [K/64, M] f32 holding the scale rounded to scale_dtype (WDL_BF16 or WDL_F16), and optionally the packed
+ * nibbles [M, K/2] (byte j: low nibble = code 2j, high nibble = code 2j+1). K % 64 == 0.
+ * Replaces the activation quantizer of live::w4a4_linear (native/ops/w4a4_ops.cpp:22-29) and, for rows of a
+ * weight, w4a4.int4_groups(R, "max") (src/wan_dit_lab/quantization/w4a4.py:81-100). */
+int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16_t* smooth, int M, int K,
+                           int scale_dtype, int code_format, void* codes, float* scales, uint8_t* packed,
+                           void* stream);
+
+/* Unpacks a packed INT4 weight: qweight [N, K/2] (low nibble = even k, two's complement) and wscales [K/64, N]
+ * (scale_dtype WDL_BF16 or WDL_F16) into codes [N, K] (one byte each, code_format) and scales [K/64, N] f32,
+ * the device layout of wdl_w4a4_gemm. The load-time counterpart of the packing in w4a4.quantize
+ * (src/wan_dit_lab/quantization/w4a4.py:171-179). */
+int wdl_w4a4_unpack_weight(const uint8_t* qweight, const void* wscales, int scale_dtype, int N, int K,
+                           int code_format, void* codes, float* scales, void* stream);
+
+/* y [M, N] bf16 (row stride ldy) = sum_g a_scales[g, m] * w_scales[g, n] * (sum_{k in g} a[m, k] w[n, k]) + bias[n]
+ * on tcgen05 tensor cores. a [M, K] and w [N, K] codes in code_format (activation codes [-8, 15], weight codes
+ * [-8, 7]), scales f32 ([K/64, M] and [K/64, N]), bias f32 [N] nullable. N % 256 == 0, K % 128 == 0, 16-byte
+ * aligned pointers. The GEMM of live::w4a4_linear (native/ops/w4a4_ops.cpp:36-38). */
+int wdl_w4a4_gemm(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                  const float* bias, int M, int N, int K, uint16_t* y, int64_t ldy, void* stream);
+
+/* Same product, fused with the gated residual update of a Wan block:
+ * out [M, N] f32 = residual[m, n] + float(bf16(product + bias[n])) * gate[n]   (gate nullable: factor 1).
+ * out may alias residual. The residual additions of WanBlock.forward (src/wan_dit_lab/models/block.py:76-79). */
+int wdl_w4a4_gemm_residual(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                           int code_format, const float* bias, const float* gate, const float* residual, int64_t ldr,
+                           int M, int N, int K, float* out, int64_t ldo, void* stream);
+
+/* Debug / parity view of the same GEMM: out [M, N] int32 (row stride ldo) = the exact integer partial
+ * sum_{k in group} a[m, k] w[n, k] of one group of 64 input channels, read from the tensor-core accumulator
+ * (TMEM) as the promotion sees it. No reference counterpart (Nunchaku keeps these in registers); it pins the
+ * integer accumulators bit for bit. */
+int wdl_w4a4_gemm_group_partials(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                                 int code_format, int M, int N, int K, int group, int32_t* out, int64_t ldo,
+                                 void* stream);
+
+/* Bytes of scratch wdl_w4a4_linear needs for M tokens of K channels. */
+size_t wdl_w4a4_linear_workspace(int M, int K);
+
+/* y [M, N] bf16 = x W^T + bias for x [M, K] bf16 (row stride ldx): activation quantization (smooth nullable)
+ * then the W4A4 GEMM, W given as unpacked codes [N, K] (code_format) and scales [K/64, N] f32. workspace:
+ * caller-owned device scratch of wdl_w4a4_linear_workspace(M, K) bytes, 256-byte aligned. live::w4a4_linear
+ * (native/ops/w4a4_ops.cpp:31-40), without the low-rank branch (proj_down / proj_up of rank 0). */
+int wdl_w4a4_linear(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t* smooth, int scale_dtype,
+                    const void* w, const float* w_scales, int code_format, const float* bias, int N, uint16_t* y,
+                    int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WDL_B200_H */

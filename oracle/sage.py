@@ -1,0 +1,128 @@
+"""Oracle of SageAttention over the FP8 KV cache. Test infrastructure only (see oracle/__init__.py).
+
+Reference (src/wan_dit_lab/kernels/sage_kv.py; SageAttention 2.2.0's kernel itself is third-party and absent):
+  - _load :29-40 — tokens [0, at) are cache FP8 x per-(token, head) scale, [at, at + n) the chunk in float32.
+  - _sum_max :44-56 — per (b, h, d) sum of K over all L tokens (mean = sum / L), and max|V|.
+  - _quant_k :60-85 — K - mean to INT8: in a block of 64 tokens, scale g (0..3) covers tokens 8 i + 2 g and
+    8 i + 2 g + 1; scale = max|x| / 127 + 1e-7; q = trunc(x / scale + 0.5 sign(x)) (half away from zero).
+  - V_MAX = 2.25 :24; _quant_v :89-105 — v_scale[d] = max(max|V_d|, 1e-8) / 2.25, V / v_scale to E4M3,
+    transposed to [B, D, H, padded tokens], permuted within 16 tokens as [0,1,8,9,2,3,10,11,4,5,12,13,6,7,14,15].
+  - quant_q :112-124 — Q to INT8: within 32 tokens lane l of 8 holds tokens l, l+8, l+16, l+24 (one scale for
+    the four), padded to blocks of 128; scales [B, H, blocks * 8].
+  - the attention: softmax(q k^T * sq * sk * sm_scale) (v * v_scale), sm_scale = D^-0.5 (sage_kv.py:133),
+    non-causal over cache and chunk (native/ops/sage_ops.cpp:15-16). Exactly computed here over the
+    dequantized operands (float64); subtracting the key mean leaves softmax unchanged.
+"""
+
+import numpy as np
+
+from oracle.fp8 import from_e4m3_bits, to_e4m3_bits
+
+V_MAX = 2.25
+BLKQ, WARPQ, BLKK = 128, 32, 64
+PERM16 = np.array([0, 1, 8, 9, 2, 3, 10, 11, 4, 5, 12, 13, 6, 7, 14, 15])
+
+
+def load(cache, scale, chunk, at):
+    """[B, L, H, D] float32: the cache bytes times their scales before `at`, the chunk after."""
+    c = from_e4m3_bits(cache[:, :at]) * np.asarray(scale[:, :at], np.float32)
+    return np.concatenate([c.astype(np.float32), np.asarray(chunk, np.float32)], axis=1)
+
+
+def trunc_half_away(y):
+    return np.trunc(y + np.where(y >= 0, 0.5, -0.5).astype(np.float32)).astype(np.int8)
+
+
+def quant_k(K):
+    """K [B, L, H, D] float32 -> (k_int8 [B, L, H, D], k_scale [B, H, blocks * 4], mean [B, H, D])."""
+    B, L, H, D = K.shape
+    mean = (K.astype(np.float64).sum(axis=1) / L).astype(np.float32)  # [B, H, D]
+    blocks = -(-L // BLKK)
+    padded = np.zeros((B, blocks * BLKK, H, D), np.float32)
+    padded[:, :L] = K - mean[:, None]
+    x = padded.reshape(B, blocks, 8, 4, 2, H, D)  # token = 64 blk + 8 i + 2 g + j
+    scale = (np.abs(x).max(axis=(2, 4, 6)) / np.float32(127.0) + np.float32(1e-7)).astype(np.float32)  # [B, blk, 4, H]
+    q = trunc_half_away((x / scale[:, :, None, :, None, :, None]).astype(np.float32))
+    q = q.reshape(B, blocks * BLKK, H, D)[:, :L]
+    return q, scale.transpose(0, 3, 1, 2).reshape(B, H, blocks * 4), mean
+
+
+def quant_v(V):
+    """V [B, L, H, D] float32 -> (v_fp8 bytes [B, D, H, padded], v_scale [B, H, D])."""
+    B, L, H, D = V.shape
+    vmax = np.abs(V).max(axis=1)  # [B, H, D]
+    v_scale = (np.maximum(vmax, np.float32(1e-8)) / np.float32(V_MAX)).astype(np.float32)
+    blocks = -(-L // BLKK)
+    padded = blocks * BLKK
+    out = np.zeros((B, D, H, padded), np.uint8)
+    q = to_e4m3_bits((V / v_scale[:, None]).astype(np.float32))  # [B, L, H, D]
+    i = np.arange(L)
+    j = i % 16
+    pair = j // 2
+    to = i - j + (pair % 4) * 4 + (pair // 4) * 2 + j % 2
+    out[:, :, :, to] = q.transpose(0, 3, 2, 1)
+    return out, v_scale
+
+
+def unpermute_v(v_fp8, L):
+    """[B, D, H, padded] Sage layout -> E4M3 bytes [B, L, H, D] in token order."""
+    i = np.arange(L)
+    j = i % 16
+    pair = j // 2
+    to = i - j + (pair % 4) * 4 + (pair // 4) * 2 + j % 2
+    return v_fp8[:, :, :, to].transpose(0, 3, 2, 1)
+
+
+def quant_q(Q):
+    """Q [B, n, H, D] float32 -> (q_int8 [B, n, H, D], q_scale [B, H, blocks * 8])."""
+    B, n, H, D = Q.shape
+    blocks = -(-n // BLKQ) * (BLKQ // WARPQ)
+    x = np.zeros((B, blocks * WARPQ, H, D), np.float32)
+    x[:, :n] = Q
+    x = x.reshape(B, blocks, 4, 8, H, D)
+    scale = (np.abs(x).max(axis=(2, 5), keepdims=True) / np.float32(127.0) + np.float32(1e-7)).astype(np.float32)
+    q = trunc_half_away((x / scale).astype(np.float32)).reshape(B, blocks * WARPQ, H, D)[:, :n]
+    return q, scale.reshape(B, blocks, 8, H).transpose(0, 3, 1, 2).reshape(B, H, blocks * 8)
+
+
+def attention(q, k, v, sm_scale=None):
+    """Exact softmax(q k^T * sm_scale) v per head, float64: q [B, n, H, D], k, v [B, L, H, D]."""
+    q, k, v = (np.asarray(t, np.float64) for t in (q, k, v))
+    sm_scale = q.shape[-1] ** -0.5 if sm_scale is None else sm_scale
+    s = np.einsum("bnhd,blhd->bhnl", q, k) * sm_scale
+    s -= s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    return np.einsum("bhnl,blhd->bnhd", p, v)
+
+
+def sage_attention(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=None):
+    """sage_kv.attend on the dequantized Sage operands: what the INT8 / FP8 kernel approximates, exactly."""
+    Kf = load(cache_k, cache_ks, K, at)
+    Vf = load(cache_v, cache_vs, V, at)
+    kq, ks, _ = quant_k(Kf)
+    v8, vs = quant_v(Vf)
+    qq, qs = quant_q(np.asarray(Q, np.float32))
+    L = Kf.shape[1]
+    kd = dequant_k(kq, ks)
+    qd = dequant_q(qq, qs)
+    vd = from_e4m3_bits(unpermute_v(v8, L)) * vs[:, None]
+    return attention(qd, kd, vd, sm_scale)
+
+
+def dequant_k(kq, ks):
+    B, L, H, D = kq.shape
+    blocks = ks.shape[-1] // 4
+    tok = np.arange(L)
+    g = (tok % 8) // 2
+    idx = (tok // BLKK) * 4 + g  # [L]
+    scale = ks[:, :, idx].transpose(0, 2, 1)  # [B, L, H]
+    return kq.astype(np.float32) * scale[..., None]
+
+
+def dequant_q(qq, qs):
+    B, n, H, D = qq.shape
+    tok = np.arange(n)
+    idx = (tok // WARPQ) * 8 + tok % 8
+    scale = qs[:, :, idx].transpose(0, 2, 1)
+    return qq.astype(np.float32) * scale[..., None]

@@ -1,0 +1,112 @@
+"""Oracle of the W4A4 (SVDQuant INT4) linear: group quantization, nibble packing, exact integer group
+partials and the scaled sum. Test infrastructure only (see oracle/__init__.py).
+
+Reference:
+  - int4_groups(R, "max"): src/wan_dit_lab/quantization/w4a4.py:81-100 — scale = max(amax, 1e-8) / 7 per group
+    of 64, code = round-half-even(R / scale) clamped to [-8, 7].
+  - the stored scale dtype: w4a4.py:174 (bfloat16; BASELINE config 1 states float16).
+  - live::w4a4_linear: native/ops/w4a4_ops.cpp:22-40 — quantize the activation per token per 64-group,
+    then y = sum_g sx * sw * (int partial) + bias (Nunchaku gemm_w4a4, third-party, restated here from
+    SVDQuant's published algorithm: per-group INT4 x INT4 -> INT32, promoted with both group scales).
+  - smoothing: the kernel divides x by smooth before quantizing (w4a4.py:9-11, :177).
+  - gelu_mlp: w4a4.py:195-204 — hidden = GELU_tanh(x W1^T + b1) + 0.171875 quantized unsigned [0, 15].
+"""
+
+import numpy as np
+import torch
+
+GROUP = 64
+GELU_SHIFT = 0.171875
+
+
+def round_to(x, dtype):
+    """float32 array rounded to bfloat16 / float16 (round to nearest even) and back to float32."""
+    t = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    return t.to(getattr(torch, dtype)).float().numpy()
+
+
+def int4_groups(x, smooth=None, unsigned=False):
+    """Rows of x [M, K] float32 in INT4 groups of 64 (w4a4.py:86-100): codes int8 [M, K], fp32 scales [M, K/64].
+    smooth [K]: x / smooth first (fp32). unsigned: codes in [0, 15] with scale = max / 15 (the hidden layer of
+    gelu_mlp, whose input is GELU + 0.171875 >= 0)."""
+    x = np.asarray(x, dtype=np.float32)
+    if smooth is not None:
+        x = (x / np.asarray(smooth, dtype=np.float32)[None, :]).astype(np.float32)
+    M, K = x.shape
+    g = x.reshape(M, K // GROUP, GROUP)
+    top = np.maximum(np.abs(g).max(axis=-1), np.float32(1e-8))
+    scale = (top / np.float32(15.0 if unsigned else 7.0)).astype(np.float32)
+    q = np.rint(g / scale[..., None]).astype(np.float32)
+    q = np.clip(q, 0, 15) if unsigned else np.clip(q, -8, 7)
+    return q.astype(np.int8).reshape(M, K), scale
+
+
+def pack_nibbles(codes):
+    """codes [M, K] in [-8, 7] -> uint8 [M, K/2]: byte j holds code 2j in its low nibble, 2j+1 in its high."""
+    c = np.asarray(codes).astype(np.int16) & 0xF
+    return (c[:, 0::2] | (c[:, 1::2] << 4)).astype(np.uint8)
+
+
+def unpack_nibbles(packed):
+    """uint8 [M, K/2] -> signed codes int8 [M, K] (two's complement nibbles)."""
+    p = np.asarray(packed, dtype=np.uint8).astype(np.int16)
+    lo, hi = p & 0xF, p >> 4
+    lo = np.where(lo >= 8, lo - 16, lo)
+    hi = np.where(hi >= 8, hi - 16, hi)
+    out = np.empty((p.shape[0], p.shape[1] * 2), dtype=np.int8)
+    out[:, 0::2], out[:, 1::2] = lo, hi
+    return out
+
+
+def group_partials(xq, wq, groups=None):
+    """Exact integer group partials P[g, m, n] = sum_{k in g} xq[m, k] wq[n, k], as int32. Computed with float32
+    matmuls: every term and every partial sum is an integer of magnitude < 2^24, so float32 is exact."""
+    xq = np.asarray(xq, dtype=np.float32)
+    wq = np.asarray(wq, dtype=np.float32)
+    M, K = xq.shape
+    G = K // GROUP
+    groups = range(G) if groups is None else groups
+    out = []
+    for g in groups:
+        s = slice(g * GROUP, (g + 1) * GROUP)
+        out.append(xq[:, s] @ wq[:, s].T)
+    return np.stack(out).astype(np.int32)
+
+
+def gemm(xq, sx, wq, sw, bias=None, chunk=16):
+    """y [M, N] float32 = sum_g sx[g, m] * sw[g, n] * P_g[m, n] + bias[n], accumulated in float32 over g in order
+    (sx [K/64, M], sw [K/64, N] are the stored, rounded scales)."""
+    xq = np.asarray(xq, dtype=np.float32)
+    wq = np.asarray(wq, dtype=np.float32)
+    M, K = xq.shape
+    N = wq.shape[0]
+    G = K // GROUP
+    y = np.zeros((M, N), dtype=np.float32)
+    for g0 in range(0, G, chunk):
+        gs = list(range(g0, min(G, g0 + chunk)))
+        P = group_partials(xq, wq, gs).astype(np.float32)
+        for i, g in enumerate(gs):
+            y += P[i] * (sx[g][:, None] * sw[g][None, :]).astype(np.float32)
+    if bias is not None:
+        y += np.asarray(bias, dtype=np.float32)[None, :]
+    return y
+
+
+def linear(x_bf16, w_codes, w_scales, bias=None, smooth=None, scale_dtype="bfloat16"):
+    """live::w4a4_linear without a low-rank branch: x [M, K] (bfloat16 values as float32) -> y float32 before the
+    final bfloat16 rounding, plus the activation codes and scales it used."""
+    xq, sx = int4_groups(x_bf16, smooth)
+    sx_stored = round_to(sx, scale_dtype).T.copy()  # [K/64, M]
+    y = gemm(xq, sx_stored, w_codes, w_scales, bias)
+    return y, xq, sx_stored
+
+
+def weight(W, scale_dtype="bfloat16"):
+    """W [N, K] float32 -> codes [N, K] int8, fp32 scales [N, K/64], stored scales [K/64, N] (rounded)."""
+    q, s = int4_groups(W)
+    return q, s, round_to(s, scale_dtype).T.copy()
+
+
+def gelu_tanh(x):
+    x = np.asarray(x, dtype=np.float32)
+    return (0.5 * x * (1.0 + np.tanh(np.float32(0.7978845608028654) * (x + np.float32(0.044715) * x ** 3)))).astype(np.float32)

@@ -1,0 +1,60 @@
+// Internal interface of the W4A4 GEMM and the activation quantizer (not part of the public C-ABI).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace wdl {
+
+// cuTensorMapEncodeTiled, resolved once through the runtime's driver entry point (no link to libcuda).
+bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* base, const cuuint64_t* dims,
+                  const cuuint64_t* strides, const cuuint32_t* box, const cuuint32_t* elem_strides,
+                  CUtensorMapInterleave interleave, CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2,
+                  CUtensorMapFloatOOBfill fill);
+
+namespace w4a4 {
+
+// How the 4-bit integer codes are held, one per byte. Both are exact for codes in [-8, 15]; E4M3 lets the
+// tensor core (kind::f8f6f4) leave float32 group partials that need no conversion before promotion.
+enum CodeFormat : int {
+  kCodesInt8 = 0,  // two's complement int8 (tcgen05 kind::i8, int32 partials)
+  kCodesE4M3 = 1,  // the code's value as an FP8 E4M3 number (tcgen05 kind::f8f6f4, fp32 partials)
+};
+
+enum EpilogueMode : int {
+  kEpiBf16 = 0,         // out bf16 [M, N] = acc + bias
+  kEpiResidualF32 = 1,  // out f32 [M, N] = residual + float(bf16(acc + bias)) * gate (gate optional)
+  kEpiDumpGroup = 2,    // out int32 [M, N] = the raw integer partial of group dump_group (debug / parity)
+};
+
+struct GemmEpilogue {
+  int mode;
+  const float* ascale;    // [K / 64, M] activation group scales
+  const float* bias;      // [N] or null
+  const float* gate;      // [N] or null (kEpiResidualF32)
+  const float* residual;  // [M, ld_res] f32 (kEpiResidualF32)
+  int64_t ld_res;
+  void* out;  // bf16, f32 or int32 per mode, row stride ld_out elements
+  int64_t ld_out;
+  int dump_group;  // kEpiDumpGroup
+};
+
+struct GemmArgs {
+  const int8_t* a;  // [M, lda] activation codes, one per byte
+  int64_t lda;      // bytes between rows of a (multiple of 16)
+  const int8_t* b;  // [N, ldb] weight codes, one per byte
+  int64_t ldb;
+  const float* wscale;  // [K / 64, N] weight group scales
+  int M, N, K;
+  uint32_t a_signed;  // int8 codes: 1 signed, 0 unsigned (the fused MLP's hidden layer)
+  int code_format;    // CodeFormat of both operands
+  GemmEpilogue ep;
+  uint32_t* err;  // device error word
+};
+
+// Validates and launches; returns 0, or a nonzero status with *why set.
+int gemm_launch(const GemmArgs& args, cudaStream_t stream, const char** why);
+
+}  // namespace w4a4
+}  // namespace wdl

@@ -1,0 +1,182 @@
+// INT4 group quantization of rows (activations on every call, weights at load) and the unpacking of packed
+// weights into the one-code-per-byte layout of the W4A4 GEMM.
+//
+// Rule (per row, per group of 64 consecutive columns), as w4a4.int4_groups(R, "max") of the reference
+// (src/wan_dit_lab/quantization/w4a4.py:86-100) states it for weights and BASELINE's config 1 for activations:
+//   scale = max(max|x|, 1e-8) / 7                      fp32, IEEE division
+//   code  = clamp(round_half_even(x / scale), -8, 7)   fp32 IEEE division, then rint
+// and the stored scale is that fp32 scale rounded to the scale dtype (bf16 in the repo's packs, fp16 in
+// BASELINE's config 1), as w4a4.quantize stores it (w4a4.py:174).
+//
+// One warp per row; a lane holds 8 consecutive columns (16-byte loads of bf16), 8 lanes make one group, so a
+// group's max is 3 shuffles. Loads and code stores are 128-bit / 64-bit vector accesses: the kernel is
+// HBM-bound (bytes per row: K * in_size + K + K / 64 * 4, plus K / 2 when packing).
+#include "common.cuh"
+#include "w4a4_quant.h"
+
+namespace wdl {
+namespace w4a4 {
+
+__device__ __forceinline__ float round_scale(float s, int scale_dtype) {
+  return scale_dtype == 1 ? __half2float(__float2half_rn(s)) : __bfloat162float(__float2bfloat16_rn(s));
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+
+// The byte of a code in the GEMM's operand format: two's complement int8, or the code's value as E4M3 (exact for
+// every integer in [-16, 16]).
+template <bool kE4M3>
+__device__ __forceinline__ uint32_t code_byte(int q) {
+  if constexpr (kE4M3)
+    return static_cast<uint32_t>(__nv_cvt_float_to_fp8(static_cast<float>(q), __NV_SATFINITE, __NV_E4M3));
+  else
+    return static_cast<uint32_t>(q) & 0xFFu;
+}
+
+template <typename T, bool kSmooth, bool kPack, bool kE4M3>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ x, int64_t ldx,
+                                                            const __nv_bfloat16* __restrict__ smooth, int M, int K,
+                                                            int scale_dtype, int8_t* __restrict__ codes,
+                                                            float* __restrict__ scales,
+                                                            uint8_t* __restrict__ packed) {
+  const int lane = threadIdx.x & 31;
+  const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (m >= M) return;
+  const T* xr = x + static_cast<int64_t>(m) * ldx;
+  for (int k0 = 0; k0 < K; k0 += 256) {
+    const int k = k0 + lane * 8;
+    const bool valid = k < K;  // K % 64 == 0: a group of 8 lanes is valid or invalid as a whole
+    float v[8];
+    if (valid) {
+      load8<T>(xr + k, v);
+      if (kSmooth) {
+        float s[8];
+        load8<__nv_bfloat16>(smooth + k, s);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fdiv_rn(v[i], s[i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+    if (!valid) continue;
+    const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
+    int q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = max(-8, min(7, __float2int_rn(__fdiv_rn(v[i], scale))));
+    uint2 c;
+    c.x = code_byte<kE4M3>(q[0]) | (code_byte<kE4M3>(q[1]) << 8) | (code_byte<kE4M3>(q[2]) << 16) |
+          (code_byte<kE4M3>(q[3]) << 24);
+    c.y = code_byte<kE4M3>(q[4]) | (code_byte<kE4M3>(q[5]) << 8) | (code_byte<kE4M3>(q[6]) << 16) |
+          (code_byte<kE4M3>(q[7]) << 24);
+    *reinterpret_cast<uint2*>(codes + static_cast<int64_t>(m) * K + k) = c;
+    if (kPack) {
+      uint32_t p = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) p |= static_cast<uint32_t>((q[2 * i] & 0xF) | ((q[2 * i + 1] & 0xF) << 4)) << (8 * i);
+      *reinterpret_cast<uint32_t*>(packed + static_cast<int64_t>(m) * (K / 2) + k / 2) = p;
+    }
+    if ((lane & 7) == 0) scales[static_cast<int64_t>(k / 64) * M + m] = round_scale(scale, scale_dtype);
+  }
+}
+
+// codes [N, K] from qweight [N, K/2]: one thread per 4 packed bytes (8 codes), 32-bit load, 64-bit store.
+template <bool kE4M3>
+__global__ void unpack_codes_kernel(const uint8_t* __restrict__ qweight, int64_t words, int8_t* __restrict__ codes) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= words) return;
+  const uint32_t p = reinterpret_cast<const uint32_t*>(qweight)[i];
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t byte = (p >> (8 * j)) & 0xFFu;
+    const int even = static_cast<int>(byte << 28) >> 28;  // sign-extend the low nibble
+    const int odd = static_cast<int>((byte >> 4) << 28) >> 28;
+    const uint32_t pair = code_byte<kE4M3>(even) | (code_byte<kE4M3>(odd) << 8);
+    if (j < 2)
+      lo |= pair << (16 * j);
+    else
+      hi |= pair << (16 * (j - 2));
+  }
+  reinterpret_cast<uint2*>(codes)[i] = make_uint2(lo, hi);
+}
+
+__global__ void scales_to_f32_kernel(const uint16_t* __restrict__ in, int64_t n, int scale_dtype,
+                                     float* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint16_t b = in[i];
+  out[i] = scale_dtype == 1 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b));
+}
+
+template <typename T, bool kE4M3>
+static void launch_rows(const void* x, int64_t ldx, const uint16_t* smooth, int M, int K, int scale_dtype,
+                        int8_t* codes, float* scales, uint8_t* packed, cudaStream_t stream) {
+  const int threads = 256;
+  const int blocks = (M * 32 + threads - 1) / threads;
+  const T* xt = static_cast<const T*>(x);
+  const __nv_bfloat16* sm = reinterpret_cast<const __nv_bfloat16*>(smooth);
+  auto go = [&](auto kernel) { kernel<<<blocks, threads, 0, stream>>>(xt, ldx, sm, M, K, scale_dtype, codes, scales, packed); };
+  if (smooth) {
+    if (packed) go(quantize_rows_kernel<T, true, true, kE4M3>);
+    else go(quantize_rows_kernel<T, true, false, kE4M3>);
+  } else {
+    if (packed) go(quantize_rows_kernel<T, false, true, kE4M3>);
+    else go(quantize_rows_kernel<T, false, false, kE4M3>);
+  }
+}
+
+void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_t* smooth, int M, int K,
+                          int scale_dtype, int code_format, int8_t* codes, float* scales, uint8_t* packed,
+                          cudaStream_t stream) {
+  if (x_dtype == 2) {
+    if (code_format == 1) launch_rows<float, true>(x, ldx, smooth, M, K, scale_dtype, codes, scales, packed, stream);
+    else launch_rows<float, false>(x, ldx, smooth, M, K, scale_dtype, codes, scales, packed, stream);
+  } else {
+    if (code_format == 1)
+      launch_rows<__nv_bfloat16, true>(x, ldx, smooth, M, K, scale_dtype, codes, scales, packed, stream);
+    else
+      launch_rows<__nv_bfloat16, false>(x, ldx, smooth, M, K, scale_dtype, codes, scales, packed, stream);
+  }
+}
+
+void unpack_weight_launch(const uint8_t* qweight, const uint16_t* wscales, int scale_dtype, int N, int K,
+                          int code_format, int8_t* codes, float* scales, cudaStream_t stream) {
+  const int64_t words = static_cast<int64_t>(N) * K / 8;
+  const unsigned grid = static_cast<unsigned>((words + 255) / 256);
+  if (code_format == 1)
+    unpack_codes_kernel<true><<<grid, 256, 0, stream>>>(qweight, words, codes);
+  else
+    unpack_codes_kernel<false><<<grid, 256, 0, stream>>>(qweight, words, codes);
+  const int64_t ns = static_cast<int64_t>(K / 64) * N;
+  scales_to_f32_kernel<<<static_cast<unsigned>((ns + 255) / 256), 256, 0, stream>>>(wscales, ns, scale_dtype, scales);
+}
+
+}  // namespace w4a4
+}  // namespace wdl

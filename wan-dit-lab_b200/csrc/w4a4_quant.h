@@ -1,0 +1,22 @@
+// Internal interface of the INT4 group quantizer and the weight unpacker.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace wdl {
+namespace w4a4 {
+
+// x_dtype: 0 bf16, 2 f32. Requirements (checked by the caller): K % 64 == 0, ldx * size and x 16-byte aligned,
+// codes 8-byte aligned, packed 4-byte aligned.
+// code_format: 0 int8 two's complement, 1 E4M3 (see CodeFormat in w4a4_gemm.h)
+void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_t* smooth, int M, int K,
+                          int scale_dtype, int code_format, int8_t* codes, float* scales, uint8_t* packed,
+                          cudaStream_t stream);
+
+// N * K % 8 == 0; qweight 4-byte aligned, codes 8-byte aligned.
+void unpack_weight_launch(const uint8_t* qweight, const uint16_t* wscales, int scale_dtype, int N, int K,
+                          int code_format, int8_t* codes, float* scales, cudaStream_t stream);
+
+}  // namespace w4a4
+}  // namespace wdl
