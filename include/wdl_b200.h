@@ -103,6 +103,76 @@ int wdl_w4a4_linear(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t
                     const void* w, const float* w_scales, int code_format, const float* bias, int N, uint16_t* y,
                     int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- 3D RoPE, the FP8 KV cache, the QKV preparation of self-attention ------------------------------------- */
+
+/* Stores K and V [B, N, H, D] (dtypes WDL_BF16 / WDL_F16 / WDL_F32, element strides k_strides[4], v_strides[4],
+ * any positive strides) into rows [at, at + N) of the FP8 caches cache_k, cache_v [B, capacity, H, D] (E4M3,
+ * contiguous) with one float32 scale per (token, head) in cache_ks, cache_vs [B, capacity, H]:
+ * scale = max(max|x|, 1e-12) / 448, byte = round-to-nearest-even(x / scale). Nothing else is written.
+ * kernels/cache_fp8.py:75-105 store_kv_fp8 (arithmetic of quantization/fp8.py:37-41 quantize_rows). */
+int wdl_store_kv_fp8(const void* k, int k_dtype, const int64_t* k_strides, const void* v, int v_dtype,
+                     const int64_t* v_strides, int B, int N, int H, int D, uint8_t* cache_k, float* cache_ks,
+                     uint8_t* cache_v, float* cache_vs, int capacity, int at, void* stream);
+
+/* Rotates x [B, L, H, D] (dtype 0 bf16, 1 f16, 2 f32, 3 f64; element strides x_strides[4]) by 3D RoPE into out
+ * [B, L, H, D] (contiguous, out_dtype). grids [B, 3] host array of (frames, height, width) per sample (B <= 64);
+ * freq [2, positions, D/2] (f32 or f64, element strides freq_strides[3]) the cos / sin table; start: time
+ * position of the first frame. Computed in float32, or float64 when x or freq is float64; tokens past
+ * f h w copied. kernels/rope_triton.py:101-144 rope_apply (forward), models/rope.py:12-31. */
+int wdl_rope_apply(const void* x, int x_dtype, const int64_t* x_strides, int B, int L, int H, int D, const int* grids,
+                   const void* freq, int freq_dtype, const int64_t* freq_strides, int positions, int start, void* out,
+                   int out_dtype, void* stream);
+
+/* The QKV chain of self-attention on a chunk of n tokens, from one read of each row of qkv [n, ld] bf16
+ * (q | k | v, dim = heads x 128 channels each, dim in {1024, 2048, 3072, 4096}): RMSNorm of q and of k over all
+ * dim channels (float32 statistics, rounded to bf16, times the float32 weights norm_q / norm_k), 3D RoPE of both
+ * with the float32 table freq [2, positions, 64] (chunk grid (n / (grid_h grid_w), grid_h, grid_w), time
+ * position start for its first frame), q_out / k_out [n, dim] float32, and, when cache_k is not null, the rotated
+ * K and the raw V stored into the FP8 cache rows [at, at + n) of cache_k / cache_v [capacity, heads, 128] with
+ * their per-(token, head) scales. FusedQKVAttention.forward (quantization/w4a4.py:252-262) with
+ * MultiHeadAttention's norms (models/multi_head_attention.py:28-44) and KVCache.store
+ * (generation/causal.py:177-184). */
+int wdl_qkv_prep(const uint16_t* qkv, int64_t ld, int n, int dim, const float* norm_q, const float* norm_k, float eps,
+                 const float* freq, int positions, int grid_h, int grid_w, int start, float* q_out, float* k_out,
+                 uint8_t* cache_k, float* cache_ks, uint8_t* cache_v, float* cache_vs, int capacity, int at,
+                 void* stream);
+
+/* ---- SageAttention over the FP8 KV cache ----------------------------------------------------------------- */
+/* Layouts of the quantized operands (this library's own; SageAttention's sm89 layouts are kernel-internal):
+ *   q_i8 [H, npad, 128] int8, q_scale [H, npad / 32 * 8] f32      token t: scale (t / 32) * 8 + t % 8
+ *   k_i8 [H, Lpad, 128] int8, k_scale [H, Lpad / 64 * 4] f32      key j:   scale (j / 64) * 4 + (j % 8) / 2
+ *   v_f8 [H, 128, Lpad] e4m3 (keys contiguous), v_scale [H, 128] f32
+ * npad = nq rounded up to 128, Lpad = L = at + n rounded up to 128; padding holds zero codes.
+ * Cache: cache_k / cache_v [capacity, H, 128] e4m3 with scales cache_ks / cache_vs [capacity, H] (batch 1).
+ * Chunk: k [n, ld_k], v [n, ld_v] (k_dtype / v_dtype WDL_F32 or WDL_BF16), head h at column h * 128. */
+
+/* The quantization of SageAttention 2 read straight from the FP8 cache (tokens [0, at)) and the chunk
+ * (tokens [at, at + n)): key mean over all L = at + n keys, K - mean to INT8 with 4 scales per 64 keys
+ * (keys 8 i + 2 g, 8 i + 2 g + 1; scale max|x| / 127 + 1e-7, round half away from zero), V / v_scale to E4M3
+ * with v_scale = max(max|V_d|, 1e-8) / 2.25 per channel, Q [nq, ld_q] float32 to INT8 with one scale per
+ * 4 tokens (l, l + 8, l + 16, l + 24 of 32). work: wdl_sage_prep_workspace(L, H) bytes of scratch.
+ * kernels/sage_kv.py:29-124 (_load, _sum_max, _quant_k, _quant_v, quant_q). */
+size_t wdl_sage_prep_workspace(int L, int H);
+int wdl_sage_prep(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
+                  const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype, int64_t ld_k,
+                  const void* v, int v_dtype, int64_t ld_v, int n, int H, int8_t* q_i8, float* q_scale, int8_t* k_i8,
+                  float* k_scale, uint8_t* v_f8, float* v_scale, void* work, size_t work_bytes, void* stream);
+
+/* out [nq, ld_out] bf16 (head h at column h * 128) = softmax(q k^T * q_scale * k_scale * sm_scale) (v * v_scale)
+ * over all L keys, non-causal, from the quantized operands above: INT8 Q K^T on tcgen05 kind::i8, P = E4M3(448 p)
+ * times FP8 V on kind::f8f6f4, fp32 accumulation in TMEM. live::sage_sm89 (native/ops/sage_ops.cpp:12-19). */
+int wdl_sage_attention(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale,
+                       const uint8_t* v_f8, const float* v_scale, int nq, int L, int H, float sm_scale, uint16_t* out,
+                       int64_t ld_out, void* stream);
+
+/* Both in one call, the quantized operands in the caller's workspace of wdl_sage_attend_workspace(nq, L, H) bytes
+ * (256-byte aligned). sage_kv.attend (kernels/sage_kv.py:127-176) with heads = tokens = None. */
+size_t wdl_sage_attend_workspace(int nq, int L, int H);
+int wdl_sage_attend(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
+                    const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype, int64_t ld_k,
+                    const void* v, int v_dtype, int64_t ld_v, int n, int H, float sm_scale, uint16_t* out,
+                    int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

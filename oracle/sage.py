@@ -89,11 +89,16 @@ def attention(q, k, v, sm_scale=None):
     """Exact softmax(q k^T * sm_scale) v per head, float64: q [B, n, H, D], k, v [B, L, H, D]."""
     q, k, v = (np.asarray(t, np.float64) for t in (q, k, v))
     sm_scale = q.shape[-1] ** -0.5 if sm_scale is None else sm_scale
-    s = np.einsum("bnhd,blhd->bhnl", q, k) * sm_scale
-    s -= s.max(-1, keepdims=True)
-    p = np.exp(s)
-    p /= p.sum(-1, keepdims=True)
-    return np.einsum("bhnl,blhd->bnhd", p, v)
+    B, n, H, D = q.shape
+    out = np.empty((B, n, H, v.shape[-1]))
+    for b in range(B):
+        for h in range(H):
+            s = (q[b, :, h] @ k[b, :, h].T) * sm_scale
+            s -= s.max(-1, keepdims=True)
+            p = np.exp(s)
+            p /= p.sum(-1, keepdims=True)
+            out[b, :, h] = p @ v[b, :, h]
+    return out
 
 
 def sage_attention(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=None):

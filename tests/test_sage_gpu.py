@@ -1,0 +1,88 @@
+"""SageAttention over the FP8 cache on the B200 kernels against the CPU oracle (oracle/sage.py): the quantized
+operands in value space (Q INT8 and scales bitwise; K INT8 within +-1 and its scales to 1e-5, since the key
+mean is a float sum in another order; V FP8 bytes >= 99.9 % equal), and the attention output against exact
+attention over the dequantized operands (cosine >= 0.999, the stated bar) and against exact attention over the
+unquantized keys and values (the reference's test_sage_kv.py:86-98 style)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fp8 as of
+from oracle import sage as osage
+
+pytestmark = pytest.mark.gpu
+
+
+def setup(at, n, nq, H, seed=0, k_dtype=torch.float32):
+    g = torch.Generator().manual_seed(seed)
+    total = at + n + 64
+    ck, cks = of.quantize_rows((torch.randn(1, total, H, 128, generator=g) + 0.5).numpy())
+    cv, cvs = of.quantize_rows((torch.randn(1, total, H, 128, generator=g) * 0.7).numpy())
+    K = (torch.randn(1, n, H, 128, generator=g) + 0.5).to(k_dtype)
+    V = torch.randn(1, n, H, 128, generator=g).to(torch.bfloat16)
+    Q = torch.randn(1, nq, H, 128, generator=g)
+    host = dict(ck=ck, cks=cks, cv=cv, cvs=cvs, K=K.float().numpy(), V=V.float().numpy(), Q=Q.numpy())
+    dev = dict(ck=torch.from_numpy(ck).view(torch.float8_e4m3fn).cuda(), cks=torch.from_numpy(cks).cuda(),
+               cv=torch.from_numpy(cv).view(torch.float8_e4m3fn).cuda(), cvs=torch.from_numpy(cvs).cuda(),
+               K=K.cuda(), V=V.cuda(), Q=Q.cuda())
+    return host, dev
+
+
+def cosine(a, b):
+    a, b = np.asarray(a, np.float64).ravel(), np.asarray(b, np.float64).ravel()
+    return float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
+
+
+@pytest.mark.parametrize("at,n,nq,H", [(200, 150, 150, 2), (0, 300, 300, 1), (4176, 1392, 1392, 24)])
+def test_quantized_operands_match_oracle(at, n, nq, H):
+    from wan_dit_lab_b200.kernels import sage_kv
+    host, d = setup(at, n, nq, H)
+    ops = {k: v.cpu().numpy() for k, v in sage_kv.prepare(d["Q"], d["ck"], d["cks"], d["cv"], d["cvs"], at, d["K"],
+                                                          d["V"]).items()}
+    L = at + n
+    Kf = osage.load(host["ck"], host["cks"], host["K"], at)
+    Vf = osage.load(host["cv"], host["cvs"], host["V"], at)
+    kq, ks, _ = osage.quant_k(Kf)
+    qq, qs = osage.quant_q(host["Q"])
+    v8, vs = osage.quant_v(Vf)
+    # Q: [H, npad, 128] -> [1, nq, H, 128]
+    np.testing.assert_array_equal(ops["q_i8"][:, :nq].transpose(1, 0, 2)[None], qq)
+    np.testing.assert_array_equal(ops["q_scale"][:, :qs.shape[-1]][None], qs)
+    got_k = ops["k_i8"][:, :L].transpose(1, 0, 2)[None].astype(int)
+    assert np.abs(got_k - kq.astype(int)).max() <= 1
+    assert (got_k == kq).mean() > 0.999
+    np.testing.assert_allclose(ops["k_scale"][:, :ks.shape[-1]][None], ks, rtol=1e-5)
+    np.testing.assert_allclose(ops["v_scale"][None], vs, rtol=1e-6)
+    got_v = ops["v_f8"][:, :, :L].transpose(2, 0, 1)[None]  # [1, L, H, 128]
+    assert (got_v == osage.unpermute_v(v8, L)).mean() > 0.999
+    assert not ops["k_i8"][:, L:].any() and not ops["v_f8"][:, :, L:].any()  # zero padding
+
+
+@pytest.mark.parametrize("at,n,nq,H", [(200, 150, 150, 2), (0, 300, 300, 1), (4176, 1392, 1392, 24), (9360, 3120, 3120, 2)])
+def test_attention_matches_oracle(at, n, nq, H):
+    from wan_dit_lab_b200.kernels import sage_kv
+    from wan_dit_lab_b200 import _native
+    host, d = setup(at, n, nq, H, seed=at + n)
+    out = sage_kv.attend(d["Q"], d["ck"], d["cks"], d["cv"], d["cvs"], at, d["K"], d["V"]).float().cpu().numpy()
+    assert _native.device_error() == 0
+    quantized = osage.sage_attention(host["Q"], host["ck"], host["cks"], host["cv"], host["cvs"], at, host["K"], host["V"])
+    exact = osage.attention(host["Q"], osage.load(host["ck"], host["cks"], host["K"], at),
+                            osage.load(host["cv"], host["cvs"], host["V"], at))
+    c_q, c_e = cosine(out, quantized), cosine(out, exact)
+    err = lambda x: float(np.linalg.norm(x - exact) / np.linalg.norm(exact))  # noqa: E731
+    print(f"at {at} n {n}: cos vs dequantized {c_q:.6f}, vs exact {c_e:.6f}; rel err kernel {err(out):.4f}, "
+          f"dequantized oracle {err(quantized):.4f}")
+    assert c_q >= 0.999 and c_e >= 0.999
+    assert err(out) < 1.2 * err(quantized) + 2e-2  # P in FP8 adds its own rounding on top of Q / K / V's
+
+
+def test_attend_rejects_invalid_contracts():
+    from wan_dit_lab_b200.kernels import sage_kv
+    host, d = setup(20, 10, 10, 1)
+    with pytest.raises(ValueError):
+        sage_kv.attend(d["Q"], d["ck"], d["cks"], d["cv"], d["cvs"], 10 ** 6, d["K"], d["V"])
+    with pytest.raises(NotImplementedError):
+        sage_kv.attend(d["Q"], d["ck"], d["cks"], d["cv"], d["cvs"], 20, d["K"], d["V"], heads=torch.zeros(1))
+    with pytest.raises(TypeError):
+        sage_kv.attend(d["Q"], d["ck"].float(), d["cks"], d["cv"], d["cvs"], 20, d["K"], d["V"])

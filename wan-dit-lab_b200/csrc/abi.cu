@@ -2,12 +2,15 @@
 // status codes and per-thread error messages, the per-device error word, and the tensor-map encoder.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
 #include "../../include/wdl_b200.h"
 #include "common.cuh"
 #include "w4a4_gemm.h"
+#include "rope_kv.h"
+#include "sage.h"
 #include "w4a4_quant.h"
 
 namespace {
@@ -158,6 +161,11 @@ static void operands(wdl::w4a4::GemmArgs& g, const void* a, const float* a_scale
                      int code_format, int M, int N, int K) {
   g.a = static_cast<const int8_t*>(a), g.lda = K, g.b = static_cast<const int8_t*>(w), g.ldb = K;
   g.wscale = w_scales, g.M = M, g.N = N, g.K = K, g.a_signed = 1u, g.code_format = code_format;
+  static const int variant = [] {
+    const char* v = getenv("WDL_GEMM_VARIANT");
+    return v ? atoi(v) : 0;
+  }();
+  g.variant = variant;
   g.ep.ascale = a_scales;
 }
 
@@ -220,6 +228,171 @@ int wdl_w4a4_linear(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t
                                   stream);
   if (st != WDL_OK) return st;
   return wdl_w4a4_gemm(codes, scales, w, w_scales, code_format, bias, M, N, K, y, ldy, stream);
+}
+
+int wdl_store_kv_fp8(const void* k, int k_dtype, const int64_t* k_strides, const void* v, int v_dtype,
+                     const int64_t* v_strides, int B, int N, int H, int D, uint8_t* cache_k, float* cache_ks,
+                     uint8_t* cache_v, float* cache_vs, int capacity, int at, void* stream) {
+  if (B < 0 || N < 0 || H < 0 || D < 1) return fail(WDL_ERR_ARGUMENT, "K and V must have matching [B,N,H,D] shapes");
+  for (int dt : {k_dtype, v_dtype})
+    if (dt != WDL_BF16 && dt != WDL_F16 && dt != WDL_F32) return fail(WDL_ERR_ARGUMENT, "K and V must be FP16, BF16 or FP32");
+  if (at < 0 || at + N > capacity) return fail(WDL_ERR_ARGUMENT, "Write exceeds cache bounds");
+  if (!k_strides || !v_strides) return fail(WDL_ERR_ARGUMENT, "strides must not be null");
+  for (int i = 0; i < 4; ++i)
+    if (k_strides[i] < 0 || v_strides[i] < 0) return fail(WDL_ERR_ARGUMENT, "strides must be nonnegative");
+  if (static_cast<int64_t>(B) * N * H == 0) return ok();
+  if (!k || !v || !cache_k || !cache_ks || !cache_v || !cache_vs) return fail(WDL_ERR_ARGUMENT, "null pointer");
+  wdl::ropekv::StoreArgs a{};
+  a.k = k, a.v = v, a.k_dtype = k_dtype, a.v_dtype = v_dtype;
+  for (int i = 0; i < 4; ++i) a.k_strides[i] = k_strides[i], a.v_strides[i] = v_strides[i];
+  a.B = B, a.N = N, a.H = H, a.D = D, a.cache_k = cache_k, a.cache_ks = cache_ks, a.cache_v = cache_v;
+  a.cache_vs = cache_vs, a.capacity = capacity, a.at = at;
+  wdl::ropekv::store_kv_launch(a, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "store_kv_fp8 launch");
+}
+
+int wdl_rope_apply(const void* x, int x_dtype, const int64_t* x_strides, int B, int L, int H, int D, const int* grids,
+                   const void* freq, int freq_dtype, const int64_t* freq_strides, int positions, int start, void* out,
+                   int out_dtype, void* stream) {
+  if (x_dtype < 0 || x_dtype > 3 || out_dtype < 0 || out_dtype > 3)
+    return fail(WDL_ERR_ARGUMENT, "Floating input and output dtypes required");
+  if (freq_dtype != WDL_F32 && freq_dtype != 3) return fail(WDL_ERR_ARGUMENT, "Floating input and real FP32/FP64 frequencies required");
+  if (B < 1 || L < 0 || H < 0 || D < 2 || D % 2) return fail(WDL_ERR_ARGUMENT, "Input must be (batch, token, heads, even dim)");
+  if (B > 64) return fail(WDL_ERR_ARGUMENT, "at most 64 samples per call");
+  if (start < 0) return fail(WDL_ERR_ARGUMENT, "start_frame must be a nonnegative integer");
+  if (!grids || !x_strides || !freq_strides) return fail(WDL_ERR_ARGUMENT, "null metadata");
+  const int spatial = (D / 2) / 3;
+  for (int b = 0; b < B; ++b) {
+    const int f = grids[3 * b], h = grids[3 * b + 1], w = grids[3 * b + 2];
+    if (f < 0 || h <= 0 || w <= 0 || static_cast<int64_t>(f) * h * w > L)
+      return fail(WDL_ERR_ARGUMENT, "Grid exceeds sequence length or has invalid dimensions");
+    if (start + f > positions || (spatial && (h > positions || w > positions)))
+      return fail(WDL_ERR_ARGUMENT, "Grid or offset exceeds frequency bounds");
+  }
+  if (static_cast<int64_t>(L) * H == 0) return ok();
+  if (!x || !freq || !out) return fail(WDL_ERR_ARGUMENT, "null pointer");
+  wdl::ropekv::RopeArgs a{};
+  a.x = x, a.x_dtype = x_dtype, a.B = B, a.L = L, a.H = H, a.D = D, a.freq = freq, a.freq_dtype = freq_dtype;
+  for (int i = 0; i < 4; ++i) a.x_strides[i] = x_strides[i];
+  for (int i = 0; i < 3; ++i) a.f_strides[i] = freq_strides[i];
+  for (int i = 0; i < 3 * B; ++i) a.grids[i] = grids[i];
+  a.start = start, a.out = out, a.out_dtype = out_dtype;
+  wdl::ropekv::rope_launch(a, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "rope launch");
+}
+
+int wdl_qkv_prep(const uint16_t* qkv, int64_t ld, int n, int dim, const float* norm_q, const float* norm_k, float eps,
+                 const float* freq, int positions, int grid_h, int grid_w, int start, float* q_out, float* k_out,
+                 uint8_t* cache_k, float* cache_ks, uint8_t* cache_v, float* cache_vs, int capacity, int at,
+                 void* stream) {
+  if (dim != 1024 && dim != 2048 && dim != 3072 && dim != 4096)
+    return fail(WDL_ERR_ARGUMENT, "dim must be 1024, 2048, 3072 or 4096 (heads of 128)");
+  if (n < 0 || ld < 3 * dim || (ld * 2) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "qkv rows must hold 3 dim channels, 16-byte aligned");
+  if (grid_h <= 0 || grid_w <= 0 || n % (grid_h * grid_w) != 0)
+    return fail(WDL_ERR_ARGUMENT, "n must be a whole number of frames of grid_h x grid_w tokens");
+  if (start < 0 || start + n / (grid_h * grid_w) > positions || grid_h > positions || grid_w > positions)
+    return fail(WDL_ERR_ARGUMENT, "Grid or offset exceeds frequency bounds");
+  if (cache_k && (at < 0 || at + n > capacity)) return fail(WDL_ERR_ARGUMENT, "Write exceeds cache bounds");
+  if (n == 0) return ok();
+  if (!qkv || !norm_q || !norm_k || !freq || !q_out || !k_out) return fail(WDL_ERR_ARGUMENT, "null pointer");
+  if (cache_k && (!cache_ks || !cache_v || !cache_vs)) return fail(WDL_ERR_ARGUMENT, "null cache pointer");
+  if (!aligned(qkv, 16) || !aligned(q_out, 16) || !aligned(k_out, 16) || (cache_k && (!aligned(cache_k, 8) || !aligned(cache_v, 8))))
+    return fail(WDL_ERR_ARGUMENT, "misaligned pointer");
+  wdl::ropekv::QkvPrepArgs a{};
+  a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv), a.ld_qkv = ld, a.n = n, a.dim = dim, a.norm_q = norm_q;
+  a.norm_k = norm_k, a.eps = eps, a.freq = freq, a.freq_table_stride = static_cast<int64_t>(positions) * 64;
+  a.freq_positions_stride = 64, a.grid_h = grid_h, a.grid_w = grid_w, a.start = start, a.q_out = q_out;
+  a.k_out = k_out, a.cache_k = cache_k, a.cache_ks = cache_ks, a.cache_v = cache_v, a.cache_vs = cache_vs, a.at = at;
+  wdl::ropekv::qkv_prep_launch(a, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "qkv_prep launch");
+}
+
+size_t wdl_sage_prep_workspace(int L, int H) {
+  if (L <= 0 || H <= 0) return 0;
+  return wdl::sage::prep_workspace_floats(L, H) * sizeof(float);
+}
+
+static size_t pad128(int x) { return (static_cast<size_t>(x) + 127) / 128 * 128; }
+static size_t up256(size_t x) { return (x + 255) / 256 * 256; }
+
+int wdl_sage_prep(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
+                  const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype, int64_t ld_k,
+                  const void* v, int v_dtype, int64_t ld_v, int n, int H, int8_t* q_i8, float* q_scale, int8_t* k_i8,
+                  float* k_scale, uint8_t* v_f8, float* v_scale, void* work, size_t work_bytes, void* stream) {
+  if (nq <= 0 || n < 0 || at < 0 || H <= 0 || at + n <= 0) return fail(WDL_ERR_ARGUMENT, "nq, H and L = at + n must be positive");
+  if ((k_dtype != WDL_F32 && k_dtype != WDL_BF16) || (v_dtype != WDL_F32 && v_dtype != WDL_BF16))
+    return fail(WDL_ERR_ARGUMENT, "chunk K and V must be float32 or bf16");
+  if (ld_q < static_cast<int64_t>(H) * 128 || (n > 0 && (ld_k < static_cast<int64_t>(H) * 128 || ld_v < static_cast<int64_t>(H) * 128)))
+    return fail(WDL_ERR_ARGUMENT, "row strides must hold H x 128 channels");
+  if (at > 0 && (!cache_k || !cache_ks || !cache_v || !cache_vs)) return fail(WDL_ERR_ARGUMENT, "null cache pointer");
+  if (!q || (n > 0 && (!k || !v)) || !q_i8 || !q_scale || !k_i8 || !k_scale || !v_f8 || !v_scale)
+    return fail(WDL_ERR_ARGUMENT, "null pointer");
+  if (!work || work_bytes < wdl_sage_prep_workspace(at + n, H))
+    return fail(WDL_ERR_ARGUMENT, "workspace of %zu bytes required", wdl_sage_prep_workspace(at + n, H));
+  if (!aligned(q_i8, 16) || !aligned(k_i8, 16) || !aligned(v_f8, 16)) return fail(WDL_ERR_ARGUMENT, "misaligned output");
+  wdl::sage::PrepArgs a{};
+  a.cache_k = cache_k, a.cache_ks = cache_ks, a.cache_v = cache_v, a.cache_vs = cache_vs, a.at = at;
+  a.k_chunk = k, a.ld_k = ld_k, a.k_bf16 = k_dtype == WDL_BF16, a.v_chunk = v, a.ld_v = ld_v, a.v_bf16 = v_dtype == WDL_BF16;
+  a.n = n, a.H = H, a.q = q, a.ld_q = ld_q, a.nq = nq, a.q_i8 = q_i8, a.q_scale = q_scale, a.k_i8 = k_i8;
+  a.k_scale = k_scale, a.v_f8 = v_f8, a.v_scale = v_scale, a.work = static_cast<float*>(work);
+  wdl::sage::prep_launch(a, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "sage prep launch");
+}
+
+int wdl_sage_attention(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale,
+                       const uint8_t* v_f8, const float* v_scale, int nq, int L, int H, float sm_scale, uint16_t* out,
+                       int64_t ld_out, void* stream) {
+  if (nq <= 0 || L <= 0 || H <= 0) return fail(WDL_ERR_ARGUMENT, "nq, L and H must be positive");
+  if (ld_out < static_cast<int64_t>(H) * 128 || (ld_out * 2) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ld_out must hold H x 128 channels, 16-byte rows");
+  if (!q_i8 || !q_scale || !k_i8 || !k_scale || !v_f8 || !v_scale || !out) return fail(WDL_ERR_ARGUMENT, "null pointer");
+  if (!aligned(q_i8, 16) || !aligned(k_i8, 16) || !aligned(v_f8, 16) || !aligned(out, 16))
+    return fail(WDL_ERR_ARGUMENT, "misaligned pointer");
+  uint32_t* err = error_word();
+  if (!err) return fail(WDL_ERR_CUDA, "cannot resolve the device error word");
+  wdl::sage::AttnArgs a{};
+  a.q_i8 = q_i8, a.q_scale = q_scale, a.k_i8 = k_i8, a.k_scale = k_scale, a.v_f8 = v_f8, a.v_scale = v_scale;
+  a.nq = nq, a.L = L, a.H = H, a.sm_scale_log2 = sm_scale * 1.4426950408889634f;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out), a.ld_out = ld_out;
+  const char* why = "";
+  const int st = wdl::sage::attn_launch(a, err, static_cast<cudaStream_t>(stream), &why);
+  if (st != 0) return fail(WDL_ERR_CUDA, "%s", why);
+  return ok();
+}
+
+size_t wdl_sage_attend_workspace(int nq, int L, int H) {
+  if (nq <= 0 || L <= 0 || H <= 0) return 0;
+  const size_t np = pad128(nq), lp = pad128(L), h = static_cast<size_t>(H);
+  return up256(h * np * 128) + up256(h * np / 32 * 8 * 4) + up256(h * lp * 128) + up256(h * lp / 64 * 4 * 4) +
+         up256(h * 128 * lp) + up256(h * 128 * 4) + up256(wdl_sage_prep_workspace(L, H));
+}
+
+int wdl_sage_attend(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
+                    const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype, int64_t ld_k,
+                    const void* v, int v_dtype, int64_t ld_v, int n, int H, float sm_scale, uint16_t* out,
+                    int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream) {
+  const int L = at + n;
+  if (nq <= 0 || L <= 0 || H <= 0) return fail(WDL_ERR_ARGUMENT, "nq, H and L = at + n must be positive");
+  const size_t need = wdl_sage_attend_workspace(nq, L, H);
+  if (!workspace || workspace_bytes < need) return fail(WDL_ERR_ARGUMENT, "workspace of %zu bytes required", need);
+  if (!aligned(workspace, 256)) return fail(WDL_ERR_ARGUMENT, "workspace must be 256-byte aligned");
+  const size_t np = pad128(nq), lp = pad128(L), h = static_cast<size_t>(H);
+  char* p = static_cast<char*>(workspace);
+  int8_t* q_i8 = reinterpret_cast<int8_t*>(p);
+  p += up256(h * np * 128);
+  float* q_scale = reinterpret_cast<float*>(p);
+  p += up256(h * np / 32 * 8 * 4);
+  int8_t* k_i8 = reinterpret_cast<int8_t*>(p);
+  p += up256(h * lp * 128);
+  float* k_scale = reinterpret_cast<float*>(p);
+  p += up256(h * lp / 64 * 4 * 4);
+  uint8_t* v_f8 = reinterpret_cast<uint8_t*>(p);
+  p += up256(h * 128 * lp);
+  float* v_scale = reinterpret_cast<float*>(p);
+  p += up256(h * 128 * 4);
+  int st = wdl_sage_prep(q, ld_q, nq, cache_k, cache_ks, cache_v, cache_vs, at, k, k_dtype, ld_k, v, v_dtype, ld_v, n,
+                         H, q_i8, q_scale, k_i8, k_scale, v_f8, v_scale, p, wdl_sage_prep_workspace(L, H), stream);
+  if (st != WDL_OK) return st;
+  return wdl_sage_attention(q_i8, q_scale, k_i8, k_scale, v_f8, v_scale, nq, L, H, sm_scale, out, ld_out, stream);
 }
 
 }  // extern "C"

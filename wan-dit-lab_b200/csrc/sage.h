@@ -1,0 +1,60 @@
+// Internal interface of the SageAttention quantizers (sage.cu) and the attention kernel (sage_attn.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace wdl {
+
+bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* base, const cuuint64_t* dims,
+                  const cuuint64_t* strides, const cuuint32_t* box, const cuuint32_t* elem_strides,
+                  CUtensorMapInterleave interleave, CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2,
+                  CUtensorMapFloatOOBfill fill);
+
+namespace sage {
+
+struct PrepArgs {
+  const uint8_t* cache_k;  // [cap, H, 128] e4m3, tokens [0, at)
+  const float* cache_ks;   // [cap, H]
+  const uint8_t* cache_v;
+  const float* cache_vs;
+  int at;
+  const void* k_chunk;  // [n, ld_k] float32 or bf16 (k_bf16), head h at column h * 128: tokens [at, at + n)
+  int64_t ld_k;
+  int k_bf16;
+  const void* v_chunk;  // [n, ld_v] float32 or bf16 (v_bf16)
+  int64_t ld_v;
+  int v_bf16;
+  int n, H;
+  const float* q;  // [nq, ld_q] float32
+  int64_t ld_q;
+  int nq;
+  int8_t* q_i8;  // [H, npad, 128]
+  float* q_scale;  // [H, npad / 32 * 8]
+  int8_t* k_i8;  // [H, Lpad, 128]
+  float* k_scale;  // [H, Lpad / 64 * 4]
+  uint8_t* v_f8;   // [H, 128, Lpad]
+  float* v_scale;  // [H, 128]
+  float* work;     // prep_workspace_floats(L, H) floats
+};
+void prep_launch(const PrepArgs& a, cudaStream_t s);
+size_t prep_workspace_floats(int L, int H);
+
+struct AttnArgs {
+  const int8_t* q_i8;
+  const float* q_scale;
+  const int8_t* k_i8;
+  const float* k_scale;
+  const uint8_t* v_f8;
+  const float* v_scale;
+  int nq, L, H;
+  float sm_scale_log2;  // sm_scale * log2(e)
+  __nv_bfloat16* out;   // [nq, ld_out] bf16, head h at column h * 128
+  int64_t ld_out;
+};
+int attn_launch(const AttnArgs& a, uint32_t* err, cudaStream_t s, const char** why);
+
+}  // namespace sage
+}  // namespace wdl

@@ -1,0 +1,290 @@
+// SageAttention's attention on sm_100a tensor cores: O = softmax(q k^T * sq * sk * sm_scale) (v * v_scale) for
+// one head and 128 queries per CTA, over all L keys (non-causal: a chunk attends to the cached frames and to
+// itself, native/ops/sage_ops.cpp:15-16 of the reference), in the layouts of sage.cu.
+//
+// Per key tile of 128:
+//   S = Q K^T               tcgen05.mma kind::i8 (int32 in TMEM), M = N = 128, K = 128
+//   softmax                 4 warps, thread = query row: s = S * (q_scale * k_scale * sm_scale * log2 e),
+//                           online max / sum, p = 2^(s - m); P = E4M3(p * 448) into shared memory (the 128-byte
+//                           swizzled K-major layout of an MMA A operand); O rescaled in TMEM when the max grows
+//   O += P V                tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> f32 in TMEM), M = N = K = 128
+// and finally O * v_scale / (448 l) in bf16. The P scale 448 and the per-channel V scale are SageAttention 2's
+// FP8 P V scheme (sage_kv.py:24 V_MAX = 2.25 keeps |V / v_scale| <= 2.25).
+//
+// Warps: 0 TMA producer (Q once, K and V tiles, 2 stages), 1 TMEM owner + MMA issuer, 2-5 softmax (warp w owns
+// TMEM lanes 32 (w % 4) .. +31). TMEM: S in columns 0-127 (int32), O in 128-255 (fp32); 256 columns, two CTAs
+// per SM. The next tile's Q K^T is issued before this tile's P V so it overlaps the softmax.
+#include "common.cuh"
+#include "sage.h"
+
+namespace wdl {
+namespace sage {
+
+constexpr int BQ = 128, BKV = 128, HD = 128;
+constexpr int kAttnThreads = 192;
+constexpr uint32_t kAttnTmemCols = 256;
+constexpr float kPScale = 448.f;
+
+struct __align__(1024) AttnSmem {
+  uint8_t q[BQ * HD];
+  uint8_t k[2][BKV * HD];
+  uint8_t v[2][HD * BKV];
+  uint8_t p[BQ * BKV];
+  uint64_t q_full, kv_full[2], kv_empty[2], s_full, s_empty, p_full, o_done;
+  uint32_t tmem_base;
+};
+constexpr size_t kAttnSmemBytes = sizeof(AttnSmem) + 1024;
+
+__global__ void __launch_bounds__(kAttnThreads, 2)
+    attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                const __grid_constant__ CUtensorMap map_v, AttnArgs a, uint32_t* err) {
+  extern __shared__ uint8_t smem_raw[];
+  AttnSmem& sm = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, h = blockIdx.y;
+  const int T = (a.L + BKV - 1) / BKV;
+  const int npad = (a.nq + BQ - 1) / BQ * BQ, Lpad = T * BKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.kv_full[i], 1);
+      mbar_init(&sm.kv_empty[i], 1);
+    }
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.s_empty, 4);
+    mbar_init(&sm.p_full, 4);
+    mbar_init(&sm.o_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, kAttnTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t t_s = tmem, t_o = tmem + BKV;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensor_map(&map_q);
+      prefetch_tensor_map(&map_k);
+      prefetch_tensor_map(&map_v);
+      mbar_arrive_expect_tx(&sm.q_full, BQ * HD);
+      tma_load_2d(sm.q, &map_q, &sm.q_full, 0, h * npad + qt * BQ);
+      int issued = 0;
+      for (int j = 0; j < T; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&sm.kv_empty[st], ((j >> 1) & 1) ^ 1, err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&sm.kv_full[st], 2 * BKV * HD);
+        tma_load_2d(sm.k[st], &map_k, &sm.kv_full[st], 0, h * Lpad + j * BKV);
+        tma_load_2d(sm.v[st], &map_v, &sm.kv_full[st], j * BKV, h * HD);
+        issued = j + 1;
+      }
+      mbar_wait(&sm.q_full, 0, err, kErrWaitFull);
+      for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
+        mbar_wait(&sm.kv_full[j & 1], (j >> 1) & 1, err, kErrWaitFull);
+    }
+  } else if (warp == 1) {
+    const uint32_t id_qk = make_idesc(2, 1, 1, BQ, BKV);  // s8 x s8 -> s32
+    const uint32_t id_pv = make_idesc(1, 0, 0, BQ, HD);   // e4m3 x e4m3 -> f32
+    const uint32_t q0 = smem_u32(sm.q), p0 = smem_u32(sm.p);
+    bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.q_full, 0, err, kErrWaitFull)) &&
+              __all_sync(0xFFFFFFFFu, mbar_wait(&sm.kv_full[0], 0, err, kErrWaitFull));
+    if (ok) {
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t k0 = smem_u32(sm.k[0]);
+#pragma unroll
+        for (int kk = 0; kk < HD / 32; ++kk)
+          mma_i8(t_s, smem_desc_k128(q0 + kk * 32), smem_desc_k128(k0 + kk * 32), id_qk, kk > 0);
+        tc_commit(&sm.s_full);
+      }
+      __syncwarp();
+    }
+    for (int j = 0; j < T && ok; ++j) {
+      if (j + 1 < T) {
+        const int st = (j + 1) & 1;
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.kv_full[st], ((j + 1) >> 1) & 1, err, kErrWaitFull)) &&
+             __all_sync(0xFFFFFFFFu, mbar_wait(&sm.s_empty, j & 1, err, kErrWaitAccEmpty));
+        if (!ok) break;
+        tc_fence_after();
+        if (elect_one()) {
+          const uint32_t k0 = smem_u32(sm.k[st]);
+#pragma unroll
+          for (int kk = 0; kk < HD / 32; ++kk)
+            mma_i8(t_s, smem_desc_k128(q0 + kk * 32), smem_desc_k128(k0 + kk * 32), id_qk, kk > 0);
+          tc_commit(&sm.s_full);
+        }
+        __syncwarp();
+      }
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.p_full, j & 1, err, kErrWaitAccFull));
+      if (!ok) break;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t v0 = smem_u32(sm.v[j & 1]);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 32; ++kk)
+          mma_f8(t_o, smem_desc_k128(p0 + kk * 32), smem_desc_k128(v0 + kk * 32), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&sm.o_done);
+        tc_commit(&sm.kv_empty[j & 1]);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ---------------- softmax: thread = query row ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int t = qt * BQ + row;  // query token
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const float qs = a.q_scale[static_cast<int64_t>(h) * (npad / 32) * 8 + (t / 32) * 8 + (t % 8)];
+    const float c = qs * a.sm_scale_log2;
+    const float* ks_head = a.k_scale + static_cast<int64_t>(h) * (Lpad / 64) * 4;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    uint8_t* prow = sm.p + (row >> 3) * 1024 + (row & 7) * 128;
+    for (int j = 0; j < T; ++j) {
+      float w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = c * __ldg(ks_head + j * 8 + i);
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.s_full, j & 1, err, kErrWaitAccFull));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t s[4][32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tmem_ld32(t_s + lane_off + q * 32, s[q]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.s_empty);
+      float f[128];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = q * 32 + i;
+          f[col] = static_cast<float>(static_cast<int32_t>(s[q][i])) * w[(col / 64) * 4 + (col % 8) / 2];
+        }
+      const int lim = a.L - j * BKV;
+      if (lim < BKV) {
+#pragma unroll
+        for (int col = 0; col < 128; ++col)
+          if (col >= lim) f[col] = -INFINITY;
+      }
+#pragma unroll
+      for (int col = 0; col < 128; ++col) mx = fmaxf(mx, f[col]);
+      const float m_new = fmaxf(m, mx);
+      const float alpha = ex2(m - m_new);
+      float sum = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int col = 0; col < 128; col += 4) {
+        const float p0 = ex2(f[col] - m_new), p1 = ex2(f[col + 1] - m_new);
+        const float p2 = ex2(f[col + 2] - m_new), p3 = ex2(f[col + 3] - m_new);
+        sum += (p0 + p1) + (p2 + p3);
+        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(p0 * kPScale, p1 * kPScale), __NV_SATFINITE, __NV_E4M3);
+        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(p2 * kPScale, p3 * kPScale), __NV_SATFINITE, __NV_E4M3);
+        pk[col / 4] = lo | (hi << 16);
+      }
+      l = l * alpha + sum;
+      if (j > 0) {
+        // P V of the previous tile must be done: O is then stable and the P buffer free
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.o_done, (j - 1) & 1, err, kErrWaitAccFull));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xFFFFFFFFu, m_new > m)) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t o[32];
+            tmem_ld32(t_o + lane_off + q * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(t_o + lane_off + q * 32, o);
+          }
+          tmem_st_wait();
+        }
+      }
+#pragma unroll
+      for (int chunk = 0; chunk < 8; ++chunk)
+        *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) =
+            make_uint4(pk[chunk * 4], pk[chunk * 4 + 1], pk[chunk * 4 + 2], pk[chunk * 4 + 3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full);
+      m = m_new;
+    }
+    if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.o_done, (T - 1) & 1, err, kErrWaitAccFull));
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.f / (kPScale * l);
+      const float* vsc = a.v_scale + h * HD;
+      __nv_bfloat16* out = a.out + static_cast<int64_t>(t) * a.ld_out + h * HD;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t o[32];
+        tmem_ld32(t_o + lane_off + q * 32, o);
+        tmem_ld_wait();
+        if (t < a.nq) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint32_t wv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int d = q * 32 + i + 2 * e;
+              const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o[i + 2 * e]) * __ldg(vsc + d) * inv,
+                                                              __uint_as_float(o[i + 2 * e + 1]) * __ldg(vsc + d + 1) * inv);
+              wv[e] = *reinterpret_cast<const uint32_t*>(&b2);
+            }
+            *reinterpret_cast<uint4*>(out + q * 32 + i) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kAttnTmemCols);
+  }
+}
+
+static bool map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+int attn_launch(const AttnArgs& a, uint32_t* err, cudaStream_t s, const char** why) {
+  const int npad = (a.nq + BQ - 1) / BQ * BQ, Lpad = (a.L + BKV - 1) / BKV * BKV;
+  CUtensorMap mq, mk, mv;
+  if (!map_2d(&mq, a.q_i8, HD, static_cast<uint64_t>(a.H) * npad, HD) ||
+      !map_2d(&mk, a.k_i8, HD, static_cast<uint64_t>(a.H) * Lpad, HD) ||
+      !map_2d(&mv, a.v_f8, Lpad, static_cast<uint64_t>(a.H) * HD, Lpad)) {
+    *why = "cuTensorMapEncodeTiled rejected an attention operand";
+    return 2;
+  }
+  cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kAttnSmemBytes));
+  if (e == cudaSuccess) {
+    attn_kernel<<<dim3(npad / BQ, a.H), kAttnThreads, kAttnSmemBytes, s>>>(mq, mk, mv, a, err);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return 3;
+  }
+  return 0;
+}
+
+}  // namespace sage
+}  // namespace wdl

@@ -63,22 +63,35 @@ __device__ __forceinline__ float4 lds128(uint32_t addr) {
   return v;
 }
 
-// acc += P * (sx * w) for two adjacent columns at once (packed f32x2 multiply and fused multiply-add). P is
-// the group partial as the tensor core left it: fp32 bits (E4M3-coded operands) or int32 (int8 codes).
-template <bool kFp8>
-__device__ __forceinline__ void promote2(uint64_t& acc, uint32_t p0, uint32_t p1, float w0, float w1, uint64_t sx2) {
-  uint64_t p;
-  if constexpr (kFp8) {
-    asm("mov.b64 %0, {%1, %2};" : "=l"(p) : "r"(p0), "r"(p1));
-  } else {
-    p = pack2(static_cast<float>(static_cast<int32_t>(p0)), static_cast<float>(static_cast<int32_t>(p1)));
-  }
-  uint64_t sc;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(sc) : "l"(sx2), "l"(pack2(w0, w1)));
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(p), "l"(sc));
+__device__ __forceinline__ float partial(uint32_t p, bool fp8) {
+  return fp8 ? __uint_as_float(p) : static_cast<float>(static_cast<int32_t>(p));
 }
 
-template <int kMode, bool kFp8>
+// acc += P * (sx * w) for two adjacent columns. P is the group partial as the tensor core left it: fp32 bits
+// (E4M3-coded operands) or int32 (int8 codes). kPacked: one f32x2 multiply and one f32x2 fused multiply-add
+// for the pair; else two scalar multiplies and two scalar FMAs (same roundings either way).
+template <bool kFp8, bool kPacked>
+__device__ __forceinline__ void promote2(uint64_t& acc, uint32_t p0, uint32_t p1, float w0, float w1, uint64_t sx2) {
+  if constexpr (kPacked) {
+    uint64_t p;
+    if constexpr (kFp8) {
+      asm("mov.b64 %0, {%1, %2};" : "=l"(p) : "r"(p0), "r"(p1));
+    } else {
+      p = pack2(partial(p0, false), partial(p1, false));
+    }
+    uint64_t sc;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(sc) : "l"(sx2), "l"(pack2(w0, w1)));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(p), "l"(sc));
+  } else {
+    const float sx = unpack2(sx2).x;
+    float2 a = unpack2(acc);
+    a.x = fmaf(partial(p0, kFp8), __fmul_rn(sx, w0), a.x);
+    a.y = fmaf(partial(p1, kFp8), __fmul_rn(sx, w1), a.y);
+    acc = pack2(a.x, a.y);
+  }
+}
+
+template <int kMode, bool kFp8, bool kPacked>
 __global__ void __launch_bounds__(kThreads, 1)
     w4a4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      const __grid_constant__ CUtensorMap map_ws, GemmEpilogue ep, int M, int N, int K,
@@ -118,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem_base;
 
   if (warp < 4) {
-    setmaxnreg_dec<40>();
+    setmaxnreg_dec<56>();
     if (warp == 0 && lane == 0) {
       // ---------------- TMA producer ----------------
       int issued = 0;
@@ -177,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&sm.mma_done, 0, err, kErrWaitAccFull);
     }
   } else {
-    setmaxnreg_inc<232>();
+    setmaxnreg_inc<224>();
     // ---------------- promotion + epilogue ----------------
     const int q = warp & 3, h = (warp - 4) >> 2;
     const int row = q * 32 + lane;
@@ -204,13 +217,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
       }
       const uint32_t ws = smem_u32(&sm.ws[s][sub][h * 128]);
+      const uint32_t t_buf = t_row + b * BN;
+      // Drain the group's 128 columns in 4 chunks of 32, loading chunk c + 1 while chunk c is promoted.
+      uint32_t ra[32], rb[32];
+      tmem_ld32(t_buf, ra);
+      tmem_ld_wait(ra);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(t_row + b * BN + half * 64, r0);
-        tmem_ld32(t_row + b * BN + half * 64 + 32, r1);
-        tmem_ld_wait();
-        if (half == 1) {
+      for (int c = 0; c < 4; ++c) {
+        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+        if (c < 3) tmem_ld32(t_buf + (c + 1) * 32, nxt);
+        if (c == 3) {  // every column of this buffer is in registers: the MMA may overwrite it
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
@@ -218,23 +235,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (kMode == kEpiDumpGroup) {
           if (g == ep.dump_group && row_ok) {
             int32_t* o = reinterpret_cast<int32_t*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n_tile * BN +
-                         h * 128 + half * 64;
+                         h * 128 + c * 32;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              o[j] = kFp8 ? __float2int_rn(__uint_as_float(r0[j])) : static_cast<int32_t>(r0[j]);
-              o[32 + j] = kFp8 ? __float2int_rn(__uint_as_float(r1[j])) : static_cast<int32_t>(r1[j]);
-            }
+            for (int j = 0; j < 32; ++j) o[j] = kFp8 ? __float2int_rn(__uint_as_float(cur[j])) : static_cast<int32_t>(cur[j]);
           }
         }
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
-          const float4 w0 = lds128(ws + (half * 64 + j) * 4);
-          const float4 w1 = lds128(ws + (half * 64 + 32 + j) * 4);
-          promote2<kFp8>(acc2[(half * 64 + j) / 2], r0[j], r0[j + 1], w0.x, w0.y, sx2);
-          promote2<kFp8>(acc2[(half * 64 + j) / 2 + 1], r0[j + 2], r0[j + 3], w0.z, w0.w, sx2);
-          promote2<kFp8>(acc2[(half * 64 + 32 + j) / 2], r1[j], r1[j + 1], w1.x, w1.y, sx2);
-          promote2<kFp8>(acc2[(half * 64 + 32 + j) / 2 + 1], r1[j + 2], r1[j + 3], w1.z, w1.w, sx2);
+          const float4 w = lds128(ws + (c * 32 + j) * 4);
+          promote2<kFp8, kPacked>(acc2[(c * 32 + j) / 2], cur[j], cur[j + 1], w.x, w.y, sx2);
+          promote2<kFp8, kPacked>(acc2[(c * 32 + j) / 2 + 1], cur[j + 2], cur[j + 3], w.z, w.w, sx2);
         }
+        if (c < 3) tmem_ld_wait(nxt);
       }
       if (sub == GPS - 1) {
         __syncwarp();
@@ -342,13 +354,21 @@ int gemm_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
     if (e == cudaSuccess) kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mw, a.ep, a.M, a.N, a.K, a.a_signed, a.err);
   };
   const bool fp8 = a.code_format == kCodesE4M3;
-  switch (a.ep.mode * 2 + (fp8 ? 1 : 0)) {
-    case kEpiBf16 * 2: launch(w4a4_gemm_kernel<kEpiBf16, false>); break;
-    case kEpiBf16 * 2 + 1: launch(w4a4_gemm_kernel<kEpiBf16, true>); break;
-    case kEpiResidualF32 * 2: launch(w4a4_gemm_kernel<kEpiResidualF32, false>); break;
-    case kEpiResidualF32 * 2 + 1: launch(w4a4_gemm_kernel<kEpiResidualF32, true>); break;
-    case kEpiDumpGroup * 2: launch(w4a4_gemm_kernel<kEpiDumpGroup, false>); break;
-    case kEpiDumpGroup * 2 + 1: launch(w4a4_gemm_kernel<kEpiDumpGroup, true>); break;
+  const bool packed = a.variant == 1;
+  switch (a.ep.mode * 4 + (fp8 ? 2 : 0) + (packed ? 1 : 0)) {
+#define WDL_GEMM_CASE(MODE, FP8, PACKED) \
+  case MODE * 4 + (FP8 ? 2 : 0) + (PACKED ? 1 : 0): launch(w4a4_gemm_kernel<MODE, FP8, PACKED>); break;
+    WDL_GEMM_CASE(kEpiBf16, false, false)
+    WDL_GEMM_CASE(kEpiBf16, false, true)
+    WDL_GEMM_CASE(kEpiBf16, true, false)
+    WDL_GEMM_CASE(kEpiBf16, true, true)
+    WDL_GEMM_CASE(kEpiResidualF32, false, false)
+    WDL_GEMM_CASE(kEpiResidualF32, false, true)
+    WDL_GEMM_CASE(kEpiResidualF32, true, false)
+    WDL_GEMM_CASE(kEpiResidualF32, true, true)
+    WDL_GEMM_CASE(kEpiDumpGroup, false, false)
+    WDL_GEMM_CASE(kEpiDumpGroup, true, false)
+#undef WDL_GEMM_CASE
     default: *why = "unknown epilogue mode"; return 1;
   }
   if (e == cudaSuccess) e = cudaGetLastError();

@@ -49,6 +49,7 @@ struct GemmArgs {
   int M, N, K;
   uint32_t a_signed;  // int8 codes: 1 signed, 0 unsigned (the fused MLP's hidden layer)
   int code_format;    // CodeFormat of both operands
+  int variant;        // promotion arithmetic: 0 scalar fp32, 1 packed f32x2 (same roundings)
   GemmEpilogue ep;
   uint32_t* err;  // device error word
 };
