@@ -92,6 +92,17 @@ int wdl_w4a4_gemm_group_partials(const void* a, const float* a_scales, const voi
                                  int code_format, int M, int N, int K, int group, int32_t* out, int64_t ldo,
                                  void* stream);
 
+/* The first layer of the fused feed forward (Nunchaku's fused_gelu_mlp, live::w4a4_gelu_mlp of
+ * native/ops/w4a4_ops.cpp:44-63; quantization/w4a4.py:195-204): the same product plus bias, then
+ * u = GELU_tanh(y) + shift (shift 0.171875 = GELU_SHIFT makes u >= 0), divided by the next layer's smoothing
+ * smooth_next ([N] bf16, nullable), quantized to UNSIGNED INT4 per group of 64 outputs (scale = max(max u, 1e-8)
+ * / 15, code = round-half-even(u / scale) in [0, 15]) straight into the next layer's operand: codes [M, ldc]
+ * (E4M3 format) and scales [N / 64, M] f32 rounded to scale_dtype. The hidden layer never exists in 16 bits.
+ * code_format must be WDL_CODES_E4M3. */
+int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                          const float* bias, const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N,
+                          int K, uint8_t* codes, int64_t ldc, float* scales, void* stream);
+
 /* Bytes of scratch wdl_w4a4_linear needs for M tokens of K channels. */
 size_t wdl_w4a4_linear_workspace(int M, int K);
 
@@ -137,6 +148,27 @@ int wdl_qkv_prep(const uint16_t* qkv, int64_t ld, int n, int dim, const float* n
                  uint8_t* cache_k, float* cache_ks, uint8_t* cache_v, float* cache_vs, int capacity, int at,
                  void* stream);
 
+/* ---- normalizations of the block, fused with what consumes them ------------------------------------------- */
+
+/* LayerNorm of x [M, K] (x_dtype WDL_F32 or WDL_BF16, row stride ldx; K % 256 == 0, K <= 4096) over K channels
+ * (float32 statistics, eps; ln_w / ln_b [K] float32 affine, nullable), rounded to bf16 when round_ln_bf16 (the
+ * residual stream is bf16: .type_as), then when mod_shift is not null y * (1 + mod_scale) + mod_shift (float32
+ * [K] each), then rounded to bf16 (the next linear layer's input) and quantized as wdl_w4a4_quantize_rows does
+ * (smooth [K] bf16 nullable): codes [M, K] (code_format), scales [K / 64, M] (scale_dtype).
+ * models/block.py:75-79 norm1 / norm2 (modulated) and norm3 (affine) feeding quantization/w4a4.py:229-231. */
+int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float eps, const float* ln_w,
+                 const float* ln_b, int round_ln_bf16, const float* mod_shift, const float* mod_scale,
+                 const uint16_t* smooth, int scale_dtype, int code_format, void* codes, float* scales, void* stream);
+
+/* RMSNorm of rows: out [M, ldo] f32 = bf16(x * rsqrt(mean(x^2) + eps)) * w for x [M, ldx] bf16 (K % 256 == 0,
+ * K <= 4096). models/rms_norm.py:10-13 (the query norm of cross-attention, models/multi_head_attention.py:118). */
+int wdl_rms_rows(const uint16_t* x, int64_t ldx, int M, int K, const float* w, float eps, float* out, int64_t ldo,
+                 void* stream);
+
+/* out [blocks, 6, dim] f32 = time_in [6, dim] + modulation [blocks, 6, dim]: the (time_in + self.modulation)
+ * of every block of a model at once (models/block.py:75). */
+int wdl_modulation(const float* time_in, const float* modulation, int blocks, int dim, float* out, void* stream);
+
 /* ---- SageAttention over the FP8 KV cache ----------------------------------------------------------------- */
 /* Layouts of the quantized operands (this library's own; SageAttention's sm89 layouts are kernel-internal):
  *   q_i8 [H, npad, 128] int8, q_scale [H, npad / 32 * 8] f32      token t: scale (t / 32) * 8 + t % 8
@@ -164,6 +196,14 @@ int wdl_sage_prep(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, 
 int wdl_sage_attention(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale,
                        const uint8_t* v_f8, const float* v_scale, int nq, int L, int H, float sm_scale, uint16_t* out,
                        int64_t ld_out, void* stream);
+
+/* The K / V half of wdl_sage_prep alone (the keys and values of cross-attention are quantized once per prompt:
+ * at = 0, the prompt's n tokens as the chunk), and the Q half alone. */
+int wdl_sage_prep_kv(const uint8_t* cache_k, const float* cache_ks, const uint8_t* cache_v, const float* cache_vs,
+                     int at, const void* k, int k_dtype, int64_t ld_k, const void* v, int v_dtype, int64_t ld_v, int n,
+                     int H, int8_t* k_i8, float* k_scale, uint8_t* v_f8, float* v_scale, void* work, size_t work_bytes,
+                     void* stream);
+int wdl_sage_quant_q(const float* q, int64_t ld_q, int nq, int H, int8_t* q_i8, float* q_scale, void* stream);
 
 /* Both in one call, the quantized operands in the caller's workspace of wdl_sage_attend_workspace(nq, L, H) bytes
  * (256-byte aligned). sage_kv.attend (kernels/sage_kv.py:127-176) with heads = tokens = None. */

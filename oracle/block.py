@@ -1,0 +1,94 @@
+"""Oracle of one Wan block forward with W4A4 linears and SageAttention over the FP8 cache. Test infrastructure
+only (see oracle/__init__.py).
+
+Reference: src/wan_dit_lab/models/block.py:22-29 (WanBlock.forward), models/multi_head_attention.py:28-44,
+quantization/w4a4.py:248-262 (FusedQKVAttention), :195-204 (gelu_mlp: GELU + 0.171875, unsigned INT4 hidden),
+generation/causal.py:177-220 (KVCache.store / attend with Sage), models/rope.py, models/rms_norm.py,
+models/layer_norm.py. Every linear follows oracle.w4a4.linear on the packed weights given; attention is Sage's
+quantization with P V in FP8 tile by tile (oracle.sage.sage_attention, fp8_p); statistics in float64.
+"""
+
+import numpy as np
+
+from oracle import fp8 as of
+from oracle import rope as orope
+from oracle import sage as osage
+from oracle import w4a4 as ow
+
+GELU_SHIFT = 0.171875
+
+
+def bf16(x):
+    return ow.round_to(np.asarray(x, np.float32), "bfloat16")
+
+
+def layer(parts):
+    """(codes [N, K] int8, stored scales [K/64, N] float32, bias [N] float32) of packed W4A4 parts (numpy)."""
+    codes = ow.unpack_nibbles(parts["qweight"])
+    return codes, parts["wscales"].astype(np.float32), parts["bias"].astype(np.float32)
+
+
+def linear(x_bf16_values, parts, smooth=None, act_scale="bfloat16"):
+    """y float32 = W4A4 linear of x (bf16 values) on the packed parts (before the bf16 rounding of the output)."""
+    codes, ws, b = layer(parts)
+    y, _, _ = ow.linear(x_bf16_values, codes, ws, b, smooth, act_scale)
+    return y
+
+
+def layer_norm(x, eps=1e-6, w=None, b=None):
+    return orope.layer_norm(x, eps, w, b)
+
+
+def block(X, mod, parts, norms, cache, at, freq, grid, start, text, heads, trace=None):
+    """X [n, dim] float32 (updated copy returned), mod [6, dim] float32 (time_in + modulation), parts {layer: packed
+    numpy parts}, norms dict(norm_q, norm_k, cross_norm_q, cross_norm_k, norm3_w, norm3_b), cache: dict(k, ks, v, vs)
+    numpy FP8 buffers [cap, H, 128] / [cap, H, 1] (written in place at `at`), text [T, dim] bf16 values (the
+    prompt after the text embedding)."""
+    X = np.array(X, np.float32, copy=True)
+    n, dim = X.shape
+    keep = (lambda k, v: trace.__setitem__(k, np.array(v, copy=True))) if trace is not None else (lambda k, v: None)
+    sh_a, sc_a, g_a, sh_f, sc_f, g_f = mod
+    # self-attention
+    x1 = bf16((layer_norm(X) * (np.float32(1) + sc_a)).astype(np.float32) + sh_a)
+    keep("x1", x1)
+    qkv = bf16(linear(x1, parts["self_attn.qkv"]))
+    keep("qkv", qkv)
+    q, k, v = qkv[:, :dim], qkv[:, dim:2 * dim], qkv[:, 2 * dim:]
+    frames = n // (grid[1] * grid[2])
+    rot = lambda t: orope.rope_apply(t.reshape(1, n, heads, 128), (frames, grid[1], grid[2]), freq, start)  # noqa: E731
+    Q = rot(orope.rms_norm(q, norms["norm_q"], round_to="bfloat16"))
+    K = rot(orope.rms_norm(k, norms["norm_k"], round_to="bfloat16"))
+    V = v.reshape(1, n, heads, 128)
+    cache["k"][:, at:at + n], cache["ks"][:, at:at + n] = of.quantize_rows(K)
+    cache["v"][:, at:at + n], cache["vs"][:, at:at + n] = of.quantize_rows(V)
+    A = osage.sage_attention(Q, cache["k"], cache["ks"], cache["v"], cache["vs"], at, K, V, fp8_p=True)
+    keep("q", Q.reshape(n, dim)), keep("k", K.reshape(n, dim)), keep("attn", A.reshape(n, dim))
+    o = bf16(linear(bf16(A.reshape(n, dim)), parts["self_attn.o"]))
+    X = (X + o * g_a).astype(np.float32)
+    keep("x_after_self", X)
+    # cross-attention
+    x3 = bf16(layer_norm(X, w=norms["norm3_w"], b=norms["norm3_b"]))
+    cq = bf16(linear(x3, parts["cross_attn.q"]))
+    keep("cq", cq)
+    CQ = orope.rms_norm(cq, norms["cross_norm_q"], round_to="bfloat16").reshape(1, n, heads, 128)
+    T = text.shape[0]
+    ck = orope.rms_norm(bf16(linear(text, parts["cross_attn.k"])), norms["cross_norm_k"], round_to="bfloat16")
+    cv = bf16(linear(text, parts["cross_attn.v"]))
+    empty = np.zeros((1, 0, heads, 128), np.uint8)
+    CA = osage.sage_attention(CQ, empty, np.zeros((1, 0, heads, 1), np.float32), empty,
+                              np.zeros((1, 0, heads, 1), np.float32), 0, ck.reshape(1, T, heads, 128),
+                              cv.reshape(1, T, heads, 128), fp8_p=True)
+    keep("cattn", CA.reshape(n, dim))
+    co = bf16(linear(bf16(CA.reshape(n, dim)), parts["cross_attn.o"]))
+    X = (X + co).astype(np.float32)
+    keep("x_after_cross", X)
+    # feed forward: fc1, GELU + shift quantized unsigned, fc2
+    x2 = bf16((layer_norm(X) * (np.float32(1) + sc_f)).astype(np.float32) + sh_f)
+    h = linear(x2, parts["ffn.0"])
+    u = (ow.gelu_tanh(h) + np.float32(GELU_SHIFT)).astype(np.float32)
+    hq, hs = ow.int4_groups(u, unsigned=True)
+    keep("hcodes", hq), keep("hscales", ow.round_to(hs, "bfloat16").T.copy())
+    codes, ws, b = layer(parts["ffn.2"])
+    f = bf16(ow.gemm(hq, ow.round_to(hs, "bfloat16").T.copy(), codes, ws, b))
+    X = (X + f * g_f).astype(np.float32)
+    return X

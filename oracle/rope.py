@@ -64,7 +64,8 @@ def rope_apply(x, grid, freq, start=0, out_dtype=None):
         t = torch.from_numpy(np.ascontiguousarray(out))
         if work == np.float64 and out_dtype in ("bfloat16", "float16"):
             t = t.float()  # PyTorch casts float64 to 16 bits through float32
-        out = t.to(getattr(torch, out_dtype)).float().numpy()
+        t = t.to(getattr(torch, out_dtype))
+        out = t.numpy() if out_dtype in ("float32", "float64") else t.float().numpy()  # 16-bit values as float32
     return out
 
 

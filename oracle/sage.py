@@ -101,8 +101,39 @@ def attention(q, k, v, sm_scale=None):
     return out
 
 
-def sage_attention(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=None):
-    """sage_kv.attend on the dequantized Sage operands: what the INT8 / FP8 kernel approximates, exactly."""
+def attention_fp8_p(q, k, v_codes, v_scale, sm_scale=None, tile=128, p_scale=448.0):
+    """SageAttention 2's P V in FP8, per head: online softmax over key tiles of `tile` (running max m, sum l, the
+    output rescaled by 2^(m_old - m_new)), each tile's P = E4M3(2^(s - m) * p_scale) times the FP8 V codes
+    (float64 accumulation), the channel scale and 1 / (p_scale l) applied at the end. q, k dequantized
+    [B, n, H, D] / [B, L, H, D]; v_codes [B, L, H, D] the E4M3 values of V / v_scale; v_scale [B, H, D]."""
+    q, k, vc = (np.asarray(t, np.float64) for t in (q, k, v_codes))
+    sm_scale = q.shape[-1] ** -0.5 if sm_scale is None else sm_scale
+    B, n, H, D = q.shape
+    L = k.shape[1]
+    out = np.empty((B, n, H, D))
+    c = sm_scale * np.log2(np.e)
+    for b in range(B):
+        for h in range(H):
+            s = (q[b, :, h] @ k[b, :, h].T) * c
+            m = np.full(n, -np.inf)
+            lsum = np.zeros(n)
+            o = np.zeros((n, D))
+            for j in range(0, L, tile):
+                st = s[:, j:j + tile]
+                m_new = np.maximum(m, st.max(1))
+                alpha = np.exp2(m - m_new)
+                p = np.exp2(st - m_new[:, None])
+                lsum = lsum * alpha + p.sum(1)
+                p8 = from_e4m3_bits(to_e4m3_bits((p * p_scale).astype(np.float32))).astype(np.float64)
+                o = o * alpha[:, None] + p8 @ vc[b, j:j + tile, h]
+                m = m_new
+            out[b, :, h] = o * v_scale[b, h][None, :] / (p_scale * lsum[:, None])
+    return out
+
+
+def sage_attention(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=None, fp8_p=False):
+    """sage_kv.attend on the dequantized Sage operands: what the INT8 / FP8 kernel approximates, exactly; with
+    fp8_p, P V in FP8 tile by tile as the kernel computes it (attention_fp8_p)."""
     Kf = load(cache_k, cache_ks, K, at)
     Vf = load(cache_v, cache_vs, V, at)
     kq, ks, _ = quant_k(Kf)
@@ -111,6 +142,8 @@ def sage_attention(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=N
     L = Kf.shape[1]
     kd = dequant_k(kq, ks)
     qd = dequant_q(qq, qs)
+    if fp8_p:
+        return attention_fp8_p(qd, kd, from_e4m3_bits(unpermute_v(v8, L)), vs, sm_scale)
     vd = from_e4m3_bits(unpermute_v(v8, L)) * vs[:, None]
     return attention(qd, kd, vd, sm_scale)
 

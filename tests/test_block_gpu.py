@@ -1,0 +1,87 @@
+"""One Wan block on the B200 kernels against the oracle block (oracle/block.py) on the same packed W4A4 weights,
+inputs, FP8 cache and prompt: the block's residual update within relative L2 2e-2 (bf16 outputs of every
+linear, FP8 P in the Sage kernel and float32 sums in other orders), the chunk's FP8 cache rows nearly all equal,
+and the W4A4 block stays close to the float block (the reference's style, tests/test_w4a4.py:63-87)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import block as ob
+from oracle import fp8 as of
+from oracle import rope as orope
+
+pytestmark = pytest.mark.gpu
+
+
+def random_state(dim, ffn, seed):
+    g = torch.Generator().manual_seed(seed)
+    r = lambda *s: torch.randn(*s, generator=g) * 0.02  # noqa: E731
+    st = {}
+    for attn in ("self_attn", "cross_attn"):
+        for name in ("q", "k", "v", "o"):
+            st[f"{attn}.{name}.weight"], st[f"{attn}.{name}.bias"] = r(dim, dim), r(dim)
+        st[f"{attn}.norm_q.weight"] = 1 + r(dim) * 5
+        st[f"{attn}.norm_k.weight"] = 1 + r(dim) * 5
+    st["ffn.0.weight"], st["ffn.0.bias"] = r(ffn, dim), r(ffn)
+    st["ffn.2.weight"], st["ffn.2.bias"] = r(dim, ffn), r(dim)
+    st["norm3.weight"], st["norm3.bias"] = 1 + r(dim) * 5, r(dim)
+    st["modulation"] = torch.randn(1, 6, dim, generator=g) / dim ** 0.5
+    return st
+
+
+def numpy_parts(parts):
+    return {k: {p: v.float().cpu().numpy() if v.dtype != torch.uint8 else v.cpu().numpy() for p, v in t.items()}
+            for k, t in parts.items()}
+
+
+@pytest.mark.parametrize("dim,heads,ffn,frames,h,w,at,text", [(1024, 8, 4096, 2, 4, 8, 128, 32),
+                                                               (2048, 16, 4096, 3, 4, 16, 384, 64)])
+def test_block_matches_oracle(dim, heads, ffn, frames, h, w, at, text):
+    from wan_dit_lab_b200.models.block import Buffers, WanBlockB200
+    from wan_dit_lab_b200 import _native
+    n = frames * h * w
+    state = random_state(dim, ffn, 1)
+    blk = WanBlockB200(state, dim, ffn, heads)
+    g = torch.Generator().manual_seed(2)
+    X = torch.randn(n, dim, generator=g)
+    time_in = torch.randn(6, dim, generator=g) * 0.1
+    ctx = (torch.randn(text, dim, generator=g)).to(torch.bfloat16)
+    cap = at + n + 16
+    ck8, cks = of.quantize_rows((torch.randn(1, cap, heads, 128, generator=g) + 0.3).numpy())
+    cv8, cvs = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    freq = orope.table(1024).astype(np.float32)
+    start = at // (h * w)
+    dev = "cuda"
+    cache = (torch.from_numpy(ck8[0]).to(dev), torch.from_numpy(cks[0, ..., 0]).to(dev),
+             torch.from_numpy(cv8[0]).to(dev), torch.from_numpy(cvs[0, ..., 0]).to(dev), cap)
+    buf = Buffers(n, dim, ffn, heads, at + n, text, dev)
+    mod = blk.modulation_of(time_in.to(dev))
+    cross = blk.cross_kv(ctx.to(dev))
+    Xd = X.to(dev)
+    gt = {}
+    blk.forward(Xd, mod, cache, at, torch.from_numpy(freq).to(dev), (frames, h, w), start, cross, buf, trace=gt)
+    assert _native.device_error() == 0
+    got = Xd.cpu().numpy()
+    norms = dict(norm_q=blk.norm_q.cpu().numpy(), norm_k=blk.norm_k.cpu().numpy(),
+                 cross_norm_q=blk.cross_norm_q.cpu().numpy(), cross_norm_k=blk.cross_norm_k.cpu().numpy(),
+                 norm3_w=blk.norm3_w.cpu().numpy(), norm3_b=blk.norm3_b.cpu().numpy())
+    ocache = dict(k=ck8.copy(), ks=cks.copy(), v=cv8.copy(), vs=cvs.copy())
+    ot = {}
+    expected = ob.block(X.numpy(), mod.cpu().numpy(), numpy_parts(blk.parts), norms, ocache, at, freq, (frames, h, w),
+                        start, ctx.float().numpy(), heads, trace=ot)
+    rel = lambda a, b: float(np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(b), 1e-30))  # noqa: E731
+    from oracle import fp8 as of8
+    stages = {"qkv": rel(gt["qkv"].float().cpu().numpy(), ot["qkv"])}
+    for name in ("q", "k", "attn", "x_after_self", "cq", "cattn", "x_after_cross", "hscales"):
+        stages[name] = rel(gt[name].float().cpu().numpy(), ot[name])
+    stages["hcodes"] = rel(of8.from_e4m3_bits(gt["hcodes"].cpu().numpy()), ot["hcodes"].astype(np.float32))
+    print("stages:", {k: round(v, 5) for k, v in stages.items()})
+    d_got, d_exp = got - X.numpy(), expected - X.numpy()
+    err = float(np.linalg.norm(d_got - d_exp) / np.linalg.norm(d_exp))
+    print(f"block dim {dim}: residual update relative L2 vs oracle {err:.4f}")
+    assert err <= 2e-2
+    for name, gpu in (("k", cache[0]), ("v", cache[2])):
+        rows = gpu[at:at + n].cpu().numpy()
+        assert (rows == ocache[name][0, at:at + n]).mean() > 0.99
+    assert not torch.equal(cache[0][:at].cpu(), torch.zeros_like(cache[0][:at].cpu()))

@@ -69,6 +69,9 @@ def test_attention_matches_oracle(at, n, nq, H):
     quantized = osage.sage_attention(host["Q"], host["ck"], host["cks"], host["cv"], host["cvs"], at, host["K"], host["V"])
     exact = osage.attention(host["Q"], osage.load(host["ck"], host["cks"], host["K"], at),
                             osage.load(host["cv"], host["cvs"], host["V"], at))
+    emulated = osage.sage_attention(host["Q"], host["ck"], host["cks"], host["cv"], host["cvs"], at, host["K"], host["V"],
+                                    fp8_p=True)
+    assert float(np.linalg.norm(out - emulated) / np.linalg.norm(emulated)) < 5e-3  # the kernel's own FP8 P V
     c_q, c_e = cosine(out, quantized), cosine(out, exact)
     err = lambda x: float(np.linalg.norm(x - exact) / np.linalg.norm(exact))  # noqa: E731
     print(f"at {at} n {n}: cos vs dequantized {c_q:.6f}, vs exact {c_e:.6f}; rel err kernel {err(out):.4f}, "

@@ -9,6 +9,7 @@
 #include "../../include/wdl_b200.h"
 #include "common.cuh"
 #include "w4a4_gemm.h"
+#include "norm_quant.h"
 #include "rope_kv.h"
 #include "sage.h"
 #include "w4a4_quant.h"
@@ -202,6 +203,21 @@ int wdl_w4a4_gemm_group_partials(const void* a, const float* a_scales, const voi
   return gemm_common(g, stream);
 }
 
+int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                          const float* bias, const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N,
+                          int K, uint8_t* codes, int64_t ldc, float* scales, void* stream) {
+  if (code_format != WDL_CODES_E4M3) return fail(WDL_ERR_ARGUMENT, "the unsigned hidden codes need the E4M3 code format");
+  if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
+  if (ldc < N || ldc % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldc must be >= N and a multiple of 16");
+  if (!scales) return fail(WDL_ERR_ARGUMENT, "null scales");
+  wdl::w4a4::GemmArgs g{};
+  operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
+  g.ep.mode = wdl::w4a4::kEpiGeluU4, g.ep.bias = bias, g.ep.out = codes, g.ep.ld_out = ldc, g.ep.out_scales = scales;
+  g.ep.out_smooth = reinterpret_cast<const __nv_bfloat16*>(smooth_next), g.ep.out_scale_dtype = scale_dtype;
+  g.ep.gelu_shift = shift;
+  return gemm_common(g, stream);
+}
+
 size_t wdl_w4a4_linear_workspace(int M, int K) {
   if (M <= 0 || K <= 0) return 0;
   const size_t codes = (static_cast<size_t>(M) * K + 255) / 256 * 256;
@@ -305,6 +321,76 @@ int wdl_qkv_prep(const uint16_t* qkv, int64_t ld, int n, int dim, const float* n
   a.k_out = k_out, a.cache_k = cache_k, a.cache_ks = cache_ks, a.cache_v = cache_v, a.cache_vs = cache_vs, a.at = at;
   wdl::ropekv::qkv_prep_launch(a, static_cast<cudaStream_t>(stream));
   return cuda_status(cudaGetLastError(), "qkv_prep launch");
+}
+
+int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float eps, const float* ln_w,
+                 const float* ln_b, int round_ln_bf16, const float* mod_shift, const float* mod_scale,
+                 const uint16_t* smooth, int scale_dtype, int code_format, void* codes, float* scales, void* stream) {
+  if (x_dtype != WDL_F32 && x_dtype != WDL_BF16) return fail(WDL_ERR_ARGUMENT, "x must be float32 or bf16");
+  if (K <= 0 || K % 256 != 0 || K > 4096) return fail(WDL_ERR_ARGUMENT, "K must be a multiple of 256, at most 4096");
+  if (M < 0 || ldx < K) return fail(WDL_ERR_ARGUMENT, "M >= 0 and ldx >= K required");
+  if ((ldx * (x_dtype == WDL_F32 ? 4 : 2)) % 16 != 0 || !aligned(x, 16)) return fail(WDL_ERR_ARGUMENT, "x rows must be 16-byte aligned");
+  if ((ln_w == nullptr) != (ln_b == nullptr) || (mod_shift == nullptr) != (mod_scale == nullptr))
+    return fail(WDL_ERR_ARGUMENT, "affine weight / bias and modulation shift / scale come in pairs");
+  if (!valid_codes(code_format) || (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16))
+    return fail(WDL_ERR_ARGUMENT, "invalid code format or scale dtype");
+  if (M == 0) return ok();
+  if (!codes || !scales || !aligned(codes, 8)) return fail(WDL_ERR_ARGUMENT, "null or misaligned output");
+  wdl::norm::LnQuantArgs a{};
+  a.x = x, a.x_f32 = x_dtype == WDL_F32, a.ldx = ldx, a.M = M, a.K = K, a.eps = eps, a.ln_w = ln_w, a.ln_b = ln_b;
+  a.round_ln_bf16 = round_ln_bf16, a.mod_shift = mod_shift, a.mod_scale = mod_scale;
+  a.smooth = reinterpret_cast<const __nv_bfloat16*>(smooth), a.scale_dtype = scale_dtype, a.code_format = code_format;
+  a.codes = static_cast<uint8_t*>(codes), a.scales = scales;
+  wdl::norm::ln_quant_launch(a, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "ln_quant launch");
+}
+
+int wdl_rms_rows(const uint16_t* x, int64_t ldx, int M, int K, const float* w, float eps, float* out, int64_t ldo,
+                 void* stream) {
+  if (K <= 0 || K % 256 != 0 || K > 4096) return fail(WDL_ERR_ARGUMENT, "K must be a multiple of 256, at most 4096");
+  if (M < 0 || ldx < K || ldo < K || (ldx * 2) % 16 != 0 || (ldo * 4) % 16 != 0)
+    return fail(WDL_ERR_ARGUMENT, "row strides must hold K channels, 16-byte aligned");
+  if (M == 0) return ok();
+  if (!x || !w || !out || !aligned(x, 16) || !aligned(out, 16)) return fail(WDL_ERR_ARGUMENT, "null or misaligned pointer");
+  wdl::norm::rms_rows_launch(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, K, w, eps, out, ldo,
+                             static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "rms_rows launch");
+}
+
+int wdl_modulation(const float* time_in, const float* modulation, int blocks, int dim, float* out, void* stream) {
+  if (blocks <= 0 || dim <= 0) return fail(WDL_ERR_ARGUMENT, "blocks and dim must be positive");
+  if (!time_in || !modulation || !out) return fail(WDL_ERR_ARGUMENT, "null pointer");
+  wdl::norm::modulation_launch(time_in, modulation, blocks, dim, out, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "modulation launch");
+}
+
+int wdl_sage_prep_kv(const uint8_t* cache_k, const float* cache_ks, const uint8_t* cache_v, const float* cache_vs,
+                     int at, const void* k, int k_dtype, int64_t ld_k, const void* v, int v_dtype, int64_t ld_v, int n,
+                     int H, int8_t* k_i8, float* k_scale, uint8_t* v_f8, float* v_scale, void* work, size_t work_bytes,
+                     void* stream) {
+  if (n < 0 || at < 0 || H <= 0 || at + n <= 0) return fail(WDL_ERR_ARGUMENT, "H and L = at + n must be positive");
+  if ((k_dtype != WDL_F32 && k_dtype != WDL_BF16) || (v_dtype != WDL_F32 && v_dtype != WDL_BF16))
+    return fail(WDL_ERR_ARGUMENT, "chunk K and V must be float32 or bf16");
+  if (n > 0 && (ld_k < static_cast<int64_t>(H) * 128 || ld_v < static_cast<int64_t>(H) * 128))
+    return fail(WDL_ERR_ARGUMENT, "row strides must hold H x 128 channels");
+  if (at > 0 && (!cache_k || !cache_ks || !cache_v || !cache_vs)) return fail(WDL_ERR_ARGUMENT, "null cache pointer");
+  if ((n > 0 && (!k || !v)) || !k_i8 || !k_scale || !v_f8 || !v_scale) return fail(WDL_ERR_ARGUMENT, "null pointer");
+  if (!work || work_bytes < wdl::sage::prep_workspace_floats(at + n, H) * sizeof(float))
+    return fail(WDL_ERR_ARGUMENT, "workspace too small");
+  wdl::sage::PrepArgs a{};
+  a.cache_k = cache_k, a.cache_ks = cache_ks, a.cache_v = cache_v, a.cache_vs = cache_vs, a.at = at;
+  a.k_chunk = k, a.ld_k = ld_k, a.k_bf16 = k_dtype == WDL_BF16, a.v_chunk = v, a.ld_v = ld_v, a.v_bf16 = v_dtype == WDL_BF16;
+  a.n = n, a.H = H, a.k_i8 = k_i8, a.k_scale = k_scale, a.v_f8 = v_f8, a.v_scale = v_scale;
+  a.work = static_cast<float*>(work);
+  wdl::sage::prep_kv_launch(a, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "sage kv prep launch");
+}
+
+int wdl_sage_quant_q(const float* q, int64_t ld_q, int nq, int H, int8_t* q_i8, float* q_scale, void* stream) {
+  if (nq <= 0 || H <= 0 || ld_q < static_cast<int64_t>(H) * 128) return fail(WDL_ERR_ARGUMENT, "invalid Q shape");
+  if (!q || !q_i8 || !q_scale || !aligned(q_i8, 8)) return fail(WDL_ERR_ARGUMENT, "null or misaligned pointer");
+  wdl::sage::quant_q_launch(q, ld_q, nq, H, q_i8, q_scale, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "sage quant_q launch");
 }
 
 size_t wdl_sage_prep_workspace(int L, int H) {

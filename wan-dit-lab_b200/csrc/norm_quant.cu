@@ -1,0 +1,172 @@
+// The normalizations of a Wan block fused with what consumes them:
+//
+//  * ln_quant — LayerNorm over dim channels (models/layer_norm.py:5-7: float32 statistics, eps 1e-6, optional
+//    affine weight / bias as norm3), its result rounded to the residual stream's dtype when that is bf16
+//    (.type_as(X)), the AdaLN modulation y * (1 + scale) + shift with scale / shift rows of
+//    (time_in + modulation) (models/block.py:75-79, each product and sum rounded in float32), the cast to bf16
+//    of the linear layer that follows (PackedW4A4Linear.forward, quantization/w4a4.py:229-231), then that
+//    layer's activation quantization: division by its smoothing vector and symmetric INT4 groups of 64
+//    (scale = max(max|x|, 1e-8) / 7, round half to even, codes in the GEMM's operand format). One warp per row.
+//  * rms_rows — RMSNorm of rows (models/rms_norm.py:10-13): x * rsqrt(mean(x^2) + eps) rounded to bf16, times
+//    the float32 weight; the query norm of cross-attention (models/multi_head_attention.py:118).
+//  * modulation — (time_in + modulation) of every block at once (models/block.py:75): [blocks, 6, dim] fp32.
+#include "common.cuh"
+#include "norm_quant.h"
+
+namespace wdl {
+namespace norm {
+
+constexpr int kMaxChunks = 16;  // dim <= 16 * 256
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
+  if constexpr (std::is_same<T, float>::value) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x, v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+template <typename TX>
+__global__ void __launch_bounds__(256) ln_quant_kernel(const TX* __restrict__ x, LnQuantArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (m >= a.M) return;
+  const int K = a.K, chunks = K / 256;
+  const TX* row = x + static_cast<int64_t>(m) * a.ldx;
+  float v[kMaxChunks][8];
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+    if (c < chunks) {
+      load8<TX>(row + c * 256 + lane * 8, v[c]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += v[c][i];
+    }
+  const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(K));
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+    if (c < chunks)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[c][i] - mean;
+        ss = fmaf(d, d, ss);
+      }
+  const float rstd = __frsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(ss), static_cast<float>(K)), a.eps));
+  uint8_t* codes = a.codes + static_cast<int64_t>(m) * K;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    if (c >= chunks) break;
+    const int k = c * 256 + lane * 8;
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float t = __fmul_rn(v[c][i] - mean, rstd);
+      if (a.ln_w) t = __fadd_rn(__fmul_rn(t, __ldg(a.ln_w + k + i)), __ldg(a.ln_b + k + i));
+      if (a.round_ln_bf16) t = bf16r(t);
+      if (a.mod_shift) {
+        const float one_plus = __fadd_rn(1.f, __ldg(a.mod_scale + k + i));
+        t = __fadd_rn(__fmul_rn(t, one_plus), __ldg(a.mod_shift + k + i));
+      }
+      t = bf16r(t);  // the linear layer's input is bf16
+      if (a.smooth) t = __fdiv_rn(t, __bfloat162float(a.smooth[k + i]));
+      y[i] = t;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+    const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
+    uint32_t w[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int q = max(-8, min(7, __float2int_rn(__fdiv_rn(y[i], scale))));
+      const uint32_t byte = a.code_format == 1
+                                ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(static_cast<float>(q), __NV_SATFINITE, __NV_E4M3))
+                                : (static_cast<uint32_t>(q) & 0xFFu);
+      w[i / 4] |= byte << (8 * (i % 4));
+    }
+    *reinterpret_cast<uint2*>(codes + k) = make_uint2(w[0], w[1]);
+    if ((lane & 7) == 0)
+      a.scales[static_cast<int64_t>(k / 64) * a.M + m] =
+          a.scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16r(scale);
+  }
+}
+
+void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s) {
+  const unsigned blocks = static_cast<unsigned>((static_cast<int64_t>(a.M) * 32 + 255) / 256);
+  if (a.x_f32)
+    ln_quant_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(a.x), a);
+  else
+    ln_quant_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a);
+}
+
+__global__ void __launch_bounds__(256) rms_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int M, int K,
+                                                       const float* __restrict__ w, float eps, float* __restrict__ out,
+                                                       int64_t ldo) {
+  const int lane = threadIdx.x & 31;
+  const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (m >= M) return;
+  const int chunks = K / 256;
+  const __nv_bfloat16* row = x + static_cast<int64_t>(m) * ldx;
+  float v[kMaxChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+    if (c < chunks) {
+      load8<__nv_bfloat16>(row + c * 256 + lane * 8, v[c]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(v[c][i], v[c][i], ss);
+    }
+  const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(ss), static_cast<float>(K)), eps));
+  float* o = out + static_cast<int64_t>(m) * ldo;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c)
+    if (c < chunks) {
+      const int k = c * 256 + lane * 8;
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(bf16r(__fmul_rn(v[c][i], r)), __ldg(w + k + i));
+      *reinterpret_cast<float4*>(o + k) = make_float4(y[0], y[1], y[2], y[3]);
+      *reinterpret_cast<float4*>(o + k + 4) = make_float4(y[4], y[5], y[6], y[7]);
+    }
+}
+
+void rms_rows_launch(const __nv_bfloat16* x, int64_t ldx, int M, int K, const float* w, float eps, float* out,
+                     int64_t ldo, cudaStream_t s) {
+  const unsigned blocks = static_cast<unsigned>((static_cast<int64_t>(M) * 32 + 255) / 256);
+  rms_rows_kernel<<<blocks, 256, 0, s>>>(x, ldx, M, K, w, eps, out, ldo);
+}
+
+__global__ void modulation_kernel(const float* __restrict__ time_in, const float* __restrict__ modulation, int64_t n,
+                                  int64_t per_block, float* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __fadd_rn(time_in[i % per_block], modulation[i]);
+}
+
+void modulation_launch(const float* time_in, const float* modulation, int blocks, int dim, float* out, cudaStream_t s) {
+  const int64_t n = static_cast<int64_t>(blocks) * 6 * dim;
+  modulation_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(time_in, modulation, n, 6 * dim, out);
+}
+
+}  // namespace norm
+}  // namespace wdl

@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(128) quant_q_kernel(const float* q, int64_t ld
   if (c == 0) q_scale[static_cast<int64_t>(h) * (npad / 32) * 8 + blk * 8 + l] = scale;
 }
 
-void prep_launch(const PrepArgs& a, cudaStream_t s) {
+void prep_kv_launch(const PrepArgs& a, cudaStream_t s) {
   const int L = a.at + a.n;
   Source ks{a.cache_k, a.cache_ks, a.k_chunk, a.ld_k, a.k_bf16, a.at, L, a.H};
   Source vs{a.cache_v, a.cache_vs, a.v_chunk, a.ld_v, a.v_bf16, a.at, L, a.H};
@@ -186,8 +186,16 @@ void prep_launch(const PrepArgs& a, cudaStream_t s) {
   partials_kernel<<<dim3(tiles, a.H), 128, 0, s>>>(ks, vs, ksum, vmax);
   reduce_kernel<<<a.H, 128, 0, s>>>(ksum, vmax, tiles, a.H, L, kmean, a.v_scale);
   quant_kv_kernel<<<dim3(Lpad / 64, a.H), 128, 0, s>>>(ks, vs, kmean, a.v_scale, Lpad, a.k_i8, a.k_scale, a.v_f8);
-  const int npad = (a.nq + 127) / 128 * 128;
-  quant_q_kernel<<<dim3(npad / 32, a.H), 128, 0, s>>>(a.q, a.ld_q, a.nq, npad, a.q_i8, a.q_scale);
+}
+
+void quant_q_launch(const float* q, int64_t ld_q, int nq, int H, int8_t* q_i8, float* q_scale, cudaStream_t s) {
+  const int npad = (nq + 127) / 128 * 128;
+  quant_q_kernel<<<dim3(npad / 32, H), 128, 0, s>>>(q, ld_q, nq, npad, q_i8, q_scale);
+}
+
+void prep_launch(const PrepArgs& a, cudaStream_t s) {
+  prep_kv_launch(a, s);
+  quant_q_launch(a.q, a.ld_q, a.nq, a.H, a.q_i8, a.q_scale, s);
 }
 
 size_t prep_workspace_floats(int L, int H) {

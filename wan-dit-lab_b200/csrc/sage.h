@@ -39,7 +39,9 @@ struct PrepArgs {
   float* v_scale;  // [H, 128]
   float* work;     // prep_workspace_floats(L, H) floats
 };
-void prep_launch(const PrepArgs& a, cudaStream_t s);
+void prep_launch(const PrepArgs& a, cudaStream_t s);     // K / V then Q
+void prep_kv_launch(const PrepArgs& a, cudaStream_t s);  // K / V only (q fields unused)
+void quant_q_launch(const float* q, int64_t ld_q, int nq, int H, int8_t* q_i8, float* q_scale, cudaStream_t s);
 size_t prep_workspace_floats(int L, int H);
 
 struct AttnArgs {

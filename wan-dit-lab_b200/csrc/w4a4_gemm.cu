@@ -45,6 +45,14 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + alignment slack of the 
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// GELU in its tanh form (torch.nn.GELU(approximate="tanh"), the feed forward of models/block.py:8-9):
+// 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))), in float32.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float cube = x * x * x;
+  const float inner = 0.7978845608028654f * (x + 0.044715f * cube);
+  return 0.5f * x * (1.f + tanhf(inner));
+}
+
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
@@ -279,6 +287,43 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk.w = *reinterpret_cast<uint32_t*>(&t3);
           *reinterpret_cast<uint4*>(out + j) = pk;
         }
+      } else if constexpr (kMode == kEpiGeluU4) {
+        // the fused MLP's hidden layer (reference quantization/w4a4.py:195-204, native/ops/w4a4_ops.cpp:44-63):
+        // u = GELU(acc + bias) + shift (>= 0), divided by the next layer's smoothing, quantized unsigned per group
+        // of 64 columns: scale = max(max u, 1e-8) / 15, code = round-half-even(u / scale) clamped to [0, 15]
+        uint8_t* codes = reinterpret_cast<uint8_t*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
+#pragma unroll
+        for (int g2 = 0; g2 < 2; ++g2) {
+          float u[64];
+          float amax = 0.f;
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const int n = n0 + g2 * 64 + j;
+            float t = __fadd_rn(gelu_tanh(acc[g2 * 64 + j] + (ep.bias ? __ldg(ep.bias + n) : 0.f)), ep.gelu_shift);
+            if (ep.out_smooth) t = __fdiv_rn(t, __bfloat162float(ep.out_smooth[n]));
+            u[j] = t;
+            amax = fmaxf(amax, fabsf(t));
+          }
+          const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 15.f);
+#pragma unroll
+          for (int j = 0; j < 64; j += 16) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint32_t word = 0;
+#pragma unroll
+              for (int b = 0; b < 4; ++b) {
+                const int q = max(0, min(15, __float2int_rn(__fdiv_rn(u[j + e * 4 + b], scale))));
+                word |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(static_cast<float>(q), __NV_SATFINITE, __NV_E4M3))
+                        << (8 * b);
+              }
+              w[e] = word;
+            }
+            *reinterpret_cast<uint4*>(codes + g2 * 64 + j) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+          ep.out_scales[static_cast<size_t>((n0 + g2 * 64) / 64) * M + m] =
+              ep.out_scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16_round(scale);
+        }
       } else if constexpr (kMode == kEpiResidualF32) {
         // residual stream update in fp32: x_new = x + float(bf16(acc + bias)) * gate   (gate 1 when absent)
         float* out = reinterpret_cast<float*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
@@ -368,6 +413,8 @@ int gemm_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
     WDL_GEMM_CASE(kEpiResidualF32, true, true)
     WDL_GEMM_CASE(kEpiDumpGroup, false, false)
     WDL_GEMM_CASE(kEpiDumpGroup, true, false)
+    WDL_GEMM_CASE(kEpiGeluU4, true, false)
+    WDL_GEMM_CASE(kEpiGeluU4, true, true)
 #undef WDL_GEMM_CASE
     default: *why = "unknown epilogue mode"; return 1;
   }

@@ -26,6 +26,7 @@ enum EpilogueMode : int {
   kEpiBf16 = 0,         // out bf16 [M, N] = acc + bias
   kEpiResidualF32 = 1,  // out f32 [M, N] = residual + float(bf16(acc + bias)) * gate (gate optional)
   kEpiDumpGroup = 2,    // out int32 [M, N] = the raw integer partial of group dump_group (debug / parity)
+  kEpiGeluU4 = 3,       // out codes [M, N] (E4M3) + out_scales [N / 64, M]: unsigned INT4 of GELU(acc + bias) + shift
 };
 
 struct GemmEpilogue {
@@ -38,6 +39,10 @@ struct GemmEpilogue {
   void* out;  // bf16, f32 or int32 per mode, row stride ld_out elements
   int64_t ld_out;
   int dump_group;  // kEpiDumpGroup
+  float* out_scales;                // kEpiGeluU4: [N / 64, M] group scales of the hidden codes
+  const __nv_bfloat16* out_smooth;  // kEpiGeluU4: [N] the next layer's smoothing (nullable)
+  int out_scale_dtype;              // kEpiGeluU4: 0 bf16, 1 f16 rounding of the stored scales
+  float gelu_shift;                 // kEpiGeluU4: added after GELU (0.171875)
 };
 
 struct GemmArgs {

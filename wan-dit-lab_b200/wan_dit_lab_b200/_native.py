@@ -35,6 +35,12 @@ SIGNATURES = {
     "wdl_rope_apply": (_I, [_P, _I, _P, _I, _I, _I, _I, _P, _P, _I, _P, _I, _I, _P, _I, _P]),
     "wdl_qkv_prep": (_I, [_P, _I64, _I, _I, _P, _P, ctypes.c_float, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,
                           _I, _I, _P]),
+    "wdl_w4a4_gemm_gelu_u4": (_I, [_P, _P, _P, _P, _I, _P, _P, ctypes.c_float, _I, _I, _I, _I, _P, _I64, _P, _P]),
+    "wdl_ln_quant": (_I, [_P, _I, _I64, _I, _I, ctypes.c_float, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P, _P]),
+    "wdl_rms_rows": (_I, [_P, _I64, _I, _I, _P, ctypes.c_float, _P, _I64, _P]),
+    "wdl_modulation": (_I, [_P, _P, _I, _I, _P, _P]),
+    "wdl_sage_prep_kv": (_I, [_P, _P, _P, _P, _I, _P, _I, _I64, _P, _I, _I64, _I, _I, _P, _P, _P, _P, _P, _SZ, _P]),
+    "wdl_sage_quant_q": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "wdl_sage_prep_workspace": (_SZ, [_I, _I]),
     "wdl_sage_prep": (_I, [_P, _I64, _I, _P, _P, _P, _P, _I, _P, _I, _I64, _P, _I, _I64, _I, _I, _P, _P, _P, _P, _P,
                            _P, _P, _SZ, _P]),
