@@ -1,15 +1,23 @@
 """Benchmark of the B200 hot path of wan-dit-lab's Wan-5B DiT block forward.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload linear]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload rollout|linear]
+
+Workload "rollout" (default): the full 30-layer Wan2.2-TI2V-5B-shaped DiT with random-init
+W4A4 weights (N(0, 0.02), seed 6) generating a 512x928 video chunk by chunk: latent [48, 21, 32, 58] N(0,1)
+noise (seed 8), a 512 x 4096 bf16 prompt N(0,1) (seed 9), chunks of 3 latent frames (1392 tokens), 4 DMD steps
++ 1 write pass per chunk, an FP8 KV window of 21 latent frames, 7 chunks. One step = one whole rollout of 21
+latent frames; metric = latent frames / s (value summed over ranks: one independent stream per GPU). The W4A4
+GEMMs (5 per block, 150 per pass) are timed with CUDA events in one extra instrumented chunk after the timed
+region: their algorithmic int ops over their event time is the roofline figure.
 
 Workload "linear" (the W4A4 QKV linear): X bf16 [1392, 3072] N(0,1) with 1% outlier
 channels x20, W [9216, 3072] N(0, 0.02) quantized to INT4 groups of 64 with float16 scales; one step = one
-w4a4 linear call (activation quantizer + tcgen05 kind::i8 GEMM) on inputs resident in HBM. Inputs are
-synthetic and seeded (the reference publishes no dataset for this path).
+w4a4 linear call (activation quantizer + tcgen05 GEMM) on inputs resident in HBM. Inputs are synthetic and
+seeded (the reference publishes no dataset for this path).
 
 Timing: W warm-up steps, then K timed steps. Every timed step is bracketed by CUDA events on the launching
 stream; between steps (outside the events) a 512 MiB buffer is written to flush the 126 MB L2, so each step
-starts cold. Under torchrun every rank runs its own replica (this path shards into independent streams: no
+starts cold (the rollout's 5 GB of weights exceed L2 anyway). Under torchrun every rank runs its own replica (this path shards into independent streams: no
 collective on the data path); the time is the max over ranks, the value the sum of the ranks' work over it.
 
 One JSON line (rank 0): metric/value/unit, e2e (the same call from pinned host buffers, copies included),
@@ -36,7 +44,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "wan-dit-lab_b200"))
 sys.path.insert(0, str(ROOT))
 
-METRIC = "W4A4 GEMM TOPS vs INT8 peak"
+METRIC = "latent frames/s per GPU (5B DiT, 512x928) and W4A4 GEMM TOPS vs INT8 peak"
+METRIC_LINEAR = "W4A4 GEMM TOPS vs INT8 peak"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 INT8_NOMINAL_TOPS = 4500.0
 CODES = "e4m3"  # operand code format of the W4A4 GEMM (--codes)
@@ -198,48 +207,160 @@ def cpu_linear_sample(x, W, rows=256):
     return dt, 2 * rows * W.shape[0] * W.shape[1], f"{rows} of 1392 tokens, full N and K (oracle port, numpy)"
 
 
-WORKLOADS = {"linear": linear_workload}
+def rollout_workload(device, rank=0):
+    from wan_dit_lab_b200.generation import causal
+    from wan_dit_lab_b200.models.block import WanBlockB200
+    torch.manual_seed(0)
+    model = causal.random_model(seed=6, device=device)
+    g = torch.Generator().manual_seed(8 + 1000 * rank)  # one independent seeded stream per rank
+    noise = torch.randn(48, 21, 32, 58, generator=g)
+    text = torch.randn(1, 512, 4096, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
+    stream = causal.Stream(model, text.to(device), 512, 928, torch.Generator(device=device).manual_seed(10 + rank),
+                           vae_stride=16)
+    noise_d = noise.to(device)
+    out = torch.empty_like(noise_d)
+    chunks = noise.shape[1] // causal.CHUNK
+
+    def step():
+        stream.reset()
+        for c in range(chunks):
+            out[:, 3 * c:3 * c + 3] = stream.next_chunk(noise_d[:, 3 * c:3 * c + 3])
+
+    noise_host = noise.pin_memory()
+    out_host = torch.empty_like(noise).pin_memory()
+
+    def e2e_step():
+        noise_d.copy_(noise_host, non_blocking=True)
+        step()
+        out_host.copy_(out, non_blocking=True)
+
+    gemm_log = []
+
+    def gemm_only():
+        """One instrumented chunk: the W4A4 GEMM launches bracketed by CUDA events (returns seconds, ops)."""
+        gemm_log.clear()
+        WanBlockB200.gemm_timer = lambda e0, e1, ops: gemm_log.append((e0, e1, ops))
+        try:
+            stream.reset()
+            stream.next_chunk(noise_d[:, :3])
+        finally:
+            WanBlockB200.gemm_timer = None
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b, _ in gemm_log) / 1e3, sum(o for _, _, o in gemm_log), len(gemm_log)
+
+    per_block = 2 * 1392 * 3072 * (9216 + 3072 + 3072 + 3072 + 2 * 14336)
+    return dict(step=step, e2e=e2e_step, gemm_probe=gemm_only, frames=21,
+                launches_per_step=chunks * 5 * (1 + 30 * 20),
+                h2d=noise.numel() * 4, d2h=noise.numel() * 4,
+                config={"workload": "BASELINE config 4: 30-layer 5B DiT rollout, 512x928, 7 chunks x (4 DMD steps + "
+                                    "write pass), FP8 KV window 21 frames",
+                        "model": "Wan2.2-TI2V-5B shape, random init N(0,0.02), W4A4 (INT4 g64, bf16 scales, rank 0)",
+                        "tokens_per_chunk": 1392, "keys_per_chunk": [1392 * (c + 1) for c in range(7)],
+                        "codes": CODES, "l2": "inputs larger than L2 (5 GB of weights per pass)"},
+                algorithmic={"gemm_int_ops_per_block_pass": per_block, "gemm_launches_per_block_pass": 5},
+                cpu=lambda: cpu_block_sample(), dtype="W4A4 (int4 x int4 exact on fp8/int8 tensor cores) + INT8/FP8 Sage "
+                                                      "attention; fp32 residual stream")
+
+
+def cpu_block_sample(tokens=64):
+    """The oracle block (oracle/block.py) on `tokens` of a chunk at full width (dim 3072, 24 heads, FFN 14336,
+    1392 cached keys, 512 prompt tokens), all host threads; extrapolated by tokens to a 1392-token chunk, x 30
+    blocks x 35 passes per 21-frame rollout. Returns (seconds per rollout, frames, sample description)."""
+    from oracle import block as ob
+    from oracle import fp8 as of
+    from oracle import rope as orope
+    from oracle import w4a4 as ow
+    torch.set_num_threads(os.cpu_count())
+    dim, heads, ffn = 3072, 24, 14336
+    g = torch.Generator().manual_seed(11)
+
+    def packed(N, K):
+        W = (torch.randn(N, K, generator=g) * 0.02).numpy()
+        q, s, _ = ow.weight(W)
+        return dict(qweight=ow.pack_nibbles(q), wscales=ow.round_to(s, "bfloat16").T.copy(),
+                    bias=(torch.randn(N, generator=g) * 0.02).numpy())
+
+    parts = {"self_attn.qkv": packed(3 * dim, dim), "self_attn.o": packed(dim, dim), "cross_attn.q": packed(dim, dim),
+             "cross_attn.k": packed(dim, dim), "cross_attn.v": packed(dim, dim), "cross_attn.o": packed(dim, dim),
+             "ffn.0": packed(ffn, dim), "ffn.2": packed(dim, ffn)}
+    ones = np.ones(dim, np.float32)
+    norms = dict(norm_q=ones, norm_k=ones, cross_norm_q=ones, cross_norm_k=ones, norm3_w=ones, norm3_b=ones * 0)
+    at, n = 1392, tokens
+    cap = at + n
+    ck, cks = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    cv, cvs = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    cache = dict(k=ck, ks=cks, v=cv, vs=cvs)
+    X = torch.randn(n, dim, generator=g).numpy()
+    mod = (torch.randn(6, dim, generator=g) * 0.05).numpy()
+    text = ow.round_to(torch.randn(512, dim, generator=g).numpy(), "bfloat16")
+    freq = orope.table(64).astype(np.float32)
+    t0 = time.perf_counter()
+    ob.block(X, mod, parts, norms, cache, at, freq, (1, 1, n), 3, text, heads)
+    dt = time.perf_counter() - t0
+    per_rollout = dt * (1392 / n) * 30 * 35
+    return per_rollout, 21, (f"oracle block (numpy, {os.cpu_count()} threads) on {n} of 1392 tokens at full width, "
+                             "extrapolated x 1392/{n} tokens x 30 blocks x 35 passes per 21-frame rollout").replace("{n}", str(n))
+
+
+WORKLOADS = {"rollout": rollout_workload, "linear": linear_workload}
 
 
 def reference_arm(args, rank, world):
-    """The reference's arithmetic on the host CPU: the oracle port, each step a bounded sample."""
+    """The reference's arithmetic on the host CPU (the oracle port), each step a bounded sample of the workload,
+    on rank 0 only."""
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count())
-    x = seeded((1392, 3072), 0, outliers=0.01).to(torch.bfloat16)
-    W = seeded((9216, 3072), 1, scale=0.02)
-    for _ in range(args.warmup):
-        cpu_linear_sample(x, W, rows=64)
-    times, ops = [], 0
-    for _ in range(args.steps):
-        dt, ops, sample = cpu_linear_sample(x, W, rows=128)
-        times.append(dt)
-    t = statistics.mean(times)
-    value = ops / t / 1e12
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
+    times = []
+    if args.workload == "rollout":
+        for _ in range(args.warmup):
+            cpu_block_sample(tokens=16)
+        for _ in range(args.steps):
+            per_rollout, frames, sample = cpu_block_sample(tokens=32)
+            times.append(per_rollout)
+        t = statistics.mean(times)
+        value, unit, metric = 21 / t, "latent frames/s", METRIC
+        config = {"workload": "BASELINE config 4 (30-layer rollout, 512x928), extrapolated from one oracle block on 32 "
+                              "tokens per step"}
+    else:
+        x = seeded((1392, 3072), 0, outliers=0.01).to(torch.bfloat16)
+        W = seeded((9216, 3072), 1, scale=0.02)
+        for _ in range(args.warmup):
+            cpu_linear_sample(x, W, rows=64)
+        for _ in range(args.steps):
+            dt, ops, sample = cpu_linear_sample(x, W, rows=128)
+            times.append(ops / dt)
+        value, unit, metric = statistics.mean(times) / 1e12, "TOPS", METRIC_LINEAR
+        t = 2 * 128 * 9216 * 3072 / (value * 1e12)
+        config = {"workload": "BASELINE config 1: W4A4 QKV linear X[1392,3072] x W[9216,3072]^T",
+                  "sample": "128 of 1392 tokens per step"}
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int4 x int4 (fp32 emulation)", "data": "synthetic",
-            "config": {"workload": "BASELINE config 1: W4A4 QKV linear X[1392,3072] x W[9216,3072]^T",
-                       "sample": "128 of 1392 tokens per step"},
-            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port",
-                             "sample": sample},
-            "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "scaling": "weak", "vs_baseline": None, "dtype": "W4A4 emulated exactly in float32/64 (numpy)",
+            "data": "synthetic (seeded, BASELINE shapes)", "config": config,
+            "cpu_baseline": {"value": value, "unit": unit, "cores": os.cpu_count(), "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20)
-    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--steps", type=int, default=None, help="timed steps (default 5 rollouts / 20 linears)")
+    parser.add_argument("--warmup", type=int, default=None, help="warm-up steps (>= 3)")
     parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
-    parser.add_argument("--workload", default="linear", choices=sorted(WORKLOADS))
+    parser.add_argument("--workload", default="rollout", choices=sorted(WORKLOADS))
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     parser.add_argument("--codes", default="e4m3", choices=("e4m3", "int8"),
                         help="operand code format of the W4A4 GEMM: e4m3 (kind::f8f6f4) or int8 (kind::i8)")
     args = parser.parse_args()
     global CODES
     CODES = args.codes
+    rollout = args.workload == "rollout"
+    if args.steps is None:
+        args.steps = 5 if rollout else 20
+    if args.warmup is None:
+        args.warmup = 3 if rollout else 5
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -253,9 +374,9 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
 
-    wl = WORKLOADS[args.workload](device)
+    wl = WORKLOADS[args.workload](device, rank) if rollout else WORKLOADS[args.workload](device)
     stream = torch.cuda.current_stream(device)
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     flush = lambda: flush_l2(flush_buf)  # noqa: E731
@@ -270,48 +391,59 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    # main timed region: K steps through the public entry point, inputs resident in HBM
+    # the timed region: K steps through the public API, inputs resident in HBM
     barrier()
     with Clocks(local) as clocks:
         times = timed_steps(wl["step"], args.steps, flush, stream)
     barrier()
     step_s = sum(times) / len(times)
-    # dominant kernel alone, same discipline
-    kernel_times = timed_steps(wl["kernel"], args.steps, flush, stream)
-    kernel_s = sum(kernel_times) / len(kernel_times)
-    # end to end from pinned host buffers
-    for _ in range(2):
+    # end to end from pinned host buffers (host <-> device copies inside the timed region)
+    for _ in range(2 if not rollout else 1):
         wl["e2e"]()
     e2e_times = timed_steps(wl["e2e"], args.steps, flush, stream)
     e2e_s = sum(e2e_times) / len(e2e_times)
+    # the dominant kernel
+    if rollout:
+        gemm_s, gemm_ops, gemm_launches = wl["gemm_probe"]()
+        achieved = gemm_ops / gemm_s / 1e12
+        kernel_ms = gemm_s / gemm_launches * 1e3
+    else:
+        kernel_times = timed_steps(wl["kernel"], args.steps, flush, stream)
+        kernel_s = sum(kernel_times) / len(kernel_times)
+        achieved, kernel_ms, gemm_launches = wl["ops"] / kernel_s / 1e12, kernel_s * 1e3, 1
 
     total = torch.tensor([step_s, e2e_s], device=device, dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(total, op=dist.ReduceOp.MAX)
     step_max, e2e_max = total.tolist()
-    ops = wl["ops"]
-    value = world * ops / step_max / 1e12
-    e2e_value = world * ops / e2e_max / 1e12
-    achieved = ops / kernel_s / 1e12
+    if rollout:
+        value, e2e_value, unit, metric = world * wl["frames"] / step_max, world * wl["frames"] / e2e_max, "latent frames/s", METRIC
+    else:
+        value, e2e_value, unit, metric = world * wl["ops"] / step_max / 1e12, world * wl["ops"] / e2e_max / 1e12, "TOPS", METRIC_LINEAR
 
     cpu = None
     if rank == 0 and not args.no_cpu:
-        dt, cpu_ops, sample = wl["cpu"]()
-        cpu = {"value": cpu_ops / dt / 1e12, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port", "sample": sample}
+        if rollout:
+            per_rollout, frames, sample = wl["cpu"]()
+            cpu = {"value": frames / per_rollout, "unit": unit, "cores": os.cpu_count(), "kind": "port", "sample": sample}
+        else:
+            dt, cpu_ops, sample = wl["cpu"]()
+            cpu = {"value": cpu_ops / dt / 1e12, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port", "sample": sample}
 
     if rank == 0:
+        dtype = wl["dtype"] if CODES == "int8" else wl["dtype"].replace("int8 tensor cores", "e4m3-coded integers on fp8 tensor cores, exact")
         line = {
-            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_max * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": wl["dtype"] if CODES == "int8" else wl["dtype"].replace("int8 tensor cores", "e4m3-coded integers on fp8 tensor cores, exact"), "data": "synthetic (seeded, BASELINE shapes)",
-            "config": {**wl["config"], "parallelism": f"replicas{world}" if world > 1 else "single"},
-            "e2e": {"value": e2e_value, "unit": "TOPS", "ms_per_step": e2e_max * 1e3,
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded, BASELINE shapes)",
+            "config": {**wl["config"], "parallelism": f"streams{world}" if world > 1 else "single"},
+            "e2e": {"value": e2e_value, "unit": unit, "ms_per_step": e2e_max * 1e3,
                     "h2d_bytes_per_step": wl["h2d"], "d2h_bytes_per_step": wl["d2h"]},
             "gpu_launches": wl["launches_per_step"] * args.steps,
-            "roofline": {"bound": "tensor", "kernel": "w4a4_gemm_kernel", "achieved": achieved,
-                         "peak": peak, "unit": "TOPS", "frac": achieved / peak, "peak_source": peak_source,
-                         "frac_of_nominal_int8": achieved / INT8_NOMINAL_TOPS, "kernel_ms": kernel_s * 1e3,
-                         "algorithmic": wl["algorithmic"], "traffic": None},
+            "roofline": {"bound": "tensor", "kernel": "w4a4_gemm_kernel", "achieved": achieved, "peak": peak,
+                         "unit": "TOPS", "frac": achieved / peak, "peak_source": peak_source,
+                         "frac_of_nominal_int8": achieved / INT8_NOMINAL_TOPS, "kernel_ms": kernel_ms,
+                         "launches_measured": gemm_launches, "algorithmic": wl["algorithmic"], "traffic": None},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
         }

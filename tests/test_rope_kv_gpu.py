@@ -241,7 +241,9 @@ def test_qkv_prep_matches_oracle_chain(n, dim, grid, start, at):
         got = out.cpu().numpy()
         exact = (got == rot).mean()
         assert exact >= 0.999, exact  # RMSNorm's float32 sum in another order may move a bf16 rounding
-        np.testing.assert_allclose(got, rot, rtol=2 ** -7, atol=1e-6)
+        # one bf16 step of a normalized input (|x| ~ 1) moves a rotated value by up to ~2^-7 absolutely, and more
+        # than that relatively where the rotation cancels
+        np.testing.assert_allclose(got, rot, rtol=2 ** -7, atol=2 ** -6)
     # the stored rows are quantize_rows of the rotated keys the kernel produced, and of the raw values, bit for bit
     kq, ksc = of.quantize_rows(k_out.cpu().numpy().reshape(n, heads, 128))
     vq, vsc = of.quantize_rows(x[:, 2 * dim:].reshape(n, heads, 128))

@@ -1,0 +1,264 @@
+"""Chunked autoregressive generation (Self-Forcing's DMD sampler) on the B200 Wan model, after the reference's
+src/wan_dit_lab/generation/causal.py (sigmas, KVCache, Stream.next_chunk) and models/model.py (WanModel).
+
+A chunk of `chunk` latent frames is denoised in len(STEPS) passes of the model while it attends to itself and to
+the keys / values of the frames before it, kept in an FP8 cache per block; one more pass with t = 0 writes its
+clean keys / values, and commit keeps them. The cache is a buffer of max_tokens + chunk tokens: a sink of the
+first frames that is never evicted, then a ring; once the ring is full the chunk's tokens replace those of the
+oldest frames (the reference's default eviction, causal.py:298-337 without Participative Compression).
+
+The model's edges (patch embedding, time embedding and projection, text embedding, head, unpatchify;
+models/model.py:32-84, models/head.py:13-18) run as plain bf16 PyTorch ops (cuBLAS / cuDNN library calls); the
+30 blocks run on the B200 kernels (models/block.py).
+"""
+
+import math
+
+import torch
+
+from wan_dit_lab_b200 import _native
+from wan_dit_lab_b200.models.block import Buffers, WanBlockB200
+
+SHIFT = 5.0  # timestep_shift of the distilled model (reference causal.py:35)
+STEPS = (1000, 750, 500, 250)  # its four timesteps before the shift (causal.py:36)
+CHUNK = 3  # latent frames generated together (causal.py:37)
+CONTEXT = 21  # latent frames attention looks back at (causal.py:38)
+
+
+def sigmas(shift=SHIFT, steps=STEPS):
+    """sigma = shift u / (1 + (shift - 1) u), u = t / 1000 (reference causal.py:41-45): 1, 0.9375, 0.8333, 0.625."""
+    u = torch.tensor(steps, dtype=torch.float64) / 1000
+    return (shift * u / (1 + (shift - 1) * u)).tolist()
+
+
+def rope_table(positions, head_dim=128):
+    """cos / sin [2, positions, head_dim / 2] float32 of the time / height / width axes (models/rope.py:4-10,
+    runtime/live_presets.py:52-61 with float32 tables): dims d - 4 (d // 6), 2 (d // 6), 2 (d // 6)."""
+    d = head_dim
+
+    def rope(count, dim):
+        pos = torch.arange(count, dtype=torch.float64)[:, None]
+        ang = pos * 10000 ** (-2 * torch.arange(dim // 2, dtype=torch.float64) / dim)
+        return torch.stack((torch.cos(ang), torch.sin(ang)))
+
+    return torch.cat([rope(positions, d - 4 * (d // 6)), rope(positions, 2 * (d // 6)), rope(positions, 2 * (d // 6))],
+                     dim=-1).float()
+
+
+class KVCache:
+    """FP8 keys / values of the finished frames of one block: [max_tokens + chunk tokens, heads, 128] E4M3 with
+    one float32 scale per (token, head), the first sink_tokens never evicted (reference KVCache,
+    causal.py:48-337, fp8=True, positions "video", no Participative Compression / decay / Forcing-KV)."""
+
+    fp8 = True
+
+    def __init__(self, max_tokens, sink_tokens, n, heads, device):
+        self.max_tokens, self.sink_tokens, self.n = max_tokens, sink_tokens, n
+        cap = max_tokens + n
+        self.capacity = cap
+        self.k = torch.zeros(cap, heads, 128, dtype=torch.uint8, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.ks = torch.zeros(cap, heads, device=device)
+        self.vs = torch.zeros_like(self.ks)
+        ring = max_tokens - sink_tokens
+        self.frame_of = torch.zeros(ring, dtype=torch.long, device=device)
+        self.saved = 0
+        self.frames = 0
+
+    def buffers(self):
+        return self.k, self.ks, self.v, self.vs, self.capacity
+
+    def full(self):
+        return self.saved == self.max_tokens
+
+    def commit(self, chunk_frames, per_frame):
+        """Keeps the chunk last written at `saved` (reference KVCache.commit, causal.py:298-327)."""
+        n, at, sink = self.n, self.saved, self.sink_tokens
+        if at + n <= self.max_tokens:  # filling: the chunk stays where it was written
+            if at + n > sink:
+                lo = max(at, sink)
+                self.frame_of[lo - sink:at + n - sink] = self.frames + (torch.arange(lo, at + n, device=self.k.device) - at) // per_frame
+            self.saved += n
+        elif self.max_tokens > sink:  # full: replace the tokens of the oldest frames of the ring
+            slots = torch.topk(self.frame_of, n, largest=False).indices
+            to = sink + slots
+            for buf in (self.k, self.v, self.ks, self.vs):
+                buf[to] = buf[at:at + n].clone()
+            self.frame_of[slots] = self.frames + torch.arange(n, device=self.k.device) // per_frame
+        self.frames += chunk_frames
+
+
+class WanModelB200:
+    """Wan2.2-TI2V-5B-shaped DiT (reference models/model.py WanModel with the Live preset's W4A4 blocks).
+    state: the model's state dict (reference parameter names); its blocks are quantized to W4A4 at load."""
+
+    def __init__(self, state, dim=3072, ffn_dim=14336, freq_dim=256, in_dim=48, out_dim=48, num_heads=24,
+                 num_layers=30, eps=1e-6, device="cuda", block_parts=None, blocks=None):
+        self.dim, self.heads, self.out_dim, self.freq_dim, self.eps = dim, num_heads, out_dim, freq_dim, eps
+        self.ffn_dim = ffn_dim
+        dev = torch.device(device)
+        g = lambda k: state[k].to(dev)  # noqa: E731
+        bf = lambda k: state[k].to(dev, torch.bfloat16)  # noqa: E731
+        self.patch_w, self.patch_b = bf("patch_embedding.weight"), bf("patch_embedding.bias")
+        self.text = [(bf(f"text_embedding.{i}.weight"), bf(f"text_embedding.{i}.bias")) for i in (0, 2)]
+        self.time = [(bf(f"time_embedding.{i}.weight"), bf(f"time_embedding.{i}.bias")) for i in (0, 2)]
+        self.proj = (bf("time_projection.1.weight"), bf("time_projection.1.bias"))
+        self.head_w, self.head_b = bf("head.head.weight"), bf("head.head.bias")
+        self.head_mod = g("head.modulation").float()
+        if blocks is None:
+            blocks = []
+            for i in range(num_layers):
+                prefix = f"blocks.{i}."
+                sub = {k[len(prefix):]: v for k, v in state.items() if k.startswith(prefix)}
+                blocks.append(WanBlockB200(sub, dim, ffn_dim, num_heads, eps, device=dev,
+                                           parts=None if block_parts is None else block_parts[i]))
+        self.blocks = blocks
+        # (time_in + modulation) of all blocks in one launch per pass
+        self.modulation = torch.stack([b.modulation for b in blocks]).contiguous()  # [layers, 6, dim]
+        self.mods = torch.empty_like(self.modulation)
+        self.device = dev
+
+    # ---- edges (bf16 PyTorch ops, as the reference runs them under autocast)
+    def text_embedding(self, context):
+        (w0, b0), (w2, b2) = self.text
+        h = torch.nn.functional.gelu(torch.nn.functional.linear(context.to(torch.bfloat16), w0, b0), approximate="tanh")
+        return torch.nn.functional.linear(h, w2, b2)
+
+    def time_in(self, t):
+        """e0 [6, dim] float32 and t_emb [dim] of timestep t (models/model.py:38-41)."""
+        omega = 10000 ** (-torch.arange(self.freq_dim // 2, dtype=torch.float64, device=self.device) / (self.freq_dim // 2))
+        theta = torch.tensor([float(t)], dtype=torch.float64, device=self.device)[:, None] * omega[None, :]
+        s = torch.cat([torch.cos(theta), torch.sin(theta)], dim=1).float().to(torch.bfloat16)
+        (w0, b0), (w2, b2) = self.time
+        temb = torch.nn.functional.linear(torch.nn.functional.silu(torch.nn.functional.linear(s, w0, b0)), w2, b2)
+        e0 = torch.nn.functional.linear(torch.nn.functional.silu(temb), *self.proj).unflatten(1, (6, -1))
+        return e0[0].float().contiguous(), temb[0]
+
+    def patch_embed(self, x):
+        """[C, f, H, W] latents -> [f (H/2) (W/2), dim] bf16 tokens (Conv3d kernel / stride (1, 2, 2))."""
+        y = torch.nn.functional.conv3d(x[None].to(torch.bfloat16), self.patch_w, self.patch_b, stride=(1, 2, 2))
+        return y.flatten(2).transpose(1, 2)[0]
+
+    def head(self, X, temb, grid):
+        """Head.forward (models/head.py:13-18) and unpatchify (models/model.py:81-84): [out_dim, f, 2h, 2w]."""
+        shift, scale = (self.head_mod + temb.float()[None, None]).chunk(2, dim=1)
+        xn = torch.nn.functional.layer_norm(X, (self.dim,), eps=self.eps)
+        y = torch.nn.functional.linear((xn * (1 + scale[0]) + shift[0]).to(torch.bfloat16), self.head_w, self.head_b)
+        f, h, w = grid
+        y = y.view(1, f, h, w, 1, 2, 2, self.out_dim)
+        return y.permute(0, 7, 1, 4, 2, 5, 3, 6).reshape(self.out_dim, f, h * 2, w * 2)
+
+    def cross_kvs(self, context):
+        ctx = self.text_embedding(context)
+        return [b.cross_kv(ctx[0] if ctx.ndim == 3 else ctx) for b in self.blocks]
+
+    def forward(self, x, t, grid, freq, start, caches, cross, buf):
+        """One pass over a chunk x [C, f, H, W] at timestep t: the flow prediction [out_dim, f, H, W] (float32).
+        Every block stores the chunk's keys / values into its cache at cache.saved and attends to [0, saved + n)."""
+        X = self.patch_embed(x).float()
+        e0, temb = self.time_in(t)
+        _native.check(_native.lib().wdl_modulation(e0.data_ptr(), self.modulation.data_ptr(), len(self.blocks), self.dim,
+                                                   self.mods.data_ptr(), _native.stream()))
+        for i, blk in enumerate(self.blocks):
+            blk.forward(X, self.mods[i], caches[i].buffers(), caches[i].saved, freq, grid, start, cross[i], buf,
+                        x_is_bf16=(i == 0))
+        return self.head(X, temb, grid).float()
+
+
+class Stream:
+    """A video, chunk by chunk (reference Stream with sampler "dmd", kv_fp8, attention "sage", positions "video",
+    write_pass True, cross_cache True): next_chunk denoises a chunk in len(levels) passes, writes its keys and
+    values with one more pass at t = 0, and commits them."""
+
+    def __init__(self, model, context, height, width, generator=None, max_frames=CONTEXT, sink_frames=0, chunk=CHUNK,
+                 vae_stride=8, positions=1024):
+        h, w = height // vae_stride, width // vae_stride
+        self.tokens = (h // 2) * (w // 2)
+        self.grid = (chunk, h // 2, w // 2)
+        self.chunk, self.model = chunk, model
+        n = chunk * self.tokens
+        self.shape = (model.out_dim, chunk, h, w)
+        self.caches = [KVCache((max_frames - chunk) * self.tokens, sink_frames * self.tokens, n, model.heads, model.device)
+                       for _ in model.blocks]
+        self.freq = rope_table(positions).to(model.device)
+        self.cross = model.cross_kvs(context.to(model.device))
+        text_tokens = self.cross[0].tokens
+        self.buf = Buffers(n, model.dim, model.ffn_dim, model.heads, max_frames * self.tokens, text_tokens, model.device)
+        self.levels = sigmas()
+        self.generator = generator
+        self.start = 0
+
+    def reset(self):
+        """A new video under the same prompt: caches emptied (buffers kept), frames counted from 0 again."""
+        for cache in self.caches:
+            cache.saved, cache.frames = 0, 0
+            cache.frame_of.zero_()
+        self.start = 0
+
+    @torch.no_grad()
+    def next_chunk(self, noise=None):
+        """Latents [C, chunk, H, W] of the next chunk (reference causal.py:681-758, dmd sampler)."""
+        dev = self.model.device
+        x = torch.randn(self.shape, generator=self.generator, device=dev) if noise is None else noise
+        run = lambda xx, t: self.model.forward(xx, t, self.grid, self.freq, self.start, self.caches, self.cross, self.buf)  # noqa: E731
+        x0 = x
+        for i, sigma in enumerate(self.levels):
+            flow = run(x, 1000 * sigma)
+            x0 = x - sigma * flow
+            if i + 1 < len(self.levels):
+                fresh = torch.randn(x0.shape, generator=self.generator, device=dev)
+                x = (1 - self.levels[i + 1]) * x0 + self.levels[i + 1] * fresh
+        run(x0, 0.0)  # the write pass: the clean chunk's keys and values
+        for cache in self.caches:
+            cache.commit(self.chunk, self.tokens)
+        self.start += self.chunk
+        return x0
+
+
+def random_block_state(g, dim, ffn_dim, device):
+    """One block's random-init weights: N(0, 0.02), norm weights around 1, modulation N(0, 1) / sqrt(dim)."""
+    r = lambda *s: torch.randn(*s, generator=g, device=device) * 0.02  # noqa: E731
+    st = {}
+    for attn in ("self_attn", "cross_attn"):
+        for name in ("q", "k", "v", "o"):
+            st[f"{attn}.{name}.weight"], st[f"{attn}.{name}.bias"] = r(dim, dim), r(dim)
+        st[f"{attn}.norm_q.weight"] = 1 + r(dim)
+        st[f"{attn}.norm_k.weight"] = 1 + r(dim)
+    st["ffn.0.weight"], st["ffn.0.bias"] = r(ffn_dim, dim), r(ffn_dim)
+    st["ffn.2.weight"], st["ffn.2.bias"] = r(dim, ffn_dim), r(dim)
+    st["norm3.weight"], st["norm3.bias"] = 1 + r(dim), r(dim)
+    st["modulation"] = torch.randn(1, 6, dim, generator=g, device=device) / math.sqrt(dim)
+    return st
+
+
+def random_model(dim=3072, ffn_dim=14336, freq_dim=256, in_dim=48, out_dim=48, num_heads=24, num_layers=30,
+                 text_dim=4096, seed=6, device="cuda"):
+    """A WanModelB200 of the Wan2.2-TI2V-5B shape with random-init weights (N(0, 0.02)),
+    generated on `device` from one seed, one block at a time (each block's float weights are dropped once it
+    is quantized to W4A4)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    edges = random_state(dim, freq_dim=freq_dim, in_dim=in_dim, out_dim=out_dim, num_layers=0, text_dim=text_dim,
+                         generator=g, device=device)
+    blocks = [WanBlockB200(random_block_state(g, dim, ffn_dim, device), dim, ffn_dim, num_heads, device=device)
+              for _ in range(num_layers)]
+    return WanModelB200(edges, dim, ffn_dim, freq_dim, in_dim, out_dim, num_heads, num_layers, device=device,
+                        blocks=blocks)
+
+
+def random_state(dim=3072, ffn_dim=14336, freq_dim=256, in_dim=48, out_dim=48, num_layers=30, text_dim=4096, seed=6,
+                 device="cuda", generator=None):
+    """Random-init weights of the Wan2.2-TI2V-5B shape, N(0, 0.02) (norm weights around 1, modulations
+    N(0, 1) / sqrt(dim) as WanBlock initializes them), generated on `device` from one seed."""
+    g = torch.Generator(device=device).manual_seed(seed) if generator is None else generator
+    r = lambda *s: torch.randn(*s, generator=g, device=device) * 0.02  # noqa: E731
+    st = {"patch_embedding.weight": r(dim, in_dim, 1, 2, 2), "patch_embedding.bias": r(dim),
+          "text_embedding.0.weight": r(dim, text_dim), "text_embedding.0.bias": r(dim),
+          "text_embedding.2.weight": r(dim, dim), "text_embedding.2.bias": r(dim),
+          "time_embedding.0.weight": r(dim, freq_dim), "time_embedding.0.bias": r(dim),
+          "time_embedding.2.weight": r(dim, dim), "time_embedding.2.bias": r(dim),
+          "time_projection.1.weight": r(6 * dim, dim), "time_projection.1.bias": r(6 * dim),
+          "head.head.weight": r(4 * out_dim, dim), "head.head.bias": r(4 * out_dim),
+          "head.modulation": torch.randn(1, 2, dim, generator=g, device=device) / math.sqrt(dim)}
+    for i in range(num_layers):
+        st.update({f"blocks.{i}.{k}": v for k, v in random_block_state(g, dim, ffn_dim, device).items()})
+    return st

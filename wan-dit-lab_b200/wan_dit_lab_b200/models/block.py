@@ -122,6 +122,10 @@ class WanBlockB200:
         return CrossKV(k_i8, k_scale, v_f8, v_scale, T)
 
     # ---- chunk
+    # When set (a callable taking (start, stop) CUDA events and the layer's int ops), every GEMM launch of forward
+    # is bracketed by CUDA events on the current stream: the benchmark's per-kernel timing of the W4A4 GEMMs.
+    gemm_timer = None
+
     def forward(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, trace=None):
         """X [n, dim] float32, updated in place (the block's output). mod [6, dim] float32: this block's
         time_in + modulation. cache: (k, ks, v, vs, capacity) FP8 cache buffers of this block
@@ -141,18 +145,29 @@ class WanBlockB200:
         L = self.layers
         mod_ptr = lambda i: mod.data_ptr() + i * dim * 4  # noqa: E731
 
+        timer = WanBlockB200.gemm_timer
+
+        def timed(layer, launch):
+            if timer is None:
+                return launch()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            launch()
+            e1.record()
+            timer(e0, e1, 2 * n * layer.N * layer.K)
+
         def gemm(layer, out):
-            _native.check(lib.wdl_w4a4_gemm(buf.codes.data_ptr(), buf.scales.data_ptr(), layer.codes.data_ptr(),
+            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm(buf.codes.data_ptr(), buf.scales.data_ptr(), layer.codes.data_ptr(),
                                             layer.scales.data_ptr(), fmt, _native.ptr(layer.bias), n, layer.N, layer.K,
-                                            out.data_ptr(), out.stride(0), st))
+                                            out.data_ptr(), out.stride(0), st)))
 
         def gemm_residual(layer, gate_row, codes=None, scales=None):
             c = buf.codes if codes is None else codes
             s = buf.scales if scales is None else scales
-            _native.check(lib.wdl_w4a4_gemm_residual(
+            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_residual(
                 c.data_ptr(), s.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), fmt,
                 _native.ptr(layer.bias), None if gate_row is None else mod_ptr(gate_row), X.data_ptr(), dim, n, layer.N,
-                layer.K, X.data_ptr(), dim, st))
+                layer.K, X.data_ptr(), dim, st)))
 
         def ln_quant(shift_row, scale_row, affine, layer, round_bf16):
             _native.check(lib.wdl_ln_quant(
@@ -199,10 +214,10 @@ class WanBlockB200:
         # feed forward
         fc1, fc2 = L["ffn.0"], L["ffn.2"]
         ln_quant(3, 4, False, fc1, x_is_bf16)
-        _native.check(lib.wdl_w4a4_gemm_gelu_u4(buf.codes.data_ptr(), buf.scales.data_ptr(), fc1.codes.data_ptr(),
-                                                fc1.scales.data_ptr(), fmt, _native.ptr(fc1.bias), _native.ptr(fc2.smooth),
-                                                w4a4.GELU_SHIFT, sd, n, fc1.N, fc1.K, buf.hcodes.data_ptr(),
-                                                buf.hcodes.stride(0), buf.hscales.data_ptr(), st))
+        timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4(
+            buf.codes.data_ptr(), buf.scales.data_ptr(), fc1.codes.data_ptr(), fc1.scales.data_ptr(), fmt,
+            _native.ptr(fc1.bias), _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N, fc1.K, buf.hcodes.data_ptr(),
+            buf.hcodes.stride(0), buf.hscales.data_ptr(), st)))
         keep("hcodes", buf.hcodes), keep("hscales", buf.hscales)
         gemm_residual(fc2, 5, buf.hcodes, buf.hscales)
         return X
