@@ -114,6 +114,19 @@ int wdl_w4a4_linear(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t
                     const void* w, const float* w_scales, int code_format, const float* bias, int N, uint16_t* y,
                     int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The W4A4 linear of wdl_w4a4_linear for callers that cannot allocate device memory: no workspace argument and
+ * no allocation of any kind inside. Its scratch (the activation's INT4 codes and scales between the quantizer and
+ * the GEMM) is a fixed array of WDL_W4A4_LINEAR_NOALLOC_MAX_BYTES in the library's own device memory, held by
+ * every device that loads the library until the process exits. Calls needing more than that (M * K * 17 / 16
+ * bytes, rounded up) return WDL_ERR_ARGUMENT. The first call on a device resolves the array's device address
+ * (cudaGetSymbolAddress) and should come before any stream capture. All calls on a device share the array: calls
+ * that overlap on the GPU race and must be ordered by the caller. Otherwise as wdl_w4a4_linear.
+ * No counterpart in the reference: live::w4a4_linear always allocates its scratch (native/ops/w4a4_ops.cpp:22-29). */
+#define WDL_W4A4_LINEAR_NOALLOC_MAX_BYTES ((size_t)16 << 20)
+int wdl_w4a4_linear_noalloc(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t* smooth, int scale_dtype,
+                            const void* w, const float* w_scales, int code_format, const float* bias, int N, uint16_t* y,
+                            int64_t ldy, void* stream);
+
 /* ---- 3D RoPE, the FP8 KV cache, the QKV preparation of self-attention ------------------------------------- */
 
 /* Stores K and V [B, N, H, D] (dtypes WDL_BF16 / WDL_F16 / WDL_F32, element strides k_strides[4], v_strides[4],

@@ -61,6 +61,13 @@ int cuda_status(cudaError_t e, const char* what) {
 
 namespace wdl {
 
+int set_last_error(int code, const char* message) {
+  g_error = message ? message : "";
+  return code;
+}
+
+uint32_t* device_error_word() { return error_word(); }
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);

@@ -31,6 +31,7 @@ SIGNATURES = {
     "wdl_w4a4_gemm_group_partials": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I64, _P]),
     "wdl_w4a4_linear_workspace": (_SZ, [_I, _I]),
     "wdl_w4a4_linear": (_I, [_P, _I64, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P, _I64, _P, _SZ, _P]),
+    "wdl_w4a4_linear_noalloc": (_I, [_P, _I64, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P, _I64, _P]),
     "wdl_store_kv_fp8": (_I, [_P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _P]),
     "wdl_rope_apply": (_I, [_P, _I, _P, _I, _I, _I, _I, _P, _P, _I, _P, _I, _I, _P, _I, _P]),
     "wdl_qkv_prep": (_I, [_P, _I64, _I, _I, _P, _P, ctypes.c_float, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,
