@@ -207,11 +207,11 @@ def cpu_linear_sample(x, W, rows=256):
     return dt, 2 * rows * W.shape[0] * W.shape[1], f"{rows} of 1392 tokens, full N and K (oracle port, numpy)"
 
 
-def rollout_workload(device, rank=0):
+def rollout_workload(device, rank=0, chunks=7, layers=30):
     from wan_dit_lab_b200.generation import causal
     from wan_dit_lab_b200.models.block import WanBlockB200
     torch.manual_seed(0)
-    model = causal.random_model(seed=6, device=device)
+    model = causal.random_model(seed=6, device=device, num_layers=layers)
     g = torch.Generator().manual_seed(8 + 1000 * rank)  # one independent seeded stream per rank
     noise = torch.randn(48, 21, 32, 58, generator=g)
     text = torch.randn(1, 512, 4096, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
@@ -219,7 +219,6 @@ def rollout_workload(device, rank=0):
                            vae_stride=16)
     noise_d = noise.to(device)
     out = torch.empty_like(noise_d)
-    chunks = noise.shape[1] // causal.CHUNK
 
     def step():
         stream.reset()
@@ -249,13 +248,14 @@ def rollout_workload(device, rank=0):
         return sum(a.elapsed_time(b) for a, b, _ in gemm_log) / 1e3, sum(o for _, _, o in gemm_log), len(gemm_log)
 
     per_block = 2 * 1392 * 3072 * (9216 + 3072 + 3072 + 3072 + 2 * 14336)
-    return dict(step=step, e2e=e2e_step, gemm_probe=gemm_only, frames=21,
-                launches_per_step=chunks * 5 * (1 + 30 * 20),
+    return dict(step=step, e2e=e2e_step, gemm_probe=gemm_only, frames=3 * chunks,
+                launches_per_step=chunks * 5 * (1 + layers * 20),
                 h2d=noise.numel() * 4, d2h=noise.numel() * 4,
                 config={"workload": "BASELINE config 4: 30-layer 5B DiT rollout, 512x928, 7 chunks x (4 DMD steps + "
                                     "write pass), FP8 KV window 21 frames",
                         "model": "Wan2.2-TI2V-5B shape, random init N(0,0.02), W4A4 (INT4 g64, bf16 scales, rank 0)",
-                        "tokens_per_chunk": 1392, "keys_per_chunk": [1392 * (c + 1) for c in range(7)],
+                        "tokens_per_chunk": 1392, "keys_per_chunk": [1392 * (c + 1) for c in range(chunks)],
+                        "chunks": chunks, "layers": layers,
                         "codes": CODES, "l2": "inputs larger than L2 (5 GB of weights per pass)"},
                 algorithmic={"gemm_int_ops_per_block_pass": per_block, "gemm_launches_per_block_pass": 5},
                 cpu=lambda: cpu_block_sample(), dtype="W4A4 (int4 x int4 exact on fp8/int8 tensor cores) + INT8/FP8 Sage "
@@ -353,6 +353,8 @@ def main():
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     parser.add_argument("--codes", default="e4m3", choices=("e4m3", "int8"),
                         help="operand code format of the W4A4 GEMM: e4m3 (kind::f8f6f4) or int8 (kind::i8)")
+    parser.add_argument("--chunks", type=int, default=7, help="rollout chunks (profiling; BASELINE config 4: 7)")
+    parser.add_argument("--layers", type=int, default=30, help="model layers (profiling; BASELINE config 4: 30)")
     args = parser.parse_args()
     global CODES
     CODES = args.codes
@@ -376,7 +378,7 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
 
-    wl = WORKLOADS[args.workload](device, rank) if rollout else WORKLOADS[args.workload](device)
+    wl = WORKLOADS[args.workload](device, rank, args.chunks, args.layers) if rollout else WORKLOADS[args.workload](device)
     stream = torch.cuda.current_stream(device)
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     flush = lambda: flush_l2(flush_buf)  # noqa: E731
