@@ -305,6 +305,19 @@ def cpu_block_sample(tokens=64):
 WORKLOADS = {"rollout": rollout_workload, "linear": linear_workload}
 
 
+def combine_ranks(dist, seconds, device):
+    """Max over ranks of each of the per-rank durations `seconds` (every rank calls this, in the same order)."""
+    t = torch.tensor(seconds, device=device, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def job_rate(world, units_per_rank, seconds_max):
+    """Whole-job throughput: every rank processes units_per_rank; the job lasts as long as its slowest rank."""
+    return world * units_per_rank / seconds_max
+
+
 def reference_arm(args, rank, world):
     """The reference's arithmetic on the host CPU (the oracle port), each step a bounded sample of the workload,
     on rank 0 only."""
@@ -414,14 +427,13 @@ def main():
         kernel_s = sum(kernel_times) / len(kernel_times)
         achieved, kernel_ms, gemm_launches = wl["ops"] / kernel_s / 1e12, kernel_s * 1e3, 1
 
-    total = torch.tensor([step_s, e2e_s], device=device, dtype=torch.float64)
-    if dist is not None:
-        dist.all_reduce(total, op=dist.ReduceOp.MAX)
-    step_max, e2e_max = total.tolist()
+    step_max, e2e_max = combine_ranks(dist, [step_s, e2e_s], device)
     if rollout:
-        value, e2e_value, unit, metric = world * wl["frames"] / step_max, world * wl["frames"] / e2e_max, "latent frames/s", METRIC
+        value, e2e_value = job_rate(world, wl["frames"], step_max), job_rate(world, wl["frames"], e2e_max)
+        unit, metric = "latent frames/s", METRIC
     else:
-        value, e2e_value, unit, metric = world * wl["ops"] / step_max / 1e12, world * wl["ops"] / e2e_max / 1e12, "TOPS", METRIC_LINEAR
+        value, e2e_value = job_rate(world, wl["ops"], step_max) / 1e12, job_rate(world, wl["ops"], e2e_max) / 1e12
+        unit, metric = "TOPS", METRIC_LINEAR
 
     cpu = None
     if rank == 0 and not args.no_cpu:

@@ -167,14 +167,15 @@ int wdl_qkv_prep(const uint16_t* qkv, int64_t ld, int n, int dim, const float* n
  * (float32 statistics, eps; ln_w / ln_b [K] float32 affine, nullable), rounded to bf16 when round_ln_bf16 (the
  * residual stream is bf16: .type_as), then when mod_shift is not null y * (1 + mod_scale) + mod_shift (float32
  * [K] each), then rounded to bf16 (the next linear layer's input) and quantized as wdl_w4a4_quantize_rows does
- * (smooth [K] bf16 nullable): codes [M, K] (code_format), scales [K / 64, M] (scale_dtype).
+ * (smooth [K] bf16 nullable): codes [M, K] (code_format), scales [K / 64, M] (scale_dtype). The [K] vectors are
+ * 16-byte aligned.
  * models/block.py:75-79 norm1 / norm2 (modulated) and norm3 (affine) feeding quantization/w4a4.py:229-231. */
 int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float eps, const float* ln_w,
                  const float* ln_b, int round_ln_bf16, const float* mod_shift, const float* mod_scale,
                  const uint16_t* smooth, int scale_dtype, int code_format, void* codes, float* scales, void* stream);
 
 /* RMSNorm of rows: out [M, ldo] f32 = bf16(x * rsqrt(mean(x^2) + eps)) * w for x [M, ldx] bf16 (K % 256 == 0,
- * K <= 4096). models/rms_norm.py:10-13 (the query norm of cross-attention, models/multi_head_attention.py:118). */
+ * K <= 4096; x, w and out 16-byte aligned). models/rms_norm.py:10-13 (the query norm of cross-attention, models/multi_head_attention.py:118). */
 int wdl_rms_rows(const uint16_t* x, int64_t ldx, int M, int K, const float* w, float eps, float* out, int64_t ldo,
                  void* stream);
 
@@ -189,7 +190,9 @@ int wdl_modulation(const float* time_in, const float* modulation, int blocks, in
  *   v_f8 [H, 128, Lpad] e4m3 (keys contiguous), v_scale [H, 128] f32
  * npad = nq rounded up to 128, Lpad = L = at + n rounded up to 128; padding holds zero codes.
  * Cache: cache_k / cache_v [capacity, H, 128] e4m3 with scales cache_ks / cache_vs [capacity, H] (batch 1).
- * Chunk: k [n, ld_k], v [n, ld_v] (k_dtype / v_dtype WDL_F32 or WDL_BF16), head h at column h * 128. */
+ * Chunk: k [n, ld_k], v [n, ld_v] (k_dtype / v_dtype WDL_F32 or WDL_BF16), head h at column h * 128.
+ * Alignment: cache bases 4 bytes; chunk bases 16 bytes (float32) or 8 bytes (bf16) with ld_k, ld_v multiples of
+ * 4; q 16 bytes with ld_q a multiple of 4; q_i8, k_i8, v_f8 and v_scale 16 bytes. */
 
 /* The quantization of SageAttention 2 read straight from the FP8 cache (tokens [0, at)) and the chunk
  * (tokens [at, at + n)): key mean over all L = at + n keys, K - mean to INT8 with 4 scales per 64 keys

@@ -1,0 +1,119 @@
+"""The C ABI without a GPU: libwdl_b200.so loads, exports every entry point include/wdl_b200.h declares (with the
+argument counts the ctypes binding declares), and rejects invalid calls with WDL_ERR_ARGUMENT and a message
+before it touches the device, as the reference's operators raise on bad shapes before launching
+(kernels/cache_fp8.py:75-100, native/ops/w4a4_ops.cpp:20-35)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "wdl_b200.h"
+
+
+def declarations():
+    """name -> number of parameters, for every function the header declares."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"^[A-Za-z_][\w \t\*]*?\b(wdl_\w+)\s*\(([^)]*)\)\s*;", text, flags=re.M):
+        params = m.group(2).strip()
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+@pytest.fixture(scope="module")
+def native():
+    from wan_dit_lab_b200 import _native
+    return _native
+
+
+def test_header_declares_the_bound_entry_points(native):
+    decl = declarations()
+    assert len(decl) >= 25
+    assert set(decl) == set(native.SIGNATURES), set(decl) ^ set(native.SIGNATURES)
+    for name, count in decl.items():
+        assert len(native.SIGNATURES[name][1]) == count, name
+
+
+def test_library_exports_every_declared_symbol(native):
+    raw = ctypes.CDLL(str(native.LIBRARY))
+    missing = [name for name in declarations() if not hasattr(raw, name)]
+    assert not missing, missing
+    lib = native.lib()
+    assert lib.wdl_version().startswith(b"wdl_b200")
+
+
+FAKE = 1 << 20  # a 256-byte aligned address the library only checks, never dereferences, in these calls
+
+
+def test_gemm_shapes_rejected_before_any_launch(native):
+    lib = native.lib()
+    st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_E4M3, None, 128, 300, 256, FAKE, 512, None)
+    assert st == native.ERR_ARGUMENT and b"multiple of 256" in lib.wdl_last_error()
+    st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_E4M3, None, 128, 256, 200, FAKE, 256, None)
+    assert st == native.ERR_ARGUMENT and b"multiple of 128" in lib.wdl_last_error()
+    st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE + 8, FAKE, native.CODES_E4M3, None, 128, 256, 256, FAKE, 256, None)
+    assert st == native.ERR_ARGUMENT and b"16-byte" in lib.wdl_last_error()
+    st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, 7, None, 128, 256, 256, FAKE, 256, None)
+    assert st == native.ERR_ARGUMENT and b"code format" in lib.wdl_last_error()
+    assert lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_E4M3, None, 0, 256, 256, FAKE, 256, None) == 0
+
+
+def test_workspace_sizes(native):
+    lib = native.lib()
+    M, K = 1392, 3072
+    assert lib.wdl_w4a4_linear_workspace(M, K) == (M * K + 255) // 256 * 256 + (K // 64) * M * 4
+    assert lib.wdl_w4a4_linear_workspace(0, K) == 0
+    L, H = 5568, 24
+    assert lib.wdl_sage_prep_workspace(L, H) == (2 * ((L + 63) // 64) + 1) * H * 128 * 4
+    np_, lp = 1408, 5632
+    up = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    want = (up(H * np_ * 128) + up(H * np_ // 32 * 8 * 4) + up(H * lp * 128) + up(H * lp // 64 * 4 * 4) +
+            up(H * 128 * lp) + up(H * 128 * 4) + up(lib.wdl_sage_prep_workspace(L, H)))
+    assert lib.wdl_sage_attend_workspace(1392, L, H) == want
+
+
+def test_linear_validation(native):
+    lib = native.lib()
+    need = lib.wdl_w4a4_linear_workspace(128, 256)
+    st = lib.wdl_w4a4_linear(FAKE, 256, 128, 256, None, native.BF16, FAKE, FAKE, native.CODES_E4M3, None, 256, FAKE,
+                             256, FAKE, need - 1, None)
+    assert st == native.ERR_ARGUMENT and b"workspace" in lib.wdl_last_error()
+    st = lib.wdl_w4a4_linear(FAKE, 256, 128, 256, None, native.BF16, FAKE, FAKE, native.CODES_E4M3, None, 256, FAKE,
+                             256, FAKE + 16, need, None)
+    assert st == native.ERR_ARGUMENT and b"256-byte" in lib.wdl_last_error()
+    M = 2 * (16 << 20) // 4096
+    st = lib.wdl_w4a4_linear_noalloc(FAKE, 4096, M, 4096, None, native.BF16, FAKE, FAKE, native.CODES_E4M3, None, 256,
+                                     FAKE, 256, None)
+    assert st == native.ERR_ARGUMENT and b"16 MiB" in lib.wdl_last_error()
+
+
+def test_norm_and_cache_validation(native):
+    lib = native.lib()
+    st = lib.wdl_ln_quant(FAKE, native.F32, 1000, 4, 1000, 1e-6, None, None, 0, None, None, None, native.BF16,
+                          native.CODES_E4M3, FAKE, FAKE, None)
+    assert st == native.ERR_ARGUMENT and b"multiple of 256" in lib.wdl_last_error()
+    st = lib.wdl_ln_quant(FAKE, native.F32, 1024, 4, 1024, 1e-6, FAKE, None, 0, None, None, None, native.BF16,
+                          native.CODES_E4M3, FAKE, FAKE, None)
+    assert st == native.ERR_ARGUMENT and b"pairs" in lib.wdl_last_error()
+    st = lib.wdl_ln_quant(FAKE, native.F32, 1024, 4, 1024, 1e-6, FAKE + 4, FAKE, 0, None, None, None, native.BF16,
+                          native.CODES_E4M3, FAKE, FAKE, None)
+    assert st == native.ERR_ARGUMENT and b"16-byte" in lib.wdl_last_error()
+    st = lib.wdl_rms_rows(FAKE, 3072, 4, 3072, FAKE + 4, 1e-6, FAKE, 3072, None)
+    assert st == native.ERR_ARGUMENT
+    # Sage quantizers: float32 chunk rows must start 16-byte aligned
+    work = lib.wdl_sage_prep_workspace(256, 2)
+    st = lib.wdl_sage_prep_kv(None, None, None, None, 0, FAKE + 8, native.F32, 256, FAKE, native.BF16, 256, 256, 2,
+                              FAKE, FAKE, FAKE, FAKE, FAKE, work, None)
+    assert st == native.ERR_ARGUMENT and b"misaligned" in lib.wdl_last_error()
+    st = lib.wdl_sage_quant_q(FAKE, 258, 64, 2, FAKE, FAKE, None)
+    assert st == native.ERR_ARGUMENT
+
+
+def test_python_layer_raises_value_error(native):
+    lib = native.lib()
+    st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_E4M3, None, 128, 300, 256, FAKE, 512, None)
+    with pytest.raises(ValueError, match="multiple of 256"):
+        native.check(st)

@@ -156,9 +156,10 @@ static int gemm_common(wdl::w4a4::GemmArgs& a, void* stream) {
   if (!a.a || !a.b || !a.wscale || !a.ep.ascale || !a.ep.out) return fail(WDL_ERR_ARGUMENT, "null operand pointer");
   if (!aligned(a.ep.out, 16) || (a.ep.residual && !aligned(a.ep.residual, 16)))
     return fail(WDL_ERR_ARGUMENT, "output and residual must be 16-byte aligned");
+  const char* why = "";
+  if (wdl::w4a4::gemm_validate(a, &why) != 0) return fail(WDL_ERR_ARGUMENT, "%s", why);
   a.err = error_word();
   if (!a.err) return fail(WDL_ERR_CUDA, "cannot resolve the device error word");
-  const char* why = "";
   const int st = wdl::w4a4::gemm_launch(a, static_cast<cudaStream_t>(stream), &why);
   if (st == 1) return fail(WDL_ERR_ARGUMENT, "%s", why);
   if (st != 0) return fail(WDL_ERR_CUDA, "%s", why);
@@ -343,6 +344,9 @@ int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float ep
     return fail(WDL_ERR_ARGUMENT, "invalid code format or scale dtype");
   if (M == 0) return ok();
   if (!codes || !scales || !aligned(codes, 8)) return fail(WDL_ERR_ARGUMENT, "null or misaligned output");
+  if (!aligned(ln_w, 16) || !aligned(ln_b, 16) || !aligned(mod_shift, 16) || !aligned(mod_scale, 16) ||
+      !aligned(smooth, 16))
+    return fail(WDL_ERR_ARGUMENT, "ln_w, ln_b, mod_shift, mod_scale and smooth must be 16-byte aligned");
   wdl::norm::LnQuantArgs a{};
   a.x = x, a.x_f32 = x_dtype == WDL_F32, a.ldx = ldx, a.M = M, a.K = K, a.eps = eps, a.ln_w = ln_w, a.ln_b = ln_b;
   a.round_ln_bf16 = round_ln_bf16, a.mod_shift = mod_shift, a.mod_scale = mod_scale;
@@ -358,7 +362,8 @@ int wdl_rms_rows(const uint16_t* x, int64_t ldx, int M, int K, const float* w, f
   if (M < 0 || ldx < K || ldo < K || (ldx * 2) % 16 != 0 || (ldo * 4) % 16 != 0)
     return fail(WDL_ERR_ARGUMENT, "row strides must hold K channels, 16-byte aligned");
   if (M == 0) return ok();
-  if (!x || !w || !out || !aligned(x, 16) || !aligned(out, 16)) return fail(WDL_ERR_ARGUMENT, "null or misaligned pointer");
+  if (!x || !w || !out || !aligned(x, 16) || !aligned(out, 16) || !aligned(w, 16))
+    return fail(WDL_ERR_ARGUMENT, "null or misaligned pointer");
   wdl::norm::rms_rows_launch(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, K, w, eps, out, ldo,
                              static_cast<cudaStream_t>(stream));
   return cuda_status(cudaGetLastError(), "rms_rows launch");
@@ -369,6 +374,16 @@ int wdl_modulation(const float* time_in, const float* modulation, int blocks, in
   if (!time_in || !modulation || !out) return fail(WDL_ERR_ARGUMENT, "null pointer");
   wdl::norm::modulation_launch(time_in, modulation, blocks, dim, out, static_cast<cudaStream_t>(stream));
   return cuda_status(cudaGetLastError(), "modulation launch");
+}
+
+// The Sage quantizers read four channels at a time: cache rows from 4-byte aligned bases, chunk rows of float32
+// from 16-byte aligned bases (bf16: 8-byte), row strides a multiple of 4 elements.
+static bool sage_sources_aligned(const uint8_t* cache_k, const uint8_t* cache_v, int at, const void* k, int k_dtype,
+                                 int64_t ld_k, const void* v, int v_dtype, int64_t ld_v, int n) {
+  if (at > 0 && (!aligned(cache_k, 4) || !aligned(cache_v, 4))) return false;
+  if (n <= 0) return true;
+  return aligned(k, k_dtype == WDL_F32 ? 16 : 8) && aligned(v, v_dtype == WDL_F32 ? 16 : 8) && ld_k % 4 == 0 &&
+         ld_v % 4 == 0;
 }
 
 int wdl_sage_prep_kv(const uint8_t* cache_k, const float* cache_ks, const uint8_t* cache_v, const float* cache_vs,
@@ -384,6 +399,9 @@ int wdl_sage_prep_kv(const uint8_t* cache_k, const float* cache_ks, const uint8_
   if ((n > 0 && (!k || !v)) || !k_i8 || !k_scale || !v_f8 || !v_scale) return fail(WDL_ERR_ARGUMENT, "null pointer");
   if (!work || work_bytes < wdl::sage::prep_workspace_floats(at + n, H) * sizeof(float))
     return fail(WDL_ERR_ARGUMENT, "workspace too small");
+  if (!sage_sources_aligned(cache_k, cache_v, at, k, k_dtype, ld_k, v, v_dtype, ld_v, n) || !aligned(k_i8, 16) ||
+      !aligned(v_f8, 16) || !aligned(v_scale, 16))
+    return fail(WDL_ERR_ARGUMENT, "misaligned K / V source or output");
   wdl::sage::PrepArgs a{};
   a.cache_k = cache_k, a.cache_ks = cache_ks, a.cache_v = cache_v, a.cache_vs = cache_vs, a.at = at;
   a.k_chunk = k, a.ld_k = ld_k, a.k_bf16 = k_dtype == WDL_BF16, a.v_chunk = v, a.ld_v = ld_v, a.v_bf16 = v_dtype == WDL_BF16;
@@ -395,7 +413,8 @@ int wdl_sage_prep_kv(const uint8_t* cache_k, const float* cache_ks, const uint8_
 
 int wdl_sage_quant_q(const float* q, int64_t ld_q, int nq, int H, int8_t* q_i8, float* q_scale, void* stream) {
   if (nq <= 0 || H <= 0 || ld_q < static_cast<int64_t>(H) * 128) return fail(WDL_ERR_ARGUMENT, "invalid Q shape");
-  if (!q || !q_i8 || !q_scale || !aligned(q_i8, 8)) return fail(WDL_ERR_ARGUMENT, "null or misaligned pointer");
+  if (!q || !q_i8 || !q_scale || !aligned(q_i8, 8) || !aligned(q, 16) || ld_q % 4 != 0)
+    return fail(WDL_ERR_ARGUMENT, "null or misaligned pointer (q 16-byte aligned, ld_q a multiple of 4)");
   wdl::sage::quant_q_launch(q, ld_q, nq, H, q_i8, q_scale, static_cast<cudaStream_t>(stream));
   return cuda_status(cudaGetLastError(), "sage quant_q launch");
 }
@@ -422,7 +441,9 @@ int wdl_sage_prep(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, 
     return fail(WDL_ERR_ARGUMENT, "null pointer");
   if (!work || work_bytes < wdl_sage_prep_workspace(at + n, H))
     return fail(WDL_ERR_ARGUMENT, "workspace of %zu bytes required", wdl_sage_prep_workspace(at + n, H));
-  if (!aligned(q_i8, 16) || !aligned(k_i8, 16) || !aligned(v_f8, 16)) return fail(WDL_ERR_ARGUMENT, "misaligned output");
+  if (!aligned(q_i8, 16) || !aligned(k_i8, 16) || !aligned(v_f8, 16) || !aligned(v_scale, 16) || !aligned(q, 16) ||
+      ld_q % 4 != 0 || !sage_sources_aligned(cache_k, cache_v, at, k, k_dtype, ld_k, v, v_dtype, ld_v, n))
+    return fail(WDL_ERR_ARGUMENT, "misaligned input or output");
   wdl::sage::PrepArgs a{};
   a.cache_k = cache_k, a.cache_ks = cache_ks, a.cache_v = cache_v, a.cache_vs = cache_vs, a.at = at;
   a.k_chunk = k, a.ld_k = ld_k, a.k_bf16 = k_dtype == WDL_BF16, a.v_chunk = v, a.ld_v = ld_v, a.v_bf16 = v_dtype == WDL_BF16;

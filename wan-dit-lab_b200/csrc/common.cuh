@@ -200,6 +200,17 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// x / s rounded to nearest even, given r = the correctly rounded reciprocal of s (__frcp_rn(s), computed once
+// for many x): Markstein's method (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Develop. 34(1), 1990): q = RN(x r), the remainder x - s q exact by one
+// FMA, q' = RN(q + rem r) is the correctly rounded quotient whenever no intermediate underflows or overflows.
+// Three instructions instead of a full IEEE division per element; tests check it equals __fdiv_rn.
+__device__ __forceinline__ float div_rn_by(float x, float s, float r) {
+  const float q = __fmul_rn(x, r);
+  const float rem = __fmaf_rn(-q, s, x);
+  return __fmaf_rn(rem, r, q);
+}
+
 // 2^x on the special function unit (PTX ex2.approx; -inf gives +0).
 __device__ __forceinline__ float ex2(float x) {
   float y;

@@ -6,7 +6,7 @@
 //    (time_in + modulation) (models/block.py:75-79, each product and sum rounded in float32), the cast to bf16
 //    of the linear layer that follows (PackedW4A4Linear.forward, quantization/w4a4.py:229-231), then that
 //    layer's activation quantization: division by its smoothing vector and symmetric INT4 groups of 64
-//    (scale = max(max|x|, 1e-8) / 7, round half to even, codes in the GEMM's operand format). One warp per row.
+//    (scale = max(max|x|, 1e-8) / 7, round half to even, codes in the GEMM's operand format). One CTA of 128 threads per row.
 //  * rms_rows — RMSNorm of rows (models/rms_norm.py:10-13): x * rsqrt(mean(x^2) + eps) rounded to bf16, times
 //    the float32 weight; the query norm of cross-attention (models/multi_head_attention.py:118).
 //  * modulation — (time_in + modulation) of every block at once (models/block.py:75): [blocks, 6, dim] fp32.
@@ -15,8 +15,6 @@
 
 namespace wdl {
 namespace norm {
-
-constexpr int kMaxChunks = 16;  // dim <= 16 * 256
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -43,51 +41,84 @@ __device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// One CTA of 128 threads per row: thread t holds channels c * 1024 + 8 t .. + 7 of every 1024-channel chunk c
+// (the last chunk may be partial: K % 256 == 0, so a group of 64 channels is wholly present or absent), so 8
+// consecutive threads hold one group of 64 (its max: 3 shuffles) and the row statistics are two CTA sums.
+constexpr int kRowThreads = 128;
+constexpr int kRowChunks = 4;  // K <= 4096
+
+__device__ __forceinline__ float block_sum128(float v, float* red) {
+  v = warp_sum(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return (red[0] + red[1]) + (red[2] + red[3]);
+}
+
+__device__ __forceinline__ uint32_t code_byte(int q, int fmt) {
+  return fmt == 1 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(static_cast<float>(q), __NV_SATFINITE, __NV_E4M3))
+                  : (static_cast<uint32_t>(q) & 0xFFu);
+}
+
 template <typename TX>
-__global__ void __launch_bounds__(256) ln_quant_kernel(const TX* __restrict__ x, LnQuantArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (m >= a.M) return;
-  const int K = a.K, chunks = K / 256;
+__global__ void __launch_bounds__(kRowThreads) ln_quant_kernel(const TX* __restrict__ x, LnQuantArgs a) {
+  __shared__ float red[kRowThreads / 32];
+  const int t = threadIdx.x, m = blockIdx.x;
+  const int K = a.K;
   const TX* row = x + static_cast<int64_t>(m) * a.ldx;
-  float v[kMaxChunks][8];
+  float v[kRowChunks][8];
   float s = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c)
-    if (c < chunks) {
-      load8<TX>(row + c * 256 + lane * 8, v[c]);
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int k = c * 1024 + t * 8;
+    if (k < K) {
+      load8<TX>(row + k, v[c]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) s += v[c][i];
     }
-  const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(K));
+  }
+  const float mean = __fdiv_rn(block_sum128(s, red), static_cast<float>(K));
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c)
-    if (c < chunks)
+  for (int c = 0; c < kRowChunks; ++c)
+    if (c * 1024 + t * 8 < K)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float d = v[c][i] - mean;
         ss = fmaf(d, d, ss);
       }
-  const float rstd = __frsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(ss), static_cast<float>(K)), a.eps));
+  const float rstd = __frsqrt_rn(__fadd_rn(__fdiv_rn(block_sum128(ss, red), static_cast<float>(K)), a.eps));
   uint8_t* codes = a.codes + static_cast<int64_t>(m) * K;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    if (c >= chunks) break;
-    const int k = c * 256 + lane * 8;
+  for (int c = 0; c < kRowChunks; ++c) {
+    if (c * 1024 >= K) break;  // uniform over the CTA
+    const int k = c * 1024 + t * 8;
+    const bool valid = k < K;  // uniform over each group of 8 threads
     float y[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float t = __fmul_rn(v[c][i] - mean, rstd);
-      if (a.ln_w) t = __fadd_rn(__fmul_rn(t, __ldg(a.ln_w + k + i)), __ldg(a.ln_b + k + i));
-      if (a.round_ln_bf16) t = bf16r(t);
-      if (a.mod_shift) {
-        const float one_plus = __fadd_rn(1.f, __ldg(a.mod_scale + k + i));
-        t = __fadd_rn(__fmul_rn(t, one_plus), __ldg(a.mod_shift + k + i));
+    if (valid) {
+      float w[8], b[8], sh[8], sc[8], sm[8];
+      if (a.ln_w) {
+        load8<float>(a.ln_w + k, w);
+        load8<float>(a.ln_b + k, b);
       }
-      t = bf16r(t);  // the linear layer's input is bf16
-      if (a.smooth) t = __fdiv_rn(t, __bfloat162float(a.smooth[k + i]));
-      y[i] = t;
+      if (a.mod_shift) {
+        load8<float>(a.mod_shift + k, sh);
+        load8<float>(a.mod_scale + k, sc);
+      }
+      if (a.smooth) load8<__nv_bfloat16>(a.smooth + k, sm);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float u = __fmul_rn(v[c][i] - mean, rstd);
+        if (a.ln_w) u = __fadd_rn(__fmul_rn(u, w[i]), b[i]);
+        if (a.round_ln_bf16) u = bf16r(u);
+        if (a.mod_shift) u = __fadd_rn(__fmul_rn(u, __fadd_rn(1.f, sc[i])), sh[i]);
+        u = bf16r(u);  // the linear layer's input is bf16
+        if (a.smooth) u = __fdiv_rn(u, sm[i]);
+        y[i] = u;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = 0.f;
     }
     float amax = 0.f;
 #pragma unroll
@@ -95,66 +126,68 @@ __global__ void __launch_bounds__(256) ln_quant_kernel(const TX* __restrict__ x,
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+    if (!valid) continue;
     const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
-    uint32_t w[2] = {0, 0};
+    const float r = __frcp_rn(scale);
+    uint32_t wd[2] = {0, 0};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int q = max(-8, min(7, __float2int_rn(__fdiv_rn(y[i], scale))));
-      const uint32_t byte = a.code_format == 1
-                                ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(static_cast<float>(q), __NV_SATFINITE, __NV_E4M3))
-                                : (static_cast<uint32_t>(q) & 0xFFu);
-      w[i / 4] |= byte << (8 * (i % 4));
+      const int q = max(-8, min(7, __float2int_rn(div_rn_by(y[i], scale, r))));
+      wd[i / 4] |= code_byte(q, a.code_format) << (8 * (i % 4));
     }
-    *reinterpret_cast<uint2*>(codes + k) = make_uint2(w[0], w[1]);
-    if ((lane & 7) == 0)
+    *reinterpret_cast<uint2*>(codes + k) = make_uint2(wd[0], wd[1]);
+    if ((t & 7) == 0)
       a.scales[static_cast<int64_t>(k / 64) * a.M + m] =
           a.scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16r(scale);
   }
 }
 
 void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s) {
-  const unsigned blocks = static_cast<unsigned>((static_cast<int64_t>(a.M) * 32 + 255) / 256);
+  if (a.M == 0) return;
   if (a.x_f32)
-    ln_quant_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(a.x), a);
+    ln_quant_kernel<float><<<a.M, kRowThreads, 0, s>>>(static_cast<const float*>(a.x), a);
   else
-    ln_quant_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a);
+    ln_quant_kernel<__nv_bfloat16><<<a.M, kRowThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a);
 }
 
-__global__ void __launch_bounds__(256) rms_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int M, int K,
-                                                       const float* __restrict__ w, float eps, float* __restrict__ out,
-                                                       int64_t ldo) {
-  const int lane = threadIdx.x & 31;
-  const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (m >= M) return;
-  const int chunks = K / 256;
+// Same thread layout as ln_quant: one CTA of 128 threads per row.
+__global__ void __launch_bounds__(kRowThreads) rms_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                               int K, const float* __restrict__ w, float eps,
+                                                               float* __restrict__ out, int64_t ldo) {
+  __shared__ float red[kRowThreads / 32];
+  const int t = threadIdx.x, m = blockIdx.x;
   const __nv_bfloat16* row = x + static_cast<int64_t>(m) * ldx;
-  float v[kMaxChunks][8];
+  float v[kRowChunks][8];
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c)
-    if (c < chunks) {
-      load8<__nv_bfloat16>(row + c * 256 + lane * 8, v[c]);
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int k = c * 1024 + t * 8;
+    if (k < K) {
+      load8<__nv_bfloat16>(row + k, v[c]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss = fmaf(v[c][i], v[c][i], ss);
     }
-  const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(ss), static_cast<float>(K)), eps));
+  }
+  const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(block_sum128(ss, red), static_cast<float>(K)), eps));
   float* o = out + static_cast<int64_t>(m) * ldo;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c)
-    if (c < chunks) {
-      const int k = c * 256 + lane * 8;
-      float y[8];
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int k = c * 1024 + t * 8;
+    if (k < K) {
+      float wk[8], y[8];
+      load8<float>(w + k, wk);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(bf16r(__fmul_rn(v[c][i], r)), __ldg(w + k + i));
+      for (int i = 0; i < 8; ++i) y[i] = __fmul_rn(bf16r(__fmul_rn(v[c][i], r)), wk[i]);
       *reinterpret_cast<float4*>(o + k) = make_float4(y[0], y[1], y[2], y[3]);
       *reinterpret_cast<float4*>(o + k + 4) = make_float4(y[4], y[5], y[6], y[7]);
     }
+  }
 }
 
 void rms_rows_launch(const __nv_bfloat16* x, int64_t ldx, int M, int K, const float* w, float eps, float* out,
                      int64_t ldo, cudaStream_t s) {
-  const unsigned blocks = static_cast<unsigned>((static_cast<int64_t>(M) * 32 + 255) / 256);
-  rms_rows_kernel<<<blocks, 256, 0, s>>>(x, ldx, M, K, w, eps, out, ldo);
+  if (M == 0) return;
+  rms_rows_kernel<<<M, kRowThreads, 0, s>>>(x, ldx, K, w, eps, out, ldo);
 }
 
 __global__ void modulation_kernel(const float* __restrict__ time_in, const float* __restrict__ modulation, int64_t n,

@@ -217,6 +217,15 @@ __device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, float (&v)[8]
   }
 }
 
+// 8 values / scale rounded to E4M3 (the division correctly rounded, Markstein's method), packed in 8 bytes.
+__device__ __forceinline__ uint2 e4m3x8(const float (&y)[8], float scale) {
+  const float r = __frcp_rn(scale);
+  uint32_t w[2] = {0, 0};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i / 4] |= static_cast<uint32_t>(e4m3(div_rn_by(y[i], scale, r))) << (8 * (i % 4));
+  return make_uint2(w[0], w[1]);
+}
+
 template <int kPasses>
 __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
   __shared__ float red[kPrepThreads / 32];
@@ -275,11 +284,7 @@ __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
         for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
         const float scale = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
         const int64_t crow = static_cast<int64_t>(a.at + t) * (dim / 128) + head;
-        uint2 q8;
-        q8.x = e4m3(__fdiv_rn(y[0], scale)) | (e4m3(__fdiv_rn(y[1], scale)) << 8) |
-               (e4m3(__fdiv_rn(y[2], scale)) << 16) | (static_cast<uint32_t>(e4m3(__fdiv_rn(y[3], scale))) << 24);
-        q8.y = e4m3(__fdiv_rn(y[4], scale)) | (e4m3(__fdiv_rn(y[5], scale)) << 8) |
-               (e4m3(__fdiv_rn(y[6], scale)) << 16) | (static_cast<uint32_t>(e4m3(__fdiv_rn(y[7], scale))) << 24);
+        const uint2 q8 = e4m3x8(y, scale);
         *reinterpret_cast<uint2*>(a.cache_k + crow * 128 + d0) = q8;
         if ((tid & 15) == 0) a.cache_ks[crow] = scale;
       }
@@ -300,11 +305,7 @@ __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
       for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
       const float scale = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
       const int64_t crow = static_cast<int64_t>(a.at + t) * (dim / 128) + head;
-      uint2 q8;
-      q8.x = e4m3(__fdiv_rn(y[0], scale)) | (e4m3(__fdiv_rn(y[1], scale)) << 8) |
-             (e4m3(__fdiv_rn(y[2], scale)) << 16) | (static_cast<uint32_t>(e4m3(__fdiv_rn(y[3], scale))) << 24);
-      q8.y = e4m3(__fdiv_rn(y[4], scale)) | (e4m3(__fdiv_rn(y[5], scale)) << 8) |
-             (e4m3(__fdiv_rn(y[6], scale)) << 16) | (static_cast<uint32_t>(e4m3(__fdiv_rn(y[7], scale))) << 24);
+      const uint2 q8 = e4m3x8(y, scale);
       *reinterpret_cast<uint2*>(a.cache_v + crow * 128 + d0) = q8;
       if ((tid & 15) == 0) a.cache_vs[crow] = scale;
     }

@@ -21,13 +21,9 @@ __device__ __forceinline__ uint8_t e4m3(float x) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
 }
 
-__device__ __forceinline__ float e4m3_value(uint8_t b) {
-  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
-  return __half2float(__half(h));
-}
-
-// Token j of head h, channel d, as _load of sage_kv.py:29-40 reads it: the cache byte times its scale before
-// `at`, the chunk's value after.
+// Channels d .. d + 3 (d % 4 == 0) of token j of head h, as _load of sage_kv.py:29-40 reads them: the cache
+// bytes times their scale before `at`, the chunk's values after. One 32-bit load of four E4M3 bytes (decoded two
+// at a time through f16x2, exactly), or one 16-byte / 8-byte load of four float32 / bf16 values.
 struct Source {
   const uint8_t* cache;  // [cap, H, 128]
   const float* scale;    // [cap, H]
@@ -35,24 +31,53 @@ struct Source {
   int64_t ld;
   int chunk_bf16;
   int at, L, H;
-  __device__ __forceinline__ float get(int j, int h, int d) const {
-    if (j < at) return e4m3_value(cache[(static_cast<int64_t>(j) * H + h) * 128 + d]) * scale[static_cast<int64_t>(j) * H + h];
+  __device__ __forceinline__ void get4(int j, int h, int d, float (&o)[4]) const {
+    if (j < at) {
+      const int64_t r = static_cast<int64_t>(j) * H + h;
+      const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(cache + r * 128 + d));
+      const float s = __ldg(scale + r);
+      const __half2 lo(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w & 0xFFFFu), __NV_E4M3));
+      const __half2 hi(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w >> 16), __NV_E4M3));
+      const float2 a = __half22float2(lo), b = __half22float2(hi);
+      o[0] = a.x * s, o[1] = a.y * s, o[2] = b.x * s, o[3] = b.y * s;
+      return;
+    }
     const int64_t off = static_cast<int64_t>(j - at) * ld + h * 128 + d;
-    return chunk_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(chunk)[off]) : static_cast<const float*>(chunk)[off];
+    if (chunk_bf16) {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(chunk) + off));
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+      o[0] = a.x, o[1] = a.y, o[2] = b.x, o[3] = b.y;
+    } else {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(chunk) + off));
+      o[0] = f.x, o[1] = f.y, o[2] = f.z, o[3] = f.w;
+    }
   }
 };
 
-// ---- pass 1: per (64-token tile, head), per channel: sum of K and max |V| over the tile (thread = channel)
+// ---- pass 1: per (64-token tile, head), per channel: sum of K and max |V| over the tile. Warp w reads the 16
+// tokens 16 w .. 16 w + 15 of the tile, lane l channels 4 l .. 4 l + 3 (one 128-byte row segment per token);
+// the four warps' partials meet in shared memory.
 __global__ void __launch_bounds__(128) partials_kernel(Source ks, Source vs, float* ksum, float* vmax) {
-  const int tile = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
-  float s = 0.f, m = 0.f;
-  const int j0 = tile * 64, j1 = min(ks.L, j0 + 64);
+  __shared__ float red[2][4][128];
+  const int tile = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float s[4] = {0.f, 0.f, 0.f, 0.f}, m[4] = {0.f, 0.f, 0.f, 0.f};
+  const int j0 = tile * 64 + warp * 16, j1 = min(ks.L, j0 + 16);
   for (int j = j0; j < j1; ++j) {
-    s += ks.get(j, h, d);
-    m = fmaxf(m, fabsf(vs.get(j, h, d)));
+    float k[4], v[4];
+    ks.get4(j, h, lane * 4, k);
+    vs.get4(j, h, lane * 4, v);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) s[c] += k[c], m[c] = fmaxf(m[c], fabsf(v[c]));
   }
-  ksum[(static_cast<int64_t>(tile) * ks.H + h) * 128 + d] = s;
-  vmax[(static_cast<int64_t>(tile) * ks.H + h) * 128 + d] = m;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) red[0][warp][lane * 4 + c] = s[c], red[1][warp][lane * 4 + c] = m[c];
+  __syncthreads();
+  const int d = threadIdx.x;
+  const int64_t o = (static_cast<int64_t>(tile) * ks.H + h) * 128 + d;
+  ksum[o] = (red[0][0][d] + red[0][1][d]) + (red[0][2][d] + red[0][3][d]);
+  vmax[o] = fmaxf(fmaxf(red[1][0][d], red[1][1][d]), fmaxf(red[1][2][d], red[1][3][d]));
 }
 
 // ---- pass 2: per head: key mean (sum / L) and the V channel scales max(max|V|, 1e-8) / 2.25 (V_MAX, :24)
@@ -68,20 +93,29 @@ __global__ void __launch_bounds__(128) reduce_kernel(const float* ksum, const fl
   v_scale[h * 128 + d] = __fdiv_rn(fmaxf(m, 1e-8f), 2.25f);
 }
 
+// Sage's INT8 rounding: trunc(y + 0.5 sign(y)) with y = x / scale (the division correctly rounded).
+__device__ __forceinline__ uint32_t sage_i8(float x, float scale, float rcp) {
+  const float y = div_rn_by(x, scale, rcp);
+  return static_cast<uint32_t>(static_cast<int>(truncf(__fadd_rn(y, y >= 0.f ? 0.5f : -0.5f)))) & 0xFFu;
+}
+
 // ---- pass 3: K - mean to INT8 and V to FP8, per (64-key block, head). 128 threads.
 // K (_quant_k, sage_kv.py:60-85): warp g holds the 16 keys 8 i + 2 g, 8 i + 2 g + 1 (i = 0..7) of the block,
 // lane l channels 4 l .. 4 l + 3; scale = max|x| / 127 + 1e-7 over the 16 x 128 values; code = trunc(x / scale
-// + 0.5 sign(x)). V (_quant_v, :89-105): thread = channel d, V / v_scale[d] rounded to E4M3, stored transposed.
+// + 0.5 sign(x)). V (_quant_v, :89-105): warp g keys 16 g .. 16 g + 15, lane l channels 4 l .. 4 l + 3, each
+// V / v_scale[d] rounded to E4M3; the codes are transposed through shared memory (each lane packs its 16 keys
+// of a channel into one 16-byte store) and leave as one 64-byte row segment per channel.
+constexpr int kVtPitch = 80;  // bytes per channel row of the transpose tile: 16-byte aligned, reads conflict-free
+
 __global__ void __launch_bounds__(128) quant_kv_kernel(Source ks, Source vs, const float* kmean, const float* v_scale,
                                                        int Lpad, int8_t* k_i8, float* k_scale, uint8_t* v_f8) {
+  __shared__ __align__(16) uint8_t vt[128 * kVtPitch];
   const int blk = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L = ks.L;
   {
     const int g = warp;
-    float mean[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) mean[c] = kmean[h * 128 + lane * 4 + c];
+    const float4 mean = *reinterpret_cast<const float4*>(kmean + h * 128 + lane * 4);
     float x[16][4];
     float amax = 0.f;
 #pragma unroll
@@ -89,52 +123,66 @@ __global__ void __launch_bounds__(128) quant_kv_kernel(Source ks, Source vs, con
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int j = blk * 64 + 8 * i + 2 * g + e;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float v = j < L ? __fsub_rn(ks.get(j, h, lane * 4 + c), mean[c]) : 0.f;
-          x[2 * i + e][c] = v;
-          amax = fmaxf(amax, fabsf(v));
+        float* r = x[2 * i + e];
+        if (j < L) {
+          ks.get4(j, h, lane * 4, x[2 * i + e]);
+          r[0] = __fsub_rn(r[0], mean.x), r[1] = __fsub_rn(r[1], mean.y);
+          r[2] = __fsub_rn(r[2], mean.z), r[3] = __fsub_rn(r[3], mean.w);
+        } else {
+          r[0] = r[1] = r[2] = r[3] = 0.f;
         }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) amax = fmaxf(amax, fabsf(r[c]));
       }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
     const float scale = __fadd_rn(__fdiv_rn(amax, 127.f), 1e-7f);
+    const float rcp = __frcp_rn(scale);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int j = blk * 64 + 8 * i + 2 * g + e;
         uint32_t packed = 0;
+        if (j < L)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float y = __fdiv_rn(x[2 * i + e][c], scale);
-          const int q = j < L ? static_cast<int>(truncf(__fadd_rn(y, y >= 0.f ? 0.5f : -0.5f))) : 0;
-          packed |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * c);
-        }
+          for (int c = 0; c < 4; ++c) packed |= sage_i8(x[2 * i + e][c], scale, rcp) << (8 * c);
         *reinterpret_cast<uint32_t*>(k_i8 + (static_cast<int64_t>(h) * Lpad + j) * 128 + lane * 4) = packed;
       }
     if (lane == 0) k_scale[static_cast<int64_t>(h) * (Lpad / 64) * 4 + blk * 4 + g] = scale;
   }
   {
-    const int d = threadIdx.x;
-    const float s = v_scale[h * 128 + d];
-    uint8_t* row = v_f8 + (static_cast<int64_t>(h) * 128 + d) * Lpad + blk * 64;
+    const int g = warp;
+    const float4 sv = *reinterpret_cast<const float4*>(v_scale + h * 128 + lane * 4);
+    const float s[4] = {sv.x, sv.y, sv.z, sv.w};
+    float rcp[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t w[4];
+    for (int c = 0; c < 4; ++c) rcp[c] = __frcp_rn(s[c]);
+    uint32_t w[4][4];  // [channel c][key word]: keys 16 g + 4 kw .. + 3 of channel 4 lane + c
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        uint32_t word = 0;
+    for (int kw = 0; kw < 4; ++kw) {
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const int j = blk * 64 + q * 16 + k * 4 + b;
-          const uint8_t byte = j < L ? e4m3(__fdiv_rn(vs.get(j, h, d), s)) : 0;
-          word |= static_cast<uint32_t>(byte) << (8 * b);
+      for (int c = 0; c < 4; ++c) w[c][kw] = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int j = blk * 64 + g * 16 + kw * 4 + b;
+        if (j < L) {
+          float v[4];
+          vs.get4(j, h, lane * 4, v);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) w[c][kw] |= static_cast<uint32_t>(e4m3(div_rn_by(v[c], s[c], rcp[c]))) << (8 * b);
         }
-        w[k] = word;
       }
-      *reinterpret_cast<uint4*>(row + q * 16) = make_uint4(w[0], w[1], w[2], w[3]);
     }
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(vt + (lane * 4 + c) * kVtPitch + g * 16) = make_uint4(w[c][0], w[c][1], w[c][2], w[c][3]);
+    __syncthreads();
+    const int d = threadIdx.x;
+    const uint4* src = reinterpret_cast<const uint4*>(vt + d * kVtPitch);
+    uint4* dst = reinterpret_cast<uint4*>(v_f8 + (static_cast<int64_t>(h) * 128 + d) * Lpad + blk * 64);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[q] = src[q];
   }
 }
 
@@ -149,26 +197,28 @@ __global__ void __launch_bounds__(128) quant_q_kernel(const float* q, int64_t ld
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int t = blk * 32 + r * 8 + l;
-    const float* src = q + static_cast<int64_t>(t) * ldq + h * 128 + c * 8;
+    if (t < n) {
+      const float4* src = reinterpret_cast<const float4*>(q + static_cast<int64_t>(t) * ldq + h * 128 + c * 8);
+      const float4 a = __ldg(src), b = __ldg(src + 1);
+      x[r][0] = a.x, x[r][1] = a.y, x[r][2] = a.z, x[r][3] = a.w;
+      x[r][4] = b.x, x[r][5] = b.y, x[r][6] = b.z, x[r][7] = b.w;
+    } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      x[r][i] = t < n ? src[i] : 0.f;
-      amax = fmaxf(amax, fabsf(x[r][i]));
+      for (int i = 0; i < 8; ++i) x[r][i] = 0.f;
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[r][i]));
   }
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
   const float scale = __fadd_rn(__fdiv_rn(amax, 127.f), 1e-7f);
+  const float rcp = __frcp_rn(scale);
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int t = blk * 32 + r * 8 + l;
     uint32_t w[2] = {0, 0};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float y = __fdiv_rn(x[r][i], scale);
-      const int qv = static_cast<int>(truncf(__fadd_rn(y, y >= 0.f ? 0.5f : -0.5f)));
-      w[i / 4] |= (static_cast<uint32_t>(qv) & 0xFFu) << (8 * (i % 4));
-    }
+    for (int i = 0; i < 8; ++i) w[i / 4] |= sage_i8(x[r][i], scale, rcp) << (8 * (i % 4));
     *reinterpret_cast<uint2*>(q_i8 + (static_cast<int64_t>(h) * npad + t) * 128 + c * 8) = make_uint2(w[0], w[1]);
   }
   if (c == 0) q_scale[static_cast<int64_t>(h) * (npad / 32) * 8 + blk * 8 + l] = scale;

@@ -305,6 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             amax = fmaxf(amax, fabsf(t));
           }
           const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 15.f);
+          const float rcp = __frcp_rn(scale);
 #pragma unroll
           for (int j = 0; j < 64; j += 16) {
             uint32_t w[4];
@@ -313,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t word = 0;
 #pragma unroll
               for (int b = 0; b < 4; ++b) {
-                const int q = max(0, min(15, __float2int_rn(__fdiv_rn(u[j + e * 4 + b], scale))));
+                const int q = max(0, min(15, __float2int_rn(div_rn_by(u[j + e * 4 + b], scale, rcp))));
                 word |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(static_cast<float>(q), __NV_SATFINITE, __NV_E4M3))
                         << (8 * b);
               }
@@ -366,7 +367,7 @@ static bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void*
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-int gemm_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
+int gemm_validate(const GemmArgs& a, const char** why) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) {
     *why = "M, N and K must be positive";
     return 1;
@@ -384,6 +385,11 @@ int gemm_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
     *why = "operand pointers must be 16-byte aligned";
     return 1;
   }
+  return 0;
+}
+
+int gemm_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
+  if (gemm_validate(a, why) != 0) return 1;
   CUtensorMap ma, mb, mw;
   if (!make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.a, a.K, a.M, a.lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.b, a.K, a.N, a.ldb, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||

@@ -60,6 +60,8 @@ struct GemmArgs {
 };
 
 // Validates and launches; returns 0, or a nonzero status with *why set.
+// Shape and alignment checks of gemm_launch alone (no CUDA call): 0, or 1 with *why set.
+int gemm_validate(const GemmArgs& a, const char** why);
 int gemm_launch(const GemmArgs& args, cudaStream_t stream, const char** why);
 
 }  // namespace w4a4

@@ -87,9 +87,10 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
     if (!valid) continue;
     const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
+    const float r = __frcp_rn(scale);
     int q[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = max(-8, min(7, __float2int_rn(__fdiv_rn(v[i], scale))));
+    for (int i = 0; i < 8; ++i) q[i] = max(-8, min(7, __float2int_rn(div_rn_by(v[i], scale, r))));
     uint2 c;
     c.x = code_byte<kE4M3>(q[0]) | (code_byte<kE4M3>(q[1]) << 8) | (code_byte<kE4M3>(q[2]) << 16) |
           (code_byte<kE4M3>(q[3]) << 24);
