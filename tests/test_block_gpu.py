@@ -85,3 +85,35 @@ def test_block_matches_oracle(dim, heads, ffn, frames, h, w, at, text):
         rows = gpu[at:at + n].cpu().numpy()
         assert (rows == ocache[name][0, at:at + n]).mean() > 0.99
     assert not torch.equal(cache[0][:at].cpu(), torch.zeros_like(cache[0][:at].cpu()))
+
+
+def test_block_scale_products_on_tensor_cores_bit_identical():
+    """The block with the padded-scale code format (the group-scale products formed by a tf32 MMA) gives the same
+    bits as with the E4M3 format (products formed on the CUDA cores): residual stream, hidden codes and scales."""
+    from wan_dit_lab_b200.models.block import Buffers, WanBlockB200
+    from wan_dit_lab_b200 import _native
+    dim, heads, ffn, frames, h, w, at, text = 1024, 8, 4096, 2, 4, 8, 128, 32
+    n = frames * h * w
+    state = random_state(dim, ffn, 3)
+    g = torch.Generator().manual_seed(4)
+    X = torch.randn(n, dim, generator=g)
+    time_in = torch.randn(6, dim, generator=g) * 0.1
+    ctx = (torch.randn(text, dim, generator=g)).to(torch.bfloat16)
+    cap = at + n + 16
+    ck8, cks = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    cv8, cvs = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    freq = torch.from_numpy(orope.table(1024).astype(np.float32)).cuda()
+    outs = {}
+    for fmt in ("e4m3", "e4m3ts"):
+        blk = WanBlockB200(state, dim, ffn, heads, code_format=fmt)
+        cache = (torch.from_numpy(ck8[0]).cuda(), torch.from_numpy(cks[0, ..., 0]).cuda(),
+                 torch.from_numpy(cv8[0]).cuda(), torch.from_numpy(cvs[0, ..., 0]).cuda(), cap)
+        buf = Buffers(n, dim, ffn, heads, at + n, text, "cuda")
+        Xd = X.cuda()
+        trace = {}
+        blk.forward(Xd, blk.modulation_of(time_in.cuda()), cache, at, freq, (frames, h, w), at // (h * w),
+                    blk.cross_kv(ctx.cuda()), buf, trace=trace)
+        assert _native.device_error() == 0
+        outs[fmt] = (Xd.cpu(), trace["hcodes"].cpu(), trace["hscales"].cpu(), cache[0].cpu())
+    for a, b in zip(outs["e4m3"], outs["e4m3ts"]):
+        assert torch.equal(a, b)

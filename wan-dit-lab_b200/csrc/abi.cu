@@ -115,7 +115,10 @@ int wdl_device_error(void* stream, uint32_t* code) {
   return ok();
 }
 
-static bool valid_codes(int f) { return f == WDL_CODES_INT8 || f == WDL_CODES_E4M3; }
+static bool valid_codes(int f) { return f == WDL_CODES_INT8 || f == WDL_CODES_E4M3 || f == WDL_CODES_E4M3_TS; }
+
+// Scale arrays of the padded format hold 16-byte entries read by TMA.
+static bool scales_aligned(const void* p, int code_format) { return aligned(p, code_format == WDL_CODES_E4M3_TS ? 16 : 4); }
 
 int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16_t* smooth, int M, int K,
                            int scale_dtype, int code_format, void* codes, float* scales, uint8_t* packed,
@@ -129,7 +132,8 @@ int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16
   if (M == 0) return ok();
   if (!x || !codes || !scales) return fail(WDL_ERR_ARGUMENT, "x, codes and scales must not be null");
   if (!aligned(x, 16) || (ldx * esize) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "x rows must be 16-byte aligned");
-  if (!aligned(codes, 8) || !aligned(scales, 4) || (packed && !aligned(packed, 4)) || (smooth && !aligned(smooth, 16)))
+  if (!aligned(codes, 8) || !scales_aligned(scales, code_format) || (packed && !aligned(packed, 4)) ||
+      (smooth && !aligned(smooth, 16)))
     return fail(WDL_ERR_ARGUMENT, "misaligned output or smooth pointer");
   wdl::w4a4::quantize_rows_launch(x, x_dtype, ldx, smooth, M, K, scale_dtype, code_format,
                                   static_cast<int8_t*>(codes), scales, packed, static_cast<cudaStream_t>(stream));
@@ -142,7 +146,7 @@ int wdl_w4a4_unpack_weight(const uint8_t* qweight, const void* wscales, int scal
   if (N <= 0 || K <= 0 || K % 64 != 0) return fail(WDL_ERR_ARGUMENT, "N > 0 and K a positive multiple of 64 required");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
   if (!qweight || !wscales || !codes || !scales) return fail(WDL_ERR_ARGUMENT, "null pointer");
-  if (!aligned(qweight, 4) || !aligned(codes, 8) || !aligned(wscales, 2) || !aligned(scales, 4))
+  if (!aligned(qweight, 4) || !aligned(codes, 8) || !aligned(wscales, 2) || !scales_aligned(scales, code_format))
     return fail(WDL_ERR_ARGUMENT, "misaligned pointer");
   wdl::w4a4::unpack_weight_launch(qweight, static_cast<const uint16_t*>(wscales), scale_dtype, N, K, code_format,
                                   static_cast<int8_t*>(codes), scales, static_cast<cudaStream_t>(stream));
@@ -156,11 +160,14 @@ static int gemm_common(wdl::w4a4::GemmArgs& a, void* stream) {
   if (!a.a || !a.b || !a.wscale || !a.ep.ascale || !a.ep.out) return fail(WDL_ERR_ARGUMENT, "null operand pointer");
   if (!aligned(a.ep.out, 16) || (a.ep.residual && !aligned(a.ep.residual, 16)))
     return fail(WDL_ERR_ARGUMENT, "output and residual must be 16-byte aligned");
+  const bool ts = a.code_format == WDL_CODES_E4M3_TS;
   const char* why = "";
-  if (wdl::w4a4::gemm_validate(a, &why) != 0) return fail(WDL_ERR_ARGUMENT, "%s", why);
+  if ((ts ? wdl::w4a4::gemm_ts_validate(a, &why) : wdl::w4a4::gemm_validate(a, &why)) != 0)
+    return fail(WDL_ERR_ARGUMENT, "%s", why);
   a.err = error_word();
   if (!a.err) return fail(WDL_ERR_CUDA, "cannot resolve the device error word");
-  const int st = wdl::w4a4::gemm_launch(a, static_cast<cudaStream_t>(stream), &why);
+  const int st = ts ? wdl::w4a4::gemm_ts_launch(a, static_cast<cudaStream_t>(stream), &why)
+                    : wdl::w4a4::gemm_launch(a, static_cast<cudaStream_t>(stream), &why);
   if (st == 1) return fail(WDL_ERR_ARGUMENT, "%s", why);
   if (st != 0) return fail(WDL_ERR_CUDA, "%s", why);
   return ok();
@@ -214,7 +221,8 @@ int wdl_w4a4_gemm_group_partials(const void* a, const float* a_scales, const voi
 int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                           const float* bias, const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N,
                           int K, uint8_t* codes, int64_t ldc, float* scales, void* stream) {
-  if (code_format != WDL_CODES_E4M3) return fail(WDL_ERR_ARGUMENT, "the unsigned hidden codes need the E4M3 code format");
+  if (code_format != WDL_CODES_E4M3 && code_format != WDL_CODES_E4M3_TS)
+    return fail(WDL_ERR_ARGUMENT, "the unsigned hidden codes need an E4M3 code format");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
   if (ldc < N || ldc % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldc must be >= N and a multiple of 16");
   if (!scales) return fail(WDL_ERR_ARGUMENT, "null scales");
@@ -229,7 +237,7 @@ int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, c
 size_t wdl_w4a4_linear_workspace(int M, int K) {
   if (M <= 0 || K <= 0) return 0;
   const size_t codes = (static_cast<size_t>(M) * K + 255) / 256 * 256;
-  const size_t scales = static_cast<size_t>(K / 64) * M * 4;
+  const size_t scales = static_cast<size_t>(K / 64) * M * 16;  // room for the padded scales of WDL_CODES_E4M3_TS
   return codes + scales;
 }
 
@@ -238,7 +246,8 @@ int wdl_w4a4_linear(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t
                     int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
   if (M < 0) return fail(WDL_ERR_ARGUMENT, "M must be >= 0");
   if (M == 0) return ok();
-  if (K % 128 != 0 || N % 256 != 0) return fail(WDL_ERR_ARGUMENT, "K % 128 == 0 and N % 256 == 0 required");
+  if (K % 128 != 0 || N % (code_format == WDL_CODES_E4M3_TS ? 128 : 256) != 0)
+    return fail(WDL_ERR_ARGUMENT, "K % 128 == 0 and N % 256 == 0 (N % 128 == 0 with padded scales) required");
   if (ldy < N || (ldy * 2) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldy must be >= N with 16-byte aligned rows");
   if (!valid_codes(code_format)) return fail(WDL_ERR_ARGUMENT, "unknown code format %d", code_format);
   const size_t need = wdl_w4a4_linear_workspace(M, K);
@@ -343,7 +352,8 @@ int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float ep
   if (!valid_codes(code_format) || (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16))
     return fail(WDL_ERR_ARGUMENT, "invalid code format or scale dtype");
   if (M == 0) return ok();
-  if (!codes || !scales || !aligned(codes, 8)) return fail(WDL_ERR_ARGUMENT, "null or misaligned output");
+  if (!codes || !scales || !aligned(codes, 8) || !scales_aligned(scales, code_format))
+    return fail(WDL_ERR_ARGUMENT, "null or misaligned output");
   if (!aligned(ln_w, 16) || !aligned(ln_b, 16) || !aligned(mod_shift, 16) || !aligned(mod_scale, 16) ||
       !aligned(smooth, 16))
     return fail(WDL_ERR_ARGUMENT, "ln_w, ln_b, mod_shift, mod_scale and smooth must be 16-byte aligned");

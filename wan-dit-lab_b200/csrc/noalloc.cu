@@ -65,8 +65,10 @@ int wdl_w4a4_linear_noalloc(const uint16_t* x, int64_t ldx, int M, int K, const 
                             uint16_t* y, int64_t ldy, void* stream) {
   if (M < 0) return fail(WDL_ERR_ARGUMENT, "M must be >= 0");
   if (M == 0) return wdl::set_last_error(WDL_OK, "");
-  if (K <= 0 || K % 128 != 0 || N <= 0 || N % 256 != 0) return fail(WDL_ERR_ARGUMENT, "K % 128 == 0 and N % 256 == 0 required");
-  if (code_format != WDL_CODES_INT8 && code_format != WDL_CODES_E4M3) return fail(WDL_ERR_ARGUMENT, "unknown code format");
+  if (K <= 0 || K % 128 != 0 || N <= 0 || N % (code_format == WDL_CODES_E4M3_TS ? 128 : 256) != 0)
+    return fail(WDL_ERR_ARGUMENT, "K % 128 == 0 and N % 256 == 0 (N % 128 == 0 with padded scales) required");
+  if (code_format != WDL_CODES_INT8 && code_format != WDL_CODES_E4M3 && code_format != WDL_CODES_E4M3_TS)
+    return fail(WDL_ERR_ARGUMENT, "unknown code format");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
   if (ldx < K || (ldx * 2) % 16 != 0 || ldy < N || (ldy * 2) % 16 != 0)
     return fail(WDL_ERR_ARGUMENT, "ldx >= K and ldy >= N with 16-byte aligned rows required");
@@ -74,10 +76,12 @@ int wdl_w4a4_linear_noalloc(const uint16_t* x, int64_t ldx, int M, int K, const 
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15)
     return fail(WDL_ERR_ARGUMENT, "x, w and y must be 16-byte aligned");
   const size_t codes_bytes = (static_cast<size_t>(M) * K + 255) / 256 * 256;
-  const size_t need = codes_bytes + static_cast<size_t>(K / 64) * M * sizeof(float);
+  const size_t scale_bytes = code_format == WDL_CODES_E4M3_TS ? 16 : sizeof(float);  // padded (s, 0, 0, 0)
+  const size_t need = codes_bytes + static_cast<size_t>(K / 64) * M * scale_bytes;
   if (need > kScratchBytes)
     return fail(WDL_ERR_ARGUMENT,
-                "wdl_w4a4_linear_noalloc: M * K too large for its fixed 16 MiB scratch (needs M * K * 17 / 16 bytes); "
+                "wdl_w4a4_linear_noalloc: M * K too large for its fixed 16 MiB scratch (needs M * K * 17 / 16 bytes, "
+                "M * K * 5 / 4 with padded scales); "
                 "use wdl_w4a4_linear with a caller workspace");
   void* scratch = nullptr;
   const int st = scratch_address(&scratch);
@@ -95,7 +99,8 @@ int wdl_w4a4_linear_noalloc(const uint16_t* x, int64_t ldx, int M, int K, const 
   g.a_signed = 1u, g.code_format = code_format, g.err = err;
   g.ep.mode = wdl::w4a4::kEpiBf16, g.ep.ascale = scales, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = ldy;
   const char* why = "";
-  const int gs = wdl::w4a4::gemm_launch(g, s, &why);
+  const int gs = code_format == WDL_CODES_E4M3_TS ? wdl::w4a4::gemm_ts_launch(g, s, &why)
+                                                   : wdl::w4a4::gemm_launch(g, s, &why);
   if (gs == 1) return fail(WDL_ERR_ARGUMENT, why);
   if (gs != 0) return fail(WDL_ERR_CUDA, why);
   return wdl::set_last_error(WDL_OK, "");

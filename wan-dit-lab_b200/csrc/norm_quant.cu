@@ -56,7 +56,7 @@ __device__ __forceinline__ float block_sum128(float v, float* red) {
 }
 
 __device__ __forceinline__ uint32_t code_byte(int q, int fmt) {
-  return fmt == 1 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(static_cast<float>(q), __NV_SATFINITE, __NV_E4M3))
+  return fmt != 0 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(static_cast<float>(q), __NV_SATFINITE, __NV_E4M3))
                   : (static_cast<uint32_t>(q) & 0xFFu);
 }
 
@@ -136,9 +136,14 @@ __global__ void __launch_bounds__(kRowThreads) ln_quant_kernel(const TX* __restr
       wd[i / 4] |= code_byte(q, a.code_format) << (8 * (i % 4));
     }
     *reinterpret_cast<uint2*>(codes + k) = make_uint2(wd[0], wd[1]);
-    if ((t & 7) == 0)
-      a.scales[static_cast<int64_t>(k / 64) * a.M + m] =
-          a.scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16r(scale);
+    if ((t & 7) == 0) {
+      const float stored = a.scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16r(scale);
+      const int64_t i = static_cast<int64_t>(k / 64) * a.M + m;
+      if (a.code_format == 2)  // padded (s, 0, 0, 0) for the tensor-core scale product
+        *reinterpret_cast<float4*>(a.scales + i * 4) = make_float4(stored, 0.f, 0.f, 0.f);
+      else
+        a.scales[i] = stored;
+    }
   }
 }
 

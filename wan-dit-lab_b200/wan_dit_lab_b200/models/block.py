@@ -43,9 +43,9 @@ class Buffers:
         bf = dict(dtype=torch.bfloat16, device=device)
         width = max(dim, ffn_dim)
         self.codes = torch.empty(n, width, **u8)
-        self.scales = torch.empty(width // 64, n, **f32)
+        self.scales = torch.empty(width // 64, n, 4, **f32)  # room for the padded scales of "e4m3ts"
         self.hcodes = torch.empty(n, ffn_dim, **u8)
-        self.hscales = torch.empty(ffn_dim // 64, n, **f32)
+        self.hscales = torch.empty(ffn_dim // 64, n, 4, **f32)
         self.qkv = torch.empty(n, 3 * dim, **bf)
         self.q = torch.empty(n, dim, **f32)
         self.k = torch.empty(n, dim, **f32)
@@ -218,7 +218,11 @@ class WanBlockB200:
             buf.codes.data_ptr(), buf.scales.data_ptr(), fc1.codes.data_ptr(), fc1.scales.data_ptr(), fmt,
             _native.ptr(fc1.bias), _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N, fc1.K, buf.hcodes.data_ptr(),
             buf.hcodes.stride(0), buf.hscales.data_ptr(), st)))
-        keep("hcodes", buf.hcodes), keep("hscales", buf.hscales)
+        keep("hcodes", buf.hcodes)
+        if trace is not None:  # the hidden scales [ffn / 64, n] as the GEMM reads them (padded: element 0 of 4)
+            G = buf.hscales.shape[0]
+            keep("hscales", buf.hscales[..., 0] if fmt == _native.CODES_E4M3_TS
+                 else buf.hscales.view(-1)[:G * n].view(G, n))
         gemm_residual(fc2, 5, buf.hcodes, buf.hscales)
         return X
 

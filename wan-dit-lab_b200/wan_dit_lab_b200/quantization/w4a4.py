@@ -20,8 +20,10 @@ from wan_dit_lab_b200 import _native
 
 GROUP = 64  # input channels per INT4 scale (reference w4a4.py:29)
 # How the GEMM's operands hold the 4-bit codes in HBM, one per byte: E4M3 (the code's value as an FP8 number,
-# tcgen05 kind::f8f6f4, float32 group partials) or int8 (kind::i8, int32 partials). Both exact; E4M3 spares
-# the promotion an int-to-float conversion per accumulator element and group.
+# tcgen05 kind::f8f6f4, float32 group partials) or int8 (kind::i8, int32 partials). All exact; E4M3 spares
+# the promotion an int-to-float conversion per accumulator element and group. "e4m3ts" keeps E4M3 codes and
+# stores each group scale padded to 16 bytes (s, 0, 0, 0), so that the GEMM forms the scale products on the
+# tensor cores too (same results bit for bit, one CUDA-core operation per element and group instead of two).
 CODE_FORMAT = "e4m3"
 GELU_SHIFT = 0.171875  # GELU(x) + GELU_SHIFT >= 0: the hidden layer of gelu_mlp is quantized unsigned (w4a4.py:195)
 PARTS = ("qweight", "wscales", "proj_down", "proj_up", "smooth", "bias")  # w4a4.py:207
@@ -40,13 +42,19 @@ def _scale_code(dtype):
 
 
 def _code_format(name):
-    return {"e4m3": _native.CODES_E4M3, "int8": _native.CODES_INT8}[name]
+    return {"e4m3": _native.CODES_E4M3, "int8": _native.CODES_INT8, "e4m3ts": _native.CODES_E4M3_TS}[name]
+
+
+def scale_shape(groups, rows, code_format):
+    """Shape of a [groups, rows] scale array in the given code format (padded to 4 float32 for "e4m3ts")."""
+    return (groups, rows, 4) if _code_format(code_format) == _native.CODES_E4M3_TS else (groups, rows)
 
 
 def quantize_rows(x, scale_dtype=torch.bfloat16, smooth=None, packed=False, code_format="int8"):
     """Rows of x [M, K] (bfloat16 or float32, CUDA) in symmetric INT4 groups of GROUP: codes [M, K] int8, scales
     [K / GROUP, M] float32 (holding values rounded to scale_dtype) and, with packed, the nibbles [M, K / 2] uint8.
-    code_format "int8" gives the codes as int8 integers, "e4m3" as the GEMM's E4M3 bytes (a uint8 tensor).
+    code_format "int8" gives the codes as int8 integers, "e4m3" as the GEMM's E4M3 bytes (a uint8 tensor),
+    "e4m3ts" E4M3 bytes with scales [K / GROUP, M, 4] holding (s, 0, 0, 0).
     scale = max(max|x_g|, 1e-8) / 7, code = round-half-even(x / scale) clamped to [-8, 7] (the rule of
     int4_groups, reference w4a4.py:86-100); smooth [K] bfloat16 divides x first."""
     _cuda(x, "x")
@@ -58,7 +66,7 @@ def quantize_rows(x, scale_dtype=torch.bfloat16, smooth=None, packed=False, code
         x = x.contiguous()
     M, K = x.shape
     codes = torch.empty(M, K, dtype=torch.int8 if code_format == "int8" else torch.uint8, device=x.device)
-    scales = torch.empty(K // GROUP, M, dtype=torch.float32, device=x.device)
+    scales = torch.empty(scale_shape(K // GROUP, M, code_format), dtype=torch.float32, device=x.device)
     nib = torch.empty(M, K // 2, dtype=torch.uint8, device=x.device) if packed else None
     if smooth is not None:
         smooth = _cuda(smooth, "smooth").to(torch.bfloat16).contiguous()
@@ -135,7 +143,7 @@ def smoothing(act_amax, weight, alpha=0.5):
 
 class PreparedW4A4:
     """A W4A4 layer in the GEMM's device layout: codes [N, K] one byte each (CODE_FORMAT), scales [K/64, N]
-    float32, bias [N] float32 (or None), smooth [K] bfloat16 (or None when it is all ones), made once from the
+    float32 ([K/64, N, 4] padded in "e4m3ts"), bias [N] float32 (or None), smooth [K] bfloat16 (or None when it is all ones), made once from the
     packed parts."""
 
     def __init__(self, qweight, wscales, proj_down, proj_up, smooth, bias, code_format=None):
@@ -150,7 +158,8 @@ class PreparedW4A4:
         self.scale_dtype = wscales.dtype
         self.code_format = _code_format(code_format or CODE_FORMAT)
         self.codes = torch.empty(N, K, dtype=torch.uint8, device=qweight.device)
-        self.scales = torch.empty(K // GROUP, N, dtype=torch.float32, device=qweight.device)
+        self.scales = torch.empty(scale_shape(K // GROUP, N, code_format or CODE_FORMAT), dtype=torch.float32,
+                                  device=qweight.device)
         q = qweight.contiguous().view(torch.uint8)
         ws = wscales.contiguous()
         with torch.cuda.device(q.device):
