@@ -15,8 +15,10 @@
 //
 // Operands: codes are E4M3 bytes of the 4-bit integers (exact for [-8, 15]; kind::f8f6f4 leaves P_g as exact
 // float32 integers). Scales are stored padded for the tensor core: [K / 64][rows][4] float32 holding
-// (s, 0, 0, 0), so that a TMA box of 128 rows x 16 bytes lands as the first K-half (4 tf32 columns) of a
-// K-major no-swizzle operand; the second K-half is a block of zeros written once.
+// (s, 0, 0, 0), so that the 128 rows of a tile, 2048 contiguous bytes, land by one bulk copy as the first K-half
+// (4 tf32 columns) of a K-major no-swizzle operand; the second K-half is a block of zeros written once. (A
+// tensor-map box of 128 rows x 16 bytes moves the same bytes row by row, and measured at less than half the
+// GEMM's throughput.)
 //
 // Tile 128 x 128, two groups per pipeline stage, one CTA per SM, 12 warps:
 //   warp 0      TMA producer: A, B code tiles (128-byte swizzle) and the four scale blocks of the stage
@@ -38,7 +40,6 @@ constexpr int SCALE_BLOCK = 4096;             // 128 rows x 8 tf32: data half (T
 constexpr int SCALE_DATA = 2048;              // 128 rows x 16 bytes
 constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kStageTx = A_BYTES + B_BYTES + 2 * GPS * SCALE_DATA;
 
 struct __align__(1024) Smem {
   // the scale operand blocks come first: every descriptor built on them points inside this structure
@@ -95,8 +96,7 @@ __device__ __forceinline__ void promote32(float (&acc)[64], int base, const uint
 template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_ts_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   const __grid_constant__ CUtensorMap map_sa, const __grid_constant__ CUtensorMap map_sb,
-                   GemmEpilogue ep, int M, int N, int K, uint32_t* err) {
+                   const float* __restrict__ wscale, GemmEpilogue ep, int M, int N, int K, uint32_t* err) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -127,8 +127,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tensor_map(&map_a);
     prefetch_tensor_map(&map_b);
-    prefetch_tensor_map(&map_sa);
-    prefetch_tensor_map(&map_sb);
   }
   if (warp == 1) {
     tmem_alloc(&sm.tmem_base, kTmemCols);
@@ -143,19 +141,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     setmaxnreg_dec<56>();
     if (warp == 0 && lane == 0) {
       // ---------------- TMA producer ----------------
+      // activation scale rows of this tile: 128, or fewer in the last group of the last row tile (rows past
+      // G * M do not exist; the rows of the next group that a partial tile reads feed only rows >= M)
+      const int64_t a_rows_total = static_cast<int64_t>(G) * M;
       int issued = 0;
       for (int kt = 0; kt < KT; ++kt) {
         const int s = kt % STAGES;
         const uint32_t ph = (kt / STAGES) & 1;
         if (!mbar_wait(&sm.empty[s], ph ^ 1, err, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&sm.full[s], kStageTx);
+        uint32_t a_bytes[GPS];
+        uint32_t tx = A_BYTES + B_BYTES + GPS * SCALE_DATA;
+#pragma unroll
+        for (int sub = 0; sub < GPS; ++sub) {
+          const int64_t row0 = static_cast<int64_t>(kt * GPS + sub) * M + m_tile * BM;
+          const int64_t rows = a_rows_total - row0 < BM ? a_rows_total - row0 : BM;
+          a_bytes[sub] = static_cast<uint32_t>(rows) * 16u;
+          tx += a_bytes[sub];
+        }
+        mbar_arrive_expect_tx(&sm.full[s], tx);
         tma_load_2d(sm.a[s], &map_a, &sm.full[s], kt * BK, m_tile * BM);
         tma_load_2d(sm.b[s], &map_b, &sm.full[s], kt * BK, n_tile * BN);
 #pragma unroll
         for (int sub = 0; sub < GPS; ++sub) {
           const int g = kt * GPS + sub;
-          tma_load_2d(sm.sa[s][sub], &map_sa, &sm.full[s], 0, g * M + m_tile * BM);
-          tma_load_2d(sm.sb[s][sub], &map_sb, &sm.full[s], 0, g * N + n_tile * BN);
+          bulk_load(sm.sa[s][sub], ep.ascale + (static_cast<int64_t>(g) * M + m_tile * BM) * 4, a_bytes[sub],
+                    &sm.full[s]);
+          bulk_load(sm.sb[s][sub], wscale + (static_cast<int64_t>(g) * N + n_tile * BN) * 4, SCALE_DATA,
+                    &sm.full[s]);
         }
         issued = kt + 1;
       }
@@ -217,23 +229,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t tp = t_row + b * BN, ts = t_row + 2 * BN + b * BN;
+      // all four loads in flight at once, one wait, then the buffer pair goes back to the MMA issuer before any
+      // arithmetic: the release comes one TMEM round trip after the commit
       uint32_t p0[32], s0[32], p1[32], s1[32];
       tmem_ld32(tp, p0);
       tmem_ld32(ts, s0);
-      tmem_ld_wait();
       tmem_ld32(tp + 32, p1);
       tmem_ld32(ts + 32, s1);
-      if constexpr (kMode == kEpiDumpGroup) {
-        if (g == ep.dump_group && row_ok) {
-          int32_t* o = reinterpret_cast<int32_t*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n_tile * BN + h * 64;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = __float2int_rn(__uint_as_float(p0[j]));
-        }
-      }
-      promote32(acc, 0, p0, s0);
+      tmem_ld_wait(p0);
+      tmem_ld_wait(s0);
       tmem_ld_wait(p1);
       tmem_ld_wait(s1);
-      // every column of this buffer pair is in registers: the MMA may overwrite it
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
@@ -241,9 +247,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (g == ep.dump_group && row_ok) {
           int32_t* o = reinterpret_cast<int32_t*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n_tile * BN + h * 64;
 #pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __float2int_rn(__uint_as_float(p0[j]));
+#pragma unroll
           for (int j = 0; j < 32; ++j) o[32 + j] = __float2int_rn(__uint_as_float(p1[j]));
         }
       }
+      promote32(acc, 0, p0, s0);
       promote32(acc, 32, p1, s1);
     }
 
@@ -372,16 +381,11 @@ int gemm_ts_validate(const GemmArgs& a, const char** why) {
 
 int gemm_ts_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
   if (gemm_ts_validate(a, why) != 0) return 1;
-  const int G = a.K / ts::GROUP;
-  CUtensorMap ma, mb, msa, msb;
+  CUtensorMap ma, mb;
   if (!ts::make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.a, a.K, a.M, a.lda, ts::BK, ts::BM,
                        CU_TENSOR_MAP_SWIZZLE_128B) ||
       !ts::make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.b, a.K, a.N, a.ldb, ts::BK, ts::BN,
-                       CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !ts::make_map_2d(&msa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.ep.ascale, 4, static_cast<uint64_t>(G) * a.M, 16, 4,
-                       ts::BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !ts::make_map_2d(&msb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.wscale, 4, static_cast<uint64_t>(G) * a.N, 16, 4,
-                       ts::BN, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+                       CU_TENSOR_MAP_SWIZZLE_128B)) {
     *why = "cuTensorMapEncodeTiled rejected an operand (alignment or stride)";
     return 2;
   }
@@ -390,7 +394,7 @@ int gemm_ts_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
   auto launch = [&](auto kernel) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(ts::kSmemBytes));
     if (e == cudaSuccess)
-      kernel<<<grid, ts::kThreads, ts::kSmemBytes, stream>>>(ma, mb, msa, msb, a.ep, a.M, a.N, a.K, a.err);
+      kernel<<<grid, ts::kThreads, ts::kSmemBytes, stream>>>(ma, mb, a.wscale, a.ep, a.M, a.N, a.K, a.err);
   };
   switch (a.ep.mode) {
     case kEpiBf16: launch(ts::gemm_ts_kernel<kEpiBf16>); break;
