@@ -160,8 +160,8 @@ def linear_workload(device):
     xd = x.to(device)
     lib = _native.lib()
     work = torch.empty(lib.wdl_w4a4_linear_workspace(M, K), dtype=torch.uint8, device=device)
-    codes = work[: M * K].view(torch.int8)
-    scales = work[(M * K + 255) // 256 * 256:].view(torch.float32)
+    codes = work[: M * K * 2]  # the activation codes the quantizer left in the workspace (one or two bytes each)
+    scales = work[(M * K * 2 + 255) // 256 * 256:].view(torch.float32)
     y = torch.empty(M, N, dtype=torch.bfloat16, device=device)
     st = _native.stream(device)
 
@@ -366,9 +366,10 @@ def main():
     parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
     parser.add_argument("--workload", default="rollout", choices=sorted(WORKLOADS))
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
-    parser.add_argument("--codes", default="e4m3", choices=("e4m3", "e4m3ts", "int8"),
+    parser.add_argument("--codes", default="e4m3", choices=("e4m3", "e4m3ts", "f16fold", "int8"),
                         help="operand code format of the W4A4 GEMM: e4m3 (kind::f8f6f4), e4m3ts (e4m3 with the group "
-                             "scale products on the tensor cores) or int8 (kind::i8)")
+                             "scale products on the tensor cores), f16fold (float16 codes and scale-folded weights, "
+                             "kind::f16) or int8 (kind::i8)")
     parser.add_argument("--chunks", type=int, default=7, help="rollout chunks (profiling; BASELINE config 4: 7)")
     parser.add_argument("--layers", type=int, default=30, help="model layers (profiling; BASELINE config 4: 30)")
     args = parser.parse_args()

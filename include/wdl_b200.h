@@ -43,6 +43,13 @@ extern "C" {
 #define WDL_CODES_INT8 0
 #define WDL_CODES_E4M3 1
 #define WDL_CODES_E4M3_TS 2
+/* WDL_CODES_F16_FOLD holds float16 operands: activation codes as float16 integers (two bytes each), weights
+ * folded with their group scales, w16 = code * sw * 2^-F (wdl_w4a4_fold_weight), exact when the weight scales are
+ * bf16. The GEMM (tcgen05 kind::f16) then accumulates sw * 2^-F * P per group exactly and its epilogue needs one
+ * fused multiply-add by sx * 2^F per element and group; results equal WDL_CODES_E4M3's bit for bit. In this
+ * format the GEMM's w_scales argument points to the single float 2^F, activation scales are [K/64, M] f32 as in
+ * WDL_CODES_E4M3, N % 256 == 0, K % 64 == 0, and the group-partials view is not available. */
+#define WDL_CODES_F16_FOLD 3
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* wdl_last_error(void);
@@ -74,6 +81,14 @@ int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16
  * (src/wan_dit_lab/quantization/w4a4.py:171-179). */
 int wdl_w4a4_unpack_weight(const uint8_t* qweight, const void* wscales, int scale_dtype, int N, int K,
                            int code_format, void* codes, float* scales, void* stream);
+
+/* Folds a packed INT4 weight (qweight [N, K/2], wscales [K/64, N] bf16 or f16) into float16 operands of
+ * WDL_CODES_F16_FOLD: w16 [N, K] = code * wscale * 2^-shift. Adds to *inexact (a device counter the caller zeroes)
+ * the number of elements that are not exactly a normal float16 number; with any, the layer must use another code
+ * format. bf16 scales and shift = ceil(log2(8 * max wscale)) - 15 make every element exact unless the layer's group
+ * scales span more than about 2^25. The load-time counterpart of w4a4.quantize (w4a4.py:171-179) for this format. */
+int wdl_w4a4_fold_weight(const uint8_t* qweight, const void* wscales, int scale_dtype, int N, int K, int shift,
+                         uint16_t* w16, uint32_t* inexact, void* stream);
 
 /* y [M, N] bf16 (row stride ldy) = sum_g a_scales[g, m] * w_scales[g, n] * (sum_{k in g} a[m, k] w[n, k]) + bias[n]
  * on tcgen05 tensor cores. a [M, K] and w [N, K] codes in code_format (activation codes [-8, 15], weight codes

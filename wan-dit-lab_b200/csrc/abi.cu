@@ -115,7 +115,12 @@ int wdl_device_error(void* stream, uint32_t* code) {
   return ok();
 }
 
-static bool valid_codes(int f) { return f == WDL_CODES_INT8 || f == WDL_CODES_E4M3 || f == WDL_CODES_E4M3_TS; }
+static bool valid_codes(int f) {
+  return f == WDL_CODES_INT8 || f == WDL_CODES_E4M3 || f == WDL_CODES_E4M3_TS || f == WDL_CODES_F16_FOLD;
+}
+
+// Bytes of one code in a code format's operand (float16 codes of the folded format take two).
+static int code_bytes(int f) { return f == WDL_CODES_F16_FOLD ? 2 : 1; }
 
 // Scale arrays of the padded format hold 16-byte entries read by TMA.
 static bool scales_aligned(const void* p, int code_format) { return aligned(p, code_format == WDL_CODES_E4M3_TS ? 16 : 4); }
@@ -132,8 +137,8 @@ int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16
   if (M == 0) return ok();
   if (!x || !codes || !scales) return fail(WDL_ERR_ARGUMENT, "x, codes and scales must not be null");
   if (!aligned(x, 16) || (ldx * esize) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "x rows must be 16-byte aligned");
-  if (!aligned(codes, 8) || !scales_aligned(scales, code_format) || (packed && !aligned(packed, 4)) ||
-      (smooth && !aligned(smooth, 16)))
+  if (!aligned(codes, 8 * code_bytes(code_format)) || !scales_aligned(scales, code_format) ||
+      (packed && !aligned(packed, 4)) || (smooth && !aligned(smooth, 16)))
     return fail(WDL_ERR_ARGUMENT, "misaligned output or smooth pointer");
   wdl::w4a4::quantize_rows_launch(x, x_dtype, ldx, smooth, M, K, scale_dtype, code_format,
                                   static_cast<int8_t*>(codes), scales, packed, static_cast<cudaStream_t>(stream));
@@ -143,6 +148,8 @@ int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16
 int wdl_w4a4_unpack_weight(const uint8_t* qweight, const void* wscales, int scale_dtype, int N, int K,
                            int code_format, void* codes, float* scales, void* stream) {
   if (!valid_codes(code_format)) return fail(WDL_ERR_ARGUMENT, "unknown code format %d", code_format);
+  if (code_format == WDL_CODES_F16_FOLD)
+    return fail(WDL_ERR_ARGUMENT, "folded weights are made by wdl_w4a4_fold_weight");
   if (N <= 0 || K <= 0 || K % 64 != 0) return fail(WDL_ERR_ARGUMENT, "N > 0 and K a positive multiple of 64 required");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
   if (!qweight || !wscales || !codes || !scales) return fail(WDL_ERR_ARGUMENT, "null pointer");
@@ -153,6 +160,19 @@ int wdl_w4a4_unpack_weight(const uint8_t* qweight, const void* wscales, int scal
   return cuda_status(cudaGetLastError(), "unpack_weight launch");
 }
 
+int wdl_w4a4_fold_weight(const uint8_t* qweight, const void* wscales, int scale_dtype, int N, int K, int shift,
+                         uint16_t* w16, uint32_t* inexact, void* stream) {
+  if (N <= 0 || K <= 0 || K % 64 != 0) return fail(WDL_ERR_ARGUMENT, "N > 0 and K a positive multiple of 64 required");
+  if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
+  if (shift < -100 || shift > 100) return fail(WDL_ERR_ARGUMENT, "shift out of range");
+  if (!qweight || !wscales || !w16 || !inexact) return fail(WDL_ERR_ARGUMENT, "null pointer");
+  if (!aligned(qweight, 4) || !aligned(w16, 16) || !aligned(wscales, 2) || !aligned(inexact, 4))
+    return fail(WDL_ERR_ARGUMENT, "misaligned pointer");
+  wdl::w4a4::fold_weight_launch(qweight, static_cast<const uint16_t*>(wscales), scale_dtype, N, K, shift, w16,
+                                reinterpret_cast<unsigned int*>(inexact), static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "fold_weight launch");
+}
+
 static int gemm_common(wdl::w4a4::GemmArgs& a, void* stream) {
   if (!valid_codes(a.code_format)) return fail(WDL_ERR_ARGUMENT, "unknown code format %d", a.code_format);
   if (a.M < 0) return fail(WDL_ERR_ARGUMENT, "M must be >= 0");
@@ -160,14 +180,18 @@ static int gemm_common(wdl::w4a4::GemmArgs& a, void* stream) {
   if (!a.a || !a.b || !a.wscale || !a.ep.ascale || !a.ep.out) return fail(WDL_ERR_ARGUMENT, "null operand pointer");
   if (!aligned(a.ep.out, 16) || (a.ep.residual && !aligned(a.ep.residual, 16)))
     return fail(WDL_ERR_ARGUMENT, "output and residual must be 16-byte aligned");
-  const bool ts = a.code_format == WDL_CODES_E4M3_TS;
+  const int f = a.code_format;
   const char* why = "";
-  if ((ts ? wdl::w4a4::gemm_ts_validate(a, &why) : wdl::w4a4::gemm_validate(a, &why)) != 0)
-    return fail(WDL_ERR_ARGUMENT, "%s", why);
+  const int v = f == WDL_CODES_E4M3_TS    ? wdl::w4a4::gemm_ts_validate(a, &why)
+                : f == WDL_CODES_F16_FOLD ? wdl::w4a4::gemm_fold_validate(a, &why)
+                                          : wdl::w4a4::gemm_validate(a, &why);
+  if (v != 0) return fail(WDL_ERR_ARGUMENT, "%s", why);
   a.err = error_word();
   if (!a.err) return fail(WDL_ERR_CUDA, "cannot resolve the device error word");
-  const int st = ts ? wdl::w4a4::gemm_ts_launch(a, static_cast<cudaStream_t>(stream), &why)
-                    : wdl::w4a4::gemm_launch(a, static_cast<cudaStream_t>(stream), &why);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int st = f == WDL_CODES_E4M3_TS    ? wdl::w4a4::gemm_ts_launch(a, s, &why)
+                 : f == WDL_CODES_F16_FOLD ? wdl::w4a4::gemm_fold_launch(a, s, &why)
+                                           : wdl::w4a4::gemm_launch(a, s, &why);
   if (st == 1) return fail(WDL_ERR_ARGUMENT, "%s", why);
   if (st != 0) return fail(WDL_ERR_CUDA, "%s", why);
   return ok();
@@ -221,10 +245,11 @@ int wdl_w4a4_gemm_group_partials(const void* a, const float* a_scales, const voi
 int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                           const float* bias, const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N,
                           int K, uint8_t* codes, int64_t ldc, float* scales, void* stream) {
-  if (code_format != WDL_CODES_E4M3 && code_format != WDL_CODES_E4M3_TS)
-    return fail(WDL_ERR_ARGUMENT, "the unsigned hidden codes need an E4M3 code format");
+  if (code_format == WDL_CODES_INT8)
+    return fail(WDL_ERR_ARGUMENT, "the unsigned hidden codes need an E4M3 or float16 code format");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
   if (ldc < N || ldc % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldc must be >= N and a multiple of 16");
+  if (!aligned(codes, 16)) return fail(WDL_ERR_ARGUMENT, "codes must be 16-byte aligned");
   if (!scales) return fail(WDL_ERR_ARGUMENT, "null scales");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
@@ -236,7 +261,7 @@ int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, c
 
 size_t wdl_w4a4_linear_workspace(int M, int K) {
   if (M <= 0 || K <= 0) return 0;
-  const size_t codes = (static_cast<size_t>(M) * K + 255) / 256 * 256;
+  const size_t codes = (static_cast<size_t>(M) * K * 2 + 255) / 256 * 256;  // room for float16 codes
   const size_t scales = static_cast<size_t>(K / 64) * M * 16;  // room for the padded scales of WDL_CODES_E4M3_TS
   return codes + scales;
 }
@@ -256,7 +281,7 @@ int wdl_w4a4_linear(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t
   if (!aligned(workspace, 256)) return fail(WDL_ERR_ARGUMENT, "workspace must be 256-byte aligned");
   if (!w || !w_scales) return fail(WDL_ERR_ARGUMENT, "null weight pointer");
   int8_t* codes = static_cast<int8_t*>(workspace);
-  float* scales = reinterpret_cast<float*>(static_cast<char*>(workspace) + (static_cast<size_t>(M) * K + 255) / 256 * 256);
+  float* scales = reinterpret_cast<float*>(static_cast<char*>(workspace) + (static_cast<size_t>(M) * K * 2 + 255) / 256 * 256);
   int st = wdl_w4a4_quantize_rows(x, WDL_BF16, ldx, smooth, M, K, scale_dtype, code_format, codes, scales, nullptr,
                                   stream);
   if (st != WDL_OK) return st;
@@ -352,7 +377,7 @@ int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float ep
   if (!valid_codes(code_format) || (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16))
     return fail(WDL_ERR_ARGUMENT, "invalid code format or scale dtype");
   if (M == 0) return ok();
-  if (!codes || !scales || !aligned(codes, 8) || !scales_aligned(scales, code_format))
+  if (!codes || !scales || !aligned(codes, 8 * code_bytes(code_format)) || !scales_aligned(scales, code_format))
     return fail(WDL_ERR_ARGUMENT, "null or misaligned output");
   if (!aligned(ln_w, 16) || !aligned(ln_b, 16) || !aligned(mod_shift, 16) || !aligned(mod_scale, 16) ||
       !aligned(smooth, 16))

@@ -68,7 +68,7 @@ int wdl_w4a4_linear_noalloc(const uint16_t* x, int64_t ldx, int M, int K, const 
   if (K <= 0 || K % 128 != 0 || N <= 0 || N % (code_format == WDL_CODES_E4M3_TS ? 128 : 256) != 0)
     return fail(WDL_ERR_ARGUMENT, "K % 128 == 0 and N % 256 == 0 (N % 128 == 0 with padded scales) required");
   if (code_format != WDL_CODES_INT8 && code_format != WDL_CODES_E4M3 && code_format != WDL_CODES_E4M3_TS)
-    return fail(WDL_ERR_ARGUMENT, "unknown code format");
+    return fail(WDL_ERR_ARGUMENT, "unknown code format (the folded float16 format is not supported here)");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
   if (ldx < K || (ldx * 2) % 16 != 0 || ldy < N || (ldy * 2) % 16 != 0)
     return fail(WDL_ERR_ARGUMENT, "ldx >= K and ldy >= N with 16-byte aligned rows required");

@@ -129,13 +129,25 @@ __global__ void __launch_bounds__(kRowThreads) ln_quant_kernel(const TX* __restr
     if (!valid) continue;
     const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
     const float r = __frcp_rn(scale);
-    uint32_t wd[2] = {0, 0};
+    if (a.code_format == 3) {  // float16 codes, two bytes each
+      uint32_t hw[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int q = max(-8, min(7, __float2int_rn(div_rn_by(y[i], scale, r))));
-      wd[i / 4] |= code_byte(q, a.code_format) << (8 * (i % 4));
+      for (int i = 0; i < 8; i += 2) {
+        const int q0 = max(-8, min(7, __float2int_rn(div_rn_by(y[i], scale, r))));
+        const int q1 = max(-8, min(7, __float2int_rn(div_rn_by(y[i + 1], scale, r))));
+        hw[i / 2] = static_cast<uint32_t>(__half_as_ushort(__int2half_rn(q0))) |
+                    (static_cast<uint32_t>(__half_as_ushort(__int2half_rn(q1))) << 16);
+      }
+      *reinterpret_cast<uint4*>(a.codes + (static_cast<int64_t>(m) * K + k) * 2) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    } else {
+      uint32_t wd[2] = {0, 0};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = max(-8, min(7, __float2int_rn(div_rn_by(y[i], scale, r))));
+        wd[i / 4] |= code_byte(q, a.code_format) << (8 * (i % 4));
+      }
+      *reinterpret_cast<uint2*>(codes + k) = make_uint2(wd[0], wd[1]);
     }
-    *reinterpret_cast<uint2*>(codes + k) = make_uint2(wd[0], wd[1]);
     if ((t & 7) == 0) {
       const float stored = a.scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16r(scale);
       const int64_t i = static_cast<int64_t>(k / 64) * a.M + m;

@@ -22,6 +22,8 @@ enum CodeFormat : int {
   kCodesE4M3 = 1,  // the code's value as an FP8 E4M3 number (tcgen05 kind::f8f6f4, fp32 partials)
   kCodesE4M3Ts = 2,  // E4M3 codes, group scales padded to 16 bytes (s, 0, 0, 0): the tensor-core scale product
                      // GEMM (w4a4_gemm_ts.cu), scales [K / 64, rows, 4]
+  kCodesF16Fold = 3,  // float16 operands: activation codes, weights folded with their bf16 group scales and one
+                      // power of two 2^-F (w4a4_gemm_fold.cu); the weight "scales" argument is the float 2^F
 };
 
 enum EpilogueMode : int {
@@ -69,6 +71,14 @@ int gemm_launch(const GemmArgs& args, cudaStream_t stream, const char** why);
 // The same GEMM for kCodesE4M3Ts operands (N % 128 == 0, K % 128 == 0; scales padded, 16-byte aligned).
 int gemm_ts_validate(const GemmArgs& a, const char** why);
 int gemm_ts_launch(const GemmArgs& args, cudaStream_t stream, const char** why);
+
+// The same GEMM for kCodesF16Fold operands (N % 256 == 0, K % 64 == 0; wscale = the float 2^F; no dump mode).
+int gemm_fold_validate(const GemmArgs& a, const char** why);
+int gemm_fold_launch(const GemmArgs& args, cudaStream_t stream, const char** why);
+// w16 [N, K] float16 = code * wscale * 2^-shift from packed codes and bf16 / f16 scales [K / 64, N];
+// *inexact (device) counts elements that are not exact normal float16 numbers.
+void fold_weight_launch(const uint8_t* qweight, const uint16_t* wscales, int scale_dtype, int N, int K, int shift,
+                        uint16_t* w16, unsigned int* inexact, cudaStream_t stream);
 
 }  // namespace w4a4
 }  // namespace wdl

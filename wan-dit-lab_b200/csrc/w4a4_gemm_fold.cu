@@ -1,0 +1,372 @@
+// W4A4 GEMM with the weight group scales folded into 16-bit weights (code format "f16 fold").
+//
+//   y[m, n] = sum_g  sx[g, m] * (sw[g, n] * P_g[m, n]),   P_g[m, n] = sum_{k in group g} xq[m, k] * wq[n, k]
+//
+// SVDQuant's INT4 linear (Nunchaku's gemm_w4a4, called from the reference's native/ops/w4a4_ops.cpp:36). The
+// promotion of the INT4 kernels multiplies each exact group partial by sx * sw: two float32 operations per
+// accumulator element and group on the CUDA cores, twice the tensor-core time of the group. Here the weight
+// scale travels with the weight instead. With bf16 weight scales (the repo's packing, w4a4.py:177) every
+// product wq * sw has at most 3 + 8 = 11 significant bits, so it is an exact float16 number once the layer is
+// shifted by one power of two 2^-F into float16's normal range (wdl_w4a4_fold_weight checks every element and
+// reports any that is not exact). The activation codes are exact float16 integers. A kind::f16 tcgen05.mma of
+// codes x folded weights then accumulates, for each group, sw[g, n] * 2^-F * P_g[m, n]: every partial sum is an
+// integer (|P| <= 4096, 13 bits) times sw (8 bits), 21 significant bits, exact in float32 in any order. The
+// epilogue adds it with ONE fused multiply-add by the per-row scalar sx[g, m] * 2^F:
+//   acc = fma(sw 2^-F P, sx 2^F, acc) = round(acc + sx sw P),
+// the same rounding of the same exact product as the CUDA-core promotion fma(P, sx * sw, acc) (sx * sw is exact
+// too), so results equal the E4M3 / int8 kernels' bit for bit. The price is the 16-bit tensor rate (half the
+// 8-bit rate) and 2-byte operands; the CUDA cores, which bound the other kernels, do half the work and no
+// shared-memory scale loads.
+//
+// Tile 128 x 256, one group (64 k = 128 bytes of a row) per pipeline stage, 4 stages, one CTA per SM, 12 warps:
+//   warp 0      TMA producer: A, B tiles (128-byte swizzle)
+//   warp 1      TMEM owner and MMA issuer: 4 x K=16 kind::f16 MMAs per group into TMEM buffer (group % 2)
+//   warps 4-11  promotion + epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (its rows) and columns
+//               128 ((w - 4) / 4) .. +127, keeps 128 fp32 accumulators per thread
+// TMEM: 2 buffers x 256 columns = all 512.
+#include "common.cuh"
+#include "w4a4_gemm.h"
+
+namespace wdl {
+namespace w4a4 {
+namespace fold {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+constexpr int kThreads = 384;
+constexpr uint32_t kTmemCols = 512;
+
+struct __align__(1024) Smem {
+  uint8_t a[STAGES][A_BYTES];
+  uint8_t b[STAGES][B_BYTES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+};
+
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float cube = x * x * x;
+  const float inner = 0.7978845608028654f * (x + 0.044715f * cube);
+  return 0.5f * x * (1.f + tanhf(inner));
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_fold_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const float* __restrict__ fold_scale, GemmEpilogue ep, int M, int N, int K, uint32_t* err) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
+  const int G = K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 8);
+    }
+    mbar_init(&sm.mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensor_map(&map_a);
+    prefetch_tensor_map(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp < 4) {
+    setmaxnreg_dec<56>();
+    if (warp == 0 && lane == 0) {
+      // ---------------- TMA producer ----------------
+      int issued = 0;
+      for (int g = 0; g < G; ++g) {
+        const int s = g % STAGES;
+        const uint32_t ph = (g / STAGES) & 1;
+        if (!mbar_wait(&sm.empty[s], ph ^ 1, err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&sm.full[s], A_BYTES + B_BYTES);
+        tma_load_2d(sm.a[s], &map_a, &sm.full[s], g * BK, m_tile * BM);
+        tma_load_2d(sm.b[s], &map_b, &sm.full[s], g * BK, n_tile * BN);
+        issued = g + 1;
+      }
+      for (int g = (issued > STAGES ? issued - STAGES : 0); g < issued; ++g)
+        mbar_wait(&sm.full[g % STAGES], (g / STAGES) & 1, err, kErrWaitFull);
+    } else if (warp == 1) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = make_idesc(1, 0, 0, BM, BN);  // f16 x f16 -> f32
+      bool ok = true;
+      for (int g = 0; g < G && ok; ++g) {
+        const int s = g % STAGES, b = g & 1;
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.full[s], (g / STAGES) & 1, err, kErrWaitFull)) &&
+             __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_empty[b], ((g >> 1) & 1) ^ 1, err, kErrWaitAccEmpty));
+        if (!ok) break;
+        tc_fence_after();
+        if (elect_one()) {
+          const uint32_t a0 = smem_u32(sm.a[s]), b0 = smem_u32(sm.b[s]);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_f16(tmem + b * BN, smem_desc_k128(a0 + kk * 32), smem_desc_k128(b0 + kk * 32), idesc, kk > 0);
+          tc_commit(&sm.acc_full[b]);
+          tc_commit(&sm.empty[s]);
+        }
+        __syncwarp();
+      }
+      if (elect_one()) tc_commit(&sm.mma_done);
+      __syncwarp();
+      mbar_wait(&sm.mma_done, 0, err, kErrWaitAccFull);
+    }
+  } else {
+    setmaxnreg_inc<224>();
+    // ---------------- promotion + epilogue ----------------
+    const int q = warp & 3, h = (warp - 4) >> 2;
+    const int row = q * 32 + lane;
+    const int m = m_tile * BM + row;
+    const bool row_ok = m < M;
+    const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + h * 128;
+    const float unfold = __ldg(fold_scale);  // 2^F
+    float acc[128];
+#pragma unroll
+    for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+
+    // sx[g, m] * 2^F (exact: a power of two), loaded a group ahead
+    float mul_next = row_ok ? __fmul_rn(__ldg(ep.ascale + m), unfold) : 0.f;
+    bool ok = true;
+    for (int g = 0; g < G; ++g) {
+      const int b = g & 1;
+      const float mul = mul_next;
+      if (g + 1 < G) mul_next = row_ok ? __fmul_rn(__ldg(ep.ascale + static_cast<size_t>(g + 1) * M + m), unfold) : 0.f;
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_full[b], (g >> 1) & 1, err, kErrWaitAccFull));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t t_buf = t_row + b * BN;
+      // Drain the group's 128 columns in 4 chunks of 32, loading chunk c + 1 while chunk c is promoted.
+      uint32_t ra[32], rb[32];
+      tmem_ld32(t_buf, ra);
+      tmem_ld_wait(ra);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+        if (c < 3) tmem_ld32(t_buf + (c + 1) * 32, nxt);
+        if (c == 3) {  // every column of this buffer is in registers: the MMA may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[c * 32 + j] = fmaf(__uint_as_float(cur[j]), mul, acc[c * 32 + j]);
+        if (c < 3) tmem_ld_wait(nxt);
+      }
+    }
+
+    if (ok && row_ok) {
+      const int n0 = n_tile * BN + h * 128;
+      if constexpr (kMode == kEpiBf16) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
+#pragma unroll
+        for (int j = 0; j < 128; j += 8) {
+          float v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = acc[j + i] + (ep.bias ? __ldg(ep.bias + n0 + j + i) : 0.f);
+          uint4 pk;
+          __nv_bfloat162 t0 = __floats2bfloat162_rn(v[0], v[1]), t1 = __floats2bfloat162_rn(v[2], v[3]);
+          __nv_bfloat162 t2 = __floats2bfloat162_rn(v[4], v[5]), t3 = __floats2bfloat162_rn(v[6], v[7]);
+          pk.x = *reinterpret_cast<uint32_t*>(&t0);
+          pk.y = *reinterpret_cast<uint32_t*>(&t1);
+          pk.z = *reinterpret_cast<uint32_t*>(&t2);
+          pk.w = *reinterpret_cast<uint32_t*>(&t3);
+          *reinterpret_cast<uint4*>(out + j) = pk;
+        }
+      } else if constexpr (kMode == kEpiGeluU4) {
+        // the fused MLP's hidden layer (reference quantization/w4a4.py:195-204, native/ops/w4a4_ops.cpp:44-63):
+        // u = GELU(acc + bias) + shift, divided by the next layer's smoothing, quantized unsigned per group of 64
+        // columns: scale = max(max u, 1e-8) / 15, code = round-half-even(u / scale) clamped to [0, 15], stored as
+        // the next layer's float16 operand (exact integers) with the scale [N / 64, M] rounded to its dtype.
+        uint16_t* codes = reinterpret_cast<uint16_t*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
+#pragma unroll
+        for (int g2 = 0; g2 < 2; ++g2) {
+          float amax = 0.f;
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const int n = n0 + g2 * 64 + j;
+            float t = __fadd_rn(gelu_tanh(acc[g2 * 64 + j] + (ep.bias ? __ldg(ep.bias + n) : 0.f)), ep.gelu_shift);
+            if (ep.out_smooth) t = __fdiv_rn(t, __bfloat162float(ep.out_smooth[n]));
+            acc[g2 * 64 + j] = t;
+            amax = fmaxf(amax, fabsf(t));
+          }
+          const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 15.f);
+          const float rcp = __frcp_rn(scale);
+#pragma unroll
+          for (int j = 0; j < 64; j += 8) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int q0 = max(0, min(15, __float2int_rn(div_rn_by(acc[g2 * 64 + j + 2 * e], scale, rcp))));
+              const int q1 = max(0, min(15, __float2int_rn(div_rn_by(acc[g2 * 64 + j + 2 * e + 1], scale, rcp))));
+              w[e] = static_cast<uint32_t>(__half_as_ushort(__int2half_rn(q0))) |
+                     (static_cast<uint32_t>(__half_as_ushort(__int2half_rn(q1))) << 16);
+            }
+            *reinterpret_cast<uint4*>(codes + g2 * 64 + j) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+          ep.out_scales[static_cast<size_t>((n0 + g2 * 64) / 64) * M + m] =
+              ep.out_scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16_round(scale);
+        }
+      } else if constexpr (kMode == kEpiResidualF32) {
+        // residual stream update in fp32: x_new = x + float(bf16(acc + bias)) * gate   (gate 1 when absent)
+        float* out = reinterpret_cast<float*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
+        const float* res = ep.residual + static_cast<size_t>(m) * ep.ld_res + n0;
+#pragma unroll
+        for (int j = 0; j < 128; j += 4) {
+          const float4 r = *reinterpret_cast<const float4*>(res + j);
+          float v[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float o = bf16_round(acc[j + i] + (ep.bias ? __ldg(ep.bias + n0 + j + i) : 0.f));
+            v[i] = ep.gate ? __fadd_rn(v[i], __fmul_rn(o, __ldg(ep.gate + n0 + j + i))) : __fadd_rn(v[i], o);
+          }
+          *reinterpret_cast<float4*>(out + j) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Folded weights: w16[n, k] = float16(wq[n, k] * sw[k / 64, n] * 2^-F). One thread per 8 codes (4 packed bytes);
+// an element whose value is not exactly a normal float16 number (or zero) is counted in *inexact.
+__global__ void fold_weight_kernel(const uint8_t* __restrict__ qweight, const uint16_t* __restrict__ wscales,
+                                   int scale_dtype, int N, int K, float unshift, uint16_t* __restrict__ w16,
+                                   unsigned int* __restrict__ inexact) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // word index
+  const int64_t words = static_cast<int64_t>(N) * K / 8;
+  if (i >= words) return;
+  const int64_t e0 = i * 8;
+  const int n = static_cast<int>(e0 / K), k = static_cast<int>(e0 % K);
+  const uint16_t sbits = wscales[static_cast<int64_t>(k / 64) * N + n];
+  const float sw = scale_dtype == 1 ? __half2float(__ushort_as_half(sbits)) : __bfloat162float(__ushort_as_bfloat16(sbits));
+  const float f = __fmul_rn(sw, unshift);  // exact: a power of two
+  const uint32_t p = reinterpret_cast<const uint32_t*>(qweight)[i];
+  uint32_t out[4];
+  unsigned int bad = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t byte = (p >> (8 * j)) & 0xFFu;
+    const int lo = static_cast<int>(byte << 28) >> 28, hi = static_cast<int>((byte >> 4) << 28) >> 28;
+    uint32_t pair = 0;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const float v = __fmul_rn(static_cast<float>(t ? hi : lo), f);  // exact in float32 (<= 22 bits)
+      const __half hv = __float2half_rn(v);
+      const float back = __half2float(hv);
+      if (back != v || (v != 0.f && fabsf(v) < 6.103515625e-05f)) ++bad;  // not exact, or a subnormal
+      pair |= static_cast<uint32_t>(__half_as_ushort(hv)) << (16 * t);
+    }
+    out[j] = pair;
+  }
+  reinterpret_cast<uint4*>(w16)[i] = make_uint4(out[0], out[1], out[2], out[3]);
+  if (bad) atomicAdd(inexact, bad);
+}
+
+static bool make_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                        uint32_t box_inner, uint32_t box_outer) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+}  // namespace fold
+
+int gemm_fold_validate(const GemmArgs& a, const char** why) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) {
+    *why = "M, N and K must be positive";
+    return 1;
+  }
+  if (a.N % fold::BN != 0) {
+    *why = "N must be a multiple of 256";
+    return 1;
+  }
+  if (a.K % fold::BK != 0) {
+    *why = "K must be a multiple of 64";
+    return 1;
+  }
+  if (a.ep.mode == kEpiDumpGroup) {
+    *why = "the folded format holds no separate integer group partials (use an E4M3 or int8 format)";
+    return 1;
+  }
+  if ((reinterpret_cast<uintptr_t>(a.a) | reinterpret_cast<uintptr_t>(a.b) | (a.lda * 2) | (a.ldb * 2)) & 15) {
+    *why = "operands must be 16-byte aligned with 16-byte aligned rows";
+    return 1;
+  }
+  if (!a.wscale || (reinterpret_cast<uintptr_t>(a.wscale) & 3)) {
+    *why = "w_scales must point to the float 2^F of the folded weights";
+    return 1;
+  }
+  return 0;
+}
+
+int gemm_fold_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
+  if (gemm_fold_validate(a, why) != 0) return 1;
+  CUtensorMap ma, mb;
+  if (!fold::make_map_2d(&ma, a.a, a.K, a.M, a.lda * 2, fold::BK, fold::BM) ||
+      !fold::make_map_2d(&mb, a.b, a.K, a.N, a.ldb * 2, fold::BK, fold::BN)) {
+    *why = "cuTensorMapEncodeTiled rejected an operand (alignment or stride)";
+    return 2;
+  }
+  const dim3 grid(a.N / fold::BN, (a.M + fold::BM - 1) / fold::BM);
+  cudaError_t e = cudaSuccess;
+  auto launch = [&](auto kernel) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(fold::kSmemBytes));
+    if (e == cudaSuccess)
+      kernel<<<grid, fold::kThreads, fold::kSmemBytes, stream>>>(ma, mb, a.wscale, a.ep, a.M, a.N, a.K, a.err);
+  };
+  switch (a.ep.mode) {
+    case kEpiBf16: launch(fold::gemm_fold_kernel<kEpiBf16>); break;
+    case kEpiResidualF32: launch(fold::gemm_fold_kernel<kEpiResidualF32>); break;
+    case kEpiGeluU4: launch(fold::gemm_fold_kernel<kEpiGeluU4>); break;
+    default: *why = "unknown epilogue mode"; return 1;
+  }
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return 3;
+  }
+  return 0;
+}
+
+void fold_weight_launch(const uint8_t* qweight, const uint16_t* wscales, int scale_dtype, int N, int K, int shift,
+                        uint16_t* w16, unsigned int* inexact, cudaStream_t stream) {
+  const int64_t words = static_cast<int64_t>(N) * K / 8;
+  fold::fold_weight_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0, stream>>>(
+      qweight, wscales, scale_dtype, N, K, ldexpf(1.f, -shift), w16, inexact);
+}
+
+}  // namespace w4a4
+}  // namespace wdl

@@ -53,6 +53,12 @@ __device__ __forceinline__ uint32_t code_byte(int q) {
     return static_cast<uint32_t>(q) & 0xFFu;
 }
 
+// Two codes as float16 halves of a 32-bit word (the folded format's activation operand; exact integers).
+__device__ __forceinline__ uint32_t code_pair_f16(int lo, int hi) {
+  return static_cast<uint32_t>(__half_as_ushort(__int2half_rn(lo))) |
+         (static_cast<uint32_t>(__half_as_ushort(__int2half_rn(hi))) << 16);
+}
+
 // Scale i of a [K / 64, rows] scale array: one float32, or (scale_pad) the 16-byte (s, 0, 0, 0) that the
 // tensor-core scale product of the E4M3 / padded-scale GEMM loads as a tf32 operand row.
 __device__ __forceinline__ void store_scale(float* scales, int64_t i, int scale_pad, float s) {
@@ -62,7 +68,8 @@ __device__ __forceinline__ void store_scale(float* scales, int64_t i, int scale_
     scales[i] = s;
 }
 
-template <typename T, bool kSmooth, bool kPack, bool kE4M3>
+// kFmt: 0 int8 bytes, 1 E4M3 bytes, 3 float16 (two bytes per code)
+template <typename T, bool kSmooth, bool kPack, int kFmt>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ x, int64_t ldx,
                                                             const __nv_bfloat16* __restrict__ smooth, int M, int K,
                                                             int scale_dtype, int8_t* __restrict__ codes,
@@ -100,12 +107,19 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
     int q[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[i] = max(-8, min(7, __float2int_rn(div_rn_by(v[i], scale, r))));
-    uint2 c;
-    c.x = code_byte<kE4M3>(q[0]) | (code_byte<kE4M3>(q[1]) << 8) | (code_byte<kE4M3>(q[2]) << 16) |
-          (code_byte<kE4M3>(q[3]) << 24);
-    c.y = code_byte<kE4M3>(q[4]) | (code_byte<kE4M3>(q[5]) << 8) | (code_byte<kE4M3>(q[6]) << 16) |
-          (code_byte<kE4M3>(q[7]) << 24);
-    *reinterpret_cast<uint2*>(codes + static_cast<int64_t>(m) * K + k) = c;
+    if constexpr (kFmt == 3) {
+      *reinterpret_cast<uint4*>(codes + (static_cast<int64_t>(m) * K + k) * 2) =
+          make_uint4(code_pair_f16(q[0], q[1]), code_pair_f16(q[2], q[3]), code_pair_f16(q[4], q[5]),
+                     code_pair_f16(q[6], q[7]));
+    } else {
+      constexpr bool kE4M3 = kFmt == 1;
+      uint2 c;
+      c.x = code_byte<kE4M3>(q[0]) | (code_byte<kE4M3>(q[1]) << 8) | (code_byte<kE4M3>(q[2]) << 16) |
+            (code_byte<kE4M3>(q[3]) << 24);
+      c.y = code_byte<kE4M3>(q[4]) | (code_byte<kE4M3>(q[5]) << 8) | (code_byte<kE4M3>(q[6]) << 16) |
+            (code_byte<kE4M3>(q[7]) << 24);
+      *reinterpret_cast<uint2*>(codes + static_cast<int64_t>(m) * K + k) = c;
+    }
     if (kPack) {
       uint32_t p = 0;
 #pragma unroll
@@ -146,7 +160,7 @@ __global__ void scales_to_f32_kernel(const uint16_t* __restrict__ in, int64_t n,
               scale_dtype == 1 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b)));
 }
 
-template <typename T, bool kE4M3>
+template <typename T, int kFmt>
 static void launch_rows(const void* x, int64_t ldx, const uint16_t* smooth, int M, int K, int scale_dtype,
                         int8_t* codes, float* scales, int scale_pad, uint8_t* packed, cudaStream_t stream) {
   const int threads = 256;
@@ -157,11 +171,11 @@ static void launch_rows(const void* x, int64_t ldx, const uint16_t* smooth, int 
     kernel<<<blocks, threads, 0, stream>>>(xt, ldx, sm, M, K, scale_dtype, codes, scales, scale_pad, packed);
   };
   if (smooth) {
-    if (packed) go(quantize_rows_kernel<T, true, true, kE4M3>);
-    else go(quantize_rows_kernel<T, true, false, kE4M3>);
+    if (packed) go(quantize_rows_kernel<T, true, true, kFmt>);
+    else go(quantize_rows_kernel<T, true, false, kFmt>);
   } else {
-    if (packed) go(quantize_rows_kernel<T, false, true, kE4M3>);
-    else go(quantize_rows_kernel<T, false, false, kE4M3>);
+    if (packed) go(quantize_rows_kernel<T, false, true, kFmt>);
+    else go(quantize_rows_kernel<T, false, false, kFmt>);
   }
 }
 
@@ -169,15 +183,14 @@ void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_
                           int scale_dtype, int code_format, int8_t* codes, float* scales, uint8_t* packed,
                           cudaStream_t stream) {
   const int pad = code_format == 2;
-  if (x_dtype == 2) {
-    if (code_format != 0) launch_rows<float, true>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
-    else launch_rows<float, false>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
-  } else {
-    if (code_format != 0)
-      launch_rows<__nv_bfloat16, true>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
-    else
-      launch_rows<__nv_bfloat16, false>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
-  }
+  auto go = [&](auto t) {
+    using T = decltype(t);
+    if (code_format == 3) launch_rows<T, 3>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
+    else if (code_format != 0) launch_rows<T, 1>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
+    else launch_rows<T, 0>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
+  };
+  if (x_dtype == 2) go(float{});
+  else go(__nv_bfloat16{});
 }
 
 void unpack_weight_launch(const uint8_t* qweight, const uint16_t* wscales, int scale_dtype, int N, int K,

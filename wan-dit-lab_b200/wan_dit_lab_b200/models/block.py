@@ -42,9 +42,9 @@ class Buffers:
         f32 = dict(dtype=torch.float32, device=device)
         bf = dict(dtype=torch.bfloat16, device=device)
         width = max(dim, ffn_dim)
-        self.codes = torch.empty(n, width, **u8)
+        self.codes = torch.empty(n, 2 * width, **u8)  # room for the float16 codes of "f16fold"
         self.scales = torch.empty(width // 64, n, 4, **f32)  # room for the padded scales of "e4m3ts"
-        self.hcodes = torch.empty(n, ffn_dim, **u8)
+        self.hcodes = torch.empty(n, 2 * ffn_dim, **u8)  # rows of ffn_dim codes, one or two bytes each
         self.hscales = torch.empty(ffn_dim // 64, n, 4, **f32)
         self.qkv = torch.empty(n, 3 * dim, **bf)
         self.q = torch.empty(n, dim, **f32)
@@ -90,6 +90,10 @@ class WanBlockB200:
         self.parts = parts
         self.layers = {name: w4a4.PreparedW4A4(*(t[k] for k in w4a4.PARTS), code_format=code_format)
                        for name, t in parts.items()}
+        if len({layer.code_format for layer in self.layers.values()}) > 1:
+            # a layer could not take the requested format: the block's quantizers feed every layer one format
+            self.layers = {name: w4a4.PreparedW4A4(*(t[k] for k in w4a4.PARTS), code_format="e4m3")
+                           for name, t in parts.items()}
         self.code_format = self.layers["self_attn.qkv"].code_format
         self.norm_q, self.norm_k = _f32(p["self_attn.norm_q.weight"]), _f32(p["self_attn.norm_k.weight"])
         self.cross_norm_q, self.cross_norm_k = _f32(p["cross_attn.norm_q.weight"]), _f32(p["cross_attn.norm_k.weight"])
@@ -217,8 +221,13 @@ class WanBlockB200:
         timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4(
             buf.codes.data_ptr(), buf.scales.data_ptr(), fc1.codes.data_ptr(), fc1.scales.data_ptr(), fmt,
             _native.ptr(fc1.bias), _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N, fc1.K, buf.hcodes.data_ptr(),
-            buf.hcodes.stride(0), buf.hscales.data_ptr(), st)))
-        keep("hcodes", buf.hcodes)
+            fc1.N, buf.hscales.data_ptr(), st)))
+        if trace is not None:  # the hidden codes [n, ffn] as float values, whatever their operand format
+            raw = buf.hcodes.view(-1)
+            if fmt == _native.CODES_F16_FOLD:
+                trace["hcodes"] = raw[:n * fc1.N * 2].view(torch.float16).view(n, fc1.N).float()
+            else:
+                trace["hcodes"] = raw[:n * fc1.N].view(torch.float8_e4m3fn).view(n, fc1.N).float()
         if trace is not None:  # the hidden scales [ffn / 64, n] as the GEMM reads them (padded: element 0 of 4)
             G = buf.hscales.shape[0]
             keep("hscales", buf.hscales[..., 0] if fmt == _native.CODES_E4M3_TS

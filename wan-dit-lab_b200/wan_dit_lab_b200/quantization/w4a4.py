@@ -14,6 +14,8 @@ or on first use (w4a4_linear) the codes are unpacked once into the GEMM's device
 nibble is unpacked inside the GEMM's main loop.
 """
 
+import math
+
 import torch
 
 from wan_dit_lab_b200 import _native
@@ -24,6 +26,9 @@ GROUP = 64  # input channels per INT4 scale (reference w4a4.py:29)
 # the promotion an int-to-float conversion per accumulator element and group. "e4m3ts" keeps E4M3 codes and
 # stores each group scale padded to 16 bytes (s, 0, 0, 0), so that the GEMM forms the scale products on the
 # tensor cores too (same results bit for bit, one CUDA-core operation per element and group instead of two).
+# "f16fold" holds float16 operands: activation codes, and weights folded with their bf16 group scales (exact),
+# so that the GEMM's promotion is one fused multiply-add by the activation scale (same results bit for bit); a
+# layer whose folded weights would not be exact (non-bf16 scales) falls back to "e4m3".
 CODE_FORMAT = "e4m3"
 GELU_SHIFT = 0.171875  # GELU(x) + GELU_SHIFT >= 0: the hidden layer of gelu_mlp is quantized unsigned (w4a4.py:195)
 PARTS = ("qweight", "wscales", "proj_down", "proj_up", "smooth", "bias")  # w4a4.py:207
@@ -42,7 +47,8 @@ def _scale_code(dtype):
 
 
 def _code_format(name):
-    return {"e4m3": _native.CODES_E4M3, "int8": _native.CODES_INT8, "e4m3ts": _native.CODES_E4M3_TS}[name]
+    return {"e4m3": _native.CODES_E4M3, "int8": _native.CODES_INT8, "e4m3ts": _native.CODES_E4M3_TS,
+            "f16fold": _native.CODES_F16_FOLD}[name]
 
 
 def scale_shape(groups, rows, code_format):
@@ -54,7 +60,7 @@ def quantize_rows(x, scale_dtype=torch.bfloat16, smooth=None, packed=False, code
     """Rows of x [M, K] (bfloat16 or float32, CUDA) in symmetric INT4 groups of GROUP: codes [M, K] int8, scales
     [K / GROUP, M] float32 (holding values rounded to scale_dtype) and, with packed, the nibbles [M, K / 2] uint8.
     code_format "int8" gives the codes as int8 integers, "e4m3" as the GEMM's E4M3 bytes (a uint8 tensor),
-    "e4m3ts" E4M3 bytes with scales [K / GROUP, M, 4] holding (s, 0, 0, 0).
+    "e4m3ts" E4M3 bytes with scales [K / GROUP, M, 4] holding (s, 0, 0, 0), "f16fold" float16 codes.
     scale = max(max|x_g|, 1e-8) / 7, code = round-half-even(x / scale) clamped to [-8, 7] (the rule of
     int4_groups, reference w4a4.py:86-100); smooth [K] bfloat16 divides x first."""
     _cuda(x, "x")
@@ -65,7 +71,8 @@ def quantize_rows(x, scale_dtype=torch.bfloat16, smooth=None, packed=False, code
     if x.stride(1) != 1:
         x = x.contiguous()
     M, K = x.shape
-    codes = torch.empty(M, K, dtype=torch.int8 if code_format == "int8" else torch.uint8, device=x.device)
+    dtype = {"int8": torch.int8, "f16fold": torch.float16}.get(code_format, torch.uint8)
+    codes = torch.empty(M, K, dtype=dtype, device=x.device)
     scales = torch.empty(scale_shape(K // GROUP, M, code_format), dtype=torch.float32, device=x.device)
     nib = torch.empty(M, K // 2, dtype=torch.uint8, device=x.device) if packed else None
     if smooth is not None:
@@ -156,20 +163,43 @@ class PreparedW4A4:
             raise NotImplementedError("the low-rank branch (proj_down/proj_up of rank > 0) is not implemented yet")
         self.N, self.K = N, K
         self.scale_dtype = wscales.dtype
-        self.code_format = _code_format(code_format or CODE_FORMAT)
-        self.codes = torch.empty(N, K, dtype=torch.uint8, device=qweight.device)
-        self.scales = torch.empty(scale_shape(K // GROUP, N, code_format or CODE_FORMAT), dtype=torch.float32,
-                                  device=qweight.device)
+        fmt = code_format or CODE_FORMAT
         q = qweight.contiguous().view(torch.uint8)
         ws = wscales.contiguous()
-        with torch.cuda.device(q.device):
-            _native.check(_native.lib().wdl_w4a4_unpack_weight(
-                q.data_ptr(), ws.data_ptr(), _scale_code(ws.dtype), N, K, self.code_format, self.codes.data_ptr(),
-                self.scales.data_ptr(), _native.stream()))
+        if fmt == "f16fold" and not self._fold(q, ws, N, K):
+            fmt = "e4m3"  # the folded weights would not be exact: keep the 8-bit codes
+        self.code_format = _code_format(fmt)
+        if fmt != "f16fold":
+            self.codes = torch.empty(N, K, dtype=torch.uint8, device=qweight.device)
+            self.scales = torch.empty(scale_shape(K // GROUP, N, fmt), dtype=torch.float32, device=qweight.device)
+            with torch.cuda.device(q.device):
+                _native.check(_native.lib().wdl_w4a4_unpack_weight(
+                    q.data_ptr(), ws.data_ptr(), _scale_code(ws.dtype), N, K, self.code_format, self.codes.data_ptr(),
+                    self.scales.data_ptr(), _native.stream()))
         self.bias = None if bias is None else bias.float().contiguous()
         ones = smooth is None or bool((smooth == 1).all())
         self.smooth = None if ones else smooth.to(torch.bfloat16).contiguous()
         self.out_features = N
+
+    def _fold(self, q, ws, N, K):
+        """The folded format's weights: codes [N, K] float16 = code * wscale * 2^-F with one power of two per layer
+        (the largest product lands below 2^15), and scales = the float 2^F the GEMM multiplies back. False when
+        any element would not be an exact normal float16 number."""
+        if ws.dtype != torch.bfloat16:
+            return False
+        top = float(ws.float().abs().max())
+        shift = math.ceil(math.log2(8 * top)) - 15 if top > 0 else 0
+        codes = torch.empty(N, K, dtype=torch.float16, device=q.device)
+        inexact = torch.zeros(1, dtype=torch.int32, device=q.device)
+        with torch.cuda.device(q.device):
+            _native.check(_native.lib().wdl_w4a4_fold_weight(q.data_ptr(), ws.data_ptr(), _scale_code(ws.dtype), N,
+                                                             K, shift, codes.data_ptr(), inexact.data_ptr(),
+                                                             _native.stream()))
+        if int(inexact.item()) != 0:
+            return False
+        self.codes = codes
+        self.scales = torch.tensor([2.0 ** shift], dtype=torch.float32, device=q.device)
+        return True
 
     def __call__(self, x):
         """y [M, N] bfloat16 = x W^T + b for x [M, K] bfloat16."""
