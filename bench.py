@@ -48,7 +48,19 @@ METRIC = "latent frames/s per GPU (5B DiT, 512x928) and W4A4 GEMM TOPS vs INT8 p
 METRIC_LINEAR = "W4A4 GEMM TOPS vs INT8 peak"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 INT8_NOMINAL_TOPS = 4500.0
-CODES = "e4m3"  # operand code format of the W4A4 GEMM (--codes)
+CODES = "f16fold"  # operand code format of the W4A4 GEMM (--codes)
+GEMM_KERNEL = {"int8": "w4a4_gemm_kernel", "e4m3": "w4a4_gemm_kernel", "e4m3ts": "gemm_ts_kernel",
+               "f16fold": "gemm_fold_kernel"}
+
+
+def _measured_bf16_peak():
+    try:
+        return float(json.loads(PEAKS_FILE.read_text())["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+F16_PEAK_TFLOPS = _measured_bf16_peak()  # the folded format runs on the 16-bit tensor pipe: its own ceiling
 
 
 def seeded(shape, seed, scale=1.0, outliers=0.0):
@@ -366,7 +378,7 @@ def main():
     parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
     parser.add_argument("--workload", default="rollout", choices=sorted(WORKLOADS))
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
-    parser.add_argument("--codes", default="e4m3", choices=("e4m3", "e4m3ts", "f16fold", "int8"),
+    parser.add_argument("--codes", default="f16fold", choices=("e4m3", "e4m3ts", "f16fold", "int8"),
                         help="operand code format of the W4A4 GEMM: e4m3 (kind::f8f6f4), e4m3ts (e4m3 with the group "
                              "scale products on the tensor cores), f16fold (float16 codes and scale-folded weights, "
                              "kind::f16) or int8 (kind::i8)")
@@ -451,7 +463,11 @@ def main():
             cpu = {"value": cpu_ops / dt / 1e12, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port", "sample": sample}
 
     if rank == 0:
-        dtype = wl["dtype"] if CODES == "int8" else wl["dtype"].replace("int8 tensor cores", "e4m3-coded integers on fp8 tensor cores, exact")
+        dtype = wl["dtype"].replace("int8 tensor cores", {
+            "int8": "int8 tensor cores (kind::i8)",
+            "e4m3": "e4m3-coded integers on fp8 tensor cores (kind::f8f6f4), exact",
+            "e4m3ts": "e4m3-coded integers on fp8 tensor cores, scale products by tf32 MMA, exact",
+            "f16fold": "f16 tensor cores (kind::f16): int4 codes x int4 weights folded with their bf16 group scales, exact"}[CODES])
         line = {
             "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_max * 1e3, "higher_is_better": True, "scaling": "weak",
@@ -460,8 +476,9 @@ def main():
             "e2e": {"value": e2e_value, "unit": unit, "ms_per_step": e2e_max * 1e3,
                     "h2d_bytes_per_step": wl["h2d"], "d2h_bytes_per_step": wl["d2h"]},
             "gpu_launches": wl["launches_per_step"] * args.steps,
-            "roofline": {"bound": "tensor", "kernel": "w4a4_gemm_kernel", "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "tensor", "kernel": GEMM_KERNEL[CODES], "achieved": achieved, "peak": peak,
                          "unit": "TOPS", "frac": achieved / peak, "peak_source": peak_source,
+                         "frac_of_measured_bf16_peak": achieved / F16_PEAK_TFLOPS if F16_PEAK_TFLOPS else None,
                          "frac_of_nominal_int8": achieved / INT8_NOMINAL_TOPS, "kernel_ms": kernel_ms,
                          "launches_measured": gemm_launches, "algorithmic": wl["algorithmic"], "traffic": None},
             "cpu_baseline": cpu,

@@ -203,7 +203,7 @@ static void operands(wdl::w4a4::GemmArgs& g, const void* a, const float* a_scale
   g.wscale = w_scales, g.M = M, g.N = N, g.K = K, g.a_signed = 1u, g.code_format = code_format;
   static const int variant = [] {
     const char* v = getenv("WDL_GEMM_VARIANT");
-    return v ? atoi(v) : 0;
+    return v ? atoi(v) : 1;  // f32x2 promotion by default (the scalar one needs more registers than it has)
   }();
   g.variant = variant;
   g.ep.ascale = a_scales;

@@ -209,12 +209,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int j = 0; j < 64; ++j) acc2[j] = 0ull;
 
-    float sx_next = row_ok ? __ldg(ep.ascale + m) : 0.f;
+    // sx[g, m], loaded kAhead groups ahead through a ring of registers: a group lasts well under the latency of
+    // a load that misses L2, and the promotion of every element waits on it
+    constexpr int kAhead = 4;
+    float sxr[kAhead];
+#pragma unroll
+    for (int i = 0; i < kAhead; ++i) sxr[i] = row_ok && i < G ? __ldg(ep.ascale + static_cast<size_t>(i) * M + m) : 0.f;
     bool ok = true;
     for (int g = 0; g < G; ++g) {
       const int b = g & 1, kt = g / GPS, s = kt % STAGES, sub = g % GPS;
-      const uint64_t sx2 = pack2(sx_next, sx_next);
-      if (g + 1 < G) sx_next = row_ok ? __ldg(ep.ascale + static_cast<size_t>(g + 1) * M + m) : 0.f;
+      const uint64_t sx2 = pack2(sxr[0], sxr[0]);
+#pragma unroll
+      for (int i = 0; i + 1 < kAhead; ++i) sxr[i] = sxr[i + 1];
+      sxr[kAhead - 1] = row_ok && g + kAhead < G ? __ldg(ep.ascale + static_cast<size_t>(g + kAhead) * M + m) : 0.f;
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_full[b], (g >> 1) & 1, err, kErrWaitAccFull));
       if (!ok) break;
       tc_fence_after();
@@ -418,7 +425,9 @@ int gemm_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
     WDL_GEMM_CASE(kEpiResidualF32, true, false)
     WDL_GEMM_CASE(kEpiResidualF32, true, true)
     WDL_GEMM_CASE(kEpiDumpGroup, false, false)
+    WDL_GEMM_CASE(kEpiDumpGroup, false, true)
     WDL_GEMM_CASE(kEpiDumpGroup, true, false)
+    WDL_GEMM_CASE(kEpiDumpGroup, true, true)
     WDL_GEMM_CASE(kEpiGeluU4, true, false)
     WDL_GEMM_CASE(kEpiGeluU4, true, true)
 #undef WDL_GEMM_CASE

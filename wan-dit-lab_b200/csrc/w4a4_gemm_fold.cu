@@ -146,34 +146,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int j = 0; j < 128; ++j) acc[j] = 0.f;
 
-    // sx[g, m] * 2^F (exact: a power of two), loaded a group ahead
-    float mul_next = row_ok ? __fmul_rn(__ldg(ep.ascale + m), unfold) : 0.f;
+    // sx[g, m], loaded kAhead groups ahead through a ring of registers: a group lasts well under the latency of
+    // a load that misses L2, and the promotion of every element waits on it
+    constexpr int kAhead = 4;
+    float sxr[kAhead];
+#pragma unroll
+    for (int i = 0; i < kAhead; ++i) sxr[i] = row_ok && i < G ? __ldg(ep.ascale + static_cast<size_t>(i) * M + m) : 0.f;
     bool ok = true;
     for (int g = 0; g < G; ++g) {
       const int b = g & 1;
-      const float mul = mul_next;
-      if (g + 1 < G) mul_next = row_ok ? __fmul_rn(__ldg(ep.ascale + static_cast<size_t>(g + 1) * M + m), unfold) : 0.f;
+      const float mul = __fmul_rn(sxr[0], unfold);  // sx * 2^F, exact: a power of two
+#pragma unroll
+      for (int i = 0; i + 1 < kAhead; ++i) sxr[i] = sxr[i + 1];
+      sxr[kAhead - 1] = row_ok && g + kAhead < G ? __ldg(ep.ascale + static_cast<size_t>(g + kAhead) * M + m) : 0.f;
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_full[b], (g >> 1) & 1, err, kErrWaitAccFull));
       if (!ok) break;
       tc_fence_after();
       const uint32_t t_buf = t_row + b * BN;
-      // Drain the group's 128 columns in 4 chunks of 32, loading chunk c + 1 while chunk c is promoted.
+      // Drain the group's 128 columns in two rounds of 64 (two 32-column loads in flight, one wait each round):
+      // tcgen05.wait::ld waits for every load of the thread, so fewer, larger rounds expose its latency less.
       uint32_t ra[32], rb[32];
-      tmem_ld32(t_buf, ra);
-      tmem_ld_wait(ra);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
-        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
-        if (c < 3) tmem_ld32(t_buf + (c + 1) * 32, nxt);
-        if (c == 3) {  // every column of this buffer is in registers: the MMA may overwrite it
+      for (int r = 0; r < 2; ++r) {
+        tmem_ld32(t_buf + r * 64, ra);
+        tmem_ld32(t_buf + r * 64 + 32, rb);
+        tmem_ld_wait(ra);
+        tmem_ld_wait(rb);
+        if (r == 1) {  // every column of this buffer is in registers: the MMA may overwrite it
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.acc_empty[b]);
         }
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[c * 32 + j] = fmaf(__uint_as_float(cur[j]), mul, acc[c * 32 + j]);
-        if (c < 3) tmem_ld_wait(nxt);
+        for (int j = 0; j < 32; ++j) acc[r * 64 + j] = fmaf(__uint_as_float(ra[j]), mul, acc[r * 64 + j]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[r * 64 + 32 + j] = fmaf(__uint_as_float(rb[j]), mul, acc[r * 64 + 32 + j]);
       }
     }
 

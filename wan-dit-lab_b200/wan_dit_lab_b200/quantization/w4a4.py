@@ -29,7 +29,7 @@ GROUP = 64  # input channels per INT4 scale (reference w4a4.py:29)
 # "f16fold" holds float16 operands: activation codes, and weights folded with their bf16 group scales (exact),
 # so that the GEMM's promotion is one fused multiply-add by the activation scale (same results bit for bit); a
 # layer whose folded weights would not be exact (non-bf16 scales) falls back to "e4m3".
-CODE_FORMAT = "e4m3"
+CODE_FORMAT = "f16fold"
 GELU_SHIFT = 0.171875  # GELU(x) + GELU_SHIFT >= 0: the hidden layer of gelu_mlp is quantized unsigned (w4a4.py:195)
 PARTS = ("qweight", "wscales", "proj_down", "proj_up", "smooth", "bias")  # w4a4.py:207
 
