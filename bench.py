@@ -271,7 +271,7 @@ def rollout_workload(device, rank=0, chunks=7, layers=30):
                         "tokens_per_chunk": 1392, "keys_per_chunk": [1392 * (c + 1) for c in range(chunks)],
                         "chunks": chunks, "layers": layers,
                         "codes": CODES, "l2": "inputs larger than L2 (5 GB of weights per pass)"},
-                algorithmic={"gemm_int_ops_per_block_pass": per_block, "gemm_launches_per_block_pass": 5},
+                algorithmic={"gemm_int_ops_per_block_pass": per_block, "gemm_launches_per_block_pass": 6},
                 cpu=lambda: cpu_block_sample(), dtype="W4A4 (int4 x int4 exact on fp8/int8 tensor cores) + INT8/FP8 Sage "
                                                       "attention; fp32 residual stream")
 

@@ -101,7 +101,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
+  // row tiles vary fastest: the CTAs that run together share their weight tile (read from HBM about once)
+  const int m_tile = blockIdx.x, n_tile = blockIdx.y;
   const int G = K / GROUP, KT = K / BK;
 
   // zero halves of the scale blocks (never written again), made visible to the tensor core's proxy
@@ -389,7 +390,7 @@ int gemm_ts_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
     *why = "cuTensorMapEncodeTiled rejected an operand (alignment or stride)";
     return 2;
   }
-  const dim3 grid(a.N / ts::BN, (a.M + ts::BM - 1) / ts::BM);
+  const dim3 grid((a.M + ts::BM - 1) / ts::BM, a.N / ts::BN);
   cudaError_t e = cudaSuccess;
   auto launch = [&](auto kernel) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(ts::kSmemBytes));
