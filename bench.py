@@ -60,6 +60,11 @@ def _measured_bf16_peak():
         return None
 
 
+# DRAM traffic per GEMM launch from one ncu capture of a block pass (dram__bytes_read.sum + dram__bytes_write.sum,
+# mean over its six launches); the capture and its command are in the profiles folder.
+GEMM_TRAFFIC = {"f16fold": 133.9e6}
+GEMM_TRAFFIC_SOURCE = "profiles/gemm_fold_kernel_block_pass_1392_tokens.md"
+
 F16_PEAK_TFLOPS = _measured_bf16_peak()  # the folded format runs on the 16-bit tensor pipe: its own ceiling
 
 
@@ -480,7 +485,10 @@ def main():
                          "unit": "TOPS", "frac": achieved / peak, "peak_source": peak_source,
                          "frac_of_measured_bf16_peak": achieved / F16_PEAK_TFLOPS if F16_PEAK_TFLOPS else None,
                          "frac_of_nominal_int8": achieved / INT8_NOMINAL_TOPS, "kernel_ms": kernel_ms,
-                         "launches_measured": gemm_launches, "algorithmic": wl["algorithmic"], "traffic": None},
+                         "launches_measured": gemm_launches, "algorithmic": wl["algorithmic"],
+                         "traffic": GEMM_TRAFFIC.get(CODES) if rollout else None,
+                         "traffic_unit": "DRAM bytes read + written per GEMM launch (mean of a block pass's six)",
+                         "traffic_source": GEMM_TRAFFIC_SOURCE if rollout and CODES in GEMM_TRAFFIC else None},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
         }
