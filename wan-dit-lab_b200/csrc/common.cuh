@@ -226,6 +226,17 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// GELU in its tanh form (torch.nn.GELU(approximate="tanh"), the feed forward of models/block.py:8-9):
+// 0.5 x (1 + tanh(y)), y = sqrt(2 / pi) (x + 0.044715 x^3). From tanh(y) = 1 - 2 / (e^(2y) + 1) it equals
+// x - x / (e^(2y) + 1); e^(2y) = 2^(2 y log2(e)) on the special function unit, the quotient by the fast division
+// (relative error of a few 1e-7, against the 2^-4 steps of the INT4 codes the result is quantized to). Saturates
+// cleanly: e^(2y) -> inf gives x, e^(2y) -> 0 gives 0.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float y = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  const float e = ex2(2.885390081777927f * y);
+  return x - __fdividef(x, e + 1.f);
+}
+
 // tcgen05.wait::ld that also names the 32 destination registers of the load it completes, so that the compiler
 // cannot move any use of them above the wait.
 __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {

@@ -45,14 +45,6 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;  // + alignment slack of the 
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// GELU in its tanh form (torch.nn.GELU(approximate="tanh"), the feed forward of models/block.py:8-9):
-// 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3))), in float32.
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float cube = x * x * x;
-  const float inner = 0.7978845608028654f * (x + 0.044715f * cube);
-  return 0.5f * x * (1.f + tanhf(inner));
-}
-
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));

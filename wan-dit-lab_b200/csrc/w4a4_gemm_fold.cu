@@ -51,12 +51,6 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float cube = x * x * x;
-  const float inner = 0.7978845608028654f * (x + 0.044715f * cube);
-  return 0.5f * x * (1.f + tanhf(inner));
-}
-
 template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_fold_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -185,6 +179,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
+    if constexpr (kMode == kEpiResidualF32) {
+      // Residual update through a per-warp 32 x 32 transpose in shared memory (the pipeline buffers, idle once every
+      // MMA has completed): lane l then owns column l of a 32-column block and the warp reads and writes whole rows
+      // (128 contiguous bytes) instead of 32 rows at once, all 32 rows' loads in flight together; bias and gate are
+      // loaded once per column. Same arithmetic per element as a thread-per-row update.
+      fence_proxy_async_smem();
+      float* tw = reinterpret_cast<float*>(sm.a[0]) + (warp - 4) * 32 * 33;
+      const int m0 = m_tile * BM + q * 32;
+#pragma unroll
+      for (int blk = 0; blk < 4; ++blk) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = acc[blk * 32 + j];
+        __syncwarp();
+        const int n = n_tile * BN + h * 128 + blk * 32 + lane;
+        const float bn = ep.bias ? __ldg(ep.bias + n) : 0.f;
+        if (ok) {
+          {
+            // residual stream update in fp32: x_new = x + float(bf16(acc + bias)) * gate   (gate 1 when absent)
+            const float gn = ep.gate ? __ldg(ep.gate + n) : 0.f;
+            float* out = reinterpret_cast<float*>(ep.out) + n;
+            const float* res = ep.residual + n;
+            float x[32];  // all 32 rows' residuals in flight at once
+#pragma unroll
+            for (int r = 0; r < 32; ++r) x[r] = m0 + r < M ? res[static_cast<size_t>(m0 + r) * ep.ld_res] : 0.f;
+#pragma unroll
+            for (int r = 0; r < 32; ++r) {
+              const float o = bf16_round(tw[r * 33 + lane] + bn);
+              if (m0 + r < M)
+                out[static_cast<size_t>(m0 + r) * ep.ld_out] = ep.gate ? __fadd_rn(x[r], __fmul_rn(o, gn)) : __fadd_rn(x[r], o);
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
     if (ok && row_ok) {
       const int n0 = n_tile * BN + h * 128;
       if constexpr (kMode == kEpiBf16) {
@@ -236,21 +265,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ep.out_scales[static_cast<size_t>((n0 + g2 * 64) / 64) * M + m] =
               ep.out_scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16_round(scale);
-        }
-      } else if constexpr (kMode == kEpiResidualF32) {
-        // residual stream update in fp32: x_new = x + float(bf16(acc + bias)) * gate   (gate 1 when absent)
-        float* out = reinterpret_cast<float*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
-        const float* res = ep.residual + static_cast<size_t>(m) * ep.ld_res + n0;
-#pragma unroll
-        for (int j = 0; j < 128; j += 4) {
-          const float4 r = *reinterpret_cast<const float4*>(res + j);
-          float v[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float o = bf16_round(acc[j + i] + (ep.bias ? __ldg(ep.bias + n0 + j + i) : 0.f));
-            v[i] = ep.gate ? __fadd_rn(v[i], __fmul_rn(o, __ldg(ep.gate + n0 + j + i))) : __fadd_rn(v[i], o);
-          }
-          *reinterpret_cast<float4*>(out + j) = make_float4(v[0], v[1], v[2], v[3]);
         }
       }
     }

@@ -81,12 +81,6 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t desc_a, uint6
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float cube = x * x * x;
-  const float inner = 0.7978845608028654f * (x + 0.044715f * cube);
-  return 0.5f * x * (1.f + tanhf(inner));
-}
-
 // acc[j] = fma(P[j], S[j], acc[j]) for the 32 columns of one TMEM chunk.
 __device__ __forceinline__ void promote32(float (&acc)[64], int base, const uint32_t (&p)[32], const uint32_t (&s)[32]) {
 #pragma unroll
