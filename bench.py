@@ -277,7 +277,7 @@ def rollout_workload(device, rank=0, chunks=7, layers=30):
                         "chunks": chunks, "layers": layers,
                         "codes": CODES, "l2": "inputs larger than L2 (5 GB of weights per pass)"},
                 algorithmic={"gemm_int_ops_per_block_pass": per_block, "gemm_launches_per_block_pass": 6},
-                cpu=lambda: cpu_block_sample(), dtype="W4A4 (int4 x int4 exact on fp8/int8 tensor cores) + INT8/FP8 Sage "
+                cpu=lambda: cpu_block_sample(), dtype="W4A4 (int4 x int4 exact on int8 tensor cores) + INT8/FP8 Sage "
                                                       "attention; fp32 residual stream")
 
 

@@ -53,6 +53,60 @@ struct Source {
       o[0] = f.x, o[1] = f.y, o[2] = f.z, o[3] = f.w;
     }
   }
+
+  // Channels d .. d + 3 of N keys j[0..N) (those with valid[i]), all loads issued before any is used. `where`:
+  // 1 every key is in the cache, 2 every key in the chunk, 0 mixed (then key by key through get4).
+  template <int N>
+  __device__ __forceinline__ void gather4(const int (&j)[N], const bool (&valid)[N], int where, int h, int d,
+                                          float (&o)[N][4]) const {
+    if (where == 1) {
+      uint32_t w[N];
+      float s[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int64_t r = static_cast<int64_t>(valid[i] ? j[i] : 0) * H + h;
+        w[i] = valid[i] ? __ldg(reinterpret_cast<const uint32_t*>(cache + r * 128 + d)) : 0u;
+        s[i] = valid[i] ? __ldg(scale + r) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const __half2 lo(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[i] & 0xFFFFu), __NV_E4M3));
+        const __half2 hi(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[i] >> 16), __NV_E4M3));
+        const float2 a = __half22float2(lo), b = __half22float2(hi);
+        o[i][0] = a.x * s[i], o[i][1] = a.y * s[i], o[i][2] = b.x * s[i], o[i][3] = b.y * s[i];
+      }
+    } else if (where == 2 && chunk_bf16) {
+      uint2 u[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        u[i] = valid[i] ? __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(chunk) +
+                                                               static_cast<int64_t>(j[i] - at) * ld + h * 128 + d))
+                        : make_uint2(0u, 0u);
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[i].x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[i].y));
+        o[i][0] = a.x, o[i][1] = a.y, o[i][2] = b.x, o[i][3] = b.y;
+      }
+    } else if (where == 2) {
+      float4 f[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        f[i] = valid[i] ? __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(chunk) +
+                                                                static_cast<int64_t>(j[i] - at) * ld + h * 128 + d))
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < N; ++i) o[i][0] = f[i].x, o[i][1] = f[i].y, o[i][2] = f[i].z, o[i][3] = f[i].w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        if (valid[i]) get4(j[i], h, d, o[i]);
+        else o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      }
+    }
+  }
+  // where the keys [j0, j1) lie: 1 all cached, 2 all in the chunk, 0 both
+  __device__ __forceinline__ int where(int j0, int j1) const { return j1 <= at ? 1 : (j0 >= at ? 2 : 0); }
 };
 
 // ---- pass 1: per (64-token tile, head), per channel: sum of K and max |V| over the tile. Warp w reads the 16
@@ -63,13 +117,21 @@ __global__ void __launch_bounds__(128) partials_kernel(Source ks, Source vs, flo
   const int tile = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float s[4] = {0.f, 0.f, 0.f, 0.f}, m[4] = {0.f, 0.f, 0.f, 0.f};
-  const int j0 = tile * 64 + warp * 16, j1 = min(ks.L, j0 + 16);
-  for (int j = j0; j < j1; ++j) {
-    float k[4], v[4];
-    ks.get4(j, h, lane * 4, k);
-    vs.get4(j, h, lane * 4, v);
+  const int j0 = tile * 64 + warp * 16;
+  const int where = ks.where(j0, min(ks.L, j0 + 16));
+  int j[8];
+  bool valid[8];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) s[c] += k[c], m[c] = fmaxf(m[c], fabsf(v[c]));
+  for (int half = 0; half < 2; ++half) {  // 8 keys at a time: 16 loads (K and V) in flight per lane
+#pragma unroll
+    for (int i = 0; i < 8; ++i) j[i] = j0 + half * 8 + i, valid[i] = j[i] < ks.L;
+    float k[8][4], v[8][4];
+    ks.gather4(j, valid, where, h, lane * 4, k);
+    vs.gather4(j, valid, where, h, lane * 4, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)  // keys in order: the same float sums as one key at a time
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[c] += k[i][c], m[c] = fmaxf(m[c], fabsf(v[i][c]));
   }
 #pragma unroll
   for (int c = 0; c < 4; ++c) red[0][warp][lane * 4 + c] = s[c], red[1][warp][lane * 4 + c] = m[c];
@@ -85,7 +147,18 @@ __global__ void __launch_bounds__(128) reduce_kernel(const float* ksum, const fl
                                                      float* kmean, float* v_scale) {
   const int h = blockIdx.x, d = threadIdx.x;
   float s = 0.f, m = 0.f;
-  for (int t = 0; t < tiles; ++t) {
+  int t = 0;
+  for (; t + 8 <= tiles; t += 8) {  // 16 loads in flight, then summed in tile order
+    float a[8], b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      a[i] = ksum[(static_cast<int64_t>(t + i) * H + h) * 128 + d];
+      b[i] = vmax[(static_cast<int64_t>(t + i) * H + h) * 128 + d];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += a[i], m = fmaxf(m, b[i]);
+  }
+  for (; t < tiles; ++t) {
     s += ksum[(static_cast<int64_t>(t) * H + h) * 128 + d];
     m = fmaxf(m, vmax[(static_cast<int64_t>(t) * H + h) * 128 + d]);
   }
@@ -118,22 +191,23 @@ __global__ void __launch_bounds__(128) quant_kv_kernel(Source ks, Source vs, con
     const float4 mean = *reinterpret_cast<const float4*>(kmean + h * 128 + lane * 4);
     float x[16][4];
     float amax = 0.f;
+    int jj[16];
+    bool valid[16];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int j = blk * 64 + 8 * i + 2 * g + e;
-        float* r = x[2 * i + e];
-        if (j < L) {
-          ks.get4(j, h, lane * 4, x[2 * i + e]);
-          r[0] = __fsub_rn(r[0], mean.x), r[1] = __fsub_rn(r[1], mean.y);
-          r[2] = __fsub_rn(r[2], mean.z), r[3] = __fsub_rn(r[3], mean.w);
-        } else {
-          r[0] = r[1] = r[2] = r[3] = 0.f;
-        }
+      for (int e = 0; e < 2; ++e) jj[2 * i + e] = blk * 64 + 8 * i + 2 * g + e, valid[2 * i + e] = jj[2 * i + e] < L;
+    ks.gather4(jj, valid, ks.where(blk * 64, min(L, blk * 64 + 64)), h, lane * 4, x);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) amax = fmaxf(amax, fabsf(r[c]));
+    for (int t = 0; t < 16; ++t) {
+      float* r = x[t];
+      if (valid[t]) {
+        r[0] = __fsub_rn(r[0], mean.x), r[1] = __fsub_rn(r[1], mean.y);
+        r[2] = __fsub_rn(r[2], mean.z), r[3] = __fsub_rn(r[3], mean.w);
       }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) amax = fmaxf(amax, fabsf(r[c]));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
     const float scale = __fadd_rn(__fdiv_rn(amax, 127.f), 1e-7f);
@@ -159,20 +233,22 @@ __global__ void __launch_bounds__(128) quant_kv_kernel(Source ks, Source vs, con
 #pragma unroll
     for (int c = 0; c < 4; ++c) rcp[c] = __frcp_rn(s[c]);
     uint32_t w[4][4];  // [channel c][key word]: keys 16 g + 4 kw .. + 3 of channel 4 lane + c
+    int jj[16];
+    bool valid[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) jj[t] = blk * 64 + g * 16 + t, valid[t] = jj[t] < L;
+    float v[16][4];
+    vs.gather4(jj, valid, vs.where(blk * 64, min(L, blk * 64 + 64)), h, lane * 4, v);
 #pragma unroll
     for (int kw = 0; kw < 4; ++kw) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) w[c][kw] = 0;
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const int j = blk * 64 + g * 16 + kw * 4 + b;
-        if (j < L) {
-          float v[4];
-          vs.get4(j, h, lane * 4, v);
+      for (int b = 0; b < 4; ++b)
+        if (valid[kw * 4 + b])
 #pragma unroll
-          for (int c = 0; c < 4; ++c) w[c][kw] |= static_cast<uint32_t>(e4m3(div_rn_by(v[c], s[c], rcp[c]))) << (8 * b);
-        }
-      }
+          for (int c = 0; c < 4; ++c)
+            w[c][kw] |= static_cast<uint32_t>(e4m3(div_rn_by(v[kw * 4 + b][c], s[c], rcp[c]))) << (8 * b);
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c)
