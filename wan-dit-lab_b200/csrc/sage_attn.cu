@@ -17,6 +17,10 @@
 #include "common.cuh"
 #include "sage.h"
 
+#include <climits>
+#include <cstdint>
+#include <type_traits>
+
 namespace wdl {
 namespace sage {
 
@@ -24,6 +28,7 @@ constexpr int BQ = 128, BKV = 128, HD = 128;
 constexpr int kAttnThreads = 192;
 constexpr uint32_t kAttnTmemCols = 256;
 constexpr float kPScale = 448.f;
+constexpr float kLog2PScale = 8.807354922057604f;  // log2(448)
 
 struct __align__(1024) AttnSmem {
   uint8_t q[BQ * HD];
@@ -153,10 +158,17 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     uint8_t* prow = sm.p + (row >> 3) * 1024 + (row & 7) * 128;
+    float ks_next[8];  // the next tile's key scales, loaded a tile ahead (off the critical path)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ks_next[i] = __ldg(ks_head + i);
     for (int j = 0; j < T; ++j) {
       float w[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[i] = c * __ldg(ks_head + j * 8 + i);
+      for (int i = 0; i < 8; ++i) w[i] = c * ks_next[i];
+      if (j + 1 < T) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ks_next[i] = __ldg(ks_head + (j + 1) * 8 + i);
+      }
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.s_full, j & 1, err, kErrWaitAccFull));
       if (!ok) break;
       tc_fence_after();
@@ -167,36 +179,48 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.s_empty);
-      float f[128];
-      float mx = -INFINITY;
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = q * 32 + i;
-          f[col] = exact_float(s[q][i]) * w[(col / 64) * 4 + (col % 8) / 2];
-        }
-      const int lim = a.L - j * BKV;
-      if (lim < BKV) {
-#pragma unroll
-        for (int col = 0; col < 128; ++col)
-          if (col >= lim) f[col] = -INFINITY;
-      }
-#pragma unroll
-      for (int col = 0; col < 128; ++col) mx = fmaxf(mx, f[col]);
-      const float m_new = fmaxf(m, mx);
-      const float alpha = ex2(m - m_new);
-      float sum = 0.f;
+      // Row max per scale group over the integer scores: w > 0 and rounding is monotonic, so max(S) * w rounds
+      // to max(S * w) (the same m as scaling every score first). Then one FMA per score gives the exponent
+      // argument S * w + log2(448) - m, so that 2^arg = 448 p directly (P's FP8 scale folded in); l sums 448 p.
+      const int lim = a.L - j * BKV;  // valid keys of this tile (all 128 but in the last one)
+      float m_new = m, alpha = 1.f, sum = 0.f;
       uint32_t pk[32];
+      auto tile = [&](auto masked) {
+        constexpr bool kMasked = decltype(masked)::value;
+        int32_t gmax[8];
 #pragma unroll
-      for (int col = 0; col < 128; col += 4) {
-        const float p0 = ex2(f[col] - m_new), p1 = ex2(f[col + 1] - m_new);
-        const float p2 = ex2(f[col + 2] - m_new), p3 = ex2(f[col + 3] - m_new);
-        sum += (p0 + p1) + (p2 + p3);
-        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(p0 * kPScale, p1 * kPScale), __NV_SATFINITE, __NV_E4M3);
-        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(p2 * kPScale, p3 * kPScale), __NV_SATFINITE, __NV_E4M3);
-        pk[col / 4] = lo | (hi << 16);
-      }
+        for (int g = 0; g < 8; ++g) gmax[g] = INT32_MIN;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = q * 32 + i, g = (col / 64) * 4 + (col % 8) / 2;
+            if (!kMasked || col < lim) gmax[g] = max(gmax[g], static_cast<int32_t>(s[q][i]));
+          }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          if (gmax[g] != INT32_MIN) mx = fmaxf(mx, exact_float(static_cast<uint32_t>(gmax[g])) * w[g]);
+        m_new = fmaxf(m, mx);
+        alpha = ex2(m - m_new);
+        const float base = kLog2PScale - m_new;
+#pragma unroll
+        for (int col = 0; col < 128; col += 4) {
+          float p[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c2 = col + e, g = (c2 / 64) * 4 + (c2 % 8) / 2;
+            p[e] = ex2(fmaf(exact_float(s[c2 / 32][c2 % 32]), w[g], base));
+            if (kMasked && c2 >= lim) p[e] = 0.f;
+          }
+          sum += (p[0] + p[1]) + (p[2] + p[3]);
+          const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(p[0], p[1]), __NV_SATFINITE, __NV_E4M3);
+          const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(p[2], p[3]), __NV_SATFINITE, __NV_E4M3);
+          pk[col / 4] = lo | (hi << 16);
+        }
+      };
+      if (lim >= BKV) tile(std::false_type{});
+      else tile(std::true_type{});
       l = l * alpha + sum;
       if (j > 0) {
         // P V of the previous tile must be done: O is then stable and the P buffer free
@@ -229,7 +253,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.o_done, (T - 1) & 1, err, kErrWaitAccFull));
     if (ok) {
       tc_fence_after();
-      const float inv = 1.f / (kPScale * l);
+      const float inv = 1.f / l;  // l sums 448 p
       const float* vsc = a.v_scale + h * HD;
       __nv_bfloat16* out = a.out + static_cast<int64_t>(t) * a.ld_out + h * HD;
 #pragma unroll
