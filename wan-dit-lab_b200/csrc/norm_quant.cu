@@ -61,7 +61,7 @@ __device__ __forceinline__ uint32_t code_byte(int q, int fmt) {
 }
 
 template <typename TX>
-__global__ void __launch_bounds__(kRowThreads) ln_quant_kernel(const TX* __restrict__ x, LnQuantArgs a) {
+__global__ void __launch_bounds__(kRowThreads, 6) ln_quant_kernel(const TX* __restrict__ x, LnQuantArgs a) {
   __shared__ float red[kRowThreads / 32];
   const int t = threadIdx.x, m = blockIdx.x;
   const int K = a.K;
@@ -168,7 +168,7 @@ void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s) {
 }
 
 // Same thread layout as ln_quant: one CTA of 128 threads per row.
-__global__ void __launch_bounds__(kRowThreads) rms_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+__global__ void __launch_bounds__(kRowThreads, 8) rms_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                                int K, const float* __restrict__ w, float eps,
                                                                float* __restrict__ out, int64_t ldo) {
   __shared__ float red[kRowThreads / 32];

@@ -79,54 +79,64 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
   const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (m >= M) return;
   const T* xr = x + static_cast<int64_t>(m) * ldx;
-  for (int k0 = 0; k0 < K; k0 += 256) {
-    const int k = k0 + lane * 8;
-    const bool valid = k < K;  // K % 64 == 0: a group of 8 lanes is valid or invalid as a whole
-    float v[8];
-    if (valid) {
-      load8<T>(xr + k, v);
-      if (kSmooth) {
-        float s[8];
-        load8<__nv_bfloat16>(smooth + k, s);
+  // four 256-column chunks per round, their loads issued together (K % 64 == 0: a group of 8 lanes is valid or
+  // invalid as a whole)
+  for (int k0 = 0; k0 < K; k0 += 1024) {
+    float v[4][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __fdiv_rn(v[i], s[i]);
+    for (int c = 0; c < 4; ++c) {
+      const int k = k0 + c * 256 + lane * 8;
+      if (k < K) {
+        load8<T>(xr + k, v[c]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[c][i] = 0.f;
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = 0.f;
     }
-    float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
-    if (!valid) continue;
-    const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
-    const float r = __frcp_rn(scale);
-    int q[8];
+    for (int c = 0; c < 4; ++c) {
+      if (k0 + c * 256 >= K) break;  // uniform over the warp
+      const int k = k0 + c * 256 + lane * 8;
+      const bool valid = k < K;
+      if (kSmooth && valid) {
+        float sm[8];
+        load8<__nv_bfloat16>(smooth + k, sm);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = max(-8, min(7, __float2int_rn(div_rn_by(v[i], scale, r))));
-    if constexpr (kFmt == 3) {
-      *reinterpret_cast<uint4*>(codes + (static_cast<int64_t>(m) * K + k) * 2) =
-          make_uint4(code_pair_f16(q[0], q[1]), code_pair_f16(q[2], q[3]), code_pair_f16(q[4], q[5]),
-                     code_pair_f16(q[6], q[7]));
-    } else {
-      constexpr bool kE4M3 = kFmt == 1;
-      uint2 c;
-      c.x = code_byte<kE4M3>(q[0]) | (code_byte<kE4M3>(q[1]) << 8) | (code_byte<kE4M3>(q[2]) << 16) |
-            (code_byte<kE4M3>(q[3]) << 24);
-      c.y = code_byte<kE4M3>(q[4]) | (code_byte<kE4M3>(q[5]) << 8) | (code_byte<kE4M3>(q[6]) << 16) |
-            (code_byte<kE4M3>(q[7]) << 24);
-      *reinterpret_cast<uint2*>(codes + static_cast<int64_t>(m) * K + k) = c;
+        for (int i = 0; i < 8; ++i) v[c][i] = __fdiv_rn(v[c][i], sm[i]);
+      }
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[c][i]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+      if (!valid) continue;
+      const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
+      const float r = __frcp_rn(scale);
+      int q[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[i] = max(-8, min(7, __float2int_rn(div_rn_by(v[c][i], scale, r))));
+      if constexpr (kFmt == 3) {
+        *reinterpret_cast<uint4*>(codes + (static_cast<int64_t>(m) * K + k) * 2) =
+            make_uint4(code_pair_f16(q[0], q[1]), code_pair_f16(q[2], q[3]), code_pair_f16(q[4], q[5]),
+                       code_pair_f16(q[6], q[7]));
+      } else {
+        constexpr bool kE4M3 = kFmt == 1;
+        uint2 cw;
+        cw.x = code_byte<kE4M3>(q[0]) | (code_byte<kE4M3>(q[1]) << 8) | (code_byte<kE4M3>(q[2]) << 16) |
+               (code_byte<kE4M3>(q[3]) << 24);
+        cw.y = code_byte<kE4M3>(q[4]) | (code_byte<kE4M3>(q[5]) << 8) | (code_byte<kE4M3>(q[6]) << 16) |
+               (code_byte<kE4M3>(q[7]) << 24);
+        *reinterpret_cast<uint2*>(codes + static_cast<int64_t>(m) * K + k) = cw;
+      }
+      if (kPack) {
+        uint32_t pw = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pw |= static_cast<uint32_t>((q[2 * i] & 0xF) | ((q[2 * i + 1] & 0xF) << 4)) << (8 * i);
+        *reinterpret_cast<uint32_t*>(packed + static_cast<int64_t>(m) * (K / 2) + k / 2) = pw;
+      }
+      if ((lane & 7) == 0) store_scale(scales, static_cast<int64_t>(k / 64) * M + m, scale_pad, round_scale(scale, scale_dtype));
     }
-    if (kPack) {
-      uint32_t p = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) p |= static_cast<uint32_t>((q[2 * i] & 0xF) | ((q[2 * i + 1] & 0xF) << 4)) << (8 * i);
-      *reinterpret_cast<uint32_t*>(packed + static_cast<int64_t>(m) * (K / 2) + k / 2) = p;
-    }
-    if ((lane & 7) == 0) store_scale(scales, static_cast<int64_t>(k / 64) * M + m, scale_pad, round_scale(scale, scale_dtype));
   }
 }
 
