@@ -123,6 +123,25 @@ int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, c
                           const float* bias, const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N,
                           int K, uint8_t* codes, int64_t ldc, float* scales, void* stream);
 
+/* The same three GEMMs with the SVDQuant low-rank branch: `addend` [M, ld_add] f32 (nullable) is added to the
+ * product before the bias, i.e. lora_act * proj_up^T with lora_act = x * proj_down (w4a4_ops.cpp:27, 36: Nunchaku
+ * computes both in the activation quantizer and the GEMM epilogue; here the caller forms the rank-r products, plain
+ * GEMMs, and the epilogue adds them before the bf16 rounding, residual update or GELU). The GELU variant can also
+ * write gelu_out [M, ld_gelu] f32 = GELU(y) before shift and smoothing: the input of the next layer's low-rank
+ * branch (w4a4.py:195-204, the branch reads the hidden activation without the shift). */
+int wdl_w4a4_gemm_add(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                      const float* bias, const float* addend, int64_t ld_add, int M, int N, int K, uint16_t* y,
+                      int64_t ldy, void* stream);
+int wdl_w4a4_gemm_residual_add(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                               int code_format, const float* bias, const float* addend, int64_t ld_add,
+                               const float* gate, const float* residual, int64_t ldr, int M, int N, int K, float* out,
+                               int64_t ldo, void* stream);
+int wdl_w4a4_gemm_gelu_u4_add(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                              int code_format, const float* bias, const float* addend, int64_t ld_add,
+                              const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N, int K,
+                              uint8_t* codes, int64_t ldc, float* scales, float* gelu_out, int64_t ld_gelu,
+                              void* stream);
+
 /* Bytes of scratch wdl_w4a4_linear needs for M tokens of K channels (any code format). */
 size_t wdl_w4a4_linear_workspace(int M, int K);
 

@@ -110,3 +110,40 @@ def weight(W, scale_dtype="bfloat16"):
 def gelu_tanh(x):
     x = np.asarray(x, dtype=np.float32)
     return (0.5 * x * (1.0 + np.tanh(np.float32(0.7978845608028654) * (x + np.float32(0.044715) * x ** 3)))).astype(np.float32)
+
+
+def lowrank(x, down, up):
+    """The SVDQuant low-rank branch (x proj_down) proj_up^T in float32: x [M, K] the layer's input before
+    smoothing (proj_down is already divided by the smoothing, w4a4.py:175), down [K, r], up [N, r]
+    (the bfloat16 factors as float32). Nunchaku forms it in its quantizer (lora_act, fp32) and GEMM epilogue
+    (native/ops/w4a4_ops.cpp:27, 36)."""
+    x = np.asarray(x, np.float32)
+    return ((x @ np.asarray(down, np.float32)).astype(np.float32) @ np.asarray(up, np.float32).T).astype(np.float32)
+
+
+def linear_lowrank(x_bf16, w_codes, w_scales, down, up, bias=None, smooth=None, scale_dtype="bfloat16"):
+    """live::w4a4_linear with its low-rank branch: the INT4 product (linear above, no bias) + the branch + bias,
+    float32 before the final bfloat16 rounding."""
+    y, _, _ = linear(x_bf16, w_codes, w_scales, None, smooth, scale_dtype)
+    if down is not None and np.asarray(down).size:
+        y = y + lowrank(x_bf16, down, up)
+    if bias is not None:
+        y = y + np.asarray(bias, np.float32)[None, :]
+    return y.astype(np.float32)
+
+
+def gelu_mlp(x_bf16, l1, l2, scale_dtype="bfloat16"):
+    """live::w4a4_gelu_mlp (w4a4_ops.cpp:44-63, w4a4.py:195-204) with low-rank branches: h = layer 1 (INT4 + branch
+    + bias); g = GELU_tanh(h); the hidden layer g + 0.171875, divided by layer 2's smoothing, quantized unsigned
+    (scales rounded to scale_dtype); y = layer 2's INT4 product + branch of g (without the shift) + bias. l1, l2:
+    dicts codes [N, K], scales [K/64, N] (stored), down, up, bias, smooth (or None). Returns y float32."""
+    h = linear_lowrank(x_bf16, l1["codes"], l1["scales"], l1["down"], l1["up"], l1["bias"], l1.get("smooth"),
+                       scale_dtype)
+    g = gelu_tanh(h)
+    u = (g + np.float32(GELU_SHIFT)).astype(np.float32)
+    hq, hs = int4_groups(u, l2.get("smooth"), unsigned=True)
+    y = gemm(hq, round_to(hs, scale_dtype).T.copy(), l2["codes"], l2["scales"])
+    if l2["down"] is not None and np.asarray(l2["down"]).size:
+        y = y + lowrank(g, l2["down"], l2["up"])
+    y = y + np.asarray(l2["bias"], np.float32)[None, :]
+    return y.astype(np.float32)

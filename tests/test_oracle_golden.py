@@ -161,3 +161,18 @@ def test_sage_dequantized_attention_is_close_to_exact(n):
     exact = osage.attention(Q, osage.load(ck, cks, K, at), osage.load(cv, cvs, V, at))
     cos = float((sage * exact).sum() / np.linalg.norm(sage) / np.linalg.norm(exact))
     assert cos >= 0.999
+
+
+def test_oracle_lowrank_linear_reduces_to_linear():
+    """The oracle's low-rank linear without a branch is the plain linear, and its branch is linear in x."""
+    rng = np.random.default_rng(5)
+    M, K, N, r = 9, 128, 64, 4
+    x = ow.round_to(rng.standard_normal((M, K)).astype(np.float32), "bfloat16")
+    wq, _, sw = ow.weight(rng.standard_normal((N, K)).astype(np.float32) * 0.02)
+    b = rng.standard_normal(N).astype(np.float32)
+    y0, _, _ = ow.linear(x, wq, sw, b)
+    np.testing.assert_array_equal(ow.linear_lowrank(x, wq, sw, None, None, b), y0)
+    down, up = rng.standard_normal((K, r)).astype(np.float32), rng.standard_normal((N, r)).astype(np.float32)
+    y = ow.linear_lowrank(x, wq, sw, down, up, b)
+    np.testing.assert_allclose(y - y0, (x.astype(np.float64) @ down) @ up.T, rtol=1e-4, atol=1e-3)
+    np.testing.assert_allclose(ow.lowrank(2 * x, down, up), 2 * ow.lowrank(x, down, up), rtol=1e-6)

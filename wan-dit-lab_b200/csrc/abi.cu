@@ -209,23 +209,47 @@ static void operands(wdl::w4a4::GemmArgs& g, const void* a, const float* a_scale
   g.ep.ascale = a_scales;
 }
 
-int wdl_w4a4_gemm(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
-                  const float* bias, int M, int N, int K, uint16_t* y, int64_t ldy, void* stream) {
+// The low-rank branch's fp32 addend [M, ld_add], when given.
+static int set_addend(wdl::w4a4::GemmArgs& g, const float* addend, int64_t ld_add, int N) {
+  if (!addend) return ok();
+  if (ld_add < N || !aligned(addend, 4)) return fail(WDL_ERR_ARGUMENT, "addend rows must hold N floats");
+  g.ep.addend = addend, g.ep.ld_add = ld_add;
+  return ok();
+}
+
+int wdl_w4a4_gemm_add(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                      const float* bias, const float* addend, int64_t ld_add, int M, int N, int K, uint16_t* y,
+                      int64_t ldy, void* stream) {
   if (ldy < N || (ldy * 2) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldy must be >= N with 16-byte aligned rows");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
+  if (set_addend(g, addend, ld_add, N) != WDL_OK) return WDL_ERR_ARGUMENT;
   g.ep.mode = wdl::w4a4::kEpiBf16, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = ldy;
   return gemm_common(g, stream);
+}
+
+int wdl_w4a4_gemm(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                  const float* bias, int M, int N, int K, uint16_t* y, int64_t ldy, void* stream) {
+  return wdl_w4a4_gemm_add(a, a_scales, w, w_scales, code_format, bias, nullptr, 0, M, N, K, y, ldy, stream);
 }
 
 int wdl_w4a4_gemm_residual(const void* a, const float* a_scales, const void* w, const float* w_scales,
                            int code_format, const float* bias, const float* gate, const float* residual, int64_t ldr,
                            int M, int N, int K, float* out, int64_t ldo, void* stream) {
+  return wdl_w4a4_gemm_residual_add(a, a_scales, w, w_scales, code_format, bias, nullptr, 0, gate, residual, ldr, M,
+                                    N, K, out, ldo, stream);
+}
+
+int wdl_w4a4_gemm_residual_add(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                               int code_format, const float* bias, const float* addend, int64_t ld_add,
+                               const float* gate, const float* residual, int64_t ldr, int M, int N, int K, float* out,
+                               int64_t ldo, void* stream) {
   if (!residual) return fail(WDL_ERR_ARGUMENT, "residual must not be null");
   if (ldr < N || ldo < N || (ldr * 4) % 16 != 0 || (ldo * 4) % 16 != 0)
     return fail(WDL_ERR_ARGUMENT, "ldr, ldo must be >= N with 16-byte aligned rows");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
+  if (set_addend(g, addend, ld_add, N) != WDL_OK) return WDL_ERR_ARGUMENT;
   g.ep.mode = wdl::w4a4::kEpiResidualF32, g.ep.bias = bias, g.ep.gate = gate;
   g.ep.residual = residual, g.ep.ld_res = ldr, g.ep.out = out, g.ep.ld_out = ldo;
   return gemm_common(g, stream);
@@ -245,6 +269,16 @@ int wdl_w4a4_gemm_group_partials(const void* a, const float* a_scales, const voi
 int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                           const float* bias, const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N,
                           int K, uint8_t* codes, int64_t ldc, float* scales, void* stream) {
+  return wdl_w4a4_gemm_gelu_u4_add(a, a_scales, w, w_scales, code_format, bias, nullptr, 0, smooth_next, shift,
+                                   scale_dtype, M, N, K, codes, ldc, scales, nullptr, 0, stream);
+}
+
+int wdl_w4a4_gemm_gelu_u4_add(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                              int code_format, const float* bias, const float* addend, int64_t ld_add,
+                              const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N, int K,
+                              uint8_t* codes, int64_t ldc, float* scales, float* gelu_out, int64_t ld_gelu,
+                              void* stream) {
+  if (gelu_out && (ld_gelu < N || !aligned(gelu_out, 4))) return fail(WDL_ERR_ARGUMENT, "gelu_out rows must hold N floats");
   if (code_format == WDL_CODES_INT8)
     return fail(WDL_ERR_ARGUMENT, "the unsigned hidden codes need an E4M3 or float16 code format");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
@@ -253,6 +287,8 @@ int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, c
   if (!scales) return fail(WDL_ERR_ARGUMENT, "null scales");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
+  if (set_addend(g, addend, ld_add, N) != WDL_OK) return WDL_ERR_ARGUMENT;
+  g.ep.gelu_out = gelu_out, g.ep.ld_gelu = ld_gelu;
   g.ep.mode = wdl::w4a4::kEpiGeluU4, g.ep.bias = bias, g.ep.out = codes, g.ep.ld_out = ldc, g.ep.out_scales = scales;
   g.ep.out_smooth = reinterpret_cast<const __nv_bfloat16*>(smooth_next), g.ep.out_scale_dtype = scale_dtype;
   g.ep.gelu_shift = shift;

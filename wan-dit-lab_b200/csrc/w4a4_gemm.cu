@@ -271,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (ok && row_ok) {
       const int n0 = n_tile * BN + h * 128;
+      add_addend<128>(ep, m, n0, acc);
       if constexpr (kMode == kEpiBf16) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
 #pragma unroll
@@ -299,7 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 64; ++j) {
             const int n = n0 + g2 * 64 + j;
-            float t = __fadd_rn(gelu_tanh(acc[g2 * 64 + j] + (ep.bias ? __ldg(ep.bias + n) : 0.f)), ep.gelu_shift);
+            const float gv = gelu_tanh(acc[g2 * 64 + j] + (ep.bias ? __ldg(ep.bias + n) : 0.f));
+            if (ep.gelu_out) ep.gelu_out[static_cast<size_t>(m) * ep.ld_gelu + n] = gv;
+            float t = __fadd_rn(gv, ep.gelu_shift);
             if (ep.out_smooth) t = __fdiv_rn(t, __bfloat162float(ep.out_smooth[n]));
             u[j] = t;
             amax = fmaxf(amax, fabsf(t));

@@ -47,7 +47,23 @@ struct GemmEpilogue {
   const __nv_bfloat16* out_smooth;  // kEpiGeluU4: [N] the next layer's smoothing (nullable)
   int out_scale_dtype;              // kEpiGeluU4: 0 bf16, 1 f16 rounding of the stored scales
   float gelu_shift;                 // kEpiGeluU4: added after GELU (0.171875)
+  const float* addend;  // [M, ld_add] f32 added to the product before bias (the low-rank branch), nullable
+  int64_t ld_add;
+  float* gelu_out;  // kEpiGeluU4: [M, ld_gelu] f32 GELU(y) before shift and smoothing (the next low-rank input), nullable
+  int64_t ld_gelu;
 };
+
+#ifdef __CUDACC__
+// Adds row m, columns [n0, n0 + kCount) of the low-rank branch's product into acc (before the bias), when the
+// epilogue has one. A separate pass over the finished accumulators keeps the modes' own loops as they are without it.
+template <int kCount>
+__device__ __forceinline__ void add_addend(const GemmEpilogue& ep, int m, int n0, float* acc) {
+  if (!ep.addend) return;
+  const float* p = ep.addend + static_cast<size_t>(m) * ep.ld_add + n0;
+#pragma unroll
+  for (int j = 0; j < kCount; ++j) acc[j] += __ldg(p + j);
+}
+#endif
 
 struct GemmArgs {
   const int8_t* a;  // [M, lda] activation codes, one per byte

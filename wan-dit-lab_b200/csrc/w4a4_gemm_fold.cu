@@ -179,6 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
+    if (ok && row_ok) add_addend<128>(ep, m, n_tile * BN + h * 128, acc);
+
     if constexpr (kMode == kEpiResidualF32) {
       // Residual update through a per-warp 32 x 32 transpose in shared memory (the pipeline buffers, idle once every
       // MMA has completed): lane l then owns column l of a 32-column block and the warp reads and writes whole rows
@@ -244,7 +246,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 64; ++j) {
             const int n = n0 + g2 * 64 + j;
-            float t = __fadd_rn(gelu_tanh(acc[g2 * 64 + j] + (ep.bias ? __ldg(ep.bias + n) : 0.f)), ep.gelu_shift);
+            const float gv = gelu_tanh(acc[g2 * 64 + j] + (ep.bias ? __ldg(ep.bias + n) : 0.f));
+            if (ep.gelu_out) ep.gelu_out[static_cast<size_t>(m) * ep.ld_gelu + n] = gv;
+            float t = __fadd_rn(gv, ep.gelu_shift);
             if (ep.out_smooth) t = __fdiv_rn(t, __bfloat162float(ep.out_smooth[n]));
             acc[g2 * 64 + j] = t;
             amax = fmaxf(amax, fabsf(t));

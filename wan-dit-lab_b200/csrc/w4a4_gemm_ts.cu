@@ -253,6 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (ok && row_ok) {
       const int n0 = n_tile * BN + h * 64;
+      add_addend<64>(ep, m, n0, acc);
       if constexpr (kMode == kEpiBf16) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
 #pragma unroll
@@ -279,7 +280,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 64; ++j) {
           const int n = n0 + j;
-          float t = __fadd_rn(gelu_tanh(acc[j] + (ep.bias ? __ldg(ep.bias + n) : 0.f)), ep.gelu_shift);
+          const float gv = gelu_tanh(acc[j] + (ep.bias ? __ldg(ep.bias + n) : 0.f));
+          if (ep.gelu_out) ep.gelu_out[static_cast<size_t>(m) * ep.ld_gelu + n] = gv;
+          float t = __fadd_rn(gv, ep.gelu_shift);
           if (ep.out_smooth) t = __fdiv_rn(t, __bfloat162float(ep.out_smooth[n]));
           acc[j] = t;
           amax = fmaxf(amax, fabsf(t));

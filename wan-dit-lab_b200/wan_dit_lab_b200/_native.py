@@ -30,6 +30,10 @@ SIGNATURES = {
     "wdl_w4a4_gemm": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _P, _I64, _P]),
     "wdl_w4a4_gemm_residual": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _I64, _I, _I, _I, _P, _I64, _P]),
     "wdl_w4a4_gemm_group_partials": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I64, _P]),
+    "wdl_w4a4_gemm_add": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _I, _I, _I, _P, _I64, _P]),
+    "wdl_w4a4_gemm_residual_add": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _P, _P, _I64, _I, _I, _I, _P, _I64, _P]),
+    "wdl_w4a4_gemm_gelu_u4_add": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _P, ctypes.c_float, _I, _I, _I, _I, _P,
+                                       _I64, _P, _P, _I64, _P]),
     "wdl_w4a4_linear_workspace": (_SZ, [_I, _I]),
     "wdl_w4a4_linear": (_I, [_P, _I64, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P, _I64, _P, _SZ, _P]),
     "wdl_w4a4_linear_noalloc": (_I, [_P, _I64, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P, _I64, _P]),

@@ -90,6 +90,9 @@ class WanBlockB200:
         self.parts = parts
         self.layers = {name: w4a4.PreparedW4A4(*(t[k] for k in w4a4.PARTS), code_format=code_format)
                        for name, t in parts.items()}
+        if any(layer.rank for layer in self.layers.values()):
+            raise NotImplementedError("the fused block runs rank-0 W4A4 layers; low-rank packs run through "
+                                      "w4a4.PackedW4A4Linear / w4a4.gelu_mlp")
         if len({layer.code_format for layer in self.layers.values()}) > 1:
             # a layer could not take the requested format: the block's quantizers feed every layer one format
             self.layers = {name: w4a4.PreparedW4A4(*(t[k] for k in w4a4.PARTS), code_format="e4m3")

@@ -159,10 +159,17 @@ class PreparedW4A4:
         K = 2 * half
         if wscales.shape != (K // GROUP, N):
             raise ValueError(f"wscales must be [K/64, N] = [{K // GROUP}, {N}], got {tuple(wscales.shape)}")
-        if proj_down is not None and proj_down.numel() and proj_down.shape[-1] > 0:
-            raise NotImplementedError("the low-rank branch (proj_down/proj_up of rank > 0) is not implemented yet")
         self.N, self.K = N, K
+        # the SVDQuant low-rank branch (rank r, bf16 factors): proj_down [K, r] (already divided by the smoothing:
+        # the branch reads x itself), proj_up [N, r]; y += (x proj_down) proj_up^T, added in the GEMM epilogue
+        self.rank = 0 if proj_down is None or proj_down.numel() == 0 else int(proj_down.shape[-1])
+        if self.rank:
+            if proj_down.shape != (K, self.rank) or proj_up is None or proj_up.shape != (N, self.rank):
+                raise ValueError(f"proj_down must be [K, r] = [{K}, r] and proj_up [N, r] = [{N}, r]")
+            self.down = proj_down.float().contiguous()
+            self.up = proj_up.float().contiguous()
         self.scale_dtype = wscales.dtype
+        self._parts = (qweight, wscales, proj_down, proj_up, smooth, bias)
         fmt = code_format or CODE_FORMAT
         q = qweight.contiguous().view(torch.uint8)
         ws = wscales.contiguous()
@@ -201,6 +208,25 @@ class PreparedW4A4:
         self.scales = torch.tensor([2.0 ** shift], dtype=torch.float32, device=q.device)
         return True
 
+    def lowrank(self, x):
+        """The low-rank branch's contribution (x proj_down) proj_up^T [M, N] float32 for x [M, K] (the layer's
+        input before smoothing), or None at rank 0: two plain float32 GEMMs (cuBLAS); Nunchaku forms the same
+        products in its quantizer and GEMM epilogue (w4a4_ops.cpp:27, 36)."""
+        if not self.rank:
+            return None
+        return ((x.float() @ self.down) @ self.up.t()).contiguous()
+
+    def quantize_input(self, x, work):
+        """x [M, K] bfloat16 -> (codes, scales) of this layer's code format, in the workspace `work`."""
+        M, K = x.shape
+        lib = _native.lib()
+        codes = work[: M * K * 2]
+        scales = work[(M * K * 2 + 255) // 256 * 256:].view(torch.float32)
+        _native.check(lib.wdl_w4a4_quantize_rows(x.data_ptr(), _native.BF16, x.stride(0), _native.ptr(self.smooth), M,
+                                                 K, _scale_code(self.scale_dtype), self.code_format, codes.data_ptr(),
+                                                 scales.data_ptr(), None, _native.stream()))
+        return codes, scales
+
     def __call__(self, x):
         """y [M, N] bfloat16 = x W^T + b for x [M, K] bfloat16."""
         M, K = x.shape
@@ -214,10 +240,18 @@ class PreparedW4A4:
         lib = _native.lib()
         work = torch.empty(lib.wdl_w4a4_linear_workspace(M, K), dtype=torch.uint8, device=x.device)
         with torch.cuda.device(x.device):
-            _native.check(lib.wdl_w4a4_linear(
-                x.data_ptr(), x.stride(0), M, K, _native.ptr(self.smooth), _scale_code(self.scale_dtype),
-                self.codes.data_ptr(), self.scales.data_ptr(), self.code_format, _native.ptr(self.bias), self.N,
-                y.data_ptr(), self.N, work.data_ptr(), work.numel(), _native.stream()))
+            if not self.rank:
+                _native.check(lib.wdl_w4a4_linear(
+                    x.data_ptr(), x.stride(0), M, K, _native.ptr(self.smooth), _scale_code(self.scale_dtype),
+                    self.codes.data_ptr(), self.scales.data_ptr(), self.code_format, _native.ptr(self.bias), self.N,
+                    y.data_ptr(), self.N, work.data_ptr(), work.numel(), _native.stream()))
+            else:
+                add = self.lowrank(x)
+                codes, scales = self.quantize_input(x, work)
+                _native.check(lib.wdl_w4a4_gemm_add(
+                    codes.data_ptr(), scales.data_ptr(), self.codes.data_ptr(), self.scales.data_ptr(),
+                    self.code_format, _native.ptr(self.bias), add.data_ptr(), self.N, M, self.N, K, y.data_ptr(),
+                    self.N, _native.stream()))
         return y
 
 
@@ -225,9 +259,8 @@ _prepared = {}
 
 
 def _prepare(qweight, wscales, proj_down, proj_up, smooth, bias):
-    key = (qweight.data_ptr(), qweight._version, wscales.data_ptr(), wscales._version,
-           None if bias is None else (bias.data_ptr(), bias._version),
-           None if smooth is None else (smooth.data_ptr(), smooth._version))
+    ver = lambda t: None if t is None else (t.data_ptr(), t._version)  # noqa: E731
+    key = (ver(qweight), ver(wscales), ver(bias), ver(smooth), ver(proj_down), ver(proj_up))
     layer = _prepared.get(key)
     if layer is None:
         if len(_prepared) > 256:
@@ -246,6 +279,56 @@ def linear(x, t):
     return w4a4_linear(x, *(t[part] for part in PARTS))
 
 
+def _same_format(l1, l2):
+    if l1.code_format == l2.code_format:
+        return l1, l2
+    # the hidden codes are written in the first layer's format and read in the second's: one format for both
+    parts = lambda l: l._parts  # noqa: E731
+    return (PreparedW4A4(*parts(l1), code_format="e4m3"), PreparedW4A4(*parts(l2), code_format="e4m3"))
+
+
+def w4a4_gelu_mlp(x, *parts):
+    """live::w4a4_gelu_mlp (reference native/ops/w4a4_ops.cpp:44-63, w4a4.py:198-204): y [M, N2] bfloat16 =
+    GELU(x W1^T + b1) W2^T + b2 for x [M, K] bfloat16 and the six parts of each layer (the second made with
+    shift=GELU_SHIFT). The first GEMM's epilogue applies GELU, adds the shift and quantizes the hidden layer to
+    unsigned INT4 straight into the second GEMM's operand; with low-rank branches it also keeps GELU's output for
+    the second layer's branch (which reads it without the shift)."""
+    if len(parts) != 12:
+        raise ValueError("w4a4_gelu_mlp takes the six parts of each of the two layers")
+    l1, l2 = _same_format(_prepare(*parts[:6]), _prepare(*parts[6:]))
+    if x.dtype != torch.bfloat16:
+        raise TypeError("x must be bfloat16")
+    if x.ndim != 2 or x.shape[1] != l1.K or l2.K != l1.N:
+        raise ValueError("x must be [M, K] of the first layer, whose N is the second layer's K")
+    x = x.contiguous()
+    M, lib, st = x.shape[0], _native.lib(), _native.stream()
+    work = torch.empty(lib.wdl_w4a4_linear_workspace(M, l1.K), dtype=torch.uint8, device=x.device)
+    hidden = torch.empty(M * l1.N * 2, dtype=torch.uint8, device=x.device)  # the hidden codes, 1 or 2 bytes each
+    hscales = torch.empty(scale_shape(l1.N // GROUP, M, "e4m3ts" if l2.code_format == _native.CODES_E4M3_TS else
+                                      "e4m3"), dtype=torch.float32, device=x.device)
+    gelu = torch.empty(M, l1.N, dtype=torch.float32, device=x.device) if l2.rank else None
+    y = torch.empty(M, l2.N, dtype=torch.bfloat16, device=x.device)
+    with torch.cuda.device(x.device):
+        add1 = l1.lowrank(x)
+        codes, scales = l1.quantize_input(x, work)
+        _native.check(lib.wdl_w4a4_gemm_gelu_u4_add(
+            codes.data_ptr(), scales.data_ptr(), l1.codes.data_ptr(), l1.scales.data_ptr(), l1.code_format,
+            _native.ptr(l1.bias), _native.ptr(add1), l1.N, _native.ptr(l2.smooth), GELU_SHIFT,
+            _scale_code(l2.scale_dtype), M, l1.N, l1.K, hidden.data_ptr(), l1.N, hscales.data_ptr(),
+            _native.ptr(gelu), l1.N, st))
+        add2 = l2.lowrank(gelu) if l2.rank else None
+        _native.check(lib.wdl_w4a4_gemm_add(
+            hidden.data_ptr(), hscales.data_ptr(), l2.codes.data_ptr(), l2.scales.data_ptr(), l2.code_format,
+            _native.ptr(l2.bias), _native.ptr(add2), l2.N, M, l2.N, l2.K, y.data_ptr(), l2.N, st))
+    return y
+
+
+def gelu_mlp(x, t1, t2):
+    """y = GELU(x W1^T + b1) W2^T + b2 (GELU in tanh form, Wan's feed forward) for x [M, K] bfloat16 and t1, t2
+    the tensors of quantize, t2 made with shift=GELU_SHIFT (reference w4a4.py:198-204)."""
+    return w4a4_gelu_mlp(x, *(t1[part] for part in PARTS), *(t2[part] for part in PARTS))
+
+
 class PackedW4A4Linear(torch.nn.Module):
     """A linear layer in W4A4 over the parts of quantize (reference w4a4.py:220-231); unpacked once, here."""
 
@@ -256,4 +339,17 @@ class PackedW4A4Linear(torch.nn.Module):
 
     def forward(self, X):
         y = self.layer(X.reshape(-1, X.shape[-1]).to(torch.bfloat16).contiguous())
+        return y.reshape(*X.shape[:-1], self.out_features)
+
+
+class PackedW4A4GeluMLP(torch.nn.Module):
+    """Wan's feed forward (Linear, GELU in tanh form, Linear) in W4A4 as one gelu_mlp (reference w4a4.py:234-245)."""
+
+    def __init__(self, fc1, fc2):
+        super().__init__()
+        self.parts = [fc1[name] for name in PARTS] + [fc2[name] for name in PARTS]
+        self.out_features = fc2["proj_up"].shape[0] if fc2["proj_up"].numel() else fc2["wscales"].shape[-1]
+
+    def forward(self, X):
+        y = w4a4_gelu_mlp(X.reshape(-1, X.shape[-1]).to(torch.bfloat16).contiguous(), *self.parts)
         return y.reshape(*X.shape[:-1], self.out_features)
