@@ -224,18 +224,24 @@ def cpu_linear_sample(x, W, rows=256):
     return dt, 2 * rows * W.shape[0] * W.shape[1], f"{rows} of 1392 tokens, full N and K (oracle port, numpy)"
 
 
-def rollout_workload(device, rank=0, chunks=7, layers=30):
+def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None):
+    """tp = (world, reduce): one stream split across the ranks (tensor parallelism), else one stream per rank."""
     from wan_dit_lab_b200.generation import causal
     from wan_dit_lab_b200.models.block import WanBlockB200
+    from wan_dit_lab_b200.models.block_tp import WanBlockTP
     from wan_dit_lab_b200.quantization import w4a4
     w4a4.CODE_FORMAT = CODES  # every block's layers in the --codes operand format
     torch.manual_seed(0)
-    model = causal.random_model(seed=6, device=device, num_layers=layers)
-    g = torch.Generator().manual_seed(8 + 1000 * rank)  # one independent seeded stream per rank
+    world = 1 if tp is None else tp[0]
+    model = causal.random_model(seed=6, device=device, num_layers=layers,
+                                shard=None if tp is None else (rank, world), reduce=None if tp is None else tp[1])
+    block_cls = WanBlockB200 if tp is None else WanBlockTP
+    seed_rank = rank if tp is None else 0  # the ranks of a split stream share its noise
+    g = torch.Generator().manual_seed(8 + 1000 * seed_rank)  # one independent seeded stream per rank
     noise = torch.randn(48, 21, 32, 58, generator=g)
     text = torch.randn(1, 512, 4096, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
-    stream = causal.Stream(model, text.to(device), 512, 928, torch.Generator(device=device).manual_seed(10 + rank),
-                           vae_stride=16)
+    stream = causal.Stream(model, text.to(device), 512, 928,
+                           torch.Generator(device=device).manual_seed(10 + seed_rank), vae_stride=16)
     noise_d = noise.to(device)
     out = torch.empty_like(noise_d)
 
@@ -257,24 +263,26 @@ def rollout_workload(device, rank=0, chunks=7, layers=30):
     def gemm_only():
         """One instrumented chunk: the W4A4 GEMM launches bracketed by CUDA events (returns seconds, ops)."""
         gemm_log.clear()
-        WanBlockB200.gemm_timer = lambda e0, e1, ops: gemm_log.append((e0, e1, ops))
+        block_cls.gemm_timer = lambda e0, e1, ops: gemm_log.append((e0, e1, ops))
         try:
             stream.reset()
             stream.next_chunk(noise_d[:, :3])
         finally:
-            WanBlockB200.gemm_timer = None
+            block_cls.gemm_timer = None
         torch.cuda.synchronize()
         return sum(a.elapsed_time(b) for a, b, _ in gemm_log) / 1e3, sum(o for _, _, o in gemm_log), len(gemm_log)
 
-    per_block = 2 * 1392 * 3072 * (9216 + 3072 + 3072 + 3072 + 2 * 14336)
+    per_block = 2 * 1392 * 3072 * (9216 + 3072 + 3072 + 3072 + 2 * 14336) // world  # this rank's share
+    # kernels per block: 20 (5 for Sage attention over the cache), 25 with the split (rows_sumsq x 2, the sharded
+    # norms in place of the fused ones, residual_update x 3); + 1 modulation launch per pass
     return dict(step=step, e2e=e2e_step, gemm_probe=gemm_only, frames=3 * chunks,
-                launches_per_step=chunks * 5 * (1 + layers * 20),
+                launches_per_step=chunks * 5 * (1 + layers * (20 if tp is None else 25)),
                 h2d=noise.numel() * 4, d2h=noise.numel() * 4,
                 config={"workload": "BASELINE config 4: 30-layer 5B DiT rollout, 512x928, 7 chunks x (4 DMD steps + "
                                     "write pass), FP8 KV window 21 frames",
                         "model": "Wan2.2-TI2V-5B shape, random init N(0,0.02), W4A4 (INT4 g64, bf16 scales, rank 0)",
                         "tokens_per_chunk": 1392, "keys_per_chunk": [1392 * (c + 1) for c in range(chunks)],
-                        "chunks": chunks, "layers": layers,
+                        "chunks": chunks, "layers": layers, **({} if tp is None else {"tensor_parallel": world}),
                         "codes": CODES, "l2": "inputs larger than L2 (5 GB of weights per pass)"},
                 algorithmic={"gemm_int_ops_per_block_pass": per_block, "gemm_launches_per_block_pass": 6},
                 cpu=lambda: cpu_block_sample(), dtype="W4A4 (int4 x int4 exact on int8 tensor cores) + INT8/FP8 Sage "
@@ -389,6 +397,9 @@ def main():
                              "kind::f16) or int8 (kind::i8)")
     parser.add_argument("--chunks", type=int, default=7, help="rollout chunks (profiling; BASELINE config 4: 7)")
     parser.add_argument("--layers", type=int, default=30, help="model layers (profiling; BASELINE config 4: 30)")
+    parser.add_argument("--tp", action="store_true",
+                        help="BASELINE config 5b: one stream split across the ranks (heads / hidden channels, NCCL "
+                             "all-reduce after O, cross-O and FFN-2) instead of one independent stream per rank")
     args = parser.parse_args()
     global CODES
     CODES = args.codes
@@ -412,7 +423,11 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
 
-    wl = WORKLOADS[args.workload](device, rank, args.chunks, args.layers) if rollout else WORKLOADS[args.workload](device)
+    if args.tp and not rollout:
+        parser.error("--tp splits the rollout")
+    tp = (world, (lambda t: dist.all_reduce(t)) if dist is not None else (lambda t: None)) if args.tp else None
+    wl = (WORKLOADS[args.workload](device, rank, args.chunks, args.layers, tp) if rollout
+          else WORKLOADS[args.workload](device))
     stream = torch.cuda.current_stream(device)
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     flush = lambda: flush_l2(flush_buf)  # noqa: E731
@@ -451,8 +466,9 @@ def main():
         achieved, kernel_ms, gemm_launches = wl["ops"] / kernel_s / 1e12, kernel_s * 1e3, 1
 
     step_max, e2e_max = combine_ranks(dist, [step_s, e2e_s], device)
+    streams = 1 if args.tp else world  # a split stream is one unit of work on all ranks (strong scaling)
     if rollout:
-        value, e2e_value = job_rate(world, wl["frames"], step_max), job_rate(world, wl["frames"], e2e_max)
+        value, e2e_value = job_rate(streams, wl["frames"], step_max), job_rate(streams, wl["frames"], e2e_max)
         unit, metric = "latent frames/s", METRIC
     else:
         value, e2e_value = job_rate(world, wl["ops"], step_max) / 1e12, job_rate(world, wl["ops"], e2e_max) / 1e12
@@ -475,9 +491,11 @@ def main():
             "f16fold": "f16 tensor cores (kind::f16): int4 codes x int4 weights folded with their bf16 group scales, exact"}[CODES])
         line = {
             "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step_max * 1e3, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": step_max * 1e3, "higher_is_better": True,
+            "scaling": "strong" if args.tp else "weak",
             "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded, BASELINE shapes)",
-            "config": {**wl["config"], "parallelism": f"streams{world}" if world > 1 else "single"},
+            "config": {**wl["config"], "parallelism": (f"tp{world}" if args.tp else f"streams{world}") if world > 1
+                       else "single"},
             "e2e": {"value": e2e_value, "unit": unit, "ms_per_step": e2e_max * 1e3,
                     "h2d_bytes_per_step": wl["h2d"], "d2h_bytes_per_step": wl["d2h"]},
             "gpu_launches": wl["launches_per_step"] * args.steps,
@@ -486,9 +504,10 @@ def main():
                          "frac_of_measured_bf16_peak": achieved / F16_PEAK_TFLOPS if F16_PEAK_TFLOPS else None,
                          "frac_of_nominal_int8": achieved / INT8_NOMINAL_TOPS, "kernel_ms": kernel_ms,
                          "launches_measured": gemm_launches, "algorithmic": wl["algorithmic"],
-                         "traffic": GEMM_TRAFFIC.get(CODES) if rollout else None,
+                         "traffic": GEMM_TRAFFIC.get(CODES) if rollout and not args.tp else None,
                          "traffic_unit": "DRAM bytes read + written per GEMM launch (mean of a block pass's six)",
-                         "traffic_source": GEMM_TRAFFIC_SOURCE if rollout and CODES in GEMM_TRAFFIC else None},
+                         "traffic_source": GEMM_TRAFFIC_SOURCE if rollout and not args.tp and CODES in GEMM_TRAFFIC
+                         else None},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
         }

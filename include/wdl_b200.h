@@ -142,6 +142,16 @@ int wdl_w4a4_gemm_gelu_u4_add(const void* a, const float* a_scales, const void* 
                               uint8_t* codes, int64_t ldc, float* scales, float* gelu_out, int64_t ld_gelu,
                               void* stream);
 
+/* out [M, ldo] f32 = the GEMM's product (+ addend, + bias when given), not rounded: a tensor-parallel shard's
+ * share of a row-parallel layer (its slice of the K input channels), summed across shards (NCCL all-reduce) before
+ * wdl_residual_update applies bias, bf16 rounding, gate and residual. Groups of 64 never straddle shards, so each
+ * shard's INT4 activation groups are those of the whole layer. No reference counterpart (the reference runs one
+ * GPU per stream); the row-parallel split of O, cross-O and FFN-2 that this serves is described with the
+ * reference's linears (quantization/w4a4.py:220-262). */
+int wdl_w4a4_gemm_f32(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                      const float* bias, const float* addend, int64_t ld_add, int M, int N, int K, float* out,
+                      int64_t ldo, void* stream);
+
 /* Bytes of scratch wdl_w4a4_linear needs for M tokens of K channels (any code format). */
 size_t wdl_w4a4_linear_workspace(int M, int K);
 
@@ -200,6 +210,17 @@ int wdl_qkv_prep(const uint16_t* qkv, int64_t ld, int n, int dim, const float* n
                  uint8_t* cache_k, float* cache_ks, uint8_t* cache_v, float* cache_vs, int capacity, int at,
                  void* stream);
 
+/* wdl_qkv_prep on a tensor-parallel shard's heads: dim = this shard's heads x 128 (any multiple of 128 up to
+ * 4096), norm_q / norm_k its slices of the weights, and sumsq [n, 2] f32 the sums of squares of each token's q and
+ * k over all norm_dim channels of all shards (wdl_rows_sumsq per shard, summed across shards), so that the RMSNorm
+ * divides by the whole row's statistics. sumsq null: the shard is the whole row (norm_dim must equal dim). The
+ * cache rows hold this shard's heads ([capacity, dim / 128, 128]). MultiHeadAttention's q / k norms span all heads
+ * (models/multi_head_attention.py:28-44). */
+int wdl_qkv_prep_sharded(const uint16_t* qkv, int64_t ld, int n, int dim, const float* norm_q, const float* norm_k,
+                         float eps, const float* sumsq, int norm_dim, const float* freq, int positions, int grid_h,
+                         int grid_w, int start, float* q_out, float* k_out, uint8_t* cache_k, float* cache_ks,
+                         uint8_t* cache_v, float* cache_vs, int capacity, int at, void* stream);
+
 /* ---- normalizations of the block, fused with what consumes them ------------------------------------------- */
 
 /* LayerNorm of x [M, K] (x_dtype WDL_F32 or WDL_BF16, row stride ldx; K % 256 == 0, K <= 4096) over K channels
@@ -217,6 +238,22 @@ int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float ep
  * K <= 4096; x, w and out 16-byte aligned). models/rms_norm.py:10-13 (the query norm of cross-attention, models/multi_head_attention.py:118). */
 int wdl_rms_rows(const uint16_t* x, int64_t ldx, int M, int K, const float* w, float eps, float* out, int64_t ldo,
                  void* stream);
+
+/* wdl_rms_rows over a shard's slice of K channels (K % 128 == 0) of rows normalized over norm_dim channels:
+ * sumsq [M] f32 holds each row's sum of squares over all of them (nullable: the slice is the row, norm_dim = K). */
+int wdl_rms_rows_sharded(const uint16_t* x, int64_t ldx, int M, int K, const float* w, float eps, const float* sumsq,
+                         int norm_dim, float* out, int64_t ldo, void* stream);
+
+/* out [M, parts] f32: the sum of squares of each bf16 row's `parts` slices of K channels (slice p starts at
+ * channel p * part_stride; K % 8 == 0, 16-byte aligned rows). A shard's share of an RMSNorm's statistics. */
+int wdl_rows_sumsq(const uint16_t* x, int64_t ldx, int M, int K, int parts, int64_t part_stride, float* out,
+                   void* stream);
+
+/* x [M, ldx] f32 += gate * float(bf16(partial + bias)) (gate, bias [N] f32 nullable: gate 1, bias 0), for
+ * partial [M, ldp] f32 the all-reduced product of a row-parallel layer: the residual epilogue of
+ * wdl_w4a4_gemm_residual after the sum across shards (models/block.py:76-79 X + y * gate). N % 4 == 0. */
+int wdl_residual_update(const float* partial, int64_t ldp, const float* bias, const float* gate, float* x, int64_t ldx,
+                        int M, int N, void* stream);
 
 /* out [blocks, 6, dim] f32 = time_in [6, dim] + modulation [blocks, 6, dim]: the (time_in + self.modulation)
  * of every block of a model at once (models/block.py:75). */

@@ -37,7 +37,7 @@ def _rank(rank, world, port, out):
 
 def test_two_gloo_ranks_take_the_max_and_sum_the_work():
     world, port = 2, free_port()
-    out = mp.Manager().dict()
+    out = mp.get_context("spawn").Manager().dict()
     mp.spawn(_rank, args=(world, port, out), nprocs=world, join=True)
     for rank in range(world):
         step, e2e, rate = out[rank]

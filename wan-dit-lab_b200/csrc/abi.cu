@@ -255,6 +255,17 @@ int wdl_w4a4_gemm_residual_add(const void* a, const float* a_scales, const void*
   return gemm_common(g, stream);
 }
 
+int wdl_w4a4_gemm_f32(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                      const float* bias, const float* addend, int64_t ld_add, int M, int N, int K, float* out,
+                      int64_t ldo, void* stream) {
+  if (ldo < N || (ldo * 4) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldo must be >= N with 16-byte aligned rows");
+  wdl::w4a4::GemmArgs g{};
+  operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
+  if (set_addend(g, addend, ld_add, N) != WDL_OK) return WDL_ERR_ARGUMENT;
+  g.ep.mode = wdl::w4a4::kEpiResidualF32, g.ep.bias = bias, g.ep.residual = nullptr, g.ep.out = out, g.ep.ld_out = ldo;
+  return gemm_common(g, stream);
+}
+
 int wdl_w4a4_gemm_group_partials(const void* a, const float* a_scales, const void* w, const float* w_scales,
                                  int code_format, int M, int N, int K, int group, int32_t* out, int64_t ldo,
                                  void* stream) {
@@ -381,6 +392,17 @@ int wdl_qkv_prep(const uint16_t* qkv, int64_t ld, int n, int dim, const float* n
                  void* stream) {
   if (dim != 1024 && dim != 2048 && dim != 3072 && dim != 4096)
     return fail(WDL_ERR_ARGUMENT, "dim must be 1024, 2048, 3072 or 4096 (heads of 128)");
+  return wdl_qkv_prep_sharded(qkv, ld, n, dim, norm_q, norm_k, eps, nullptr, dim, freq, positions, grid_h, grid_w,
+                              start, q_out, k_out, cache_k, cache_ks, cache_v, cache_vs, capacity, at, stream);
+}
+
+int wdl_qkv_prep_sharded(const uint16_t* qkv, int64_t ld, int n, int dim, const float* norm_q, const float* norm_k,
+                         float eps, const float* sumsq, int norm_dim, const float* freq, int positions, int grid_h,
+                         int grid_w, int start, float* q_out, float* k_out, uint8_t* cache_k, float* cache_ks,
+                         uint8_t* cache_v, float* cache_vs, int capacity, int at, void* stream) {
+  if (dim <= 0 || dim % 128 != 0 || dim > 4096) return fail(WDL_ERR_ARGUMENT, "dim must be a multiple of 128 (heads), at most 4096");
+  if (sumsq ? norm_dim < dim : norm_dim != dim)
+    return fail(WDL_ERR_ARGUMENT, "norm_dim must be dim, or (with sumsq) the channels of all shards");
   if (n < 0 || ld < 3 * dim || (ld * 2) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "qkv rows must hold 3 dim channels, 16-byte aligned");
   if (grid_h <= 0 || grid_w <= 0 || n % (grid_h * grid_w) != 0)
     return fail(WDL_ERR_ARGUMENT, "n must be a whole number of frames of grid_h x grid_w tokens");
@@ -390,11 +412,13 @@ int wdl_qkv_prep(const uint16_t* qkv, int64_t ld, int n, int dim, const float* n
   if (n == 0) return ok();
   if (!qkv || !norm_q || !norm_k || !freq || !q_out || !k_out) return fail(WDL_ERR_ARGUMENT, "null pointer");
   if (cache_k && (!cache_ks || !cache_v || !cache_vs)) return fail(WDL_ERR_ARGUMENT, "null cache pointer");
-  if (!aligned(qkv, 16) || !aligned(q_out, 16) || !aligned(k_out, 16) || (cache_k && (!aligned(cache_k, 8) || !aligned(cache_v, 8))))
+  if (!aligned(qkv, 16) || !aligned(q_out, 16) || !aligned(k_out, 16) || !aligned(sumsq, 8) ||
+      (cache_k && (!aligned(cache_k, 8) || !aligned(cache_v, 8))))
     return fail(WDL_ERR_ARGUMENT, "misaligned pointer");
   wdl::ropekv::QkvPrepArgs a{};
   a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv), a.ld_qkv = ld, a.n = n, a.dim = dim, a.norm_q = norm_q;
-  a.norm_k = norm_k, a.eps = eps, a.freq = freq, a.freq_table_stride = static_cast<int64_t>(positions) * 64;
+  a.norm_k = norm_k, a.eps = eps, a.sumsq = sumsq, a.norm_dim = norm_dim, a.freq = freq;
+  a.freq_table_stride = static_cast<int64_t>(positions) * 64;
   a.freq_positions_stride = 64, a.grid_h = grid_h, a.grid_w = grid_w, a.start = start, a.q_out = q_out;
   a.k_out = k_out, a.cache_k = cache_k, a.cache_ks = cache_ks, a.cache_v = cache_v, a.cache_vs = cache_vs, a.at = at;
   wdl::ropekv::qkv_prep_launch(a, static_cast<cudaStream_t>(stream));
@@ -430,14 +454,48 @@ int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float ep
 int wdl_rms_rows(const uint16_t* x, int64_t ldx, int M, int K, const float* w, float eps, float* out, int64_t ldo,
                  void* stream) {
   if (K <= 0 || K % 256 != 0 || K > 4096) return fail(WDL_ERR_ARGUMENT, "K must be a multiple of 256, at most 4096");
+  return wdl_rms_rows_sharded(x, ldx, M, K, w, eps, nullptr, K, out, ldo, stream);
+}
+
+int wdl_rms_rows_sharded(const uint16_t* x, int64_t ldx, int M, int K, const float* w, float eps, const float* sumsq,
+                         int norm_dim, float* out, int64_t ldo, void* stream) {
+  if (K <= 0 || K % 128 != 0 || K > 4096) return fail(WDL_ERR_ARGUMENT, "K must be a multiple of 128, at most 4096");
+  if (sumsq ? norm_dim < K : norm_dim != K)
+    return fail(WDL_ERR_ARGUMENT, "norm_dim must be K, or (with sumsq) the channels of all shards");
   if (M < 0 || ldx < K || ldo < K || (ldx * 2) % 16 != 0 || (ldo * 4) % 16 != 0)
     return fail(WDL_ERR_ARGUMENT, "row strides must hold K channels, 16-byte aligned");
   if (M == 0) return ok();
-  if (!x || !w || !out || !aligned(x, 16) || !aligned(out, 16) || !aligned(w, 16))
+  if (!x || !w || !out || !aligned(x, 16) || !aligned(out, 16) || !aligned(w, 16) || !aligned(sumsq, 4))
     return fail(WDL_ERR_ARGUMENT, "null or misaligned pointer");
-  wdl::norm::rms_rows_launch(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, K, w, eps, out, ldo,
+  wdl::norm::rms_rows_launch(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, K, w, eps, sumsq, norm_dim, out, ldo,
                              static_cast<cudaStream_t>(stream));
   return cuda_status(cudaGetLastError(), "rms_rows launch");
+}
+
+int wdl_rows_sumsq(const uint16_t* x, int64_t ldx, int M, int K, int parts, int64_t part_stride, float* out,
+                   void* stream) {
+  if (K <= 0 || K % 8 != 0 || K > 4096) return fail(WDL_ERR_ARGUMENT, "K must be a multiple of 8, at most 4096");
+  if (parts < 1 || part_stride < 0 || (parts > 1 && part_stride < K) || (part_stride * 2) % 16 != 0)
+    return fail(WDL_ERR_ARGUMENT, "parts >= 1 slices of K channels, 16-byte aligned, not overlapping");
+  if (M < 0 || ldx < (parts - 1) * part_stride + K || (ldx * 2) % 16 != 0)
+    return fail(WDL_ERR_ARGUMENT, "rows must hold every slice, 16-byte aligned");
+  if (M == 0) return ok();
+  if (!x || !out || !aligned(x, 16) || !aligned(out, 4)) return fail(WDL_ERR_ARGUMENT, "null or misaligned pointer");
+  wdl::norm::rows_sumsq_launch(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, K, parts, part_stride, out,
+                               static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "rows_sumsq launch");
+}
+
+int wdl_residual_update(const float* partial, int64_t ldp, const float* bias, const float* gate, float* x, int64_t ldx,
+                        int M, int N, void* stream) {
+  if (M < 0 || N <= 0 || N % 4 != 0) return fail(WDL_ERR_ARGUMENT, "M >= 0 and N a positive multiple of 4 required");
+  if (ldp < N || ldx < N || (ldp * 4) % 16 != 0 || (ldx * 4) % 16 != 0)
+    return fail(WDL_ERR_ARGUMENT, "ldp, ldx must be >= N with 16-byte aligned rows");
+  if (M == 0) return ok();
+  if (!partial || !x || !aligned(partial, 16) || !aligned(x, 16) || !aligned(bias, 4) || !aligned(gate, 4))
+    return fail(WDL_ERR_ARGUMENT, "null or misaligned pointer");
+  wdl::norm::residual_update_launch(partial, ldp, bias, gate, x, ldx, M, N, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError(), "residual_update launch");
 }
 
 int wdl_modulation(const float* time_in, const float* modulation, int blocks, int dim, float* out, void* stream) {

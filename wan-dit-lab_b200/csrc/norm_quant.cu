@@ -10,6 +10,8 @@
 //  * rms_rows — RMSNorm of rows (models/rms_norm.py:10-13): x * rsqrt(mean(x^2) + eps) rounded to bf16, times
 //    the float32 weight; the query norm of cross-attention (models/multi_head_attention.py:118).
 //  * modulation — (time_in + modulation) of every block at once (models/block.py:75): [blocks, 6, dim] fp32.
+#include <algorithm>
+
 #include "common.cuh"
 #include "norm_quant.h"
 
@@ -168,8 +170,11 @@ void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s) {
 }
 
 // Same thread layout as ln_quant: one CTA of 128 threads per row.
+// sumsq (nullable): the sum of squares of each row over all norm_dim channels, when this call holds only a slice
+// of them (a tensor-parallel shard: the slices' sums added across shards); else the row's own sum over K = norm_dim.
 __global__ void __launch_bounds__(kRowThreads, 8) rms_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                                int K, const float* __restrict__ w, float eps,
+                                                               const float* __restrict__ sumsq, int norm_dim,
                                                                float* __restrict__ out, int64_t ldo) {
   __shared__ float red[kRowThreads / 32];
   const int t = threadIdx.x, m = blockIdx.x;
@@ -185,7 +190,8 @@ __global__ void __launch_bounds__(kRowThreads, 8) rms_rows_kernel(const __nv_bfl
       for (int i = 0; i < 8; ++i) ss = fmaf(v[c][i], v[c][i], ss);
     }
   }
-  const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(block_sum128(ss, red), static_cast<float>(K)), eps));
+  const float total = block_sum128(ss, red);
+  const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(sumsq ? __ldg(sumsq + m) : total, static_cast<float>(norm_dim)), eps));
   float* o = out + static_cast<int64_t>(m) * ldo;
 #pragma unroll
   for (int c = 0; c < kRowChunks; ++c) {
@@ -201,10 +207,74 @@ __global__ void __launch_bounds__(kRowThreads, 8) rms_rows_kernel(const __nv_bfl
   }
 }
 
-void rms_rows_launch(const __nv_bfloat16* x, int64_t ldx, int M, int K, const float* w, float eps, float* out,
-                     int64_t ldo, cudaStream_t s) {
+void rms_rows_launch(const __nv_bfloat16* x, int64_t ldx, int M, int K, const float* w, float eps, const float* sumsq,
+                     int norm_dim, float* out, int64_t ldo, cudaStream_t s) {
   if (M == 0) return;
-  rms_rows_kernel<<<M, kRowThreads, 0, s>>>(x, ldx, K, w, eps, out, ldo);
+  rms_rows_kernel<<<M, kRowThreads, 0, s>>>(x, ldx, K, w, eps, sumsq, norm_dim, out, ldo);
+}
+
+// Sums of squares of `parts` slices of K channels of each bf16 row (slice p starts at channel p * part_stride):
+// out[m * parts + p]. Same thread layout and summation order as rms_rows. A tensor-parallel shard's share of an
+// RMSNorm over channels split across shards (the q / k norms of self-attention, the query norm of cross-attention).
+__global__ void __launch_bounds__(kRowThreads, 8) rows_sumsq_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                 int K, int parts, int64_t part_stride,
+                                                                 float* __restrict__ out) {
+  __shared__ float red[kRowThreads / 32];
+  const int t = threadIdx.x, m = blockIdx.x;
+  for (int p = 0; p < parts; ++p) {
+    const __nv_bfloat16* row = x + static_cast<int64_t>(m) * ldx + p * part_stride;
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < kRowChunks; ++c) {
+      const int k = c * 1024 + t * 8;
+      if (k < K) {
+        float v[8];
+        load8<__nv_bfloat16>(row + k, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+      }
+    }
+    const float total = block_sum128(ss, red);
+    if (t == 0) out[static_cast<int64_t>(m) * parts + p] = total;
+  }
+}
+
+void rows_sumsq_launch(const __nv_bfloat16* x, int64_t ldx, int M, int K, int parts, int64_t part_stride, float* out,
+                       cudaStream_t s) {
+  if (M == 0) return;
+  rows_sumsq_kernel<<<M, kRowThreads, 0, s>>>(x, ldx, K, parts, part_stride, out);
+}
+
+// The residual update after a row-parallel layer's shards have been summed (tensor-parallel blocks): x += gate *
+// float(bf16(partial + bias)) (gate 1 when null), the arithmetic of the GEMM's residual epilogue. Four columns per
+// thread (N % 4 == 0, 16-byte aligned rows).
+__global__ void residual_update_kernel(const float* __restrict__ partial, int64_t ldp, const float* __restrict__ bias,
+                                       const float* __restrict__ gate, float* __restrict__ x, int64_t ldx, int M,
+                                       int N) {
+  const int64_t quads = static_cast<int64_t>(M) * (N / 4);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < quads;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(i / (N / 4)), n = static_cast<int>(i % (N / 4)) * 4;
+    const float4 p = *reinterpret_cast<const float4*>(partial + static_cast<int64_t>(m) * ldp + n);
+    float4* xp = reinterpret_cast<float4*>(x + static_cast<int64_t>(m) * ldx + n);
+    const float4 xv = *xp;
+    const float pv[4] = {p.x, p.y, p.z, p.w};
+    float v[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float o = bf16r(pv[j] + (bias ? __ldg(bias + n + j) : 0.f));
+      v[j] = gate ? __fadd_rn(v[j], __fmul_rn(o, __ldg(gate + n + j))) : __fadd_rn(v[j], o);
+    }
+    *xp = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+void residual_update_launch(const float* partial, int64_t ldp, const float* bias, const float* gate, float* x,
+                            int64_t ldx, int M, int N, cudaStream_t s) {
+  const int64_t quads = static_cast<int64_t>(M) * (N / 4);
+  if (quads == 0) return;
+  const int blocks = static_cast<int>(std::min<int64_t>((quads + 255) / 256, 148 * 8));
+  residual_update_kernel<<<blocks, 256, 0, s>>>(partial, ldp, bias, gate, x, ldx, M, N);
 }
 
 __global__ void modulation_kernel(const float* __restrict__ time_in, const float* __restrict__ modulation, int64_t n,

@@ -27,8 +27,12 @@ struct LnQuantArgs {
 };
 void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s);
 
-void rms_rows_launch(const __nv_bfloat16* x, int64_t ldx, int M, int K, const float* w, float eps, float* out,
-                     int64_t ldo, cudaStream_t s);
+void rms_rows_launch(const __nv_bfloat16* x, int64_t ldx, int M, int K, const float* w, float eps, const float* sumsq,
+                     int norm_dim, float* out, int64_t ldo, cudaStream_t s);
+void rows_sumsq_launch(const __nv_bfloat16* x, int64_t ldx, int M, int K, int parts, int64_t part_stride, float* out,
+                       cudaStream_t s);
+void residual_update_launch(const float* partial, int64_t ldp, const float* bias, const float* gate, float* x,
+                            int64_t ldx, int M, int N, cudaStream_t s);
 
 void modulation_launch(const float* time_in, const float* modulation, int blocks, int dim, float* out, cudaStream_t s);
 

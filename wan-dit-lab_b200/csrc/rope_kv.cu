@@ -231,36 +231,46 @@ __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
   __shared__ float red[kPrepThreads / 32];
   const int t = blockIdx.x;  // token of the chunk
   const int tid = threadIdx.x;
-  const int dim = kPasses * 1024;
+  const int dim = a.dim;  // this call's channels of q (a multiple of 128, at most kPasses * 1024)
   const __nv_bfloat16* row = a.qkv + static_cast<int64_t>(t) * a.ld_qkv;
   const int gh = a.grid_h, gw = a.grid_w;
   const int pos_t = a.start + t / (gh * gw), pos_h = t / gw % gh, pos_w = t % gw;
   const int time_pairs = 64 - 2 * 21;  // head_dim 128: 22 time pairs, 21 height, 21 width
 
-  // q (part 0) and k (part 1): RMSNorm over the whole row of dim channels, RoPE per head
+  // q (part 0) and k (part 1): RMSNorm over the whole row of norm_dim channels, RoPE per head. A thread whose
+  // channels lie past dim (a partial last pass) joins every shuffle and sum but loads and stores nothing; the
+  // 16 lanes of a head are all in or all out.
 #pragma unroll
   for (int part = 0; part < 2; ++part) {
     float v[kPasses][8];
     float ss = 0.f;
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
-      load8_bf16(row + part * dim + p * 1024 + tid * 8, v[p]);
+      const int c0 = p * 1024 + tid * 8;
+      if (c0 < dim) {
+        load8_bf16(row + part * dim + c0, v[p]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[p][i] = 0.f;
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss = fmaf(v[p][i], v[p][i], ss);
     }
-    const float total = block_sum(ss, red);
-    const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(dim)), a.eps));
+    const float own = block_sum(ss, red);
+    const float total = a.sumsq ? __ldg(a.sumsq + static_cast<int64_t>(t) * 2 + part) : own;
+    const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(a.norm_dim)), a.eps));
     const float* w = part == 0 ? a.norm_q : a.norm_k;
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
       const int c0 = p * 1024 + tid * 8;  // channel of v[p][0]
+      const bool act = c0 < dim;
       const int head = c0 >> 7, d0 = c0 & 127;
       float y[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         // (x * rsqrt(mean + eps)) rounded to x's bf16, then times the float32 weight
         const float n = __bfloat162float(__float2bfloat16_rn(__fmul_rn(v[p][i], r)));
-        y[i] = __fmul_rn(n, __ldg(w + c0 + i));
+        y[i] = act ? __fmul_rn(n, __ldg(w + c0 + i)) : 0.f;
       }
       // RoPE on the 4 pairs (float32 table; products and difference rounded separately)
 #pragma unroll
@@ -273,20 +283,24 @@ __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
         y[2 * j] = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s));
         y[2 * j + 1] = __fadd_rn(__fmul_rn(o, c), __fmul_rn(e, s));
       }
-      float* dst = (part == 0 ? a.q_out : a.k_out) + static_cast<int64_t>(t) * dim + c0;
-      *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);
-      *reinterpret_cast<float4*>(dst + 4) = make_float4(y[4], y[5], y[6], y[7]);
+      if (act) {
+        float* dst = (part == 0 ? a.q_out : a.k_out) + static_cast<int64_t>(t) * dim + c0;
+        *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(y[4], y[5], y[6], y[7]);
+      }
       if (part == 1 && a.cache_k) {  // FP8 store of the rotated key row of this head (16 lanes)
         float amax = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-        const float scale = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
-        const int64_t crow = static_cast<int64_t>(a.at + t) * (dim / 128) + head;
-        const uint2 q8 = e4m3x8(y, scale);
-        *reinterpret_cast<uint2*>(a.cache_k + crow * 128 + d0) = q8;
-        if ((tid & 15) == 0) a.cache_ks[crow] = scale;
+        if (act) {
+          const float scale = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
+          const int64_t crow = static_cast<int64_t>(a.at + t) * (dim / 128) + head;
+          const uint2 q8 = e4m3x8(y, scale);
+          *reinterpret_cast<uint2*>(a.cache_k + crow * 128 + d0) = q8;
+          if ((tid & 15) == 0) a.cache_ks[crow] = scale;
+        }
       }
     }
   }
@@ -295,28 +309,36 @@ __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
       const int c0 = p * 1024 + tid * 8;
+      const bool act = c0 < dim;
       const int head = c0 >> 7, d0 = c0 & 127;
       float y[8];
-      load8_bf16(row + 2 * dim + c0, y);
+      if (act) {
+        load8_bf16(row + 2 * dim + c0, y);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = 0.f;
+      }
       float amax = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-      const float scale = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
-      const int64_t crow = static_cast<int64_t>(a.at + t) * (dim / 128) + head;
-      const uint2 q8 = e4m3x8(y, scale);
-      *reinterpret_cast<uint2*>(a.cache_v + crow * 128 + d0) = q8;
-      if ((tid & 15) == 0) a.cache_vs[crow] = scale;
+      if (act) {
+        const float scale = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
+        const int64_t crow = static_cast<int64_t>(a.at + t) * (dim / 128) + head;
+        const uint2 q8 = e4m3x8(y, scale);
+        *reinterpret_cast<uint2*>(a.cache_v + crow * 128 + d0) = q8;
+        if ((tid & 15) == 0) a.cache_vs[crow] = scale;
+      }
     }
   }
 }
 
 void qkv_prep_launch(const QkvPrepArgs& a, cudaStream_t s) {
-  switch (a.dim) {
-    case 1024: qkv_prep_kernel<1><<<a.n, kPrepThreads, 0, s>>>(a); break;
-    case 2048: qkv_prep_kernel<2><<<a.n, kPrepThreads, 0, s>>>(a); break;
-    case 3072: qkv_prep_kernel<3><<<a.n, kPrepThreads, 0, s>>>(a); break;
+  switch ((a.dim + 1023) / 1024) {
+    case 1: qkv_prep_kernel<1><<<a.n, kPrepThreads, 0, s>>>(a); break;
+    case 2: qkv_prep_kernel<2><<<a.n, kPrepThreads, 0, s>>>(a); break;
+    case 3: qkv_prep_kernel<3><<<a.n, kPrepThreads, 0, s>>>(a); break;
     default: qkv_prep_kernel<4><<<a.n, kPrepThreads, 0, s>>>(a); break;
   }
 }

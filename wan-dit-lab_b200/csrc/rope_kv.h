@@ -40,10 +40,12 @@ void rope_launch(const RopeArgs& a, cudaStream_t s);
 struct QkvPrepArgs {
   const __nv_bfloat16* qkv;  // [n, ld_qkv]: q | k | v of dim channels each
   int64_t ld_qkv;
-  int n, dim;  // tokens, channels of q (heads * 128)
-  const float* norm_q;  // [dim] RMSNorm weights
+  int n, dim;  // tokens, channels of q in this call (heads * 128)
+  const float* norm_q;  // [dim] RMSNorm weights (this call's slice)
   const float* norm_k;
   float eps;
+  const float* sumsq;  // [n, 2] sums of squares of q and k over all norm_dim channels (nullable: this call's own)
+  int norm_dim;        // channels the RMSNorm averages over (dim unless the heads are split across shards)
   const float* freq;  // [2, P, 64] float32, contiguous
   int64_t freq_table_stride, freq_positions_stride;
   int grid_h, grid_w, start;  // token t: positions (start + t / (h w), t / w % h, t % w)

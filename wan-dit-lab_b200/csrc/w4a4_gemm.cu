@@ -331,15 +331,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else if constexpr (kMode == kEpiResidualF32) {
         // residual stream update in fp32: x_new = x + float(bf16(acc + bias)) * gate   (gate 1 when absent)
         float* out = reinterpret_cast<float*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
-        const float* res = ep.residual + static_cast<size_t>(m) * ep.ld_res + n0;
+        // without a residual: the fp32 partial product acc (+ bias) of a row-parallel shard, unrounded
+        const float* res = ep.residual ? ep.residual + static_cast<size_t>(m) * ep.ld_res + n0 : nullptr;
 #pragma unroll
         for (int j = 0; j < 128; j += 4) {
-          const float4 r = *reinterpret_cast<const float4*>(res + j);
+          const float4 r = res ? *reinterpret_cast<const float4*>(res + j) : make_float4(0.f, 0.f, 0.f, 0.f);
           float v[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float o = bf16_round(acc[j + i] + (ep.bias ? __ldg(ep.bias + n0 + j + i) : 0.f));
-            v[i] = ep.gate ? __fadd_rn(v[i], __fmul_rn(o, __ldg(ep.gate + n0 + j + i))) : __fadd_rn(v[i], o);
+            const float p = acc[j + i] + (ep.bias ? __ldg(ep.bias + n0 + j + i) : 0.f);
+            const float o = bf16_round(p);
+            v[i] = !res ? p : ep.gate ? __fadd_rn(v[i], __fmul_rn(o, __ldg(ep.gate + n0 + j + i))) : __fadd_rn(v[i], o);
           }
           *reinterpret_cast<float4*>(out + j) = make_float4(v[0], v[1], v[2], v[3]);
         }

@@ -135,6 +135,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const int m = m_tile * BM + row;
     const bool row_ok = m < M;
+    // N % 128 == 0: the last column tile may hold only its first half (the TMA zero-fills the missing weight rows)
+    const bool col_ok = n_tile * BN + h * 128 < N;
     const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + h * 128;
     const float unfold = __ldg(fold_scale);  // 2^F
     float acc[128];
@@ -179,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
-    if (ok && row_ok) add_addend<128>(ep, m, n_tile * BN + h * 128, acc);
+    if (ok && row_ok && col_ok) add_addend<128>(ep, m, n_tile * BN + h * 128, acc);
 
     if constexpr (kMode == kEpiResidualF32) {
       // Residual update through a per-warp 32 x 32 transpose in shared memory (the pipeline buffers, idle once every
@@ -195,8 +197,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = acc[blk * 32 + j];
         __syncwarp();
         const int n = n_tile * BN + h * 128 + blk * 32 + lane;
-        const float bn = ep.bias ? __ldg(ep.bias + n) : 0.f;
-        if (ok) {
+        const float bn = ep.bias && col_ok ? __ldg(ep.bias + n) : 0.f;
+        if (ok && col_ok && !ep.residual) {
+          // a partial product in fp32 (a shard's share of a row-parallel layer, summed across shards before the
+          // bias, rounding and residual update): out = acc (+ bias), no rounding
+          float* out = reinterpret_cast<float*>(ep.out) + n;
+#pragma unroll
+          for (int r = 0; r < 32; ++r)
+            if (m0 + r < M) out[static_cast<size_t>(m0 + r) * ep.ld_out] = tw[r * 33 + lane] + bn;
+        } else if (ok && col_ok) {
           {
             // residual stream update in fp32: x_new = x + float(bf16(acc + bias)) * gate   (gate 1 when absent)
             const float gn = ep.gate ? __ldg(ep.gate + n) : 0.f;
@@ -216,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
       }
     }
-    if (ok && row_ok) {
+    if (ok && row_ok && col_ok) {
       const int n0 = n_tile * BN + h * 128;
       if constexpr (kMode == kEpiBf16) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
@@ -335,8 +344,8 @@ int gemm_fold_validate(const GemmArgs& a, const char** why) {
     *why = "M, N and K must be positive";
     return 1;
   }
-  if (a.N % fold::BN != 0) {
-    *why = "N must be a multiple of 256";
+  if (a.N % 128 != 0 || a.N < fold::BN) {
+    *why = "N must be a multiple of 128 and at least 256";
     return 1;
   }
   if (a.K % fold::BK != 0) {
@@ -366,7 +375,7 @@ int gemm_fold_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
     *why = "cuTensorMapEncodeTiled rejected an operand (alignment or stride)";
     return 2;
   }
-  const dim3 grid((a.M + fold::BM - 1) / fold::BM, a.N / fold::BN);
+  const dim3 grid((a.M + fold::BM - 1) / fold::BM, (a.N + fold::BN - 1) / fold::BN);
   cudaError_t e = cudaSuccess;
   auto launch = [&](auto kernel) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(fold::kSmemBytes));

@@ -34,6 +34,7 @@ SIGNATURES = {
     "wdl_w4a4_gemm_residual_add": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _P, _P, _I64, _I, _I, _I, _P, _I64, _P]),
     "wdl_w4a4_gemm_gelu_u4_add": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _P, ctypes.c_float, _I, _I, _I, _I, _P,
                                        _I64, _P, _P, _I64, _P]),
+    "wdl_w4a4_gemm_f32": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _I, _I, _I, _P, _I64, _P]),
     "wdl_w4a4_linear_workspace": (_SZ, [_I, _I]),
     "wdl_w4a4_linear": (_I, [_P, _I64, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P, _I64, _P, _SZ, _P]),
     "wdl_w4a4_linear_noalloc": (_I, [_P, _I64, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P, _I64, _P]),
@@ -41,9 +42,14 @@ SIGNATURES = {
     "wdl_rope_apply": (_I, [_P, _I, _P, _I, _I, _I, _I, _P, _P, _I, _P, _I, _I, _P, _I, _P]),
     "wdl_qkv_prep": (_I, [_P, _I64, _I, _I, _P, _P, ctypes.c_float, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,
                           _I, _I, _P]),
+    "wdl_qkv_prep_sharded": (_I, [_P, _I64, _I, _I, _P, _P, ctypes.c_float, _P, _I, _P, _I, _I, _I, _I, _P, _P, _P,
+                                  _P, _P, _P, _I, _I, _P]),
     "wdl_w4a4_gemm_gelu_u4": (_I, [_P, _P, _P, _P, _I, _P, _P, ctypes.c_float, _I, _I, _I, _I, _P, _I64, _P, _P]),
     "wdl_ln_quant": (_I, [_P, _I, _I64, _I, _I, ctypes.c_float, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P, _P]),
     "wdl_rms_rows": (_I, [_P, _I64, _I, _I, _P, ctypes.c_float, _P, _I64, _P]),
+    "wdl_rms_rows_sharded": (_I, [_P, _I64, _I, _I, _P, ctypes.c_float, _P, _I, _P, _I64, _P]),
+    "wdl_rows_sumsq": (_I, [_P, _I64, _I, _I, _I, _I64, _P, _P]),
+    "wdl_residual_update": (_I, [_P, _I64, _P, _P, _P, _I64, _I, _I, _P]),
     "wdl_modulation": (_I, [_P, _P, _I, _I, _P, _P]),
     "wdl_sage_prep_kv": (_I, [_P, _P, _P, _P, _I, _P, _I, _I64, _P, _I, _I64, _I, _I, _P, _P, _P, _P, _P, _SZ, _P]),
     "wdl_sage_quant_q": (_I, [_P, _I64, _I, _I, _P, _P, _P]),

@@ -17,7 +17,7 @@ import math
 import torch
 
 from wan_dit_lab_b200 import _native
-from wan_dit_lab_b200.models.block import Buffers, WanBlockB200
+from wan_dit_lab_b200.models.block import WanBlockB200
 
 SHIFT = 5.0  # timestep_shift of the distilled model (reference causal.py:35)
 STEPS = (1000, 750, 500, 250)  # its four timesteps before the shift (causal.py:36)
@@ -178,12 +178,13 @@ class Stream:
         self.chunk, self.model = chunk, model
         n = chunk * self.tokens
         self.shape = (model.out_dim, chunk, h, w)
-        self.caches = [KVCache((max_frames - chunk) * self.tokens, sink_frames * self.tokens, n, model.heads, model.device)
+        heads = model.blocks[0].kv_heads  # all of them, or this tensor-parallel shard's
+        self.caches = [KVCache((max_frames - chunk) * self.tokens, sink_frames * self.tokens, n, heads, model.device)
                        for _ in model.blocks]
         self.freq = rope_table(positions).to(model.device)
         self.cross = model.cross_kvs(context.to(model.device))
         text_tokens = self.cross[0].tokens
-        self.buf = Buffers(n, model.dim, model.ffn_dim, model.heads, max_frames * self.tokens, text_tokens, model.device)
+        self.buf = model.blocks[0].buffers(n, max_frames * self.tokens, text_tokens, model.device)
         self.levels = sigmas()
         self.generator = generator
         self.start = 0
@@ -232,15 +233,22 @@ def random_block_state(g, dim, ffn_dim, device):
 
 
 def random_model(dim=3072, ffn_dim=14336, freq_dim=256, in_dim=48, out_dim=48, num_heads=24, num_layers=30,
-                 text_dim=4096, seed=6, device="cuda"):
+                 text_dim=4096, seed=6, device="cuda", shard=None, reduce=None):
     """A WanModelB200 of the Wan2.2-TI2V-5B shape with random-init weights (N(0, 0.02)),
     generated on `device` from one seed, one block at a time (each block's float weights are dropped once it
-    is quantized to W4A4)."""
+    is quantized to W4A4). shard = (rank, world): this rank's tensor-parallel shard of every block (every rank
+    generates the same weights from the seed and keeps its heads and hidden channels); reduce: the in-place sum
+    across ranks (torch.distributed.all_reduce)."""
     g = torch.Generator(device=device).manual_seed(seed)
     edges = random_state(dim, freq_dim=freq_dim, in_dim=in_dim, out_dim=out_dim, num_layers=0, text_dim=text_dim,
                          generator=g, device=device)
-    blocks = [WanBlockB200(random_block_state(g, dim, ffn_dim, device), dim, ffn_dim, num_heads, device=device)
-              for _ in range(num_layers)]
+    if shard is None:
+        make = lambda st: WanBlockB200(st, dim, ffn_dim, num_heads, device=device)  # noqa: E731
+    else:
+        from wan_dit_lab_b200.models.block_tp import WanBlockTP
+        make = lambda st: WanBlockTP(st, dim, ffn_dim, num_heads, shard[0], shard[1], device=device,  # noqa: E731
+                                     reduce=reduce)
+    blocks = [make(random_block_state(g, dim, ffn_dim, device)) for _ in range(num_layers)]
     return WanModelB200(edges, dim, ffn_dim, freq_dim, in_dim, out_dim, num_heads, num_layers, device=device,
                         blocks=blocks)
 

@@ -34,28 +34,50 @@ def _f32(t):
 
 
 class Buffers:
-    """Scratch of one chunk of n tokens, shared by all the blocks of a model (they run one after another)."""
+    """Scratch of one chunk of n tokens, shared by all the blocks of a model (they run one after another). heads:
+    the heads this process holds (all of them, or a tensor-parallel shard's), ffn_dim its hidden channels; dim the
+    model's width (the residual stream). sharded: also the fp32 partial products and RMS statistics that a
+    tensor-parallel block sums across shards."""
 
-    def __init__(self, n, dim, ffn_dim, heads, max_keys, text_tokens, device):
+    def __init__(self, n, dim, ffn_dim, heads, max_keys, text_tokens, device, sharded=False):
         self.n, self.dim, self.ffn = n, dim, ffn_dim
         u8 = dict(dtype=torch.uint8, device=device)
         f32 = dict(dtype=torch.float32, device=device)
         bf = dict(dtype=torch.bfloat16, device=device)
+        hd = heads * HEAD_DIM
         width = max(dim, ffn_dim)
         self.codes = torch.empty(n, 2 * width, **u8)  # room for the float16 codes of "f16fold"
         self.scales = torch.empty(width // 64, n, 4, **f32)  # room for the padded scales of "e4m3ts"
         self.hcodes = torch.empty(n, 2 * ffn_dim, **u8)  # rows of ffn_dim codes, one or two bytes each
         self.hscales = torch.empty(ffn_dim // 64, n, 4, **f32)
-        self.qkv = torch.empty(n, 3 * dim, **bf)
-        self.q = torch.empty(n, dim, **f32)
-        self.k = torch.empty(n, dim, **f32)
-        self.attn = torch.empty(n, dim, **bf)
-        self.cq = torch.empty(n, dim, **bf)
+        self.qkv = torch.empty(n, 3 * hd, **bf)
+        self.q = torch.empty(n, hd, **f32)
+        self.k = torch.empty(n, hd, **f32)
+        self.attn = torch.empty(n, hd, **bf)
+        self.cq = torch.empty(n, hd, **bf)
         npad = -(-n // 128) * 128
         self.q_i8 = torch.empty(heads, npad, HEAD_DIM, dtype=torch.int8, device=device)
         self.q_scale = torch.empty(heads, npad // 32 * 8, **f32)
         lib = _native.lib()
         self.sage = torch.empty(lib.wdl_sage_attend_workspace(n, max_keys, heads), **u8)
+        if sharded:
+            self.partial = torch.empty(n, dim, **f32)  # a row-parallel layer's share of its product
+            self.sumsq = torch.empty(n, 2, **f32)  # the shard's share of the q / k RMS statistics
+
+
+def quantize_block(p, scale_dtype=torch.bfloat16):
+    """The W4A4 parts {layer: quantize() tensors} of a block's float weights p (the reference's names; rank 0; q, k
+    and v of self-attention as one qkv layer, FusedQKVAttention; ffn.2 made for gelu_mlp's shifted input)."""
+    parts = {}
+    cat = lambda *names: torch.cat([p[n] for n in names])  # noqa: E731
+    parts["self_attn.qkv"] = w4a4.quantize(cat("self_attn.q.weight", "self_attn.k.weight", "self_attn.v.weight"),
+                                           cat("self_attn.q.bias", "self_attn.k.bias", "self_attn.v.bias"),
+                                           rank=0, scale_dtype=scale_dtype)
+    for name in ("self_attn.o", "cross_attn.q", "cross_attn.k", "cross_attn.v", "cross_attn.o", "ffn.0"):
+        parts[name] = w4a4.quantize(p[f"{name}.weight"], p[f"{name}.bias"], rank=0, scale_dtype=scale_dtype)
+    parts["ffn.2"] = w4a4.quantize(p["ffn.2.weight"], p["ffn.2.bias"], rank=0, shift=w4a4.GELU_SHIFT,
+                                   scale_dtype=scale_dtype)
+    return parts
 
 
 class CrossKV:
@@ -74,19 +96,12 @@ class WanBlockB200:
     def __init__(self, state, dim, ffn_dim, heads, eps=1e-6, device="cuda", parts=None, scale_dtype=torch.bfloat16,
                  code_format=None):
         self.dim, self.ffn_dim, self.heads, self.eps = dim, ffn_dim, heads, eps
+        self.kv_heads = heads  # the heads of this process's KV cache and attention
         if dim != heads * HEAD_DIM:
             raise ValueError("head_dim must be 128")
         p = {k: v.to(device) for k, v in state.items()}
         if parts is None:
-            parts = {}
-            cat = lambda *names: torch.cat([p[n] for n in names])  # noqa: E731
-            parts["self_attn.qkv"] = w4a4.quantize(cat("self_attn.q.weight", "self_attn.k.weight", "self_attn.v.weight"),
-                                                   cat("self_attn.q.bias", "self_attn.k.bias", "self_attn.v.bias"),
-                                                   rank=0, scale_dtype=scale_dtype)
-            for name in ("self_attn.o", "cross_attn.q", "cross_attn.k", "cross_attn.v", "cross_attn.o", "ffn.0"):
-                parts[name] = w4a4.quantize(p[f"{name}.weight"], p[f"{name}.bias"], rank=0, scale_dtype=scale_dtype)
-            parts["ffn.2"] = w4a4.quantize(p["ffn.2.weight"], p["ffn.2.bias"], rank=0, shift=w4a4.GELU_SHIFT,
-                                           scale_dtype=scale_dtype)
+            parts = quantize_block(p, scale_dtype)
         self.parts = parts
         self.layers = {name: w4a4.PreparedW4A4(*(t[k] for k in w4a4.PARTS), code_format=code_format)
                        for name, t in parts.items()}
@@ -237,6 +252,10 @@ class WanBlockB200:
                  else buf.hscales.view(-1)[:G * n].view(G, n))
         gemm_residual(fc2, 5, buf.hcodes, buf.hscales)
         return X
+
+    def buffers(self, n, max_keys, text_tokens, device):
+        """Scratch for chunks of n tokens attending to up to max_keys keys."""
+        return Buffers(n, self.dim, self.ffn_dim, self.kv_heads, max_keys, text_tokens, device)
 
     def modulation_of(self, time_in):
         """time_in [6, dim] float32 + this block's modulation (models/block.py:75)."""
