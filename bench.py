@@ -224,7 +224,7 @@ def cpu_linear_sample(x, W, rows=256):
     return dt, 2 * rows * W.shape[0] * W.shape[1], f"{rows} of 1392 tokens, full N and K (oracle port, numpy)"
 
 
-def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None):
+def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True):
     """tp = (world, reduce): one stream split across the ranks (tensor parallelism), else one stream per rank."""
     from wan_dit_lab_b200.generation import causal
     from wan_dit_lab_b200.models.block import WanBlockB200
@@ -241,7 +241,8 @@ def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None):
     noise = torch.randn(48, 21, 32, 58, generator=g)
     text = torch.randn(1, 512, 4096, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
     stream = causal.Stream(model, text.to(device), 512, 928,
-                           torch.Generator(device=device).manual_seed(10 + seed_rank), vae_stride=16)
+                           torch.Generator(device=device).manual_seed(10 + seed_rank), vae_stride=16,
+                           cuda_graph=graphs and tp is None)  # passes replayed from CUDA graphs
     noise_d = noise.to(device)
     out = torch.empty_like(noise_d)
 
@@ -264,11 +265,13 @@ def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None):
         """One instrumented chunk: the W4A4 GEMM launches bracketed by CUDA events (returns seconds, ops)."""
         gemm_log.clear()
         block_cls.gemm_timer = lambda e0, e1, ops: gemm_log.append((e0, e1, ops))
+        graphed, stream.use_graphs = stream.use_graphs, False  # launched eagerly, so that each GEMM can be timed
         try:
             stream.reset()
             stream.next_chunk(noise_d[:, :3])
         finally:
             block_cls.gemm_timer = None
+            stream.use_graphs = graphed
         torch.cuda.synchronize()
         return sum(a.elapsed_time(b) for a, b, _ in gemm_log) / 1e3, sum(o for _, _, o in gemm_log), len(gemm_log)
 
@@ -283,6 +286,7 @@ def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None):
                         "model": "Wan2.2-TI2V-5B shape, random init N(0,0.02), W4A4 (INT4 g64, bf16 scales, rank 0)",
                         "tokens_per_chunk": 1392, "keys_per_chunk": [1392 * (c + 1) for c in range(chunks)],
                         "chunks": chunks, "layers": layers, **({} if tp is None else {"tensor_parallel": world}),
+                        "cuda_graphs": bool(graphs and tp is None),
                         "codes": CODES, "l2": "inputs larger than L2 (5 GB of weights per pass)"},
                 algorithmic={"gemm_int_ops_per_block_pass": per_block, "gemm_launches_per_block_pass": 6},
                 cpu=lambda: cpu_block_sample(), dtype="W4A4 (int4 x int4 exact on int8 tensor cores) + INT8/FP8 Sage "
@@ -397,6 +401,7 @@ def main():
                              "kind::f16) or int8 (kind::i8)")
     parser.add_argument("--chunks", type=int, default=7, help="rollout chunks (profiling; BASELINE config 4: 7)")
     parser.add_argument("--layers", type=int, default=30, help="model layers (profiling; BASELINE config 4: 30)")
+    parser.add_argument("--eager", action="store_true", help="launch every kernel from Python (no CUDA graphs)")
     parser.add_argument("--tp", action="store_true",
                         help="BASELINE config 5b: one stream split across the ranks (heads / hidden channels, NCCL "
                              "all-reduce after O, cross-O and FFN-2) instead of one independent stream per rank")
@@ -426,7 +431,7 @@ def main():
     if args.tp and not rollout:
         parser.error("--tp splits the rollout")
     tp = (world, (lambda t: dist.all_reduce(t)) if dist is not None else (lambda t: None)) if args.tp else None
-    wl = (WORKLOADS[args.workload](device, rank, args.chunks, args.layers, tp) if rollout
+    wl = (WORKLOADS[args.workload](device, rank, args.chunks, args.layers, tp, not args.eager) if rollout
           else WORKLOADS[args.workload](device))
     stream = torch.cuda.current_stream(device)
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)

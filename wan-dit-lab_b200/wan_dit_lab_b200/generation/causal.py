@@ -117,6 +117,7 @@ class WanModelB200:
         self.modulation = torch.stack([b.modulation for b in blocks]).contiguous()  # [layers, 6, dim]
         self.mods = torch.empty_like(self.modulation)
         self.device = dev
+        self._times = {}
 
     # ---- edges (bf16 PyTorch ops, as the reference runs them under autocast)
     def text_embedding(self, context):
@@ -148,6 +149,15 @@ class WanModelB200:
         y = y.view(1, f, h, w, 1, 2, 2, self.out_dim)
         return y.permute(0, 7, 1, 4, 2, 5, 3, 6).reshape(self.out_dim, f, h * 2, w * 2)
 
+    def time_cached(self, t):
+        """time_in(t), kept per timestep (a rollout uses the same five): no host-to-device copy on later passes."""
+        key = float(t)
+        got = self._times.get(key)
+        if got is None:
+            got = self.time_in(t)
+            self._times[key] = got
+        return got
+
     def cross_kvs(self, context):
         ctx = self.text_embedding(context)
         return [b.cross_kv(ctx[0] if ctx.ndim == 3 else ctx) for b in self.blocks]
@@ -155,8 +165,13 @@ class WanModelB200:
     def forward(self, x, t, grid, freq, start, caches, cross, buf):
         """One pass over a chunk x [C, f, H, W] at timestep t: the flow prediction [out_dim, f, H, W] (float32).
         Every block stores the chunk's keys / values into its cache at cache.saved and attends to [0, saved + n)."""
+        e0, temb = self.time_cached(t)
+        return self.forward_embedded(x, e0, temb, grid, freq, start, caches, cross, buf)
+
+    def forward_embedded(self, x, e0, temb, grid, freq, start, caches, cross, buf):
+        """forward with the timestep already embedded (e0 [6, dim] float32, temb [dim]): every tensor it reads is
+        on the device, so that a pass can be recorded into a CUDA graph over fixed buffers."""
         X = self.patch_embed(x).float()
-        e0, temb = self.time_in(t)
         _native.check(_native.lib().wdl_modulation(e0.data_ptr(), self.modulation.data_ptr(), len(self.blocks), self.dim,
                                                    self.mods.data_ptr(), _native.stream()))
         for i, blk in enumerate(self.blocks):
@@ -165,13 +180,52 @@ class WanModelB200:
         return self.head(X, temb, grid).float()
 
 
+class PassGraphs:
+    """Passes of the model over a chunk replayed from CUDA graphs (reference Pass, causal.py:381-413). A pass reads
+    fixed buffers (latents, time embedding, the chunk's RoPE table, caches, prompt keys / values, scratch); what
+    changes between chunks on the device side is the cache fill `saved` (where the chunk's keys go and how many
+    keys attention reads), so there is one graph per fill level: one per chunk until the cache is full, then one
+    for every later chunk. Each is recorded on its first use after one eager run of the same pass (which writes
+    the same cache rows the recorded pass then writes again), and a pass is then three device copies and one
+    replay: no kernel launched from Python."""
+
+    def __init__(self, model, shape, max_graphs=16):
+        dev = model.device
+        self.model, self.max_graphs = model, max_graphs
+        self.x = torch.empty(shape, device=dev)
+        self.e0 = torch.empty(6, model.dim, device=dev)
+        self.temb = torch.empty(model.dim, dtype=torch.bfloat16, device=dev)
+        self.pool = torch.cuda.graph_pool_handle()
+        self.graphs = {}  # saved -> (graph, output)
+
+    def run(self, x, t, grid, freq, caches, cross, buf):
+        e0, temb = self.model.time_cached(t)
+        self.x.copy_(x)
+        self.e0.copy_(e0)
+        self.temb.copy_(temb)
+        key = caches[0].saved
+        entry = self.graphs.pop(key, None)
+        if entry is None:
+            args = (self.x, self.e0, self.temb, grid, freq, 0, caches, cross, buf)
+            self.model.forward_embedded(*args)  # warm-up: lazy initializations happen outside the capture
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, pool=self.pool, capture_error_mode="thread_local"):
+                out = self.model.forward_embedded(*args)
+            entry = (graph, out)
+            if len(self.graphs) >= self.max_graphs:
+                self.graphs.pop(next(iter(self.graphs)))
+        self.graphs[key] = entry  # most recently used last
+        entry[0].replay()
+        return entry[1]
+
+
 class Stream:
     """A video, chunk by chunk (reference Stream with sampler "dmd", kv_fp8, attention "sage", positions "video",
     write_pass True, cross_cache True): next_chunk denoises a chunk in len(levels) passes, writes its keys and
     values with one more pass at t = 0, and commits them."""
 
     def __init__(self, model, context, height, width, generator=None, max_frames=CONTEXT, sink_frames=0, chunk=CHUNK,
-                 vae_stride=8, positions=1024):
+                 vae_stride=8, positions=1024, cuda_graph=False):
         h, w = height // vae_stride, width // vae_stride
         self.tokens = (h // 2) * (w // 2)
         self.grid = (chunk, h // 2, w // 2)
@@ -182,12 +236,17 @@ class Stream:
         self.caches = [KVCache((max_frames - chunk) * self.tokens, sink_frames * self.tokens, n, heads, model.device)
                        for _ in model.blocks]
         self.freq = rope_table(positions).to(model.device)
+        # the chunk's table: its frames' time angles in rows 0.. (the kernels run with start 0), height / width
+        # angles as in the whole table (reference Stream's chunk_freqs), refreshed in place before every chunk
+        self.chunk_freq = self.freq.clone()
         self.cross = model.cross_kvs(context.to(model.device))
         text_tokens = self.cross[0].tokens
         self.buf = model.blocks[0].buffers(n, max_frames * self.tokens, text_tokens, model.device)
         self.levels = sigmas()
         self.generator = generator
         self.start = 0
+        self.graphs = PassGraphs(model, self.shape) if cuda_graph else None
+        self.use_graphs = cuda_graph
 
     def reset(self):
         """A new video under the same prompt: caches emptied (buffers kept), frames counted from 0 again."""
@@ -201,7 +260,13 @@ class Stream:
         """Latents [C, chunk, H, W] of the next chunk (reference causal.py:681-758, dmd sampler)."""
         dev = self.model.device
         x = torch.randn(self.shape, generator=self.generator, device=dev) if noise is None else noise
-        run = lambda xx, t: self.model.forward(xx, t, self.grid, self.freq, self.start, self.caches, self.cross, self.buf)  # noqa: E731
+        time_pairs = 64 - 2 * 21  # head_dim 128: the first 22 angle pairs are the time axis
+        self.chunk_freq[:, :self.chunk, :time_pairs].copy_(self.freq[:, self.start:self.start + self.chunk, :time_pairs])
+        if self.use_graphs:
+            run = lambda xx, t: self.graphs.run(xx, t, self.grid, self.chunk_freq, self.caches, self.cross, self.buf)  # noqa: E731
+        else:
+            run = lambda xx, t: self.model.forward(xx, t, self.grid, self.chunk_freq, 0, self.caches, self.cross,  # noqa: E731
+                                                   self.buf)
         x0 = x
         for i, sigma in enumerate(self.levels):
             flow = run(x, 1000 * sigma)
