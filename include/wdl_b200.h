@@ -305,6 +305,18 @@ int wdl_sage_attend(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k
                     const void* v, int v_dtype, int64_t ld_v, int n, int H, float sm_scale, uint16_t* out,
                     int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* wdl_sage_attend with Forcing-KV's index maps (sage_kv.attend heads / tokens, kernels/sage_kv.py:127-134; used by
+ * KVCache.attend_split, generation/causal.py:222-240): the cache holds cache_rows rows of cache_heads heads
+ * ([cache_rows, cache_heads, 128] and [cache_rows, cache_heads]); head h of the call (of q, k, v, out; H of them)
+ * is cache head heads[h] (null: h, and then cache_heads == H); cached key j < at is cache row tokens[j] (null: row
+ * j, and then at <= cache_rows). Neither copies the cache. A map entry out of range is read as 0 and reported in
+ * the device error word (wdl_device_error). */
+int wdl_sage_attend_maps(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
+                         const uint8_t* cache_v, const float* cache_vs, int cache_rows, int cache_heads,
+                         const int32_t* heads, const int32_t* tokens, int at, const void* k, int k_dtype, int64_t ld_k,
+                         const void* v, int v_dtype, int64_t ld_v, int n, int H, float sm_scale, uint16_t* out,
+                         int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

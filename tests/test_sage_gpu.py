@@ -85,7 +85,49 @@ def test_attend_rejects_invalid_contracts():
     host, d = setup(20, 10, 10, 1)
     with pytest.raises(ValueError):
         sage_kv.attend(d["Q"], d["ck"], d["cks"], d["cv"], d["cvs"], 10 ** 6, d["K"], d["V"])
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError):  # a head map must be int32 [H]
         sage_kv.attend(d["Q"], d["ck"], d["cks"], d["cv"], d["cvs"], 20, d["K"], d["V"], heads=torch.zeros(1))
     with pytest.raises(TypeError):
         sage_kv.attend(d["Q"], d["ck"].float(), d["cks"], d["cv"], d["cvs"], 20, d["K"], d["V"])
+
+
+@pytest.mark.parametrize("at,n,H,cache_heads", [(200, 150, 2, 4), (1392, 1392, 3, 8)])
+def test_forcing_kv_maps_equal_a_gathered_cache(at, n, H, cache_heads):
+    """Head and token maps (Forcing-KV, sage_kv.py:127-134) read the cache in place: the result equals, bit for bit,
+    attention over a copy of the cache gathered through the same maps."""
+    from wan_dit_lab_b200.kernels import sage_kv
+    from wan_dit_lab_b200 import _native
+    rows = at + 300
+    _, d = setup(rows, n, n, cache_heads, seed=7)
+    g = torch.Generator().manual_seed(8)
+    heads = torch.randperm(cache_heads, generator=g)[:H].to(torch.int32).cuda()
+    tokens = torch.randperm(rows, generator=g)[:at].to(torch.int32).cuda()
+    Q, K, V = (d[x][:, :, :H].contiguous() for x in ("Q", "K", "V"))
+    got = sage_kv.attend(Q, d["ck"], d["cks"], d["cv"], d["cvs"], at, K, V, heads=heads, tokens=tokens)
+    assert _native.device_error() == 0
+    t, h = tokens.long(), heads.long()
+    gather = lambda c: c[:, t][:, :, h].contiguous()  # noqa: E731
+    want = sage_kv.attend(Q, gather(d["ck"]), gather(d["cks"]), gather(d["cv"]), gather(d["cvs"]), at, K, V)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    # heads alone over the whole window, tokens alone with every head
+    got_h = sage_kv.attend(Q, d["ck"], d["cks"], d["cv"], d["cvs"], at, K, V, heads=heads)
+    want_h = sage_kv.attend(Q, d["ck"][:, :, h].contiguous(), d["cks"][:, :, h].contiguous(),
+                            d["cv"][:, :, h].contiguous(), d["cvs"][:, :, h].contiguous(), at, K, V)
+    assert torch.equal(got_h, want_h)
+    assert _native.device_error() == 0
+
+
+def test_forcing_kv_map_out_of_range_is_reported():
+    """A token map entry past the cache is caught by the kernel's own bounds check: read as row 0, reported."""
+    from wan_dit_lab_b200.kernels import sage_kv
+    from wan_dit_lab_b200 import _native
+    at, n, H = 64, 64, 1
+    _, d = setup(at, n, n, H, seed=9)
+    tokens = torch.arange(at, dtype=torch.int32).cuda()
+    tokens[5] = d["ck"].shape[1] + 1000
+    out = sage_kv.attend(d["Q"], d["ck"], d["cks"], d["cv"], d["cvs"], at, d["K"], d["V"], tokens=tokens)
+    with pytest.raises(RuntimeError, match="index map.*code 7"):
+        _native.device_error()
+    assert torch.isfinite(out.float()).all()
+    assert _native.device_error() == 0  # read and cleared

@@ -110,7 +110,9 @@ int wdl_device_error(void* stream, uint32_t* code) {
   if (*code != 0) {
     const uint32_t zero = 0;
     cudaMemcpy(w, &zero, sizeof(zero), cudaMemcpyHostToDevice);
-    return fail(WDL_ERR_DEVICE, "a kernel gave up a bounded wait (device error code %u)", *code);
+    return fail(WDL_ERR_DEVICE, "%s (device error code %u)",
+                *code == wdl::kErrIndex ? "an index map held an entry out of range" : "a kernel gave up a bounded wait",
+                *code);
   }
   return ok();
 }
@@ -556,10 +558,20 @@ size_t wdl_sage_prep_workspace(int L, int H) {
 static size_t pad128(int x) { return (static_cast<size_t>(x) + 127) / 128 * 128; }
 static size_t up256(size_t x) { return (x + 255) / 256 * 256; }
 
-int wdl_sage_prep(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
-                  const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype, int64_t ld_k,
-                  const void* v, int v_dtype, int64_t ld_v, int n, int H, int8_t* q_i8, float* q_scale, int8_t* k_i8,
-                  float* k_scale, uint8_t* v_f8, float* v_scale, void* work, size_t work_bytes, void* stream) {
+}  // extern "C"
+
+// Forcing-KV's index maps of a Sage call (null: none).
+struct SageMaps {
+  int cache_rows, cache_heads;
+  const int32_t* heads;
+  const int32_t* tokens;
+};
+
+static int sage_prep_impl(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
+                          const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype,
+                          int64_t ld_k, const void* v, int v_dtype, int64_t ld_v, int n, int H, int8_t* q_i8,
+                          float* q_scale, int8_t* k_i8, float* k_scale, uint8_t* v_f8, float* v_scale, void* work,
+                          size_t work_bytes, const SageMaps* maps, void* stream) {
   if (nq <= 0 || n < 0 || at < 0 || H <= 0 || at + n <= 0) return fail(WDL_ERR_ARGUMENT, "nq, H and L = at + n must be positive");
   if ((k_dtype != WDL_F32 && k_dtype != WDL_BF16) || (v_dtype != WDL_F32 && v_dtype != WDL_BF16))
     return fail(WDL_ERR_ARGUMENT, "chunk K and V must be float32 or bf16");
@@ -578,8 +590,23 @@ int wdl_sage_prep(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, 
   a.k_chunk = k, a.ld_k = ld_k, a.k_bf16 = k_dtype == WDL_BF16, a.v_chunk = v, a.ld_v = ld_v, a.v_bf16 = v_dtype == WDL_BF16;
   a.n = n, a.H = H, a.q = q, a.ld_q = ld_q, a.nq = nq, a.q_i8 = q_i8, a.q_scale = q_scale, a.k_i8 = k_i8;
   a.k_scale = k_scale, a.v_f8 = v_f8, a.v_scale = v_scale, a.work = static_cast<float*>(work);
+  if (maps) {
+    a.cache_H = maps->cache_heads, a.cache_rows = maps->cache_rows, a.hmap = maps->heads, a.tmap = maps->tokens;
+    a.err = error_word();
+    if (!a.err) return fail(WDL_ERR_CUDA, "cannot resolve the device error word");
+  }
   wdl::sage::prep_launch(a, static_cast<cudaStream_t>(stream));
   return cuda_status(cudaGetLastError(), "sage prep launch");
+}
+
+extern "C" {
+
+int wdl_sage_prep(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
+                  const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype, int64_t ld_k,
+                  const void* v, int v_dtype, int64_t ld_v, int n, int H, int8_t* q_i8, float* q_scale, int8_t* k_i8,
+                  float* k_scale, uint8_t* v_f8, float* v_scale, void* work, size_t work_bytes, void* stream) {
+  return sage_prep_impl(q, ld_q, nq, cache_k, cache_ks, cache_v, cache_vs, at, k, k_dtype, ld_k, v, v_dtype, ld_v, n,
+                        H, q_i8, q_scale, k_i8, k_scale, v_f8, v_scale, work, work_bytes, nullptr, stream);
 }
 
 int wdl_sage_attention(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale,
@@ -609,10 +636,13 @@ size_t wdl_sage_attend_workspace(int nq, int L, int H) {
          up256(h * 128 * lp) + up256(h * 128 * 4) + up256(wdl_sage_prep_workspace(L, H));
 }
 
-int wdl_sage_attend(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
-                    const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype, int64_t ld_k,
-                    const void* v, int v_dtype, int64_t ld_v, int n, int H, float sm_scale, uint16_t* out,
-                    int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+static int sage_attend_impl(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
+                            const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype,
+                            int64_t ld_k, const void* v, int v_dtype, int64_t ld_v, int n, int H, float sm_scale,
+                            uint16_t* out, int64_t ld_out, void* workspace, size_t workspace_bytes,
+                            const SageMaps* maps, void* stream) {
   const int L = at + n;
   if (nq <= 0 || L <= 0 || H <= 0) return fail(WDL_ERR_ARGUMENT, "nq, H and L = at + n must be positive");
   const size_t need = wdl_sage_attend_workspace(nq, L, H);
@@ -632,10 +662,35 @@ int wdl_sage_attend(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k
   p += up256(h * 128 * lp);
   float* v_scale = reinterpret_cast<float*>(p);
   p += up256(h * 128 * 4);
-  int st = wdl_sage_prep(q, ld_q, nq, cache_k, cache_ks, cache_v, cache_vs, at, k, k_dtype, ld_k, v, v_dtype, ld_v, n,
-                         H, q_i8, q_scale, k_i8, k_scale, v_f8, v_scale, p, wdl_sage_prep_workspace(L, H), stream);
+  int st = sage_prep_impl(q, ld_q, nq, cache_k, cache_ks, cache_v, cache_vs, at, k, k_dtype, ld_k, v, v_dtype, ld_v,
+                          n, H, q_i8, q_scale, k_i8, k_scale, v_f8, v_scale, p, wdl_sage_prep_workspace(L, H), maps,
+                          stream);
   if (st != WDL_OK) return st;
   return wdl_sage_attention(q_i8, q_scale, k_i8, k_scale, v_f8, v_scale, nq, L, H, sm_scale, out, ld_out, stream);
+}
+
+extern "C" {
+
+int wdl_sage_attend(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
+                    const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype, int64_t ld_k,
+                    const void* v, int v_dtype, int64_t ld_v, int n, int H, float sm_scale, uint16_t* out,
+                    int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream) {
+  return sage_attend_impl(q, ld_q, nq, cache_k, cache_ks, cache_v, cache_vs, at, k, k_dtype, ld_k, v, v_dtype, ld_v, n,
+                          H, sm_scale, out, ld_out, workspace, workspace_bytes, nullptr, stream);
+}
+
+int wdl_sage_attend_maps(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
+                         const uint8_t* cache_v, const float* cache_vs, int cache_rows, int cache_heads,
+                         const int32_t* heads, const int32_t* tokens, int at, const void* k, int k_dtype, int64_t ld_k,
+                         const void* v, int v_dtype, int64_t ld_v, int n, int H, float sm_scale, uint16_t* out,
+                         int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (cache_rows < 0 || cache_heads <= 0) return fail(WDL_ERR_ARGUMENT, "cache_rows >= 0 and cache_heads > 0 required");
+  if (!heads && cache_heads != H) return fail(WDL_ERR_ARGUMENT, "without a head map the cache holds the call's H heads");
+  if (!tokens && at > cache_rows) return fail(WDL_ERR_ARGUMENT, "without a token map at must not exceed cache_rows");
+  if (!aligned(heads, 4) || !aligned(tokens, 4)) return fail(WDL_ERR_ARGUMENT, "misaligned map");
+  const SageMaps maps{cache_rows, cache_heads, heads, tokens};
+  return sage_attend_impl(q, ld_q, nq, cache_k, cache_ks, cache_v, cache_vs, at, k, k_dtype, ld_k, v, v_dtype, ld_v, n,
+                          H, sm_scale, out, ld_out, workspace, workspace_bytes, &maps, stream);
 }
 
 }  // extern "C"

@@ -28,6 +28,7 @@ enum DeviceError : uint32_t {
   kErrWaitAccEmpty = 4,  // the MMA issuer gave up waiting for a drained accumulator
   kErrWaitScale = 5,     // the producer gave up waiting for a released scale stage
   kErrTmemAlloc = 6,     // the TMEM allocation did not return a usable address
+  kErrIndex = 7,         // an index map held an entry out of range (the entry was read as 0)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -24,16 +24,41 @@ __device__ __forceinline__ uint8_t e4m3(float x) {
 // Channels d .. d + 3 (d % 4 == 0) of token j of head h, as _load of sage_kv.py:29-40 reads them: the cache
 // bytes times their scale before `at`, the chunk's values after. One 32-bit load of four E4M3 bytes (decoded two
 // at a time through f16x2, exactly), or one 16-byte / 8-byte load of four float32 / bf16 values.
+// With Forcing-KV's maps (sage_kv.py:127-134): head h of the call is cache head hmap[h] (the cache keeping all
+// cache_H of them) and cached key j is cache row tmap[j]; an entry out of range is reported (kErrIndex) and read
+// as row / head 0. Without maps, key j is row j and head h is cache head h.
 struct Source {
-  const uint8_t* cache;  // [cap, H, 128]
-  const float* scale;    // [cap, H]
+  const uint8_t* cache;  // [cache_rows, cache_H, 128]
+  const float* scale;    // [cache_rows, cache_H]
   const void* chunk;     // [n, ld] float32 (keys) or bf16 (values), head h at column h * 128
   int64_t ld;
   int chunk_bf16;
   int at, L, H;
+  int cache_H, cache_rows;
+  const int* hmap;  // [H] or null
+  const int* tmap;  // [at] or null
+  uint32_t* err;
+  __device__ __forceinline__ int cache_head(int h) const {
+    if (!hmap) return h;
+    const int c = __ldg(hmap + h);
+    if (c < 0 || c >= cache_H) {
+      atomicCAS(err, 0u, static_cast<uint32_t>(kErrIndex));
+      return 0;
+    }
+    return c;
+  }
+  __device__ __forceinline__ int64_t cache_row(int j) const {
+    if (!tmap) return j;
+    const int r = __ldg(tmap + j);
+    if (r < 0 || r >= cache_rows) {
+      atomicCAS(err, 0u, static_cast<uint32_t>(kErrIndex));
+      return 0;
+    }
+    return r;
+  }
   __device__ __forceinline__ void get4(int j, int h, int d, float (&o)[4]) const {
     if (j < at) {
-      const int64_t r = static_cast<int64_t>(j) * H + h;
+      const int64_t r = cache_row(j) * cache_H + cache_head(h);
       const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(cache + r * 128 + d));
       const float s = __ldg(scale + r);
       const __half2 lo(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w & 0xFFFFu), __NV_E4M3));
@@ -62,9 +87,13 @@ struct Source {
     if (where == 1) {
       uint32_t w[N];
       float s[N];
+      int64_t rows[N];
+      const int ch = cache_head(h);
+#pragma unroll
+      for (int i = 0; i < N; ++i) rows[i] = valid[i] ? cache_row(j[i]) : 0;  // all map loads before the data loads
 #pragma unroll
       for (int i = 0; i < N; ++i) {
-        const int64_t r = static_cast<int64_t>(valid[i] ? j[i] : 0) * H + h;
+        const int64_t r = rows[i] * cache_H + ch;
         w[i] = valid[i] ? __ldg(reinterpret_cast<const uint32_t*>(cache + r * 128 + d)) : 0u;
         s[i] = valid[i] ? __ldg(scale + r) : 0.f;
       }
@@ -302,8 +331,11 @@ __global__ void __launch_bounds__(128) quant_q_kernel(const float* q, int64_t ld
 
 void prep_kv_launch(const PrepArgs& a, cudaStream_t s) {
   const int L = a.at + a.n;
-  Source ks{a.cache_k, a.cache_ks, a.k_chunk, a.ld_k, a.k_bf16, a.at, L, a.H};
-  Source vs{a.cache_v, a.cache_vs, a.v_chunk, a.ld_v, a.v_bf16, a.at, L, a.H};
+  const int cache_H = a.cache_H > 0 ? a.cache_H : a.H;
+  Source ks{a.cache_k, a.cache_ks, a.k_chunk, a.ld_k, a.k_bf16, a.at, L, a.H, cache_H, a.cache_rows, a.hmap, a.tmap,
+            a.err};
+  Source vs{a.cache_v, a.cache_vs, a.v_chunk, a.ld_v, a.v_bf16, a.at, L, a.H, cache_H, a.cache_rows, a.hmap, a.tmap,
+            a.err};
   const int tiles = (L + 63) / 64;
   const int Lpad = (L + 127) / 128 * 128;
   float* ksum = a.work;

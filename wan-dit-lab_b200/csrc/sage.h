@@ -38,6 +38,12 @@ struct PrepArgs {
   uint8_t* v_f8;   // [H, 128, Lpad]
   float* v_scale;  // [H, 128]
   float* work;     // prep_workspace_floats(L, H) floats
+  // Forcing-KV maps (all optional): the cache holds cache_H heads per row (0: H) and cache_rows rows; head h is
+  // cache head hmap[h], cached key j is cache row tmap[j]. err: the device error word (out-of-range entries).
+  int cache_H, cache_rows;
+  const int* hmap;
+  const int* tmap;
+  uint32_t* err;
 };
 void prep_launch(const PrepArgs& a, cudaStream_t s);     // K / V then Q
 void prep_kv_launch(const PrepArgs& a, cudaStream_t s);  // K / V only (q fields unused)

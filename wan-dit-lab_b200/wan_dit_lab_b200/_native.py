@@ -60,6 +60,8 @@ SIGNATURES = {
     "wdl_sage_attend_workspace": (_SZ, [_I, _I, _I]),
     "wdl_sage_attend": (_I, [_P, _I64, _I, _P, _P, _P, _P, _I, _P, _I, _I64, _P, _I, _I64, _I, _I, ctypes.c_float,
                              _P, _I64, _P, _SZ, _P]),
+    "wdl_sage_attend_maps": (_I, [_P, _I64, _I, _P, _P, _P, _P, _I, _I, _P, _P, _I, _P, _I, _I64, _P, _I, _I64, _I,
+                                  _I, ctypes.c_float, _P, _I64, _P, _SZ, _P]),
 }
 
 _lib = None
@@ -98,7 +100,9 @@ def stream(device=None):
 
 
 def device_error(device=None):
-    """Synchronises the current stream and raises if a kernel gave up a bounded wait since the last check."""
+    """Synchronises the current stream and reads (and clears) the device error word: 0, or raises RuntimeError
+    naming the code a kernel recorded since the last check (a bounded wait given up, or an index map entry out of
+    range)."""
     code = ctypes.c_uint32(0)
     check(lib().wdl_device_error(stream(device), ctypes.byref(code)))
     return code.value

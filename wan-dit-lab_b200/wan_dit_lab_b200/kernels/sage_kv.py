@@ -15,7 +15,7 @@ V_MAX = 2.25  # the largest |V| in FP8 after the channel scale (reference sage_k
 BLKQ, WARPQ, BLKK = 128, 32, 64
 
 
-def _validate(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V):
+def _validate(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, heads=None, tokens=None):
     if Q.ndim != 4 or K.ndim != 4 or V.shape != K.shape:
         raise ValueError("Q, K, V must be [B, tokens, heads, head_dim] with K and V alike")
     B, nq, H, D = Q.shape
@@ -23,13 +23,18 @@ def _validate(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V):
         raise ValueError("the B200 Sage path takes batch 1 (one video stream per call)")
     if D != 128 or K.shape[2] != H or K.shape[3] != D:
         raise ValueError("head_dim 128 and matching heads required")
-    if cache_k.shape[0] != 1 or cache_k.shape[2:] != (H, D) or cache_v.shape != cache_k.shape:
+    if (cache_k.shape[0] != 1 or cache_k.shape[3] != D or cache_v.shape != cache_k.shape
+            or (heads is None and cache_k.shape[2] != H)):
         raise ValueError("Cache dimensions must match inputs")
+    for name, m, count in (("heads", heads, H), ("tokens", tokens, at)):
+        if m is not None and (m.dtype != torch.int32 or m.ndim != 1 or m.numel() != count or m.device != Q.device
+                              or not m.is_contiguous()):
+            raise ValueError(f"{name} must be a contiguous int32 [{count}] tensor on Q's device")
     if cache_k.dtype != torch.float8_e4m3fn or cache_v.dtype != torch.float8_e4m3fn:
         raise TypeError("Cache values must be FP8 E4M3FN")
     if cache_ks.dtype != torch.float32 or cache_vs.dtype != torch.float32:
         raise TypeError("Cache scales must be FP32")
-    if not isinstance(at, int) or at < 0 or at > cache_k.shape[1]:
+    if not isinstance(at, int) or at < 0 or (tokens is None and at > cache_k.shape[1]):
         raise ValueError("at exceeds cache bounds")
     if K.dtype not in (torch.float32, torch.bfloat16) or V.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError("chunk K and V must be float32 or bfloat16")
@@ -77,11 +82,11 @@ def prepare(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V):
 def attend(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=None, heads=None, tokens=None):
     """softmax(Q K^T / sqrt(d)) V over the cached tokens [0, at) (FP8 cache_k, cache_v with scales per token and
     head cache_ks, cache_vs [1, tokens, H, 1]) and the chunk's own K, V [1, n, H, D]; Q [1, n_q, H, D]. Returns
-    [1, n_q, H, D] in bfloat16 (reference sage_kv.py:127-134). The Forcing-KV maps heads / tokens are not
-    supported on this path."""
-    if heads is not None or tokens is not None:
-        raise NotImplementedError("head / token index maps (Forcing-KV) are not implemented on the B200 path")
-    _validate(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V)
+    [1, n_q, H, D] in bfloat16 (reference sage_kv.py:127-134). heads (int32 [H]): head h of Q, K, V is cache head
+    heads[h], the cache keeping all of them; tokens (int32 [at]): cached token i is cache token tokens[i]. Neither
+    copies the cache (wdl_sage_attend_maps reads through them; an entry out of range is reported by
+    wan_dit_lab_b200._native.device_error())."""
+    _validate(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, heads, tokens)
     _, nq, H, D = Q.shape
     n = K.shape[1]
     L = at + n
@@ -91,9 +96,16 @@ def attend(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=None, hea
     lib = _native.lib()
     work = torch.empty(lib.wdl_sage_attend_workspace(nq, L, H), dtype=torch.uint8, device=Q.device)
     with torch.cuda.device(Q.device):
-        _native.check(lib.wdl_sage_attend(
-            q.data_ptr(), q.stride(0), nq, cache_k.data_ptr(), cache_ks.data_ptr(), cache_v.data_ptr(),
-            cache_vs.data_ptr(), at, k.data_ptr(), _native.DTYPE_CODE[k.dtype], k.stride(0), v.data_ptr(),
-            _native.DTYPE_CODE[v.dtype], v.stride(0), n, H, sm_scale, out.data_ptr(), H * D, work.data_ptr(),
-            work.numel(), _native.stream()))
+        if heads is None and tokens is None:
+            _native.check(lib.wdl_sage_attend(
+                q.data_ptr(), q.stride(0), nq, cache_k.data_ptr(), cache_ks.data_ptr(), cache_v.data_ptr(),
+                cache_vs.data_ptr(), at, k.data_ptr(), _native.DTYPE_CODE[k.dtype], k.stride(0), v.data_ptr(),
+                _native.DTYPE_CODE[v.dtype], v.stride(0), n, H, sm_scale, out.data_ptr(), H * D, work.data_ptr(),
+                work.numel(), _native.stream()))
+        else:
+            _native.check(lib.wdl_sage_attend_maps(
+                q.data_ptr(), q.stride(0), nq, cache_k.data_ptr(), cache_ks.data_ptr(), cache_v.data_ptr(),
+                cache_vs.data_ptr(), cache_k.shape[1], cache_k.shape[2], _native.ptr(heads), _native.ptr(tokens), at,
+                k.data_ptr(), _native.DTYPE_CODE[k.dtype], k.stride(0), v.data_ptr(), _native.DTYPE_CODE[v.dtype],
+                v.stride(0), n, H, sm_scale, out.data_ptr(), H * D, work.data_ptr(), work.numel(), _native.stream()))
     return out
