@@ -233,6 +233,13 @@ int wdl_qkv_prep_sharded(const uint16_t* qkv, int64_t ld, int n, int dim, const 
 int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float eps, const float* ln_w,
                  const float* ln_b, int round_ln_bf16, const float* mod_shift, const float* mod_scale,
                  const uint16_t* smooth, int scale_dtype, int code_format, void* codes, float* scales, void* stream);
+/* wdl_ln_quant that also writes the layer's bf16 input (after LayerNorm and modulation, before the smoothing)
+ * to x_out [M, ld_xo]: what an SVDQuant low-rank branch multiplies by proj_down (Nunchaku's activation quantizer
+ * forms x proj_down from the same values, native/ops/w4a4_ops.cpp:27). */
+int wdl_ln_quant_keep(const void* x, int x_dtype, int64_t ldx, int M, int K, float eps, const float* ln_w,
+                      const float* ln_b, int round_ln_bf16, const float* mod_shift, const float* mod_scale,
+                      const uint16_t* smooth, int scale_dtype, int code_format, void* codes, float* scales,
+                      uint16_t* x_out, int64_t ld_xo, void* stream);
 
 /* RMSNorm of rows: out [M, ldo] f32 = bf16(x * rsqrt(mean(x^2) + eps)) * w for x [M, ldx] bf16 (K % 256 == 0,
  * K <= 4096; x, w and out 16-byte aligned). models/rms_norm.py:10-13 (the query norm of cross-attention, models/multi_head_attention.py:118). */

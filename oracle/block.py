@@ -28,11 +28,13 @@ def layer(parts):
     return codes, parts["wscales"].astype(np.float32), parts["bias"].astype(np.float32)
 
 
-def linear(x_bf16_values, parts, smooth=None, act_scale="bfloat16"):
-    """y float32 = W4A4 linear of x (bf16 values) on the packed parts (before the bf16 rounding of the output)."""
+def linear(x_bf16_values, parts, act_scale="bfloat16"):
+    """y float32 = W4A4 linear of x (bf16 values) on the packed parts (before the bf16 rounding of the output):
+    x divided by the parts' smoothing before its INT4 groups, plus the SVDQuant low-rank branch
+    (x proj_down) proj_up^T when the parts have one (quantization/w4a4.py:141-180)."""
     codes, ws, b = layer(parts)
-    y, _, _ = ow.linear(x_bf16_values, codes, ws, b, smooth, act_scale)
-    return y
+    return ow.linear_lowrank(x_bf16_values, codes, ws, parts.get("proj_down"), parts.get("proj_up"), b,
+                             parts.get("smooth"), act_scale)
 
 
 def layer_norm(x, eps=1e-6, w=None, b=None):
@@ -85,10 +87,15 @@ def block(X, mod, parts, norms, cache, at, freq, grid, start, text, heads, trace
     # feed forward: fc1, GELU + shift quantized unsigned, fc2
     x2 = bf16((layer_norm(X) * (np.float32(1) + sc_f)).astype(np.float32) + sh_f)
     h = linear(x2, parts["ffn.0"])
-    u = (ow.gelu_tanh(h) + np.float32(GELU_SHIFT)).astype(np.float32)
-    hq, hs = ow.int4_groups(u, unsigned=True)
+    g = ow.gelu_tanh(h)
+    u = (g + np.float32(GELU_SHIFT)).astype(np.float32)
+    hq, hs = ow.int4_groups(u, parts["ffn.2"].get("smooth"), unsigned=True)
     keep("hcodes", hq), keep("hscales", ow.round_to(hs, "bfloat16").T.copy())
     codes, ws, b = layer(parts["ffn.2"])
-    f = bf16(ow.gemm(hq, ow.round_to(hs, "bfloat16").T.copy(), codes, ws, b))
+    f = ow.gemm(hq, ow.round_to(hs, "bfloat16").T.copy(), codes, ws)
+    down, up = parts["ffn.2"].get("proj_down"), parts["ffn.2"].get("proj_up")
+    if down is not None and np.asarray(down).size:  # the second branch reads GELU's output without the shift
+        f = f + ow.lowrank(g, down, up)
+    f = bf16(f + b[None, :])
     X = (X + f * g_f).astype(np.float32)
     return X

@@ -119,3 +119,78 @@ def test_block_code_formats_bit_identical(other):
         outs[fmt] = (Xd.cpu(), trace["hcodes"].cpu(), trace["hscales"].cpu(), cache[0].cpu())
     for a, b in zip(outs["e4m3"], outs[other]):
         assert torch.equal(a, b)
+
+
+def lowrank_parts(state, rank, seed):
+    """quantize() parts of every layer with SVDQuant low-rank branches of `rank` and random smoothing vectors (the
+    second FFN layer made for gelu_mlp's shifted input)."""
+    from wan_dit_lab_b200.quantization import w4a4
+    g = torch.Generator().manual_seed(seed)
+    cuda = {k: v.cuda() for k, v in state.items()}
+    smooth = lambda K: (torch.rand(K, generator=g) * 2 + 0.5).cuda()  # noqa: E731
+    cat = lambda *names: torch.cat([cuda[nm] for nm in names])  # noqa: E731
+    dim = state["norm3.weight"].numel()
+    parts = {"self_attn.qkv": w4a4.quantize(cat("self_attn.q.weight", "self_attn.k.weight", "self_attn.v.weight"),
+                                            cat("self_attn.q.bias", "self_attn.k.bias", "self_attn.v.bias"),
+                                            smooth=smooth(dim), rank=rank)}
+    for name in ("self_attn.o", "cross_attn.q", "cross_attn.k", "cross_attn.v", "cross_attn.o", "ffn.0"):
+        W = cuda[f"{name}.weight"]
+        parts[name] = w4a4.quantize(W, cuda[f"{name}.bias"], smooth=smooth(W.shape[1]), rank=rank)
+    W = cuda["ffn.2.weight"]
+    parts["ffn.2"] = w4a4.quantize(W, cuda["ffn.2.bias"], smooth=smooth(W.shape[1]), rank=rank, shift=w4a4.GELU_SHIFT)
+    return parts
+
+
+@pytest.mark.parametrize("rank", [32])
+def test_block_with_lowrank_branches_and_smoothing_matches_oracle(rank):
+    """Packs with SVDQuant low-rank branches and smoothing: the fused block adds every branch's product in its
+    GEMM epilogues (the second FFN layer's from GELU's output) and matches the oracle block on the same parts."""
+    from wan_dit_lab_b200.models.block import WanBlockB200
+    from wan_dit_lab_b200 import _native
+    dim, heads, ffn, frames, h, w, at, text = 1024, 8, 4096, 2, 4, 8, 128, 32
+    n = frames * h * w
+    state = random_state(dim, ffn, 5)
+    parts = lowrank_parts(state, rank, 6)
+    blk = WanBlockB200(state, dim, ffn, heads, parts=parts)
+    assert blk.lowrank and all(layer.rank == rank for layer in blk.layers.values())
+    g = torch.Generator().manual_seed(7)
+    X = torch.randn(n, dim, generator=g)
+    time_in = torch.randn(6, dim, generator=g) * 0.1
+    ctx = (torch.randn(text, dim, generator=g)).to(torch.bfloat16)
+    cap = at + n + 16
+    ck8, cks = of.quantize_rows((torch.randn(1, cap, heads, 128, generator=g) + 0.3).numpy())
+    cv8, cvs = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    freq = orope.table(1024).astype(np.float32)
+    start = at // (h * w)
+    cache = (torch.from_numpy(ck8[0]).cuda(), torch.from_numpy(cks[0, ..., 0]).cuda(),
+             torch.from_numpy(cv8[0]).cuda(), torch.from_numpy(cvs[0, ..., 0]).cuda(), cap)
+    buf = blk.buffers(n, at + n, text, "cuda")
+    mod = blk.modulation_of(time_in.cuda())
+    Xd = X.cuda()
+    gt = {}
+    blk.forward(Xd, mod, cache, at, torch.from_numpy(freq).cuda(), (frames, h, w), start, blk.cross_kv(ctx.cuda()), buf,
+                trace=gt)
+    assert _native.device_error() == 0
+    norms = dict(norm_q=blk.norm_q.cpu().numpy(), norm_k=blk.norm_k.cpu().numpy(),
+                 cross_norm_q=blk.cross_norm_q.cpu().numpy(), cross_norm_k=blk.cross_norm_k.cpu().numpy(),
+                 norm3_w=blk.norm3_w.cpu().numpy(), norm3_b=blk.norm3_b.cpu().numpy())
+    ocache = dict(k=ck8.copy(), ks=cks.copy(), v=cv8.copy(), vs=cvs.copy())
+    ot = {}
+    expected = ob.block(X.numpy(), mod.cpu().numpy(), numpy_parts(parts), norms, ocache, at, freq, (frames, h, w),
+                        start, ctx.float().numpy(), heads, trace=ot)
+    rel = lambda a, b: float(np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(b), 1e-30))  # noqa: E731
+    stages = {name: rel(gt[name].float().cpu().numpy(), ot[name])
+              for name in ("qkv", "q", "k", "attn", "x_after_self", "cq", "cattn", "x_after_cross", "hscales")}
+    stages["hcodes"] = rel(gt["hcodes"].cpu().numpy(), ot["hcodes"].astype(np.float32))
+    print("stages:", {k: round(v, 5) for k, v in stages.items()})
+    d_got, d_exp = Xd.cpu().numpy() - X.numpy(), expected - X.numpy()
+    err = float(np.linalg.norm(d_got - d_exp) / np.linalg.norm(d_exp))
+    print(f"rank {rank} block: residual update relative L2 vs oracle {err:.4f}")
+    # each linear within the stated bar (bf16 relative L2 <= 1e-2); the block as a whole within 5e-2: the branch's
+    # float32 products are summed in another order by the library GEMM than by numpy, and the few bf16 outputs
+    # that round the other way move INT8 K codes, FP8 P and the hidden INT4 codes across rounding boundaries
+    # downstream (at rank 0 there is no such sum and the block stays within 2e-2)
+    assert stages["qkv"] <= 1e-3 and stages["cq"] <= 1e-2
+    assert err <= 5e-2
+    for name, gpu in (("k", cache[0]), ("v", cache[2])):
+        assert (gpu[at:at + n].cpu().numpy() == ocache[name][0, at:at + n]).mean() > 0.99

@@ -57,3 +57,29 @@ def test_chunk_rope_table_equals_start_offset():
     shifted = model.forward(x, 750.0, s.grid, s.chunk_freq, 0, s.caches, s.cross, s.buf).clone()
     whole = model.forward(x, 750.0, s.grid, s.freq, 3, s.caches, s.cross, s.buf)
     assert torch.equal(shifted, whole)
+
+
+def test_graph_replay_with_lowrank_blocks():
+    """Blocks with SVDQuant low-rank branches (their float32 products formed by library GEMMs inside the recorded
+    pass) replay as they run eagerly."""
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from test_block_gpu import lowrank_parts, random_state
+    from wan_dit_lab_b200.generation import causal
+    from wan_dit_lab_b200.models.block import WanBlockB200
+    edges = causal.random_state(DIM, num_layers=0, text_dim=TEXT_DIM, seed=8, device="cuda")
+    blocks = []
+    for i in range(LAYERS):
+        st = random_state(DIM, FFN, 20 + i)
+        blocks.append(WanBlockB200(st, DIM, FFN, HEADS, parts=lowrank_parts(st, 16, 30 + i)))
+    model = causal.WanModelB200(edges, DIM, FFN, num_heads=HEADS, num_layers=LAYERS, device="cuda", blocks=blocks)
+    text = torch.randn(1, 64, TEXT_DIM, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).cuda()
+    eager, graphed = stream(model, text, False), stream(model, text, True)
+    assert hasattr(eager.buf, "xin")
+    noise = torch.randn(48, 9, 16, 16, generator=torch.Generator().manual_seed(9)).cuda()
+    for c in range(3):
+        a = eager.next_chunk(noise[:, 3 * c:3 * c + 3])
+        b = graphed.next_chunk(noise[:, 3 * c:3 * c + 3])
+        torch.cuda.synchronize()
+        assert torch.equal(a, b), f"chunk {c}"

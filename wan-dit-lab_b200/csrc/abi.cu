@@ -430,6 +430,14 @@ int wdl_qkv_prep_sharded(const uint16_t* qkv, int64_t ld, int n, int dim, const 
 int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float eps, const float* ln_w,
                  const float* ln_b, int round_ln_bf16, const float* mod_shift, const float* mod_scale,
                  const uint16_t* smooth, int scale_dtype, int code_format, void* codes, float* scales, void* stream) {
+  return wdl_ln_quant_keep(x, x_dtype, ldx, M, K, eps, ln_w, ln_b, round_ln_bf16, mod_shift, mod_scale, smooth,
+                           scale_dtype, code_format, codes, scales, nullptr, 0, stream);
+}
+
+int wdl_ln_quant_keep(const void* x, int x_dtype, int64_t ldx, int M, int K, float eps, const float* ln_w,
+                      const float* ln_b, int round_ln_bf16, const float* mod_shift, const float* mod_scale,
+                      const uint16_t* smooth, int scale_dtype, int code_format, void* codes, float* scales,
+                      uint16_t* x_out, int64_t ld_xo, void* stream) {
   if (x_dtype != WDL_F32 && x_dtype != WDL_BF16) return fail(WDL_ERR_ARGUMENT, "x must be float32 or bf16");
   if (K <= 0 || K % 256 != 0 || K > 4096) return fail(WDL_ERR_ARGUMENT, "K must be a multiple of 256, at most 4096");
   if (M < 0 || ldx < K) return fail(WDL_ERR_ARGUMENT, "M >= 0 and ldx >= K required");
@@ -444,11 +452,14 @@ int wdl_ln_quant(const void* x, int x_dtype, int64_t ldx, int M, int K, float ep
   if (!aligned(ln_w, 16) || !aligned(ln_b, 16) || !aligned(mod_shift, 16) || !aligned(mod_scale, 16) ||
       !aligned(smooth, 16))
     return fail(WDL_ERR_ARGUMENT, "ln_w, ln_b, mod_shift, mod_scale and smooth must be 16-byte aligned");
+  if (x_out && (ld_xo < K || (ld_xo * 2) % 16 != 0 || !aligned(x_out, 16)))
+    return fail(WDL_ERR_ARGUMENT, "x_out rows must hold K bf16 channels, 16-byte aligned");
   wdl::norm::LnQuantArgs a{};
   a.x = x, a.x_f32 = x_dtype == WDL_F32, a.ldx = ldx, a.M = M, a.K = K, a.eps = eps, a.ln_w = ln_w, a.ln_b = ln_b;
   a.round_ln_bf16 = round_ln_bf16, a.mod_shift = mod_shift, a.mod_scale = mod_scale;
   a.smooth = reinterpret_cast<const __nv_bfloat16*>(smooth), a.scale_dtype = scale_dtype, a.code_format = code_format;
   a.codes = static_cast<uint8_t*>(codes), a.scales = scales;
+  a.x_out = reinterpret_cast<__nv_bfloat16*>(x_out), a.ld_xo = ld_xo;
   wdl::norm::ln_quant_launch(a, static_cast<cudaStream_t>(stream));
   return cuda_status(cudaGetLastError(), "ln_quant launch");
 }

@@ -62,7 +62,7 @@ __device__ __forceinline__ uint32_t code_byte(int q, int fmt) {
                   : (static_cast<uint32_t>(q) & 0xFFu);
 }
 
-template <typename TX>
+template <typename TX, bool kKeep>  // kKeep: also write the bf16 layer input to a.x_out
 __global__ void __launch_bounds__(kRowThreads, 6) ln_quant_kernel(const TX* __restrict__ x, LnQuantArgs a) {
   __shared__ float red[kRowThreads / 32];
   const int t = threadIdx.x, m = blockIdx.x;
@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_quant_kernel(const TX* __re
     const bool valid = k < K;  // uniform over each group of 8 threads
     float y[8];
     if (valid) {
-      float w[8], b[8], sh[8], sc[8], sm[8];
+      float w[8], b[8], sh[8], sc[8], sm[8], xb[8];
       if (a.ln_w) {
         load8<float>(a.ln_w + k, w);
         load8<float>(a.ln_b + k, b);
@@ -115,8 +115,18 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_quant_kernel(const TX* __re
         if (a.round_ln_bf16) u = bf16r(u);
         if (a.mod_shift) u = __fadd_rn(__fmul_rn(u, __fadd_rn(1.f, sc[i])), sh[i]);
         u = bf16r(u);  // the linear layer's input is bf16
+        if constexpr (kKeep) xb[i] = u;
         if (a.smooth) u = __fdiv_rn(u, sm[i]);
         y[i] = u;
+      }
+      if constexpr (kKeep) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __nv_bfloat162 p2 = __floats2bfloat162_rn(xb[2 * i], xb[2 * i + 1]);
+          pk[i] = *reinterpret_cast<const uint32_t*>(&p2);
+        }
+        *reinterpret_cast<uint4*>(a.x_out + static_cast<int64_t>(m) * a.ld_xo + k) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
     } else {
 #pragma unroll
@@ -163,10 +173,14 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_quant_kernel(const TX* __re
 
 void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s) {
   if (a.M == 0) return;
-  if (a.x_f32)
-    ln_quant_kernel<float><<<a.M, kRowThreads, 0, s>>>(static_cast<const float*>(a.x), a);
+  if (a.x_f32 && a.x_out)
+    ln_quant_kernel<float, true><<<a.M, kRowThreads, 0, s>>>(static_cast<const float*>(a.x), a);
+  else if (a.x_f32)
+    ln_quant_kernel<float, false><<<a.M, kRowThreads, 0, s>>>(static_cast<const float*>(a.x), a);
+  else if (a.x_out)
+    ln_quant_kernel<__nv_bfloat16, true><<<a.M, kRowThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a);
   else
-    ln_quant_kernel<__nv_bfloat16><<<a.M, kRowThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a);
+    ln_quant_kernel<__nv_bfloat16, false><<<a.M, kRowThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a);
 }
 
 // Same thread layout as ln_quant: one CTA of 128 threads per row.

@@ -24,6 +24,8 @@ struct LnQuantArgs {
   int code_format;  // 0 int8, 1 e4m3, 2 e4m3 with padded scales, 3 float16 codes
   uint8_t* codes;   // [M, K] (two bytes per code in format 3)
   float* scales;    // [K / 64, M] ([K / 64, M, 4] as (s, 0, 0, 0) for code format 2)
+  __nv_bfloat16* x_out;  // [M, ld_xo]: the layer's bf16 input before smoothing (nullable; a low-rank branch reads it)
+  int64_t ld_xo;
 };
 void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s);
 

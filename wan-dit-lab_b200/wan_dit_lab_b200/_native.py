@@ -46,6 +46,8 @@ SIGNATURES = {
                                   _P, _P, _P, _I, _I, _P]),
     "wdl_w4a4_gemm_gelu_u4": (_I, [_P, _P, _P, _P, _I, _P, _P, ctypes.c_float, _I, _I, _I, _I, _P, _I64, _P, _P]),
     "wdl_ln_quant": (_I, [_P, _I, _I64, _I, _I, ctypes.c_float, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P, _P]),
+    "wdl_ln_quant_keep": (_I, [_P, _I, _I64, _I, _I, ctypes.c_float, _P, _P, _I, _P, _P, _P, _I, _I, _P, _P, _P,
+                               _I64, _P]),
     "wdl_rms_rows": (_I, [_P, _I64, _I, _I, _P, ctypes.c_float, _P, _I64, _P]),
     "wdl_rms_rows_sharded": (_I, [_P, _I64, _I, _I, _P, ctypes.c_float, _P, _I, _P, _I64, _P]),
     "wdl_rows_sumsq": (_I, [_P, _I64, _I, _I, _I, _I64, _P, _P]),

@@ -241,7 +241,8 @@ class Stream:
         self.chunk_freq = self.freq.clone()
         self.cross = model.cross_kvs(context.to(model.device))
         text_tokens = self.cross[0].tokens
-        self.buf = model.blocks[0].buffers(n, max_frames * self.tokens, text_tokens, model.device)
+        self.buf = model.blocks[0].buffers(n, max_frames * self.tokens, text_tokens, model.device,
+                                           lowrank=any(getattr(b, "lowrank", False) for b in model.blocks))
         self.levels = sigmas()
         self.generator = generator
         self.start = 0

@@ -39,7 +39,7 @@ class Buffers:
     model's width (the residual stream). sharded: also the fp32 partial products and RMS statistics that a
     tensor-parallel block sums across shards."""
 
-    def __init__(self, n, dim, ffn_dim, heads, max_keys, text_tokens, device, sharded=False):
+    def __init__(self, n, dim, ffn_dim, heads, max_keys, text_tokens, device, sharded=False, lowrank=False):
         self.n, self.dim, self.ffn = n, dim, ffn_dim
         u8 = dict(dtype=torch.uint8, device=device)
         f32 = dict(dtype=torch.float32, device=device)
@@ -63,6 +63,9 @@ class Buffers:
         if sharded:
             self.partial = torch.empty(n, dim, **f32)  # a row-parallel layer's share of its product
             self.sumsq = torch.empty(n, 2, **f32)  # the shard's share of the q / k RMS statistics
+        if lowrank:  # the inputs of SVDQuant low-rank branches that no other buffer holds
+            self.xin = torch.empty(n, dim, **bf)  # a layer's bf16 input after LayerNorm / modulation
+            self.gelu = torch.empty(n, ffn_dim, **f32)  # GELU's output in the feed forward (before the shift)
 
 
 def quantize_block(p, scale_dtype=torch.bfloat16):
@@ -90,8 +93,9 @@ class CrossKV:
 class WanBlockB200:
     """One Wan block with its weights in the kernels' layouts, made from a WanBlock state dict (the reference's
     parameter names: self_attn.{q,k,v,o}, cross_attn.{q,k,v,o}, ffn.{0,2}, norm3, *.norm_q / norm_k, modulation).
-    Every linear layer is W4A4 (INT4 groups of 64, rank 0 low-rank branch): quantize from float weights, or
-    pass `parts` {layer: quantize() tensors} of a converted pack."""
+    Every linear layer is W4A4 (INT4 groups of 64): quantized here from float weights at rank 0, or given as
+    `parts` {layer: quantize() tensors} of a converted pack, with SVDQuant low-rank branches of any rank and
+    smoothing vectors."""
 
     def __init__(self, state, dim, ffn_dim, heads, eps=1e-6, device="cuda", parts=None, scale_dtype=torch.bfloat16,
                  code_format=None):
@@ -105,9 +109,9 @@ class WanBlockB200:
         self.parts = parts
         self.layers = {name: w4a4.PreparedW4A4(*(t[k] for k in w4a4.PARTS), code_format=code_format)
                        for name, t in parts.items()}
-        if any(layer.rank for layer in self.layers.values()):
-            raise NotImplementedError("the fused block runs rank-0 W4A4 layers; low-rank packs run through "
-                                      "w4a4.PackedW4A4Linear / w4a4.gelu_mlp")
+        # SVDQuant low-rank branches (rank r > 0): their [n, N] products, (x proj_down) proj_up^T in float32,
+        # enter the GEMM epilogues before the bias (wdl_w4a4_gemm_add and relatives)
+        self.lowrank = any(layer.rank for layer in self.layers.values())
         if len({layer.code_format for layer in self.layers.values()}) > 1:
             # a layer could not take the requested format: the block's quantizers feed every layer one format
             self.layers = {name: w4a4.PreparedW4A4(*(t[k] for k in w4a4.PARTS), code_format="e4m3")
@@ -178,25 +182,35 @@ class WanBlockB200:
             e1.record()
             timer(e0, e1, 2 * n * layer.N * layer.K)
 
-        def gemm(layer, out):
-            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm(buf.codes.data_ptr(), buf.scales.data_ptr(), layer.codes.data_ptr(),
-                                            layer.scales.data_ptr(), fmt, _native.ptr(layer.bias), n, layer.N, layer.K,
-                                            out.data_ptr(), out.stride(0), st)))
+        def lora(layer, x):
+            """The layer's low-rank product [n, N] float32 for its bf16 / float32 input x, or None at rank 0."""
+            return layer.lowrank(x[:n]) if layer.rank else None
 
-        def gemm_residual(layer, gate_row, codes=None, scales=None):
+        def gemm(layer, out, add=None):
+            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_add(
+                buf.codes.data_ptr(), buf.scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), fmt,
+                _native.ptr(layer.bias), _native.ptr(add), layer.N, n, layer.N, layer.K, out.data_ptr(), out.stride(0),
+                st)))
+
+        def gemm_residual(layer, gate_row, codes=None, scales=None, add=None):
             c = buf.codes if codes is None else codes
             s = buf.scales if scales is None else scales
-            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_residual(
+            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_residual_add(
                 c.data_ptr(), s.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), fmt,
-                _native.ptr(layer.bias), None if gate_row is None else mod_ptr(gate_row), X.data_ptr(), dim, n, layer.N,
-                layer.K, X.data_ptr(), dim, st)))
+                _native.ptr(layer.bias), _native.ptr(add), layer.N, None if gate_row is None else mod_ptr(gate_row),
+                X.data_ptr(), dim, n, layer.N, layer.K, X.data_ptr(), dim, st)))
 
         def ln_quant(shift_row, scale_row, affine, layer, round_bf16):
-            _native.check(lib.wdl_ln_quant(
+            """Codes and scales of the layer's input; with a low-rank branch also the bf16 input itself (buf.xin),
+            whose product with the branch is returned (else None)."""
+            keep = buf.xin if layer.rank else None
+            _native.check(lib.wdl_ln_quant_keep(
                 X.data_ptr(), _native.F32, dim, n, dim, self.eps, self.norm3_w.data_ptr() if affine else None,
                 self.norm3_b.data_ptr() if affine else None, 1 if round_bf16 else 0,
                 None if shift_row is None else mod_ptr(shift_row), None if scale_row is None else mod_ptr(scale_row),
-                _native.ptr(layer.smooth), sd, fmt, buf.codes.data_ptr(), buf.scales.data_ptr(), st))
+                _native.ptr(layer.smooth), sd, fmt, buf.codes.data_ptr(), buf.scales.data_ptr(), _native.ptr(keep),
+                dim, st))
+            return None if keep is None else lora(layer, keep)
 
         def quantize(x, layer):
             _native.check(lib.wdl_w4a4_quantize_rows(x.data_ptr(), _native.BF16, x.stride(0), _native.ptr(layer.smooth),
@@ -204,8 +218,8 @@ class WanBlockB200:
                                                      None, st))
 
         # self-attention
-        ln_quant(0, 1, False, L["self_attn.qkv"], x_is_bf16)
-        gemm(L["self_attn.qkv"], buf.qkv)
+        add = ln_quant(0, 1, False, L["self_attn.qkv"], x_is_bf16)
+        gemm(L["self_attn.qkv"], buf.qkv, add)
         keep("qkv", buf.qkv)
         _native.check(lib.wdl_qkv_prep(buf.qkv.data_ptr(), 3 * dim, n, dim, self.norm_q.data_ptr(),
                                        self.norm_k.data_ptr(), self.eps, freq.data_ptr(), freq.shape[1], grid[1],
@@ -217,11 +231,11 @@ class WanBlockB200:
             HEAD_DIM ** -0.5, buf.attn.data_ptr(), dim, buf.sage.data_ptr(), buf.sage.numel(), st))
         keep("q", buf.q), keep("k", buf.k), keep("attn", buf.attn)
         quantize(buf.attn, L["self_attn.o"])
-        gemm_residual(L["self_attn.o"], 2)
+        gemm_residual(L["self_attn.o"], 2, add=lora(L["self_attn.o"], buf.attn))
         keep("x_after_self", X)
         # cross-attention
-        ln_quant(None, None, True, L["cross_attn.q"], x_is_bf16)
-        gemm(L["cross_attn.q"], buf.cq)
+        add = ln_quant(None, None, True, L["cross_attn.q"], x_is_bf16)
+        gemm(L["cross_attn.q"], buf.cq, add)
         keep("cq", buf.cq)
         _native.check(lib.wdl_rms_rows(buf.cq.data_ptr(), dim, n, dim, self.cross_norm_q.data_ptr(), self.eps,
                                        buf.q.data_ptr(), dim, st))
@@ -231,15 +245,16 @@ class WanBlockB200:
                                              n, cross.tokens, H, HEAD_DIM ** -0.5, buf.attn.data_ptr(), dim, st))
         keep("cattn", buf.attn)
         quantize(buf.attn, L["cross_attn.o"])
-        gemm_residual(L["cross_attn.o"], None)
+        gemm_residual(L["cross_attn.o"], None, add=lora(L["cross_attn.o"], buf.attn))
         keep("x_after_cross", X)
         # feed forward
         fc1, fc2 = L["ffn.0"], L["ffn.2"]
-        ln_quant(3, 4, False, fc1, x_is_bf16)
-        timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4(
+        add = ln_quant(3, 4, False, fc1, x_is_bf16)
+        gelu = buf.gelu if fc2.rank else None  # the second layer's branch reads GELU's output without the shift
+        timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4_add(
             buf.codes.data_ptr(), buf.scales.data_ptr(), fc1.codes.data_ptr(), fc1.scales.data_ptr(), fmt,
-            _native.ptr(fc1.bias), _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N, fc1.K, buf.hcodes.data_ptr(),
-            fc1.N, buf.hscales.data_ptr(), st)))
+            _native.ptr(fc1.bias), _native.ptr(add), fc1.N, _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N,
+            fc1.K, buf.hcodes.data_ptr(), fc1.N, buf.hscales.data_ptr(), _native.ptr(gelu), fc1.N, st)))
         if trace is not None:  # the hidden codes [n, ffn] as float values, whatever their operand format
             raw = buf.hcodes.view(-1)
             if fmt == _native.CODES_F16_FOLD:
@@ -250,12 +265,14 @@ class WanBlockB200:
             G = buf.hscales.shape[0]
             keep("hscales", buf.hscales[..., 0] if fmt == _native.CODES_E4M3_TS
                  else buf.hscales.view(-1)[:G * n].view(G, n))
-        gemm_residual(fc2, 5, buf.hcodes, buf.hscales)
+        gemm_residual(fc2, 5, buf.hcodes, buf.hscales, add=None if gelu is None else lora(fc2, gelu))
         return X
 
-    def buffers(self, n, max_keys, text_tokens, device):
-        """Scratch for chunks of n tokens attending to up to max_keys keys."""
-        return Buffers(n, self.dim, self.ffn_dim, self.kv_heads, max_keys, text_tokens, device)
+    def buffers(self, n, max_keys, text_tokens, device, lowrank=None):
+        """Scratch for chunks of n tokens attending to up to max_keys keys (lowrank: with the inputs of low-rank
+        branches; default: whether this block has any)."""
+        return Buffers(n, self.dim, self.ffn_dim, self.kv_heads, max_keys, text_tokens, device,
+                       lowrank=self.lowrank if lowrank is None else lowrank)
 
     def modulation_of(self, time_in):
         """time_in [6, dim] float32 + this block's modulation (models/block.py:75)."""

@@ -147,7 +147,7 @@ class WanBlockTP:
         self.modulation = _f32(p["modulation"]).reshape(6, dim)
         self.act_scale_dtype = _native.BF16
 
-    def buffers(self, n, max_keys, text_tokens, device):
+    def buffers(self, n, max_keys, text_tokens, device, lowrank=False):
         return Buffers(n, self.dim, self.local_ffn, self.kv_heads, max_keys, text_tokens, device, sharded=True)
 
     def modulation_of(self, time_in):
