@@ -50,6 +50,16 @@ extern "C" {
  * format the GEMM's w_scales argument points to the single float 2^F, activation scales are [K/64, M] f32 as in
  * WDL_CODES_E4M3, N % 256 == 0, K % 64 == 0, and the group-partials view is not available. */
 #define WDL_CODES_F16_FOLD 3
+/* WDL_CODES_F16_PRE: float16 activations with their bf16 group scales folded in as well, float16(code * sx *
+ * 2^-E_m) with one power of two per row m (8 times the row's largest |value| in [2^14, 2^15)), and the rows'
+ * 2^E_m [M] float32 as the activation "scales"; weights as WDL_CODES_F16_FOLD (the same folded buffers). Both
+ * operands then carry every scale: the GEMM accumulates all of K on the tensor cores (no per-group promotion) and
+ * multiplies each row by 2^E_m 2^F once. Exact operands (a code has <= 3 significant bits, a bf16 scale 8; a group
+ * whose scale is below 2^-25 of its row's largest rounds to float16 subnormals); the sum is the tensor core's
+ * float32 accumulation, within float32 rounding of the per-group promotion (not bit-identical to it). Written by
+ * wdl_w4a4_quantize_rows / wdl_ln_quant (bf16 scales only); signed codes only: the GELU epilogue of a GEMM in
+ * this format writes the (unsigned) hidden layer in WDL_CODES_F16_FOLD. */
+#define WDL_CODES_F16_PRE 4
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* wdl_last_error(void);

@@ -35,14 +35,19 @@ def numpy_parts(parts):
             for k, t in parts.items()}
 
 
+# The bar on the block's update: 2e-2 for the folded format, whose GEMM sums every group's exact product in the
+# oracle's order; 4e-2 for the prescaled one, whose tensor cores sum all of K in their own float32 order: a few
+# bf16 outputs round the other way, and the INT8 K / FP8 P / INT4 hidden requantizations downstream carry those
+# steps across their own rounding boundaries (each linear stays within 2e-3 of the oracle, test_w4a4_pre_gpu).
+@pytest.mark.parametrize("code_format,bar", [("f16fold", 2e-2), ("f16pre", 4e-2)])
 @pytest.mark.parametrize("dim,heads,ffn,frames,h,w,at,text", [(1024, 8, 4096, 2, 4, 8, 128, 32),
                                                                (2048, 16, 4096, 3, 4, 16, 384, 64)])
-def test_block_matches_oracle(dim, heads, ffn, frames, h, w, at, text):
+def test_block_matches_oracle(dim, heads, ffn, frames, h, w, at, text, code_format, bar):
     from wan_dit_lab_b200.models.block import Buffers, WanBlockB200
     from wan_dit_lab_b200 import _native
     n = frames * h * w
     state = random_state(dim, ffn, 1)
-    blk = WanBlockB200(state, dim, ffn, heads)
+    blk = WanBlockB200(state, dim, ffn, heads, code_format=code_format)
     g = torch.Generator().manual_seed(2)
     X = torch.randn(n, dim, generator=g)
     time_in = torch.randn(6, dim, generator=g) * 0.1
@@ -78,8 +83,8 @@ def test_block_matches_oracle(dim, heads, ffn, frames, h, w, at, text):
     print("stages:", {k: round(v, 5) for k, v in stages.items()})
     d_got, d_exp = got - X.numpy(), expected - X.numpy()
     err = float(np.linalg.norm(d_got - d_exp) / np.linalg.norm(d_exp))
-    print(f"block dim {dim}: residual update relative L2 vs oracle {err:.4f}")
-    assert err <= 2e-2
+    print(f"block dim {dim} ({code_format}): residual update relative L2 vs oracle {err:.4f}")
+    assert err <= bar
     for name, gpu in (("k", cache[0]), ("v", cache[2])):
         rows = gpu[at:at + n].cpu().numpy()
         assert (rows == ocache[name][0, at:at + n]).mean() > 0.99

@@ -1,0 +1,172 @@
+"""The prescaled float16 code format (WDL_CODES_F16_PRE): activations float16(code * stored scale * 2^-E_m), one
+power of two per row, weights folded as in WDL_CODES_F16_FOLD; the GEMM accumulates all of K on the tensor cores.
+The quantizers' values are exact (equal bit for bit to the folded format's codes times its scales, rescaled);
+the GEMM equals the per-group promotion of the folded format within float32 rounding (bf16 outputs >= 99.9 %
+bit-equal, relative L2 <= 2e-4: one bf16 step where the two float32 sums straddle a rounding boundary; the
+float32 partial products within 1e-6), in every epilogue; the W4A4 linear stays within 2e-3 of the oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import w4a4 as ow
+
+pytestmark = pytest.mark.gpu
+
+
+def native():
+    from wan_dit_lab_b200 import _native
+    return _native
+
+
+def seeded(shape, seed, scale=1.0, outliers=0.0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(*shape, generator=g) * scale
+    if outliers:
+        cols = torch.randperm(shape[-1], generator=g)[: max(1, int(outliers * shape[-1]))]
+        x[..., cols] *= 20
+    return x
+
+
+def rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def expected_prescaled(codes, scales, rows_scale):
+    """float16(code * stored scale / 2^E_m) from the folded format's codes [M, K] and scales [K/64, M]."""
+    per_col = scales.t().repeat_interleave(64, dim=1)  # [M, K]
+    return (codes.float() * per_col / rows_scale[:, None]).half()
+
+
+@pytest.mark.parametrize("M,K,smooth,dtype", [(300, 1024, False, torch.bfloat16), (129, 3072, True, torch.bfloat16),
+                                              (37, 256, False, torch.float32)])
+def test_quantize_rows_prescaled_values_exact(M, K, smooth, dtype):
+    from wan_dit_lab_b200.quantization import w4a4
+    x = seeded((M, K), 1, outliers=0.01).to(dtype).cuda()
+    s = (seeded((K,), 2).abs() + 0.5).to(torch.bfloat16).cuda() if smooth else None
+    c3, s3 = w4a4.quantize_rows(x, torch.bfloat16, smooth=s, code_format="f16fold")
+    pre, rs = w4a4.quantize_rows(x, torch.bfloat16, smooth=s, code_format="f16pre")
+    assert rs.shape == (M,)
+    mant, _ = torch.frexp(rs)
+    assert bool((mant == 0.5).all())  # powers of two
+    top = s3.max(dim=0).values * 8 / rs  # 8 x the row's largest scale, rescaled: in [2^14, 2^15)
+    assert bool(((top >= 2 ** 14) & (top < 2 ** 15)).all())
+    want = expected_prescaled(c3, s3, rs)
+    assert torch.equal(pre.view(torch.int16), want.view(torch.int16))
+
+
+def test_ln_quant_prescaled_values_exact():
+    _native = native()
+    lib, st = _native.lib(), _native.stream()
+    M, K = 200, 3072
+    g = torch.Generator().manual_seed(3)
+    X = torch.randn(M, K, generator=g).cuda()
+    shift, scale = (torch.randn(K, generator=g) * 0.1).cuda(), (torch.randn(K, generator=g) * 0.1).cuda()
+    smooth = (torch.rand(K, generator=g) + 0.5).to(torch.bfloat16).cuda()
+    out = {}
+    for fmt, shape in ((3, (K // 64, M)), (4, (M,))):
+        codes = torch.empty(M, K, dtype=torch.float16, device="cuda")
+        sc = torch.empty(shape, device="cuda")
+        _native.check(lib.wdl_ln_quant(X.data_ptr(), _native.F32, K, M, K, 1e-6, None, None, 0, shift.data_ptr(),
+                                       scale.data_ptr(), smooth.data_ptr(), _native.BF16, fmt, codes.data_ptr(),
+                                       sc.data_ptr(), st))
+        out[fmt] = (codes, sc)
+    want = expected_prescaled(out[3][0], out[3][1], out[4][1])
+    assert torch.equal(out[4][0].view(torch.int16), want.view(torch.int16))
+
+
+def prepared(N, K, seed):
+    from wan_dit_lab_b200.quantization import w4a4
+    W = seeded((N, K), seed, scale=0.02)
+    b = seeded((N,), seed + 1, scale=0.1)
+    parts = w4a4.quantize(W.cuda(), b.cuda(), rank=0)
+    return (W, b, parts, w4a4.PreparedW4A4(*(parts[p] for p in w4a4.PARTS), code_format="f16fold"),
+            w4a4.PreparedW4A4(*(parts[p] for p in w4a4.PARTS), code_format="f16pre"))
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 768, 1024), (1392, 3072, 3072), (64, 384, 512)])
+def test_gemm_prescaled_matches_folded_in_every_epilogue(M, N, K):
+    from wan_dit_lab_b200.quantization import w4a4
+    _native = native()
+    lib, st = _native.lib(), _native.stream()
+    x = seeded((M, K), 4, outliers=0.01).to(torch.bfloat16).cuda()
+    _, _, _, fold, pre = prepared(N, K, 5)
+    assert fold.code_format == 3 and pre.code_format == 4
+    c3, s3 = w4a4.quantize_rows(x, torch.bfloat16, code_format="f16fold")
+    c4, s4 = w4a4.quantize_rows(x, torch.bfloat16, code_format="f16pre")
+    ops = {3: (c3, s3, fold), 4: (c4, s4, pre)}
+    res = seeded((M, N), 6).cuda()
+    gate = seeded((N,), 7).cuda()
+    outs = {}
+    for f, (c, s, L) in ops.items():
+        y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        _native.check(lib.wdl_w4a4_gemm(c.data_ptr(), s.data_ptr(), L.codes.data_ptr(), L.scales.data_ptr(), f,
+                                        L.bias.data_ptr(), M, N, K, y.data_ptr(), N, st))
+        r = res.clone()
+        _native.check(lib.wdl_w4a4_gemm_residual(c.data_ptr(), s.data_ptr(), L.codes.data_ptr(), L.scales.data_ptr(),
+                                                 f, L.bias.data_ptr(), gate.data_ptr(), r.data_ptr(), N, M, N, K,
+                                                 r.data_ptr(), N, st))
+        p = torch.empty(M, N, device="cuda")
+        _native.check(lib.wdl_w4a4_gemm_f32(c.data_ptr(), s.data_ptr(), L.codes.data_ptr(), L.scales.data_ptr(), f,
+                                            None, None, 0, M, N, K, p.data_ptr(), N, st))
+        hc = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        hs = torch.empty(N // 64, M, device="cuda")
+        _native.check(lib.wdl_w4a4_gemm_gelu_u4(c.data_ptr(), s.data_ptr(), L.codes.data_ptr(), L.scales.data_ptr(),
+                                                f, L.bias.data_ptr(), None, 0.171875, _native.BF16, M, N, K,
+                                                hc.data_ptr(), N, hs.data_ptr(), st))
+        outs[f] = (y, r, p, hc, hs)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    (y3, r3, p3, hc3, hs3), (y4, r4, p4, hc4, hs4) = outs[3], outs[4]
+    assert rel(p4.cpu(), p3.cpu()) <= 1e-6
+    # bf16 outputs: where the two float32 sums straddle a bf16 rounding boundary, one bf16 step apart
+    assert rel(y4.float().cpu(), y3.float().cpu()) <= 2e-4 and (y4 == y3).float().mean().item() >= 0.999
+    assert rel(r4.cpu(), r3.cpu()) <= 2e-4 and (r4 == r3).float().mean().item() >= 0.999
+    assert (hc4 == hc3).float().mean().item() >= 0.999 and rel(hs4.cpu(), hs3.cpu()) <= 2e-4
+
+
+def test_linear_prescaled_against_oracle():
+    """BASELINE config 1's shapes with bf16 scales (the prescaled format's own): within 2e-3 of the oracle."""
+    M, K, N = 1392, 3072, 9216
+    x = seeded((M, K), 0, outliers=0.01).to(torch.bfloat16)
+    W, _, parts, _, pre = prepared(N, K, 1)
+    assert pre.code_format == 4
+    y = pre(x.cuda()).float().cpu().numpy()
+    o_codes = ow.unpack_nibbles(parts["qweight"].cpu().numpy())
+    expected, _, _ = ow.linear(x.float().numpy(), o_codes, parts["wscales"].float().cpu().numpy(),
+                               parts["bias"].float().cpu().numpy())
+    assert rel(y, expected) <= 2e-3
+    assert native().device_error() == 0
+
+
+def test_block_prescaled_matches_folded_block():
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from test_block_gpu import random_state
+    from oracle import fp8 as of
+    from oracle import rope as orope
+    from wan_dit_lab_b200.models.block import Buffers, WanBlockB200
+    dim, heads, ffn, frames, h, w, at, text = 1024, 8, 4096, 2, 4, 8, 128, 32
+    n = frames * h * w
+    state = random_state(dim, ffn, 9)
+    g = torch.Generator().manual_seed(10)
+    X = torch.randn(n, dim, generator=g)
+    time_in = torch.randn(6, dim, generator=g) * 0.1
+    ctx = torch.randn(text, dim, generator=g).to(torch.bfloat16)
+    cap = at + n + 16
+    ck8, cks = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    cv8, cvs = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    freq = torch.from_numpy(orope.table(1024).astype(np.float32)).cuda()
+    outs = {}
+    for fmt in ("f16fold", "f16pre"):
+        blk = WanBlockB200(state, dim, ffn, heads, code_format=fmt)
+        cache = (torch.from_numpy(ck8[0]).cuda(), torch.from_numpy(cks[0, ..., 0]).cuda(),
+                 torch.from_numpy(cv8[0]).cuda(), torch.from_numpy(cvs[0, ..., 0]).cuda(), cap)
+        Xd = X.cuda()
+        blk.forward(Xd, blk.modulation_of(time_in.cuda()), cache, at, freq, (frames, h, w), at // (h * w),
+                    blk.cross_kv(ctx.cuda()), Buffers(n, dim, ffn, heads, at + n, text, "cuda"))
+        outs[fmt] = Xd.cpu() - X
+    assert native().device_error() == 0
+    assert rel(outs["f16pre"].numpy(), outs["f16fold"].numpy()) <= 1e-3

@@ -118,11 +118,13 @@ int wdl_device_error(void* stream, uint32_t* code) {
 }
 
 static bool valid_codes(int f) {
-  return f == WDL_CODES_INT8 || f == WDL_CODES_E4M3 || f == WDL_CODES_E4M3_TS || f == WDL_CODES_F16_FOLD;
+  return f == WDL_CODES_INT8 || f == WDL_CODES_E4M3 || f == WDL_CODES_E4M3_TS || f == WDL_CODES_F16_FOLD ||
+         f == WDL_CODES_F16_PRE;
 }
 
 // Bytes of one code in a code format's operand (float16 codes of the folded format take two).
-static int code_bytes(int f) { return f == WDL_CODES_F16_FOLD ? 2 : 1; }
+static int code_bytes(int f) { return f == WDL_CODES_F16_FOLD || f == WDL_CODES_F16_PRE ? 2 : 1; }
+static bool folded(int f) { return f == WDL_CODES_F16_FOLD || f == WDL_CODES_F16_PRE; }
 
 // Scale arrays of the padded format hold 16-byte entries read by TMA.
 static bool scales_aligned(const void* p, int code_format) { return aligned(p, code_format == WDL_CODES_E4M3_TS ? 16 : 4); }
@@ -135,6 +137,8 @@ int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16
   if (x_dtype != WDL_BF16 && x_dtype != WDL_F32) return fail(WDL_ERR_ARGUMENT, "x must be bf16 or f32");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
   if (ldx < K) return fail(WDL_ERR_ARGUMENT, "ldx (%lld) < K (%d)", static_cast<long long>(ldx), K);
+  if (code_format == WDL_CODES_F16_PRE && (scale_dtype != WDL_BF16 || packed))
+    return fail(WDL_ERR_ARGUMENT, "the prescaled format takes bf16 scales (exact products) and no packed copy");
   const int64_t esize = x_dtype == WDL_F32 ? 4 : 2;
   if (M == 0) return ok();
   if (!x || !codes || !scales) return fail(WDL_ERR_ARGUMENT, "x, codes and scales must not be null");
@@ -150,8 +154,7 @@ int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16
 int wdl_w4a4_unpack_weight(const uint8_t* qweight, const void* wscales, int scale_dtype, int N, int K,
                            int code_format, void* codes, float* scales, void* stream) {
   if (!valid_codes(code_format)) return fail(WDL_ERR_ARGUMENT, "unknown code format %d", code_format);
-  if (code_format == WDL_CODES_F16_FOLD)
-    return fail(WDL_ERR_ARGUMENT, "folded weights are made by wdl_w4a4_fold_weight");
+  if (folded(code_format)) return fail(WDL_ERR_ARGUMENT, "folded weights are made by wdl_w4a4_fold_weight");
   if (N <= 0 || K <= 0 || K % 64 != 0) return fail(WDL_ERR_ARGUMENT, "N > 0 and K a positive multiple of 64 required");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
   if (!qweight || !wscales || !codes || !scales) return fail(WDL_ERR_ARGUMENT, "null pointer");
@@ -184,15 +187,15 @@ static int gemm_common(wdl::w4a4::GemmArgs& a, void* stream) {
     return fail(WDL_ERR_ARGUMENT, "output and residual must be 16-byte aligned");
   const int f = a.code_format;
   const char* why = "";
-  const int v = f == WDL_CODES_E4M3_TS    ? wdl::w4a4::gemm_ts_validate(a, &why)
-                : f == WDL_CODES_F16_FOLD ? wdl::w4a4::gemm_fold_validate(a, &why)
+  const int v = f == WDL_CODES_E4M3_TS ? wdl::w4a4::gemm_ts_validate(a, &why)
+                : folded(f)             ? wdl::w4a4::gemm_fold_validate(a, &why)
                                           : wdl::w4a4::gemm_validate(a, &why);
   if (v != 0) return fail(WDL_ERR_ARGUMENT, "%s", why);
   a.err = error_word();
   if (!a.err) return fail(WDL_ERR_CUDA, "cannot resolve the device error word");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int st = f == WDL_CODES_E4M3_TS    ? wdl::w4a4::gemm_ts_launch(a, s, &why)
-                 : f == WDL_CODES_F16_FOLD ? wdl::w4a4::gemm_fold_launch(a, s, &why)
+  const int st = f == WDL_CODES_E4M3_TS ? wdl::w4a4::gemm_ts_launch(a, s, &why)
+                 : folded(f)             ? wdl::w4a4::gemm_fold_launch(a, s, &why)
                                            : wdl::w4a4::gemm_launch(a, s, &why);
   if (st == 1) return fail(WDL_ERR_ARGUMENT, "%s", why);
   if (st != 0) return fail(WDL_ERR_CUDA, "%s", why);
@@ -444,8 +447,9 @@ int wdl_ln_quant_keep(const void* x, int x_dtype, int64_t ldx, int M, int K, flo
   if ((ldx * (x_dtype == WDL_F32 ? 4 : 2)) % 16 != 0 || !aligned(x, 16)) return fail(WDL_ERR_ARGUMENT, "x rows must be 16-byte aligned");
   if ((ln_w == nullptr) != (ln_b == nullptr) || (mod_shift == nullptr) != (mod_scale == nullptr))
     return fail(WDL_ERR_ARGUMENT, "affine weight / bias and modulation shift / scale come in pairs");
-  if (!valid_codes(code_format) || (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16))
-    return fail(WDL_ERR_ARGUMENT, "invalid code format or scale dtype");
+  if (!valid_codes(code_format) || (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) ||
+      (code_format == WDL_CODES_F16_PRE && scale_dtype != WDL_BF16))
+    return fail(WDL_ERR_ARGUMENT, "invalid code format or scale dtype (the prescaled format takes bf16 scales)");
   if (M == 0) return ok();
   if (!codes || !scales || !aligned(codes, 8 * code_bytes(code_format)) || !scales_aligned(scales, code_format))
     return fail(WDL_ERR_ARGUMENT, "null or misaligned output");

@@ -11,6 +11,7 @@
 //    the float32 weight; the query norm of cross-attention (models/multi_head_attention.py:118).
 //  * modulation — (time_in + modulation) of every block at once (models/block.py:75): [blocks, 6, dim] fp32.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "norm_quant.h"
@@ -62,8 +63,11 @@ __device__ __forceinline__ uint32_t code_byte(int q, int fmt) {
                   : (static_cast<uint32_t>(q) & 0xFFu);
 }
 
-template <typename TX, bool kKeep>  // kKeep: also write the bf16 layer input to a.x_out
-__global__ void __launch_bounds__(kRowThreads, 6) ln_quant_kernel(const TX* __restrict__ x, LnQuantArgs a) {
+// kKeep: also write the bf16 layer input to a.x_out. kPre: code format 4, the prescaled float16 activations
+// float16(code * stored scale * 2^-E_m) with the row's 2^E_m in a.scales[m] (E_m from the row's largest stored
+// scale, as quantize_rows_pre_kernel: w4a4_quant.cu); the codes and scales are those of the other formats.
+template <typename TX, bool kKeep, bool kPre>
+__global__ void __launch_bounds__(kRowThreads, kPre ? 4 : 6) ln_quant_kernel(const TX* __restrict__ x, LnQuantArgs a) {
   __shared__ float red[kRowThreads / 32];
   const int t = threadIdx.x, m = blockIdx.x;
   const int K = a.K;
@@ -91,6 +95,7 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_quant_kernel(const TX* __re
       }
   const float rstd = __frsqrt_rn(__fadd_rn(__fdiv_rn(block_sum128(ss, red), static_cast<float>(K)), a.eps));
   uint8_t* codes = a.codes + static_cast<int64_t>(m) * K;
+  float pre_scale[kRowChunks], pre_stored[kRowChunks];  // kPre: each chunk's group scale and stored scale
 #pragma unroll
   for (int c = 0; c < kRowChunks; ++c) {
     if (c * 1024 >= K) break;  // uniform over the CTA
@@ -138,6 +143,13 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_quant_kernel(const TX* __re
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+    if constexpr (kPre) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[c][i] = y[i];  // kept for the second pass
+      pre_scale[c] = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
+      pre_stored[c] = valid ? bf16r(pre_scale[c]) : 0.f;
+      continue;
+    }
     if (!valid) continue;
     const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
     const float r = __frcp_rn(scale);
@@ -169,18 +181,59 @@ __global__ void __launch_bounds__(kRowThreads, 6) ln_quant_kernel(const TX* __re
         a.scales[i] = stored;
     }
   }
+  if constexpr (kPre) {
+    float top = 0.f;
+#pragma unroll
+    for (int c = 0; c < kRowChunks; ++c)
+      if (c * 1024 < K) top = fmaxf(top, pre_stored[c]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
+    __syncthreads();
+    if ((t & 31) == 0) red[t >> 5] = top;
+    __syncthreads();
+    top = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const uint32_t e = (__float_as_uint(top) >> 23) & 0xFFu;  // 8 top 2^(138-e) in [2^14, 2^15)
+    const float down = __uint_as_float((265u - e) << 23);
+    if (t == 0) a.scales[m] = __uint_as_float((e - 11u) << 23);  // 2^(e - 138)
+    uint16_t* out = reinterpret_cast<uint16_t*>(a.codes) + static_cast<int64_t>(m) * K;
+#pragma unroll
+    for (int c = 0; c < kRowChunks; ++c) {
+      const int k = c * 1024 + t * 8;
+      if (k >= K) continue;
+      const float scale = pre_scale[c], stored = pre_stored[c];
+      const float r = __frcp_rn(scale);
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const int q0 = max(-8, min(7, __float2int_rn(div_rn_by(v[c][i], scale, r))));
+        const int q1 = max(-8, min(7, __float2int_rn(div_rn_by(v[c][i + 1], scale, r))));
+        const __half2 h = __floats2half2_rn(__fmul_rn(static_cast<float>(q0) * stored, down),
+                                            __fmul_rn(static_cast<float>(q1) * stored, down));
+        w[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(out + k) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
 }
 
 void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s) {
   if (a.M == 0) return;
-  if (a.x_f32 && a.x_out)
-    ln_quant_kernel<float, true><<<a.M, kRowThreads, 0, s>>>(static_cast<const float*>(a.x), a);
-  else if (a.x_f32)
-    ln_quant_kernel<float, false><<<a.M, kRowThreads, 0, s>>>(static_cast<const float*>(a.x), a);
-  else if (a.x_out)
-    ln_quant_kernel<__nv_bfloat16, true><<<a.M, kRowThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a);
-  else
-    ln_quant_kernel<__nv_bfloat16, false><<<a.M, kRowThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(a.x), a);
+  auto go = [&](auto xt, auto keep, auto pre) {
+    using TX = decltype(xt);
+    ln_quant_kernel<TX, decltype(keep)::value, decltype(pre)::value>
+        <<<a.M, kRowThreads, 0, s>>>(static_cast<const TX*>(a.x), a);
+  };
+  using T_ = std::true_type;
+  using F_ = std::false_type;
+  const bool pre = a.code_format == 4, keep = a.x_out != nullptr;
+  if (a.x_f32) {
+    if (pre) keep ? go(float{}, T_{}, T_{}) : go(float{}, F_{}, T_{});
+    else keep ? go(float{}, T_{}, F_{}) : go(float{}, F_{}, F_{});
+  } else {
+    const __nv_bfloat16 b{};
+    if (pre) keep ? go(b, T_{}, T_{}) : go(b, F_{}, T_{});
+    else keep ? go(b, T_{}, F_{}) : go(b, F_{}, F_{});
+  }
 }
 
 // Same thread layout as ln_quant: one CTA of 128 threads per row.

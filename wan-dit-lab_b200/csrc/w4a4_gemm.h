@@ -24,6 +24,10 @@ enum CodeFormat : int {
                      // GEMM (w4a4_gemm_ts.cu), scales [K / 64, rows, 4]
   kCodesF16Fold = 3,  // float16 operands: activation codes, weights folded with their bf16 group scales and one
                       // power of two 2^-F (w4a4_gemm_fold.cu); the weight "scales" argument is the float 2^F
+  kCodesF16Pre = 4,   // float16 activations with their bf16 group scales folded in too: code * sx * 2^-E_m, one
+                      // power of two per row (exact: a code has <= 3 significant bits, sx 8); the activation
+                      // "scales" are the rows' 2^E_m [M]; weights as kCodesF16Fold. The GEMM accumulates all of K
+                      // in TMEM (no per-group promotion); GELU epilogues write the hidden layer in kCodesF16Fold.
 };
 
 enum EpilogueMode : int {

@@ -51,7 +51,126 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// The end of a tile for one epilogue thread: row m_tile * BM + 32 q + lane of the 128 columns n_tile * BN + 128 h
+// .. + 127 in acc (the finished fp32 products): the low-rank addend, then the mode's epilogue. tw: this warp's
+// 32 x 33 floats of shared-memory scratch (residual mode).
 template <int kMode>
+__device__ __forceinline__ void finish_tile(float (&acc)[128], const GemmEpilogue& ep, float* tw, int M, int N,
+                                            int m_tile, int n_tile, int q, int h, int lane, bool ok) {
+  const int row = q * 32 + lane;
+  const int m = m_tile * BM + row;
+  const bool row_ok = m < M;
+  // N % 128 == 0: the last column tile may hold only its first half (the TMA zero-fills the missing weight rows)
+  const bool col_ok = n_tile * BN + h * 128 < N;
+  if (ok && row_ok && col_ok) add_addend<128>(ep, m, n_tile * BN + h * 128, acc);
+
+  if constexpr (kMode == kEpiResidualF32) {
+    // Residual update through a per-warp 32 x 32 transpose in shared memory (the pipeline buffers, idle once every
+    // MMA has completed): lane l then owns column l of a 32-column block and the warp reads and writes whole rows
+    // (128 contiguous bytes) instead of 32 rows at once, all 32 rows' loads in flight together; bias and gate are
+    // loaded once per column. Same arithmetic per element as a thread-per-row update.
+    const int m0 = m_tile * BM + q * 32;
+#pragma unroll
+    for (int blk = 0; blk < 4; ++blk) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = acc[blk * 32 + j];
+      __syncwarp();
+      const int n = n_tile * BN + h * 128 + blk * 32 + lane;
+      const float bn = ep.bias && col_ok ? __ldg(ep.bias + n) : 0.f;
+      if (ok && col_ok && !ep.residual) {
+        // a partial product in fp32 (a shard's share of a row-parallel layer, summed across shards before the
+        // bias, rounding and residual update): out = acc (+ bias), no rounding
+        float* out = reinterpret_cast<float*>(ep.out) + n;
+#pragma unroll
+        for (int r = 0; r < 32; ++r)
+          if (m0 + r < M) out[static_cast<size_t>(m0 + r) * ep.ld_out] = tw[r * 33 + lane] + bn;
+      } else if (ok && col_ok) {
+        {
+          // residual stream update in fp32: x_new = x + float(bf16(acc + bias)) * gate   (gate 1 when absent)
+          const float gn = ep.gate ? __ldg(ep.gate + n) : 0.f;
+          float* out = reinterpret_cast<float*>(ep.out) + n;
+          const float* res = ep.residual + n;
+          float x[32];  // all 32 rows' residuals in flight at once
+#pragma unroll
+          for (int r = 0; r < 32; ++r) x[r] = m0 + r < M ? res[static_cast<size_t>(m0 + r) * ep.ld_res] : 0.f;
+#pragma unroll
+          for (int r = 0; r < 32; ++r) {
+            const float o = bf16_round(tw[r * 33 + lane] + bn);
+            if (m0 + r < M)
+              out[static_cast<size_t>(m0 + r) * ep.ld_out] = ep.gate ? __fadd_rn(x[r], __fmul_rn(o, gn)) : __fadd_rn(x[r], o);
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+  if (ok && row_ok && col_ok) {
+    const int n0 = n_tile * BN + h * 128;
+    if constexpr (kMode == kEpiBf16) {
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
+#pragma unroll
+      for (int j = 0; j < 128; j += 8) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = acc[j + i] + (ep.bias ? __ldg(ep.bias + n0 + j + i) : 0.f);
+        uint4 pk;
+        __nv_bfloat162 t0 = __floats2bfloat162_rn(v[0], v[1]), t1 = __floats2bfloat162_rn(v[2], v[3]);
+        __nv_bfloat162 t2 = __floats2bfloat162_rn(v[4], v[5]), t3 = __floats2bfloat162_rn(v[6], v[7]);
+        pk.x = *reinterpret_cast<uint32_t*>(&t0);
+        pk.y = *reinterpret_cast<uint32_t*>(&t1);
+        pk.z = *reinterpret_cast<uint32_t*>(&t2);
+        pk.w = *reinterpret_cast<uint32_t*>(&t3);
+        *reinterpret_cast<uint4*>(out + j) = pk;
+      }
+    } else if constexpr (kMode == kEpiGeluU4) {
+      // the fused MLP's hidden layer (reference quantization/w4a4.py:195-204, native/ops/w4a4_ops.cpp:44-63):
+      // u = GELU(acc + bias) + shift, divided by the next layer's smoothing, quantized unsigned per group of 64
+      // columns: scale = max(max u, 1e-8) / 15, code = round-half-even(u / scale) clamped to [0, 15], stored as
+      // the next layer's float16 operand (exact integers) with the scale [N / 64, M] rounded to its dtype.
+      uint16_t* codes = reinterpret_cast<uint16_t*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
+#pragma unroll
+      for (int g2 = 0; g2 < 2; ++g2) {
+        float amax = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          const int n = n0 + g2 * 64 + j;
+          const float gv = gelu_tanh(acc[g2 * 64 + j] + (ep.bias ? __ldg(ep.bias + n) : 0.f));
+          if (ep.gelu_out) ep.gelu_out[static_cast<size_t>(m) * ep.ld_gelu + n] = gv;
+          float t = __fadd_rn(gv, ep.gelu_shift);
+          if (ep.out_smooth) t = __fdiv_rn(t, __bfloat162float(ep.out_smooth[n]));
+          acc[g2 * 64 + j] = t;
+          amax = fmaxf(amax, fabsf(t));
+        }
+        const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 15.f);
+        const float rcp = __frcp_rn(scale);
+#pragma unroll
+        for (int j = 0; j < 64; j += 8) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            // clamp to [0, 15], then round half to even by adding and subtracting 1.5 2^23 (exact below 2^22):
+            // the codes of rint-then-clamp, without a conversion instruction; two per float16 pack
+            float r2[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const float d = fminf(fmaxf(div_rn_by(acc[g2 * 64 + j + 2 * e + t], scale, rcp), 0.f), 15.f);
+              r2[t] = __fsub_rn(__fadd_rn(d, 12582912.f), 12582912.f);
+            }
+            const __half2 hp = __floats2half2_rn(r2[0], r2[1]);
+            w[e] = *reinterpret_cast<const uint32_t*>(&hp);
+          }
+          *reinterpret_cast<uint4*>(codes + g2 * 64 + j) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        ep.out_scales[static_cast<size_t>((n0 + g2 * 64) / 64) * M + m] =
+            ep.out_scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16_round(scale);
+      }
+    }
+  }
+}
+
+// kPre: activations in the prescaled format (kCodesF16Pre): every group's products carry both scales, so the MMA
+// accumulates all of K into one TMEM buffer and the epilogue multiplies each row by 2^(E_m + F) once.
+template <int kMode, bool kPre>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_fold_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      const float* __restrict__ fold_scale, GemmEpilogue ep, int M, int N, int K, uint32_t* err) {
@@ -109,22 +228,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = make_idesc(1, 0, 0, BM, BN);  // f16 x f16 -> f32
       bool ok = true;
       for (int g = 0; g < G && ok; ++g) {
-        const int s = g % STAGES, b = g & 1;
+        const int s = g % STAGES, b = kPre ? 0 : g & 1;
         ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.full[s], (g / STAGES) & 1, err, kErrWaitFull)) &&
-             __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_empty[b], ((g >> 1) & 1) ^ 1, err, kErrWaitAccEmpty));
+             (kPre || __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_empty[b], ((g >> 1) & 1) ^ 1, err, kErrWaitAccEmpty)));
         if (!ok) break;
         tc_fence_after();
         if (elect_one()) {
           const uint32_t a0 = smem_u32(sm.a[s]), b0 = smem_u32(sm.b[s]);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            mma_f16(tmem + b * BN, smem_desc_k128(a0 + kk * 32), smem_desc_k128(b0 + kk * 32), idesc, kk > 0);
-          tc_commit(&sm.acc_full[b]);
+            mma_f16(tmem + b * BN, smem_desc_k128(a0 + kk * 32), smem_desc_k128(b0 + kk * 32), idesc,
+                    kPre ? (g > 0 || kk > 0) : kk > 0);
+          if (!kPre) tc_commit(&sm.acc_full[b]);
           tc_commit(&sm.empty[s]);
         }
         __syncwarp();
       }
-      if (elect_one()) tc_commit(&sm.mma_done);
+      if (elect_one()) {
+        if (kPre) tc_commit(&sm.acc_full[0]);  // the whole of K accumulated
+        tc_commit(&sm.mma_done);
+      }
       __syncwarp();
       mbar_wait(&sm.mma_done, 0, err, kErrWaitAccFull);
     }
@@ -135,22 +258,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const int m = m_tile * BM + row;
     const bool row_ok = m < M;
-    // N % 128 == 0: the last column tile may hold only its first half (the TMA zero-fills the missing weight rows)
-    const bool col_ok = n_tile * BN + h * 128 < N;
     const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + h * 128;
     const float unfold = __ldg(fold_scale);  // 2^F
     float acc[128];
 #pragma unroll
     for (int j = 0; j < 128; ++j) acc[j] = 0.f;
 
+    bool ok = true;
+    if constexpr (kPre) {
+      // one drain of the accumulated products, each row scaled by 2^E_m * 2^F (exact: powers of two)
+      const float mul = __fmul_rn(row_ok ? __ldg(ep.ascale + m) : 0.f, unfold);
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_full[0], 0, err, kErrWaitAccFull));
+      if (ok) {
+        tc_fence_after();
+        uint32_t ra[32], rb[32];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          tmem_ld32(t_row + r * 64, ra);
+          tmem_ld32(t_row + r * 64 + 32, rb);
+          tmem_ld_wait(ra);
+          tmem_ld_wait(rb);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[r * 64 + j] = __fmul_rn(__uint_as_float(ra[j]), mul);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[r * 64 + 32 + j] = __fmul_rn(__uint_as_float(rb[j]), mul);
+        }
+      }
+    }
     // sx[g, m], loaded kAhead groups ahead through a ring of registers: a group lasts well under the latency of
     // a load that misses L2, and the promotion of every element waits on it
     constexpr int kAhead = 4;
     float sxr[kAhead];
 #pragma unroll
-    for (int i = 0; i < kAhead; ++i) sxr[i] = row_ok && i < G ? __ldg(ep.ascale + static_cast<size_t>(i) * M + m) : 0.f;
-    bool ok = true;
-    for (int g = 0; g < G; ++g) {
+    for (int i = 0; i < kAhead; ++i)
+      sxr[i] = !kPre && row_ok && i < G ? __ldg(ep.ascale + static_cast<size_t>(i) * M + m) : 0.f;
+    for (int g = 0; g < (kPre ? 0 : G); ++g) {
       const int b = g & 1;
       const float mul = __fmul_rn(sxr[0], unfold);  // sx * 2^F, exact: a power of two
 #pragma unroll
@@ -181,105 +323,164 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
-    if (ok && row_ok && col_ok) add_addend<128>(ep, m, n_tile * BN + h * 128, acc);
+    if constexpr (kMode == kEpiResidualF32) fence_proxy_async_smem();  // the scratch is a pipeline buffer
+    finish_tile<kMode>(acc, ep, reinterpret_cast<float*>(sm.a[0]) + (warp - 4) * 32 * 33, M, N, m_tile, n_tile, q,
+                       h, lane, ok);
+  }
 
-    if constexpr (kMode == kEpiResidualF32) {
-      // Residual update through a per-warp 32 x 32 transpose in shared memory (the pipeline buffers, idle once every
-      // MMA has completed): lane l then owns column l of a 32-column block and the warp reads and writes whole rows
-      // (128 contiguous bytes) instead of 32 rows at once, all 32 rows' loads in flight together; bias and gate are
-      // loaded once per column. Same arithmetic per element as a thread-per-row update.
-      fence_proxy_async_smem();
-      float* tw = reinterpret_cast<float*>(sm.a[0]) + (warp - 4) * 32 * 33;
-      const int m0 = m_tile * BM + q * 32;
-#pragma unroll
-      for (int blk = 0; blk < 4; ++blk) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) tw[lane * 33 + j] = acc[blk * 32 + j];
-        __syncwarp();
-        const int n = n_tile * BN + h * 128 + blk * 32 + lane;
-        const float bn = ep.bias && col_ok ? __ldg(ep.bias + n) : 0.f;
-        if (ok && col_ok && !ep.residual) {
-          // a partial product in fp32 (a shard's share of a row-parallel layer, summed across shards before the
-          // bias, rounding and residual update): out = acc (+ bias), no rounding
-          float* out = reinterpret_cast<float*>(ep.out) + n;
-#pragma unroll
-          for (int r = 0; r < 32; ++r)
-            if (m0 + r < M) out[static_cast<size_t>(m0 + r) * ep.ld_out] = tw[r * 33 + lane] + bn;
-        } else if (ok && col_ok) {
-          {
-            // residual stream update in fp32: x_new = x + float(bf16(acc + bias)) * gate   (gate 1 when absent)
-            const float gn = ep.gate ? __ldg(ep.gate + n) : 0.f;
-            float* out = reinterpret_cast<float*>(ep.out) + n;
-            const float* res = ep.residual + n;
-            float x[32];  // all 32 rows' residuals in flight at once
-#pragma unroll
-            for (int r = 0; r < 32; ++r) x[r] = m0 + r < M ? res[static_cast<size_t>(m0 + r) * ep.ld_res] : 0.f;
-#pragma unroll
-            for (int r = 0; r < 32; ++r) {
-              const float o = bf16_round(tw[r * 33 + lane] + bn);
-              if (m0 + r < M)
-                out[static_cast<size_t>(m0 + r) * ep.ld_out] = ep.gate ? __fadd_rn(x[r], __fmul_rn(o, gn)) : __fadd_rn(x[r], o);
-            }
-          }
-        }
-        __syncwarp();
-      }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---- the prescaled format (kCodesF16Pre), persistent ------------------------------------------------------------
+// With both scales folded into the operands, a tile is one plain accumulation over all of K: its accumulator
+// (256 TMEM columns) is drained once, at the end. One CTA per SM loops over the tiles (tile t: m tile t % m_tiles,
+// n tile t / m_tiles, so that the CTAs running together share weight tiles) with two accumulators: the MMA
+// accumulates tile i + 1 into one while the epilogue warps drain tile i from the other and finish it (scale by
+// 2^E_m 2^F, addend, bias, mode), so the epilogue is hidden behind the next tile's main loop. The TMA producer and
+// the pipeline stages run on across tile boundaries. Same warp roles as gemm_fold_kernel; the residual mode's
+// transposes use scratch of their own (the stages stay busy).
+struct __align__(1024) SmemP {
+  uint8_t a[STAGES][A_BYTES];
+  uint8_t b[STAGES][B_BYTES];
+  float scratch[8][32 * 33];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+};
+
+constexpr size_t kSmemPBytes = sizeof(SmemP) + 1024;
+
+template <int kMode>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pre_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                    const float* __restrict__ fold_scale, GemmEpilogue ep, int M, int N, int K, uint32_t* err) {
+  extern __shared__ uint8_t smem_raw[];
+  SmemP& sm = *reinterpret_cast<SmemP*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = K / BK;
+  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+  const int tiles = m_tiles * n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
     }
-    if (ok && row_ok && col_ok) {
-      const int n0 = n_tile * BN + h * 128;
-      if constexpr (kMode == kEpiBf16) {
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
-#pragma unroll
-        for (int j = 0; j < 128; j += 8) {
-          float v[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = acc[j + i] + (ep.bias ? __ldg(ep.bias + n0 + j + i) : 0.f);
-          uint4 pk;
-          __nv_bfloat162 t0 = __floats2bfloat162_rn(v[0], v[1]), t1 = __floats2bfloat162_rn(v[2], v[3]);
-          __nv_bfloat162 t2 = __floats2bfloat162_rn(v[4], v[5]), t3 = __floats2bfloat162_rn(v[6], v[7]);
-          pk.x = *reinterpret_cast<uint32_t*>(&t0);
-          pk.y = *reinterpret_cast<uint32_t*>(&t1);
-          pk.z = *reinterpret_cast<uint32_t*>(&t2);
-          pk.w = *reinterpret_cast<uint32_t*>(&t3);
-          *reinterpret_cast<uint4*>(out + j) = pk;
-        }
-      } else if constexpr (kMode == kEpiGeluU4) {
-        // the fused MLP's hidden layer (reference quantization/w4a4.py:195-204, native/ops/w4a4_ops.cpp:44-63):
-        // u = GELU(acc + bias) + shift, divided by the next layer's smoothing, quantized unsigned per group of 64
-        // columns: scale = max(max u, 1e-8) / 15, code = round-half-even(u / scale) clamped to [0, 15], stored as
-        // the next layer's float16 operand (exact integers) with the scale [N / 64, M] rounded to its dtype.
-        uint16_t* codes = reinterpret_cast<uint16_t*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
-#pragma unroll
-        for (int g2 = 0; g2 < 2; ++g2) {
-          float amax = 0.f;
-#pragma unroll
-          for (int j = 0; j < 64; ++j) {
-            const int n = n0 + g2 * 64 + j;
-            const float gv = gelu_tanh(acc[g2 * 64 + j] + (ep.bias ? __ldg(ep.bias + n) : 0.f));
-            if (ep.gelu_out) ep.gelu_out[static_cast<size_t>(m) * ep.ld_gelu + n] = gv;
-            float t = __fadd_rn(gv, ep.gelu_shift);
-            if (ep.out_smooth) t = __fdiv_rn(t, __bfloat162float(ep.out_smooth[n]));
-            acc[g2 * 64 + j] = t;
-            amax = fmaxf(amax, fabsf(t));
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 8);
+    }
+    mbar_init(&sm.mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensor_map(&map_a);
+    prefetch_tensor_map(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp < 4) {
+    setmaxnreg_dec<56>();
+    if (warp == 0 && lane == 0) {
+      // ---------------- TMA producer: every k block of every tile of this CTA, through the ring of stages
+      int kb = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int m_tile = t % m_tiles, n_tile = t / m_tiles;
+        for (int g = 0; g < G; ++g, ++kb) {
+          const int s = kb % STAGES;
+          if (!mbar_wait(&sm.empty[s], ((kb / STAGES) & 1) ^ 1, err, kErrWaitEmpty)) {
+            ok = false;
+            break;
           }
-          const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), 15.f);
-          const float rcp = __frcp_rn(scale);
-#pragma unroll
-          for (int j = 0; j < 64; j += 8) {
-            uint32_t w[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int q0 = max(0, min(15, __float2int_rn(div_rn_by(acc[g2 * 64 + j + 2 * e], scale, rcp))));
-              const int q1 = max(0, min(15, __float2int_rn(div_rn_by(acc[g2 * 64 + j + 2 * e + 1], scale, rcp))));
-              w[e] = static_cast<uint32_t>(__half_as_ushort(__int2half_rn(q0))) |
-                     (static_cast<uint32_t>(__half_as_ushort(__int2half_rn(q1))) << 16);
-            }
-            *reinterpret_cast<uint4*>(codes + g2 * 64 + j) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-          ep.out_scales[static_cast<size_t>((n0 + g2 * 64) / 64) * M + m] =
-              ep.out_scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16_round(scale);
+          mbar_arrive_expect_tx(&sm.full[s], A_BYTES + B_BYTES);
+          tma_load_2d(sm.a[s], &map_a, &sm.full[s], g * BK, m_tile * BM);
+          tma_load_2d(sm.b[s], &map_b, &sm.full[s], g * BK, n_tile * BN);
         }
       }
+      for (int j = (kb > STAGES ? kb - STAGES : 0); j < kb; ++j)  // no copy in flight at exit
+        mbar_wait(&sm.full[j % STAGES], (j / STAGES) & 1, err, kErrWaitFull);
+    } else if (warp == 1) {
+      // ---------------- MMA issuer: tile i into accumulator i % 2, all of K
+      const uint32_t idesc = make_idesc(1, 0, 0, BM, BN);  // f16 x f16 -> f32
+      bool ok = true;
+      int kb = 0, i = 0;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+        const int b = i & 1;
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_empty[b], ((i >> 1) & 1) ^ 1, err, kErrWaitAccEmpty));
+        if (!ok) break;
+        tc_fence_after();
+        for (int g = 0; g < G; ++g, ++kb) {
+          const int s = kb % STAGES;
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.full[s], (kb / STAGES) & 1, err, kErrWaitFull));
+          if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t a0 = smem_u32(sm.a[s]), b0 = smem_u32(sm.b[s]);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              mma_f16(tmem + b * BN, smem_desc_k128(a0 + kk * 32), smem_desc_k128(b0 + kk * 32), idesc,
+                      g > 0 || kk > 0);
+            tc_commit(&sm.empty[s]);
+          }
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (elect_one()) tc_commit(&sm.acc_full[b]);
+        __syncwarp();
+      }
+      if (elect_one()) tc_commit(&sm.mma_done);
+      __syncwarp();
+      mbar_wait(&sm.mma_done, 0, err, kErrWaitAccFull);
+    }
+  } else {
+    setmaxnreg_inc<224>();
+    // ---------------- epilogue: drain tile i's accumulator, hand it back, finish the tile
+    const int q = warp & 3, h = (warp - 4) >> 2;
+    const float unfold = __ldg(fold_scale);  // 2^F
+    float* tw = sm.scratch[warp - 4];
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int m_tile = t % m_tiles, n_tile = t / m_tiles;
+      const int b = i & 1;
+      const int m = m_tile * BM + q * 32 + lane;
+      const float mul = __fmul_rn(m < M ? __ldg(ep.ascale + m) : 0.f, unfold);  // 2^E_m 2^F: exact
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_full[b], (i >> 1) & 1, err, kErrWaitAccFull))) break;
+      tc_fence_after();
+      const uint32_t t_buf = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN + h * 128;
+      float acc[128];
+      uint32_t ra[32], rb[32];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        tmem_ld32(t_buf + r * 64, ra);
+        tmem_ld32(t_buf + r * 64 + 32, rb);
+        tmem_ld_wait(ra);
+        tmem_ld_wait(rb);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[r * 64 + j] = __fmul_rn(__uint_as_float(ra[j]), mul);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[r * 64 + 32 + j] = __fmul_rn(__uint_as_float(rb[j]), mul);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[b]);  // every column in registers: the MMA may reuse the buffer
+      finish_tile<kMode>(acc, ep, tw, M, N, m_tile, n_tile, q, h, lane, true);
     }
   }
 
@@ -377,15 +578,41 @@ int gemm_fold_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
   }
   const dim3 grid((a.M + fold::BM - 1) / fold::BM, (a.N + fold::BN - 1) / fold::BN);
   cudaError_t e = cudaSuccess;
+  if (a.code_format == kCodesF16Pre) {  // persistent: one CTA per SM (or per tile, when there are fewer)
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = static_cast<int>(grid.x * grid.y);
+    const dim3 pgrid(tiles < sms ? tiles : sms);
+    auto launch_p = [&](auto kernel) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(fold::kSmemPBytes));
+      if (e == cudaSuccess)
+        kernel<<<pgrid, fold::kThreads, fold::kSmemPBytes, stream>>>(ma, mb, a.wscale, a.ep, a.M, a.N, a.K, a.err);
+    };
+    switch (a.ep.mode) {
+      case kEpiBf16: launch_p(fold::gemm_pre_kernel<kEpiBf16>); break;
+      case kEpiResidualF32: launch_p(fold::gemm_pre_kernel<kEpiResidualF32>); break;
+      case kEpiGeluU4: launch_p(fold::gemm_pre_kernel<kEpiGeluU4>); break;
+      default: *why = "unknown epilogue mode"; return 1;
+    }
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      *why = cudaGetErrorString(e);
+      return 3;
+    }
+    return 0;
+  }
   auto launch = [&](auto kernel) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(fold::kSmemBytes));
     if (e == cudaSuccess)
       kernel<<<grid, fold::kThreads, fold::kSmemBytes, stream>>>(ma, mb, a.wscale, a.ep, a.M, a.N, a.K, a.err);
   };
+  const bool pre = a.code_format == kCodesF16Pre;
   switch (a.ep.mode) {
-    case kEpiBf16: launch(fold::gemm_fold_kernel<kEpiBf16>); break;
-    case kEpiResidualF32: launch(fold::gemm_fold_kernel<kEpiResidualF32>); break;
-    case kEpiGeluU4: launch(fold::gemm_fold_kernel<kEpiGeluU4>); break;
+    case kEpiBf16: pre ? launch(fold::gemm_fold_kernel<kEpiBf16, true>) : launch(fold::gemm_fold_kernel<kEpiBf16, false>); break;
+    case kEpiResidualF32:
+      pre ? launch(fold::gemm_fold_kernel<kEpiResidualF32, true>) : launch(fold::gemm_fold_kernel<kEpiResidualF32, false>);
+      break;
+    case kEpiGeluU4: pre ? launch(fold::gemm_fold_kernel<kEpiGeluU4, true>) : launch(fold::gemm_fold_kernel<kEpiGeluU4, false>); break;
     default: *why = "unknown epilogue mode"; return 1;
   }
   if (e == cudaSuccess) e = cudaGetLastError();

@@ -140,6 +140,77 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
   }
 }
 
+// The prescaled float16 activations (code format 4): the same codes and stored bf16 scales as above, written as
+// float16(code * stored scale * 2^-E_m) with one power of two per row, chosen from the row's largest stored scale
+// (8 * its largest |code * scale| * 2^-E_m lands in [2^14, 2^15)); rows_scale[m] = 2^E_m. Every value is exact: a
+// code has at most 3 significant bits and a bf16 scale 8, and it is a normal float16 number unless its group's
+// scale is below 2^-25 of the row's largest (then it rounds to a float16 subnormal). Two passes over the row
+// (the second reads it again from L1 / L2): the scales, then the values.
+__device__ __forceinline__ uint32_t exponent_field(float x) { return (__float_as_uint(x) >> 23) & 0xFFu; }
+
+template <typename T, bool kSmooth>
+__global__ void __launch_bounds__(256) quantize_rows_pre_kernel(const T* __restrict__ x, int64_t ldx,
+                                                                const __nv_bfloat16* __restrict__ smooth, int M,
+                                                                int K, uint16_t* __restrict__ out,
+                                                                float* __restrict__ rows_scale) {
+  const int lane = threadIdx.x & 31;
+  const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (m >= M) return;
+  const T* xr = x + static_cast<int64_t>(m) * ldx;
+  // one chunk of 256 columns per lane round: values, their group's fp32 scale and stored (bf16) scale
+  auto group = [&](int k, float (&v)[8], float& scale, float& stored) {
+    const bool valid = k < K;
+    if (valid) {
+      load8<T>(xr + k, v);
+      if (kSmooth) {
+        float sm[8];
+        load8<__nv_bfloat16>(smooth + k, sm);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fdiv_rn(v[i], sm[i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+    scale = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
+    stored = valid ? __bfloat162float(__float2bfloat16_rn(scale)) : 0.f;
+  };
+  float top = 0.f;
+  for (int k0 = 0; k0 < K; k0 += 256) {
+    float v[8], scale, stored;
+    group(k0 + lane * 8, v, scale, stored);
+    top = fmaxf(top, stored);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
+  const uint32_t e = exponent_field(top);  // top in [2^(e-127), 2^(e-126)): 8 top 2^(138-e) in [2^14, 2^15)
+  const float down = __uint_as_float((265u - e) << 23);  // 2^(138 - e)
+  if (lane == 0) rows_scale[m] = __uint_as_float((e - 11u) << 23);  // 2^(e - 138)
+  for (int k0 = 0; k0 < K; k0 += 256) {
+    const int k = k0 + lane * 8;
+    float v[8], scale, stored;
+    group(k, v, scale, stored);
+    if (k >= K) continue;
+    const float r = __frcp_rn(scale);
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      const int q0 = max(-8, min(7, __float2int_rn(div_rn_by(v[i], scale, r))));
+      const int q1 = max(-8, min(7, __float2int_rn(div_rn_by(v[i + 1], scale, r))));
+      const __half2 h = __floats2half2_rn(__fmul_rn(static_cast<float>(q0) * stored, down),
+                                          __fmul_rn(static_cast<float>(q1) * stored, down));
+      w[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(m) * K + k) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // codes [N, K] from qweight [N, K/2]: one thread per 4 packed bytes (8 codes), 32-bit load, 64-bit store.
 template <bool kE4M3>
 __global__ void unpack_codes_kernel(const uint8_t* __restrict__ qweight, int64_t words, int8_t* __restrict__ codes) {
@@ -195,6 +266,15 @@ void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_
   const int pad = code_format == 2;
   auto go = [&](auto t) {
     using T = decltype(t);
+    if (code_format == 4) {
+      const int blocks = (M * 32 + 255) / 256;
+      const T* xt = static_cast<const T*>(x);
+      const __nv_bfloat16* sm = reinterpret_cast<const __nv_bfloat16*>(smooth);
+      uint16_t* out = reinterpret_cast<uint16_t*>(codes);
+      if (smooth) quantize_rows_pre_kernel<T, true><<<blocks, 256, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
+      else quantize_rows_pre_kernel<T, false><<<blocks, 256, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
+      return;
+    }
     if (code_format == 3) launch_rows<T, 3>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
     else if (code_format != 0) launch_rows<T, 1>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
     else launch_rows<T, 0>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);

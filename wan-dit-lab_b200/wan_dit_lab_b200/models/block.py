@@ -195,8 +195,9 @@ class WanBlockB200:
         def gemm_residual(layer, gate_row, codes=None, scales=None, add=None):
             c = buf.codes if codes is None else codes
             s = buf.scales if scales is None else scales
+            f = fmt if codes is None else w4a4.hidden_format(fmt)  # the hidden layer's own format
             timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_residual_add(
-                c.data_ptr(), s.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), fmt,
+                c.data_ptr(), s.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), f,
                 _native.ptr(layer.bias), _native.ptr(add), layer.N, None if gate_row is None else mod_ptr(gate_row),
                 X.data_ptr(), dim, n, layer.N, layer.K, X.data_ptr(), dim, st)))
 
@@ -257,7 +258,7 @@ class WanBlockB200:
             fc1.K, buf.hcodes.data_ptr(), fc1.N, buf.hscales.data_ptr(), _native.ptr(gelu), fc1.N, st)))
         if trace is not None:  # the hidden codes [n, ffn] as float values, whatever their operand format
             raw = buf.hcodes.view(-1)
-            if fmt == _native.CODES_F16_FOLD:
+            if w4a4.hidden_format(fmt) == _native.CODES_F16_FOLD:
                 trace["hcodes"] = raw[:n * fc1.N * 2].view(torch.float16).view(n, fc1.N).float()
             else:
                 trace["hcodes"] = raw[:n * fc1.N].view(torch.float8_e4m3fn).view(n, fc1.N).float()

@@ -218,8 +218,9 @@ class WanBlockTP:
                 _native.ptr(layer.bias), n, layer.N, layer.K, out.data_ptr(), out.stride(0), st)))
 
         def partial(layer, codes, scales):
+            f = w4a4.hidden_format(fmt) if codes is buf.hcodes else fmt  # the hidden layer's own format
             timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_f32(
-                codes.data_ptr(), scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), fmt, None,
+                codes.data_ptr(), scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), f, None,
                 None, 0, n, dim, layer.K, buf.partial.data_ptr(), dim, st)))
 
         def residual(name, gate_row):

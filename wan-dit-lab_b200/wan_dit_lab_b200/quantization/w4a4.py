@@ -28,8 +28,11 @@ GROUP = 64  # input channels per INT4 scale (reference w4a4.py:29)
 # tensor cores too (same results bit for bit, one CUDA-core operation per element and group instead of two).
 # "f16fold" holds float16 operands: activation codes, and weights folded with their bf16 group scales (exact),
 # so that the GEMM's promotion is one fused multiply-add by the activation scale (same results bit for bit); a
-# layer whose folded weights would not be exact (non-bf16 scales) falls back to "e4m3".
-CODE_FORMAT = "f16fold"
+# layer whose folded weights would not be exact (non-bf16 scales) falls back to "e4m3". "f16pre" keeps the folded
+# weights and folds the activation scales into the activations too (code * sx * 2^-E per row, exact): the GEMM
+# accumulates all of K on the tensor cores and scales each row once (float32 rounding of the sum, not bit-identical
+# to the per-group promotion); the fused MLP's unsigned hidden layer stays in "f16fold".
+CODE_FORMAT = "f16pre"
 GELU_SHIFT = 0.171875  # GELU(x) + GELU_SHIFT >= 0: the hidden layer of gelu_mlp is quantized unsigned (w4a4.py:195)
 PARTS = ("qweight", "wscales", "proj_down", "proj_up", "smooth", "bias")  # w4a4.py:207
 
@@ -48,19 +51,28 @@ def _scale_code(dtype):
 
 def _code_format(name):
     return {"e4m3": _native.CODES_E4M3, "int8": _native.CODES_INT8, "e4m3ts": _native.CODES_E4M3_TS,
-            "f16fold": _native.CODES_F16_FOLD}[name]
+            "f16fold": _native.CODES_F16_FOLD, "f16pre": _native.CODES_F16_PRE}[name]
+
+
+def hidden_format(code_format):
+    """The code format (int) of the fused MLP's hidden layer, which a GELU epilogue of a GEMM in `code_format`
+    writes and the second layer's GEMM reads: the prescaled format's is the folded one (unsigned codes)."""
+    return _native.CODES_F16_FOLD if code_format == _native.CODES_F16_PRE else code_format
 
 
 def scale_shape(groups, rows, code_format):
-    """Shape of a [groups, rows] scale array in the given code format (padded to 4 float32 for "e4m3ts")."""
-    return (groups, rows, 4) if _code_format(code_format) == _native.CODES_E4M3_TS else (groups, rows)
+    """Shape of a [groups, rows] scale array in the given code format (padded to 4 float32 for "e4m3ts"; one power
+    of two per row for "f16pre")."""
+    f = _code_format(code_format)
+    return (groups, rows, 4) if f == _native.CODES_E4M3_TS else (rows,) if f == _native.CODES_F16_PRE else (groups, rows)
 
 
 def quantize_rows(x, scale_dtype=torch.bfloat16, smooth=None, packed=False, code_format="int8"):
     """Rows of x [M, K] (bfloat16 or float32, CUDA) in symmetric INT4 groups of GROUP: codes [M, K] int8, scales
     [K / GROUP, M] float32 (holding values rounded to scale_dtype) and, with packed, the nibbles [M, K / 2] uint8.
     code_format "int8" gives the codes as int8 integers, "e4m3" as the GEMM's E4M3 bytes (a uint8 tensor),
-    "e4m3ts" E4M3 bytes with scales [K / GROUP, M, 4] holding (s, 0, 0, 0), "f16fold" float16 codes.
+    "e4m3ts" E4M3 bytes with scales [K / GROUP, M, 4] holding (s, 0, 0, 0), "f16fold" float16 codes, "f16pre"
+    float16 code * scale * 2^-E_m with the rows' 2^E_m [M] as scales (bf16 scales only).
     scale = max(max|x_g|, 1e-8) / 7, code = round-half-even(x / scale) clamped to [-8, 7] (the rule of
     int4_groups, reference w4a4.py:86-100); smooth [K] bfloat16 divides x first."""
     _cuda(x, "x")
@@ -71,7 +83,7 @@ def quantize_rows(x, scale_dtype=torch.bfloat16, smooth=None, packed=False, code
     if x.stride(1) != 1:
         x = x.contiguous()
     M, K = x.shape
-    dtype = {"int8": torch.int8, "f16fold": torch.float16}.get(code_format, torch.uint8)
+    dtype = {"int8": torch.int8, "f16fold": torch.float16, "f16pre": torch.float16}.get(code_format, torch.uint8)
     codes = torch.empty(M, K, dtype=dtype, device=x.device)
     scales = torch.empty(scale_shape(K // GROUP, M, code_format), dtype=torch.float32, device=x.device)
     nib = torch.empty(M, K // 2, dtype=torch.uint8, device=x.device) if packed else None
@@ -173,10 +185,10 @@ class PreparedW4A4:
         fmt = code_format or CODE_FORMAT
         q = qweight.contiguous().view(torch.uint8)
         ws = wscales.contiguous()
-        if fmt == "f16fold" and not self._fold(q, ws, N, K):
+        if fmt in ("f16fold", "f16pre") and not self._fold(q, ws, N, K):
             fmt = "e4m3"  # the folded weights would not be exact: keep the 8-bit codes
         self.code_format = _code_format(fmt)
-        if fmt != "f16fold":
+        if fmt not in ("f16fold", "f16pre"):
             self.codes = torch.empty(N, K, dtype=torch.uint8, device=qweight.device)
             self.scales = torch.empty(scale_shape(K // GROUP, N, fmt), dtype=torch.float32, device=qweight.device)
             with torch.cuda.device(q.device):
@@ -318,7 +330,7 @@ def w4a4_gelu_mlp(x, *parts):
             _native.ptr(gelu), l1.N, st))
         add2 = l2.lowrank(gelu) if l2.rank else None
         _native.check(lib.wdl_w4a4_gemm_add(
-            hidden.data_ptr(), hscales.data_ptr(), l2.codes.data_ptr(), l2.scales.data_ptr(), l2.code_format,
+            hidden.data_ptr(), hscales.data_ptr(), l2.codes.data_ptr(), l2.scales.data_ptr(), hidden_format(l2.code_format),
             _native.ptr(l2.bias), _native.ptr(add2), l2.N, M, l2.N, l2.K, y.data_ptr(), l2.N, st))
     return y
 
