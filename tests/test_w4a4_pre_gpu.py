@@ -68,12 +68,25 @@ def test_ln_quant_prescaled_values_exact():
     for fmt, shape in ((3, (K // 64, M)), (4, (M,))):
         codes = torch.empty(M, K, dtype=torch.float16, device="cuda")
         sc = torch.empty(shape, device="cuda")
-        _native.check(lib.wdl_ln_quant(X.data_ptr(), _native.F32, K, M, K, 1e-6, None, None, 0, shift.data_ptr(),
-                                       scale.data_ptr(), smooth.data_ptr(), _native.BF16, fmt, codes.data_ptr(),
-                                       sc.data_ptr(), st))
-        out[fmt] = (codes, sc)
-    want = expected_prescaled(out[3][0], out[3][1], out[4][1])
+        kept = torch.empty(M, K, dtype=torch.bfloat16, device="cuda")  # the layer's bf16 input, before smoothing
+        _native.check(lib.wdl_ln_quant_keep(X.data_ptr(), _native.F32, K, M, K, 1e-6, None, None, 0,
+                                            shift.data_ptr(), scale.data_ptr(), smooth.data_ptr(), _native.BF16, fmt,
+                                            codes.data_ptr(), sc.data_ptr(), kept.data_ptr(), K, st))
+        out[fmt] = (codes, sc, kept)
+    # the prescaled values are exactly the folded format's codes and scales of the layer input the kernel kept
+    from wan_dit_lab_b200.quantization import w4a4
+    c3, s3 = w4a4.quantize_rows(out[4][2], torch.bfloat16, smooth=smooth, code_format="f16fold")
+    want = expected_prescaled(c3, s3, out[4][1])
     assert torch.equal(out[4][0].view(torch.int16), want.view(torch.int16))
+    # both kernels' kept inputs: the LayerNorm statistics are float sums in different orders (two warps against
+    # four per row), so a few bf16 values round the other way
+    same = (out[4][2].view(torch.int16) == out[3][2].view(torch.int16)).float().mean().item()
+    assert same >= 0.9999
+    assert float((out[4][2].float() - out[3][2].float()).abs().max()) <= 2 ** -6 * float(out[3][2].float().abs().max())
+    mean = X.mean(1, keepdim=True)
+    ln = (X - mean) * torch.rsqrt(((X - mean) ** 2).mean(1, keepdim=True) + 1e-6)
+    ref = (ln * (1 + scale) + shift).to(torch.bfloat16).float()
+    assert float((out[4][2].float() - ref).abs().max()) <= 0.02 * float(ref.abs().max())
 
 
 def prepared(N, K, seed):

@@ -11,6 +11,8 @@
 // One warp per row; a lane holds 8 consecutive columns (16-byte loads of bf16), 8 lanes make one group, so a
 // group's max is 3 shuffles. Loads and code stores are 128-bit / 64-bit vector accesses: the kernel is
 // HBM-bound (bytes per row: K * in_size + K + K / 64 * 4, plus K / 2 when packing).
+#include <type_traits>
+
 #include "common.cuh"
 #include "w4a4_quant.h"
 
@@ -211,6 +213,74 @@ __global__ void __launch_bounds__(256) quantize_rows_pre_kernel(const T* __restr
   }
 }
 
+// The same values with two warps per row (K <= 512 kChunks): the whole row in registers and one pass over it, so
+// that every row of a chunk of tokens is resident at once (as ln_quant_pre_kernel, norm_quant.cu).
+template <typename T, bool kSmooth, int kChunks>
+__global__ void __launch_bounds__(64, kChunks > 2 ? 8 : 12)
+    quantize_rows_pre2_kernel(const T* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ smooth, int M,
+                              int K, uint16_t* __restrict__ out, float* __restrict__ rows_scale) {
+  __shared__ float red[2];
+  const int t = threadIdx.x, m = blockIdx.x;
+  const T* xr = x + static_cast<int64_t>(m) * ldx;
+  float v[kChunks][8];
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int k = c * 512 + t * 8;
+    if (k < K) {
+      load8<T>(xr + k, v[c]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[c][i] = 0.f;
+    }
+  }
+  float scale[kChunks], stored[kChunks];
+  float top = 0.f;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int k = c * 512 + t * 8;
+    const bool valid = k < K;  // uniform over each group of 8 threads
+    if (kSmooth && valid) {
+      float sm[8];
+      load8<__nv_bfloat16>(smooth + k, sm);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[c][i] = __fdiv_rn(v[c][i], sm[i]);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[c][i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+    scale[c] = __fdiv_rn(fmaxf(amax, 1e-8f), 7.0f);
+    stored[c] = valid ? __bfloat162float(__float2bfloat16_rn(scale[c])) : 0.f;
+    top = fmaxf(top, stored[c]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
+  if ((t & 31) == 0) red[t >> 5] = top;
+  __syncthreads();
+  top = fmaxf(red[0], red[1]);
+  const uint32_t e = exponent_field(top);
+  const float down = __uint_as_float((265u - e) << 23);  // 2^(138 - e)
+  if (t == 0) rows_scale[m] = __uint_as_float((e - 11u) << 23);  // 2^(e - 138)
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int k = c * 512 + t * 8;
+    if (k >= K) continue;
+    const float r = __frcp_rn(scale[c]);
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      const int q0 = max(-8, min(7, __float2int_rn(div_rn_by(v[c][i], scale[c], r))));
+      const int q1 = max(-8, min(7, __float2int_rn(div_rn_by(v[c][i + 1], scale[c], r))));
+      const __half2 h = __floats2half2_rn(__fmul_rn(static_cast<float>(q0) * stored[c], down),
+                                          __fmul_rn(static_cast<float>(q1) * stored[c], down));
+      w[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(m) * K + k) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // codes [N, K] from qweight [N, K/2]: one thread per 4 packed bytes (8 codes), 32-bit load, 64-bit store.
 template <bool kE4M3>
 __global__ void unpack_codes_kernel(const uint8_t* __restrict__ qweight, int64_t words, int8_t* __restrict__ codes) {
@@ -271,6 +341,19 @@ void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_
       const T* xt = static_cast<const T*>(x);
       const __nv_bfloat16* sm = reinterpret_cast<const __nv_bfloat16*>(smooth);
       uint16_t* out = reinterpret_cast<uint16_t*>(codes);
+      if (K <= 4096) {  // two warps per row, the row in registers
+        auto go2 = [&](auto chunks) {
+          constexpr int C = decltype(chunks)::value;
+          if (smooth) quantize_rows_pre2_kernel<T, true, C><<<M, 64, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
+          else quantize_rows_pre2_kernel<T, false, C><<<M, 64, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
+        };
+        const int chunks = (K + 511) / 512;
+        if (chunks <= 2) go2(std::integral_constant<int, 2>{});
+        else if (chunks <= 4) go2(std::integral_constant<int, 4>{});
+        else if (chunks <= 6) go2(std::integral_constant<int, 6>{});
+        else go2(std::integral_constant<int, 8>{});
+        return;
+      }
       if (smooth) quantize_rows_pre_kernel<T, true><<<blocks, 256, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
       else quantize_rows_pre_kernel<T, false><<<blocks, 256, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
       return;
