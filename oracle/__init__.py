@@ -7,7 +7,7 @@ import it, and only as the checker or the timed CPU baseline. The product path (
 wan-dit-lab_b200/) never imports it.
 
 Parity pins: every function is checked against golden vectors made by the reference's own code
-(tests/golden/make_golden.py imports /root/reference/src and runs it on seeded inputs; the vectors are
+(tests/golden/make_golden.py imports the reference's src tree and runs it on seeded inputs; the vectors are
 committed as tests/golden/*.npz). The W4A4 GEMM and the activation quantizer of Nunchaku, and SageAttention's
 kernel, are third-party code absent from the reference tree; their oracle here follows the published
 algorithm and the reference's call sites, pinned where the reference pins it (int4_groups rounding, the Sage

@@ -185,4 +185,6 @@ def main(reference):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <wan-dit-lab checkout>")
+    main(sys.argv[1])
