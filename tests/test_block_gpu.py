@@ -199,3 +199,51 @@ def test_block_with_lowrank_branches_and_smoothing_matches_oracle(rank):
     assert err <= 5e-2
     for name, gpu in (("k", cache[0]), ("v", cache[2])):
         assert (gpu[at:at + n].cpu().numpy() == ocache[name][0, at:at + n]).mean() > 0.99
+
+
+def test_block_forcing_kv_head_split():
+    """Forcing-KV (reference causal.py:222-240): with the head split, the dynamic heads' attention equals the
+    whole-window attention of the plain block bit for bit, and the static heads' equals attention over the anchor
+    rows alone (sink + newest frame) through sage_kv.attend on a gathered copy of the cache."""
+    from wan_dit_lab_b200.kernels import sage_kv
+    from wan_dit_lab_b200.models.block import Buffers, WanBlockB200
+    from wan_dit_lab_b200 import _native
+    dim, heads, ffn, frames, h, w, at, text = 1024, 8, 4096, 2, 4, 8, 192, 32
+    n = frames * h * w
+    state = random_state(dim, ffn, 13)
+    blk = WanBlockB200(state, dim, ffn, heads)
+    g = torch.Generator().manual_seed(14)
+    X = torch.randn(n, dim, generator=g)
+    time_in = torch.randn(6, dim, generator=g) * 0.1
+    ctx = (torch.randn(text, dim, generator=g)).to(torch.bfloat16)
+    cap = at + n
+    ck8, cks = of.quantize_rows((torch.randn(1, cap, heads, 128, generator=g) + 0.3).numpy())
+    cv8, cvs = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    freq = torch.from_numpy(orope.table(1024).astype(np.float32)).cuda()
+    mod = blk.modulation_of(time_in.cuda())
+    cross = blk.cross_kv(ctx.cuda())
+    static = torch.tensor([1, 5], dtype=torch.int32).cuda()
+    dynamic = torch.tensor([0, 2, 3, 4, 6, 7], dtype=torch.int32).cuda()
+    anchors = torch.cat([torch.arange(32), torch.arange(at - 32, at)]).to(torch.int32).cuda()  # a sink, a frame
+    traces = []
+    for forcing in (None, (static, dynamic, anchors)):
+        cache = (torch.from_numpy(ck8[0]).cuda(), torch.from_numpy(cks[0, ..., 0]).cuda(),
+                 torch.from_numpy(cv8[0]).cuda(), torch.from_numpy(cvs[0, ..., 0]).cuda(), cap)
+        tr = {}
+        blk.forward(X.cuda(), mod, cache, at, freq, (frames, h, w), at // (h * w), cross,
+                    Buffers(n, dim, ffn, heads, cap, text, "cuda"), trace=tr, forcing=forcing)
+        traces.append((tr, cache))
+    assert _native.device_error() == 0
+    (plain, _), (split, cache) = traces
+    A0, A1 = plain["attn"].view(n, heads, 128), split["attn"].view(n, heads, 128)
+    dl, sl = dynamic.long(), static.long()
+    assert torch.equal(A1[:, dl], A0[:, dl])
+    assert not torch.equal(A1[:, sl], A0[:, sl])
+    q = split["q"].view(1, n, heads, 128)[:, :, sl].contiguous()
+    k = split["k"].view(1, n, heads, 128)[:, :, sl].contiguous()
+    v = split["qkv"][:, 2 * dim:].reshape(1, n, heads, 128)[:, :, sl].contiguous()
+    rows = anchors.long()
+    gather = lambda t: t[rows][:, sl].contiguous()[None]  # noqa: E731
+    want = sage_kv.attend(q, gather(cache[0]).view(torch.float8_e4m3fn), gather(cache[1])[..., None],
+                          gather(cache[2]).view(torch.float8_e4m3fn), gather(cache[3])[..., None], rows.numel(), k, v)
+    assert torch.equal(A1[:, sl], want[0])

@@ -1,0 +1,79 @@
+"""The FP8 KV cache's bookkeeping on CPU tensors (generation/causal.py::KVCache): which ring slots a full cache's
+chunk replaces (the ring tokens earliest in the video, the chunk's token i into the i-th earliest: reference
+KVCache.commit / evicted, causal.py:298-337), and Forcing-KV's anchor rows (the sink and the newest finished
+frame, causal.py:243-248), checked against a plain restatement of those rules."""
+
+import sys
+from pathlib import Path
+
+import torch
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "wan-dit-lab_b200"))
+
+
+def restated(frames_done, per, ring_frames, chunk_frames):
+    """Frame number and place in frame of every ring slot after `frames_done` chunks, by the reference's rules."""
+    ring = ring_frames * per
+    frame_of = [0] * ring
+    place = [0] * ring
+    saved, frames, history = 0, 0, []
+    n = chunk_frames * per
+    for _ in range(frames_done):
+        if saved + n <= ring:
+            for i in range(n):
+                frame_of[saved + i], place[saved + i] = frames + i // per, i % per
+            saved += n
+        else:
+            order = sorted(range(ring), key=lambda s: frame_of[s] * per + place[s])[:n]
+            history.append(order)
+            for i, s in enumerate(order):
+                frame_of[s], place[s] = frames + i // per, i % per
+        frames += chunk_frames
+    return frame_of, place, history
+
+
+def test_eviction_order_and_anchors_follow_the_reference():
+    from wan_dit_lab_b200.generation.causal import KVCache
+    per, chunk, ring_frames, heads = 4, 3, 6, 2
+    n = chunk * per
+    cache = KVCache(ring_frames * per, 0, n, heads, "cpu")
+    cache.set_heads([1], heads)
+    moved = []
+    for c in range(5):
+        at = cache.saved
+        marker = torch.full((n, heads, 128), c + 1, dtype=torch.uint8)
+        cache.k[at:at + n] = marker  # the chunk's keys, as a pass writes them at `saved`
+        full_before = cache.full()
+        cache.commit(chunk, per)
+        if full_before:
+            moved.append([int(r) for r in (cache.k[:, 0, 0] == c + 1).nonzero().flatten() if r < ring_frames * per])
+    frame_of, place, history = restated(5, per, ring_frames, chunk)
+    assert cache.frame_of.tolist() == frame_of and cache.place_in_frame.tolist() == place
+    assert [sorted(h) for h in history] == moved
+    # the newest finished frame's rows, after the (empty) sink
+    newest = max(frame_of)
+    want = sorted(s for s in range(len(frame_of)) if frame_of[s] == newest)
+    assert sorted(cache.anchor_tokens.tolist()) == want
+    static, dynamic, anchors = cache.forcing()
+    assert static.tolist() == [1] and dynamic.tolist() == [0] and anchors is cache.anchor_tokens
+
+
+def test_forcing_applies_only_to_a_full_cache_with_static_heads():
+    from wan_dit_lab_b200.generation.causal import KVCache
+    cache = KVCache(24, 0, 12, 3, "cpu")
+    assert cache.forcing() is None
+    cache.set_heads([0, 2], 3)
+    cache.commit(3, 4)
+    assert cache.forcing() is None  # not full yet
+    cache.commit(3, 4)
+    assert cache.full() and cache.forcing() is not None
+    cache.set_heads([], 3)
+    assert cache.forcing() is None
+    cache.reset()
+    assert cache.saved == 0 and not cache.place_in_frame.any()
+    try:
+        cache.set_heads([5], 3)
+    except ValueError:
+        pass
+    else:
+        raise AssertionError("a head out of range must be refused")

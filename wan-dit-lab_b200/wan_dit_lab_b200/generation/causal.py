@@ -48,12 +48,15 @@ def rope_table(positions, head_dim=128):
 class KVCache:
     """FP8 keys / values of the finished frames of one block: [max_tokens + chunk tokens, heads, 128] E4M3 with
     one float32 scale per (token, head), the first sink_tokens never evicted (reference KVCache,
-    causal.py:48-337, fp8=True, positions "video", no Participative Compression / decay / Forcing-KV)."""
+    causal.py:48-337, fp8=True, positions "video", no Participative Compression / decay). Forcing-KV's head split
+    (set_heads; causal.py:92-102, 222-248): once the cache is full, the static heads attend to the sink, the newest
+    finished frame and the chunk only (anchor_tokens, read through the attention's token map), the others to the
+    whole window."""
 
     fp8 = True
 
     def __init__(self, max_tokens, sink_tokens, n, heads, device):
-        self.max_tokens, self.sink_tokens, self.n = max_tokens, sink_tokens, n
+        self.max_tokens, self.sink_tokens, self.n, self.heads = max_tokens, sink_tokens, n, heads
         cap = max_tokens + n
         self.capacity = cap
         self.k = torch.zeros(cap, heads, 128, dtype=torch.uint8, device=device)
@@ -61,9 +64,13 @@ class KVCache:
         self.ks = torch.zeros(cap, heads, device=device)
         self.vs = torch.zeros_like(self.ks)
         ring = max_tokens - sink_tokens
-        self.frame_of = torch.zeros(ring, dtype=torch.long, device=device)
+        self.frame_of = torch.zeros(ring, dtype=torch.long, device=device)  # frame number of each ring token
+        self.place_in_frame = torch.zeros_like(self.frame_of)  # its index among the tokens of its frame
         self.saved = 0
         self.frames = 0
+        self.per_frame = None
+        self.static_heads = None
+        self.anchor_tokens = None
 
     def buffers(self):
         return self.k, self.ks, self.v, self.vs, self.capacity
@@ -71,21 +78,76 @@ class KVCache:
     def full(self):
         return self.saved == self.max_tokens
 
+    def reset(self):
+        """An empty cache (buffers kept): nothing saved, frames counted from 0."""
+        self.saved, self.frames = 0, 0
+        self.frame_of.zero_()
+        self.place_in_frame.zero_()
+
+    def set_heads(self, static, heads=None):
+        """Forcing-KV: the head numbers that attend to the sink, the newest finished frame and the chunk only, once
+        the cache is full (reference KVCache.set_heads, causal.py:98-102); None or empty: every head sees the whole
+        window. heads: the cache's head count (checked)."""
+        if heads is not None and heads != self.heads:
+            raise ValueError(f"the cache holds {self.heads} heads, not {heads}")
+        static = sorted(set(static or ()))
+        if any(h < 0 or h >= self.heads for h in static):
+            raise ValueError("static heads out of range")
+        self.static_heads = static or None
+        dev = self.k.device
+        if self.static_heads is None:
+            self.anchor_tokens = None
+            return
+        self.static_idx = torch.tensor(self.static_heads, dtype=torch.int32, device=dev)
+        self.dynamic_idx = torch.tensor([h for h in range(self.heads) if h not in static], dtype=torch.int32,
+                                        device=dev)
+        self.anchor_tokens = None  # made at the first commit that knows the frame size
+
+    def _order(self):
+        """Position in the video of each ring token (reference causal.py:331): frame, then place in its frame."""
+        return self.frame_of * self.per_frame + self.place_in_frame
+
+    def place_anchor(self):
+        """The cache rows of the sink and of the newest finished frame, into anchor_tokens in place (a recorded
+        CUDA graph reads them; reference KVCache.place_anchor, causal.py:243-248)."""
+        sink, per = self.sink_tokens, self.per_frame
+        if self.anchor_tokens is None:
+            self.anchor_tokens = torch.zeros(sink + per, dtype=torch.int32, device=self.k.device)
+            self.anchor_tokens[:sink] = torch.arange(sink, dtype=torch.int32, device=self.k.device)
+        newest = torch.topk(self._order(), per).indices
+        self.anchor_tokens[sink:] = (sink + newest).to(torch.int32)
+
+    def forcing(self):
+        """(static heads, dynamic heads, anchor rows) int32 device tensors when the head split applies (static
+        heads set, the cache full, a ring beyond the sink), else None."""
+        if self.static_heads is None or not self.full() or self.anchor_tokens is None:
+            return None
+        return self.static_idx, self.dynamic_idx, self.anchor_tokens
+
     def commit(self, chunk_frames, per_frame):
-        """Keeps the chunk last written at `saved` (reference KVCache.commit, causal.py:298-327)."""
+        """Keeps the chunk last written at `saved` (reference KVCache.commit / evicted, causal.py:298-337): while
+        filling it stays where it was written; once full it replaces the ring tokens earliest in the video, the
+        chunk's token i going to the i-th earliest."""
         n, at, sink = self.n, self.saved, self.sink_tokens
-        if at + n <= self.max_tokens:  # filling: the chunk stays where it was written
-            if at + n > sink:
-                lo = max(at, sink)
-                self.frame_of[lo - sink:at + n - sink] = self.frames + (torch.arange(lo, at + n, device=self.k.device) - at) // per_frame
+        self.per_frame = per_frame
+        dev = self.k.device
+        slots, i = None, None
+        if at + n <= self.max_tokens:
+            o = torch.arange(max(at, sink), max(at + n, sink), device=dev)  # its tokens past the sink
+            slots, i = o - sink, o - at
             self.saved += n
-        elif self.max_tokens > sink:  # full: replace the tokens of the oldest frames of the ring
-            slots = torch.topk(self.frame_of, n, largest=False).indices
+        elif self.max_tokens > sink:
+            slots = torch.topk(self._order(), n, largest=False).indices  # ascending: the earliest first
             to = sink + slots
             for buf in (self.k, self.v, self.ks, self.vs):
                 buf[to] = buf[at:at + n].clone()
-            self.frame_of[slots] = self.frames + torch.arange(n, device=self.k.device) // per_frame
+            i = torch.arange(n, device=dev)
+        if slots is not None and len(slots):
+            self.frame_of[slots] = self.frames + i // per_frame
+            self.place_in_frame[slots] = i % per_frame
         self.frames += chunk_frames
+        if self.static_heads is not None and self.max_tokens > sink and self.full():
+            self.place_anchor()
 
 
 class WanModelB200:
@@ -175,8 +237,10 @@ class WanModelB200:
         _native.check(_native.lib().wdl_modulation(e0.data_ptr(), self.modulation.data_ptr(), len(self.blocks), self.dim,
                                                    self.mods.data_ptr(), _native.stream()))
         for i, blk in enumerate(self.blocks):
+            forcing = caches[i].forcing()
+            kw = {} if forcing is None else {"forcing": forcing}
             blk.forward(X, self.mods[i], caches[i].buffers(), caches[i].saved, freq, grid, start, cross[i], buf,
-                        x_is_bf16=(i == 0))
+                        x_is_bf16=(i == 0), **kw)
         return self.head(X, temb, grid).float()
 
 
@@ -225,7 +289,7 @@ class Stream:
     values with one more pass at t = 0, and commits them."""
 
     def __init__(self, model, context, height, width, generator=None, max_frames=CONTEXT, sink_frames=0, chunk=CHUNK,
-                 vae_stride=8, positions=1024, cuda_graph=False):
+                 vae_stride=8, positions=1024, cuda_graph=False, static_heads=None):
         h, w = height // vae_stride, width // vae_stride
         self.tokens = (h // 2) * (w // 2)
         self.grid = (chunk, h // 2, w // 2)
@@ -235,6 +299,9 @@ class Stream:
         heads = model.blocks[0].kv_heads  # all of them, or this tensor-parallel shard's
         self.caches = [KVCache((max_frames - chunk) * self.tokens, sink_frames * self.tokens, n, heads, model.device)
                        for _ in model.blocks]
+        if static_heads:  # Forcing-KV: {block: [static heads]} (reference Stream, causal.py:490-494)
+            for index, cache in enumerate(self.caches):
+                cache.set_heads(static_heads.get(index, static_heads.get(str(index), [])), heads)
         self.freq = rope_table(positions).to(model.device)
         # the chunk's table: its frames' time angles in rows 0.. (the kernels run with start 0), height / width
         # angles as in the whole table (reference Stream's chunk_freqs), refreshed in place before every chunk
@@ -252,8 +319,7 @@ class Stream:
     def reset(self):
         """A new video under the same prompt: caches emptied (buffers kept), frames counted from 0 again."""
         for cache in self.caches:
-            cache.saved, cache.frames = 0, 0
-            cache.frame_of.zero_()
+            cache.reset()
         self.start = 0
 
     @torch.no_grad()

@@ -152,14 +152,17 @@ class WanBlockB200:
     # is bracketed by CUDA events on the current stream: the benchmark's per-kernel timing of the W4A4 GEMMs.
     gemm_timer = None
 
-    def forward(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, trace=None):
+    def forward(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, trace=None, forcing=None):
         """X [n, dim] float32, updated in place (the block's output). mod [6, dim] float32: this block's
         time_in + modulation. cache: (k, ks, v, vs, capacity) FP8 cache buffers of this block
         [capacity, heads, 128] / [capacity, heads]; the chunk's keys and values are stored at `at` and attention
         runs over [0, at + n). freq [2, positions, 64] float32 RoPE table, grid (frames, h, w) of the chunk,
         start its first frame's time position. cross: CrossKV of the prompt. x_is_bf16: the stream held bf16
         values (the first block of a model): the norms round to bf16 as .type_as does. trace: a dict that, when
-        given, receives copies of the intermediate tensors (debugging; synchronizes)."""
+        given, receives copies of the intermediate tensors (debugging; synchronizes). forcing: Forcing-KV's
+        (static heads, dynamic heads, anchor rows) of the cache (KVCache.forcing()), or None: with it, the dynamic
+        heads attend to the whole cached window and the static ones to the anchor rows (the sink and the newest
+        finished frame), both with the chunk, through the attention's head / token maps (causal.py:222-240)."""
         lib, st = _native.lib(), _native.stream()
         n, dim, H = X.shape[0], self.dim, self.heads
         ck, cks, cv, cvs, capacity = cache
@@ -226,10 +229,29 @@ class WanBlockB200:
                                        self.norm_k.data_ptr(), self.eps, freq.data_ptr(), freq.shape[1], grid[1],
                                        grid[2], start, buf.q.data_ptr(), buf.k.data_ptr(), ck.data_ptr(),
                                        cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(), capacity, at, st))
-        _native.check(lib.wdl_sage_attend(
-            buf.q.data_ptr(), dim, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(), at,
-            buf.k.data_ptr(), _native.F32, dim, buf.qkv.data_ptr() + 2 * dim * 2, _native.BF16, 3 * dim, n, H,
-            HEAD_DIM ** -0.5, buf.attn.data_ptr(), dim, buf.sage.data_ptr(), buf.sage.numel(), st))
+        if forcing is None:
+            _native.check(lib.wdl_sage_attend(
+                buf.q.data_ptr(), dim, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(), at,
+                buf.k.data_ptr(), _native.F32, dim, buf.qkv.data_ptr() + 2 * dim * 2, _native.BF16, 3 * dim, n, H,
+                HEAD_DIM ** -0.5, buf.attn.data_ptr(), dim, buf.sage.data_ptr(), buf.sage.numel(), st))
+        else:
+            static, dynamic, anchors = forcing
+            heads_of = lambda t, idx: t.view(n, H, HEAD_DIM).index_select(1, idx).reshape(n, -1)  # noqa: E731
+            out = buf.attn.view(n, H, HEAD_DIM)
+            for idx, tokens, length in ((dynamic, None, at), (static, anchors, anchors.numel())):
+                if idx.numel() == 0:
+                    continue
+                il = idx.long()
+                q_s, k_s = heads_of(buf.q, il).contiguous(), heads_of(buf.k, il).contiguous()
+                v_s = heads_of(buf.qkv[:, 2 * dim:], il).contiguous()
+                hs = idx.numel()
+                o_s = torch.empty(n, hs * HEAD_DIM, dtype=torch.bfloat16, device=X.device)
+                _native.check(lib.wdl_sage_attend_maps(
+                    q_s.data_ptr(), hs * HEAD_DIM, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(),
+                    capacity, H, idx.data_ptr(), _native.ptr(tokens), length, k_s.data_ptr(), _native.F32,
+                    hs * HEAD_DIM, v_s.data_ptr(), _native.BF16, hs * HEAD_DIM, n, hs, HEAD_DIM ** -0.5,
+                    o_s.data_ptr(), hs * HEAD_DIM, buf.sage.data_ptr(), buf.sage.numel(), st))
+                out[:, il] = o_s.view(n, hs, HEAD_DIM)
         keep("q", buf.q), keep("k", buf.k), keep("attn", buf.attn)
         quantize(buf.attn, L["self_attn.o"])
         gemm_residual(L["self_attn.o"], 2, add=lora(L["self_attn.o"], buf.attn))

@@ -182,8 +182,10 @@ class WanBlockTP:
     # bracketed by CUDA events on the current stream: the benchmark's per-kernel timing of the W4A4 GEMMs.
     gemm_timer = None
 
-    def forward(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, trace=None):
+    def forward(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, trace=None, forcing=None):
         """WanBlockB200.forward on this shard: every tensor steps() yields is summed across shards by reduce."""
+        if forcing is not None:
+            raise NotImplementedError("Forcing-KV's head split runs on the single-GPU block")
         if self.reduce is None:
             raise RuntimeError("a tensor-parallel block needs a reduce callable (or run_lockstep over its steps)")
         for t in self.steps(X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16):
