@@ -24,6 +24,10 @@
 //   warps 4-11  promotion + epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (its rows) and columns
 //               128 ((w - 4) / 4) .. +127, keeps 128 fp32 accumulators per thread
 // TMEM: 2 buffers x 256 columns = all 512.
+//
+// gemm_pre_kernel (further down) takes the prescaled activations of kCodesF16Pre instead, whose products carry
+// both scales: it accumulates all of K per tile and runs persistently (one CTA per SM, two TMEM accumulators),
+// finishing each tile behind the next tile's main loop. Both kernels share the tile epilogue (finish_tile).
 #include "common.cuh"
 #include "w4a4_gemm.h"
 
@@ -168,9 +172,7 @@ __device__ __forceinline__ void finish_tile(float (&acc)[128], const GemmEpilogu
   }
 }
 
-// kPre: activations in the prescaled format (kCodesF16Pre): every group's products carry both scales, so the MMA
-// accumulates all of K into one TMEM buffer and the epilogue multiplies each row by 2^(E_m + F) once.
-template <int kMode, bool kPre>
+template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_fold_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      const float* __restrict__ fold_scale, GemmEpilogue ep, int M, int N, int K, uint32_t* err) {
@@ -228,26 +230,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = make_idesc(1, 0, 0, BM, BN);  // f16 x f16 -> f32
       bool ok = true;
       for (int g = 0; g < G && ok; ++g) {
-        const int s = g % STAGES, b = kPre ? 0 : g & 1;
+        const int s = g % STAGES, b = g & 1;
         ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.full[s], (g / STAGES) & 1, err, kErrWaitFull)) &&
-             (kPre || __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_empty[b], ((g >> 1) & 1) ^ 1, err, kErrWaitAccEmpty)));
+             __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_empty[b], ((g >> 1) & 1) ^ 1, err, kErrWaitAccEmpty));
         if (!ok) break;
         tc_fence_after();
         if (elect_one()) {
           const uint32_t a0 = smem_u32(sm.a[s]), b0 = smem_u32(sm.b[s]);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            mma_f16(tmem + b * BN, smem_desc_k128(a0 + kk * 32), smem_desc_k128(b0 + kk * 32), idesc,
-                    kPre ? (g > 0 || kk > 0) : kk > 0);
-          if (!kPre) tc_commit(&sm.acc_full[b]);
+            mma_f16(tmem + b * BN, smem_desc_k128(a0 + kk * 32), smem_desc_k128(b0 + kk * 32), idesc, kk > 0);
+          tc_commit(&sm.acc_full[b]);
           tc_commit(&sm.empty[s]);
         }
         __syncwarp();
       }
-      if (elect_one()) {
-        if (kPre) tc_commit(&sm.acc_full[0]);  // the whole of K accumulated
-        tc_commit(&sm.mma_done);
-      }
+      if (elect_one()) tc_commit(&sm.mma_done);
       __syncwarp();
       mbar_wait(&sm.mma_done, 0, err, kErrWaitAccFull);
     }
@@ -265,34 +263,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < 128; ++j) acc[j] = 0.f;
 
     bool ok = true;
-    if constexpr (kPre) {
-      // one drain of the accumulated products, each row scaled by 2^E_m * 2^F (exact: powers of two)
-      const float mul = __fmul_rn(row_ok ? __ldg(ep.ascale + m) : 0.f, unfold);
-      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_full[0], 0, err, kErrWaitAccFull));
-      if (ok) {
-        tc_fence_after();
-        uint32_t ra[32], rb[32];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          tmem_ld32(t_row + r * 64, ra);
-          tmem_ld32(t_row + r * 64 + 32, rb);
-          tmem_ld_wait(ra);
-          tmem_ld_wait(rb);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[r * 64 + j] = __fmul_rn(__uint_as_float(ra[j]), mul);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[r * 64 + 32 + j] = __fmul_rn(__uint_as_float(rb[j]), mul);
-        }
-      }
-    }
     // sx[g, m], loaded kAhead groups ahead through a ring of registers: a group lasts well under the latency of
     // a load that misses L2, and the promotion of every element waits on it
     constexpr int kAhead = 4;
     float sxr[kAhead];
 #pragma unroll
     for (int i = 0; i < kAhead; ++i)
-      sxr[i] = !kPre && row_ok && i < G ? __ldg(ep.ascale + static_cast<size_t>(i) * M + m) : 0.f;
-    for (int g = 0; g < (kPre ? 0 : G); ++g) {
+      sxr[i] = row_ok && i < G ? __ldg(ep.ascale + static_cast<size_t>(i) * M + m) : 0.f;
+    for (int g = 0; g < G; ++g) {
       const int b = g & 1;
       const float mul = __fmul_rn(sxr[0], unfold);  // sx * 2^F, exact: a power of two
 #pragma unroll
@@ -606,13 +584,10 @@ int gemm_fold_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
     if (e == cudaSuccess)
       kernel<<<grid, fold::kThreads, fold::kSmemBytes, stream>>>(ma, mb, a.wscale, a.ep, a.M, a.N, a.K, a.err);
   };
-  const bool pre = a.code_format == kCodesF16Pre;
   switch (a.ep.mode) {
-    case kEpiBf16: pre ? launch(fold::gemm_fold_kernel<kEpiBf16, true>) : launch(fold::gemm_fold_kernel<kEpiBf16, false>); break;
-    case kEpiResidualF32:
-      pre ? launch(fold::gemm_fold_kernel<kEpiResidualF32, true>) : launch(fold::gemm_fold_kernel<kEpiResidualF32, false>);
-      break;
-    case kEpiGeluU4: pre ? launch(fold::gemm_fold_kernel<kEpiGeluU4, true>) : launch(fold::gemm_fold_kernel<kEpiGeluU4, false>); break;
+    case kEpiBf16: launch(fold::gemm_fold_kernel<kEpiBf16>); break;
+    case kEpiResidualF32: launch(fold::gemm_fold_kernel<kEpiResidualF32>); break;
+    case kEpiGeluU4: launch(fold::gemm_fold_kernel<kEpiGeluU4>); break;
     default: *why = "unknown epilogue mode"; return 1;
   }
   if (e == cudaSuccess) e = cudaGetLastError();
