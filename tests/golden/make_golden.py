@@ -184,7 +184,45 @@ def main(reference):
          grid=np.array((2, 8, 16)), **state)
 
 
+def kvcache_golden(reference):
+    """The reference KVCache's bookkeeping (generation/causal.py:160-337) on CPU tensors: six commits of a chunk of
+    3 frames x 4 tokens into a window of 6 ring frames, without and with a 3-frame sink, Forcing-KV static head 1;
+    after every commit the ring slots the chunk went to (last_slots), frame_of and place_in_frame, and the anchor
+    rows (sink + newest finished frame, place_anchor) from the first full cache on."""
+    sys.path.insert(0, str(Path(reference) / "src"))
+    from wan_dit_lab.generation import causal
+    per, chunk, ring_frames, heads, commits = 4, 3, 6, 2, 6
+    n = chunk * per
+    out = {}
+    for sink_frames in (0, 3):
+        c = causal.KVCache((ring_frames + sink_frames) * per, sink_frames * per, fp8=True, chunk=chunk)
+        c.allocate(torch.zeros(1, n, heads, 8))
+        c.set_heads([1], heads)
+        slots, frame_of, place, anchors = [], [], [], []
+        for step in range(commits):
+            c.commit()
+            slots.append(np.full(n, -1) if c.last_slots is None else
+                         np.pad(c.last_slots.numpy(), (0, n - len(c.last_slots)), constant_values=-1))
+            frame_of.append(c.frame_of.numpy().copy())
+            place.append(c.place_in_frame.numpy().copy())
+            if c.full():
+                if not hasattr(c, "anchor_tokens"):  # as attend_split makes it on the first full pass
+                    c.anchor_tokens = torch.zeros(c.sink_tokens + c.per_frame, dtype=torch.int32)
+                    c.anchor_tokens[:c.sink_tokens] = torch.arange(c.sink_tokens, dtype=torch.int32)
+                c.place_anchor()
+                anchors.append(c.anchor_tokens.numpy().copy())
+            else:
+                anchors.append(np.full(c.sink_tokens + c.per_frame, -1, dtype=np.int32))
+        key = f"sink{sink_frames}"
+        out[key + "_slots"] = np.stack(slots)
+        out[key + "_frame_of"] = np.stack(frame_of)
+        out[key + "_place"] = np.stack(place)
+        out[key + "_anchors"] = np.stack(anchors)
+    save("kvcache.npz", **out)
+
+
 if __name__ == "__main__":
     if len(sys.argv) != 2:
         sys.exit("usage: python tests/golden/make_golden.py <wan-dit-lab checkout>")
     main(sys.argv[1])
+    kvcache_golden(sys.argv[1])

@@ -77,3 +77,33 @@ def test_forcing_applies_only_to_a_full_cache_with_static_heads():
         pass
     else:
         raise AssertionError("a head out of range must be refused")
+
+
+def test_cache_matches_reference_golden():
+    """Against the reference KVCache itself (tests/golden/kvcache.npz, made by tests/golden/make_golden.py): the
+    slots every commit fills, frame_of and place_in_frame after it, and the anchor rows once full."""
+    import numpy as np
+    from wan_dit_lab_b200.generation.causal import KVCache
+    d = np.load(Path(__file__).resolve().parent / "golden" / "kvcache.npz")
+    per, chunk, ring_frames, heads = 4, 3, 6, 2
+    n = chunk * per
+    for sink_frames in (0, 3):
+        key = f"sink{sink_frames}"
+        cache = KVCache((ring_frames + sink_frames) * per, sink_frames * per, n, heads, "cpu")
+        cache.set_heads([1], heads)
+        for step in range(d[key + "_slots"].shape[0]):
+            at = cache.saved
+            ring_before = cache.k[:, 0, 0].clone()
+            cache.k[at:at + n] = step + 1  # mark the chunk's rows
+            full = cache.full()
+            cache.commit(chunk, per)
+            want = d[key + "_slots"][step]
+            want = want[want >= 0]
+            if full:  # the chunk's token i went to ring slot want[i]
+                got = [int(cache.k[sink_frames * per + s, 0, 0]) for s in want]
+                assert got == [step + 1] * len(want)
+                assert not torch.equal(cache.k[:, 0, 0], ring_before)
+            np.testing.assert_array_equal(cache.frame_of.numpy(), d[key + "_frame_of"][step])
+            np.testing.assert_array_equal(cache.place_in_frame.numpy(), d[key + "_place"][step])
+            if d[key + "_anchors"][step][0] >= 0:
+                np.testing.assert_array_equal(cache.anchor_tokens.numpy(), d[key + "_anchors"][step])
