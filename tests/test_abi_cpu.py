@@ -118,3 +118,38 @@ def test_python_layer_raises_value_error(native):
     st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_E4M3, None, 128, 300, 256, FAKE, 512, None)
     with pytest.raises(ValueError, match="multiple of 256"):
         native.check(st)
+
+
+def test_new_entry_points_validate_before_any_launch(native):
+    """The tensor-parallel, low-rank, prescaled and Forcing-KV entry points reject bad calls up front."""
+    lib = native.lib()
+    err = lambda: lib.wdl_last_error()  # noqa: E731
+    st = lib.wdl_w4a4_gemm_f32(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, None, 0, 128, 256, 256, FAKE, 128,
+                               None)
+    assert st == native.ERR_ARGUMENT and b"ldo" in err()
+    st = lib.wdl_w4a4_gemm_add(FAKE, FAKE, FAKE, FAKE, native.CODES_E4M3, None, FAKE, 255, 128, 256, 256, FAKE, 256,
+                               None)
+    assert st == native.ERR_ARGUMENT and b"addend" in err()
+    st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, 128, 200, 256, FAKE, 256, None)
+    assert st == native.ERR_ARGUMENT and b"multiple of 128" in err()
+    assert lib.wdl_rows_sumsq(FAKE, 256, 4, 0, 1, 0, FAKE, None) == native.ERR_ARGUMENT
+    st = lib.wdl_residual_update(FAKE, 8, None, None, FAKE, 8, 4, 6, None)
+    assert st == native.ERR_ARGUMENT and b"multiple of 4" in err()
+    st = lib.wdl_qkv_prep_sharded(FAKE, 300, 16, 100, FAKE, FAKE, 1e-6, FAKE, 200, FAKE, 64, 4, 4, 0, FAKE, FAKE,
+                                  None, None, None, None, 0, 0, None)
+    assert st == native.ERR_ARGUMENT and b"multiple of 128" in err()
+    st = lib.wdl_rms_rows_sharded(FAKE, 256, 4, 256, FAKE, 1e-6, None, 512, FAKE, 256, None)
+    assert st == native.ERR_ARGUMENT and b"norm_dim" in err()
+    work = lib.wdl_sage_attend_workspace(64, 128, 2)
+    st = lib.wdl_sage_attend_maps(FAKE, 256, 64, FAKE, FAKE, FAKE, FAKE, 128, 4, None, None, 64, FAKE, native.F32, 256,
+                                  FAKE, native.BF16, 256, 64, 2, 0.088, FAKE, 256, FAKE, work, None)
+    assert st == native.ERR_ARGUMENT and b"head map" in err()
+    st = lib.wdl_sage_attend_maps(FAKE, 256, 64, FAKE, FAKE, FAKE, FAKE, 32, 2, None, None, 64, FAKE, native.F32, 256,
+                                  FAKE, native.BF16, 256, 64, 2, 0.088, FAKE, 256, FAKE, work, None)
+    assert st == native.ERR_ARGUMENT and b"cache_rows" in err()
+    st = lib.wdl_ln_quant_keep(FAKE, native.F32, 1024, 4, 1024, 1e-6, None, None, 0, None, None, None, native.F16,
+                               native.CODES_F16_PRE, FAKE, FAKE, None, 0, None)
+    assert st == native.ERR_ARGUMENT and b"bf16" in err()
+    st = lib.wdl_w4a4_quantize_rows(FAKE, native.BF16, 256, None, 4, 256, native.F16, native.CODES_F16_PRE, FAKE, FAKE,
+                                    None, None)
+    assert st == native.ERR_ARGUMENT and b"bf16" in err()
