@@ -16,6 +16,10 @@ What each file holds and which reference code made it:
   kv_attend.npz         generation/causal.py:193-273 KVCache(fp8=True).attend (exact SDPA over the cache
                         read back from FP8, the chunk unquantized)
   block.npz             models/block.py:22-29 WanBlock (nn.Linear, float32) on a small seeded block
+  kvcache.npz           generation/causal.py:160-337 KVCache bookkeeping (ring slots, eviction, anchors)
+  block_pack_layout.json  quantization/w4a4.py:269-313 layers() and pack_layout() of a small WanBlock, the
+                        reference's own functions run with its quantize replaced by one that returns zero tensors
+                        of this build's part shapes (its Nunchaku packer is not in the tree), on the CPU
 """
 
 import os
@@ -221,8 +225,49 @@ def kvcache_golden(reference):
     save("kvcache.npz", **out)
 
 
+def block_pack_golden(reference):
+    """The reference's pack layout rule (quantization/w4a4.py:269-313) on a WanBlock(256, 512, 2 heads): its
+    parameter names and shapes, layers() fused and not, and pack_layout() for packs v1 and v2, rank 32 and 0, with
+    and without a layer kept in bfloat16. pack_layout quantizes a zero weight on the GPU to learn the parts'
+    shapes; here its quantize is a stand-in returning zero tensors of this build's logical parts (qweight
+    [N, K/2] uint8, wscales [K/64, N], proj_down [K, r], proj_up [N, r], smooth [K], bias [N] in bfloat16) and
+    its torch.zeros ignores the device, so the rule runs unchanged on the CPU."""
+    import json
+    import types
+    sys.path.insert(0, str(Path(reference) / "src"))
+    from wan_dit_lab.models.block import WanBlock
+    from wan_dit_lab.quantization import w4a4
+    block = WanBlock(256, 512, 2, 1e-6)
+    bf = torch.bfloat16
+
+    def stand_in(W, b=None, smooth=None, rank=32, **_):
+        N, K = W.shape
+        return dict(qweight=torch.zeros(N, K // 2, dtype=torch.uint8), wscales=torch.zeros(K // 64, N, dtype=bf),
+                    proj_down=torch.zeros(K, rank, dtype=bf), proj_up=torch.zeros(N, rank, dtype=bf),
+                    smooth=torch.zeros(K, dtype=bf), bias=torch.zeros(N, dtype=bf))
+
+    shim = types.ModuleType("torch_zeros_on_cpu")
+    shim.__dict__.update(torch.__dict__)
+    shim.zeros = lambda *a, device=None, **k: torch.zeros(*a, **k)
+    saved = w4a4.torch, w4a4.quantize
+    w4a4.torch, w4a4.quantize = shim, stand_in
+    try:
+        cases = []
+        for fused, rank, keep in ((False, 32, ()), (True, 32, ()), (True, 0, ()), (True, 16, ("cross_attn.k",))):
+            layout, size = w4a4.pack_layout(block, fused, rank, keep)
+            cases.append(dict(fused=fused, rank=rank, keep=list(keep), layout=layout, bytes_per_block=size))
+    finally:
+        w4a4.torch, w4a4.quantize = saved
+    out = dict(dim=256, ffn_dim=512, parameters=[[n, list(p.shape)] for n, p in block.named_parameters()],
+               layers={str(f): {g: [n for n, _ in m] for g, m in w4a4.layers(block, f).items()} for f in (False, True)},
+               cases=cases)
+    (HERE / "block_pack_layout.json").write_text(json.dumps(out, indent=1), encoding="utf-8")
+    print(f"block_pack_layout.json: {len(out['parameters'])} parameters, {len(cases)} layouts")
+
+
 if __name__ == "__main__":
     if len(sys.argv) != 2:
         sys.exit("usage: python tests/golden/make_golden.py <wan-dit-lab checkout>")
     main(sys.argv[1])
     kvcache_golden(sys.argv[1])
+    block_pack_golden(sys.argv[1])

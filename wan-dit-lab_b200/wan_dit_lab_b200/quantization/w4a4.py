@@ -15,6 +15,7 @@ nibble is unpacked inside the GEMM's main loop.
 """
 
 import math
+from pathlib import Path
 
 import torch
 
@@ -365,3 +366,289 @@ class PackedW4A4GeluMLP(torch.nn.Module):
     def forward(self, X):
         y = w4a4_gelu_mlp(X.reshape(-1, X.shape[-1]).to(torch.bfloat16).contiguous(), *self.parts)
         return y.reshape(*X.shape[:-1], self.out_features)
+
+
+# ---- block packs: the W4A4 tensors of every block as one uint8 row per block, mapped read-only
+# (reference w4a4.py:264-416). The file is the reference's: rows of bytes_per_block bytes, every entry 16-byte
+# aligned at the offset the manifest (<pack>.json) gives, named "<layer>.<part>" for a W4A4 layer and by the
+# parameter's name for the rest (bfloat16). What differs is the byte order of the parts: the logical one of
+# quantize here, recorded as "packing": "logical" in the manifest; the reference's packs hold Nunchaku's
+# MMA-tile order (its packer, nunchaku/lora/flux/packer.py at 302e0e9, is not in the reference tree) and are
+# refused by mapped_pack rather than misread.
+
+FORMATS = ("block_w4a4_v1", "block_w4a4_v2")  # w4a4.py:30: a layer per nn.Linear; v2 fuses q, k, v and the FFN
+PACKING = "logical"
+QKV = ("self_attn.q", "self_attn.k", "self_attn.v")  # w4a4.py:265: one layer self_attn.qkv in a fused pack
+FFN = ("ffn.0", "ffn.2")  # w4a4.py:266: one gelu_mlp in a fused pack
+FUSED_LAYERS = ("self_attn.qkv", "self_attn.o", "cross_attn.q", "cross_attn.k", "cross_attn.v", "cross_attn.o",
+                "ffn.0", "ffn.2")  # the W4A4 layers of a block_w4a4_v2 row, which the B200 block runs
+
+
+class BlockShape:
+    """The shape of a Wan block for the pack functions when no block is at hand: model width, feed-forward width,
+    the norms' eps."""
+
+    def __init__(self, dim, ffn_dim, eps=1e-6):
+        self.dim, self.ffn_dim, self.eps = dim, ffn_dim, eps
+
+
+def block_parameters(dim, ffn_dim):
+    """[(name, shape)] of a WanBlock's parameters in named_parameters order (reference models/block.py:13-20,
+    models/multi_head_attention.py:13-18): the block's own modulation [1, 6, dim] first, then per attention the q,
+    k, v, o weights and biases, norm_q and norm_k; the feed forward; norm3's weight and bias (norm1 and norm2
+    have none)."""
+    out = [("modulation", (1, 6, dim))]
+    for attention in ("self_attn", "cross_attn"):
+        for linear in "qkvo":
+            out += [(f"{attention}.{linear}.weight", (dim, dim)), (f"{attention}.{linear}.bias", (dim,))]
+        out += [(f"{attention}.norm_q.weight", (dim,)), (f"{attention}.norm_k.weight", (dim,))]
+    out += [("ffn.0.weight", (ffn_dim, dim)), ("ffn.0.bias", (ffn_dim,)), ("ffn.2.weight", (dim, ffn_dim)),
+            ("ffn.2.bias", (dim,)), ("norm3.weight", (dim,)), ("norm3.bias", (dim,))]
+    return out
+
+
+def _state(block):
+    """{name: tensor} of a block given as a module (named_parameters) or as a state dict."""
+    return dict(block.named_parameters()) if hasattr(block, "named_parameters") else dict(block)
+
+
+def _parameters(like):
+    """[(name, shape)] of the block `like`, in registration order: a module's named_parameters (the reference's
+    WanBlock, on the meta device too), BlockShape, or a WanBlock state dict (any order; checked name by name)."""
+    if hasattr(like, "named_parameters"):
+        return [(name, tuple(p.shape)) for name, p in like.named_parameters()]
+    if isinstance(like, BlockShape):
+        return block_parameters(like.dim, like.ffn_dim)
+    state = dict(like)
+    if "modulation" not in state or "ffn.0.weight" not in state:
+        raise ValueError("a WanBlock state dict needs modulation and ffn.0.weight")
+    want = block_parameters(state["modulation"].shape[-1], state["ffn.0.weight"].shape[0])
+    numel = lambda shape: math.prod(shape)  # noqa: E731
+    if set(state) != {name for name, _ in want} or any(state[n].numel() != numel(s) for n, s in want):
+        raise ValueError("the state dict does not hold a WanBlock's parameters: "
+                         f"{sorted(set(state) ^ {name for name, _ in want})[:4]}")
+    return want
+
+
+def layers(block, fused=False, keep=()):
+    """{layer: [names of the nn.Linear it is made of, stacked by output]} of a Wan block (reference
+    w4a4.py:269-276): every weight of two dimensions is a linear layer's; fused takes q, k, v of self-attention as
+    one layer self_attn.qkv; keep: names of linears left in bfloat16."""
+    out = {}
+    for name, shape in _parameters(block):
+        if name.endswith(".weight") and len(shape) == 2 and name[:-7] not in keep:
+            linear = name[:-7]
+            out.setdefault("self_attn.qkv" if fused and linear in QKV else linear, []).append(linear)
+    return out
+
+
+def part_shapes(N, K, rank, scale_dtype=torch.bfloat16):
+    """{part: (dtype name, shape, bytes)} of quantize's tensors for a weight [N, K] at `rank`, in PARTS order."""
+    if K % GROUP:
+        raise ValueError(f"a W4A4 layer's input width must be a multiple of {GROUP}, got {K}")
+    scale = str(scale_dtype).removeprefix("torch.")
+    size = torch.empty(0, dtype=scale_dtype).element_size()
+    return dict(qweight=("uint8", (N, K // 2), N * K // 2), wscales=(scale, (K // GROUP, N), K // GROUP * N * size),
+                proj_down=("bfloat16", (K, rank), K * rank * 2), proj_up=("bfloat16", (N, rank), N * rank * 2),
+                smooth=("bfloat16", (K,), K * 2), bias=("bfloat16", (N,), N * 2))
+
+
+def pack_layout(block, fused=False, rank=32, keep=(), scale_dtype=torch.bfloat16):
+    """(layout, bytes per row) of a block's pack row (reference w4a4.py:279-313): entries dict(name, dtype, shape,
+    offset, bytes) in the block's parameter order, a W4A4 layer's six parts where its first member's weight is
+    (its biases are the part bias), every other parameter in bfloat16; each entry starts 16-byte aligned. In a
+    fused pack the second feed-forward layer's parts carry gelu_mlp: True (made for GELU's shifted output)."""
+    params = _parameters(block)
+    groups = layers(block, fused, keep)
+    group_of = {member: g for g, members in groups.items() for member in members}
+    shapes = dict(params)
+    layout, offset = [], 0
+
+    def add(name, dtype, shape, size, **extra):
+        nonlocal offset
+        layout.append(dict(name=name, dtype=dtype, shape=list(shape), offset=offset, bytes=size, **extra))
+        offset += -(-size // 16) * 16
+
+    for name, shape in params:
+        owner = name.rsplit(".", 1)[0]
+        g = group_of.get(owner)
+        if g is None:
+            add(name, "bfloat16", shape, math.prod(shape) * 2)
+        elif name.endswith(".weight") and groups[g][0] == owner:
+            N = sum(shapes[f"{member}.weight"][0] for member in groups[g])
+            extra = {"gelu_mlp": True} if fused and g == FFN[1] else {}
+            for part, (dtype, part_shape, size) in part_shapes(N, shape[1], rank, scale_dtype).items():
+                add(f"{g}.{part}", dtype, part_shape, size, **extra)
+    return layout, offset
+
+
+@torch.no_grad()
+def layer_parts(block, index, amax, alpha=0.5, rank=32, fused=False, keep=(), hessians=None, rule="max",
+                scale_dtype=torch.bfloat16, device="cuda"):
+    """{layer: quantize tensors} of block number `index` (reference w4a4.py:316-333), quantized on `device`: the
+    members' weights stacked by output, the smoothing from amax {"<index>.<first member>": largest |x| of each input
+    channel} (SmoothQuant, alpha); in a fused pack the second feed-forward layer is made for gelu_mlp's shifted
+    input (its smoothing from amax + GELU_SHIFT)."""
+    state = _state(block)
+    out = {}
+    for g, members in layers(block, fused, keep).items():
+        W = torch.cat([state[f"{m}.weight"].detach().to(device, torch.float32) for m in members])
+        biases = [state.get(f"{m}.bias") for m in members]
+        b = None
+        if any(x is not None for x in biases):
+            b = torch.cat([torch.zeros(state[f"{m}.weight"].shape[0], device=device) if x is None else
+                           x.detach().to(device, torch.float32) for m, x in zip(members, biases)])
+        shift = GELU_SHIFT if fused and g == FFN[1] else 0.0
+        a = amax.get(f"{index}.{members[0]}")  # the members share their input
+        s = None if a is None else smoothing(a.to(device) + shift, W, alpha)
+        H = None if hessians is None else hessians.get(g)
+        out[g] = quantize(W, b, smooth=s, rank=rank, shift=shift, hessian=H, rule=rule, scale_dtype=scale_dtype)
+    return out
+
+
+def _put(row, entry, tensor, exact_shape):
+    """tensor's bytes into row at entry's place; the dtype and shape (or, for a raw parameter, the element count)
+    must be the entry's."""
+    if exact_shape and (str(tensor.dtype).removeprefix("torch.") != entry["dtype"] or
+                        list(tensor.shape) != entry["shape"]):
+        raise ValueError(f"{entry['name']}: {tensor.dtype} {list(tensor.shape)} where the layout has "
+                         f"{entry['dtype']} {entry['shape']}")
+    data = tensor.detach().contiguous().cpu().reshape(-1).view(torch.uint8)
+    if data.numel() != entry["bytes"]:
+        raise ValueError(f"{entry['name']}: {data.numel()} bytes where the layout has {entry['bytes']}")
+    row[entry["offset"]:entry["offset"] + entry["bytes"]] = data
+
+
+@torch.no_grad()
+def build_pack(blocks, amax, path, source, alpha=0.5, rank=32, fused=False, keep=(), hessians=None, rule="max",
+               scale_dtype=torch.bfloat16, parts=None):
+    """The blocks (modules or state dicts with WanBlock's names) as a pack at `path`, one uint8 row per block
+    (pack_layout), and its manifest <path>.json (reference w4a4.py:336-394): block_w4a4_v2 when fused, else
+    block_w4a4_v1. Written to <path>.tmp, synced, then renamed; nothing is left behind on failure, and an existing
+    pack, manifest or temporary file is never overwritten (FileExistsError). parts: per block the W4A4 tensors
+    already made ({layer: quantize tensors}, e.g. WanBlockB200.parts), instead of quantizing here."""
+    import hashlib
+    import json
+    import os
+
+    from wan_dit_lab_b200.quantization.weight_pack import source_identity
+    path = Path(path)
+    manifest, temporary = path.with_suffix(path.suffix + ".json"), path.with_suffix(path.suffix + ".tmp")
+    if any(p.exists() for p in (path, manifest, temporary)):
+        raise FileExistsError(path)
+    layout, size = pack_layout(blocks[0], fused, rank, keep, scale_dtype)
+    groups = layers(blocks[0], fused, keep)
+    where = {e["name"]: e for e in layout}
+    digest, identity = hashlib.sha256(), source_identity(source)
+    try:
+        with temporary.open("xb") as stream:
+            for index, block in enumerate(blocks):
+                if pack_layout(block, fused, rank, keep, scale_dtype) != (layout, size):
+                    raise ValueError("Packed blocks must share one layout")
+                state = _state(block)
+                tensors = parts[index] if parts is not None else layer_parts(
+                    state, index, amax, alpha, rank, fused, keep, None if hessians is None else hessians(index), rule,
+                    scale_dtype)
+                if set(tensors) != set(groups):
+                    raise ValueError(f"block {index}: W4A4 tensors for {sorted(tensors)}, the layout has "
+                                     f"{sorted(groups)}")
+                row = torch.zeros(size, dtype=torch.uint8)
+                written = set()
+                for g, t in tensors.items():
+                    for part in PARTS:
+                        _put(row, where[f"{g}.{part}"], t[part], True)
+                        written.add(f"{g}.{part}")
+                for e in layout:  # the rest in bfloat16; a W4A4 layer's bias is one of its parts
+                    if e["name"] in state and e["name"] not in written:
+                        _put(row, e, state[e["name"]].detach().to(torch.bfloat16), False)
+                payload = row.numpy().tobytes()
+                digest.update(payload)
+                stream.write(payload)
+            stream.flush()
+            os.fsync(stream.fileno())
+        if source_identity(source) != identity:
+            raise RuntimeError("Checkpoint changed during conversion")
+        os.replace(temporary, path)
+        metadata = dict(format=FORMATS[1] if fused else FORMATS[0], packing=PACKING, blocks=len(blocks), layout=layout,
+                        bytes_per_block=size, bytes=size * len(blocks), sha256=digest.hexdigest(), source=identity,
+                        alpha=alpha, rank=rank, calibrated=sorted(amax), bfloat16_layers=sorted(keep),
+                        rounding="nearest", scale_rule=rule,
+                        quantization="SVDQuant W4A4: INT4 groups of 64, low-rank branch of rank r in bfloat16, "
+                        "SmoothQuant smoothing from calibrated activation maxima; parts in logical order"
+                        + ("; q, k, v of self-attention as one layer, feed forward as the fused GELU MLP (unsigned "
+                           "INT4 hidden activation shifted by 0.171875)" if fused else ""))
+        manifest.write_text(json.dumps(metadata, indent=1), encoding="utf-8")
+        return {k: v for k, v in metadata.items() if k not in ("layout", "calibrated")}
+    except BaseException:
+        temporary.unlink(missing_ok=True)
+        path.unlink(missing_ok=True)
+        manifest.unlink(missing_ok=True)
+        raise
+
+
+def mapped_pack(blocks, path, source):
+    """(rows uint8 [blocks, bytes per block] over the file mapped read-only, layout) of a pack (reference
+    w4a4.py:397-414). blocks: the model's blocks (a sequence) or their number. ValueError when the manifest names
+    another checkpoint or format, when the parts are not in this build's logical order, or when the file is not
+    blocks x bytes_per_block long."""
+    import json
+    import warnings
+
+    import numpy as np
+
+    from wan_dit_lab_b200.quantization.weight_pack import source_identity
+    path = Path(path)
+    metadata = json.loads(path.with_suffix(path.suffix + ".json").read_text(encoding="utf-8"))
+    if metadata["format"] not in FORMATS or metadata["source"] != source_identity(source):
+        raise ValueError("Weight pack has a different checkpoint or format")
+    if metadata.get("packing") != PACKING:
+        raise ValueError("W4A4 weight pack holds its parts in Nunchaku's MMA-tile order (the reference's packer); "
+                         "this build reads packs in the logical order that build_pack writes")
+    count = blocks if isinstance(blocks, int) else len(blocks)
+    size = metadata["bytes_per_block"]
+    if metadata["blocks"] != count or path.stat().st_size != size * count or count == 0:
+        raise ValueError("W4A4 weight pack is incomplete")
+    data = np.memmap(path, dtype=np.uint8, mode="r")
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", UserWarning)  # a read-only mapping: torch warns that it is not writable
+        return torch.from_numpy(data).reshape(count, size), metadata["layout"]
+
+
+def slot_parts(row, layout):
+    """(parts {layer: {part: tensor}}, params {name: tensor}) of a pack row: views of `row`, no copy, each entry at
+    its offset with its dtype and shape."""
+    def view(e):
+        return row[e["offset"]:e["offset"] + e["bytes"]].view(getattr(torch, e["dtype"])).view(e["shape"])
+
+    entries = {e["name"]: e for e in layout}
+    names = [e["name"][:-len(".qweight")] for e in layout if e["name"].endswith(".qweight")]
+    parts = {g: {part: view(entries[f"{g}.{part}"]) for part in PARTS} for g in names}
+    taken = {f"{g}.{part}" for g in names for part in PARTS}
+    return parts, {e["name"]: view(e) for e in layout if e["name"] not in taken}
+
+
+def slot(row, like, layout, code_format=None):
+    """The block of a block_w4a4_v2 pack row as a WanBlockB200 (reference w4a4.py:399-416, which builds a module over
+    the row): a row on the host is copied to the current GPU once, the parts are views of that copy, and each layer
+    is prepared in the kernels' layout. like: the block's eps (from a WanBlock or a BlockShape; None: 1e-6). The
+    shapes come from the layout. Refused (ValueError): block_w4a4_v1 rows and rows that keep layers in bfloat16,
+    since the B200 block runs q, k, v as one W4A4 layer and the feed forward as the fused GELU MLP, whose second
+    layer is quantized for GELU's shifted output."""
+    from wan_dit_lab_b200.models.block import HEAD_DIM, WanBlockB200
+    kept = [e["name"][:-7] for e in layout if e["name"].endswith(".weight") and len(e["shape"]) == 2]
+    if kept:
+        raise ValueError(f"the B200 block runs every linear layer in W4A4; this pack keeps {kept} in bfloat16")
+    gelu = all(e.get("gelu_mlp") for e in layout if e["name"].startswith(FFN[1] + "."))
+    names = [e["name"][:-len(".qweight")] for e in layout if e["name"].endswith(".qweight")]
+    if sorted(names) != sorted(FUSED_LAYERS) or not gelu:
+        raise ValueError("a block_w4a4_v1 row (a layer per nn.Linear) cannot drive the B200 block, which runs q, k, "
+                         "v as one W4A4 layer and the feed forward as the fused GELU MLP: pack with fused=True")
+    if not row.is_cuda:
+        row = row.to("cuda")
+    parts, params = slot_parts(row, layout)
+    dim = params["modulation"].numel() // 6
+    eps = getattr(like, "eps", None)
+    if eps is None and hasattr(like, "norm1"):
+        eps = like.norm1.eps
+    return WanBlockB200(params, dim, parts["ffn.0"]["qweight"].shape[0], dim // HEAD_DIM,
+                        1e-6 if eps is None else eps, device=row.device, parts=parts, code_format=code_format)
