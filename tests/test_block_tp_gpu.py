@@ -2,7 +2,7 @@
 in lock step (run_lockstep sums what they yield, as the NCCL all-reduce does across GPUs), on the same packed
 weights, inputs, prompt and FP8 cache. The shards' residual streams are equal to each other bit for bit and to
 the whole block's within relative L2 1e-3 of the block's update (float32 sums in another order: the row-parallel
-partial products and the RMS statistics), their cache rows equal the whole cache's heads in >= 99.9 % of bytes.
+partial products, the low-rank branches' shares and the RMS statistics), their cache rows equal the whole cache's heads in >= 99.9 % of bytes.
 Also the kernels the split adds: fp32 partial GEMMs (their sum is the whole product; partial + wdl_residual_update
 equals the residual epilogue bit for bit), column counts that are multiples of 128 in the folded GEMM, sharded RMS
 statistics."""
@@ -43,21 +43,32 @@ def rel(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-@pytest.mark.parametrize("dim,heads,ffn,world,frames,h,w,at,text", [
-    (1024, 8, 4096, 2, 2, 4, 8, 128, 32),
-    (1024, 8, 4096, 4, 2, 4, 8, 128, 32),
-    (3072, 24, 14336, 8, 2, 4, 16, 256, 64),
+@pytest.mark.parametrize("dim,heads,ffn,world,frames,h,w,at,text,rank", [
+    (1024, 8, 4096, 2, 2, 4, 8, 128, 32, 0),
+    (1024, 8, 4096, 4, 2, 4, 8, 128, 32, 0),
+    (3072, 24, 14336, 8, 2, 4, 16, 256, 64, 0),
+    (1024, 8, 4096, 2, 2, 4, 8, 128, 32, 32),
+    (1024, 8, 4096, 4, 2, 4, 8, 128, 32, 32),
 ])
-def test_tp_block_matches_whole_block(dim, heads, ffn, world, frames, h, w, at, text):
-    from wan_dit_lab_b200.models.block import Buffers, WanBlockB200, quantize_block
+def test_tp_block_matches_whole_block(dim, heads, ffn, world, frames, h, w, at, text, rank):
+    """rank 32: SVDQuant low-rank branches and smoothing on every layer; the row shards' shares of each branch
+    are summed with their partial products."""
+    import sys
+    from pathlib import Path
+    from wan_dit_lab_b200.models.block import WanBlockB200, quantize_block
     from wan_dit_lab_b200.models.block_tp import WanBlockTP, run_lockstep
     _native = native()
     n = frames * h * w
     state = random_state(dim, ffn, 11)
-    parts = quantize_block({k: v.cuda() for k, v in state.items()})
+    if rank:
+        sys.path.insert(0, str(Path(__file__).resolve().parent))
+        from test_block_gpu import lowrank_parts
+        parts = lowrank_parts(state, rank, 13)
+    else:
+        parts = quantize_block({k: v.cuda() for k, v in state.items()})
     whole = WanBlockB200(state, dim, ffn, heads, parts=parts)
     shards = [WanBlockTP(state, dim, ffn, heads, r, world, parts=parts) for r in range(world)]
-    assert all(s.code_format == whole.code_format for s in shards)
+    assert all(s.code_format == whole.code_format and s.lowrank == bool(rank) for s in shards)
     g = torch.Generator().manual_seed(12)
     X = torch.randn(n, dim, generator=g).cuda()
     time_in = (torch.randn(6, dim, generator=g) * 0.1).cuda()
@@ -71,7 +82,7 @@ def test_tp_block_matches_whole_block(dim, heads, ffn, world, frames, h, w, at, 
 
     Xw = X.clone()
     whole_cache = [t.clone() for t in cache]
-    buf = Buffers(n, dim, ffn, heads, at + n, text, "cuda")
+    buf = whole.buffers(n, at + n, text, "cuda")
     whole.forward(Xw, whole.modulation_of(time_in), (*whole_cache, cap), at, freq, grid, start, whole.cross_kv(ctx),
                   buf)
 
@@ -90,13 +101,70 @@ def test_tp_block_matches_whole_block(dim, heads, ffn, world, frames, h, w, at, 
     for xr in xs[1:]:
         assert torch.equal(xr, xs[0])
     err = rel((xs[0] - X).cpu().numpy(), (Xw - X).cpu().numpy())
-    print(f"world {world}: block update vs whole block, relative L2 {err:.2e}")
+    print(f"world {world}, rank {rank}: block update vs whole block, relative L2 {err:.2e}")
     assert err <= 1e-3
     for r, c in enumerate(caches):
         for i in (0, 2):
             got = c[i][at:at + n].cpu()
             ref = whole_cache[i][at:at + n, r * hl:(r + 1) * hl].cpu()
             assert (got == ref).float().mean() >= 0.999
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_block_with_forcing_kv_split_matches_whole_block(world):
+    """Forcing-KV's head split on shards: each shard attends with the static heads among its own (renumbered),
+    the others to the whole window; the result equals the whole block's with the same split within relative L2
+    1e-3 of the update, and the shards' residual streams are equal bit for bit."""
+    from wan_dit_lab_b200.models.block import WanBlockB200, quantize_block
+    from wan_dit_lab_b200.models.block_tp import WanBlockTP, run_lockstep
+    _native = native()
+    dim, heads, ffn, frames, h, w, at, text = 1024, 8, 4096, 2, 4, 8, 192, 32
+    n = frames * h * w
+    state = random_state(dim, ffn, 15)
+    parts = quantize_block({k: v.cuda() for k, v in state.items()})
+    g = torch.Generator().manual_seed(16)
+    X = torch.randn(n, dim, generator=g).cuda()
+    time_in = (torch.randn(6, dim, generator=g) * 0.1).cuda()
+    ctx = torch.randn(text, dim, generator=g).to(torch.bfloat16).cuda()
+    cap = at + n
+    ck8, cks = of.quantize_rows((torch.randn(1, cap, heads, 128, generator=g) + 0.3).numpy())
+    cv8, cvs = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    cache = [torch.from_numpy(a).cuda() for a in (ck8[0], cks[0, ..., 0], cv8[0], cvs[0, ..., 0])]
+    freq = torch.from_numpy(orope.table(1024).astype(np.float32)).cuda()
+    grid, start = (frames, h, w), at // (h * w)
+    anchors = torch.cat([torch.arange(32), torch.arange(at - 32, at)]).to(torch.int32).cuda()  # a sink, a frame
+    static = [1, 5, 6]
+
+    def split(heads_here, first):
+        st = [x - first for x in static if first <= x < first + heads_here]
+        dy = [x for x in range(heads_here) if x not in st]
+        as_int = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
+        return as_int(st), as_int(dy), anchors
+
+    whole = WanBlockB200(state, dim, ffn, heads, parts=parts)
+    Xw = X.clone()
+    whole.forward(Xw, whole.modulation_of(time_in), (*[t.clone() for t in cache], cap), at, freq, grid, start,
+                  whole.cross_kv(ctx), whole.buffers(n, cap, text, "cuda"), forcing=split(heads, 0))
+    plain = X.clone()
+    whole.forward(plain, whole.modulation_of(time_in), (*[t.clone() for t in cache], cap), at, freq, grid, start,
+                  whole.cross_kv(ctx), whole.buffers(n, cap, text, "cuda"))
+    hl = heads // world
+    xs, gens = [], []
+    for r in range(world):
+        blk = WanBlockTP(state, dim, ffn, heads, r, world, parts=parts)
+        c = [t[:, r * hl:(r + 1) * hl].contiguous() for t in cache]
+        xr = X.clone()
+        xs.append(xr)
+        gens.append(blk.steps(xr, blk.modulation_of(time_in), (*c, cap), at, freq, grid, start, blk.cross_kv(ctx),
+                              blk.buffers(n, cap, text, "cuda"), forcing=split(hl, r * hl)))
+    run_lockstep(gens)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    for xr in xs[1:]:
+        assert torch.equal(xr, xs[0])
+    d_tp, d_whole = (xs[0] - X).cpu().numpy(), (Xw - X).cpu().numpy()
+    assert rel(d_tp, d_whole) <= 1e-3
+    assert rel((plain - X).cpu().numpy(), d_whole) > 2e-3  # the split changed the block's output
 
 
 def quantized_operands(M, N, K, seed, fmt):

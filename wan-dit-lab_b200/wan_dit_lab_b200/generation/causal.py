@@ -300,8 +300,14 @@ class Stream:
         self.caches = [KVCache((max_frames - chunk) * self.tokens, sink_frames * self.tokens, n, heads, model.device)
                        for _ in model.blocks]
         if static_heads:  # Forcing-KV: {block: [static heads]} (reference Stream, causal.py:490-494)
+            # in the model's head numbers; a tensor-parallel shard keeps those of its heads, renumbered
+            first = getattr(model.blocks[0], "rank", 0) * heads
+            total = heads * getattr(model.blocks[0], "world", 1)
             for index, cache in enumerate(self.caches):
-                cache.set_heads(static_heads.get(index, static_heads.get(str(index), [])), heads)
+                static = list(static_heads.get(index, static_heads.get(str(index), [])))
+                if any(h < 0 or h >= total for h in static):
+                    raise ValueError("static heads out of range")
+                cache.set_heads([h - first for h in static if first <= h < first + heads], heads)
         self.freq = rope_table(positions).to(model.device)
         # the chunk's table: its frames' time angles in rows 0.. (the kernels run with start 0), height / width
         # angles as in the whole table (reference Stream's chunk_freqs), refreshed in place before every chunk

@@ -83,6 +83,35 @@ def quantize_block(p, scale_dtype=torch.bfloat16):
     return parts
 
 
+def attend_forcing(buf, n, H, cache, at, forcing):
+    """Self-attention of a chunk with Forcing-KV's head split (reference causal.py:222-240), over the H heads this
+    process holds (buf.q / buf.k float32 [n, H 128], the chunk's values in buf.qkv[:, 2 H 128:], output buf.attn):
+    forcing = (static, dynamic, anchor rows) int32 device tensors in this process's head numbers. The dynamic
+    heads attend to the cached window [0, at) and the chunk, the static heads to the anchor rows (the sink and the
+    newest finished frame) and the chunk, each group through the attention's head / token maps
+    (wdl_sage_attend_maps) on gathered copies of its heads' queries, keys and values."""
+    lib, st = _native.lib(), _native.stream()
+    ck, cks, cv, cvs, capacity = cache
+    static, dynamic, anchors = forcing
+    width = H * HEAD_DIM
+    heads_of = lambda t, idx: t.view(n, H, HEAD_DIM).index_select(1, idx).reshape(n, -1)  # noqa: E731
+    out = buf.attn[:n].view(n, H, HEAD_DIM)
+    for idx, tokens, length in ((dynamic, None, at), (static, anchors, anchors.numel())):
+        if idx.numel() == 0:
+            continue
+        il = idx.long()
+        q_s, k_s = heads_of(buf.q[:n], il).contiguous(), heads_of(buf.k[:n], il).contiguous()
+        v_s = heads_of(buf.qkv[:n, 2 * width:3 * width], il).contiguous()
+        hs = idx.numel()
+        o_s = torch.empty(n, hs * HEAD_DIM, dtype=torch.bfloat16, device=buf.attn.device)
+        _native.check(lib.wdl_sage_attend_maps(
+            q_s.data_ptr(), hs * HEAD_DIM, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(),
+            capacity, H, idx.data_ptr(), _native.ptr(tokens), length, k_s.data_ptr(), _native.F32,
+            hs * HEAD_DIM, v_s.data_ptr(), _native.BF16, hs * HEAD_DIM, n, hs, HEAD_DIM ** -0.5,
+            o_s.data_ptr(), hs * HEAD_DIM, buf.sage.data_ptr(), buf.sage.numel(), st))
+        out[:, il] = o_s.view(n, hs, HEAD_DIM)
+
+
 class CrossKV:
     """The keys and values of one block's cross-attention over a prompt, quantized for the Sage kernel."""
 
@@ -235,23 +264,7 @@ class WanBlockB200:
                 buf.k.data_ptr(), _native.F32, dim, buf.qkv.data_ptr() + 2 * dim * 2, _native.BF16, 3 * dim, n, H,
                 HEAD_DIM ** -0.5, buf.attn.data_ptr(), dim, buf.sage.data_ptr(), buf.sage.numel(), st))
         else:
-            static, dynamic, anchors = forcing
-            heads_of = lambda t, idx: t.view(n, H, HEAD_DIM).index_select(1, idx).reshape(n, -1)  # noqa: E731
-            out = buf.attn.view(n, H, HEAD_DIM)
-            for idx, tokens, length in ((dynamic, None, at), (static, anchors, anchors.numel())):
-                if idx.numel() == 0:
-                    continue
-                il = idx.long()
-                q_s, k_s = heads_of(buf.q, il).contiguous(), heads_of(buf.k, il).contiguous()
-                v_s = heads_of(buf.qkv[:, 2 * dim:], il).contiguous()
-                hs = idx.numel()
-                o_s = torch.empty(n, hs * HEAD_DIM, dtype=torch.bfloat16, device=X.device)
-                _native.check(lib.wdl_sage_attend_maps(
-                    q_s.data_ptr(), hs * HEAD_DIM, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(),
-                    capacity, H, idx.data_ptr(), _native.ptr(tokens), length, k_s.data_ptr(), _native.F32,
-                    hs * HEAD_DIM, v_s.data_ptr(), _native.BF16, hs * HEAD_DIM, n, hs, HEAD_DIM ** -0.5,
-                    o_s.data_ptr(), hs * HEAD_DIM, buf.sage.data_ptr(), buf.sage.numel(), st))
-                out[:, il] = o_s.view(n, hs, HEAD_DIM)
+            attend_forcing(buf, n, H, cache, at, forcing)
         keep("q", buf.q), keep("k", buf.k), keep("attn", buf.attn)
         quantize(buf.attn, L["self_attn.o"])
         gemm_residual(L["self_attn.o"], 2, add=lora(L["self_attn.o"], buf.attn))

@@ -30,7 +30,7 @@ all shards'), which is how the split is tested against the whole block on one GP
 import torch
 
 from wan_dit_lab_b200 import _native
-from wan_dit_lab_b200.models.block import HEAD_DIM, Buffers, CrossKV, WanBlockB200, _f32, quantize_block
+from wan_dit_lab_b200.models.block import HEAD_DIM, Buffers, CrossKV, WanBlockB200, _f32, attend_forcing, quantize_block
 from wan_dit_lab_b200.quantization import w4a4
 
 ROW_PARALLEL = ("self_attn.o", "cross_attn.o", "ffn.2")
@@ -111,7 +111,7 @@ def run_lockstep(gens):
 
 class WanBlockTP:
     """Shard `rank` of `world` of one Wan block (WanBlockB200's arguments and state-dict names; every linear W4A4,
-    rank 0). reduce: a callable summing a CUDA tensor in place across the shards (None: only steps() is used)."""
+    any rank, with smoothing). reduce: a callable summing a CUDA tensor in place across the shards (None: only steps() is used)."""
 
     def __init__(self, state, dim, ffn_dim, heads, rank, world, eps=1e-6, device="cuda", parts=None,
                  scale_dtype=torch.bfloat16, code_format=None, reduce=None):
@@ -131,8 +131,10 @@ class WanBlockTP:
         fmt = code_format or w4a4.CODE_FORMAT
         self.layers = {name: w4a4.PreparedW4A4(*(t[k] for k in w4a4.PARTS), code_format=fmt)
                        for name, t in shard.items()}
-        if any(layer.rank for layer in self.layers.values()):
-            raise NotImplementedError("the tensor-parallel block runs rank-0 W4A4 layers")
+        # SVDQuant low-rank branches: a column shard's branch is (x proj_down) proj_up_shard^T, its own output
+        # columns; a row shard's, (x_shard proj_down_shard) proj_up^T, is a share of the whole branch that enters the
+        # shard's fp32 partial and is summed with the partials across shards
+        self.lowrank = any(layer.rank for layer in self.layers.values())
         if len({layer.code_format for layer in self.layers.values()}) > 1:
             self.layers = {name: w4a4.PreparedW4A4(*(t[k] for k in w4a4.PARTS), code_format="e4m3")
                            for name, t in shard.items()}
@@ -147,8 +149,11 @@ class WanBlockTP:
         self.modulation = _f32(p["modulation"]).reshape(6, dim)
         self.act_scale_dtype = _native.BF16
 
-    def buffers(self, n, max_keys, text_tokens, device, lowrank=False):
-        return Buffers(n, self.dim, self.local_ffn, self.kv_heads, max_keys, text_tokens, device, sharded=True)
+    def buffers(self, n, max_keys, text_tokens, device, lowrank=None):
+        """WanBlockB200.buffers for this shard's heads and hidden channels, with the partials and statistics that
+        are summed across shards."""
+        return Buffers(n, self.dim, self.local_ffn, self.kv_heads, max_keys, text_tokens, device, sharded=True,
+                       lowrank=self.lowrank if lowrank is None else lowrank)
 
     def modulation_of(self, time_in):
         return WanBlockB200.modulation_of(self, time_in)
@@ -184,17 +189,16 @@ class WanBlockTP:
 
     def forward(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, trace=None, forcing=None):
         """WanBlockB200.forward on this shard: every tensor steps() yields is summed across shards by reduce."""
-        if forcing is not None:
-            raise NotImplementedError("Forcing-KV's head split runs on the single-GPU block")
         if self.reduce is None:
             raise RuntimeError("a tensor-parallel block needs a reduce callable (or run_lockstep over its steps)")
-        for t in self.steps(X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16):
+        for t in self.steps(X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16, forcing):
             self.reduce(t)
         return X
 
-    def steps(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False):
+    def steps(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, forcing=None):
         """The block on this shard's heads and hidden channels (WanBlockB200.forward's arguments; cache holds this
-        shard's heads). Yields, in order: the q / k sums of squares [n, 2], the self-attention O partial [n, dim],
+        shard's heads, forcing its Forcing-KV split in this shard's head numbers, which changes no collective).
+        Yields, in order: the q / k sums of squares [n, 2], the self-attention O partial [n, dim],
         the cross query's sums of squares [n], the cross O partial, the FFN-2 partial; each must hold the sum over
         shards when the generator resumes."""
         lib, st = _native.lib(), _native.stream()
@@ -214,16 +218,21 @@ class WanBlockTP:
             e1.record()
             timer(e0, e1, 2 * n * layer.N * layer.K)
 
-        def gemm(layer, out):
-            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm(
-                buf.codes.data_ptr(), buf.scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), fmt,
-                _native.ptr(layer.bias), n, layer.N, layer.K, out.data_ptr(), out.stride(0), st)))
+        def lora(layer, x):
+            """The shard's low-rank product (float32, [n, the layer's N]) for its input x, or None at rank 0."""
+            return layer.lowrank(x[:n]) if layer.rank else None
 
-        def partial(layer, codes, scales):
+        def gemm(layer, out, add=None):
+            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_add(
+                buf.codes.data_ptr(), buf.scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), fmt,
+                _native.ptr(layer.bias), _native.ptr(add), layer.N, n, layer.N, layer.K, out.data_ptr(),
+                out.stride(0), st)))
+
+        def partial(layer, codes, scales, add=None):
             f = w4a4.hidden_format(fmt) if codes is buf.hcodes else fmt  # the hidden layer's own format
             timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_f32(
                 codes.data_ptr(), scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), f, None,
-                None, 0, n, dim, layer.K, buf.partial.data_ptr(), dim, st)))
+                _native.ptr(add), dim, n, dim, layer.K, buf.partial.data_ptr(), dim, st)))
 
         def residual(name, gate_row):
             _native.check(lib.wdl_residual_update(buf.partial.data_ptr(), dim, _native.ptr(self.bias[name]),
@@ -231,11 +240,16 @@ class WanBlockTP:
                                                   n, dim, st))
 
         def ln_quant(shift_row, scale_row, affine, layer, round_bf16):
-            _native.check(lib.wdl_ln_quant(
+            """Codes and scales of a column-parallel layer's (whole) input; with a low-rank branch also the bf16
+            input itself (buf.xin), whose product with the shard's branch is returned (else None)."""
+            keep = buf.xin if layer.rank else None
+            _native.check(lib.wdl_ln_quant_keep(
                 X.data_ptr(), _native.F32, dim, n, dim, self.eps, self.norm3_w.data_ptr() if affine else None,
                 self.norm3_b.data_ptr() if affine else None, 1 if round_bf16 else 0,
                 None if shift_row is None else mod_ptr(shift_row), None if scale_row is None else mod_ptr(scale_row),
-                _native.ptr(layer.smooth), sd, fmt, buf.codes.data_ptr(), buf.scales.data_ptr(), st))
+                _native.ptr(layer.smooth), sd, fmt, buf.codes.data_ptr(), buf.scales.data_ptr(), _native.ptr(keep),
+                dim, st))
+            return None if keep is None else lora(layer, keep)
 
         def quantize(x, layer):
             _native.check(lib.wdl_w4a4_quantize_rows(x.data_ptr(), _native.BF16, x.stride(0), _native.ptr(layer.smooth),
@@ -244,25 +258,28 @@ class WanBlockTP:
 
         sumsq = buf.sumsq[:n]
         # self-attention on this shard's heads
-        ln_quant(0, 1, False, L["self_attn.qkv"], x_is_bf16)
-        gemm(L["self_attn.qkv"], buf.qkv)  # [n, 3 d]: q | k | v of this shard's heads
+        add = ln_quant(0, 1, False, L["self_attn.qkv"], x_is_bf16)
+        gemm(L["self_attn.qkv"], buf.qkv, add)  # [n, 3 d]: q | k | v of this shard's heads
         _native.check(lib.wdl_rows_sumsq(buf.qkv.data_ptr(), 3 * d, n, d, 2, d, sumsq.data_ptr(), st))
         yield sumsq
         _native.check(lib.wdl_qkv_prep_sharded(
             buf.qkv.data_ptr(), 3 * d, n, d, self.norm_q.data_ptr(), self.norm_k.data_ptr(), self.eps,
             sumsq.data_ptr(), dim, freq.data_ptr(), freq.shape[1], grid[1], grid[2], start, buf.q.data_ptr(),
             buf.k.data_ptr(), ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(), capacity, at, st))
-        _native.check(lib.wdl_sage_attend(
-            buf.q.data_ptr(), d, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(), at,
-            buf.k.data_ptr(), _native.F32, d, buf.qkv.data_ptr() + 2 * d * 2, _native.BF16, 3 * d, n, H,
-            HEAD_DIM ** -0.5, buf.attn.data_ptr(), d, buf.sage.data_ptr(), buf.sage.numel(), st))
+        if forcing is None:
+            _native.check(lib.wdl_sage_attend(
+                buf.q.data_ptr(), d, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(), at,
+                buf.k.data_ptr(), _native.F32, d, buf.qkv.data_ptr() + 2 * d * 2, _native.BF16, 3 * d, n, H,
+                HEAD_DIM ** -0.5, buf.attn.data_ptr(), d, buf.sage.data_ptr(), buf.sage.numel(), st))
+        else:
+            attend_forcing(buf, n, H, cache, at, forcing)
         quantize(buf.attn, L["self_attn.o"])
-        partial(L["self_attn.o"], buf.codes, buf.scales)
+        partial(L["self_attn.o"], buf.codes, buf.scales, lora(L["self_attn.o"], buf.attn))
         yield buf.partial
         residual("self_attn.o", 2)
         # cross-attention on this shard's heads
-        ln_quant(None, None, True, L["cross_attn.q"], x_is_bf16)
-        gemm(L["cross_attn.q"], buf.cq)
+        add = ln_quant(None, None, True, L["cross_attn.q"], x_is_bf16)
+        gemm(L["cross_attn.q"], buf.cq, add)
         row_sums = buf.sumsq.view(-1)[:n]
         _native.check(lib.wdl_rows_sumsq(buf.cq.data_ptr(), d, n, d, 1, 0, row_sums.data_ptr(), st))
         yield row_sums
@@ -273,16 +290,17 @@ class WanBlockTP:
                                              cross.k_scale.data_ptr(), cross.v_f8.data_ptr(), cross.v_scale.data_ptr(),
                                              n, cross.tokens, H, HEAD_DIM ** -0.5, buf.attn.data_ptr(), d, st))
         quantize(buf.attn, L["cross_attn.o"])
-        partial(L["cross_attn.o"], buf.codes, buf.scales)
+        partial(L["cross_attn.o"], buf.codes, buf.scales, lora(L["cross_attn.o"], buf.attn))
         yield buf.partial
         residual("cross_attn.o", None)
         # feed forward on this shard's hidden channels
         fc1, fc2 = L["ffn.0"], L["ffn.2"]
-        ln_quant(3, 4, False, fc1, x_is_bf16)
-        timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4(
+        add = ln_quant(3, 4, False, fc1, x_is_bf16)
+        gelu = buf.gelu if fc2.rank else None  # the second layer's branch reads GELU's output (its shard's channels)
+        timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4_add(
             buf.codes.data_ptr(), buf.scales.data_ptr(), fc1.codes.data_ptr(), fc1.scales.data_ptr(), fmt,
-            _native.ptr(fc1.bias), _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N, fc1.K,
-            buf.hcodes.data_ptr(), fc1.N, buf.hscales.data_ptr(), st)))
-        partial(fc2, buf.hcodes, buf.hscales)
+            _native.ptr(fc1.bias), _native.ptr(add), fc1.N, _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N,
+            fc1.K, buf.hcodes.data_ptr(), fc1.N, buf.hscales.data_ptr(), _native.ptr(gelu), fc1.N, st)))
+        partial(fc2, buf.hcodes, buf.hscales, None if gelu is None else lora(fc2, gelu))
         yield buf.partial
         residual("ffn.2", 5)
