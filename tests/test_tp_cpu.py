@@ -75,6 +75,51 @@ def test_shards_partition_every_layer():
         assert rel <= 1e-6, (name, rel)
 
 
+def lowrank_packed(N, K, rank, seed):
+    """A layer's parts with a rank-`rank` low-rank branch and a smoothing vector (random factors: the split is
+    checked, not the decomposition)."""
+    rng = np.random.default_rng(seed)
+    bf = lambda a: torch.from_numpy(a.astype(np.float32)).to(torch.bfloat16)  # noqa: E731
+    parts = packed((rng.standard_normal((N, K)) * 0.02).astype(np.float32),
+                   (rng.standard_normal(N) * 0.1).astype(np.float32), seed)
+    parts["proj_down"] = bf(rng.standard_normal((K, rank)) * 0.05)
+    parts["proj_up"] = bf(rng.standard_normal((N, rank)) * 0.05)
+    parts["smooth"] = bf(rng.uniform(0.5, 2.5, K))
+    return parts
+
+
+def oracle_lowrank_product(parts, x):
+    """The oracle's product of x by a layer with its branch and smoothing, without bias, float32."""
+    f = lambda t: t.float().numpy()  # noqa: E731
+    return ow.linear_lowrank(x, ow.unpack_nibbles(parts["qweight"].numpy()), f(parts["wscales"]), f(parts["proj_down"]),
+                             f(parts["proj_up"]), None, f(parts["smooth"]))
+
+
+def test_lowrank_branches_shard_with_their_layers():
+    """Column shards keep proj_down whole and their rows of proj_up: their outputs are the whole layer's columns.
+    Row shards keep their rows of proj_down and smooth: their products, branch shares included, sum to the whole
+    layer's (bias kept aside, added once)."""
+    from wan_dit_lab_b200.models.block_tp import shard_columns, shard_rows
+    M, N, K, world, rank = 24, 256, 512, 4, 16
+    x = ow.round_to(np.random.default_rng(5).standard_normal((M, K)).astype(np.float32), "bfloat16")
+    parts = lowrank_packed(N, K, rank, 6)
+    whole = oracle_lowrank_product(parts, x)
+    n = N // world
+    for r in range(world):
+        sp = shard_columns(parts, torch.arange(r * n, (r + 1) * n))
+        assert sp["proj_down"] is parts["proj_down"] and sp["smooth"] is parts["smooth"]
+        got = oracle_lowrank_product(sp, x)
+        np.testing.assert_allclose(got, whole[:, r * n:(r + 1) * n], rtol=1e-6, atol=1e-6)
+    k = K // world
+    total = np.zeros_like(whole)
+    for r in range(world):
+        sp, bias = shard_rows(parts, r * k, (r + 1) * k)
+        assert bias is parts["bias"] and sp["proj_up"] is parts["proj_up"]
+        assert sp["proj_down"].shape == (k, rank) and sp["smooth"].shape == (k,)
+        total += oracle_lowrank_product(sp, x[:, r * k:(r + 1) * k])
+    assert np.linalg.norm(total - whole) / np.linalg.norm(whole) <= 1e-6
+
+
 def test_shards_reject_splits_off_group_boundaries():
     from wan_dit_lab_b200.models.block_tp import shard_block_parts, shard_rows
     parts = block_parts(256, 512, 4)
