@@ -17,6 +17,8 @@ What each file holds and which reference code made it:
                         read back from FP8, the chunk unquantized)
   block.npz             models/block.py:22-29 WanBlock (nn.Linear, float32) on a small seeded block
   kvcache.npz           generation/causal.py:160-337 KVCache bookkeeping (ring slots, eviction, anchors)
+  w4a4_calibration.npz  quantization/w4a4.py:80-137 int4_groups(R, "mse") on heavy-tailed weights and gptq(R, H)
+                        on correlated inputs with an idle channel (both on the CPU)
   block_pack_layout.json  quantization/w4a4.py:269-313 layers() and pack_layout() of a small WanBlock, the
                         reference's own functions run with its quantize replaced by one that returns zero tensors
                         of this build's part shapes (its Nunchaku packer is not in the tree), on the CPU
@@ -225,6 +227,26 @@ def kvcache_golden(reference):
     save("kvcache.npz", **out)
 
 
+def calibration_golden(reference):
+    """The reference's offline rounding options on the CPU: int4_groups(R, "mse") (w4a4.py:80-100) on Student-t
+    weights, and gptq(R, H) (w4a4.py:104-137) with H = X^T X of correlated inputs, one input channel idle (H_jj = 0)."""
+    sys.path.insert(0, str(Path(reference) / "src"))
+    from wan_dit_lab.quantization import w4a4
+    torch.manual_seed(41)  # StudentT samples from the global generator
+    g = torch.Generator().manual_seed(41)
+    R = torch.distributions.StudentT(3.0).sample((64, 512))
+    q_mse, s_mse = w4a4.int4_groups(R, rule="mse")
+    K, N = 256, 80
+    mix = torch.randn(K, K, generator=g) / K ** 0.5
+    X = torch.randn(2048, K, generator=g) @ mix + 0.3 * torch.randn(2048, K, generator=g)
+    X[:, 77] = 0  # an idle channel
+    Rg = torch.randn(N, K, generator=g)
+    H = X.T @ X
+    q_gptq, s_gptq = w4a4.gptq(Rg, H)
+    save("w4a4_calibration.npz", R=R.numpy(), q_mse=q_mse.numpy(), s_mse=s_mse.numpy(), Rg=Rg.numpy(), H=H.numpy(),
+         q_gptq=q_gptq.numpy(), s_gptq=s_gptq.numpy())
+
+
 def block_pack_golden(reference):
     """The reference's pack layout rule (quantization/w4a4.py:269-313) on a WanBlock(256, 512, 2 heads): its
     parameter names and shapes, layers() fused and not, and pack_layout() for packs v1 and v2, rank 32 and 0, with
@@ -271,3 +293,4 @@ if __name__ == "__main__":
     main(sys.argv[1])
     kvcache_golden(sys.argv[1])
     block_pack_golden(sys.argv[1])
+    calibration_golden(sys.argv[1])

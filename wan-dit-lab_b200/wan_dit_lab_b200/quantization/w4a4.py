@@ -98,16 +98,81 @@ def quantize_rows(x, scale_dtype=torch.bfloat16, smooth=None, packed=False, code
     return (codes, scales, nib) if packed else (codes, scales)
 
 
+MSE_STEPS = torch.linspace(0.5, 1.0, 26).tolist()  # the scales the "mse" rule tries, x max|x| / 7 (w4a4.py:76)
+
+
 @torch.no_grad()
 def int4_groups(R, rule="max"):
     """R [N, K] in symmetric INT4 groups of GROUP input channels: the integers [N, K] (int32) and the scales
-    [N, K / GROUP] (float32), as the reference's int4_groups (w4a4.py:81-100). Rule "max" only: the "mse" search
-    and GPTQ are offline calibration options of the reference outside the forward path."""
-    if rule != "max":
-        raise NotImplementedError("only the 'max' scale rule is implemented on the B200 path")
+    [N, K / GROUP] (float32), as the reference's int4_groups (w4a4.py:80-100). "max": scale = max|x| / 7, the
+    forward path's rule, by the quantizer kernel (R on a GPU). "mse" (offline, R on any device): of the scales
+    c max|x| / 7 for c in MSE_STEPS the one with the least squared error over the group, the smallest c among equal
+    errors; values beyond the grid are clipped to -8 / 7."""
     N, K = R.shape
-    codes, _ = quantize_rows(R.float().contiguous(), torch.bfloat16)
-    return codes.to(torch.int32), _group_scales(R.float())
+    if rule == "max":
+        codes, _ = quantize_rows(R.float().contiguous(), torch.bfloat16)
+        return codes.to(torch.int32), _group_scales(R.float())
+    if rule != "mse":
+        raise ValueError(rule)
+    groups = R.float().reshape(N, K // GROUP, GROUP)
+    top = _group_scales(R.float())
+    scale = torch.empty_like(top)
+    # every candidate of a slice of rows at once ([candidates, rows, groups, 64], about 64 MB), the first minimum
+    rows = max(1, (16 << 20) // (len(MSE_STEPS) * K))
+    for r0 in range(0, N, rows):
+        g = groups[r0:r0 + rows]
+        cand = torch.stack([top[r0:r0 + rows] * c for c in MSE_STEPS])  # [C, rows, groups]
+        back = torch.round(g / cand[..., None]).clamp(-8, 7) * cand[..., None]
+        err = ((g - back) ** 2).sum(-1)
+        scale[r0:r0 + rows] = cand.gather(0, err.argmin(0, keepdim=True))[0]
+    codes = torch.round(groups / scale[..., None]).clamp(-8, 7).to(torch.int32).reshape(N, K)
+    return codes, scale
+
+
+@torch.no_grad()
+def gptq(R, H, damp=0.01, block=128):
+    """GPTQ (Frantar et al., "GPTQ: Accurate Post-Training Quantization for Generative Pre-trained Transformers",
+    ICLR 2023) of R [N, K] into symmetric INT4 groups of GROUP input channels (reference w4a4.py:103-137), for the
+    inputs X of the layer through H = X^T X [K, K]: the columns are rounded left to right; a group's scale
+    max|x| / 7 is taken from its columns when the first of them is rounded, as earlier errors have moved them; each
+    column's error over the diagonal of U (the upper Cholesky factor of H^-1) is spread over the columns to its
+    right along U's row, inside a block of `block` columns column by column and onto the columns past the block
+    with one product. H gets damp x mean(diag H) on its diagonal; an input channel with H_jj = 0 carries nothing:
+    its weights are rounded from 0. Returns codes int32 [N, K] and scales float32 [N, K / GROUP]."""
+    W = R.detach().float().clone()
+    N, K = W.shape
+    Hd = H.detach().float().to(W.device).clone()
+    idle = Hd.diagonal() == 0
+    Hd[idle, idle] = 1
+    W[:, idle] = 0
+    Hd.diagonal().add_(damp * Hd.diagonal().mean())
+    U = torch.linalg.cholesky(torch.cholesky_inverse(torch.linalg.cholesky(Hd)), upper=True)
+    del Hd
+    codes = torch.zeros(N, K, dtype=torch.int32, device=W.device)
+    scales = torch.zeros(N, K // GROUP, device=W.device)
+    for b0 in range(0, K, block):
+        b1 = min(b0 + block, K)
+        part = W[:, b0:b1]  # a view: the block's columns move in place as their left neighbours are rounded
+        errors = torch.zeros(N, b1 - b0, device=W.device)
+        for j in range(b1 - b0):
+            c = b0 + j
+            if c % GROUP == 0:
+                scales[:, c // GROUP] = W[:, c:c + GROUP].abs().amax(dim=1).clamp(min=1e-8) / 7
+            s = scales[:, c // GROUP]
+            w = part[:, j]
+            q = torch.round(w / s).clamp(-8, 7)
+            codes[:, c] = q.to(torch.int32)
+            e = (w - q * s) / U[c, c]
+            part[:, j:] -= e[:, None] * U[c, c:b1][None, :]
+            errors[:, j] = e
+        W[:, b1:] -= errors @ U[b0:b1, b1:]
+    return codes, scales
+
+
+def _pack_nibbles(codes):
+    """int codes [N, K] in [-8, 7] -> uint8 [N, K / 2], two per byte, the even input channel in the low nibble."""
+    lo, hi = codes[:, 0::2] & 0xF, codes[:, 1::2] & 0xF
+    return (lo | (hi << 4)).to(torch.uint8)
 
 
 def _group_scales(R):
@@ -123,12 +188,15 @@ def _group_scales(R):
 def quantize(weight, bias=None, smooth=None, rank=32, shift=0.0, hessian=None, rule="max", scale_dtype=torch.bfloat16):
     """The tensors of a W4A4 layer for y = x W^T + b (reference w4a4.py:141-180): dict(qweight [N, K/2] uint8,
     wscales [K/64, N], proj_down [K, r], proj_up [N, r], smooth [K], bias [N]), bfloat16 where not INT4, in the
-    logical packed format of this module. weight [N, K] on a CUDA device; smooth [K] (ones when None); rank: of
+    logical packed format of this module. weight [N, K] (on a CUDA device for the kernel's "max" rounding; the
+    offline rules run where it is); smooth [K] (ones when None); rank: of
     the 16-bit low-rank branch taken from the SVD of W diag(s) (0: none); shift: the second layer of gelu_mlp
-    quantizes x + shift unsigned, and the bias takes off shift (R / s) 1 (w4a4.py:168-170)."""
-    if hessian is not None:
-        raise NotImplementedError("GPTQ rounding is an offline calibration option, not implemented here")
-    W = _cuda(weight, "weight").float()
+    quantizes x + shift unsigned, and the bias takes off shift (R / s) 1 (w4a4.py:168-170). hessian [K, K]: X^T X
+    of the inputs the INT4 branch multiplies by R (x + shift for gelu_mlp's second layer, before smoothing): R is
+    rounded by GPTQ in the smoothed space instead of to the nearest. rule: the INT4 scale rule of int4_groups."""
+    if hessian is None and rule == "max":
+        _cuda(weight, "weight")  # rounded by the quantizer kernel; the offline rules run on the weight's device
+    W = weight.float()
     N, K = W.shape
     s = torch.ones(K, device=W.device) if smooth is None else smooth.float().to(W.device)
     Ws = W * s[None, :]
@@ -139,8 +207,19 @@ def quantize(weight, bias=None, smooth=None, rank=32, shift=0.0, hessian=None, r
     else:
         up, down = W.new_zeros(N, 0), W.new_zeros(0, K)
         R = Ws
-    codes, scales_t, packed = quantize_rows(R.contiguous(), scale_dtype, packed=True)
-    top = _group_scales(R)  # the fp32 scales of the codes
+    if hessian is None and rule == "max":  # the forward path's rounding, by the quantizer kernel
+        codes, _, packed = quantize_rows(R.contiguous(), scale_dtype, packed=True)
+        top = _group_scales(R)  # the fp32 scales of the codes
+    else:
+        if hessian is None:
+            codes, top = int4_groups(R, rule)
+        else:  # the INT4 branch sees x / s: the Hessian of x / s is diag(1/s) H diag(1/s) (w4a4.py:163-167)
+            # a wide layer (K = 14336: H alone is 0.8 GB) on the host, beside a model on the GPU
+            where = torch.device("cpu") if K > 8192 else W.device
+            Hs = hessian.float().to(where) / s.to(where)[:, None] / s.to(where)[None, :]
+            codes, top = gptq(R.to(where), Hs)
+            codes, top = codes.to(W.device), top.to(W.device)
+        packed = _pack_nibbles(codes)
     b = torch.zeros(N, device=W.device) if bias is None else bias.float().to(W.device)
     if shift:
         Rq = (codes.view(N, K // GROUP, GROUP).float() * top[..., None]).view(N, K)  # R as INT4 holds it
