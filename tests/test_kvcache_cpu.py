@@ -6,6 +6,7 @@ frame, causal.py:243-248), checked against a plain restatement of those rules.""
 import sys
 from pathlib import Path
 
+import pytest
 import torch
 
 sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "wan-dit-lab_b200"))
@@ -107,3 +108,18 @@ def test_cache_matches_reference_golden():
             np.testing.assert_array_equal(cache.place_in_frame.numpy(), d[key + "_place"][step])
             if d[key + "_anchors"][step][0] >= 0:
                 np.testing.assert_array_equal(cache.anchor_tokens.numpy(), d[key + "_anchors"][step])
+
+
+def test_static_heads_split_across_shards():
+    """Forcing-KV's static heads in the model's numbering go to the shards that hold them, renumbered; out of
+    range is an error; one shard is the whole model."""
+    from wan_dit_lab_b200.generation.causal import shard_heads
+    static = [1, 5, 6]
+    assert shard_heads(static, 0, 1, 8) == [1, 5, 6]
+    assert [shard_heads(static, r, 2, 4) for r in range(2)] == [[1], [1, 2]]
+    assert [shard_heads(static, r, 4, 2) for r in range(4)] == [[1], [], [1], [0]]
+    assert shard_heads(None, 0, 2, 4) == []
+    with pytest.raises(ValueError):
+        shard_heads([8], 1, 2, 4)
+    with pytest.raises(ValueError):
+        shard_heads([-1], 0, 2, 4)

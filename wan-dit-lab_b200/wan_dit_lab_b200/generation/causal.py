@@ -45,6 +45,16 @@ def rope_table(positions, head_dim=128):
                      dim=-1).float()
 
 
+def shard_heads(static, rank, world, heads):
+    """The static heads (Forcing-KV, numbered over the model's heads) that tensor-parallel shard `rank` of `world`
+    holds, each holding `heads` consecutive heads, renumbered from 0; ValueError for a head outside the model."""
+    first, total = rank * heads, world * heads
+    static = list(static or ())
+    if any(h < 0 or h >= total for h in static):
+        raise ValueError("static heads out of range")
+    return [h - first for h in static if first <= h < first + heads]
+
+
 class KVCache:
     """FP8 keys / values of the finished frames of one block: [max_tokens + chunk tokens, heads, 128] E4M3 with
     one float32 scale per (token, head), the first sink_tokens never evicted (reference KVCache,
@@ -300,14 +310,10 @@ class Stream:
         self.caches = [KVCache((max_frames - chunk) * self.tokens, sink_frames * self.tokens, n, heads, model.device)
                        for _ in model.blocks]
         if static_heads:  # Forcing-KV: {block: [static heads]} (reference Stream, causal.py:490-494)
-            # in the model's head numbers; a tensor-parallel shard keeps those of its heads, renumbered
-            first = getattr(model.blocks[0], "rank", 0) * heads
-            total = heads * getattr(model.blocks[0], "world", 1)
+            rank, world = getattr(model.blocks[0], "rank", 0), getattr(model.blocks[0], "world", 1)
             for index, cache in enumerate(self.caches):
-                static = list(static_heads.get(index, static_heads.get(str(index), [])))
-                if any(h < 0 or h >= total for h in static):
-                    raise ValueError("static heads out of range")
-                cache.set_heads([h - first for h in static if first <= h < first + heads], heads)
+                static = static_heads.get(index, static_heads.get(str(index), []))
+                cache.set_heads(shard_heads(static, rank, world, heads), heads)
         self.freq = rope_table(positions).to(model.device)
         # the chunk's table: its frames' time angles in rows 0.. (the kernels run with start 0), height / width
         # angles as in the whole table (reference Stream's chunk_freqs), refreshed in place before every chunk
