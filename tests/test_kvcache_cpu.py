@@ -123,3 +123,25 @@ def test_static_heads_split_across_shards():
         shard_heads([8], 1, 2, 4)
     with pytest.raises(ValueError):
         shard_heads([-1], 0, 2, 4)
+
+
+def test_stream_gives_each_cache_its_shards_static_heads():
+    """Stream(static_heads=...) on a tensor-parallel shard: every block's cache gets the static heads among the
+    shard's own, renumbered (keys may be ints or strings, as the reference's presets give them). A stand-in model
+    on the CPU: the constructor only sizes and wires the caches and scratch."""
+    from types import SimpleNamespace
+    from wan_dit_lab_b200.generation.causal import Stream
+
+    class Shard:
+        kv_heads, rank, world, lowrank = 4, 1, 2, False
+
+        def buffers(self, *args, **kwargs):
+            return None
+
+    model = SimpleNamespace(blocks=[Shard(), Shard(), Shard()], out_dim=48, device="cpu",
+                            cross_kvs=lambda context: [SimpleNamespace(tokens=context.shape[1])])
+    s = Stream(model, torch.zeros(1, 8, 16), 64, 64, vae_stride=16, max_frames=9, static_heads={0: [1, 5], "2": [6, 7]})
+    assert [c.static_heads for c in s.caches] == [[1], None, [2, 3]]
+    assert all(c.heads == 4 for c in s.caches)
+    with pytest.raises(ValueError):
+        Stream(model, torch.zeros(1, 8, 16), 64, 64, vae_stride=16, max_frames=9, static_heads={1: [8]})
