@@ -247,3 +247,44 @@ def test_block_forcing_kv_head_split():
     want = sage_kv.attend(q, gather(cache[0]).view(torch.float8_e4m3fn), gather(cache[1])[..., None],
                           gather(cache[2]).view(torch.float8_e4m3fn), gather(cache[3])[..., None], rows.numel(), k, v)
     assert torch.equal(A1[:, sl], want[0])
+
+
+def test_block_attention_entropy_scaling():
+    """With an attention entropy ratio (reference KVCache.scale, causal.py:138-142) self-attention runs with
+    sqrt(log_{N r} N / d) for its N = at + n keys: the block's attention equals sage_kv.attend with that scale on
+    the same queries, cache and chunk, bit for bit, and differs from the unscaled block's."""
+    from wan_dit_lab_b200.kernels import sage_kv
+    from wan_dit_lab_b200.models.block import Buffers, WanBlockB200, attention_scale
+    from wan_dit_lab_b200 import _native
+    dim, heads, ffn, frames, h, w, at, text = 1024, 8, 4096, 2, 4, 8, 192, 32
+    n = frames * h * w
+    state = random_state(dim, ffn, 17)
+    blk = WanBlockB200(state, dim, ffn, heads)
+    g = torch.Generator().manual_seed(18)
+    X = torch.randn(n, dim, generator=g)
+    time_in = torch.randn(6, dim, generator=g) * 0.1
+    ctx = (torch.randn(text, dim, generator=g)).to(torch.bfloat16)
+    cap = at + n
+    ck8, cks = of.quantize_rows((torch.randn(1, cap, heads, 128, generator=g) + 0.3).numpy())
+    cv8, cvs = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
+    freq = torch.from_numpy(orope.table(1024).astype(np.float32)).cuda()
+    mod = blk.modulation_of(time_in.cuda())
+    cross = blk.cross_kv(ctx.cuda())
+    traces = []
+    for ratio in (None, 0.25):
+        cache = (torch.from_numpy(ck8[0]).cuda(), torch.from_numpy(cks[0, ..., 0]).cuda(),
+                 torch.from_numpy(cv8[0]).cuda(), torch.from_numpy(cvs[0, ..., 0]).cuda(), cap)
+        tr = {}
+        blk.forward(X.cuda(), mod, cache, at, freq, (frames, h, w), at // (h * w), cross,
+                    Buffers(n, dim, ffn, heads, cap, text, "cuda"), trace=tr, entropy_ratio=ratio)
+        traces.append((tr, cache))
+    assert _native.device_error() == 0
+    (plain, _), (scaled, cache) = traces
+    scale = attention_scale(at + n, 0.25)
+    assert scale != attention_scale(at + n) and not torch.equal(plain["attn"], scaled["attn"])
+    q = scaled["q"].view(1, n, heads, 128)
+    k = scaled["k"].view(1, n, heads, 128)
+    v = scaled["qkv"][:, 2 * dim:].reshape(1, n, heads, 128)
+    want = sage_kv.attend(q, cache[0].view(torch.float8_e4m3fn)[None], cache[1][None, ..., None],
+                          cache[2].view(torch.float8_e4m3fn)[None], cache[3][None, ..., None], at, k, v, sm_scale=scale)
+    assert torch.equal(scaled["attn"].view(1, n, heads, 128), want)

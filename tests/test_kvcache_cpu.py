@@ -145,3 +145,28 @@ def test_stream_gives_each_cache_its_shards_static_heads():
     assert all(c.heads == 4 for c in s.caches)
     with pytest.raises(ValueError):
         Stream(model, torch.zeros(1, 8, 16), 64, 64, vae_stride=16, max_frames=9, static_heads={1: [8]})
+
+
+def test_attention_entropy_scale_follows_the_reference():
+    """attention_scale (reference KVCache.scale, causal.py:138-142): 1 / sqrt(d) without a ratio, else
+    sqrt(log(N) / log(N r) / d); Stream hands its ratio to every cache."""
+    import math
+    from types import SimpleNamespace
+    from wan_dit_lab_b200.generation.causal import Stream
+    from wan_dit_lab_b200.models.block import attention_scale
+    assert attention_scale(5568) == 128 ** -0.5
+    for keys, r in ((5568, 0.5), (1392, 0.25), (9744, 2.0)):
+        assert attention_scale(keys, r) == math.sqrt(math.log(keys) / math.log(keys * r) / 128)
+    assert abs(attention_scale(1392, 1.0) - 128 ** -0.5) < 1e-15  # T = N: the trained scale
+
+    class Block:
+        kv_heads, lowrank = 2, False
+
+        def buffers(self, *args, **kwargs):
+            return None
+
+    model = SimpleNamespace(blocks=[Block(), Block()], out_dim=48, device="cpu",
+                            cross_kvs=lambda context: [SimpleNamespace(tokens=context.shape[1])])
+    s = Stream(model, torch.zeros(1, 8, 16), 64, 64, vae_stride=16, max_frames=9, attention_entropy_ratio=0.5)
+    assert [c.entropy_ratio for c in s.caches] == [0.5, 0.5]
+    assert Stream(model, torch.zeros(1, 8, 16), 64, 64, vae_stride=16, max_frames=9).caches[0].entropy_ratio is None

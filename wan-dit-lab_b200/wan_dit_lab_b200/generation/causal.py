@@ -65,8 +65,11 @@ class KVCache:
 
     fp8 = True
 
-    def __init__(self, max_tokens, sink_tokens, n, heads, device):
+    def __init__(self, max_tokens, sink_tokens, n, heads, device, entropy_ratio=None):
         self.max_tokens, self.sink_tokens, self.n, self.heads = max_tokens, sink_tokens, n, heads
+        # attention entropy scaling (reference causal.py:80-85, 138-142): with a ratio r, Q K^T over N keys is scaled
+        # by sqrt(log_{N r} N / d) instead of 1 / sqrt(d); None: 1 / sqrt(d), as trained
+        self.entropy_ratio = entropy_ratio
         cap = max_tokens + n
         self.capacity = cap
         self.k = torch.zeros(cap, heads, 128, dtype=torch.uint8, device=device)
@@ -249,6 +252,8 @@ class WanModelB200:
         for i, blk in enumerate(self.blocks):
             forcing = caches[i].forcing()
             kw = {} if forcing is None else {"forcing": forcing}
+            if caches[i].entropy_ratio is not None:
+                kw["entropy_ratio"] = caches[i].entropy_ratio
             blk.forward(X, self.mods[i], caches[i].buffers(), caches[i].saved, freq, grid, start, cross[i], buf,
                         x_is_bf16=(i == 0), **kw)
         return self.head(X, temb, grid).float()
@@ -299,7 +304,7 @@ class Stream:
     values with one more pass at t = 0, and commits them."""
 
     def __init__(self, model, context, height, width, generator=None, max_frames=CONTEXT, sink_frames=0, chunk=CHUNK,
-                 vae_stride=8, positions=1024, cuda_graph=False, static_heads=None):
+                 vae_stride=8, positions=1024, cuda_graph=False, static_heads=None, attention_entropy_ratio=None):
         h, w = height // vae_stride, width // vae_stride
         self.tokens = (h // 2) * (w // 2)
         self.grid = (chunk, h // 2, w // 2)
@@ -307,8 +312,8 @@ class Stream:
         n = chunk * self.tokens
         self.shape = (model.out_dim, chunk, h, w)
         heads = model.blocks[0].kv_heads  # all of them, or this tensor-parallel shard's
-        self.caches = [KVCache((max_frames - chunk) * self.tokens, sink_frames * self.tokens, n, heads, model.device)
-                       for _ in model.blocks]
+        self.caches = [KVCache((max_frames - chunk) * self.tokens, sink_frames * self.tokens, n, heads, model.device,
+                               attention_entropy_ratio) for _ in model.blocks]
         if static_heads:  # Forcing-KV: {block: [static heads]} (reference Stream, causal.py:490-494)
             rank, world = getattr(model.blocks[0], "rank", 0), getattr(model.blocks[0], "world", 1)
             for index, cache in enumerate(self.caches):

@@ -21,6 +21,8 @@ values depend on the prompt alone and are projected, normalized and quantized on
 (Stream.cross, generation/causal.py:558-568).
 """
 
+import math
+
 import torch
 
 from wan_dit_lab_b200 import _native
@@ -83,13 +85,23 @@ def quantize_block(p, scale_dtype=torch.bfloat16):
     return parts
 
 
-def attend_forcing(buf, n, H, cache, at, forcing):
+def attention_scale(keys, entropy_ratio=None, head_dim=HEAD_DIM):
+    """The softmax scale of Q K^T over `keys` keys (reference KVCache.scale, causal.py:138-142): 1 / sqrt(d), or
+    with an entropy ratio r, sqrt(log_T N / d) for N = keys and T = N r, which keeps attention's entropy at that of
+    the training length."""
+    if entropy_ratio is None:
+        return head_dim ** -0.5
+    return math.sqrt(math.log(keys) / math.log(keys * entropy_ratio) / head_dim)
+
+
+def attend_forcing(buf, n, H, cache, at, forcing, entropy_ratio=None):
     """Self-attention of a chunk with Forcing-KV's head split (reference causal.py:222-240), over the H heads this
     process holds (buf.q / buf.k float32 [n, H 128], the chunk's values in buf.qkv[:, 2 H 128:], output buf.attn):
     forcing = (static, dynamic, anchor rows) int32 device tensors in this process's head numbers. The dynamic
     heads attend to the cached window [0, at) and the chunk, the static heads to the anchor rows (the sink and the
     newest finished frame) and the chunk, each group through the attention's head / token maps
-    (wdl_sage_attend_maps) on gathered copies of its heads' queries, keys and values."""
+    (wdl_sage_attend_maps) on gathered copies of its heads' queries, keys and values; each group's softmax scale is
+    attention_scale of its own key count (causal.py:236-238)."""
     lib, st = _native.lib(), _native.stream()
     ck, cks, cv, cvs, capacity = cache
     static, dynamic, anchors = forcing
@@ -107,8 +119,8 @@ def attend_forcing(buf, n, H, cache, at, forcing):
         _native.check(lib.wdl_sage_attend_maps(
             q_s.data_ptr(), hs * HEAD_DIM, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(),
             capacity, H, idx.data_ptr(), _native.ptr(tokens), length, k_s.data_ptr(), _native.F32,
-            hs * HEAD_DIM, v_s.data_ptr(), _native.BF16, hs * HEAD_DIM, n, hs, HEAD_DIM ** -0.5,
-            o_s.data_ptr(), hs * HEAD_DIM, buf.sage.data_ptr(), buf.sage.numel(), st))
+            hs * HEAD_DIM, v_s.data_ptr(), _native.BF16, hs * HEAD_DIM, n, hs,
+            attention_scale(length + n, entropy_ratio), o_s.data_ptr(), hs * HEAD_DIM, buf.sage.data_ptr(), buf.sage.numel(), st))
         out[:, il] = o_s.view(n, hs, HEAD_DIM)
 
 
@@ -181,7 +193,8 @@ class WanBlockB200:
     # is bracketed by CUDA events on the current stream: the benchmark's per-kernel timing of the W4A4 GEMMs.
     gemm_timer = None
 
-    def forward(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, trace=None, forcing=None):
+    def forward(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, trace=None, forcing=None,
+                entropy_ratio=None):
         """X [n, dim] float32, updated in place (the block's output). mod [6, dim] float32: this block's
         time_in + modulation. cache: (k, ks, v, vs, capacity) FP8 cache buffers of this block
         [capacity, heads, 128] / [capacity, heads]; the chunk's keys and values are stored at `at` and attention
@@ -191,7 +204,9 @@ class WanBlockB200:
         given, receives copies of the intermediate tensors (debugging; synchronizes). forcing: Forcing-KV's
         (static heads, dynamic heads, anchor rows) of the cache (KVCache.forcing()), or None: with it, the dynamic
         heads attend to the whole cached window and the static ones to the anchor rows (the sink and the newest
-        finished frame), both with the chunk, through the attention's head / token maps (causal.py:222-240)."""
+        finished frame), both with the chunk, through the attention's head / token maps (causal.py:222-240).
+        entropy_ratio: the cache's attention entropy ratio (self-attention's softmax scale, attention_scale), or None
+        for 1 / sqrt(128)."""
         lib, st = _native.lib(), _native.stream()
         n, dim, H = X.shape[0], self.dim, self.heads
         ck, cks, cv, cvs, capacity = cache
@@ -262,9 +277,10 @@ class WanBlockB200:
             _native.check(lib.wdl_sage_attend(
                 buf.q.data_ptr(), dim, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(), at,
                 buf.k.data_ptr(), _native.F32, dim, buf.qkv.data_ptr() + 2 * dim * 2, _native.BF16, 3 * dim, n, H,
-                HEAD_DIM ** -0.5, buf.attn.data_ptr(), dim, buf.sage.data_ptr(), buf.sage.numel(), st))
+                attention_scale(at + n, entropy_ratio), buf.attn.data_ptr(), dim, buf.sage.data_ptr(), buf.sage.numel(),
+                st))
         else:
-            attend_forcing(buf, n, H, cache, at, forcing)
+            attend_forcing(buf, n, H, cache, at, forcing, entropy_ratio)
         keep("q", buf.q), keep("k", buf.k), keep("attn", buf.attn)
         quantize(buf.attn, L["self_attn.o"])
         gemm_residual(L["self_attn.o"], 2, add=lora(L["self_attn.o"], buf.attn))

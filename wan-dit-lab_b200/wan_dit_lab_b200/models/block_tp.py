@@ -30,7 +30,8 @@ all shards'), which is how the split is tested against the whole block on one GP
 import torch
 
 from wan_dit_lab_b200 import _native
-from wan_dit_lab_b200.models.block import HEAD_DIM, Buffers, CrossKV, WanBlockB200, _f32, attend_forcing, quantize_block
+from wan_dit_lab_b200.models.block import (HEAD_DIM, Buffers, CrossKV, WanBlockB200, _f32, attend_forcing,
+                                          attention_scale, quantize_block)
 from wan_dit_lab_b200.quantization import w4a4
 
 ROW_PARALLEL = ("self_attn.o", "cross_attn.o", "ffn.2")
@@ -187,15 +188,17 @@ class WanBlockTP:
     # bracketed by CUDA events on the current stream: the benchmark's per-kernel timing of the W4A4 GEMMs.
     gemm_timer = None
 
-    def forward(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, trace=None, forcing=None):
+    def forward(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, trace=None, forcing=None,
+                entropy_ratio=None):
         """WanBlockB200.forward on this shard: every tensor steps() yields is summed across shards by reduce."""
         if self.reduce is None:
             raise RuntimeError("a tensor-parallel block needs a reduce callable (or run_lockstep over its steps)")
-        for t in self.steps(X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16, forcing):
+        for t in self.steps(X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16, forcing, entropy_ratio):
             self.reduce(t)
         return X
 
-    def steps(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, forcing=None):
+    def steps(self, X, mod, cache, at, freq, grid, start, cross, buf, x_is_bf16=False, forcing=None,
+              entropy_ratio=None):
         """The block on this shard's heads and hidden channels (WanBlockB200.forward's arguments; cache holds this
         shard's heads, forcing its Forcing-KV split in this shard's head numbers, which changes no collective).
         Yields, in order: the q / k sums of squares [n, 2], the self-attention O partial [n, dim],
@@ -270,9 +273,10 @@ class WanBlockTP:
             _native.check(lib.wdl_sage_attend(
                 buf.q.data_ptr(), d, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(), at,
                 buf.k.data_ptr(), _native.F32, d, buf.qkv.data_ptr() + 2 * d * 2, _native.BF16, 3 * d, n, H,
-                HEAD_DIM ** -0.5, buf.attn.data_ptr(), d, buf.sage.data_ptr(), buf.sage.numel(), st))
+                attention_scale(at + n, entropy_ratio), buf.attn.data_ptr(), d, buf.sage.data_ptr(), buf.sage.numel(),
+                st))
         else:
-            attend_forcing(buf, n, H, cache, at, forcing)
+            attend_forcing(buf, n, H, cache, at, forcing, entropy_ratio)
         quantize(buf.attn, L["self_attn.o"])
         partial(L["self_attn.o"], buf.codes, buf.scales, lora(L["self_attn.o"], buf.attn))
         yield buf.partial
