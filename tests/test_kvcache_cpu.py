@@ -170,3 +170,66 @@ def test_attention_entropy_scale_follows_the_reference():
     s = Stream(model, torch.zeros(1, 8, 16), 64, 64, vae_stride=16, max_frames=9, attention_entropy_ratio=0.5)
     assert [c.entropy_ratio for c in s.caches] == [0.5, 0.5]
     assert Stream(model, torch.zeros(1, 8, 16), 64, 64, vae_stride=16, max_frames=9).caches[0].entropy_ratio is None
+
+
+class _Recorder:
+    """A stand-in model on the CPU that records each pass (its timestep and input) and predicts a zero flow; the
+    stream's schedule, write pass and cache bookkeeping run as they do around the real model."""
+
+    def __init__(self, layers=2):
+        from types import SimpleNamespace
+
+        class Block:
+            kv_heads, lowrank = 2, False
+
+            def buffers(self, *args, **kwargs):
+                return None
+
+        self.blocks = [Block() for _ in range(layers)]
+        self.out_dim, self.device, self.calls = 4, "cpu", []
+        self.cross_kvs = lambda context: [SimpleNamespace(tokens=context.shape[1])]
+
+    def forward(self, x, t, grid, freq, start, caches, cross, buf):
+        self.calls.append((t, x.clone(), [c.saved for c in caches]))
+        return torch.zeros_like(x)
+
+
+def test_stream_schedule_write_pass_and_context_noise():
+    """The reference Stream's options around the passes (causal.py:705-738): four denoising passes at 1000 sigma for
+    the shifted levels, then the write pass at t = 0 on the clean chunk, or at t = context_noise on the chunk noised
+    to it, or none (write_pass False); every cache commits once per chunk either way."""
+    import math
+    from wan_dit_lab_b200.generation.causal import Stream, sigmas
+    ctx = torch.zeros(1, 8, 16)
+    for kw, last in ((dict(), 0.0), (dict(context_noise=100), 100.0), (dict(write_pass=False), None),
+                     (dict(shift=3.0), 0.0)):
+        model = _Recorder()
+        s = Stream(model, ctx, 64, 64, generator=torch.Generator().manual_seed(1), vae_stride=16, max_frames=9, **kw)
+        noise = torch.randn(s.shape, generator=torch.Generator().manual_seed(2))
+        x0 = s.next_chunk(noise)
+        levels = sigmas(shift=kw.get("shift", 5.0))
+        ts = [c[0] for c in model.calls]
+        assert all(math.isclose(t, 1000 * sg) for t, sg in zip(ts, levels))
+        assert len(ts) == len(levels) + (last is not None)
+        if last is not None:
+            assert ts[-1] == last
+        # a zero flow: x0 is the pass's input, so the last denoising pass saw the levels' mix of x0 and noise
+        assert torch.equal(model.calls[0][1], noise)
+        if last == 0.0:
+            assert torch.equal(model.calls[-1][1], x0)
+        elif last == 100.0:
+            assert not torch.equal(model.calls[-1][1], x0)
+        # every pass wrote at the same place; the commit after the chunk moved it on
+        assert all(c[2] == [0, 0] for c in model.calls)
+        assert [c.saved for c in s.caches] == [s.tokens * 3] * 2 and s.start == 3
+
+
+def test_stream_window_of_a_known_length_and_sink_rule():
+    from wan_dit_lab_b200.generation.causal import Stream
+    ctx = torch.zeros(1, 8, 16)
+    s = Stream(_Recorder(), ctx, 64, 64, vae_stride=16, max_frames=21, frames=9)
+    assert s.window == 9 and s.caches[0].max_tokens == 6 * s.tokens
+    assert Stream(_Recorder(), ctx, 64, 64, vae_stride=16, max_frames=9, sink_frames=3).caches[0].sink_tokens == 3 * 4
+    assert Stream(_Recorder(), ctx, 64, 64, vae_stride=16, max_frames=9, sink_frames=6).caches[0].max_tokens == 24
+    with pytest.raises(ValueError):  # 4 sink frames leave 2 ring frames: less than a chunk
+        Stream(_Recorder(), ctx, 64, 64, vae_stride=16, max_frames=9, sink_frames=4)

@@ -300,19 +300,28 @@ class PassGraphs:
 
 class Stream:
     """A video, chunk by chunk (reference Stream with sampler "dmd", kv_fp8, attention "sage", positions "video",
-    write_pass True, cross_cache True): next_chunk denoises a chunk in len(levels) passes, writes its keys and
-    values with one more pass at t = 0, and commits them."""
+    cross_cache True, causal.py:450-758): next_chunk denoises a chunk in len(levels) passes, writes its keys and
+    values with one more pass (write_pass; at t = context_noise, the clean chunk noised to it, 0 as trained), and
+    commits them. frames: the video's length when known (the window is no longer than it); shift: of the noise
+    levels (sigmas)."""
 
     def __init__(self, model, context, height, width, generator=None, max_frames=CONTEXT, sink_frames=0, chunk=CHUNK,
-                 vae_stride=8, positions=1024, cuda_graph=False, static_heads=None, attention_entropy_ratio=None):
+                 vae_stride=8, positions=1024, cuda_graph=False, static_heads=None, attention_entropy_ratio=None,
+                 frames=None, shift=SHIFT, write_pass=True, context_noise=0):
         h, w = height // vae_stride, width // vae_stride
         self.tokens = (h // 2) * (w // 2)
         self.grid = (chunk, h // 2, w // 2)
         self.chunk, self.model = chunk, model
         n = chunk * self.tokens
         self.shape = (model.out_dim, chunk, h, w)
+        # attention sees at most max_frames with the chunk itself (reference causal.py:471-479); the ring takes a
+        # whole chunk at a time: no ring at all (sink and chunk fill the window) or at least a chunk's worth
+        window = max_frames if frames is None else min(max_frames, frames)
+        if not (sink_frames == window - chunk or 0 <= sink_frames <= window - 2 * chunk):
+            raise ValueError(f"sink_frames {sink_frames} leaves no whole chunk of ring in a window of {window}")
+        self.window = window
         heads = model.blocks[0].kv_heads  # all of them, or this tensor-parallel shard's
-        self.caches = [KVCache((max_frames - chunk) * self.tokens, sink_frames * self.tokens, n, heads, model.device,
+        self.caches = [KVCache((window - chunk) * self.tokens, sink_frames * self.tokens, n, heads, model.device,
                                attention_entropy_ratio) for _ in model.blocks]
         if static_heads:  # Forcing-KV: {block: [static heads]} (reference Stream, causal.py:490-494)
             rank, world = getattr(model.blocks[0], "rank", 0), getattr(model.blocks[0], "world", 1)
@@ -325,9 +334,12 @@ class Stream:
         self.chunk_freq = self.freq.clone()
         self.cross = model.cross_kvs(context.to(model.device))
         text_tokens = self.cross[0].tokens
-        self.buf = model.blocks[0].buffers(n, max_frames * self.tokens, text_tokens, model.device,
+        self.buf = model.blocks[0].buffers(n, window * self.tokens, text_tokens, model.device,
                                            lowrank=any(getattr(b, "lowrank", False) for b in model.blocks))
-        self.levels = sigmas()
+        self.levels = sigmas(shift=shift)
+        # write_pass False: no pass at t = 0, the cache keeps the keys and values of the last step (of x at the last
+        # noise level); context_noise: the timestep the chunk is written at (causal.py:534-538)
+        self.write_pass, self.context_noise = write_pass, context_noise
         self.generator = generator
         self.start = 0
         self.graphs = PassGraphs(model, self.shape) if cuda_graph else None
@@ -358,7 +370,13 @@ class Stream:
             if i + 1 < len(self.levels):
                 fresh = torch.randn(x0.shape, generator=self.generator, device=dev)
                 x = (1 - self.levels[i + 1]) * x0 + self.levels[i + 1] * fresh
-        run(x0, 0.0)  # the write pass: the clean chunk's keys and values
+        if self.write_pass:  # the chunk's keys and values for the cache (causal.py:725-738)
+            sigma = self.context_noise / 1000
+            if sigma > 0:
+                fresh = torch.randn(x0.shape, generator=self.generator, device=dev)
+                run((1 - sigma) * x0 + sigma * fresh, float(self.context_noise))
+            else:
+                run(x0, 0.0)
         for cache in self.caches:
             cache.commit(self.chunk, self.tokens)
         self.start += self.chunk
