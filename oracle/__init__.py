@@ -11,5 +11,7 @@ Parity pins: every function is checked against golden vectors made by the refere
 committed as tests/golden/*.npz). The W4A4 GEMM and the activation quantizer of Nunchaku, and SageAttention's
 kernel, are third-party code absent from the reference tree; their oracle here follows the published
 algorithm and the reference's call sites, pinned where the reference pins it (int4_groups rounding, the Sage
-quantizer layouts, the FP8 store bytes).
+quantizer layouts, the FP8 store bytes). Parity unpinned: the W4A4 GEMM's promotion of the exact group
+partials (Nunchaku @ 302e0e9), the fused MLP's unsigned hidden quantizer, and the Sage kernel's P V rounding
+(SageAttention 2.2.0) have no golden vector from their own code.
 """

@@ -12,6 +12,8 @@ Reference (src/wan_dit_lab/kernels/sage_kv.py; SageAttention 2.2.0's kernel itse
   - the attention: softmax(q k^T * sq * sk * sm_scale) (v * v_scale), sm_scale = D^-0.5 (sage_kv.py:133),
     non-causal over cache and chunk (native/ops/sage_ops.cpp:15-16). Exactly computed here over the
     dequantized operands (float64); subtracting the key mean leaves softmax unchanged.
+Parity unpinned for the kernel's own P V rounding (SageAttention's code is absent); the quantizers are pinned by
+the reference's Triton kernels run on the CPU.
 """
 
 import numpy as np

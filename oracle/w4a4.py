@@ -10,6 +10,8 @@ Reference:
     SVDQuant's published algorithm: per-group INT4 x INT4 -> INT32, promoted with both group scales).
   - smoothing: the kernel divides x by smooth before quantizing (w4a4.py:9-11, :177).
   - gelu_mlp: w4a4.py:195-204 — hidden = GELU_tanh(x W1^T + b1) + 0.171875 quantized unsigned [0, 15].
+Parity unpinned for the GEMM's promotion and the unsigned hidden quantizer (Nunchaku's code is absent); the weight
+and activation rounding (int4_groups) is pinned by the reference's own function.
 """
 
 import numpy as np
