@@ -32,7 +32,7 @@ extern "C" {
 #define WDL_F32 2
 
 /* How the W4A4 GEMM's operands hold their 4-bit integer codes, one code per byte. Both are exact for codes in
- * [-8, 15]. WDL_CODES_E4M3 (the default of the Python layer) holds the code's value as an FP8 E4M3 number: the
+ * [-8, 15]. WDL_CODES_E4M3 holds the code's value as an FP8 E4M3 number: the
  * tensor cores (tcgen05 kind::f8f6f4) then leave float32 group partials - exact integers - that need no
  * conversion before the scale promotion. WDL_CODES_INT8 holds two's complement int8 (tcgen05 kind::i8, int32
  * partials); signed codes only. WDL_CODES_E4M3_TS holds E4M3 codes and stores every group scale padded to 16
@@ -58,7 +58,7 @@ extern "C" {
  * whose scale is below 2^-25 of its row's largest rounds to float16 subnormals); the sum is the tensor core's
  * float32 accumulation, within float32 rounding of the per-group promotion (not bit-identical to it). Written by
  * wdl_w4a4_quantize_rows / wdl_ln_quant (bf16 scales only); signed codes only: the GELU epilogue of a GEMM in
- * this format writes the (unsigned) hidden layer in WDL_CODES_F16_FOLD. */
+ * this format writes the (unsigned) hidden layer in WDL_CODES_F16_FOLD. The default of the Python layer. */
 #define WDL_CODES_F16_PRE 4
 
 /* Message of the last failed call on this thread ("" if none). */

@@ -153,3 +153,21 @@ def test_new_entry_points_validate_before_any_launch(native):
     st = lib.wdl_w4a4_quantize_rows(FAKE, native.BF16, 256, None, 4, 256, native.F16, native.CODES_F16_PRE, FAKE, FAKE,
                                     None, None)
     assert st == native.ERR_ARGUMENT and b"bf16" in err()
+
+
+def test_a_c_program_uses_the_abi(native, tmp_path):
+    """include/wdl_b200.h is plain C11 and the library links into a C program (tests/native/abi_consumer.c), which
+    gets the version, the workspace sizes and the rejections of invalid calls, with their messages."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    lib = Path(native.LIBRARY)
+    exe = tmp_path / "abi_consumer"
+    subprocess.run([gcc, "-std=c11", "-Wall", "-Wextra", "-Werror", f"-I{ROOT / 'include'}",
+                    str(ROOT / "tests" / "native" / "abi_consumer.c"), f"-L{lib.parent}", f"-l:{lib.name}",
+                    f"-Wl,-rpath,{lib.parent}", "-o", str(exe)], check=True)
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert "PASSED" in run.stdout and "version wdl_b200" in run.stdout
