@@ -4,7 +4,6 @@ Bit-exact: activation/weight INT4 codes, their stored scales, the packed nibbles
 integer group partials read from the tensor-core accumulators. Within tolerance: the bf16 outputs (relative L2
 <= 1e-2 is the stated bar for linears; the float32 oracle rounded to bf16 is matched far tighter, <= 2e-3)."""
 
-
 import numpy as np
 import pytest
 import torch
