@@ -19,6 +19,9 @@ What each file holds and which reference code made it:
   kvcache.npz           generation/causal.py:160-337 KVCache bookkeeping (ring slots, eviction, anchors)
   w4a4_calibration.npz  quantization/w4a4.py:80-137 int4_groups(R, "mse") on heavy-tailed weights and gptq(R, H)
                         on correlated inputs with an idle channel (both on the CPU)
+  rope_stretched.npz    models/positions.py rope_at / stretch and runtime/live_presets.py:50-59 rope_table's rule:
+                        the time / height / width table with height and width stretched over the trained grid
+                        (the W4A4 Live preset: native 704x1280, 480x864, VAE stride 16), 256 positions, float32
   block_pack_layout.json  quantization/w4a4.py:269-313 layers() and pack_layout() of a small WanBlock, the
                         reference's own functions run with its quantize replaced by one that returns zero tensors
                         of this build's part shapes (its Nunchaku packer is not in the tree), on the CPU
@@ -247,6 +250,21 @@ def calibration_golden(reference):
          q_gptq=q_gptq.numpy(), s_gptq=s_gptq.numpy())
 
 
+def rope_stretched_golden(reference):
+    """The RoPE table of the W4A4 Live preset by the reference's own functions (runtime/live_presets.py:50-59 with
+    models/positions.py): time pairs from rope(), height and width from rope_at() at the positions stretched over
+    the trained token grid (stretch()), concatenated and cast to float32 as the preset's rope_dtype says; 256
+    positions instead of the preset's 65536 (the table's rows do not depend on the count)."""
+    sys.path.insert(0, str(Path(reference) / "src"))
+    from wan_dit_lab.models.positions import rope_at, stretch
+    from wan_dit_lab.models.rope import rope
+    d, count, cell = 128, 256, 2 * 16
+    scales = stretch([s // cell for s in (704, 1280)], [480 // cell, 864 // cell])
+    tables = [rope(count, d - 4 * (d // 6))] + [rope_at(count, 2 * (d // 6), sc) for sc in scales]
+    save("rope_stretched.npz", scales=np.array(scales), table=torch.cat(tables, dim=-1).to(torch.float32).numpy(),
+         at_half=rope_at(count, 42, 0.5).numpy())
+
+
 def block_pack_golden(reference):
     """The reference's pack layout rule (quantization/w4a4.py:269-313) on a WanBlock(256, 512, 2 heads): its
     parameter names and shapes, layers() fused and not, and pack_layout() for packs v1 and v2, rank 32 and 0, with
@@ -294,3 +312,4 @@ if __name__ == "__main__":
     kvcache_golden(sys.argv[1])
     block_pack_golden(sys.argv[1])
     calibration_golden(sys.argv[1])
+    rope_stretched_golden(sys.argv[1])

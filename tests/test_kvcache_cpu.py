@@ -1,7 +1,9 @@
 """The FP8 KV cache's bookkeeping on CPU tensors (generation/causal.py::KVCache): which ring slots a full cache's
 chunk replaces (the ring tokens earliest in the video, the chunk's token i into the i-th earliest: reference
 KVCache.commit / evicted, causal.py:298-337), and Forcing-KV's anchor rows (the sink and the newest finished
-frame, causal.py:243-248), checked against a plain restatement of those rules."""
+frame, causal.py:243-248), checked against a plain restatement of those rules and the reference's own KVCache
+(tests/golden/kvcache.npz). Also the host logic of Stream around the passes (the chunk schedule, the write pass,
+the window, the Forcing-KV and entropy-ratio wiring), with stand-in models on the CPU."""
 
 import sys
 from pathlib import Path
@@ -233,3 +235,4 @@ def test_stream_window_of_a_known_length_and_sink_rule():
     assert Stream(_Recorder(), ctx, 64, 64, vae_stride=16, max_frames=9, sink_frames=6).caches[0].max_tokens == 24
     with pytest.raises(ValueError):  # 4 sink frames leave 2 ring frames: less than a chunk
         Stream(_Recorder(), ctx, 64, 64, vae_stride=16, max_frames=9, sink_frames=4)
+

@@ -31,18 +31,27 @@ def sigmas(shift=SHIFT, steps=STEPS):
     return (shift * u / (1 + (shift - 1) * u)).tolist()
 
 
-def rope_table(positions, head_dim=128):
+def rope_at(count, dim, scale=1.0):
+    """cos / sin [2, count, dim / 2] float64 of one axis at the positions i * scale (models/rope.py:4-10 at scale 1,
+    models/positions.py rope_at otherwise): angle = position * 10000^(-2 j / dim)."""
+    pos = torch.arange(count, dtype=torch.float64)[:, None] * scale
+    ang = pos * 10000 ** (-2 * torch.arange(dim // 2, dtype=torch.float64) / dim)
+    return torch.stack((torch.cos(ang), torch.sin(ang)))
+
+
+def stretch(trained, now, strength=1.0):
+    """Position Interpolation of height and width (models/positions.py stretch): per side (trained / now) ** strength,
+    sizes in tokens, 1 where they are equal."""
+    return [(t / n) ** strength for t, n in zip(trained, now)]
+
+
+def rope_table(positions, head_dim=128, scales=None):
     """cos / sin [2, positions, head_dim / 2] float32 of the time / height / width axes (models/rope.py:4-10,
-    runtime/live_presets.py:52-61 with float32 tables): dims d - 4 (d // 6), 2 (d // 6), 2 (d // 6)."""
+    runtime/live_presets.py:50-59 with float32 tables): dims d - 4 (d // 6), 2 (d // 6), 2 (d // 6); scales (height,
+    width): their positions stretched over a trained grid (stretch), as the W4A4 Live preset's table."""
     d = head_dim
-
-    def rope(count, dim):
-        pos = torch.arange(count, dtype=torch.float64)[:, None]
-        ang = pos * 10000 ** (-2 * torch.arange(dim // 2, dtype=torch.float64) / dim)
-        return torch.stack((torch.cos(ang), torch.sin(ang)))
-
-    return torch.cat([rope(positions, d - 4 * (d // 6)), rope(positions, 2 * (d // 6)), rope(positions, 2 * (d // 6))],
-                     dim=-1).float()
+    hw = [rope_at(positions, 2 * (d // 6), s) for s in (scales or (1.0, 1.0))]
+    return torch.cat([rope_at(positions, d - 4 * (d // 6)), *hw], dim=-1).float()
 
 
 def shard_heads(static, rank, world, heads):
@@ -303,11 +312,11 @@ class Stream:
     cross_cache True, causal.py:450-758): next_chunk denoises a chunk in len(levels) passes, writes its keys and
     values with one more pass (write_pass; at t = context_noise, the clean chunk noised to it, 0 as trained), and
     commits them. frames: the video's length when known (the window is no longer than it); shift: of the noise
-    levels (sigmas)."""
+    levels (sigmas); rope_scales: height and width positions stretched over a trained grid (rope_table)."""
 
     def __init__(self, model, context, height, width, generator=None, max_frames=CONTEXT, sink_frames=0, chunk=CHUNK,
                  vae_stride=8, positions=1024, cuda_graph=False, static_heads=None, attention_entropy_ratio=None,
-                 frames=None, shift=SHIFT, write_pass=True, context_noise=0):
+                 frames=None, shift=SHIFT, write_pass=True, context_noise=0, rope_scales=None):
         h, w = height // vae_stride, width // vae_stride
         self.tokens = (h // 2) * (w // 2)
         self.grid = (chunk, h // 2, w // 2)
@@ -328,7 +337,7 @@ class Stream:
             for index, cache in enumerate(self.caches):
                 static = static_heads.get(index, static_heads.get(str(index), []))
                 cache.set_heads(shard_heads(static, rank, world, heads), heads)
-        self.freq = rope_table(positions).to(model.device)
+        self.freq = rope_table(positions, scales=rope_scales).to(model.device)
         # the chunk's table: its frames' time angles in rows 0.. (the kernels run with start 0), height / width
         # angles as in the whole table (reference Stream's chunk_freqs), refreshed in place before every chunk
         self.chunk_freq = self.freq.clone()
