@@ -22,6 +22,9 @@ What each file holds and which reference code made it:
   rope_stretched.npz    models/positions.py rope_at / stretch and runtime/live_presets.py:50-59 rope_table's rule:
                         the time / height / width table with height and width stretched over the trained grid
                         (the W4A4 Live preset: native 704x1280, 480x864, VAE stride 16), 256 positions, float32
+  model_edges.npz       models/model.py:32-41, 81-84 and models/head.py:13-18: WanModel's text embedding, time
+                        embedding / projection, patch embedding, head and unpatchify on a small seeded model,
+                        under bfloat16 autocast on the CPU as Stream runs it
   block_pack_layout.json  quantization/w4a4.py:269-313 layers() and pack_layout() of a small WanBlock, the
                         reference's own functions run with its quantize replaced by one that returns zero tensors
                         of this build's part shapes (its Nunchaku packer is not in the tree), on the CPU
@@ -265,6 +268,37 @@ def rope_stretched_golden(reference):
          at_half=rope_at(count, 42, 0.5).numpy())
 
 
+def model_edges_golden(reference):
+    """The edges of the reference's WanModel around the blocks (models/model.py:32-41 text / patch / time
+    embeddings, :81-84 head and unpatchify, models/head.py:13-18) on a small seeded model (dim 128, text_dim 64,
+    in / out 16), run under bfloat16 autocast on the CPU as its Stream runs the model (one chunk of 2 frames of
+    8 x 12 latents, t = 750); the state dict is saved with the outputs."""
+    sys.path.insert(0, str(Path(reference) / "src"))
+    from wan_dit_lab.models.model import WanModel
+    torch.manual_seed(61)
+    model = WanModel(dim=128, eps=1e-6, ffn_dim=512, freq_dim=256, in_dim=16, num_heads=1, num_layers=0, out_dim=16,
+                     text_len=8, text_dim=64).eval()
+    g = torch.Generator().manual_seed(62)
+    context = torch.randn(1, 8, 64, generator=g)
+    x = torch.randn(1, 16, 2, 8, 12, generator=g)
+    tokens = torch.randn(1, 2 * 4 * 6, 128, generator=g)  # the residual stream the head reads (float32)
+    t = torch.tensor([750.0])
+    with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16):
+        text = model.text_embedding(context)
+        patches = model.patch_embedding(x).flatten(2).transpose(1, 2)
+        omega = 10000 ** (-torch.arange(128, dtype=torch.float64) / 128)
+        theta = t.double()[:, None] * omega[None, :]
+        temb = model.time_embedding(torch.cat([torch.cos(theta), torch.sin(theta)], dim=1).float())
+        e0 = model.time_projection(temb).unflatten(1, (6, -1))
+        y = model.head(tokens, temb)
+        f, h, w = 2, 4, 6
+        out = y.view(1, f, h, w, 1, 2, 2, 16).permute(0, 7, 1, 4, 2, 5, 3, 6).reshape(1, 16, f, h * 2, w * 2)
+    state = {k: v.detach().numpy() for k, v in model.state_dict().items()}
+    save("model_edges.npz", context=context.numpy(), x=x.numpy(), tokens=tokens.numpy(),
+         text=text.float().numpy(), patches=patches.float().numpy(), temb=temb.float().numpy(),
+         e0=e0.float().numpy(), out=out.float().numpy(), **{"state." + k: v for k, v in state.items()})
+
+
 def block_pack_golden(reference):
     """The reference's pack layout rule (quantization/w4a4.py:269-313) on a WanBlock(256, 512, 2 heads): its
     parameter names and shapes, layers() fused and not, and pack_layout() for packs v1 and v2, rank 32 and 0, with
@@ -313,3 +347,4 @@ if __name__ == "__main__":
     block_pack_golden(sys.argv[1])
     calibration_golden(sys.argv[1])
     rope_stretched_golden(sys.argv[1])
+    model_edges_golden(sys.argv[1])
