@@ -25,6 +25,7 @@ What each file holds and which reference code made it:
   model_edges.npz       models/model.py:32-41, 81-84 and models/head.py:13-18: WanModel's text embedding, time
                         embedding / projection, patch embedding, head and unpatchify on a small seeded model,
                         under bfloat16 autocast on the CPU as Stream runs it
+  schedule.json         generation/causal.py:36-45 sigmas() at the default shift and at 3, STEPS, CHUNK, CONTEXT
   block_pack_layout.json  quantization/w4a4.py:269-313 layers() and pack_layout() of a small WanBlock, the
                         reference's own functions run with its quantize replaced by one that returns zero tensors
                         of this build's part shapes (its Nunchaku packer is not in the tree), on the CPU
@@ -299,6 +300,18 @@ def model_edges_golden(reference):
          e0=e0.float().numpy(), out=out.float().numpy(), **{"state." + k: v for k, v in state.items()})
 
 
+def schedule_golden(reference):
+    """The rollout's noise levels and sizes by the reference's own generation/causal.py (sigmas, STEPS, CHUNK,
+    CONTEXT, SHIFT)."""
+    import json
+    sys.path.insert(0, str(Path(reference) / "src"))
+    from wan_dit_lab.generation import causal
+    out = dict(shift=causal.SHIFT, steps=list(causal.STEPS), chunk=causal.CHUNK, context=causal.CONTEXT,
+               sigmas=causal.sigmas(), sigmas_shift3=causal.sigmas(shift=3.0))
+    (HERE / "schedule.json").write_text(json.dumps(out, indent=1), encoding="utf-8")
+    print("schedule.json:", out)
+
+
 def block_pack_golden(reference):
     """The reference's pack layout rule (quantization/w4a4.py:269-313) on a WanBlock(256, 512, 2 heads): its
     parameter names and shapes, layers() fused and not, and pack_layout() for packs v1 and v2, rank 32 and 0, with
@@ -348,3 +361,4 @@ if __name__ == "__main__":
     calibration_golden(sys.argv[1])
     rope_stretched_golden(sys.argv[1])
     model_edges_golden(sys.argv[1])
+    schedule_golden(sys.argv[1])

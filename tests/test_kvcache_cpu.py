@@ -236,3 +236,14 @@ def test_stream_window_of_a_known_length_and_sink_rule():
     with pytest.raises(ValueError):  # 4 sink frames leave 2 ring frames: less than a chunk
         Stream(_Recorder(), ctx, 64, 64, vae_stride=16, max_frames=9, sink_frames=4)
 
+
+
+def test_schedule_equals_the_reference():
+    """sigmas, STEPS, CHUNK, CONTEXT and SHIFT equal the reference's generation/causal.py (tests/golden/schedule.json,
+    made by its own functions)."""
+    import json
+    from wan_dit_lab_b200.generation import causal
+    g = json.loads((Path(__file__).resolve().parent / "golden" / "schedule.json").read_text())
+    assert causal.sigmas() == g["sigmas"] and causal.sigmas(shift=3.0) == g["sigmas_shift3"]
+    assert (causal.SHIFT, list(causal.STEPS), causal.CHUNK, causal.CONTEXT) == (g["shift"], g["steps"], g["chunk"],
+                                                                                 g["context"])
