@@ -57,3 +57,42 @@ def test_reference_arm_prints_on_rank_zero_only():
         assert bench.reference_arm(Args, rank=1, world=2) is None
     assert buf.getvalue() == ""
     assert torch.get_num_threads() >= 1
+
+
+def _rank_that_may_die(rank, world, port, out):
+    import datetime
+    import time
+    sys.path.insert(0, str(ROOT))
+    import bench
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(3)  # leaves between steps, before the collective that times the run
+    t0 = time.monotonic()
+    try:
+        bench.combine_ranks(dist, [1.0, 2.0], "cpu")
+        out[rank] = ("no error", time.monotonic() - t0)
+    except Exception as error:  # noqa: BLE001 - the error the surviving rank must see
+        out[rank] = (type(error).__name__, time.monotonic() - t0)
+
+
+def test_a_rank_that_dies_ends_the_others_collective_with_an_error():
+    """Failure detection on the host, as the multi-GPU runs rely on it: a rank that exits between steps makes the
+    next collective of the others (the max over ranks of the step times) fail with an error within the process
+    group's timeout instead of hanging."""
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = free_port()
+    procs = [ctx.Process(target=_rank_that_may_die, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung"
+    assert procs[1].exitcode == 3
+    assert 0 in out, "the surviving rank recorded nothing"
+    kind, waited = out[0]
+    assert kind != "no error" and waited < 60, out[0]
