@@ -171,3 +171,34 @@ def test_a_c_program_uses_the_abi(native, tmp_path):
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0, run.stdout + run.stderr
     assert "PASSED" in run.stdout and "version wdl_b200" in run.stdout
+
+
+def _ctype_of(decl):
+    """The ctypes type a C parameter or return declaration maps to: pointers as one kind, scalars by type."""
+    decl = decl.strip()
+    if "*" in decl:
+        return "pointer"
+    base = re.sub(r"\b(const|volatile)\b", "", decl).split()
+    base = base[0] if len(base) == 1 else base[-2] if len(base) > 1 else ""
+    return {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "size_t": ctypes.c_size_t, "float": ctypes.c_float,
+            "double": ctypes.c_double, "uint32_t": ctypes.c_uint32}[base]
+
+
+def test_binding_types_match_the_header_argument_by_argument(native):
+    """Every argument of every entry point is bound with the C type the header declares (pointers as pointers,
+    int / int64_t / size_t / float as such): a mismatch would pass garbage across the ABI, not fail."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    pointer_types = (ctypes.c_void_p, ctypes.c_char_p)
+    for m in re.finditer(r"^([A-Za-z_][\w \t\*]*?)\b(wdl_\w+)\s*\(([^)]*)\)\s*;", text, flags=re.M):
+        ret, name, params = m.group(1), m.group(2), m.group(3).strip()
+        restype, argtypes = native.SIGNATURES[name]
+        want_ret = _ctype_of(ret)
+        assert (restype in pointer_types) if want_ret == "pointer" else restype is want_ret, name
+        decls = [] if params in ("", "void") else [p for p in params.split(",")]
+        for i, (decl, got) in enumerate(zip(decls, argtypes)):
+            # a parameter "type name": drop the name to keep the type
+            want = _ctype_of(decl.rsplit(None, 1)[0] + (" *" if "*" in decl.rsplit(None, 1)[-1] else ""))
+            if want == "pointer":
+                assert got in pointer_types or hasattr(got, "_type_"), (name, i, decl)
+            else:
+                assert got is want, (name, i, decl, got)
