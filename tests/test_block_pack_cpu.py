@@ -138,3 +138,37 @@ def test_failed_build_leaves_nothing(tmp_path):
     with pytest.raises(ValueError, match="layout has"):
         w4a4.build_pack(blocks, {}, path, source, rank=4, fused=True, parts=[{}, {}])
     assert not any(tmp_path.glob("blocks.w4a4*"))
+
+
+def test_slot_builds_the_block_or_a_shard_over_the_rows_views(tmp_path, monkeypatch):
+    """slot hands the row's views (no copy on the row's own device) and the shapes from the layout to the block
+    class: WanBlockB200, or with shard=(rank, world) WanBlockTP with its reduce callable. The block classes are
+    stand-ins here (they need a GPU); what they receive is checked."""
+    from wan_dit_lab_b200.models import block, block_tp
+    source = tmp_path / "source.pt"
+    source.write_bytes(b"checkpoint identity")
+    blocks = [random_block(20)]
+    path = tmp_path / "blocks.w4a4"
+    w4a4.build_pack(blocks, {}, path, source, rank=4, fused=True, parts=[random_parts(blocks[0], True, 4, 21)])
+    rows, layout = w4a4.mapped_pack(1, path, source)
+    seen = []
+
+    def stand_in(kind):
+        def make(state, dim, ffn_dim, heads, *args, **kwargs):
+            seen.append((kind, state, dim, ffn_dim, heads, args, kwargs))
+            return kind
+        return make
+
+    monkeypatch.setattr(block, "WanBlockB200", stand_in("whole"))
+    monkeypatch.setattr(block_tp, "WanBlockTP", stand_in("shard"))
+    row = rows[0].clone()
+    assert w4a4.slot(row, w4a4.BlockShape(DIM, FFN, eps=1e-5), layout, device="cpu") == "whole"
+    kind, state, dim, ffn_dim, heads, args, kwargs = seen[-1]
+    assert (dim, ffn_dim, heads, args) == (DIM, FFN, DIM // 128, (1e-5,))
+    assert kwargs["parts"]["ffn.2"]["qweight"].data_ptr() >= row.data_ptr()  # views of the row, not copies
+    assert kwargs["parts"]["ffn.2"]["qweight"].untyped_storage().data_ptr() == row.untyped_storage().data_ptr()
+    assert torch.equal(state["norm3.weight"], blocks[0]["norm3.weight"].to(torch.bfloat16))
+    reduce = object()
+    assert w4a4.slot(row, None, layout, shard=(1, 2), reduce=reduce, device="cpu") == "shard"
+    kind, state, dim, ffn_dim, heads, args, kwargs = seen[-1]
+    assert args == (1, 2, 1e-6) and kwargs["reduce"] is reduce and kwargs["device"] == torch.device("cpu")

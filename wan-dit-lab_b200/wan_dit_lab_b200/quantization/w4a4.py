@@ -706,14 +706,15 @@ def slot_parts(row, layout):
     return parts, {e["name"]: view(e) for e in layout if e["name"] not in taken}
 
 
-def slot(row, like, layout, code_format=None):
+def slot(row, like, layout, code_format=None, shard=None, reduce=None, device="cuda"):
     """The block of a block_w4a4_v2 pack row as a WanBlockB200 (reference w4a4.py:399-416, which builds a module over
-    the row): a row on the host is copied to the current GPU once, the parts are views of that copy, and each layer
-    is prepared in the kernels' layout. like: the block's eps (from a WanBlock or a BlockShape; None: 1e-6). The
-    shapes come from the layout. Refused (ValueError): block_w4a4_v1 rows and rows that keep layers in bfloat16,
-    since the B200 block runs q, k, v as one W4A4 layer and the feed forward as the fused GELU MLP, whose second
-    layer is quantized for GELU's shifted output."""
-    from wan_dit_lab_b200.models.block import HEAD_DIM, WanBlockB200
+    the row): a row elsewhere is copied to `device` once, the parts are views of that copy, and each layer is
+    prepared in the kernels' layout. like: the block's eps (from a WanBlock or a BlockShape; None: 1e-6). The
+    shapes come from the layout. shard (rank, world): shard `rank` of the tensor-parallel block instead
+    (WanBlockTP, with `reduce` summing across shards). Refused (ValueError): block_w4a4_v1 rows and rows that keep
+    layers in bfloat16, since the B200 block runs q, k, v as one W4A4 layer and the feed forward as the fused GELU
+    MLP, whose second layer is quantized for GELU's shifted output."""
+    from wan_dit_lab_b200.models import block, block_tp
     kept = [e["name"][:-7] for e in layout if e["name"].endswith(".weight") and len(e["shape"]) == 2]
     if kept:
         raise ValueError(f"the B200 block runs every linear layer in W4A4; this pack keeps {kept} in bfloat16")
@@ -722,12 +723,19 @@ def slot(row, like, layout, code_format=None):
     if sorted(names) != sorted(FUSED_LAYERS) or not gelu:
         raise ValueError("a block_w4a4_v1 row (a layer per nn.Linear) cannot drive the B200 block, which runs q, k, "
                          "v as one W4A4 layer and the feed forward as the fused GELU MLP: pack with fused=True")
-    if not row.is_cuda:
-        row = row.to("cuda")
+    device = torch.device(device)
+    if row.device != device and not (device.type == row.device.type and device.index is None):
+        row = row.to(device)
     parts, params = slot_parts(row, layout)
     dim = params["modulation"].numel() // 6
     eps = getattr(like, "eps", None)
     if eps is None and hasattr(like, "norm1"):
         eps = like.norm1.eps
-    return WanBlockB200(params, dim, parts["ffn.0"]["qweight"].shape[0], dim // HEAD_DIM,
-                        1e-6 if eps is None else eps, device=row.device, parts=parts, code_format=code_format)
+    eps = 1e-6 if eps is None else eps
+    ffn_dim, heads = parts["ffn.0"]["qweight"].shape[0], dim // block.HEAD_DIM
+    if shard is None:
+        return block.WanBlockB200(params, dim, ffn_dim, heads, eps, device=row.device, parts=parts,
+                                  code_format=code_format)
+    rank, world = shard
+    return block_tp.WanBlockTP(params, dim, ffn_dim, heads, rank, world, eps, device=row.device, parts=parts,
+                               code_format=code_format, reduce=reduce)
