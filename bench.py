@@ -49,8 +49,7 @@ METRIC_LINEAR = "W4A4 GEMM TOPS vs INT8 peak"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 INT8_NOMINAL_TOPS = 4500.0
 CODES = "f16pre"  # operand code format of the W4A4 GEMM (--codes)
-GEMM_KERNEL = {"int8": "w4a4_gemm_kernel", "e4m3": "w4a4_gemm_kernel", "e4m3ts": "gemm_ts_kernel",
-               "f16fold": "gemm_fold_kernel", "f16pre": "gemm_pre_kernel (FFN-2: gemm_fold_kernel)"}
+GEMM_KERNEL = {"int8": "w4a4_gemm_kernel", "e4m3": "w4a4_gemm_kernel", "f16fold": "gemm_fold_kernel", "f16pre": "gemm_pre_kernel (FFN-2: gemm_fold_kernel)"}
 
 
 def _measured_bf16_peak():
@@ -395,9 +394,8 @@ def main():
     parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
     parser.add_argument("--workload", default="rollout", choices=sorted(WORKLOADS))
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
-    parser.add_argument("--codes", default="f16pre", choices=("e4m3", "e4m3ts", "f16fold", "f16pre", "int8"),
-                        help="operand code format of the W4A4 GEMM: e4m3 (kind::f8f6f4), e4m3ts (e4m3 with the group "
-                             "scale products on the tensor cores), f16fold (float16 codes and scale-folded weights, "
+    parser.add_argument("--codes", default="f16pre", choices=("e4m3", "f16fold", "f16pre", "int8"),
+                        help="operand code format of the W4A4 GEMM: e4m3 (kind::f8f6f4), f16fold (float16 codes and scale-folded weights, "
                              "kind::f16), f16pre (f16fold with the activation scales folded in too: all of K "
                              "accumulated on the tensor cores) or int8 (kind::i8)")
     parser.add_argument("--chunks", type=int, default=7, help="rollout chunks (profiling; BASELINE config 4: 7)")
@@ -493,7 +491,6 @@ def main():
         dtype = wl["dtype"].replace("int8 tensor cores", {
             "int8": "int8 tensor cores (kind::i8)",
             "e4m3": "e4m3-coded integers on fp8 tensor cores (kind::f8f6f4), exact",
-            "e4m3ts": "e4m3-coded integers on fp8 tensor cores, scale products by tf32 MMA, exact",
             "f16fold": "f16 tensor cores (kind::f16): int4 codes x int4 weights folded with their bf16 group scales, exact",
             "f16pre": "f16 tensor cores (kind::f16): int4 codes x bf16 scales on both operands (exact operands), "
                       "all of K accumulated in fp32 TMEM"}[CODES])

@@ -35,14 +35,9 @@ extern "C" {
  * [-8, 15]. WDL_CODES_E4M3 holds the code's value as an FP8 E4M3 number: the
  * tensor cores (tcgen05 kind::f8f6f4) then leave float32 group partials - exact integers - that need no
  * conversion before the scale promotion. WDL_CODES_INT8 holds two's complement int8 (tcgen05 kind::i8, int32
- * partials); signed codes only. WDL_CODES_E4M3_TS holds E4M3 codes and stores every group scale padded to 16
- * bytes, (s, 0, 0, 0) as 4 f32: scales [K/64, rows, 4]. The GEMM then forms the products of the activation and
- * weight scales on the tensor cores as well (a rank-1 tf32 MMA per group, exact), leaving one fused
- * multiply-add per element and group to the CUDA cores; same results as WDL_CODES_E4M3 bit for bit. With this
- * format N % 128 == 0 suffices and every scale array is 16-byte aligned. */
+ * partials); signed codes only. (Code 2 is not used.) */
 #define WDL_CODES_INT8 0
 #define WDL_CODES_E4M3 1
-#define WDL_CODES_E4M3_TS 2
 /* WDL_CODES_F16_FOLD holds float16 operands: activation codes as float16 integers (two bytes each), weights
  * folded with their group scales, w16 = code * sw * 2^-F (wdl_w4a4_fold_weight), exact when the weight scales are
  * bf16. The GEMM (tcgen05 kind::f16) then accumulates sw * 2^-F * P per group exactly and its epilogue needs one
@@ -102,8 +97,8 @@ int wdl_w4a4_fold_weight(const uint8_t* qweight, const void* wscales, int scale_
 
 /* y [M, N] bf16 (row stride ldy) = sum_g a_scales[g, m] * w_scales[g, n] * (sum_{k in g} a[m, k] w[n, k]) + bias[n]
  * on tcgen05 tensor cores. a [M, K] and w [N, K] codes in code_format (activation codes [-8, 15], weight codes
- * [-8, 7]), scales f32 ([K/64, M] and [K/64, N]), bias f32 [N] nullable. N % 256 == 0 (N % 128 == 0 with
- * WDL_CODES_E4M3_TS), K % 128 == 0, 16-byte aligned pointers. The GEMM of live::w4a4_linear (native/ops/w4a4_ops.cpp:36-38). */
+ * [-8, 7]), scales f32 ([K/64, M] and [K/64, N]), bias f32 [N] nullable. N % 256 == 0, K % 128 == 0, 16-byte
+ * aligned pointers. The GEMM of live::w4a4_linear (native/ops/w4a4_ops.cpp:36-38). */
 int wdl_w4a4_gemm(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                   const float* bias, int M, int N, int K, uint16_t* y, int64_t ldy, void* stream);
 
@@ -128,7 +123,7 @@ int wdl_w4a4_gemm_group_partials(const void* a, const float* a_scales, const voi
  * smooth_next ([N] bf16, nullable), quantized to UNSIGNED INT4 per group of 64 outputs (scale = max(max u, 1e-8)
  * / 15, code = round-half-even(u / scale) in [0, 15]) straight into the next layer's operand: codes [M, ldc]
  * (E4M3 format) and scales [N / 64, M] f32 rounded to scale_dtype. The hidden layer never exists in 16 bits.
- * code_format must be WDL_CODES_E4M3 or WDL_CODES_E4M3_TS (then the scales are written padded). */
+ * code_format must be WDL_CODES_E4M3 or one of the float16 formats. */
 int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                           const float* bias, const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N,
                           int K, uint8_t* codes, int64_t ldc, float* scales, void* stream);
@@ -177,9 +172,10 @@ int wdl_w4a4_linear(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t
  * no allocation of any kind inside. Its scratch (the activation's INT4 codes and scales between the quantizer and
  * the GEMM) is a fixed array of WDL_W4A4_LINEAR_NOALLOC_MAX_BYTES in the library's own device memory, held by
  * every device that loads the library until the process exits. Calls needing more than that (M * K * 17 / 16
- * bytes, rounded up; M * K * 5 / 4 with WDL_CODES_E4M3_TS) return WDL_ERR_ARGUMENT. The first call on a device resolves the array's device address
+ * bytes, rounded up) return WDL_ERR_ARGUMENT. The first call on a device resolves the array's device address
  * (cudaGetSymbolAddress) and should come before any stream capture. All calls on a device share the array: calls
- * that overlap on the GPU race and must be ordered by the caller. Otherwise as wdl_w4a4_linear.
+ * that overlap on the GPU race and must be ordered by the caller. code_format WDL_CODES_INT8 or WDL_CODES_E4M3;
+ * otherwise as wdl_w4a4_linear: a call it refuses launches nothing and leaves the array as it was.
  * No counterpart in the reference: live::w4a4_linear always allocates its scratch (native/ops/w4a4_ops.cpp:22-29). */
 #define WDL_W4A4_LINEAR_NOALLOC_MAX_BYTES ((size_t)16 << 20)
 int wdl_w4a4_linear_noalloc(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t* smooth, int scale_dtype,

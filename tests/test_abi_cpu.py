@@ -64,8 +64,8 @@ def test_gemm_shapes_rejected_before_any_launch(native):
 def test_workspace_sizes(native):
     lib = native.lib()
     M, K = 1392, 3072
-    # room for float16 codes and padded scales, whatever the code format
-    assert lib.wdl_w4a4_linear_workspace(M, K) == (M * K * 2 + 255) // 256 * 256 + (K // 64) * M * 16
+    # room for float16 codes and float32 group scales, whatever the code format
+    assert lib.wdl_w4a4_linear_workspace(M, K) == (M * K * 2 + 255) // 256 * 256 + (K // 64) * M * 4
     assert lib.wdl_w4a4_linear_workspace(0, K) == 0
     L, H = 5568, 24
     assert lib.wdl_sage_prep_workspace(L, H) == (2 * ((L + 63) // 64) + 1) * H * 128 * 4
@@ -89,6 +89,14 @@ def test_linear_validation(native):
     st = lib.wdl_w4a4_linear_noalloc(FAKE, 4096, M, 4096, None, native.BF16, FAKE, FAKE, native.CODES_E4M3, None, 256,
                                      FAKE, 256, None)
     assert st == native.ERR_ARGUMENT and b"16 MiB" in lib.wdl_last_error()
+    # the quantizer reads smooth 16 bytes at a time: a misaligned smooth is refused before anything runs
+    st = lib.wdl_w4a4_linear_noalloc(FAKE, 256, 128, 256, FAKE + 2, native.BF16, FAKE, FAKE, native.CODES_E4M3, None,
+                                     256, FAKE, 256, None)
+    assert st == native.ERR_ARGUMENT and b"smooth" in lib.wdl_last_error()
+    for f in (2, native.CODES_F16_FOLD):  # 2 names no format; the float16 formats are not taken here
+        st = lib.wdl_w4a4_linear_noalloc(FAKE, 256, 128, 256, None, native.BF16, FAKE, FAKE, f, None, 256, FAKE, 256,
+                                         None)
+        assert st == native.ERR_ARGUMENT and b"code format" in lib.wdl_last_error()
 
 
 def test_norm_and_cache_validation(native):

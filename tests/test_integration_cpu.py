@@ -66,3 +66,21 @@ def test_bad_requests_change_nothing():
     assert mods["sage_kv"].attend == "ref attend"  # only the steps asked for
     restore()
     assert mods["attention"].rope_apply == "ref rope"
+
+
+def test_a_step_that_fails_part_of_the_way_undoes_the_steps_before_it():
+    """A module that lacks an attribute a later step rebinds (here the operators module has no `load`): install
+    raises, and the rope / w4a4 / attention call sites it had already swapped are back to the reference's."""
+    from types import SimpleNamespace
+
+    from wan_dit_lab_b200 import integration
+    mods, _ = stand_ins()
+    original_store = mods["causal"].KVCache.store
+    mods["operators"] = SimpleNamespace()
+    with pytest.raises(AttributeError):
+        integration.install(**mods)
+    assert mods["attention"].rope_apply == "ref rope" and mods["w4a4"].rope_apply == "ref rope"
+    assert (mods["w4a4"].quantize, mods["w4a4"].w4a4_linear, mods["w4a4"].w4a4_gelu_mlp) == (
+        "ref quantize", "ref linear", "ref mlp")
+    assert mods["sage_kv"].attend == "ref attend"
+    assert mods["causal"].KVCache.store is original_store

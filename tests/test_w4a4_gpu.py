@@ -184,3 +184,36 @@ def test_invalid_arguments_raise_before_launch():
     st = _native.lib().wdl_w4a4_gemm(a.data_ptr(), s.data_ptr(), a.data_ptr(), s.data_ptr(), 1, None, 8, 200, 128,
                                     y.data_ptr(), 200, _native.stream())
     assert st == _native.ERR_ARGUMENT and b"256" in _native.lib().wdl_last_error()
+
+
+def test_prepared_layers_follow_the_weight_objects_not_their_addresses():
+    """w4a4_linear keeps each layer's device layout on its qweight tensor: a weight freed and another allocated in
+    its place (very likely at the same address) gets its own layout, an in-place change of a part is seen, and
+    many layers each keep theirs (no shared table to overflow)."""
+    from wan_dit_lab_b200.quantization import w4a4
+    g = torch.Generator().manual_seed(31)
+    M, K, N = 256, 512, 512
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+
+    def parts(seed):
+        gg = torch.Generator().manual_seed(seed)
+        return w4a4.quantize((torch.randn(N, K, generator=gg) * 0.02).cuda(), rank=0)
+
+    def fresh(p):
+        return w4a4.PackedW4A4Linear(**{k: v.clone() for k, v in p.items()})(x)
+
+    a = parts(1)
+    ya = w4a4.linear(x, a)
+    assert torch.equal(ya, fresh(a))
+    address = a["qweight"].data_ptr()
+    del a
+    b = parts(2)
+    yb = w4a4.linear(x, b)
+    assert torch.equal(yb, fresh(b)) and not torch.equal(yb, ya)
+    print("same address reused:", b["qweight"].data_ptr() == address)
+    b["wscales"].mul_(2)  # in place: the layout must be remade
+    assert torch.equal(w4a4.linear(x, b), fresh(b))
+    many = [parts(100 + i) for i in range(300)]  # more layers than one model holds, each its own layout
+    for p in many[:3] + many[-3:]:
+        assert torch.equal(w4a4.linear(x, p), fresh(p))
+    assert all(getattr(p["qweight"], "_wdl_prepared", None) is not None for p in many[:3] + many[-3:])

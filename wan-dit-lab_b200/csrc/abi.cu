@@ -118,16 +118,14 @@ int wdl_device_error(void* stream, uint32_t* code) {
 }
 
 static bool valid_codes(int f) {
-  return f == WDL_CODES_INT8 || f == WDL_CODES_E4M3 || f == WDL_CODES_E4M3_TS || f == WDL_CODES_F16_FOLD ||
-         f == WDL_CODES_F16_PRE;
+  return f == WDL_CODES_INT8 || f == WDL_CODES_E4M3 || f == WDL_CODES_F16_FOLD || f == WDL_CODES_F16_PRE;
 }
 
 // Bytes of one code in a code format's operand (float16 codes of the folded format take two).
 static int code_bytes(int f) { return f == WDL_CODES_F16_FOLD || f == WDL_CODES_F16_PRE ? 2 : 1; }
 static bool folded(int f) { return f == WDL_CODES_F16_FOLD || f == WDL_CODES_F16_PRE; }
 
-// Scale arrays of the padded format hold 16-byte entries read by TMA.
-static bool scales_aligned(const void* p, int code_format) { return aligned(p, code_format == WDL_CODES_E4M3_TS ? 16 : 4); }
+static bool scales_aligned(const void* p) { return aligned(p, 4); }
 
 int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16_t* smooth, int M, int K,
                            int scale_dtype, int code_format, void* codes, float* scales, uint8_t* packed,
@@ -143,7 +141,7 @@ int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16
   if (M == 0) return ok();
   if (!x || !codes || !scales) return fail(WDL_ERR_ARGUMENT, "x, codes and scales must not be null");
   if (!aligned(x, 16) || (ldx * esize) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "x rows must be 16-byte aligned");
-  if (!aligned(codes, 8 * code_bytes(code_format)) || !scales_aligned(scales, code_format) ||
+  if (!aligned(codes, 8 * code_bytes(code_format)) || !scales_aligned(scales) ||
       (packed && !aligned(packed, 4)) || (smooth && !aligned(smooth, 16)))
     return fail(WDL_ERR_ARGUMENT, "misaligned output or smooth pointer");
   wdl::w4a4::quantize_rows_launch(x, x_dtype, ldx, smooth, M, K, scale_dtype, code_format,
@@ -158,7 +156,7 @@ int wdl_w4a4_unpack_weight(const uint8_t* qweight, const void* wscales, int scal
   if (N <= 0 || K <= 0 || K % 64 != 0) return fail(WDL_ERR_ARGUMENT, "N > 0 and K a positive multiple of 64 required");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
   if (!qweight || !wscales || !codes || !scales) return fail(WDL_ERR_ARGUMENT, "null pointer");
-  if (!aligned(qweight, 4) || !aligned(codes, 8) || !aligned(wscales, 2) || !scales_aligned(scales, code_format))
+  if (!aligned(qweight, 4) || !aligned(codes, 8) || !aligned(wscales, 2) || !scales_aligned(scales))
     return fail(WDL_ERR_ARGUMENT, "misaligned pointer");
   wdl::w4a4::unpack_weight_launch(qweight, static_cast<const uint16_t*>(wscales), scale_dtype, N, K, code_format,
                                   static_cast<int8_t*>(codes), scales, static_cast<cudaStream_t>(stream));
@@ -187,16 +185,12 @@ static int gemm_common(wdl::w4a4::GemmArgs& a, void* stream) {
     return fail(WDL_ERR_ARGUMENT, "output and residual must be 16-byte aligned");
   const int f = a.code_format;
   const char* why = "";
-  const int v = f == WDL_CODES_E4M3_TS ? wdl::w4a4::gemm_ts_validate(a, &why)
-                : folded(f)             ? wdl::w4a4::gemm_fold_validate(a, &why)
-                                          : wdl::w4a4::gemm_validate(a, &why);
+  const int v = folded(f) ? wdl::w4a4::gemm_fold_validate(a, &why) : wdl::w4a4::gemm_validate(a, &why);
   if (v != 0) return fail(WDL_ERR_ARGUMENT, "%s", why);
   a.err = error_word();
   if (!a.err) return fail(WDL_ERR_CUDA, "cannot resolve the device error word");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int st = f == WDL_CODES_E4M3_TS ? wdl::w4a4::gemm_ts_launch(a, s, &why)
-                 : folded(f)             ? wdl::w4a4::gemm_fold_launch(a, s, &why)
-                                           : wdl::w4a4::gemm_launch(a, s, &why);
+  const int st = folded(f) ? wdl::w4a4::gemm_fold_launch(a, s, &why) : wdl::w4a4::gemm_launch(a, s, &why);
   if (st == 1) return fail(WDL_ERR_ARGUMENT, "%s", why);
   if (st != 0) return fail(WDL_ERR_CUDA, "%s", why);
   return ok();
@@ -311,10 +305,31 @@ int wdl_w4a4_gemm_gelu_u4_add(const void* a, const float* a_scales, const void* 
   return gemm_common(g, stream);
 }
 
+}  // extern "C"
+
+namespace wdl {
+// The bf16-output GEMM of a W4A4 linear over the quantized rows `codes` / `scales`, filled as every GEMM entry
+// point fills it (the same promotion variant) and checked on the host alone (shapes, alignment, tensor-map
+// limits), so that a linear the GEMM would refuse is refused before its quantizer writes anything.
+int linear_gemm_args(w4a4::GemmArgs& g, const void* codes, const float* scales, const void* w, const float* w_scales,
+                     int code_format, const float* bias, int M, int N, int K, uint16_t* y, int64_t ldy) {
+  operands(g, codes, scales, w, w_scales, code_format, M, N, K);
+  g.ep.mode = w4a4::kEpiBf16, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = ldy;
+  if (!codes || !scales || !w || !w_scales || !y) return fail(WDL_ERR_ARGUMENT, "null operand pointer");
+  if (!aligned(y, 16)) return fail(WDL_ERR_ARGUMENT, "output must be 16-byte aligned");
+  const char* why = "";
+  const int v = folded(code_format) ? w4a4::gemm_fold_validate(g, &why) : w4a4::gemm_validate(g, &why);
+  if (v != 0) return fail(WDL_ERR_ARGUMENT, "%s", why);
+  return ok();
+}
+}  // namespace wdl
+
+extern "C" {
+
 size_t wdl_w4a4_linear_workspace(int M, int K) {
   if (M <= 0 || K <= 0) return 0;
   const size_t codes = (static_cast<size_t>(M) * K * 2 + 255) / 256 * 256;  // room for float16 codes
-  const size_t scales = static_cast<size_t>(K / 64) * M * 16;  // room for the padded scales of WDL_CODES_E4M3_TS
+  const size_t scales = static_cast<size_t>(K / 64) * M * 4;
   return codes + scales;
 }
 
@@ -323,8 +338,7 @@ int wdl_w4a4_linear(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t
                     int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
   if (M < 0) return fail(WDL_ERR_ARGUMENT, "M must be >= 0");
   if (M == 0) return ok();
-  if (K % 128 != 0 || N % (code_format == WDL_CODES_E4M3_TS ? 128 : 256) != 0)
-    return fail(WDL_ERR_ARGUMENT, "K % 128 == 0 and N % 256 == 0 (N % 128 == 0 with padded scales) required");
+  if (K % 128 != 0 || N % 256 != 0) return fail(WDL_ERR_ARGUMENT, "K % 128 == 0 and N % 256 == 0 required");
   if (ldy < N || (ldy * 2) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldy must be >= N with 16-byte aligned rows");
   if (!valid_codes(code_format)) return fail(WDL_ERR_ARGUMENT, "unknown code format %d", code_format);
   const size_t need = wdl_w4a4_linear_workspace(M, K);
@@ -334,10 +348,12 @@ int wdl_w4a4_linear(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t
   if (!w || !w_scales) return fail(WDL_ERR_ARGUMENT, "null weight pointer");
   int8_t* codes = static_cast<int8_t*>(workspace);
   float* scales = reinterpret_cast<float*>(static_cast<char*>(workspace) + (static_cast<size_t>(M) * K * 2 + 255) / 256 * 256);
-  int st = wdl_w4a4_quantize_rows(x, WDL_BF16, ldx, smooth, M, K, scale_dtype, code_format, codes, scales, nullptr,
-                                  stream);
+  wdl::w4a4::GemmArgs g{};
+  int st = wdl::linear_gemm_args(g, codes, scales, w, w_scales, code_format, bias, M, N, K, y, ldy);
   if (st != WDL_OK) return st;
-  return wdl_w4a4_gemm(codes, scales, w, w_scales, code_format, bias, M, N, K, y, ldy, stream);
+  st = wdl_w4a4_quantize_rows(x, WDL_BF16, ldx, smooth, M, K, scale_dtype, code_format, codes, scales, nullptr, stream);
+  if (st != WDL_OK) return st;
+  return gemm_common(g, stream);
 }
 
 int wdl_store_kv_fp8(const void* k, int k_dtype, const int64_t* k_strides, const void* v, int v_dtype,
@@ -451,7 +467,7 @@ int wdl_ln_quant_keep(const void* x, int x_dtype, int64_t ldx, int M, int K, flo
       (code_format == WDL_CODES_F16_PRE && scale_dtype != WDL_BF16))
     return fail(WDL_ERR_ARGUMENT, "invalid code format or scale dtype (the prescaled format takes bf16 scales)");
   if (M == 0) return ok();
-  if (!codes || !scales || !aligned(codes, 8 * code_bytes(code_format)) || !scales_aligned(scales, code_format))
+  if (!codes || !scales || !aligned(codes, 8 * code_bytes(code_format)) || !scales_aligned(scales))
     return fail(WDL_ERR_ARGUMENT, "null or misaligned output");
   if (!aligned(ln_w, 16) || !aligned(ln_b, 16) || !aligned(mod_shift, 16) || !aligned(mod_scale, 16) ||
       !aligned(smooth, 16))

@@ -73,15 +73,18 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Waits for the phase of `bar` with the given parity to complete. Returns false (and records `code` in the
-// error word) if it did not within kWaitLimitNs, or if another thread has already recorded an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code) {
+// error word) if it did not within limit_ns nanoseconds (kWaitLimitNs unless the caller passes its own, as the
+// test kernel of tests/native/wait_check.cu does with a limit of about a millisecond), or if another thread has
+// already recorded an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0u) {
       if (*reinterpret_cast<volatile uint32_t*>(err) != 0) return false;
-      if (global_ns() - start > kWaitLimitNs) {
+      if (global_ns() - start > limit_ns) {
         atomicCAS(err, 0u, code);
         return false;
       }

@@ -24,10 +24,13 @@
 #include "w4a4_quant.h"
 
 namespace wdl {
-// Defined in abi.cu (C++ linkage, not part of the C ABI): the per-thread message of wdl_last_error, and the
-// device error word of the current device that bounded waits report into.
+// Defined in abi.cu (C++ linkage, not part of the C ABI): the per-thread message of wdl_last_error, the device
+// error word of the current device that bounded waits report into, and the host-side GEMM set-up.
 int set_last_error(int code, const char* message);
 uint32_t* device_error_word();
+// The bf16-output GEMM of a linear, filled and checked on the host as wdl_w4a4_linear does (abi.cu).
+int linear_gemm_args(w4a4::GemmArgs& g, const void* codes, const float* scales, const void* w, const float* w_scales,
+                     int code_format, const float* bias, int M, int N, int K, uint16_t* y, int64_t ldy);
 }  // namespace wdl
 
 namespace {
@@ -65,42 +68,42 @@ int wdl_w4a4_linear_noalloc(const uint16_t* x, int64_t ldx, int M, int K, const 
                             uint16_t* y, int64_t ldy, void* stream) {
   if (M < 0) return fail(WDL_ERR_ARGUMENT, "M must be >= 0");
   if (M == 0) return wdl::set_last_error(WDL_OK, "");
-  if (K <= 0 || K % 128 != 0 || N <= 0 || N % (code_format == WDL_CODES_E4M3_TS ? 128 : 256) != 0)
-    return fail(WDL_ERR_ARGUMENT, "K % 128 == 0 and N % 256 == 0 (N % 128 == 0 with padded scales) required");
-  if (code_format != WDL_CODES_INT8 && code_format != WDL_CODES_E4M3 && code_format != WDL_CODES_E4M3_TS)
-    return fail(WDL_ERR_ARGUMENT, "unknown code format (the folded float16 format is not supported here)");
+  if (K <= 0 || K % 128 != 0 || N <= 0 || N % 256 != 0)
+    return fail(WDL_ERR_ARGUMENT, "K % 128 == 0 and N % 256 == 0 required");
+  if (code_format != WDL_CODES_INT8 && code_format != WDL_CODES_E4M3)
+    return fail(WDL_ERR_ARGUMENT, "unknown code format (the float16 formats are not supported here)");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
   if (ldx < K || (ldx * 2) % 16 != 0 || ldy < N || (ldy * 2) % 16 != 0)
     return fail(WDL_ERR_ARGUMENT, "ldx >= K and ldy >= N with 16-byte aligned rows required");
   if (!x || !w || !w_scales || !y) return fail(WDL_ERR_ARGUMENT, "null pointer");
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15)
     return fail(WDL_ERR_ARGUMENT, "x, w and y must be 16-byte aligned");
+  // the quantizer reads smooth 16 bytes at a time
+  if (smooth && (reinterpret_cast<uintptr_t>(smooth) & 15)) return fail(WDL_ERR_ARGUMENT, "smooth must be 16-byte aligned");
   const size_t codes_bytes = (static_cast<size_t>(M) * K + 255) / 256 * 256;
-  const size_t scale_bytes = code_format == WDL_CODES_E4M3_TS ? 16 : sizeof(float);  // padded (s, 0, 0, 0)
-  const size_t need = codes_bytes + static_cast<size_t>(K / 64) * M * scale_bytes;
+  const size_t need = codes_bytes + static_cast<size_t>(K / 64) * M * sizeof(float);
   if (need > kScratchBytes)
     return fail(WDL_ERR_ARGUMENT,
-                "wdl_w4a4_linear_noalloc: M * K too large for its fixed 16 MiB scratch (needs M * K * 17 / 16 bytes, "
-                "M * K * 5 / 4 with padded scales); "
+                "wdl_w4a4_linear_noalloc: M * K too large for its fixed 16 MiB scratch (needs M * K * 17 / 16 bytes); "
                 "use wdl_w4a4_linear with a caller workspace");
   void* scratch = nullptr;
   const int st = scratch_address(&scratch);
   if (st != WDL_OK) return st;
-  uint32_t* err = wdl::device_error_word();
-  if (!err) return fail(WDL_ERR_CUDA, "wdl_w4a4_linear_noalloc: cannot resolve the device error word");
   int8_t* codes = static_cast<int8_t*>(scratch);
   float* scales = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + codes_bytes);
+  // the GEMM is filled as wdl_w4a4_linear fills it and checked on the host before anything is launched: a call it
+  // would refuse leaves the shared scratch untouched
+  wdl::w4a4::GemmArgs g{};
+  int gs = wdl::linear_gemm_args(g, codes, scales, w, w_scales, code_format, bias, M, N, K, y, ldy);
+  if (gs != WDL_OK) return gs;
+  g.err = wdl::device_error_word();
+  if (!g.err) return fail(WDL_ERR_CUDA, "wdl_w4a4_linear_noalloc: cannot resolve the device error word");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   wdl::w4a4::quantize_rows_launch(x, WDL_BF16, ldx, smooth, M, K, scale_dtype, code_format, codes, scales, nullptr, s);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(WDL_ERR_CUDA, "wdl_w4a4_linear_noalloc: quantizer launch failed");
-  wdl::w4a4::GemmArgs g{};
-  g.a = codes, g.lda = K, g.b = static_cast<const int8_t*>(w), g.ldb = K, g.wscale = w_scales, g.M = M, g.N = N, g.K = K;
-  g.a_signed = 1u, g.code_format = code_format, g.err = err;
-  g.ep.mode = wdl::w4a4::kEpiBf16, g.ep.ascale = scales, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = ldy;
   const char* why = "";
-  const int gs = code_format == WDL_CODES_E4M3_TS ? wdl::w4a4::gemm_ts_launch(g, s, &why)
-                                                   : wdl::w4a4::gemm_launch(g, s, &why);
+  gs = wdl::w4a4::gemm_launch(g, s, &why);
   if (gs == 1) return fail(WDL_ERR_ARGUMENT, why);
   if (gs != 0) return fail(WDL_ERR_CUDA, why);
   return wdl::set_last_error(WDL_OK, "");

@@ -175,10 +175,7 @@ __global__ void __launch_bounds__(kRowThreads, kPre ? 4 : 6) ln_quant_kernel(con
     if ((t & 7) == 0) {
       const float stored = a.scale_dtype == 1 ? __half2float(__float2half_rn(scale)) : bf16r(scale);
       const int64_t i = static_cast<int64_t>(k / 64) * a.M + m;
-      if (a.code_format == 2)  // padded (s, 0, 0, 0) for the tensor-core scale product
-        *reinterpret_cast<float4*>(a.scales + i * 4) = make_float4(stored, 0.f, 0.f, 0.f);
-      else
-        a.scales[i] = stored;
+      a.scales[i] = stored;
     }
   }
   if constexpr (kPre) {

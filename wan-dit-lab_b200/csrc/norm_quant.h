@@ -21,7 +21,7 @@ struct LnQuantArgs {
   const float* mod_scale;  // [K]
   const __nv_bfloat16* smooth;  // [K] (nullable)
   int scale_dtype;  // 0 bf16, 1 f16
-  int code_format;  // 0 int8, 1 e4m3, 2 e4m3 with padded scales, 3 float16 codes
+  int code_format;  // 0 int8, 1 e4m3, 3 float16 codes, 4 prescaled float16
   uint8_t* codes;   // [M, K] (two bytes per code in format 3)
   float* scales;    // [K / 64, M] ([K / 64, M, 4] as (s, 0, 0, 0) for code format 2)
   __nv_bfloat16* x_out;  // [M, ld_xo]: the layer's bf16 input before smoothing (nullable; a low-rank branch reads it)

@@ -20,8 +20,7 @@ namespace w4a4 {
 enum CodeFormat : int {
   kCodesInt8 = 0,  // two's complement int8 (tcgen05 kind::i8, int32 partials)
   kCodesE4M3 = 1,  // the code's value as an FP8 E4M3 number (tcgen05 kind::f8f6f4, fp32 partials)
-  kCodesE4M3Ts = 2,  // E4M3 codes, group scales padded to 16 bytes (s, 0, 0, 0): the tensor-core scale product
-                     // GEMM (w4a4_gemm_ts.cu), scales [K / 64, rows, 4]
+  // 2 is unused
   kCodesF16Fold = 3,  // float16 operands: activation codes, weights folded with their bf16 group scales and one
                       // power of two 2^-F (w4a4_gemm_fold.cu); the weight "scales" argument is the float 2^F
   kCodesF16Pre = 4,   // float16 activations with their bf16 group scales folded in too: code * sx * 2^-E_m, one
@@ -39,7 +38,7 @@ enum EpilogueMode : int {
 
 struct GemmEpilogue {
   int mode;
-  const float* ascale;    // [K / 64, M] activation group scales ([K / 64, M, 4] padded for kCodesE4M3Ts)
+  const float* ascale;    // [K / 64, M] activation group scales ([M] row powers of two for kCodesF16Pre)
   const float* bias;      // [N] or null
   const float* gate;      // [N] or null (kEpiResidualF32)
   const float* residual;  // [M, ld_res] f32 (kEpiResidualF32)
@@ -47,7 +46,7 @@ struct GemmEpilogue {
   void* out;  // bf16, f32 or int32 per mode, row stride ld_out elements
   int64_t ld_out;
   int dump_group;  // kEpiDumpGroup
-  float* out_scales;                // kEpiGeluU4: [N / 64, M] group scales of the hidden codes (padded x4 in ts)
+  float* out_scales;                // kEpiGeluU4: [N / 64, M] group scales of the hidden codes
   const __nv_bfloat16* out_smooth;  // kEpiGeluU4: [N] the next layer's smoothing (nullable)
   int out_scale_dtype;              // kEpiGeluU4: 0 bf16, 1 f16 rounding of the stored scales
   float gelu_shift;                 // kEpiGeluU4: added after GELU (0.171875)
@@ -74,7 +73,7 @@ struct GemmArgs {
   int64_t lda;      // bytes between rows of a (multiple of 16)
   const int8_t* b;  // [N, ldb] weight codes, one per byte
   int64_t ldb;
-  const float* wscale;  // [K / 64, N] weight group scales ([K / 64, N, 4] padded for kCodesE4M3Ts)
+  const float* wscale;  // [K / 64, N] weight group scales (the float 2^F for the float16 formats)
   int M, N, K;
   uint32_t a_signed;  // int8 codes: 1 signed, 0 unsigned (the fused MLP's hidden layer)
   int code_format;    // CodeFormat of both operands
@@ -87,10 +86,6 @@ struct GemmArgs {
 // Shape and alignment checks of gemm_launch alone (no CUDA call): 0, or 1 with *why set.
 int gemm_validate(const GemmArgs& a, const char** why);
 int gemm_launch(const GemmArgs& args, cudaStream_t stream, const char** why);
-
-// The same GEMM for kCodesE4M3Ts operands (N % 128 == 0, K % 128 == 0; scales padded, 16-byte aligned).
-int gemm_ts_validate(const GemmArgs& a, const char** why);
-int gemm_ts_launch(const GemmArgs& args, cudaStream_t stream, const char** why);
 
 // The same GEMM for kCodesF16Fold operands (N % 256 == 0, K % 64 == 0; wscale = the float 2^F; no dump mode).
 int gemm_fold_validate(const GemmArgs& a, const char** why);

@@ -61,21 +61,12 @@ __device__ __forceinline__ uint32_t code_pair_f16(int lo, int hi) {
          (static_cast<uint32_t>(__half_as_ushort(__int2half_rn(hi))) << 16);
 }
 
-// Scale i of a [K / 64, rows] scale array: one float32, or (scale_pad) the 16-byte (s, 0, 0, 0) that the
-// tensor-core scale product of the E4M3 / padded-scale GEMM loads as a tf32 operand row.
-__device__ __forceinline__ void store_scale(float* scales, int64_t i, int scale_pad, float s) {
-  if (scale_pad)
-    *reinterpret_cast<float4*>(scales + i * 4) = make_float4(s, 0.f, 0.f, 0.f);
-  else
-    scales[i] = s;
-}
-
 // kFmt: 0 int8 bytes, 1 E4M3 bytes, 3 float16 (two bytes per code)
 template <typename T, bool kSmooth, bool kPack, int kFmt>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ x, int64_t ldx,
                                                             const __nv_bfloat16* __restrict__ smooth, int M, int K,
                                                             int scale_dtype, int8_t* __restrict__ codes,
-                                                            float* __restrict__ scales, int scale_pad,
+                                                            float* __restrict__ scales,
                                                             uint8_t* __restrict__ packed) {
   const int lane = threadIdx.x & 31;
   const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -137,7 +128,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
         for (int i = 0; i < 4; ++i) pw |= static_cast<uint32_t>((q[2 * i] & 0xF) | ((q[2 * i + 1] & 0xF) << 4)) << (8 * i);
         *reinterpret_cast<uint32_t*>(packed + static_cast<int64_t>(m) * (K / 2) + k / 2) = pw;
       }
-      if ((lane & 7) == 0) store_scale(scales, static_cast<int64_t>(k / 64) * M + m, scale_pad, round_scale(scale, scale_dtype));
+      if ((lane & 7) == 0) scales[static_cast<int64_t>(k / 64) * M + m] = round_scale(scale, scale_dtype);
     }
   }
 }
@@ -302,24 +293,23 @@ __global__ void unpack_codes_kernel(const uint8_t* __restrict__ qweight, int64_t
   reinterpret_cast<uint2*>(codes)[i] = make_uint2(lo, hi);
 }
 
-__global__ void scales_to_f32_kernel(const uint16_t* __restrict__ in, int64_t n, int scale_dtype, int scale_pad,
+__global__ void scales_to_f32_kernel(const uint16_t* __restrict__ in, int64_t n, int scale_dtype,
                                      float* __restrict__ out) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const uint16_t b = in[i];
-  store_scale(out, i, scale_pad,
-              scale_dtype == 1 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b)));
+  out[i] = scale_dtype == 1 ? __half2float(__ushort_as_half(b)) : __bfloat162float(__ushort_as_bfloat16(b));
 }
 
 template <typename T, int kFmt>
 static void launch_rows(const void* x, int64_t ldx, const uint16_t* smooth, int M, int K, int scale_dtype,
-                        int8_t* codes, float* scales, int scale_pad, uint8_t* packed, cudaStream_t stream) {
+                        int8_t* codes, float* scales, uint8_t* packed, cudaStream_t stream) {
   const int threads = 256;
   const int blocks = (M * 32 + threads - 1) / threads;
   const T* xt = static_cast<const T*>(x);
   const __nv_bfloat16* sm = reinterpret_cast<const __nv_bfloat16*>(smooth);
   auto go = [&](auto kernel) {
-    kernel<<<blocks, threads, 0, stream>>>(xt, ldx, sm, M, K, scale_dtype, codes, scales, scale_pad, packed);
+    kernel<<<blocks, threads, 0, stream>>>(xt, ldx, sm, M, K, scale_dtype, codes, scales, packed);
   };
   if (smooth) {
     if (packed) go(quantize_rows_kernel<T, true, true, kFmt>);
@@ -333,7 +323,6 @@ static void launch_rows(const void* x, int64_t ldx, const uint16_t* smooth, int 
 void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_t* smooth, int M, int K,
                           int scale_dtype, int code_format, int8_t* codes, float* scales, uint8_t* packed,
                           cudaStream_t stream) {
-  const int pad = code_format == 2;
   auto go = [&](auto t) {
     using T = decltype(t);
     if (code_format == 4) {
@@ -358,9 +347,9 @@ void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_
       else quantize_rows_pre_kernel<T, false><<<blocks, 256, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
       return;
     }
-    if (code_format == 3) launch_rows<T, 3>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
-    else if (code_format != 0) launch_rows<T, 1>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
-    else launch_rows<T, 0>(x, ldx, smooth, M, K, scale_dtype, codes, scales, pad, packed, stream);
+    if (code_format == 3) launch_rows<T, 3>(x, ldx, smooth, M, K, scale_dtype, codes, scales, packed, stream);
+    else if (code_format != 0) launch_rows<T, 1>(x, ldx, smooth, M, K, scale_dtype, codes, scales, packed, stream);
+    else launch_rows<T, 0>(x, ldx, smooth, M, K, scale_dtype, codes, scales, packed, stream);
   };
   if (x_dtype == 2) go(float{});
   else go(__nv_bfloat16{});
@@ -375,8 +364,7 @@ void unpack_weight_launch(const uint8_t* qweight, const uint16_t* wscales, int s
   else
     unpack_codes_kernel<false><<<grid, 256, 0, stream>>>(qweight, words, codes);
   const int64_t ns = static_cast<int64_t>(K / 64) * N;
-  scales_to_f32_kernel<<<static_cast<unsigned>((ns + 255) / 256), 256, 0, stream>>>(wscales, ns, scale_dtype,
-                                                                                    code_format == 2, scales);
+  scales_to_f32_kernel<<<static_cast<unsigned>((ns + 255) / 256), 256, 0, stream>>>(wscales, ns, scale_dtype, scales);
 }
 
 }  // namespace w4a4

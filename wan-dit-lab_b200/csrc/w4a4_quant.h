@@ -9,8 +9,8 @@ namespace w4a4 {
 
 // x_dtype: 0 bf16, 2 f32. Requirements (checked by the caller): K % 64 == 0, ldx * size and x 16-byte aligned,
 // codes 8-byte aligned, packed 4-byte aligned.
-// code_format: 0 int8 two's complement, 1 E4M3, 2 E4M3 with scales padded to (s, 0, 0, 0), 3 float16 codes (two
-// bytes each, 16-byte aligned) (CodeFormat in w4a4_gemm.h); padded scales need 16-byte alignment.
+// code_format: 0 int8 two's complement, 1 E4M3, 3 float16 codes (two bytes each, 16-byte aligned), 4 prescaled
+// float16 values with one power of two per row (CodeFormat in w4a4_gemm.h).
 void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_t* smooth, int M, int K,
                           int scale_dtype, int code_format, int8_t* codes, float* scales, uint8_t* packed,
                           cudaStream_t stream);

@@ -14,7 +14,7 @@ LIBRARY = Path(__file__).resolve().parent / "libwdl_b200.so"
 
 OK, ERR_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3, 4
 BF16, F16, F32 = 0, 1, 2
-CODES_INT8, CODES_E4M3, CODES_E4M3_TS, CODES_F16_FOLD, CODES_F16_PRE = 0, 1, 2, 3, 4
+CODES_INT8, CODES_E4M3, CODES_F16_FOLD, CODES_F16_PRE = 0, 1, 3, 4
 DTYPE_CODE = {torch.bfloat16: BF16, torch.float16: F16, torch.float32: F32}
 
 _P, _I, _I64, _SZ, _U32P = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint32)

@@ -26,7 +26,8 @@ _NEEDS = {"rope": ("attention", "w4a4"), "kv_store": ("causal",), "w4a4": ("w4a4
 def install(steps=STEPS, **modules):
     """Rebinds the call sites of `steps` in the reference's `modules` (attention, w4a4, causal, sage_kv,
     operators) to this build's functions; returns a callable that puts every original back (in reverse order).
-    ValueError for an unknown step or a missing module, before anything is changed."""
+    ValueError for an unknown step or a missing module, before anything is changed; if a step raises part of the
+    way (an attribute the module lacks, a failed import), the steps already done are undone before it propagates."""
     steps = tuple(steps)
     for step in steps:
         if step not in _NEEDS:
@@ -40,29 +41,32 @@ def install(steps=STEPS, **modules):
         undo.append((owner, name, getattr(owner, name)))
         setattr(owner, name, value)
 
-    for step in steps:
-        if step == "rope":
-            from wan_dit_lab_b200.kernels.rope import rope_apply
-            rebind(modules["attention"], "rope_apply", rope_apply)
-            rebind(modules["w4a4"], "rope_apply", rope_apply)
-        elif step == "kv_store":
-            from wan_dit_lab_b200.kernels.cache_fp8 import install_cache_store
-            cls = modules["causal"].KVCache
-            undo.append((cls, "store", install_cache_store(cls)))
-        elif step == "w4a4":
-            from wan_dit_lab_b200.quantization import w4a4
-            for name in ("quantize", "w4a4_linear", "w4a4_gelu_mlp"):
-                rebind(modules["w4a4"], name, getattr(w4a4, name))
-        elif step == "attention":
-            from wan_dit_lab_b200.kernels import sage_kv
-            rebind(modules["sage_kv"], "attend", sage_kv.attend)
-        else:
-            from wan_dit_lab_b200.kernels import operators
-            rebind(modules["operators"], "load", operators.load)
-
     def restore():
         while undo:
             owner, name, value = undo.pop()
             setattr(owner, name, value)
 
+    try:
+        for step in steps:
+            if step == "rope":
+                from wan_dit_lab_b200.kernels.rope import rope_apply
+                rebind(modules["attention"], "rope_apply", rope_apply)
+                rebind(modules["w4a4"], "rope_apply", rope_apply)
+            elif step == "kv_store":
+                from wan_dit_lab_b200.kernels.cache_fp8 import install_cache_store
+                cls = modules["causal"].KVCache
+                undo.append((cls, "store", install_cache_store(cls)))
+            elif step == "w4a4":
+                from wan_dit_lab_b200.quantization import w4a4
+                for name in ("quantize", "w4a4_linear", "w4a4_gelu_mlp"):
+                    rebind(modules["w4a4"], name, getattr(w4a4, name))
+            elif step == "attention":
+                from wan_dit_lab_b200.kernels import sage_kv
+                rebind(modules["sage_kv"], "attend", sage_kv.attend)
+            else:
+                from wan_dit_lab_b200.kernels import operators
+                rebind(modules["operators"], "load", operators.load)
+    except BaseException:
+        restore()  # a step that fails part of the way leaves no module half swapped
+        raise
     return restore

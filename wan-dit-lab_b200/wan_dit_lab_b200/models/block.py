@@ -49,9 +49,9 @@ class Buffers:
         hd = heads * HEAD_DIM
         width = max(dim, ffn_dim)
         self.codes = torch.empty(n, 2 * width, **u8)  # room for the float16 codes of "f16fold"
-        self.scales = torch.empty(width // 64, n, 4, **f32)  # room for the padded scales of "e4m3ts"
+        self.scales = torch.empty(width // 64, n, **f32)
         self.hcodes = torch.empty(n, 2 * ffn_dim, **u8)  # rows of ffn_dim codes, one or two bytes each
-        self.hscales = torch.empty(ffn_dim // 64, n, 4, **f32)
+        self.hscales = torch.empty(ffn_dim // 64, n, **f32)
         self.qkv = torch.empty(n, 3 * hd, **bf)
         self.q = torch.empty(n, hd, **f32)
         self.k = torch.empty(n, hd, **f32)
@@ -313,10 +313,9 @@ class WanBlockB200:
                 trace["hcodes"] = raw[:n * fc1.N * 2].view(torch.float16).view(n, fc1.N).float()
             else:
                 trace["hcodes"] = raw[:n * fc1.N].view(torch.float8_e4m3fn).view(n, fc1.N).float()
-        if trace is not None:  # the hidden scales [ffn / 64, n] as the GEMM reads them (padded: element 0 of 4)
+        if trace is not None:  # the hidden scales [ffn / 64, n] as the GEMM reads them
             G = buf.hscales.shape[0]
-            keep("hscales", buf.hscales[..., 0] if fmt == _native.CODES_E4M3_TS
-                 else buf.hscales.view(-1)[:G * n].view(G, n))
+            keep("hscales", buf.hscales.view(-1)[:G * n].view(G, n))
         gemm_residual(fc2, 5, buf.hcodes, buf.hscales, add=None if gelu is None else lora(fc2, gelu))
         return X
 

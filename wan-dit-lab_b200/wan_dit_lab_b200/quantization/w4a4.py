@@ -15,6 +15,7 @@ nibble is unpacked inside the GEMM's main loop.
 """
 
 import math
+import weakref
 from pathlib import Path
 
 import torch
@@ -24,9 +25,7 @@ from wan_dit_lab_b200 import _native
 GROUP = 64  # input channels per INT4 scale (reference w4a4.py:29)
 # How the GEMM's operands hold the 4-bit codes in HBM, one per byte: E4M3 (the code's value as an FP8 number,
 # tcgen05 kind::f8f6f4, float32 group partials) or int8 (kind::i8, int32 partials). All exact; E4M3 spares
-# the promotion an int-to-float conversion per accumulator element and group. "e4m3ts" keeps E4M3 codes and
-# stores each group scale padded to 16 bytes (s, 0, 0, 0), so that the GEMM forms the scale products on the
-# tensor cores too (same results bit for bit, one CUDA-core operation per element and group instead of two).
+# the promotion an int-to-float conversion per accumulator element and group.
 # "f16fold" holds float16 operands: activation codes, and weights folded with their bf16 group scales (exact),
 # so that the GEMM's promotion is one fused multiply-add by the activation scale (same results bit for bit); a
 # layer whose folded weights would not be exact (non-bf16 scales) falls back to "e4m3". "f16pre" keeps the folded
@@ -51,8 +50,8 @@ def _scale_code(dtype):
 
 
 def _code_format(name):
-    return {"e4m3": _native.CODES_E4M3, "int8": _native.CODES_INT8, "e4m3ts": _native.CODES_E4M3_TS,
-            "f16fold": _native.CODES_F16_FOLD, "f16pre": _native.CODES_F16_PRE}[name]
+    return {"e4m3": _native.CODES_E4M3, "int8": _native.CODES_INT8, "f16fold": _native.CODES_F16_FOLD,
+            "f16pre": _native.CODES_F16_PRE}[name]
 
 
 def hidden_format(code_format):
@@ -62,17 +61,15 @@ def hidden_format(code_format):
 
 
 def scale_shape(groups, rows, code_format):
-    """Shape of a [groups, rows] scale array in the given code format (padded to 4 float32 for "e4m3ts"; one power
-    of two per row for "f16pre")."""
-    f = _code_format(code_format)
-    return (groups, rows, 4) if f == _native.CODES_E4M3_TS else (rows,) if f == _native.CODES_F16_PRE else (groups, rows)
+    """Shape of a [groups, rows] scale array in the given code format (one power of two per row for "f16pre")."""
+    return (rows,) if _code_format(code_format) == _native.CODES_F16_PRE else (groups, rows)
 
 
 def quantize_rows(x, scale_dtype=torch.bfloat16, smooth=None, packed=False, code_format="int8"):
     """Rows of x [M, K] (bfloat16 or float32, CUDA) in symmetric INT4 groups of GROUP: codes [M, K] int8, scales
     [K / GROUP, M] float32 (holding values rounded to scale_dtype) and, with packed, the nibbles [M, K / 2] uint8.
     code_format "int8" gives the codes as int8 integers, "e4m3" as the GEMM's E4M3 bytes (a uint8 tensor),
-    "e4m3ts" E4M3 bytes with scales [K / GROUP, M, 4] holding (s, 0, 0, 0), "f16fold" float16 codes, "f16pre"
+    "f16fold" float16 codes, "f16pre"
     float16 code * scale * 2^-E_m with the rows' 2^E_m [M] as scales (bf16 scales only).
     scale = max(max|x_g|, 1e-8) / 7, code = round-half-even(x / scale) clamped to [-8, 7] (the rule of
     int4_groups, reference w4a4.py:86-100); smooth [K] bfloat16 divides x first."""
@@ -242,7 +239,7 @@ def smoothing(act_amax, weight, alpha=0.5):
 
 class PreparedW4A4:
     """A W4A4 layer in the GEMM's device layout: codes [N, K] one byte each (CODE_FORMAT), scales [K/64, N]
-    float32 ([K/64, N, 4] padded in "e4m3ts"), bias [N] float32 (or None), smooth [K] bfloat16 (or None when it is all ones), made once from the
+    float32, bias [N] float32 (or None), smooth [K] bfloat16 (or None when it is all ones), made once from the
     packed parts."""
 
     def __init__(self, qweight, wscales, proj_down, proj_up, smooth, bias, code_format=None):
@@ -347,17 +344,28 @@ class PreparedW4A4:
         return y
 
 
-_prepared = {}
+def _stamp(parts):
+    """What a prepared layer was made from: for each part a weak reference to the tensor object and its in-place
+    version counter (None for an absent part)."""
+    return tuple(None if t is None else (weakref.ref(t), t._version) for t in parts)
+
+
+def _same_parts(stamp, parts):
+    return all((a is None) == (t is None) and (t is None or (a[0]() is t and a[1] == t._version))
+               for a, t in zip(stamp, parts))
 
 
 def _prepare(qweight, wscales, proj_down, proj_up, smooth, bias):
-    ver = lambda t: None if t is None else (t.data_ptr(), t._version)  # noqa: E731
-    key = (ver(qweight), ver(wscales), ver(bias), ver(smooth), ver(proj_down), ver(proj_up))
-    layer = _prepared.get(key)
-    if layer is None:
-        if len(_prepared) > 256:
-            _prepared.clear()
-        layer = _prepared[key] = PreparedW4A4(qweight, wscales, proj_down, proj_up, smooth, bias)
+    """The device layout of these packed parts, made once and kept on the qweight tensor itself (attribute
+    `_wdl_prepared`), so that it lives exactly as long as the weight does. A later call reuses it only with the very
+    same tensor objects, none modified in place since (object identity and version counter): a weight freed and
+    another allocated at its address never matches, and any number of layers and models keep their own."""
+    parts = (qweight, wscales, proj_down, proj_up, smooth, bias)
+    held = getattr(qweight, "_wdl_prepared", None)
+    if held is not None and _same_parts(held[0], parts):
+        return held[1]
+    layer = PreparedW4A4(*parts)
+    qweight._wdl_prepared = (_stamp(parts), layer)
     return layer
 
 
@@ -396,8 +404,7 @@ def w4a4_gelu_mlp(x, *parts):
     M, lib, st = x.shape[0], _native.lib(), _native.stream()
     work = torch.empty(lib.wdl_w4a4_linear_workspace(M, l1.K), dtype=torch.uint8, device=x.device)
     hidden = torch.empty(M * l1.N * 2, dtype=torch.uint8, device=x.device)  # the hidden codes, 1 or 2 bytes each
-    hscales = torch.empty(scale_shape(l1.N // GROUP, M, "e4m3ts" if l2.code_format == _native.CODES_E4M3_TS else
-                                      "e4m3"), dtype=torch.float32, device=x.device)
+    hscales = torch.empty(scale_shape(l1.N // GROUP, M, "e4m3"), dtype=torch.float32, device=x.device)
     gelu = torch.empty(M, l1.N, dtype=torch.float32, device=x.device) if l2.rank else None
     y = torch.empty(M, l2.N, dtype=torch.bfloat16, device=x.device)
     with torch.cuda.device(x.device):
