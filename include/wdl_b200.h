@@ -50,7 +50,8 @@ extern "C" {
  * 2^E_m [M] float32 as the activation "scales"; weights as WDL_CODES_F16_FOLD (the same folded buffers). Both
  * operands then carry every scale: the GEMM accumulates all of K on the tensor cores (no per-group promotion) and
  * multiplies each row by 2^E_m 2^F once. Exact operands (a code has <= 3 significant bits, a bf16 scale 8; a group
- * whose scale is below 2^-25 of its row's largest rounds to float16 subnormals); the sum is the tensor core's
+ * whose scale is below 2^-25 of its row's largest rounds to float16 subnormals, and one that then loses bits is
+ * reported as device error 8, see wdl_device_error); the sum is the tensor core's
  * float32 accumulation, within float32 rounding of the per-group promotion (not bit-identical to it). Written by
  * wdl_w4a4_quantize_rows / wdl_ln_quant (bf16 scales only); signed codes only: the GELU epilogue of a GEMM in
  * this format writes the (unsigned) hidden layer in WDL_CODES_F16_FOLD. The default of the Python layer. */
@@ -63,8 +64,11 @@ const char* wdl_last_error(void);
 const char* wdl_version(void);
 
 /* Synchronises `stream`, then reads and clears the device error word of the current device: *code = 0 when no
- * kernel gave up a bounded wait since the last call, else the first code recorded. Returns WDL_OK, or
- * WDL_ERR_DEVICE when *code != 0. No reference counterpart (the reference has no device-side waits). */
+ * kernel recorded an error since the last call, else the first code recorded: 1-6 a bounded wait given up (the
+ * kernel skipped its remaining work), 7 an index map entry out of range (read as 0), 8 a prescaled (f16pre) operand
+ * that could not hold a group's values exactly (a group scale more than 2^28 below its row's largest; the values
+ * were rounded: the call's result is refused). Returns WDL_OK, or WDL_ERR_DEVICE when *code != 0. No reference
+ * counterpart (the reference has no device-side waits). */
 int wdl_device_error(void* stream, uint32_t* code);
 
 /* ---- W4A4 (SVDQuant INT4 weights and activations, groups of 64 input channels) --------------------------- */

@@ -107,35 +107,39 @@ def attention_fp8_p(q, k, v_codes, v_scale, sm_scale=None, tile=128, p_scale=448
     """SageAttention 2's P V in FP8, per head: online softmax over key tiles of `tile` (running max m, sum l, the
     output rescaled by 2^(m_old - m_new)), each tile's P = E4M3(2^(s - m) * p_scale) times the FP8 V codes
     (float64 accumulation), the channel scale and 1 / (p_scale l) applied at the end. q, k dequantized
-    [B, n, H, D] / [B, L, H, D]; v_codes [B, L, H, D] the E4M3 values of V / v_scale; v_scale [B, H, D]."""
+    [B, n, H, D] / [B, L, H, D]; v_codes [B, L, H, D] the E4M3 values of V / v_scale; v_scale [B, H, D].
+
+    Evaluated without the loop over tiles: tile j's running max m_j is the cumulative maximum of the tiles' own
+    maxima, so every tile's P (and its E4M3 rounding) is formed at once with its own m_j, and the online rescaling
+    folds into one factor 2^(m_j - m_last) per tile and row. The same FP8 values as the loop; the float64 sums
+    differ from it only at float64 rounding."""
     q, k, vc = (np.asarray(t, np.float64) for t in (q, k, v_codes))
     sm_scale = q.shape[-1] ** -0.5 if sm_scale is None else sm_scale
     B, n, H, D = q.shape
     L = k.shape[1]
     out = np.empty((B, n, H, D))
     c = sm_scale * np.log2(np.e)
+    tiles = -(-L // tile)
+    pad = tiles * tile - L
     for b in range(B):
         for h in range(H):
             s = (q[b, :, h] @ k[b, :, h].T) * c
-            m = np.full(n, -np.inf)
-            lsum = np.zeros(n)
-            o = np.zeros((n, D))
-            for j in range(0, L, tile):
-                st = s[:, j:j + tile]
-                m_new = np.maximum(m, st.max(1))
-                alpha = np.exp2(m - m_new)
-                p = np.exp2(st - m_new[:, None])
-                lsum = lsum * alpha + p.sum(1)
-                p8 = from_e4m3_bits(to_e4m3_bits((p * p_scale).astype(np.float32))).astype(np.float64)
-                o = o * alpha[:, None] + p8 @ vc[b, j:j + tile, h]
-                m = m_new
+            st = np.pad(s, ((0, 0), (0, pad)), constant_values=-np.inf).reshape(n, tiles, tile)
+            m = np.maximum.accumulate(st.max(2), axis=1)  # [n, tiles]: the running max after each tile
+            p = np.exp2(st - m[:, :, None])  # each tile against its own running max
+            lsum = (p.sum(2) * np.exp2(m - m[:, -1:])).sum(1)
+            p8 = from_e4m3_bits(to_e4m3_bits((p * p_scale).astype(np.float32))).astype(np.float64)
+            p8 *= np.exp2(m - m[:, -1:])[:, :, None]  # the online rescaling, applied once per tile
+            o = p8.reshape(n, tiles * tile)[:, :L] @ vc[b, :, h]
             out[b, :, h] = o * v_scale[b, h][None, :] / (p_scale * lsum[:, None])
     return out
 
 
-def sage_attention(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=None, fp8_p=False):
+def sage_attention(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=None, fp8_p=False, rows=None):
     """sage_kv.attend on the dequantized Sage operands: what the INT8 / FP8 kernel approximates, exactly; with
-    fp8_p, P V in FP8 tile by tile as the kernel computes it (attention_fp8_p)."""
+    fp8_p, P V in FP8 tile by tile as the kernel computes it (attention_fp8_p). rows: the query rows to compute
+    (all when None); Q's INT8 scales are formed over every row first, so a row's result does not depend on which
+    others are computed."""
     Kf = load(cache_k, cache_ks, K, at)
     Vf = load(cache_v, cache_vs, V, at)
     kq, ks, _ = quant_k(Kf)
@@ -144,6 +148,8 @@ def sage_attention(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=N
     L = Kf.shape[1]
     kd = dequant_k(kq, ks)
     qd = dequant_q(qq, qs)
+    if rows is not None:
+        qd = qd[:, np.asarray(rows)]
     if fp8_p:
         return attention_fp8_p(qd, kd, from_e4m3_bits(unpermute_v(v8, L)), vs, sm_scale)
     vd = from_e4m3_bits(unpermute_v(v8, L)) * vs[:, None]

@@ -75,20 +75,25 @@ def group_partials(xq, wq, groups=None):
     return np.stack(out).astype(np.int32)
 
 
-def gemm(xq, sx, wq, sw, bias=None, chunk=16):
+def gemm(xq, sx, wq, sw, bias=None):
     """y [M, N] float32 = sum_g sx[g, m] * sw[g, n] * P_g[m, n] + bias[n], accumulated in float32 over g in order
     (sx [K/64, M], sw [K/64, N] are the stored, rounded scales)."""
     xq = np.asarray(xq, dtype=np.float32)
     wq = np.asarray(wq, dtype=np.float32)
+    sx = np.asarray(sx, dtype=np.float32)
+    sw = np.asarray(sw, dtype=np.float32)
     M, K = xq.shape
     N = wq.shape[0]
     G = K // GROUP
     y = np.zeros((M, N), dtype=np.float32)
-    for g0 in range(0, G, chunk):
-        gs = list(range(g0, min(G, g0 + chunk)))
-        P = group_partials(xq, wq, gs).astype(np.float32)
-        for i, g in enumerate(gs):
-            y += P[i] * (sx[g][:, None] * sw[g][None, :]).astype(np.float32)
+    P = np.empty((M, N), dtype=np.float32)
+    S = np.empty((M, N), dtype=np.float32)
+    for g in range(G):
+        s = slice(g * GROUP, (g + 1) * GROUP)
+        np.matmul(xq[:, s], wq[:, s].T, out=P)  # the exact integer partial P_g (float32 holds it exactly)
+        np.multiply(sx[g][:, None], sw[g][None, :], out=S)  # sx * sw, exact (two bf16 / f16 values)
+        np.multiply(P, S, out=P)
+        np.add(y, P, out=y)  # y += P_g (sx sw), in group order
     if bias is not None:
         y += np.asarray(bias, dtype=np.float32)[None, :]
     return y

@@ -183,3 +183,37 @@ def test_block_prescaled_matches_folded_block():
         outs[fmt] = Xd.cpu() - X
     assert native().device_error() == 0
     assert rel(outs["f16pre"].numpy(), outs["f16fold"].numpy()) <= 1e-3
+
+
+@pytest.mark.parametrize("span_log2", [20, 24, 34])
+def test_rows_with_widely_spread_group_scales_stay_exact_or_are_refused(span_log2):
+    """A row whose groups differ in scale by 2^span_log2 (one group of tiny values beside groups of ordinary ones).
+    The prescaled operand holds code * scale * 2^-E_m in float16: exact as long as every group's scale lies within
+    about 2^28 of its row's largest. Up to that the values equal the folded format's bit for bit and the GEMM the
+    exact per-group promotion (E4M3 codes) within float32 rounding; beyond it the quantizer refuses the row:
+    device error 8 (wdl_device_error), and the E4M3 format, which holds every group's scale apart, gives the exact
+    result for the same row."""
+    _native = native()
+    from wan_dit_lab_b200.quantization import w4a4
+    M, K, N = 64, 1024, 256
+    x = seeded((M, K), 11)
+    x[5, 128:192] *= 2.0 ** -span_log2  # group 2 of row 5: tiny, nonzero values
+    x[40, 0:64] *= 2.0 ** -span_log2
+    x = x.to(torch.bfloat16).cuda()
+    W = (seeded((N, K), 12) * 0.02).cuda()
+    parts = w4a4.quantize(W, rank=0)
+    assert _native.device_error() == 0
+    c3, s3 = w4a4.quantize_rows(x, torch.bfloat16, code_format="f16fold")
+    pre, rs = w4a4.quantize_rows(x, torch.bfloat16, code_format="f16pre")
+    layer = lambda fmt: w4a4.PreparedW4A4(*(parts[p] for p in w4a4.PARTS), code_format=fmt)  # noqa: E731
+    exact = layer("e4m3")(x).float()
+    if span_log2 <= 24:  # the tiny group's scale within 2^26 of the row's largest
+        assert _native.device_error() == 0
+        assert torch.equal(pre.view(torch.int16), expected_prescaled(c3, s3, rs).view(torch.int16))
+        y = layer("f16pre")(x).float()
+        assert _native.device_error() == 0
+        assert rel(y.cpu().numpy(), exact.cpu().numpy()) <= 2e-4
+    else:
+        with pytest.raises(RuntimeError, match="prescaled"):
+            _native.device_error()
+        assert _native.device_error() == 0  # read and cleared

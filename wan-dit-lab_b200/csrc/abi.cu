@@ -111,7 +111,11 @@ int wdl_device_error(void* stream, uint32_t* code) {
     const uint32_t zero = 0;
     cudaMemcpy(w, &zero, sizeof(zero), cudaMemcpyHostToDevice);
     return fail(WDL_ERR_DEVICE, "%s (device error code %u)",
-                *code == wdl::kErrIndex ? "an index map held an entry out of range" : "a kernel gave up a bounded wait",
+                *code == wdl::kErrIndex     ? "an index map held an entry out of range"
+                : *code == wdl::kErrInexact ? "a prescaled (f16pre) operand could not hold a group's values exactly: "
+                                              "a group scale lies more than 2^28 below its row's largest (use the "
+                                              "e4m3 or f16fold format for this layer)"
+                                            : "a kernel gave up a bounded wait",
                 *code);
   }
   return ok();
@@ -145,7 +149,8 @@ int wdl_w4a4_quantize_rows(const void* x, int x_dtype, int64_t ldx, const uint16
       (packed && !aligned(packed, 4)) || (smooth && !aligned(smooth, 16)))
     return fail(WDL_ERR_ARGUMENT, "misaligned output or smooth pointer");
   wdl::w4a4::quantize_rows_launch(x, x_dtype, ldx, smooth, M, K, scale_dtype, code_format,
-                                  static_cast<int8_t*>(codes), scales, packed, static_cast<cudaStream_t>(stream));
+                                  static_cast<int8_t*>(codes), scales, packed, error_word(),
+                                  static_cast<cudaStream_t>(stream));
   return cuda_status(cudaGetLastError(), "quantize_rows launch");
 }
 
@@ -480,6 +485,7 @@ int wdl_ln_quant_keep(const void* x, int x_dtype, int64_t ldx, int M, int K, flo
   a.smooth = reinterpret_cast<const __nv_bfloat16*>(smooth), a.scale_dtype = scale_dtype, a.code_format = code_format;
   a.codes = static_cast<uint8_t*>(codes), a.scales = scales;
   a.x_out = reinterpret_cast<__nv_bfloat16*>(x_out), a.ld_xo = ld_xo;
+  a.err = error_word();
   wdl::norm::ln_quant_launch(a, static_cast<cudaStream_t>(stream));
   return cuda_status(cudaGetLastError(), "ln_quant launch");
 }

@@ -29,7 +29,23 @@ enum DeviceError : uint32_t {
   kErrWaitScale = 5,     // the producer gave up waiting for a released scale stage
   kErrTmemAlloc = 6,     // the TMEM allocation did not return a usable address
   kErrIndex = 7,         // an index map held an entry out of range (the entry was read as 0)
+  kErrInexact = 8,       // a prescaled float16 operand could not hold a group's values exactly (rounded)
 };
+
+// Two values of a prescaled operand (code * stored scale * a power of two) as float16. The conversion is exact
+// unless a group's scale lies more than about 2^28 below the largest of its row (its values then fall below
+// float16's resolution); `inexact` is set when any bit was lost.
+__device__ __forceinline__ __half2 prescaled_pair(float v0, float v1, bool& inexact) {
+  const __half2 h = __floats2half2_rn(v0, v1);
+  const float2 back = __half22float2(h);
+  inexact |= (back.x != v0) | (back.y != v1);
+  return h;
+}
+
+// Records kErrInexact for a thread that saw an inexact prescaled value (err nullable).
+__device__ __forceinline__ void report_inexact(bool inexact, uint32_t* err) {
+  if (err && inexact) atomicCAS(err, 0u, static_cast<uint32_t>(kErrInexact));
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -74,8 +90,8 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 // Waits for the phase of `bar` with the given parity to complete. Returns false (and records `code` in the
 // error word) if it did not within limit_ns nanoseconds (kWaitLimitNs unless the caller passes its own, as the
-// test kernel of tests/native/wait_check.cu does with a limit of about a millisecond), or if another thread has
-// already recorded an error.
+// test kernel of tests/native/wait_check.cu does with a limit of about a millisecond), or if another wait has
+// already given up (codes up to kErrTmemAlloc; a data error such as kErrIndex or kErrInexact stops no kernel).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code,
                                           uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -83,7 +99,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0u) {
-      if (*reinterpret_cast<volatile uint32_t*>(err) != 0) return false;
+      const uint32_t seen = *reinterpret_cast<volatile uint32_t*>(err);
+      if (seen != 0 && seen <= kErrTmemAlloc) return false;
       if (global_ns() - start > limit_ns) {
         atomicCAS(err, 0u, code);
         return false;

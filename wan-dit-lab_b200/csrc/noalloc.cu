@@ -99,7 +99,8 @@ int wdl_w4a4_linear_noalloc(const uint16_t* x, int64_t ldx, int M, int K, const 
   g.err = wdl::device_error_word();
   if (!g.err) return fail(WDL_ERR_CUDA, "wdl_w4a4_linear_noalloc: cannot resolve the device error word");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  wdl::w4a4::quantize_rows_launch(x, WDL_BF16, ldx, smooth, M, K, scale_dtype, code_format, codes, scales, nullptr, s);
+  wdl::w4a4::quantize_rows_launch(x, WDL_BF16, ldx, smooth, M, K, scale_dtype, code_format, codes, scales, nullptr,
+                                  g.err, s);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(WDL_ERR_CUDA, "wdl_w4a4_linear_noalloc: quantizer launch failed");
   const char* why = "";

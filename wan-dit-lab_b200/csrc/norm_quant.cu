@@ -193,6 +193,7 @@ __global__ void __launch_bounds__(kRowThreads, kPre ? 4 : 6) ln_quant_kernel(con
     const float down = __uint_as_float((265u - e) << 23);
     if (t == 0) a.scales[m] = __uint_as_float((e - 11u) << 23);  // 2^(e - 138)
     uint16_t* out = reinterpret_cast<uint16_t*>(a.codes) + static_cast<int64_t>(m) * K;
+    bool inexact = false;
 #pragma unroll
     for (int c = 0; c < kRowChunks; ++c) {
       const int k = c * 1024 + t * 8;
@@ -204,12 +205,13 @@ __global__ void __launch_bounds__(kRowThreads, kPre ? 4 : 6) ln_quant_kernel(con
       for (int i = 0; i < 8; i += 2) {
         const int q0 = max(-8, min(7, __float2int_rn(div_rn_by(v[c][i], scale, r))));
         const int q1 = max(-8, min(7, __float2int_rn(div_rn_by(v[c][i + 1], scale, r))));
-        const __half2 h = __floats2half2_rn(__fmul_rn(static_cast<float>(q0) * stored, down),
-                                            __fmul_rn(static_cast<float>(q1) * stored, down));
+        const __half2 h = prescaled_pair(__fmul_rn(static_cast<float>(q0) * stored, down),
+                                         __fmul_rn(static_cast<float>(q1) * stored, down), inexact);
         w[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
       }
       *reinterpret_cast<uint4*>(out + k) = make_uint4(w[0], w[1], w[2], w[3]);
     }
+    report_inexact(inexact, a.err);
   }
 }
 

@@ -23,9 +23,10 @@ struct LnQuantArgs {
   int scale_dtype;  // 0 bf16, 1 f16
   int code_format;  // 0 int8, 1 e4m3, 3 float16 codes, 4 prescaled float16
   uint8_t* codes;   // [M, K] (two bytes per code in format 3)
-  float* scales;    // [K / 64, M] ([K / 64, M, 4] as (s, 0, 0, 0) for code format 2)
+  float* scales;    // [K / 64, M] (the rows' powers of two [M] in format 4)
   __nv_bfloat16* x_out;  // [M, ld_xo]: the layer's bf16 input before smoothing (nullable; a low-rank branch reads it)
   int64_t ld_xo;
+  uint32_t* err;  // device error word (nullable): format 4 records kErrInexact for a value it could not hold exactly
 };
 void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s);
 

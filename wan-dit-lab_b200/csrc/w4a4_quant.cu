@@ -137,7 +137,8 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
 // float16(code * stored scale * 2^-E_m) with one power of two per row, chosen from the row's largest stored scale
 // (8 * its largest |code * scale| * 2^-E_m lands in [2^14, 2^15)); rows_scale[m] = 2^E_m. Every value is exact: a
 // code has at most 3 significant bits and a bf16 scale 8, and it is a normal float16 number unless its group's
-// scale is below 2^-25 of the row's largest (then it rounds to a float16 subnormal). Two passes over the row
+// scale is below 2^-25 of the row's largest (then it rounds to a float16 subnormal, and a value that loses bits is
+// reported as kErrInexact in the error word). Two passes over the row
 // (the second reads it again from L1 / L2): the scales, then the values.
 __device__ __forceinline__ uint32_t exponent_field(float x) { return (__float_as_uint(x) >> 23) & 0xFFu; }
 
@@ -145,7 +146,7 @@ template <typename T, bool kSmooth>
 __global__ void __launch_bounds__(256) quantize_rows_pre_kernel(const T* __restrict__ x, int64_t ldx,
                                                                 const __nv_bfloat16* __restrict__ smooth, int M,
                                                                 int K, uint16_t* __restrict__ out,
-                                                                float* __restrict__ rows_scale) {
+                                                                float* __restrict__ rows_scale, uint32_t* err) {
   const int lane = threadIdx.x & 31;
   const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (m >= M) return;
@@ -185,6 +186,7 @@ __global__ void __launch_bounds__(256) quantize_rows_pre_kernel(const T* __restr
   const uint32_t e = exponent_field(top);  // top in [2^(e-127), 2^(e-126)): 8 top 2^(138-e) in [2^14, 2^15)
   const float down = __uint_as_float((265u - e) << 23);  // 2^(138 - e)
   if (lane == 0) rows_scale[m] = __uint_as_float((e - 11u) << 23);  // 2^(e - 138)
+  bool inexact = false;
   for (int k0 = 0; k0 < K; k0 += 256) {
     const int k = k0 + lane * 8;
     float v[8], scale, stored;
@@ -196,12 +198,13 @@ __global__ void __launch_bounds__(256) quantize_rows_pre_kernel(const T* __restr
     for (int i = 0; i < 8; i += 2) {
       const int q0 = max(-8, min(7, __float2int_rn(div_rn_by(v[i], scale, r))));
       const int q1 = max(-8, min(7, __float2int_rn(div_rn_by(v[i + 1], scale, r))));
-      const __half2 h = __floats2half2_rn(__fmul_rn(static_cast<float>(q0) * stored, down),
-                                          __fmul_rn(static_cast<float>(q1) * stored, down));
+      const __half2 h = prescaled_pair(__fmul_rn(static_cast<float>(q0) * stored, down),
+                                       __fmul_rn(static_cast<float>(q1) * stored, down), inexact);
       w[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
     }
     *reinterpret_cast<uint4*>(out + static_cast<int64_t>(m) * K + k) = make_uint4(w[0], w[1], w[2], w[3]);
   }
+  report_inexact(inexact, err);
 }
 
 // The same values with two warps per row (K <= 512 kChunks): the whole row in registers and one pass over it, so
@@ -209,7 +212,7 @@ __global__ void __launch_bounds__(256) quantize_rows_pre_kernel(const T* __restr
 template <typename T, bool kSmooth, int kChunks>
 __global__ void __launch_bounds__(64, kChunks > 2 ? 8 : 12)
     quantize_rows_pre2_kernel(const T* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ smooth, int M,
-                              int K, uint16_t* __restrict__ out, float* __restrict__ rows_scale) {
+                              int K, uint16_t* __restrict__ out, float* __restrict__ rows_scale, uint32_t* err) {
   __shared__ float red[2];
   const int t = threadIdx.x, m = blockIdx.x;
   const T* xr = x + static_cast<int64_t>(m) * ldx;
@@ -254,6 +257,7 @@ __global__ void __launch_bounds__(64, kChunks > 2 ? 8 : 12)
   const uint32_t e = exponent_field(top);
   const float down = __uint_as_float((265u - e) << 23);  // 2^(138 - e)
   if (t == 0) rows_scale[m] = __uint_as_float((e - 11u) << 23);  // 2^(e - 138)
+  bool inexact = false;
 #pragma unroll
   for (int c = 0; c < kChunks; ++c) {
     const int k = c * 512 + t * 8;
@@ -264,12 +268,13 @@ __global__ void __launch_bounds__(64, kChunks > 2 ? 8 : 12)
     for (int i = 0; i < 8; i += 2) {
       const int q0 = max(-8, min(7, __float2int_rn(div_rn_by(v[c][i], scale[c], r))));
       const int q1 = max(-8, min(7, __float2int_rn(div_rn_by(v[c][i + 1], scale[c], r))));
-      const __half2 h = __floats2half2_rn(__fmul_rn(static_cast<float>(q0) * stored[c], down),
-                                          __fmul_rn(static_cast<float>(q1) * stored[c], down));
+      const __half2 h = prescaled_pair(__fmul_rn(static_cast<float>(q0) * stored[c], down),
+                                       __fmul_rn(static_cast<float>(q1) * stored[c], down), inexact);
       w[i / 2] = *reinterpret_cast<const uint32_t*>(&h);
     }
     *reinterpret_cast<uint4*>(out + static_cast<int64_t>(m) * K + k) = make_uint4(w[0], w[1], w[2], w[3]);
   }
+  report_inexact(inexact, err);
 }
 
 // codes [N, K] from qweight [N, K/2]: one thread per 4 packed bytes (8 codes), 32-bit load, 64-bit store.
@@ -322,7 +327,7 @@ static void launch_rows(const void* x, int64_t ldx, const uint16_t* smooth, int 
 
 void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_t* smooth, int M, int K,
                           int scale_dtype, int code_format, int8_t* codes, float* scales, uint8_t* packed,
-                          cudaStream_t stream) {
+                          uint32_t* err, cudaStream_t stream) {
   auto go = [&](auto t) {
     using T = decltype(t);
     if (code_format == 4) {
@@ -333,8 +338,8 @@ void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_
       if (K <= 4096) {  // two warps per row, the row in registers
         auto go2 = [&](auto chunks) {
           constexpr int C = decltype(chunks)::value;
-          if (smooth) quantize_rows_pre2_kernel<T, true, C><<<M, 64, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
-          else quantize_rows_pre2_kernel<T, false, C><<<M, 64, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
+          if (smooth) quantize_rows_pre2_kernel<T, true, C><<<M, 64, 0, stream>>>(xt, ldx, sm, M, K, out, scales, err);
+          else quantize_rows_pre2_kernel<T, false, C><<<M, 64, 0, stream>>>(xt, ldx, sm, M, K, out, scales, err);
         };
         const int chunks = (K + 511) / 512;
         if (chunks <= 2) go2(std::integral_constant<int, 2>{});
@@ -343,8 +348,8 @@ void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_
         else go2(std::integral_constant<int, 8>{});
         return;
       }
-      if (smooth) quantize_rows_pre_kernel<T, true><<<blocks, 256, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
-      else quantize_rows_pre_kernel<T, false><<<blocks, 256, 0, stream>>>(xt, ldx, sm, M, K, out, scales);
+      if (smooth) quantize_rows_pre_kernel<T, true><<<blocks, 256, 0, stream>>>(xt, ldx, sm, M, K, out, scales, err);
+      else quantize_rows_pre_kernel<T, false><<<blocks, 256, 0, stream>>>(xt, ldx, sm, M, K, out, scales, err);
       return;
     }
     if (code_format == 3) launch_rows<T, 3>(x, ldx, smooth, M, K, scale_dtype, codes, scales, packed, stream);

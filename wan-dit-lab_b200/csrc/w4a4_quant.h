@@ -10,10 +10,11 @@ namespace w4a4 {
 // x_dtype: 0 bf16, 2 f32. Requirements (checked by the caller): K % 64 == 0, ldx * size and x 16-byte aligned,
 // codes 8-byte aligned, packed 4-byte aligned.
 // code_format: 0 int8 two's complement, 1 E4M3, 3 float16 codes (two bytes each, 16-byte aligned), 4 prescaled
-// float16 values with one power of two per row (CodeFormat in w4a4_gemm.h).
+// float16 values with one power of two per row (CodeFormat in w4a4_gemm.h). err (nullable): the device error word,
+// which the prescaled format sets to kErrInexact when a value could not be held exactly.
 void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_t* smooth, int M, int K,
                           int scale_dtype, int code_format, int8_t* codes, float* scales, uint8_t* packed,
-                          cudaStream_t stream);
+                          uint32_t* err, cudaStream_t stream);
 
 // N * K % 8 == 0; qweight 4-byte aligned, codes 8-byte aligned.
 void unpack_weight_launch(const uint8_t* qweight, const uint16_t* wscales, int scale_dtype, int N, int K,

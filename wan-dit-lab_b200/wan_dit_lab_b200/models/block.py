@@ -200,7 +200,9 @@ class WanBlockB200:
         [capacity, heads, 128] / [capacity, heads]; the chunk's keys and values are stored at `at` and attention
         runs over [0, at + n). freq [2, positions, 64] float32 RoPE table, grid (frames, h, w) of the chunk,
         start its first frame's time position. cross: CrossKV of the prompt. x_is_bf16: the stream held bf16
-        values (the first block of a model): the norms round to bf16 as .type_as does. trace: a dict that, when
+        values (the first block of a model): the first norm rounds to bf16 as .type_as does (the reference's
+        LayerNorm, models/layer_norm.py:5-7); its residual update makes the stream float32 (the gates are float32),
+        so the two later norms do not. trace: a dict that, when
         given, receives copies of the intermediate tensors (debugging; synchronizes). forcing: Forcing-KV's
         (static heads, dynamic heads, anchor rows) of the cache (KVCache.forcing()), or None: with it, the dynamic
         heads attend to the whole cached window and the static ones to the anchor rows (the sink and the newest
@@ -286,7 +288,8 @@ class WanBlockB200:
         gemm_residual(L["self_attn.o"], 2, add=lora(L["self_attn.o"], buf.attn))
         keep("x_after_self", X)
         # cross-attention
-        add = ln_quant(None, None, True, L["cross_attn.q"], x_is_bf16)
+        # the first residual update made the stream float32 (float32 gates): the later norms round only at the linear
+        add = ln_quant(None, None, True, L["cross_attn.q"], False)
         gemm(L["cross_attn.q"], buf.cq, add)
         keep("cq", buf.cq)
         _native.check(lib.wdl_rms_rows(buf.cq.data_ptr(), dim, n, dim, self.cross_norm_q.data_ptr(), self.eps,
@@ -301,7 +304,7 @@ class WanBlockB200:
         keep("x_after_cross", X)
         # feed forward
         fc1, fc2 = L["ffn.0"], L["ffn.2"]
-        add = ln_quant(3, 4, False, fc1, x_is_bf16)
+        add = ln_quant(3, 4, False, fc1, False)
         gelu = buf.gelu if fc2.rank else None  # the second layer's branch reads GELU's output without the shift
         timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4_add(
             buf.codes.data_ptr(), buf.scales.data_ptr(), fc1.codes.data_ptr(), fc1.scales.data_ptr(), fmt,

@@ -282,7 +282,8 @@ class WanBlockTP:
         yield buf.partial
         residual("self_attn.o", 2)
         # cross-attention on this shard's heads
-        add = ln_quant(None, None, True, L["cross_attn.q"], x_is_bf16)
+        # the first residual update made the stream float32 (float32 gates): the later norms round only at the linear
+        add = ln_quant(None, None, True, L["cross_attn.q"], False)
         gemm(L["cross_attn.q"], buf.cq, add)
         row_sums = buf.sumsq.view(-1)[:n]
         _native.check(lib.wdl_rows_sumsq(buf.cq.data_ptr(), d, n, d, 1, 0, row_sums.data_ptr(), st))
@@ -299,7 +300,7 @@ class WanBlockTP:
         residual("cross_attn.o", None)
         # feed forward on this shard's hidden channels
         fc1, fc2 = L["ffn.0"], L["ffn.2"]
-        add = ln_quant(3, 4, False, fc1, x_is_bf16)
+        add = ln_quant(3, 4, False, fc1, False)
         gelu = buf.gelu if fc2.rank else None  # the second layer's branch reads GELU's output (its shard's channels)
         timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4_add(
             buf.codes.data_ptr(), buf.scales.data_ptr(), fc1.codes.data_ptr(), fc1.scales.data_ptr(), fmt,
