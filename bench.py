@@ -22,9 +22,11 @@ collective on the data path); the time is the max over ranks, the value the sum 
 
 One JSON line (rank 0): metric/value/unit, e2e (the same call from pinned host buffers, copies included),
 roofline of the GEMM kernel (algorithmic int ops / its CUDA-event time vs the measured INT8 peak), the CPU
-baseline (the CPU oracle on the host cores, a bounded sample), clocks sampled by nvidia-smi while timing.
-`--impl reference` times the reference arithmetic on the host CPU (the oracle port in oracle/, since the
-reference's own W4A4 kernels are third-party sm_89 CUDA that neither runs on the CPU nor ships in its tree).
+baseline (the reference's own CPU torch path on the host cores, a bounded sample: ReferenceBlockPass), clocks
+sampled by nvidia-smi while timing. `--impl reference` times that same reference path, one block pass per step (its
+W4A4 and Sage kernels are third-party sm_89 CUDA that neither runs on a CPU nor ships in its tree; on a CPU the
+reference runs its block with bf16 nn.Linear layers and exact attention over the FP8 cache). The reference package
+is imported, unmodified, from baseline/_ref (baseline/install_reference.sh).
 """
 
 import argparse
@@ -210,17 +212,20 @@ def linear_workload(device):
                 cpu=lambda: cpu_linear_sample(x, W), dtype="int4 x int4 -> int32 (int8 tensor cores), fp32 promote")
 
 
-def cpu_linear_sample(x, W, rows=256):
-    """The oracle's W4A4 linear on `rows` tokens of the workload (quantize, exact group partials in fp32 BLAS,
-    scaled sum), single process with all host threads. Returns (seconds, int ops)."""
-    from oracle import w4a4 as ow
+def cpu_linear_sample(x, W, repeats=3):
+    """The reference's CPU torch path for this layer: its nn.Linear in bf16 (as its torch block runs q, k, v under
+    bf16 autocast; W4A4 itself has no CPU path in the reference), at full size, all host threads. Returns (seconds
+    per call, int ops, sample description)."""
     torch.set_num_threads(os.cpu_count())
-    wq, _, sw = ow.weight(W.numpy(), "float16")
-    xs = x[:rows].float().numpy()
+    xb, Wb = x.to(torch.bfloat16), W.to(torch.bfloat16)
+    torch.nn.functional.linear(xb, Wb)
     t0 = time.perf_counter()
-    ow.linear(xs, wq, sw, None, None, "float16")
-    dt = time.perf_counter() - t0
-    return dt, 2 * rows * W.shape[0] * W.shape[1], f"{rows} of 1392 tokens, full N and K (oracle port, numpy)"
+    for _ in range(repeats):
+        torch.nn.functional.linear(xb, Wb)
+    dt = (time.perf_counter() - t0) / repeats
+    return dt, 2 * x.shape[0] * W.shape[0] * W.shape[1], (
+        f"torch.nn.functional.linear in bf16 (the reference's nn.Linear) [1392,3072]x[9216,3072]^T at full size, "
+        f"{torch.get_num_threads()} threads, mean of {repeats} calls")
 
 
 def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True):
@@ -292,44 +297,82 @@ def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True):
                                                       "attention; fp32 residual stream")
 
 
-def cpu_block_sample(tokens=64):
-    """The oracle block (oracle/block.py) on `tokens` of a chunk at full width (dim 3072, 24 heads, FFN 14336,
-    1392 cached keys, 512 prompt tokens), all host threads; extrapolated by tokens to a 1392-token chunk, x 30
-    blocks x 35 passes per 21-frame rollout. Returns (seconds per rollout, frames, sample description)."""
-    from oracle import block as ob
-    from oracle import fp8 as of
-    from oracle import rope as orope
-    from oracle import w4a4 as ow
-    torch.set_num_threads(os.cpu_count())
-    dim, heads, ffn = 3072, 24, 14336
-    g = torch.Generator().manual_seed(11)
+REF_PACKAGE = ROOT / "baseline" / "_ref"
+BLOCK_PASSES_PER_ROLLOUT = 30 * 7 * 5  # 30 blocks x 7 chunks x (4 denoising passes + the write pass)
 
-    def packed(N, K):
-        W = (torch.randn(N, K, generator=g) * 0.02).numpy()
-        q, s, _ = ow.weight(W)
-        return dict(qweight=ow.pack_nibbles(q), wscales=ow.round_to(s, "bfloat16").T.copy(),
-                    bias=(torch.randn(N, generator=g) * 0.02).numpy())
 
-    parts = {"self_attn.qkv": packed(3 * dim, dim), "self_attn.o": packed(dim, dim), "cross_attn.q": packed(dim, dim),
-             "cross_attn.k": packed(dim, dim), "cross_attn.v": packed(dim, dim), "cross_attn.o": packed(dim, dim),
-             "ffn.0": packed(ffn, dim), "ffn.2": packed(dim, ffn)}
-    ones = np.ones(dim, np.float32)
-    norms = dict(norm_q=ones, norm_k=ones, cross_norm_q=ones, cross_norm_k=ones, norm3_w=ones, norm3_b=ones * 0)
-    at, n = 1392, tokens
-    cap = at + n
-    ck, cks = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
-    cv, cvs = of.quantize_rows(torch.randn(1, cap, heads, 128, generator=g).numpy())
-    cache = dict(k=ck, ks=cks, v=cv, vs=cvs)
-    X = torch.randn(n, dim, generator=g).numpy()
-    mod = (torch.randn(6, dim, generator=g) * 0.05).numpy()
-    text = ow.round_to(torch.randn(512, dim, generator=g).numpy(), "bfloat16")
-    freq = orope.table(64).astype(np.float32)
-    t0 = time.perf_counter()
-    ob.block(X, mod, parts, norms, cache, at, freq, (1, 1, n), 3, text, heads)
-    dt = time.perf_counter() - t0
-    per_rollout = dt * (1392 / n) * 30 * 35
-    return per_rollout, 21, (f"oracle block (numpy, {os.cpu_count()} threads) on {n} of 1392 tokens at full width, "
-                             "extrapolated x 1392/{n} tokens x 30 blocks x 35 passes per 21-frame rollout").replace("{n}", str(n))
+class ReferenceBlockPass:
+    """One pass of the reference's own Wan block on the host CPU, as its rollout runs it (reference
+    generation/causal.py Pass.run: the block under bf16 autocast; models/block.py WanBlock with nn.Linear layers,
+    models/multi_head_attention.py, KVCache(fp8=True).attend, which on a CPU stores the chunk in FP8 and attends
+    with exact SDPA over the cache read back to bf16). The reference package, unmodified, is imported from
+    baseline/_ref (baseline/install_reference.sh). Shapes of BASELINE config 3 inside the config-4 rollout: dim 3072,
+    24 heads, FFN 14336, a 1392-token chunk of 3 frames (16 x 29) over 4176 cached keys of 9 frames (the mean
+    cache fill before the 7 chunks of the rollout: 0, 1392, ... 8352 keys) and a 512-token prompt whose keys and
+    values are computed once (context_kv, as the reference's Stream caches them per prompt). Weights N(0, 0.02);
+    the linears in bf16, the norms and the modulation in float32 (a CPU layer_norm takes float32 parameters only).
+    Calling it times one pass (seconds); each pass writes the chunk at the same place, so passes repeat exactly."""
+
+    def __init__(self, tokens=1392, cached=4176, text=512, seed=11):
+        if not (REF_PACKAGE / "wan_dit_lab").is_dir():
+            raise RuntimeError(f"the reference package is not installed in {REF_PACKAGE}: run "
+                               "baseline/install_reference.sh")
+        if str(REF_PACKAGE) not in sys.path:
+            sys.path.insert(0, str(REF_PACKAGE))
+        from wan_dit_lab.generation.causal import KVCache
+        from wan_dit_lab.models.block import WanBlock
+        from wan_dit_lab.models.rope import rope
+        torch.set_num_threads(os.cpu_count())
+        dim, ffn, heads, per_frame = 3072, 14336, 24, 464
+        g = torch.Generator().manual_seed(seed)
+        blk = WanBlock(dim, ffn, heads, 1e-6)
+        with torch.no_grad():
+            for name, p in blk.named_parameters():
+                if name == "modulation":
+                    p.copy_(torch.randn(p.shape, generator=g) / dim ** 0.5)
+                elif "norm" in name:
+                    p.fill_(1.0 if name.endswith("weight") else 0.0)
+                else:
+                    p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+        for module in blk.modules():
+            if isinstance(module, torch.nn.Linear):
+                module.to(torch.bfloat16)
+        self.block = blk.eval()
+        d = 128  # the Live preset's float32 table: time / height / width pairs 22 / 21 / 21
+        self.freqs = torch.cat([rope(1024, d - 4 * (d // 6)), rope(1024, 2 * (d // 6)), rope(1024, 2 * (d // 6))],
+                               dim=-1).float()
+        self.grid = ((3, 16, 29),)
+        self.cache = KVCache(18 * per_frame, fp8=True, chunk=3)  # a window of 21 frames less the chunk
+        self.X = torch.randn(1, tokens, dim, generator=g)  # the float32 stream of blocks after the first
+        self.e0 = torch.randn(1, 6, dim, generator=g) * 0.1
+        context = torch.randn(1, text, dim, generator=g).to(torch.bfloat16)
+        with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16):
+            self.context_kv = blk.cross_attn.keys_values(context)
+            self.cache.allocate(torch.empty(1, tokens, heads, d, dtype=torch.bfloat16))
+            self.cache.store(0, torch.randn(1, cached, heads, d, generator=g), torch.randn(1, cached, heads, d, generator=g))
+        self.cache.saved, self.cache.frames = cached, cached // per_frame
+        self.threads = torch.get_num_threads()
+        self.sample = (f"the reference's own WanBlock (bf16 nn.Linear under autocast) + KVCache(fp8=True).attend (exact "
+                       f"SDPA over the FP8 cache) on the host CPU, {self.threads} threads: one block pass of {tokens} "
+                       f"tokens over {cached} cached keys and a {text}-token prompt, x {BLOCK_PASSES_PER_ROLLOUT} "
+                       "block passes (30 blocks x 35 passes) per 21-frame rollout")
+
+    @torch.no_grad()
+    def __call__(self):
+        with torch.autocast("cpu", dtype=torch.bfloat16):
+            t0 = time.perf_counter()
+            self.block(self.X, self.e0, grid_sizes=self.grid, freqs=self.freqs, context_kv=self.context_kv,
+                       start_frame=0, cache=self.cache)
+            return time.perf_counter() - t0
+
+
+def cpu_block_sample(passes=3):
+    """The CPU baseline of the rollout: the median of `passes` timed reference block passes (after one untimed),
+    extrapolated by block passes only. Returns (seconds per rollout, frames, sample description)."""
+    ref = ReferenceBlockPass()
+    ref()
+    per_pass = statistics.median(ref() for _ in range(passes))
+    return per_pass * BLOCK_PASSES_PER_ROLLOUT, 21, ref.sample + f"; median of {passes} passes"
 
 
 WORKLOADS = {"rollout": rollout_workload, "linear": linear_workload}
@@ -349,39 +392,43 @@ def job_rate(world, units_per_rank, seconds_max):
 
 
 def reference_arm(args, rank, world):
-    """The reference's arithmetic on the host CPU (the oracle port), each step a bounded sample of the workload,
-    on rank 0 only."""
+    """The reference's own CPU torch path on the host cores, on rank 0 only (the other ranks exit): each step one
+    reference block pass (rollout: value = 21 latent frames over the pass time x 1050 block passes per rollout) or
+    one full-size bf16 nn.Linear call (linear: TOPS)."""
     if rank != 0:
         return
-    torch.set_num_threads(os.cpu_count())
     times = []
     if args.workload == "rollout":
+        ref = ReferenceBlockPass()
         for _ in range(args.warmup):
-            cpu_block_sample(tokens=16)
-        for _ in range(args.steps):
-            per_rollout, frames, sample = cpu_block_sample(tokens=32)
-            times.append(per_rollout)
+            ref()
+        times = [ref() for _ in range(args.steps)]
         t = statistics.mean(times)
-        value, unit, metric = 21 / t, "latent frames/s", METRIC
-        config = {"workload": "BASELINE config 4 (30-layer rollout, 512x928), extrapolated from one oracle block on 32 "
-                              "tokens per step"}
+        value, unit, metric = 21 / (t * BLOCK_PASSES_PER_ROLLOUT), "latent frames/s", METRIC
+        sample = ref.sample
+        config = {"workload": "BASELINE config 4: 30-layer 5B DiT rollout, 512x928, 7 chunks x (4 DMD steps + write pass), "
+                              "FP8 KV window 21 frames", "step": "one reference block pass (BASELINE config 3 shapes, "
+                              "4176 cached keys); value extrapolates x 30 blocks x 35 passes", "threads": ref.threads}
+        dtype = "bf16 (the reference's nn.Linear under autocast), FP8 KV cache, exact SDPA"
     else:
         x = seeded((1392, 3072), 0, outliers=0.01).to(torch.bfloat16)
         W = seeded((9216, 3072), 1, scale=0.02)
         for _ in range(args.warmup):
-            cpu_linear_sample(x, W, rows=64)
+            cpu_linear_sample(x, W, repeats=1)
         for _ in range(args.steps):
-            dt, ops, sample = cpu_linear_sample(x, W, rows=128)
-            times.append(ops / dt)
-        value, unit, metric = statistics.mean(times) / 1e12, "TOPS", METRIC_LINEAR
-        t = 2 * 128 * 9216 * 3072 / (value * 1e12)
-        config = {"workload": "BASELINE config 1: W4A4 QKV linear X[1392,3072] x W[9216,3072]^T",
-                  "sample": "128 of 1392 tokens per step"}
+            dt, ops, sample = cpu_linear_sample(x, W, repeats=1)
+            times.append(dt)
+        t = statistics.mean(times)
+        value, unit, metric = ops / t / 1e12, "TOPS", METRIC_LINEAR
+        config = {"workload": "BASELINE config 1: W4A4 QKV linear X[1392,3072] x W[9216,3072]^T (bf16 nn.Linear on "
+                              "the CPU: the reference has no CPU W4A4 path)"}
+        dtype = "bf16"
     line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "W4A4 emulated exactly in float32/64 (numpy)",
-            "data": "synthetic (seeded, BASELINE shapes)", "config": config,
-            "cpu_baseline": {"value": value, "unit": unit, "cores": os.cpu_count(), "kind": "port", "sample": sample},
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded, BASELINE shapes)",
+            "config": config,
+            "cpu_baseline": {"value": value, "unit": unit, "cores": torch.get_num_threads(), "kind": "reference",
+                             "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -482,10 +529,12 @@ def main():
     if rank == 0 and not args.no_cpu:
         if rollout:
             per_rollout, frames, sample = wl["cpu"]()
-            cpu = {"value": frames / per_rollout, "unit": unit, "cores": os.cpu_count(), "kind": "port", "sample": sample}
+            cpu = {"value": frames / per_rollout, "unit": unit, "cores": torch.get_num_threads(), "kind": "reference",
+                   "sample": sample}
         else:
             dt, cpu_ops, sample = wl["cpu"]()
-            cpu = {"value": cpu_ops / dt / 1e12, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port", "sample": sample}
+            cpu = {"value": cpu_ops / dt / 1e12, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "reference",
+                   "sample": sample}
 
     if rank == 0:
         dtype = wl["dtype"].replace("int8 tensor cores", {
