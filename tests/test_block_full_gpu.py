@@ -127,12 +127,15 @@ def test_rms_norm_and_rope_of_q_and_k(run):
         rope_err = float(np.abs(run["gpu"][name].reshape(n, HEADS, 128) - rotated).max())
         b_oracle = orope.rms_norm(qkv[:, cols], np.ones(DIM, np.float32), round_to="bfloat16").reshape(n, HEADS, 128)
         equal = float((b_gpu == b_oracle).mean())
-        ulp = np.abs(b_oracle) * 2.0 ** -7 + 1e-30  # one bf16 step at the value's magnitude (upper bound)
-        worst_step = float((np.abs(b_gpu - b_oracle) / ulp).max())
-        print(f"{name}: RoPE max abs error {rope_err:.2e}; RMSNorm bf16 values equal {equal:.5f}, "
-              f"largest difference {worst_step:.2f} bf16 steps")
+        # one bf16 step at the larger value's magnitude, plus the float32 noise of rotating back (values of a few
+        # units: a few 1e-7), which for a value near zero is worth several of its own bf16 steps
+        top = np.maximum(np.abs(b_gpu), np.abs(b_oracle))
+        step = np.exp2(np.floor(np.log2(np.maximum(top, 2.0 ** -126))) - 7)
+        worst = float((np.abs(b_gpu - b_oracle) / (step + 1e-6)).max())
+        print(f"{name}: RoPE max abs error {rope_err:.2e}; RMSNorm bf16 values equal {equal:.5f}, largest "
+              f"difference {worst:.2f} (in bf16 steps + 1e-6)")
         assert rope_err <= ROPE_BAR
-        assert equal >= 0.999 and worst_step <= 1.0
+        assert equal >= 0.999 and worst <= 1.0
 
 
 def test_fp8_cache_rows_of_the_chunk(run):

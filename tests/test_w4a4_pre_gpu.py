@@ -185,29 +185,37 @@ def test_block_prescaled_matches_folded_block():
     assert rel(outs["f16pre"].numpy(), outs["f16fold"].numpy()) <= 1e-3
 
 
-@pytest.mark.parametrize("span_log2", [20, 24, 34])
-def test_rows_with_widely_spread_group_scales_stay_exact_or_are_refused(span_log2):
-    """A row whose groups differ in scale by 2^span_log2 (one group of tiny values beside groups of ordinary ones).
-    The prescaled operand holds code * scale * 2^-E_m in float16: exact as long as every group's scale lies within
-    about 2^28 of its row's largest. Up to that the values equal the folded format's bit for bit and the GEMM the
-    exact per-group promotion (E4M3 codes) within float32 rounding; beyond it the quantizer refuses the row:
-    device error 8 (wdl_device_error), and the E4M3 format, which holds every group's scale apart, gives the exact
-    result for the same row."""
+@pytest.mark.parametrize("case", ["within", "beyond"])
+def test_rows_with_widely_spread_group_scales_stay_exact_or_are_refused(case):
+    """Rows whose group scales lie far apart: a group of tiny values beside ordinary ones ("within": 2^-20 of the
+    row's scale), or beside a group of outliers 256 times larger ("beyond": the tiny group just above the 1e-8
+    floor of the scale rule, about 2^33 below the outliers). The prescaled operand holds code * scale * 2^-E_m in
+    float16: exact while every group's scale lies within about 2^28 of its row's largest. Within that the values
+    equal the folded format's bit for bit and the GEMM the exact per-group promotion (E4M3 codes) within float32
+    rounding; beyond it the quantizer refuses the row: device error 8 (wdl_device_error). The E4M3 format, which
+    holds every group's scale apart, is exact for the same rows. (A group below the 1e-8 floor quantizes to zeros,
+    which every format holds exactly.)"""
     _native = native()
     from wan_dit_lab_b200.quantization import w4a4
     M, K, N = 64, 1024, 256
     x = seeded((M, K), 11)
-    x[5, 128:192] *= 2.0 ** -span_log2  # group 2 of row 5: tiny, nonzero values
-    x[40, 0:64] *= 2.0 ** -span_log2
+    for row in (5, 40):
+        if case == "within":
+            x[row, 128:192] *= 2.0 ** -20
+        else:
+            x[row, 0:64] *= 256.0
+            x[row, 128:192] = x[row, 128:192] / x[row, 128:192].abs().max() * 1e-7  # max |x| = 1e-7 > 1e-8
     x = x.to(torch.bfloat16).cuda()
     W = (seeded((N, K), 12) * 0.02).cuda()
     parts = w4a4.quantize(W, rank=0)
+    layer = lambda fmt: w4a4.PreparedW4A4(*(parts[p] for p in w4a4.PARTS), code_format=fmt)  # noqa: E731
     assert _native.device_error() == 0
     c3, s3 = w4a4.quantize_rows(x, torch.bfloat16, code_format="f16fold")
-    pre, rs = w4a4.quantize_rows(x, torch.bfloat16, code_format="f16pre")
-    layer = lambda fmt: w4a4.PreparedW4A4(*(parts[p] for p in w4a4.PARTS), code_format=fmt)  # noqa: E731
+    assert bool((c3[5, 128:192] != 0).any())  # the tiny group holds nonzero codes
     exact = layer("e4m3")(x).float()
-    if span_log2 <= 24:  # the tiny group's scale within 2^26 of the row's largest
+    assert _native.device_error() == 0
+    pre, rs = w4a4.quantize_rows(x, torch.bfloat16, code_format="f16pre")
+    if case == "within":
         assert _native.device_error() == 0
         assert torch.equal(pre.view(torch.int16), expected_prescaled(c3, s3, rs).view(torch.int16))
         y = layer("f16pre")(x).float()

@@ -181,54 +181,69 @@ def _group_scales(R):
     return (top.cpu() / 7).to(R.device)
 
 
+def _lowrank_split(Ws, rank):
+    """W diag(s) = U V + R: the rank-r branch, up [N, r] (left singular vectors times their singular values) and
+    down [r, K], from the SVD of the smoothed weight, and the residual R left to INT4. rank 0: no branch, R = Ws."""
+    if not rank:
+        return Ws.new_zeros(Ws.shape[0], 0), Ws.new_zeros(0, Ws.shape[1]), Ws
+    left, sigma, right = torch.linalg.svd(Ws, full_matrices=False)
+    up, down = left[:, :rank] * sigma[:rank], right[:rank]
+    return up, down, Ws - up @ down
+
+
+def _round_residual(R, s, hessian, rule, scale_dtype):
+    """(codes [N, K], float32 group scales [N, K/64], packed nibbles [N, K/2]) of the residual. Without a Hessian
+    and with the "max" rule: to the nearest, by the quantizer kernel (the rounding of the forward path). Else on the
+    host side: the scale rule of int4_groups, or GPTQ with the second moment of what the INT4 branch multiplies R by,
+    x / s: H divided by s along both axes (a layer with K > 8192, whose H alone takes 0.8 GB, on the CPU)."""
+    if hessian is None and rule == "max":
+        codes, _, packed = quantize_rows(R.contiguous(), scale_dtype, packed=True)
+        return codes, _group_scales(R), packed
+    if hessian is None:
+        codes, scales = int4_groups(R, rule)
+    else:
+        host = torch.device("cpu") if R.shape[1] > 8192 else R.device
+        sh = s.to(host)
+        codes, scales = gptq(R.to(host), hessian.float().to(host).div(sh[:, None]).div(sh[None, :]))
+        codes, scales = codes.to(R.device), scales.to(R.device)
+    return codes, scales, _pack_nibbles(codes)
+
+
+def _shifted_bias(bias, shift, codes, scales, s):
+    """The layer's bias as float32; for a layer whose INT4 branch quantizes x + shift (gelu_mlp's second layer), less
+    what the shift adds through that branch, shift (R_q / s) 1, R_q being R as the codes and scales hold it
+    (w4a4.py:168-170): the low-rank branch reads x without the shift."""
+    N = codes.shape[0]
+    out = codes.new_zeros(N, dtype=torch.float32) if bias is None else bias.float().to(codes.device)
+    if not shift:
+        return out
+    held = (codes.view(N, -1, GROUP).float() * scales[..., None]).view(N, -1)
+    return out - shift * held.div(s[None, :]).sum(dim=1)
+
+
 @torch.no_grad()
 def quantize(weight, bias=None, smooth=None, rank=32, shift=0.0, hessian=None, rule="max", scale_dtype=torch.bfloat16):
     """The tensors of a W4A4 layer for y = x W^T + b (reference w4a4.py:141-180): dict(qweight [N, K/2] uint8,
     wscales [K/64, N], proj_down [K, r], proj_up [N, r], smooth [K], bias [N]), bfloat16 where not INT4, in the
     logical packed format of this module. weight [N, K] (on a CUDA device for the kernel's "max" rounding; the
-    offline rules run where it is); smooth [K] (ones when None); rank: of
-    the 16-bit low-rank branch taken from the SVD of W diag(s) (0: none); shift: the second layer of gelu_mlp
-    quantizes x + shift unsigned, and the bias takes off shift (R / s) 1 (w4a4.py:168-170). hessian [K, K]: X^T X
-    of the inputs the INT4 branch multiplies by R (x + shift for gelu_mlp's second layer, before smoothing): R is
-    rounded by GPTQ in the smoothed space instead of to the nearest. rule: the INT4 scale rule of int4_groups."""
+    offline rules run where it is); smooth [K] (ones when None): x is divided by it and W multiplied; rank: of the
+    16-bit low-rank branch (0: none); shift: the second layer of gelu_mlp quantizes x + shift unsigned
+    (_shifted_bias). hessian [K, K]: X^T X of the inputs the INT4 branch multiplies by R (x + shift for gelu_mlp's
+    second layer, before smoothing): R is rounded by GPTQ instead of to the nearest. rule: the INT4 scale rule of
+    int4_groups."""
     if hessian is None and rule == "max":
-        _cuda(weight, "weight")  # rounded by the quantizer kernel; the offline rules run on the weight's device
+        _cuda(weight, "weight")
     W = weight.float()
-    N, K = W.shape
-    s = torch.ones(K, device=W.device) if smooth is None else smooth.float().to(W.device)
-    Ws = W * s[None, :]
-    if rank:
-        U, S, Vh = torch.linalg.svd(Ws, full_matrices=False)
-        up, down = U[:, :rank] * S[:rank], Vh[:rank]
-        R = Ws - up @ down
-    else:
-        up, down = W.new_zeros(N, 0), W.new_zeros(0, K)
-        R = Ws
-    if hessian is None and rule == "max":  # the forward path's rounding, by the quantizer kernel
-        codes, _, packed = quantize_rows(R.contiguous(), scale_dtype, packed=True)
-        top = _group_scales(R)  # the fp32 scales of the codes
-    else:
-        if hessian is None:
-            codes, top = int4_groups(R, rule)
-        else:  # the INT4 branch sees x / s: the Hessian of x / s is diag(1/s) H diag(1/s) (w4a4.py:163-167)
-            # a wide layer (K = 14336: H alone is 0.8 GB) on the host, beside a model on the GPU
-            where = torch.device("cpu") if K > 8192 else W.device
-            Hs = hessian.float().to(where) / s.to(where)[:, None] / s.to(where)[None, :]
-            codes, top = gptq(R.to(where), Hs)
-            codes, top = codes.to(W.device), top.to(W.device)
-        packed = _pack_nibbles(codes)
-    b = torch.zeros(N, device=W.device) if bias is None else bias.float().to(W.device)
-    if shift:
-        Rq = (codes.view(N, K // GROUP, GROUP).float() * top[..., None]).view(N, K)  # R as INT4 holds it
-        b = b - shift * (Rq / s[None, :]).sum(dim=1)
-    return dict(
-        qweight=packed,
-        wscales=top.t().contiguous().to(scale_dtype),  # [K/64, N]
-        proj_down=(down / s[None, :]).t().contiguous().to(torch.bfloat16),  # [K, r]: the branch reads x itself
-        proj_up=up.contiguous().to(torch.bfloat16),  # [N, r]
-        smooth=s.to(torch.bfloat16),
-        bias=b.to(torch.bfloat16),
-    )
+    s = W.new_ones(W.shape[1]) if smooth is None else smooth.float().to(W.device)
+    up, down, R = _lowrank_split(W * s[None, :], rank)
+    codes, scales, packed = _round_residual(R, s, hessian, rule, scale_dtype)
+    bf = torch.bfloat16
+    return dict(qweight=packed,
+                wscales=scales.t().contiguous().to(scale_dtype),  # [K/64, N]
+                proj_down=(down / s[None, :]).t().contiguous().to(bf),  # [K, r]: the branch reads x, not x / s
+                proj_up=up.contiguous().to(bf),  # [N, r]
+                smooth=s.to(bf),
+                bias=_shifted_bias(bias, shift, codes, scales, s).to(bf))
 
 
 def smoothing(act_amax, weight, alpha=0.5):
@@ -605,99 +620,140 @@ def _put(row, entry, tensor, exact_shape):
     row[entry["offset"]:entry["offset"] + entry["bytes"]] = data
 
 
+class _PackFile:
+    """A pack being written: rows go to <path>.tmp as they come, hashed on the way; commit() makes the file durable,
+    moves it to <path> and writes the manifest beside it; abandon() removes every file it made. It never replaces an
+    existing pack, manifest or temporary file (FileExistsError before anything is opened)."""
+
+    def __init__(self, path):
+        import hashlib
+        self.path = Path(path)
+        self.manifest = self.path.with_name(self.path.name + ".json")
+        self.partial = self.path.with_name(self.path.name + ".tmp")
+        taken = next((f for f in (self.path, self.manifest, self.partial) if f.exists()), None)
+        if taken is not None:
+            raise FileExistsError(taken)
+        self.out = open(self.partial, "xb")
+        self.sha = hashlib.sha256()
+
+    def append(self, row):
+        data = memoryview(row.numpy())
+        self.sha.update(data)
+        self.out.write(data)
+
+    def commit(self, metadata):
+        import json
+        import os
+        self.out.flush()
+        os.fsync(self.out.fileno())
+        self.out.close()
+        os.replace(self.partial, self.path)
+        metadata = dict(metadata, sha256=self.sha.hexdigest())
+        self.manifest.write_text(json.dumps(metadata, indent=1), encoding="utf-8")
+        return metadata
+
+    def abandon(self):
+        self.out.close()
+        for f in (self.partial, self.path, self.manifest):
+            f.unlink(missing_ok=True)
+
+
+def _block_row(block, tensors, layout, size, groups, index):
+    """One block's uint8 row: its W4A4 parts (tensors: {layer: quantize tensors}) at their entries, then every other
+    parameter of the layout in bfloat16 (a W4A4 layer's float bias is not stored: its part is)."""
+    if set(tensors) != set(groups):
+        raise ValueError(f"block {index}: W4A4 tensors for {sorted(tensors)}, the layout has {sorted(groups)}")
+    entry = {e["name"]: e for e in layout}
+    row = torch.zeros(size, dtype=torch.uint8)
+    quantized = {f"{layer}.{part}" for layer in tensors for part in PARTS}
+    for name in sorted(quantized):
+        layer, part = name.rsplit(".", 1)
+        _put(row, entry[name], tensors[layer][part], True)
+    state = _state(block)
+    for e in layout:
+        if e["name"] not in quantized and e["name"] in state:
+            _put(row, e, state[e["name"]].detach().to(torch.bfloat16), False)
+    return row
+
+
 @torch.no_grad()
 def build_pack(blocks, amax, path, source, alpha=0.5, rank=32, fused=False, keep=(), hessians=None, rule="max",
                scale_dtype=torch.bfloat16, parts=None):
     """The blocks (modules or state dicts with WanBlock's names) as a pack at `path`, one uint8 row per block
-    (pack_layout), and its manifest <path>.json (reference w4a4.py:336-394): block_w4a4_v2 when fused, else
-    block_w4a4_v1. Written to <path>.tmp, synced, then renamed; nothing is left behind on failure, and an existing
-    pack, manifest or temporary file is never overwritten (FileExistsError). parts: per block the W4A4 tensors
-    already made ({layer: quantize tensors}, e.g. WanBlockB200.parts), instead of quantizing here."""
-    import hashlib
-    import json
-    import os
-
+    (pack_layout), and its manifest <path>.json, with the keys of the reference's (w4a4.py:361-394): block_w4a4_v2
+    when fused, else block_w4a4_v1, and "packing": "logical" for this build's part order. Written to <path>.tmp,
+    synced, then renamed; nothing is left behind on failure, and an existing pack, manifest or temporary file is
+    never overwritten (FileExistsError). parts: per block the W4A4 tensors already made ({layer: quantize tensors},
+    e.g. WanBlockB200.parts), instead of quantizing here."""
     from wan_dit_lab_b200.quantization.weight_pack import source_identity
-    path = Path(path)
-    manifest, temporary = path.with_suffix(path.suffix + ".json"), path.with_suffix(path.suffix + ".tmp")
-    if any(p.exists() for p in (path, manifest, temporary)):
-        raise FileExistsError(path)
     layout, size = pack_layout(blocks[0], fused, rank, keep, scale_dtype)
     groups = layers(blocks[0], fused, keep)
-    where = {e["name"]: e for e in layout}
-    digest, identity = hashlib.sha256(), source_identity(source)
+    before = source_identity(source)
+    pack = _PackFile(path)
     try:
-        with temporary.open("xb") as stream:
-            for index, block in enumerate(blocks):
-                if pack_layout(block, fused, rank, keep, scale_dtype) != (layout, size):
-                    raise ValueError("Packed blocks must share one layout")
-                state = _state(block)
-                tensors = parts[index] if parts is not None else layer_parts(
-                    state, index, amax, alpha, rank, fused, keep, None if hessians is None else hessians(index), rule,
-                    scale_dtype)
-                if set(tensors) != set(groups):
-                    raise ValueError(f"block {index}: W4A4 tensors for {sorted(tensors)}, the layout has "
-                                     f"{sorted(groups)}")
-                row = torch.zeros(size, dtype=torch.uint8)
-                written = set()
-                for g, t in tensors.items():
-                    for part in PARTS:
-                        _put(row, where[f"{g}.{part}"], t[part], True)
-                        written.add(f"{g}.{part}")
-                for e in layout:  # the rest in bfloat16; a W4A4 layer's bias is one of its parts
-                    if e["name"] in state and e["name"] not in written:
-                        _put(row, e, state[e["name"]].detach().to(torch.bfloat16), False)
-                payload = row.numpy().tobytes()
-                digest.update(payload)
-                stream.write(payload)
-            stream.flush()
-            os.fsync(stream.fileno())
-        if source_identity(source) != identity:
+        for index, block in enumerate(blocks):
+            if pack_layout(block, fused, rank, keep, scale_dtype) != (layout, size):
+                raise ValueError("Packed blocks must share one layout")
+            if parts is not None:
+                tensors = parts[index]
+            else:
+                tensors = layer_parts(_state(block), index, amax, alpha, rank, fused, keep,
+                                      None if hessians is None else hessians(index), rule, scale_dtype)
+            pack.append(_block_row(block, tensors, layout, size, groups, index))
+        if source_identity(source) != before:
             raise RuntimeError("Checkpoint changed during conversion")
-        os.replace(temporary, path)
-        metadata = dict(format=FORMATS[1] if fused else FORMATS[0], packing=PACKING, blocks=len(blocks), layout=layout,
-                        bytes_per_block=size, bytes=size * len(blocks), sha256=digest.hexdigest(), source=identity,
-                        alpha=alpha, rank=rank, calibrated=sorted(amax), bfloat16_layers=sorted(keep),
-                        rounding="nearest", scale_rule=rule,
-                        quantization="SVDQuant W4A4: INT4 groups of 64, low-rank branch of rank r in bfloat16, "
-                        "SmoothQuant smoothing from calibrated activation maxima; parts in logical order"
-                        + ("; q, k, v of self-attention as one layer, feed forward as the fused GELU MLP (unsigned "
-                           "INT4 hidden activation shifted by 0.171875)" if fused else ""))
-        manifest.write_text(json.dumps(metadata, indent=1), encoding="utf-8")
-        return {k: v for k, v in metadata.items() if k not in ("layout", "calibrated")}
+        what = (f"W4A4 of SVDQuant: INT4 codes in groups of {GROUP} input channels, a bfloat16 low-rank branch of rank "
+                f"{rank}, activation maxima folded in by SmoothQuant smoothing; parts in logical order")
+        if fused:
+            what += ("; self-attention's q, k, v stacked into one layer and the feed forward stored for the fused GELU "
+                     f"MLP, whose hidden activation is shifted by {GELU_SHIFT} and quantized unsigned")
+        metadata = pack.commit(dict(
+            format=FORMATS[1] if fused else FORMATS[0], packing=PACKING, blocks=len(blocks), layout=layout,
+            bytes_per_block=size, bytes=size * len(blocks), source=before, alpha=alpha, rank=rank,
+            calibrated=sorted(amax), bfloat16_layers=sorted(keep),
+            rounding="nearest" if hessians is None else "GPTQ", scale_rule=rule, quantization=what))
     except BaseException:
-        temporary.unlink(missing_ok=True)
-        path.unlink(missing_ok=True)
-        manifest.unlink(missing_ok=True)
+        pack.abandon()
         raise
+    return {k: v for k, v in metadata.items() if k not in ("layout", "calibrated")}
+
+
+def _pack_manifest(path, source):
+    """The manifest beside the pack at `path`, refused (ValueError) unless it names `source` as its checkpoint, one
+    of the block formats and this build's logical part order."""
+    import json
+
+    from wan_dit_lab_b200.quantization.weight_pack import source_identity
+    manifest = json.loads(path.with_name(path.name + ".json").read_text(encoding="utf-8"))
+    if manifest["format"] not in FORMATS or manifest["source"] != source_identity(source):
+        raise ValueError("Weight pack has a different checkpoint or format")
+    if manifest.get("packing") != PACKING:
+        raise ValueError("W4A4 weight pack holds its parts in Nunchaku's MMA-tile order (the reference's packer); "
+                         "this build reads packs in the logical order that build_pack writes")
+    return manifest
 
 
 def mapped_pack(blocks, path, source):
-    """(rows uint8 [blocks, bytes per block] over the file mapped read-only, layout) of a pack (reference
-    w4a4.py:397-414). blocks: the model's blocks (a sequence) or their number. ValueError when the manifest names
-    another checkpoint or format, when the parts are not in this build's logical order, or when the file is not
-    blocks x bytes_per_block long."""
-    import json
+    """(rows uint8 [blocks, bytes per block] over the file mapped read-only, layout) of a pack (the reference's
+    mapped_pack, w4a4.py:418-437). blocks: the model's blocks (a sequence) or their number. ValueError when the
+    manifest names another checkpoint or format, when the parts are not in this build's logical order, or when the
+    file is not blocks x bytes_per_block long. The rows read the page cache directly: nothing is copied until a
+    row is moved to a device."""
+    import mmap
     import warnings
 
-    import numpy as np
-
-    from wan_dit_lab_b200.quantization.weight_pack import source_identity
     path = Path(path)
-    metadata = json.loads(path.with_suffix(path.suffix + ".json").read_text(encoding="utf-8"))
-    if metadata["format"] not in FORMATS or metadata["source"] != source_identity(source):
-        raise ValueError("Weight pack has a different checkpoint or format")
-    if metadata.get("packing") != PACKING:
-        raise ValueError("W4A4 weight pack holds its parts in Nunchaku's MMA-tile order (the reference's packer); "
-                         "this build reads packs in the logical order that build_pack writes")
+    manifest = _pack_manifest(path, source)
     count = blocks if isinstance(blocks, int) else len(blocks)
-    size = metadata["bytes_per_block"]
-    if metadata["blocks"] != count or path.stat().st_size != size * count or count == 0:
+    size = manifest["bytes_per_block"]
+    if count == 0 or manifest["blocks"] != count or path.stat().st_size != size * count:
         raise ValueError("W4A4 weight pack is incomplete")
-    data = np.memmap(path, dtype=np.uint8, mode="r")
-    with warnings.catch_warnings():
-        warnings.simplefilter("ignore", UserWarning)  # a read-only mapping: torch warns that it is not writable
-        return torch.from_numpy(data).reshape(count, size), metadata["layout"]
+    with open(path, "rb") as f:
+        pages = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)  # stays mapped after the file is closed
+    with warnings.catch_warnings():  # the mapping is read-only, and torch warns that the tensor is not writable
+        warnings.simplefilter("ignore", UserWarning)
+        flat = torch.frombuffer(pages, dtype=torch.uint8)
+    return flat.view(count, size), manifest["layout"]
 
 
 def slot_parts(row, layout):
