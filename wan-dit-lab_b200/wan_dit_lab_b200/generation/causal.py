@@ -220,9 +220,10 @@ class WanModelB200:
         return e0[0].float().contiguous(), temb[0]
 
     def patch_embed(self, x):
-        """[C, f, H, W] latents -> [f (H/2) (W/2), dim] bf16 tokens (Conv3d kernel / stride (1, 2, 2))."""
+        """[C, f, H, W] latents -> [f (H/2) (W/2), dim] bf16 tokens (Conv3d kernel / stride (1, 2, 2)), row-major: the
+        block kernels read and update the stream as contiguous rows (the convolution's tokens come out transposed)."""
         y = torch.nn.functional.conv3d(x[None].to(torch.bfloat16), self.patch_w, self.patch_b, stride=(1, 2, 2))
-        return y.flatten(2).transpose(1, 2)[0]
+        return y.flatten(2).transpose(1, 2)[0].contiguous()
 
     def head(self, X, temb, grid):
         """Head.forward (models/head.py:13-18) and unpatchify (models/model.py:81-84): [out_dim, f, 2h, 2w]."""

@@ -209,6 +209,9 @@ class WanBlockB200:
         finished frame), both with the chunk, through the attention's head / token maps (causal.py:222-240).
         entropy_ratio: the cache's attention entropy ratio (self-attention's softmax scale, attention_scale), or None
         for 1 / sqrt(128)."""
+        if X.dtype != torch.float32 or X.dim() != 2 or not X.is_contiguous():
+            raise ValueError("X must be the float32 residual stream [n, dim], contiguous: the kernels read and update "
+                             "it as rows")
         lib, st = _native.lib(), _native.stream()
         n, dim, H = X.shape[0], self.dim, self.heads
         ck, cks, cv, cvs, capacity = cache

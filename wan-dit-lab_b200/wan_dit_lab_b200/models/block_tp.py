@@ -204,6 +204,9 @@ class WanBlockTP:
         Yields, in order: the q / k sums of squares [n, 2], the self-attention O partial [n, dim],
         the cross query's sums of squares [n], the cross O partial, the FFN-2 partial; each must hold the sum over
         shards when the generator resumes."""
+        if X.dtype != torch.float32 or X.dim() != 2 or not X.is_contiguous():
+            raise ValueError("X must be the float32 residual stream [n, dim], contiguous: the kernels read and update "
+                             "it as rows")
         lib, st = _native.lib(), _native.stream()
         n, dim, H, d = X.shape[0], self.dim, self.kv_heads, self.local_dim
         ck, cks, cv, cvs, capacity = cache
