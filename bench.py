@@ -228,8 +228,9 @@ def cpu_linear_sample(x, W, repeats=3):
         f"{torch.get_num_threads()} threads, mean of {repeats} calls")
 
 
-def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True):
-    """tp = (world, reduce): one stream split across the ranks (tensor parallelism), else one stream per rank."""
+def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True, height=512, width=928):
+    """tp = (world, reduce): one stream split across the ranks (tensor parallelism), else one stream per rank.
+    height x width pixels: 512 x 928 (464 tokens a frame) or 704 x 1280 (config 5, 880)."""
     from wan_dit_lab_b200.generation import causal
     from wan_dit_lab_b200.models.block import WanBlockB200
     from wan_dit_lab_b200.models.block_tp import WanBlockTP
@@ -242,9 +243,11 @@ def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True):
     block_cls = WanBlockB200 if tp is None else WanBlockTP
     seed_rank = rank if tp is None else 0  # the ranks of a split stream share its noise
     g = torch.Generator().manual_seed(8 + 1000 * seed_rank)  # one independent seeded stream per rank
-    noise = torch.randn(48, 21, 32, 58, generator=g)
+    lat_h, lat_w = height // 16, width // 16  # the VAE's stride 16
+    tokens = 3 * (lat_h // 2) * (lat_w // 2)  # a chunk of 3 latent frames, 2 x 2 patches
+    noise = torch.randn(48, 21, lat_h, lat_w, generator=g)
     text = torch.randn(1, 512, 4096, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
-    stream = causal.Stream(model, text.to(device), 512, 928,
+    stream = causal.Stream(model, text.to(device), height, width,
                            torch.Generator(device=device).manual_seed(10 + seed_rank), vae_stride=16,
                            cuda_graph=graphs and tp is None)  # passes replayed from CUDA graphs
     noise_d = noise.to(device)
@@ -279,21 +282,27 @@ def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True):
         torch.cuda.synchronize()
         return sum(a.elapsed_time(b) for a, b, _ in gemm_log) / 1e3, sum(o for _, _, o in gemm_log), len(gemm_log)
 
-    per_block = 2 * 1392 * 3072 * (9216 + 3072 + 3072 + 3072 + 2 * 14336) // world  # this rank's share
+    per_block = 2 * tokens * 3072 * (9216 + 3072 + 3072 + 3072 + 2 * 14336) // world  # this rank's share
+    window = 21 * tokens // 3  # keys of the 21-frame window
+    config5 = (height, width) == (704, 1280)
+    name = ("BASELINE config 5: 30-layer 5B DiT rollout, 704x1280 (880 tokens a frame, 2640-token chunks, up to 18480 "
+            "keys), 7 chunks x (4 DMD steps + write pass), FP8 KV window 21 frames" if config5 else
+            "BASELINE config 4: 30-layer 5B DiT rollout, 512x928, 7 chunks x (4 DMD steps + write pass), FP8 KV window "
+            "21 frames" if (height, width) == (512, 928) else
+            f"30-layer 5B DiT rollout, {height}x{width}, 7 chunks x (4 DMD steps + write pass), FP8 KV window 21 frames")
     # kernels per block: 20 (5 for Sage attention over the cache), 25 with the split (rows_sumsq x 2, the sharded
     # norms in place of the fused ones, residual_update x 3); + 1 modulation launch per pass
     return dict(step=step, e2e=e2e_step, gemm_probe=gemm_only, frames=3 * chunks,
                 launches_per_step=chunks * 5 * (1 + layers * (20 if tp is None else 25)),
                 h2d=noise.numel() * 4, d2h=noise.numel() * 4,
-                config={"workload": "BASELINE config 4: 30-layer 5B DiT rollout, 512x928, 7 chunks x (4 DMD steps + "
-                                    "write pass), FP8 KV window 21 frames",
+                config={"workload": name,
                         "model": "Wan2.2-TI2V-5B shape, random init N(0,0.02), W4A4 (INT4 g64, bf16 scales, rank 0)",
-                        "tokens_per_chunk": 1392, "keys_per_chunk": [1392 * (c + 1) for c in range(chunks)],
+                        "tokens_per_chunk": tokens, "keys_per_chunk": [min(tokens * (c + 1), window) for c in range(chunks)],
                         "chunks": chunks, "layers": layers, **({} if tp is None else {"tensor_parallel": world}),
                         "cuda_graphs": bool(graphs and tp is None),
                         "codes": CODES, "l2": "inputs larger than L2 (5 GB of weights per pass)"},
                 algorithmic={"gemm_int_ops_per_block_pass": per_block, "gemm_launches_per_block_pass": 6},
-                cpu=lambda: cpu_block_sample(), dtype="W4A4 (int4 x int4 exact on int8 tensor cores) + INT8/FP8 Sage "
+                cpu=lambda: cpu_block_sample(tokens=tokens, grid=(3, lat_h // 2, lat_w // 2)), dtype="W4A4 (int4 x int4 exact on int8 tensor cores) + INT8/FP8 Sage "
                                                       "attention; fp32 residual stream")
 
 
@@ -313,7 +322,7 @@ class ReferenceBlockPass:
     the linears in bf16, the norms and the modulation in float32 (a CPU layer_norm takes float32 parameters only).
     Calling it times one pass (seconds); each pass writes the chunk at the same place, so passes repeat exactly."""
 
-    def __init__(self, tokens=1392, cached=4176, text=512, seed=11):
+    def __init__(self, tokens=1392, cached=None, text=512, seed=11, grid=(3, 16, 29)):
         if not (REF_PACKAGE / "wan_dit_lab").is_dir():
             raise RuntimeError(f"the reference package is not installed in {REF_PACKAGE}: run "
                                "baseline/install_reference.sh")
@@ -323,7 +332,10 @@ class ReferenceBlockPass:
         from wan_dit_lab.models.block import WanBlock
         from wan_dit_lab.models.rope import rope
         torch.set_num_threads(os.cpu_count())
-        dim, ffn, heads, per_frame = 3072, 14336, 24, 464
+        dim, ffn, heads = 3072, 14336, 24
+        per_frame = grid[1] * grid[2]
+        if cached is None:  # the mean cache fill before the 7 chunks: 0, 1, ... 6 chunks of keys
+            cached = 3 * tokens
         g = torch.Generator().manual_seed(seed)
         blk = WanBlock(dim, ffn, heads, 1e-6)
         with torch.no_grad():
@@ -341,7 +353,7 @@ class ReferenceBlockPass:
         d = 128  # the Live preset's float32 table: time / height / width pairs 22 / 21 / 21
         self.freqs = torch.cat([rope(1024, d - 4 * (d // 6)), rope(1024, 2 * (d // 6)), rope(1024, 2 * (d // 6))],
                                dim=-1).float()
-        self.grid = ((3, 16, 29),)
+        self.grid = (tuple(grid),)
         self.cache = KVCache(18 * per_frame, fp8=True, chunk=3)  # a window of 21 frames less the chunk
         self.X = torch.randn(1, tokens, dim, generator=g)  # the float32 stream of blocks after the first
         self.e0 = torch.randn(1, 6, dim, generator=g) * 0.1
@@ -366,10 +378,10 @@ class ReferenceBlockPass:
             return time.perf_counter() - t0
 
 
-def cpu_block_sample(passes=3):
+def cpu_block_sample(passes=3, tokens=1392, grid=(3, 16, 29)):
     """The CPU baseline of the rollout: the median of `passes` timed reference block passes (after one untimed),
     extrapolated by block passes only. Returns (seconds per rollout, frames, sample description)."""
-    ref = ReferenceBlockPass()
+    ref = ReferenceBlockPass(tokens=tokens, grid=grid)
     ref()
     per_pass = statistics.median(ref() for _ in range(passes))
     return per_pass * BLOCK_PASSES_PER_ROLLOUT, 21, ref.sample + f"; median of {passes} passes"
@@ -448,6 +460,8 @@ def main():
     parser.add_argument("--chunks", type=int, default=7, help="rollout chunks (profiling; BASELINE config 4: 7)")
     parser.add_argument("--layers", type=int, default=30, help="model layers (profiling; BASELINE config 4: 30)")
     parser.add_argument("--eager", action="store_true", help="launch every kernel from Python (no CUDA graphs)")
+    parser.add_argument("--height", type=int, default=512, help="pixels (BASELINE config 4: 512; config 5: 704)")
+    parser.add_argument("--width", type=int, default=928, help="pixels (BASELINE config 4: 928; config 5: 1280)")
     parser.add_argument("--tp", action="store_true",
                         help="BASELINE config 5b: one stream split across the ranks (heads / hidden channels, NCCL "
                              "all-reduce after O, cross-O and FFN-2) instead of one independent stream per rank")
@@ -477,8 +491,8 @@ def main():
     if args.tp and not rollout:
         parser.error("--tp splits the rollout")
     tp = (world, (lambda t: dist.all_reduce(t)) if dist is not None else (lambda t: None)) if args.tp else None
-    wl = (WORKLOADS[args.workload](device, rank, args.chunks, args.layers, tp, not args.eager) if rollout
-          else WORKLOADS[args.workload](device))
+    wl = (WORKLOADS[args.workload](device, rank, args.chunks, args.layers, tp, not args.eager, args.height, args.width)
+          if rollout else WORKLOADS[args.workload](device))
     stream = torch.cuda.current_stream(device)
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)
     flush = lambda: flush_l2(flush_buf)  # noqa: E731

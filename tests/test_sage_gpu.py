@@ -59,7 +59,8 @@ def test_quantized_operands_match_oracle(at, n, nq, H):
     assert not ops["k_i8"][:, L:].any() and not ops["v_f8"][:, :, L:].any()  # zero padding
 
 
-@pytest.mark.parametrize("at,n,nq,H", [(200, 150, 150, 2), (0, 300, 300, 1), (4176, 1392, 1392, 24), (9360, 3120, 3120, 2)])
+@pytest.mark.parametrize("at,n,nq,H", [(200, 150, 150, 2), (0, 300, 300, 1), (4176, 1392, 1392, 24), (9360, 3120, 3120, 2),
+                                        (15840, 2640, 2640, 1)])  # config 5: 18480 keys, 145 key tiles
 def test_attention_matches_oracle(at, n, nq, H):
     from wan_dit_lab_b200.kernels import sage_kv
     from wan_dit_lab_b200 import _native
