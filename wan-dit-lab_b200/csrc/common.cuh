@@ -303,6 +303,86 @@ __device__ __forceinline__ uint32_t elect_one() {
   return pred;
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// CTA pairs (a cluster of two CTAs on the two SMs of a TPC): 2-SM MMAs, whose operands and accumulator are split
+// between the pair. Every tcgen05 instruction of a kernel that uses them takes .cta_group::2. No multicast form is
+// used: a signal the peer needs is relayed by a remote mbarrier arrive.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of the variable at this CTA's shared address `local` in the CTA of rank `rank`.
+__device__ __forceinline__ uint32_t peer_smem(uint32_t local, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(local), "r"(rank));
+  return out;
+}
+
+// Arrives once on an mbarrier of a CTA of the cluster (address from peer_smem), releasing this thread's prior
+// writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// The same arrive without release semantics: a signal that hands over no write of this thread (the completion of
+// tensor-core reads this thread has observed on its own barrier), so no cluster-wide fence on the way.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Both CTAs of the cluster reach this point before either goes on (all threads of both).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// A tile into this CTA's shared memory whose completed bytes count on the mbarrier at `bar_cluster` (the pair's
+// first CTA's barrier, from peer_smem(..., 0)): each CTA of a pair loads its own half of the operands and the MMA
+// issuer in the first CTA waits for both halves on one barrier.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                 int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_holder, uint32_t columns) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_holder)),
+               "r"(columns)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t columns) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(columns) : "memory");
+}
+
+// Arrives once on this CTA's `bar` when every 2-SM tcgen05.mma this thread issued before has completed (their
+// writes to both CTAs' TMEM and their reads of both CTAs' shared memory).
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// D[tmem] (+)= A * B^T over a CTA pair, 16-bit float operands, f32 accumulator: M = 256 rows of A (128 in each
+// CTA's shared memory at the same offset), N rows of B (N / 2 in each CTA), D rows 0-127 in the first CTA's TMEM
+// and 128-255 in the second's. Issued by one thread of the pair's first CTA.
+__device__ __forceinline__ void mma_f16_pair(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+      ::"r"(tmem_d), "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
 template <uint32_t kRegs>
 __device__ __forceinline__ void setmaxnreg_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));

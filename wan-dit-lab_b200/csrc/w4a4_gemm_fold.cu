@@ -470,6 +470,195 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---- the prescaled format on CTA pairs (2-SM MMAs) ---------------------------------------------------------------
+// gemm_pre_kernel is bound by how fast the TMA fills each SM's shared memory: a 128 x 256 x 64 step brings 48 KB
+// (16 KB of activations, 32 KB of weights), about 650 SM cycles at the 71-81 B per cycle measured, against 512
+// cycles of f16 MMA. Here a cluster of two CTAs (the two SMs of a TPC) computes 256 x 256 tiles with 2-SM MMAs
+// (M = 256): each CTA holds its own 128 activation rows and one half (128 rows) of the weight tile, 32 KB a step,
+// and the tensor cores of both SMs read both weight halves. Six stages of 32 KB per SM are in flight. Each CTA's
+// TMEM holds its 128 rows of the accumulator, which its epilogue warps drain and finish as in gemm_pre_kernel
+// (the same finish_tile). Roles:
+//   both CTAs, warp 0      TMA producer of its own halves; every completion counts on the first CTA's full[s]
+//   first CTA, warp 1      MMA issuer (one thread): 2-SM tcgen05.mma into accumulator (tile % 2), commits to its
+//                          empty[s] / acc_full[b]; its producer relays empty[s] to the second CTA (remote arrive)
+//   first CTA, warp 2      relays acc_full[b] to the second CTA
+//   both CTAs, warps 4-11  epilogue; every warp of both CTAs arrives on the first CTA's acc_empty[b] (16 arrivals)
+// Tiles: 256 rows x 256 columns, pair p takes tiles p, p + pairs, ... (row pairs fastest). No multicast is used.
+constexpr int PSTAGES = 6;
+constexpr int PA_BYTES = BM * BK * 2, PB_BYTES = (BN / 2) * BK * 2;  // per CTA and step: 16 KB + 16 KB
+
+struct __align__(1024) SmemPair {
+  uint8_t a[PSTAGES][PA_BYTES];
+  uint8_t b[PSTAGES][PB_BYTES];
+  float scratch[8][32 * 33];
+  uint64_t full[PSTAGES];   // first CTA: both CTAs' halves of the step in stage s have landed
+  uint64_t empty[PSTAGES];  // each CTA: its stage s may be refilled
+  uint64_t acc_full[2];     // each CTA: accumulator b holds a finished tile
+  uint64_t acc_empty[2];    // first CTA: accumulator b drained by the epilogues of both CTAs
+  uint64_t mma_done;
+  uint32_t tmem_base;
+};
+
+constexpr size_t kSmemPairBytes = sizeof(SmemPair) + 1024;
+static_assert(kSmemPairBytes <= 232448, "shared memory of a CTA pair's stage ring");
+
+template <int kMode>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pre_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                         const float* __restrict__ fold_scale, GemmEpilogue ep, int M, int N, int K, uint32_t* err) {
+  extern __shared__ uint8_t smem_raw[];
+  SmemPair& sm = *reinterpret_cast<SmemPair*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int G = K / BK;
+  const int m_pairs = (M + 2 * BM - 1) / (2 * BM), n_tiles = (N + BN - 1) / BN;
+  const int tiles = m_pairs * n_tiles;
+  const int pair = static_cast<int>(blockIdx.x >> 1), pairs = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.acc_full[b], 1);
+      mbar_init(&sm.acc_empty[b], 16);
+    }
+    mbar_init(&sm.mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensor_map(&map_a);
+    prefetch_tensor_map(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&sm.tmem_base, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialized before any remote arrive or copy completion reaches them
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp < 4) {
+    setmaxnreg_dec<56>();
+    if (warp == 0 && lane == 0) {
+      // ---------------- TMA producer (both CTAs): this CTA's halves of every step, counted on the first CTA's full[s]
+      const uint32_t full0 = peer_smem(smem_u32(&sm.full[0]), 0);
+      const uint32_t peer_empty0 = peer_smem(smem_u32(&sm.empty[0]), 1);
+      int kb = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += pairs) {
+        const int m_pair = t % m_pairs, n_tile = t / m_pairs;
+        const int row0 = (m_pair * 2 + static_cast<int>(rank)) * BM;
+        const int col0 = n_tile * BN + static_cast<int>(rank) * (BN / 2);
+        for (int g = 0; g < G; ++g, ++kb) {
+          const int s = kb % PSTAGES;
+          if (!mbar_wait(&sm.empty[s], ((kb / PSTAGES) & 1) ^ 1, err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&sm.full[s], 2 * (PA_BYTES + PB_BYTES));
+          tma_load_2d_pair(sm.a[s], &map_a, full0 + 8 * s, g * BK, row0);
+          tma_load_2d_pair(sm.b[s], &map_b, full0 + 8 * s, g * BK, col0);
+          // the MMAs that read stage s (both CTAs' halves) have completed (their commit is what empty[s] waited
+          // for): the second CTA may refill its half too. A relaxed arrive: nothing this thread wrote is handed over.
+          if (rank == 0 && kb >= PSTAGES) mbar_arrive_cluster_relaxed(peer_empty0 + 8 * s);
+        }
+      }
+      if (rank == 0)  // no copy of either CTA in flight at exit: both count on these barriers
+        for (int j = (kb > PSTAGES ? kb - PSTAGES : 0); j < kb; ++j)
+          mbar_wait(&sm.full[j % PSTAGES], (j / PSTAGES) & 1, err, kErrWaitFull);
+    } else if (warp == 1 && rank == 0) {
+      // ---------------- MMA issuer (first CTA): tile i into accumulator i % 2, all of K, 2-SM MMAs M = N = 256
+      const uint32_t idesc = make_idesc(1, 0, 0, 2 * BM, BN);  // f16 x f16 -> f32
+      bool ok = true;
+      int kb = 0, i = 0;
+      for (int t = pair; t < tiles && ok; t += pairs, ++i) {
+        const int b = i & 1;
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_empty[b], ((i >> 1) & 1) ^ 1, err, kErrWaitAccEmpty));
+        if (!ok) break;
+        tc_fence_after();
+        for (int g = 0; g < G; ++g, ++kb) {
+          const int s = kb % PSTAGES;
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.full[s], (kb / PSTAGES) & 1, err, kErrWaitFull));
+          if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t a0 = smem_u32(sm.a[s]), b0 = smem_u32(sm.b[s]);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              mma_f16_pair(tmem + b * BN, smem_desc_k128(a0 + kk * 32), smem_desc_k128(b0 + kk * 32), idesc,
+                           g > 0 || kk > 0);
+            tc_commit_pair(&sm.empty[s]);
+          }
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (elect_one()) tc_commit_pair(&sm.acc_full[b]);
+        __syncwarp();
+      }
+      if (elect_one()) tc_commit_pair(&sm.mma_done);
+      __syncwarp();
+      mbar_wait(&sm.mma_done, 0, err, kErrWaitAccFull);
+    } else if (warp == 2 && rank == 0 && lane == 0) {
+      // ---------------- relay (first CTA): accumulator b of tile i is complete in the second CTA's TMEM as well
+      const uint32_t peer_acc_full0 = peer_smem(smem_u32(&sm.acc_full[0]), 1);
+      int i = 0;
+      for (int t = pair; t < tiles; t += pairs, ++i) {
+        const int b = i & 1;
+        if (!mbar_wait(&sm.acc_full[b], (i >> 1) & 1, err, kErrWaitAccFull)) break;
+        mbar_arrive_cluster(peer_acc_full0 + 8 * b);
+      }
+    }
+  } else {
+    setmaxnreg_inc<224>();
+    // ---------------- epilogue (both CTAs): drain this CTA's 128 rows of tile i, hand the buffer back, finish
+    const int q = warp & 3, h = (warp - 4) >> 2;
+    const float unfold = __ldg(fold_scale);  // 2^F
+    float* tw = sm.scratch[warp - 4];
+    const uint32_t acc_empty0 = peer_smem(smem_u32(&sm.acc_empty[0]), 0);
+    int i = 0;
+    for (int t = pair; t < tiles; t += pairs, ++i) {
+      const int m_pair = t % m_pairs, n_tile = t / m_pairs;
+      const int m_tile = m_pair * 2 + static_cast<int>(rank);  // this CTA's 128-row tile
+      const int b = i & 1;
+      const int m = m_tile * BM + q * 32 + lane;
+      const float mul = __fmul_rn(m < M ? __ldg(ep.ascale + m) : 0.f, unfold);  // 2^E_m 2^F: exact
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&sm.acc_full[b], (i >> 1) & 1, err, kErrWaitAccFull))) break;
+      tc_fence_after();
+      const uint32_t t_buf = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * BN + h * 128;
+      float acc[128];
+      uint32_t ra[32], rb[32];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        tmem_ld32(t_buf + r * 64, ra);
+        tmem_ld32(t_buf + r * 64 + 32, rb);
+        tmem_ld_wait(ra);
+        tmem_ld_wait(rb);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[r * 64 + j] = __fmul_rn(__uint_as_float(ra[j]), mul);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[r * 64 + 32 + j] = __fmul_rn(__uint_as_float(rb[j]), mul);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * b);  // every column in registers: the MMA may reuse it
+      finish_tile<kMode>(acc, ep, tw, M, N, m_tile, n_tile, q, h, lane, true);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other's MMAs, copies or remote arrives may still reach it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
 // Folded weights: w16[n, k] = float16(wq[n, k] * sw[k / 64, n] * 2^-F). One thread per 8 codes (4 packed bytes);
 // an element whose value is not exactly a normal float16 number (or zero) is counted in *inexact.
 __global__ void fold_weight_kernel(const uint8_t* __restrict__ qweight, const uint16_t* __restrict__ wscales,
@@ -556,6 +745,54 @@ int gemm_fold_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
   }
   const dim3 grid((a.M + fold::BM - 1) / fold::BM, (a.N + fold::BN - 1) / fold::BN);
   cudaError_t e = cudaSuccess;
+  static const bool pairs_on = [] {
+    const char* v = getenv("WDL_GEMM_PAIRS");
+    return !v || atoi(v) != 0;
+  }();
+  if (a.code_format == kCodesF16Pre && pairs_on && a.M > fold::BM) {
+    // persistent CTA pairs: one pair per TPC (or per tile, when there are fewer), 2-SM MMAs on 256 x 256 tiles
+    CUtensorMap mb_half;
+    if (!fold::make_map_2d(&mb_half, a.b, a.K, a.N, a.ldb * 2, fold::BK, fold::BN / 2)) {
+      *why = "cuTensorMapEncodeTiled rejected the weights";
+      return 2;
+    }
+    const int tiles = ((a.M + 2 * fold::BM - 1) / (2 * fold::BM)) * ((a.N + fold::BN - 1) / fold::BN);
+    auto launch_pair = [&](auto kernel) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(fold::kSmemPairBytes));
+      if (e != cudaSuccess) return;
+      static int resident = 0;  // pairs that fit on the GPU at once
+      if (resident == 0) {
+        cudaLaunchConfig_t probe = {};
+        probe.gridDim = dim3(2 * 74);
+        probe.blockDim = dim3(fold::kThreads);
+        probe.dynamicSmemBytes = fold::kSmemPairBytes;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &probe) != cudaSuccess || clusters <= 0) {
+          cudaGetLastError();  // the query is advisory: fall back to one pair per two SMs
+          int dev = 0, sms = 148;
+          if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+          clusters = sms / 2;
+        }
+        resident = clusters;
+      }
+      const unsigned pairs = static_cast<unsigned>(tiles < resident ? tiles : resident);
+      kernel<<<dim3(2 * pairs), fold::kThreads, fold::kSmemPairBytes, stream>>>(ma, mb_half, a.wscale, a.ep, a.M, a.N,
+                                                                               a.K, a.err);
+    };
+    switch (a.ep.mode) {
+      case kEpiBf16: launch_pair(fold::gemm_pre_pair_kernel<kEpiBf16>); break;
+      case kEpiResidualF32: launch_pair(fold::gemm_pre_pair_kernel<kEpiResidualF32>); break;
+      case kEpiGeluU4: launch_pair(fold::gemm_pre_pair_kernel<kEpiGeluU4>); break;
+      default: *why = "unknown epilogue mode"; return 1;
+    }
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      *why = cudaGetErrorString(e);
+      return 3;
+    }
+    return 0;
+  }
   if (a.code_format == kCodesF16Pre) {  // persistent: one CTA per SM (or per tile, when there are fewer)
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
