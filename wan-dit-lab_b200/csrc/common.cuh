@@ -247,6 +247,25 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, for the share of a softmax's exponentials taken off the special function unit (which a
+// softmax over 8-bit tensor-core scores keeps the busiest unit of the SM). x is rounded to the nearest integer n by
+// adding 1.5 * 2^23 (exact for |x| < 2^22: the float's last mantissa bits then hold n), f = x - n lies in
+// [-0.5, 0.5], 2^f comes from a degree-4 polynomial and 2^n is added to its exponent field as the integer n << 23
+// (the shift keeps n's low bits, two's complement). The polynomial was fitted to 2^f on [-0.5, 0.5] for relative
+// error (Lawson's iteratively reweighted least squares on 4000 Chebyshev nodes, a near-minimax fit): 2.7e-6 at
+// most in float32 Horner form (tests/test_exp2_gpu.py checks it against exp2f). x is clamped below at -100 (the
+// result is then 2^-100, nothing anyone reads); arguments above 100 are not supported.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -100.f);
+  const float r = __fadd_rn(x, 12582912.f);
+  const float f = __fsub_rn(x, __fsub_rn(r, 12582912.f));
+  float p = fmaf(f, 0.009570101276040077f, 0.05591785907745361f);
+  p = fmaf(p, f, 0.240247443318367f);
+  p = fmaf(p, f, 0.6931217908859253f);
+  p = fmaf(p, f, 0.9999992847442627f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(r) << 23));
+}
+
 // GELU in its tanh form (torch.nn.GELU(approximate="tanh"), the feed forward of models/block.py:8-9):
 // 0.5 x (1 + tanh(y)), y = sqrt(2 / pi) (x + 0.044715 x^3). From tanh(y) = 1 - 2 / (e^(2y) + 1) it equals
 // x - x / (e^(2y) + 1); e^(2y) = 2^(2 y log2(e)) on the special function unit, the quotient by the fast division

@@ -138,61 +138,76 @@ struct Source {
   __device__ __forceinline__ int where(int j0, int j1) const { return j1 <= at ? 1 : (j0 >= at ? 2 : 0); }
 };
 
-// ---- pass 1: per (64-token tile, head), per channel: sum of K and max |V| over the tile. Warp w reads the 16
-// tokens 16 w .. 16 w + 15 of the tile, lane l channels 4 l .. 4 l + 3 (one 128-byte row segment per token);
-// the four warps' partials meet in shared memory.
+// ---- pass 1: per (64-token tile, head), per channel: sum of K (blockIdx.z 0) or max |V| (blockIdx.z 1) over the
+// tile. Warp w reads the 16 tokens 16 w .. 16 w + 15 of the tile, lane l channels 4 l .. 4 l + 3 (one 128-byte row
+// segment per token), all 16 of its loads in flight; the four warps' partials meet in shared memory. K and V in
+// separate CTAs: each has one round of loads to wait for, and twice as many CTAs hide each other's latency.
 __global__ void __launch_bounds__(128) partials_kernel(Source ks, Source vs, float* ksum, float* vmax) {
-  __shared__ float red[2][4][128];
+  __shared__ float red[4][128];
   const int tile = blockIdx.x, h = blockIdx.y;
+  const bool is_v = blockIdx.z != 0;
+  const Source& src = is_v ? vs : ks;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float s[4] = {0.f, 0.f, 0.f, 0.f}, m[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
   const int j0 = tile * 64 + warp * 16;
-  const int where = ks.where(j0, min(ks.L, j0 + 16));
-  int j[8];
-  bool valid[8];
+  int j[16];
+  bool valid[16];
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {  // 8 keys at a time: 16 loads (K and V) in flight per lane
+  for (int i = 0; i < 16; ++i) j[i] = j0 + i, valid[i] = j[i] < src.L;
+  float x[16][4];
+  src.gather4(j, valid, src.where(j0, min(src.L, j0 + 16)), h, lane * 4, x);
+  if (is_v) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) j[i] = j0 + half * 8 + i, valid[i] = j[i] < ks.L;
-    float k[8][4], v[8][4];
-    ks.gather4(j, valid, where, h, lane * 4, k);
-    vs.gather4(j, valid, where, h, lane * 4, v);
+    for (int i = 0; i < 16; ++i)
 #pragma unroll
-    for (int i = 0; i < 8; ++i)  // keys in order: the same float sums as one key at a time
+      for (int c = 0; c < 4; ++c) acc[c] = fmaxf(acc[c], fabsf(x[i][c]));
+  } else {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) s[c] += k[i][c], m[c] = fmaxf(m[c], fabsf(v[i][c]));
+    for (int i = 0; i < 16; ++i)  // keys in order
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[c] += x[i][c];
   }
 #pragma unroll
-  for (int c = 0; c < 4; ++c) red[0][warp][lane * 4 + c] = s[c], red[1][warp][lane * 4 + c] = m[c];
+  for (int c = 0; c < 4; ++c) red[warp][lane * 4 + c] = acc[c];
   __syncthreads();
   const int d = threadIdx.x;
   const int64_t o = (static_cast<int64_t>(tile) * ks.H + h) * 128 + d;
-  ksum[o] = (red[0][0][d] + red[0][1][d]) + (red[0][2][d] + red[0][3][d]);
-  vmax[o] = fmaxf(fmaxf(red[1][0][d], red[1][1][d]), fmaxf(red[1][2][d], red[1][3][d]));
+  if (is_v) vmax[o] = fmaxf(fmaxf(red[0][d], red[1][d]), fmaxf(red[2][d], red[3][d]));
+  else ksum[o] = (red[0][d] + red[1][d]) + (red[2][d] + red[3][d]);
 }
 
-// ---- pass 2: per head: key mean (sum / L) and the V channel scales max(max|V|, 1e-8) / 2.25 (V_MAX, :24)
+// ---- pass 2: per head: key mean (sum / L) and the V channel scales max(max|V|, 1e-8) / 2.25 (V_MAX, :24). CTA
+// (h, c) holds channels 32 c .. 32 c + 31; its warp w sums tiles w, w + 4, ... (16 loads in flight), and the four
+// warps' sums are added in a fixed order: a short dependent chain instead of one thread walking every tile.
 __global__ void __launch_bounds__(128) reduce_kernel(const float* ksum, const float* vmax, int tiles, int H, int L,
                                                      float* kmean, float* v_scale) {
-  const int h = blockIdx.x, d = threadIdx.x;
+  __shared__ float red[2][4][32];
+  const int h = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d = blockIdx.y * 32 + lane;
   float s = 0.f, m = 0.f;
-  int t = 0;
-  for (; t + 8 <= tiles; t += 8) {  // 16 loads in flight, then summed in tile order
+  int t = warp;
+  for (; t + 28 < tiles; t += 32) {
     float a[8], b[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      a[i] = ksum[(static_cast<int64_t>(t + i) * H + h) * 128 + d];
-      b[i] = vmax[(static_cast<int64_t>(t + i) * H + h) * 128 + d];
+      a[i] = ksum[(static_cast<int64_t>(t + 4 * i) * H + h) * 128 + d];
+      b[i] = vmax[(static_cast<int64_t>(t + 4 * i) * H + h) * 128 + d];
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) s += a[i], m = fmaxf(m, b[i]);
   }
-  for (; t < tiles; ++t) {
+  for (; t < tiles; t += 4) {
     s += ksum[(static_cast<int64_t>(t) * H + h) * 128 + d];
     m = fmaxf(m, vmax[(static_cast<int64_t>(t) * H + h) * 128 + d]);
   }
-  kmean[h * 128 + d] = __fdiv_rn(s, static_cast<float>(L));
-  v_scale[h * 128 + d] = __fdiv_rn(fmaxf(m, 1e-8f), 2.25f);
+  red[0][warp][lane] = s, red[1][warp][lane] = m;
+  __syncthreads();
+  if (warp == 0) {
+    const float sum = (red[0][0][lane] + red[0][1][lane]) + (red[0][2][lane] + red[0][3][lane]);
+    const float top = fmaxf(fmaxf(red[1][0][lane], red[1][1][lane]), fmaxf(red[1][2][lane], red[1][3][lane]));
+    kmean[h * 128 + d] = __fdiv_rn(sum, static_cast<float>(L));
+    v_scale[h * 128 + d] = __fdiv_rn(fmaxf(top, 1e-8f), 2.25f);
+  }
 }
 
 // Sage's INT8 rounding: trunc(y + 0.5 sign(y)) with y = x / scale (the division correctly rounded).
@@ -215,7 +230,7 @@ __global__ void __launch_bounds__(128) quant_kv_kernel(Source ks, Source vs, con
   const int blk = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L = ks.L;
-  {
+  if (blockIdx.z == 0) {  // K and V in separate CTAs (one round of loads each)
     const int g = warp;
     const float4 mean = *reinterpret_cast<const float4*>(kmean + h * 128 + lane * 4);
     float x[16][4];
@@ -253,8 +268,7 @@ __global__ void __launch_bounds__(128) quant_kv_kernel(Source ks, Source vs, con
         *reinterpret_cast<uint32_t*>(k_i8 + (static_cast<int64_t>(h) * Lpad + j) * 128 + lane * 4) = packed;
       }
     if (lane == 0) k_scale[static_cast<int64_t>(h) * (Lpad / 64) * 4 + blk * 4 + g] = scale;
-  }
-  {
+  } else {
     const int g = warp;
     const float4 sv = *reinterpret_cast<const float4*>(v_scale + h * 128 + lane * 4);
     const float s[4] = {sv.x, sv.y, sv.z, sv.w};
@@ -341,9 +355,9 @@ void prep_kv_launch(const PrepArgs& a, cudaStream_t s) {
   float* ksum = a.work;
   float* vmax = ksum + static_cast<int64_t>(tiles) * a.H * 128;
   float* kmean = vmax + static_cast<int64_t>(tiles) * a.H * 128;
-  partials_kernel<<<dim3(tiles, a.H), 128, 0, s>>>(ks, vs, ksum, vmax);
-  reduce_kernel<<<a.H, 128, 0, s>>>(ksum, vmax, tiles, a.H, L, kmean, a.v_scale);
-  quant_kv_kernel<<<dim3(Lpad / 64, a.H), 128, 0, s>>>(ks, vs, kmean, a.v_scale, Lpad, a.k_i8, a.k_scale, a.v_f8);
+  partials_kernel<<<dim3(tiles, a.H, 2), 128, 0, s>>>(ks, vs, ksum, vmax);
+  reduce_kernel<<<dim3(a.H, 4), 128, 0, s>>>(ksum, vmax, tiles, a.H, L, kmean, a.v_scale);
+  quant_kv_kernel<<<dim3(Lpad / 64, a.H, 2), 128, 0, s>>>(ks, vs, kmean, a.v_scale, Lpad, a.k_i8, a.k_scale, a.v_f8);
 }
 
 void quant_q_launch(const float* q, int64_t ld_q, int nq, int H, int8_t* q_i8, float* q_scale, cudaStream_t s) {

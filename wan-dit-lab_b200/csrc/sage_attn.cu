@@ -11,9 +11,13 @@
 // and finally O * v_scale / (448 l) in bf16. The P scale 448 and the per-channel V scale are SageAttention 2's
 // FP8 P V scheme (sage_kv.py:24 V_MAX = 2.25 keeps |V / v_scale| <= 2.25).
 //
-// Warps: 0 TMA producer (Q once, K and V tiles, 2 stages), 1 TMEM owner + MMA issuer, 2-5 softmax (warp w owns
-// TMEM lanes 32 (w % 4) .. +31). TMEM: S in columns 0-127 (int32), O in 128-255 (fp32); 256 columns, two CTAs
-// per SM. The next tile's Q K^T is issued before this tile's P V so it overlaps the softmax.
+// Warps: 0 TMA producer (Q once, K and V tiles, 2 stages), 1 TMEM owner + MMA issuer, 2-9 softmax: warp w owns
+// TMEM lanes 32 (w % 4) .. +31 (its 32 query rows) and one half of the columns, (w - 2) / 4, so that two threads
+// share a row: each holds 64 scores of a tile, the pair exchanges its row maximum through shared memory (an
+// mbarrier per lane quarter, two arrivals a tile, bounded waits) and keeps its own share of the row sum until the end. Four
+// softmax warps per SM sub-partition hide the latency of the exponentials and the FP8 packing. TMEM: S in columns
+// 0-127 (int32), O in 128-255 (fp32); 256 columns, two CTAs per SM. The next tile's Q K^T is issued before this
+// tile's P V so it overlaps the softmax.
 #include "common.cuh"
 #include "sage.h"
 
@@ -25,7 +29,8 @@ namespace wdl {
 namespace sage {
 
 constexpr int BQ = 128, BKV = 128, HD = 128;
-constexpr int kAttnThreads = 192;
+constexpr int kAttnThreads = 320;
+constexpr int kSoftmaxWarps = 8;
 constexpr uint32_t kAttnTmemCols = 256;
 constexpr float kPScale = 448.f;
 constexpr float kLog2PScale = 8.807354922057604f;  // log2(448)
@@ -36,6 +41,9 @@ struct __align__(1024) AttnSmem {
   uint8_t v[2][HD * BKV];
   uint8_t p[BQ * BKV];
   uint64_t q_full, kv_full[2], kv_empty[2], s_full, s_empty, p_full, o_done;
+  uint64_t pair[4];  // per lane quarter: both column halves have published their values (one phase a tile)
+  float row_max[2][2][BQ];  // [tile parity][column half][row]: the halves' maxima of a tile's scores
+  float row_sum[2][BQ];     // [column half][row]: the halves' shares of the row sum, at the end
   uint32_t tmem_base;
 };
 constexpr size_t kAttnSmemBytes = sizeof(AttnSmem) + 1024;
@@ -48,6 +56,23 @@ __device__ __forceinline__ float exact_float(uint32_t s) {
   return __fsub_rn(__uint_as_float(s + 0x4B400000u), 12582912.0f);
 }
 
+// The two warps of one lane quarter (the same 32 query rows, the two column halves) exchange values through
+// shared memory: each publishes its own (written before the call), arrives once on the quarter's barrier and waits
+// for the phase `phase`, after which the other half's values are visible. A bounded wait (it reports code 3 and
+// returns false if the other warp never arrives), so that no error path can leave a warp blocked.
+__device__ __forceinline__ bool pair_exchange(uint64_t* bar, uint32_t phase, int lane, uint32_t* err) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+  return __all_sync(0xFFFFFFFFu, mbar_wait(bar, phase & 1, err, kErrWaitAccFull));
+}
+
+// kPoly: of every four exponentials of the softmax, how many are evaluated on the FMA pipe (exp2_fma) instead of
+// the special function unit (ex2). Measured at 1392 queries x 5568 keys x 24 heads: 127 us with none, 133 us with
+// one, 145 us with two. The softmax warps are limited by instruction issue and latency rather than by the special
+// function unit (its pipe is 42 % busy), and the polynomial's nine instructions cost more issue slots than the one
+// ex2 they replace; so the share is 0.
+constexpr int kAttnPolyShare = 0;
+template <int kPoly>
 __global__ void __launch_bounds__(kAttnThreads, 2)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_v, AttnArgs a, uint32_t* err) {
@@ -65,9 +90,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       mbar_init(&sm.kv_empty[i], 1);
     }
     mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.s_empty, 4);
-    mbar_init(&sm.p_full, 4);
+    mbar_init(&sm.s_empty, kSoftmaxWarps);
+    mbar_init(&sm.p_full, kSoftmaxWarps);
     mbar_init(&sm.o_done, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&sm.pair[q], 2);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -147,70 +173,77 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       __syncwarp();
     }
   } else {
-    // ---------------- softmax: thread = query row ----------------
-    const int quarter = warp & 3;
+    // ---------------- softmax: two threads per query row, 64 scores each ----------------
+    const int quarter = warp & 3;      // TMEM lane quarter: the rows this warp may read
+    const int half = (warp - 2) >> 2;  // column half of S, P and O
     const int row = quarter * 32 + lane;
     const int t = qt * BQ + row;  // query token
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const float qs = a.q_scale[static_cast<int64_t>(h) * (npad / 32) * 8 + (t / 32) * 8 + (t % 8)];
     const float c = qs * a.sm_scale_log2;
-    const float* ks_head = a.k_scale + static_cast<int64_t>(h) * (Lpad / 64) * 4;
-    float m = -INFINITY, l = 0.f;
+    // this half's key-scale groups of a tile: columns 64 half .. + 63 hold groups 4 half .. + 3
+    const float* ks_head = a.k_scale + static_cast<int64_t>(h) * (Lpad / 64) * 4 + half * 4;
+    float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum (of 448 p)
     bool ok = true;
     uint8_t* prow = sm.p + (row >> 3) * 1024 + (row & 7) * 128;
-    float ks_next[8];  // the next tile's key scales, loaded a tile ahead (off the critical path)
+    float ks_next[4];  // the next tile's key scales, loaded a tile ahead (off the critical path)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ks_next[i] = __ldg(ks_head + i);
+    for (int i = 0; i < 4; ++i) ks_next[i] = __ldg(ks_head + i);
     for (int j = 0; j < T; ++j) {
-      float w[8];
+      float w[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[i] = c * ks_next[i];
+      for (int i = 0; i < 4; ++i) w[i] = c * ks_next[i];
       if (j + 1 < T) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ks_next[i] = __ldg(ks_head + (j + 1) * 8 + i);
+        for (int i = 0; i < 4; ++i) ks_next[i] = __ldg(ks_head + (j + 1) * 8 + i);
       }
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.s_full, j & 1, err, kErrWaitAccFull));
       if (!ok) break;
       tc_fence_after();
-      uint32_t s[4][32];
+      uint32_t s[2][32];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) tmem_ld32(t_s + lane_off + q * 32, s[q]);
+      for (int q = 0; q < 2; ++q) tmem_ld32(t_s + lane_off + half * 64 + q * 32, s[q]);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.s_empty);
       // Row max per scale group over the integer scores: w > 0 and rounding is monotonic, so max(S) * w rounds
-      // to max(S * w) (the same m as scaling every score first). Then one FMA per score gives the exponent
-      // argument S * w + log2(448) - m, so that 2^arg = 448 p directly (P's FP8 scale folded in); l sums 448 p.
-      const int lim = a.L - j * BKV;  // valid keys of this tile (all 128 but in the last one)
-      float m_new = m, alpha = 1.f, sum = 0.f;
-      uint32_t pk[32];
+      // to max(S * w) (the same m as scaling every score first); the two halves' maxima meet in shared memory.
+      // Then one FMA per score gives the exponent argument S * w + log2(448) - m, so that 2^arg = 448 p
+      // directly (P's FP8 scale folded in); l sums 448 p.
+      const int lim = a.L - j * BKV - half * 64;  // valid keys of this half of the tile (all 64 but at the end)
+      float alpha = 1.f, sum = 0.f;
+      uint32_t pk[16];
       auto tile = [&](auto masked) {
         constexpr bool kMasked = decltype(masked)::value;
-        int32_t gmax[8];
+        int32_t gmax[4];
 #pragma unroll
-        for (int g = 0; g < 8; ++g) gmax[g] = INT32_MIN;
+        for (int g = 0; g < 4; ++g) gmax[g] = INT32_MIN;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < 2; ++q)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int col = q * 32 + i, g = (col / 64) * 4 + (col % 8) / 2;
+            const int col = q * 32 + i, g = (col % 8) / 2;
             if (!kMasked || col < lim) gmax[g] = max(gmax[g], static_cast<int32_t>(s[q][i]));
           }
         float mx = -INFINITY;
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
+        for (int g = 0; g < 4; ++g)
           if (gmax[g] != INT32_MIN) mx = fmaxf(mx, exact_float(static_cast<uint32_t>(gmax[g])) * w[g]);
-        m_new = fmaxf(m, mx);
+        sm.row_max[j & 1][half][row] = mx;
+        if (!pair_exchange(&sm.pair[quarter], j, lane, err)) ok = false;
+        const float m_new = fmaxf(m, fmaxf(mx, sm.row_max[j & 1][half ^ 1][row]));
         alpha = ex2(m - m_new);
+        m = m_new;
         const float base = kLog2PScale - m_new;
 #pragma unroll
-        for (int col = 0; col < 128; col += 4) {
+        for (int col = 0; col < 64; col += 4) {
           float p[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int c2 = col + e, g = (c2 / 64) * 4 + (c2 % 8) / 2;
-            p[e] = ex2(fmaf(exact_float(s[c2 / 32][c2 % 32]), w[g], base));
+            const int c2 = col + e, g = (c2 % 8) / 2;
+            const float arg = fmaf(exact_float(s[c2 / 32][c2 % 32]), w[g], base);
+            p[e] = e >= 4 - kPoly ? exp2_fma(arg) : ex2(arg);
             if (kMasked && c2 >= lim) p[e] = 0.f;
           }
           sum += (p[0] + p[1]) + (p[2] + p[3]);
@@ -219,47 +252,55 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
           pk[col / 4] = lo | (hi << 16);
         }
       };
-      if (lim >= BKV) tile(std::false_type{});
+      const float m_old = m;
+      if (lim >= 64) tile(std::false_type{});
       else tile(std::true_type{});
+      if (!ok) break;
       l = l * alpha + sum;
       if (j > 0) {
         // P V of the previous tile must be done: O is then stable and the P buffer free
         ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.o_done, (j - 1) & 1, err, kErrWaitAccFull));
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xFFFFFFFFu, m_new > m)) {
+        if (__any_sync(0xFFFFFFFFu, m > m_old)) {  // this half of O's columns, rescaled to the new maximum
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < 2; ++q) {
             uint32_t o[32];
-            tmem_ld32(t_o + lane_off + q * 32, o);
+            tmem_ld32(t_o + lane_off + half * 64 + q * 32, o);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(t_o + lane_off + q * 32, o);
+            tmem_st32(t_o + lane_off + half * 64 + q * 32, o);
           }
           tmem_st_wait();
         }
       }
 #pragma unroll
-      for (int chunk = 0; chunk < 8; ++chunk)
-        *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) =
+      for (int chunk = 0; chunk < 4; ++chunk) {
+        const int c16 = half * 4 + chunk;  // this half's 16-byte chunks of the row
+        *reinterpret_cast<uint4*>(prow + ((c16 ^ (row & 7)) << 4)) =
             make_uint4(pk[chunk * 4], pk[chunk * 4 + 1], pk[chunk * 4 + 2], pk[chunk * 4 + 3]);
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.p_full);
-      m = m_new;
     }
     if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.o_done, (T - 1) & 1, err, kErrWaitAccFull));
+    // the row sum of both halves: one more phase of the quarter's barrier after the T of the tiles
+    sm.row_sum[half][row] = l;
+    if (ok) ok = pair_exchange(&sm.pair[quarter], T, lane, err);
+    l += sm.row_sum[half ^ 1][row];
     if (ok) {
       tc_fence_after();
       const float inv = 1.f / l;  // l sums 448 p
       const float* vsc = a.v_scale + h * HD;
       __nv_bfloat16* out = a.out + static_cast<int64_t>(t) * a.ld_out + h * HD;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
+        const int d0 = half * 64 + q * 32;  // this thread's 32 channels of the output row
         uint32_t o[32];
-        tmem_ld32(t_o + lane_off + q * 32, o);
+        tmem_ld32(t_o + lane_off + d0, o);
         tmem_ld_wait();
         if (t < a.nq) {
 #pragma unroll
@@ -267,12 +308,12 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
             uint32_t wv[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const int d = q * 32 + i + 2 * e;
+              const int d = d0 + i + 2 * e;
               const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o[i + 2 * e]) * __ldg(vsc + d) * inv,
                                                               __uint_as_float(o[i + 2 * e + 1]) * __ldg(vsc + d + 1) * inv);
               wv[e] = *reinterpret_cast<const uint32_t*>(&b2);
             }
-            *reinterpret_cast<uint4*>(out + q * 32 + i) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            *reinterpret_cast<uint4*>(out + d0 + i) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
           }
         }
       }
@@ -305,10 +346,11 @@ int attn_launch(const AttnArgs& a, uint32_t* err, cudaStream_t s, const char** w
     *why = "cuTensorMapEncodeTiled rejected an attention operand";
     return 2;
   }
-  cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  auto kernel = attn_kernel<kAttnPolyShare>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(kAttnSmemBytes));
   if (e == cudaSuccess) {
-    attn_kernel<<<dim3(npad / BQ, a.H), kAttnThreads, kAttnSmemBytes, s>>>(mq, mk, mv, a, err);
+    kernel<<<dim3(npad / BQ, a.H), kAttnThreads, kAttnSmemBytes, s>>>(mq, mk, mv, a, err);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
