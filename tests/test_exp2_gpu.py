@@ -1,6 +1,7 @@
-"""The attention softmax evaluates a share of its exponentials on the FMA pipe (csrc/common.cuh exp2_fma: round to
-the nearest integer by the 1.5 * 2^23 shift, a degree-4 polynomial for 2^f on [-0.5, 0.5], the integer added to
-the exponent field) instead of the special function unit. This checks that function against exact powers of two
+"""The attention softmax can evaluate a compile-time share of its exponentials on the FMA pipe (csrc/common.cuh
+exp2_fma: round to the nearest integer by the 1.5 * 2^23 shift, a degree-4 polynomial for 2^f on [-0.5, 0.5], the
+integer added to the exponent field) instead of the special function unit (sage_attn.cu kAttnPolyShare, 0 as
+measured fastest). This checks that function against exact powers of two
 (float64) over every argument range the softmax produces (score minus row maximum, times log2(e) and the scales:
 <= 0, down to the -100 clamp) and past it, next to CUDA's exp2f on the same arguments."""
 
