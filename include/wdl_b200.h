@@ -314,8 +314,14 @@ int wdl_sage_prep_kv(const uint8_t* cache_k, const float* cache_ks, const uint8_
                      void* stream);
 int wdl_sage_quant_q(const float* q, int64_t ld_q, int nq, int H, int8_t* q_i8, float* q_scale, void* stream);
 
-/* Both in one call, the quantized operands in the caller's workspace of wdl_sage_attend_workspace(nq, L, H) bytes
- * (256-byte aligned). sage_kv.attend (kernels/sage_kv.py:127-176) with heads = tokens = None. */
+/* Attention over the FP8 KV cache in one call: sage_kv.attend (kernels/sage_kv.py:127-176) with heads = tokens =
+ * None, scratch in the caller's workspace of wdl_sage_attend_workspace(nq, L, H) bytes (256-byte aligned). Q and
+ * K are quantized as wdl_sage_prep does. V is not re-quantized per channel: P V reads V as the cache holds it,
+ * E4M3 rows with a scale per (token, head), through TMA in place (cache_v 16-byte aligned), each key's scale
+ * folded into P before its E4M3 rounding (P = E4M3(448 p vs[t] / max vs), out = O / sum(448 p / max vs)). The
+ * chunk's values v are quantized per (token, head) by the cache's own rule (kernels/cache_fp8.py:23-41) into the
+ * workspace; v = null means the caller has already stored them in the cache at rows [at, at + n) (wdl_qkv_prep
+ * does), so that every key is read from the cache. */
 size_t wdl_sage_attend_workspace(int nq, int L, int H);
 int wdl_sage_attend(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
                     const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype, int64_t ld_k,
@@ -326,7 +332,8 @@ int wdl_sage_attend(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k
  * KVCache.attend_split, generation/causal.py:222-240): the cache holds cache_rows rows of cache_heads heads
  * ([cache_rows, cache_heads, 128] and [cache_rows, cache_heads]); head h of the call (of q, k, v, out; H of them)
  * is cache head heads[h] (null: h, and then cache_heads == H); cached key j < at is cache row tokens[j] (null: row
- * j, and then at <= cache_rows). Neither copies the cache. A map entry out of range is read as 0 and reported in
+ * j, and then at <= cache_rows). Neither copies the cache's keys; its values are gathered through the maps into
+ * the workspace in their E4M3 form (v may not be null here). A map entry out of range is read as 0 and reported in
  * the device error word (wdl_device_error). */
 int wdl_sage_attend_maps(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
                          const uint8_t* cache_v, const float* cache_vs, int cache_rows, int cache_heads,

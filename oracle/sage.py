@@ -14,11 +14,16 @@ Reference (src/wan_dit_lab/kernels/sage_kv.py; SageAttention 2.2.0's kernel itse
     dequantized operands (float64); subtracting the key mean leaves softmax unchanged.
 Parity unpinned for the kernel's own P V rounding (SageAttention's code is absent); the quantizers are pinned by
 the reference's Triton kernels run on the CPU.
+
+quant_v_tokens and attention_fp8_p's key_scale restate this build's own P V over the cache (not the reference's):
+V stays in the cache's per-(token, head) E4M3 form, the chunk's rows quantized by the cache's own rule, and each
+key's scale is folded into P before its E4M3 rounding, P = E4M3(448 p vs[t] / max vs), so that P V reads the
+cache's bytes in place.
 """
 
 import numpy as np
 
-from oracle.fp8 import from_e4m3_bits, to_e4m3_bits
+from oracle.fp8 import from_e4m3_bits, quantize_rows, to_e4m3_bits
 
 V_MAX = 2.25
 BLKQ, WARPQ, BLKK = 128, 32, 64
@@ -66,6 +71,17 @@ def quant_v(V):
     return out, v_scale
 
 
+def quant_v_tokens(cache_v, cache_vs, V, at):
+    """This build's V operand over the FP8 cache: the cached rows [0, at) as the cache holds them (E4M3 bytes and a
+    scale per token and head), the chunk's rows quantized per token and head by the cache's own rule
+    (oracle.fp8.quantize_rows, reference kernels/cache_fp8.py:23-41). Returns (bytes [B, L, H, D] uint8,
+    scales [B, L, H] float32)."""
+    c8, cs = quantize_rows(np.asarray(V, np.float32))
+    codes = np.concatenate([np.asarray(cache_v[:, :at], np.uint8), c8], axis=1)
+    scales = np.concatenate([np.asarray(cache_vs[:, :at], np.float32)[..., 0], cs[..., 0]], axis=1)
+    return codes, scales
+
+
 def unpermute_v(v_fp8, L):
     """[B, D, H, padded] Sage layout -> E4M3 bytes [B, L, H, D] in token order."""
     i = np.arange(L)
@@ -103,7 +119,7 @@ def attention(q, k, v, sm_scale=None):
     return out
 
 
-def attention_fp8_p(q, k, v_codes, v_scale, sm_scale=None, tile=128, p_scale=448.0):
+def attention_fp8_p(q, k, v_codes, v_scale, sm_scale=None, tile=128, p_scale=448.0, key_scale=None):
     """SageAttention 2's P V in FP8, per head: online softmax over key tiles of `tile` (running max m, sum l, the
     output rescaled by 2^(m_old - m_new)), each tile's P = E4M3(2^(s - m) * p_scale) times the FP8 V codes
     (float64 accumulation), the channel scale and 1 / (p_scale l) applied at the end. q, k dequantized
@@ -112,7 +128,11 @@ def attention_fp8_p(q, k, v_codes, v_scale, sm_scale=None, tile=128, p_scale=448
     Evaluated without the loop over tiles: tile j's running max m_j is the cumulative maximum of the tiles' own
     maxima, so every tile's P (and its E4M3 rounding) is formed at once with its own m_j, and the online rescaling
     folds into one factor 2^(m_j - m_last) per tile and row. The same FP8 values as the loop; the float64 sums
-    differ from it only at float64 rounding."""
+    differ from it only at float64 rounding.
+
+    key_scale [B, L, H] (v_scale then None): V's scale per key instead of per channel, folded into P before its
+    E4M3 rounding as P = E4M3(p_scale 2^(s - m) key_scale[t] / max(key_scale)); the output is then
+    O max(key_scale) / (p_scale l)."""
     q, k, vc = (np.asarray(t, np.float64) for t in (q, k, v_codes))
     sm_scale = q.shape[-1] ** -0.5 if sm_scale is None else sm_scale
     B, n, H, D = q.shape
@@ -128,28 +148,41 @@ def attention_fp8_p(q, k, v_codes, v_scale, sm_scale=None, tile=128, p_scale=448
             m = np.maximum.accumulate(st.max(2), axis=1)  # [n, tiles]: the running max after each tile
             p = np.exp2(st - m[:, :, None])  # each tile against its own running max
             lsum = (p.sum(2) * np.exp2(m - m[:, -1:])).sum(1)
-            p8 = from_e4m3_bits(to_e4m3_bits((p * p_scale).astype(np.float32))).astype(np.float64)
+            if key_scale is None:
+                p8 = from_e4m3_bits(to_e4m3_bits((p * p_scale).astype(np.float32))).astype(np.float64)
+            else:
+                ks = np.asarray(key_scale[b, :, h], np.float64)
+                kmax = ks.max()
+                kt = np.pad(ks / kmax, (0, pad)).reshape(tiles, tile)
+                p8 = from_e4m3_bits(to_e4m3_bits((p * p_scale * kt[None]).astype(np.float32))).astype(np.float64)
             p8 *= np.exp2(m - m[:, -1:])[:, :, None]  # the online rescaling, applied once per tile
             o = p8.reshape(n, tiles * tile)[:, :L] @ vc[b, :, h]
-            out[b, :, h] = o * v_scale[b, h][None, :] / (p_scale * lsum[:, None])
+            scale = v_scale[b, h][None, :] if key_scale is None else kmax
+            out[b, :, h] = o * scale / (p_scale * lsum[:, None])
     return out
 
 
-def sage_attention(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=None, fp8_p=False, rows=None):
+def sage_attention(Q, cache_k, cache_ks, cache_v, cache_vs, at, K, V, sm_scale=None, fp8_p=False, rows=None,
+                   token_v=False):
     """sage_kv.attend on the dequantized Sage operands: what the INT8 / FP8 kernel approximates, exactly; with
     fp8_p, P V in FP8 tile by tile as the kernel computes it (attention_fp8_p). rows: the query rows to compute
     (all when None); Q's INT8 scales are formed over every row first, so a row's result does not depend on which
-    others are computed."""
+    others are computed. token_v: this build's V over the cache (quant_v_tokens, the key scale folded into P)
+    instead of the reference's per-channel V."""
     Kf = load(cache_k, cache_ks, K, at)
-    Vf = load(cache_v, cache_vs, V, at)
     kq, ks, _ = quant_k(Kf)
-    v8, vs = quant_v(Vf)
     qq, qs = quant_q(np.asarray(Q, np.float32))
     L = Kf.shape[1]
     kd = dequant_k(kq, ks)
     qd = dequant_q(qq, qs)
     if rows is not None:
         qd = qd[:, np.asarray(rows)]
+    if token_v:
+        vb, vsc = quant_v_tokens(cache_v, cache_vs, V, at)
+        if fp8_p:
+            return attention_fp8_p(qd, kd, from_e4m3_bits(vb), None, sm_scale, key_scale=vsc)
+        return attention(qd, kd, from_e4m3_bits(vb) * vsc[..., None], sm_scale)
+    v8, vs = quant_v(load(cache_v, cache_vs, V, at))
     if fp8_p:
         return attention_fp8_p(qd, kd, from_e4m3_bits(unpermute_v(v8, L)), vs, sm_scale)
     vd = from_e4m3_bits(unpermute_v(v8, L)) * vs[:, None]

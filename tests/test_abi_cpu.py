@@ -72,7 +72,7 @@ def test_workspace_sizes(native):
     np_, lp = 1408, 5632
     up = lambda x: (x + 255) // 256 * 256  # noqa: E731
     want = (up(H * np_ * 128) + up(H * np_ // 32 * 8 * 4) + up(H * lp * 128) + up(H * lp // 64 * 4 * 4) +
-            up(H * 128 * lp) + up(H * 128 * 4) + up(lib.wdl_sage_prep_workspace(L, H)))
+            up(lp * H * 128) + up(H * lp * 4) + up(H * 4) + up(lib.wdl_sage_prep_workspace(L, H)))
     assert lib.wdl_sage_attend_workspace(1392, L, H) == want
 
 

@@ -170,12 +170,16 @@ def test_self_attention(run):
     ck8, cks, cv8, cvs = run["cache"]
     Q, K, V = self_attention_operands(run)
     got = run["gpu"]["attn"][ROWS]
-    emulated = osage.sage_attention(Q, ck8, cks, cv8, cvs, AT, K, V, fp8_p=True, rows=ROWS).reshape(len(ROWS), DIM)
+    # the reference's Sage arithmetic (V re-quantized per channel) and this kernel's (P V over the cache's
+    # per-token V, each key's scale folded into P)
+    reference = osage.sage_attention(Q, ck8, cks, cv8, cvs, AT, K, V, fp8_p=True, rows=ROWS).reshape(len(ROWS), DIM)
+    emulated = osage.sage_attention(Q, ck8, cks, cv8, cvs, AT, K, V, fp8_p=True, rows=ROWS,
+                                    token_v=True).reshape(len(ROWS), DIM)
     exact = osage.attention(Q[:, ROWS], osage.load(ck8, cks, K, AT), osage.load(cv8, cvs, V, AT)).reshape(len(ROWS), DIM)
-    c_emu, c_exact = cosine(got, emulated), cosine(got, exact)
-    print(f"self-attention: cosine {c_emu:.6f} vs the oracle's Sage arithmetic, {c_exact:.6f} vs exact; "
-          f"relative L2 {rel(got, emulated):.2e}")
-    assert c_emu >= COS_BAR and c_exact >= COS_BAR
+    c_ref, c_exact = cosine(got, reference), cosine(got, exact)
+    print(f"self-attention: cosine {c_ref:.6f} vs the reference's Sage arithmetic, {c_exact:.6f} vs exact; "
+          f"relative L2 {rel(got, emulated):.2e} vs its own P V emulated")
+    assert c_ref >= COS_BAR and c_exact >= COS_BAR
     assert rel(got, emulated) < 5e-3  # the kernel's FP8 P V against its emulation
 
 

@@ -1,8 +1,10 @@
 """SageAttention over the FP8 cache on the B200 kernels against the CPU oracle (oracle/sage.py): the quantized
 operands in value space (Q INT8 and scales bitwise; K INT8 within +-1 and its scales to 1e-5, since the key
 mean is a float sum in another order; V FP8 bytes >= 99.9 % equal), and the attention output against exact
-attention over the dequantized operands (cosine >= 0.999, the stated bar) and against exact attention over the
-unquantized keys and values (the reference's test_sage_kv.py:86-98 style)."""
+attention over the dequantized operands (cosine >= 0.999, the stated bar), against exact attention over the
+unquantized keys and values (the reference's test_sage_kv.py:86-98 style), against the emulation of its own P V
+over the cache's per-token V (relative L2 < 5e-3) and against the emulation of the reference's per-channel P V
+(cosine >= 0.999)."""
 
 import numpy as np
 import pytest
@@ -71,8 +73,11 @@ def test_attention_matches_oracle(at, n, nq, H):
     exact = osage.attention(host["Q"], osage.load(host["ck"], host["cks"], host["K"], at),
                             osage.load(host["cv"], host["cvs"], host["V"], at))
     emulated = osage.sage_attention(host["Q"], host["ck"], host["cks"], host["cv"], host["cvs"], at, host["K"], host["V"],
-                                    fp8_p=True)
+                                    fp8_p=True, token_v=True)
     assert float(np.linalg.norm(out - emulated) / np.linalg.norm(emulated)) < 5e-3  # the kernel's own FP8 P V
+    reference = osage.sage_attention(host["Q"], host["ck"], host["cks"], host["cv"], host["cvs"], at, host["K"],
+                                     host["V"], fp8_p=True)  # the reference's P V: V re-quantized per channel
+    assert cosine(out, reference) >= 0.999
     c_q, c_e = cosine(out, quantized), cosine(out, exact)
     err = lambda x: float(np.linalg.norm(x - exact) / np.linalg.norm(exact))  # noqa: E731
     print(f"at {at} n {n}: cos vs dequantized {c_q:.6f}, vs exact {c_e:.6f}; rel err kernel {err(out):.4f}, "
@@ -132,3 +137,36 @@ def test_forcing_kv_map_out_of_range_is_reported():
         _native.device_error()
     assert torch.isfinite(out.float()).all()
     assert _native.device_error() == 0  # read and cleared
+
+
+@pytest.mark.parametrize("at,n,H", [(200, 150, 2), (256, 100, 1), (0, 300, 2), (4176, 1392, 3)])
+def test_values_stored_in_the_cache_equal_values_given(at, n, H):
+    """P V reads V as the cache holds it. The chunk's values passed in 16 bits (quantized by the call into its
+    workspace, the keys before `at` of their 128-key tile copied beside them) and the same values stored in the
+    cache first by the cache's own store (cache_fp8.store_kv_fp8) and read from there (v null, as the model calls
+    it after wdl_qkv_prep) give the same attention, bit for bit."""
+    from wan_dit_lab_b200 import _native
+    from wan_dit_lab_b200.kernels import cache_fp8, sage_kv
+    _, d = setup(at, n, n, H, seed=11 + at)
+    given = sage_kv.attend(d["Q"], d["ck"], d["cks"], d["cv"], d["cvs"], at, d["K"], d["V"])
+    ck, cks, cv, cvs = (d[x].clone() for x in ("ck", "cks", "cv", "cvs"))
+    cache_fp8.store_kv_fp8(d["K"], d["V"], ck, cks, cv, cvs, at)
+    lib = _native.lib()
+    L = at + n
+    q = d["Q"][0].reshape(n, H * 128).contiguous()
+    k = d["K"][0].reshape(n, H * 128).contiguous()
+    out = torch.empty(n, H * 128, dtype=torch.bfloat16, device="cuda")
+    work = torch.empty(lib.wdl_sage_attend_workspace(n, L, H), dtype=torch.uint8, device="cuda")
+    _native.check(lib.wdl_sage_attend(q.data_ptr(), H * 128, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(),
+                                      cvs.data_ptr(), at, k.data_ptr(), _native.F32, H * 128, None, _native.BF16,
+                                      H * 128, n, H, 128 ** -0.5, out.data_ptr(), H * 128, work.data_ptr(),
+                                      work.numel(), _native.stream()))
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    assert torch.equal(out, given[0].reshape(n, H * 128))
+    # with index maps the chunk's values are required
+    st = lib.wdl_sage_attend_maps(q.data_ptr(), H * 128, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(),
+                                  cvs.data_ptr(), ck.shape[1], H, None, None, at, k.data_ptr(), _native.F32, H * 128,
+                                  None, _native.BF16, H * 128, n, H, 128 ** -0.5, out.data_ptr(), H * 128,
+                                  work.data_ptr(), work.numel(), _native.stream())
+    assert st == _native.ERR_ARGUMENT

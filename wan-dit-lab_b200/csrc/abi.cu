@@ -604,29 +604,51 @@ struct SageMaps {
   const int32_t* tokens;
 };
 
+// Per-token V of wdl_sage_attend (sage.h, PrepArgs::token_v): keys [0, rows0) read in place from the cache, the
+// rest from `rows`; each key's scale into tok_scale [H][Lpad], each head's largest into head_max [H].
+struct SageTokenV {
+  int rows0;
+  uint8_t* rows;
+  float* tok_scale;
+  float* head_max;
+};
+
 static int sage_prep_impl(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, const float* cache_ks,
                           const uint8_t* cache_v, const float* cache_vs, int at, const void* k, int k_dtype,
                           int64_t ld_k, const void* v, int v_dtype, int64_t ld_v, int n, int H, int8_t* q_i8,
                           float* q_scale, int8_t* k_i8, float* k_scale, uint8_t* v_f8, float* v_scale, void* work,
-                          size_t work_bytes, const SageMaps* maps, void* stream) {
+                          size_t work_bytes, const SageMaps* maps, const SageTokenV* tv, void* stream) {
   if (nq <= 0 || n < 0 || at < 0 || H <= 0 || at + n <= 0) return fail(WDL_ERR_ARGUMENT, "nq, H and L = at + n must be positive");
+  const bool v_in_cache = tv && !v;  // the chunk's values already in the cache at rows [at, at + n)
+  if (v_in_cache) {
+    if (maps || tv->rows0 != at + n) return fail(WDL_ERR_ARGUMENT, "the chunk's values are required with index maps");
+    v_dtype = WDL_BF16, ld_v = static_cast<int64_t>(H) * 128;
+  }
   if ((k_dtype != WDL_F32 && k_dtype != WDL_BF16) || (v_dtype != WDL_F32 && v_dtype != WDL_BF16))
     return fail(WDL_ERR_ARGUMENT, "chunk K and V must be float32 or bf16");
   if (ld_q < static_cast<int64_t>(H) * 128 || (n > 0 && (ld_k < static_cast<int64_t>(H) * 128 || ld_v < static_cast<int64_t>(H) * 128)))
     return fail(WDL_ERR_ARGUMENT, "row strides must hold H x 128 channels");
   if (at > 0 && (!cache_k || !cache_ks || !cache_v || !cache_vs)) return fail(WDL_ERR_ARGUMENT, "null cache pointer");
-  if (!q || (n > 0 && (!k || !v)) || !q_i8 || !q_scale || !k_i8 || !k_scale || !v_f8 || !v_scale)
+  if (v_in_cache && n > 0 && (!cache_v || !cache_vs)) return fail(WDL_ERR_ARGUMENT, "null cache pointer");
+  if (!q || (n > 0 && (!k || (!v && !v_in_cache))) || !q_i8 || !q_scale || !k_i8 || !k_scale ||
+      (!tv && (!v_f8 || !v_scale)) || (tv && (!tv->rows || !tv->tok_scale || !tv->head_max)))
     return fail(WDL_ERR_ARGUMENT, "null pointer");
   if (!work || work_bytes < wdl_sage_prep_workspace(at + n, H))
     return fail(WDL_ERR_ARGUMENT, "workspace of %zu bytes required", wdl_sage_prep_workspace(at + n, H));
-  if (!aligned(q_i8, 16) || !aligned(k_i8, 16) || !aligned(v_f8, 16) || !aligned(v_scale, 16) || !aligned(q, 16) ||
-      ld_q % 4 != 0 || !sage_sources_aligned(cache_k, cache_v, at, k, k_dtype, ld_k, v, v_dtype, ld_v, n))
+  if (!aligned(q_i8, 16) || !aligned(k_i8, 16) || (!tv && (!aligned(v_f8, 16) || !aligned(v_scale, 16))) ||
+      !aligned(q, 16) || ld_q % 4 != 0 ||
+      !sage_sources_aligned(cache_k, cache_v, at, k, k_dtype, ld_k, v, v_dtype, ld_v, n) ||
+      (tv && (!aligned(tv->rows, 16) || !aligned(tv->tok_scale, 16) || (tv->rows0 > 0 && !aligned(cache_v, 16)))))
     return fail(WDL_ERR_ARGUMENT, "misaligned input or output");
   wdl::sage::PrepArgs a{};
   a.cache_k = cache_k, a.cache_ks = cache_ks, a.cache_v = cache_v, a.cache_vs = cache_vs, a.at = at;
   a.k_chunk = k, a.ld_k = ld_k, a.k_bf16 = k_dtype == WDL_BF16, a.v_chunk = v, a.ld_v = ld_v, a.v_bf16 = v_dtype == WDL_BF16;
   a.n = n, a.H = H, a.q = q, a.ld_q = ld_q, a.nq = nq, a.q_i8 = q_i8, a.q_scale = q_scale, a.k_i8 = k_i8;
   a.k_scale = k_scale, a.v_f8 = v_f8, a.v_scale = v_scale, a.work = static_cast<float*>(work);
+  if (tv) {
+    a.token_v = 1, a.rows0 = tv->rows0, a.v_rows = tv->rows, a.v_tok_scale = tv->tok_scale;
+    a.v_head_max = tv->head_max;
+  }
   if (maps) {
     a.cache_H = maps->cache_heads, a.cache_rows = maps->cache_rows, a.hmap = maps->heads, a.tmap = maps->tokens;
     a.err = error_word();
@@ -643,7 +665,7 @@ int wdl_sage_prep(const float* q, int64_t ld_q, int nq, const uint8_t* cache_k, 
                   const void* v, int v_dtype, int64_t ld_v, int n, int H, int8_t* q_i8, float* q_scale, int8_t* k_i8,
                   float* k_scale, uint8_t* v_f8, float* v_scale, void* work, size_t work_bytes, void* stream) {
   return sage_prep_impl(q, ld_q, nq, cache_k, cache_ks, cache_v, cache_vs, at, k, k_dtype, ld_k, v, v_dtype, ld_v, n,
-                        H, q_i8, q_scale, k_i8, k_scale, v_f8, v_scale, work, work_bytes, nullptr, stream);
+                        H, q_i8, q_scale, k_i8, k_scale, v_f8, v_scale, work, work_bytes, nullptr, nullptr, stream);
 }
 
 int wdl_sage_attention(const int8_t* q_i8, const float* q_scale, const int8_t* k_i8, const float* k_scale,
@@ -670,7 +692,7 @@ size_t wdl_sage_attend_workspace(int nq, int L, int H) {
   if (nq <= 0 || L <= 0 || H <= 0) return 0;
   const size_t np = pad128(nq), lp = pad128(L), h = static_cast<size_t>(H);
   return up256(h * np * 128) + up256(h * np / 32 * 8 * 4) + up256(h * lp * 128) + up256(h * lp / 64 * 4 * 4) +
-         up256(h * 128 * lp) + up256(h * 128 * 4) + up256(wdl_sage_prep_workspace(L, H));
+         up256(lp * h * 128) + up256(h * lp * 4) + up256(h * 4) + up256(wdl_sage_prep_workspace(L, H));
 }
 
 }  // extern "C"
@@ -695,15 +717,36 @@ static int sage_attend_impl(const float* q, int64_t ld_q, int nq, const uint8_t*
   p += up256(h * lp * 128);
   float* k_scale = reinterpret_cast<float*>(p);
   p += up256(h * lp / 64 * 4 * 4);
-  uint8_t* v_f8 = reinterpret_cast<uint8_t*>(p);
-  p += up256(h * 128 * lp);
-  float* v_scale = reinterpret_cast<float*>(p);
-  p += up256(h * 128 * 4);
+  // V as the cache holds it: keys [0, rows0) in place; the rest (the cached keys of the tile that holds `at`,
+  // and the chunk's) in the scratch rows. With maps every key goes through the scratch; with the chunk's values
+  // already in the cache (v null) none does.
+  SageTokenV tv{};
+  tv.rows0 = maps ? 0 : (v ? at / 128 * 128 : L);
+  tv.rows = reinterpret_cast<uint8_t*>(p);
+  p += up256(lp * h * 128);
+  tv.tok_scale = reinterpret_cast<float*>(p);
+  p += up256(h * lp * 4);
+  tv.head_max = reinterpret_cast<float*>(p);
+  p += up256(h * 4);
+  if (ld_out < static_cast<int64_t>(H) * 128 || (ld_out * 2) % 16 != 0)
+    return fail(WDL_ERR_ARGUMENT, "ld_out must hold H x 128 channels, 16-byte rows");
+  if (!out || !aligned(out, 16)) return fail(WDL_ERR_ARGUMENT, "null or misaligned output");
   int st = sage_prep_impl(q, ld_q, nq, cache_k, cache_ks, cache_v, cache_vs, at, k, k_dtype, ld_k, v, v_dtype, ld_v,
-                          n, H, q_i8, q_scale, k_i8, k_scale, v_f8, v_scale, p, wdl_sage_prep_workspace(L, H), maps,
-                          stream);
+                          n, H, q_i8, q_scale, k_i8, k_scale, nullptr, nullptr, p, wdl_sage_prep_workspace(L, H), maps,
+                          &tv, stream);
   if (st != WDL_OK) return st;
-  return wdl_sage_attention(q_i8, q_scale, k_i8, k_scale, v_f8, v_scale, nq, L, H, sm_scale, out, ld_out, stream);
+  uint32_t* err = error_word();
+  if (!err) return fail(WDL_ERR_CUDA, "cannot resolve the device error word");
+  wdl::sage::AttnArgs a{};
+  a.q_i8 = q_i8, a.q_scale = q_scale, a.k_i8 = k_i8, a.k_scale = k_scale;
+  a.token_v = 1, a.v_rows0 = cache_v, a.ld_v0 = static_cast<int64_t>(H) * 128, a.rows0 = tv.rows0;
+  a.v_rows1 = tv.rows, a.v_tok_scale = tv.tok_scale, a.v_head_max = tv.head_max;
+  a.nq = nq, a.L = L, a.H = H, a.sm_scale_log2 = sm_scale * 1.4426950408889634f;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out), a.ld_out = ld_out;
+  const char* why = "";
+  st = wdl::sage::attn_launch(a, err, static_cast<cudaStream_t>(stream), &why);
+  if (st != 0) return fail(WDL_ERR_CUDA, "%s", why);
+  return ok();
 }
 
 extern "C" {

@@ -304,7 +304,23 @@ __device__ __forceinline__ uint64_t smem_desc_k128(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor of a dense tcgen05.mma with both operands K-major.
+// Shared-memory descriptor of an MN-major operand tile in the 128-byte swizzled layout whose MN extent is one
+// 128-byte row (128 8-bit elements): rows of 128 bytes along K, 8-row atoms of 1024 bytes (what a TMA tile load
+// with box {128 bytes, rows} and 128-byte swizzle writes). The stride byte offset steps from one 8-row K group to
+// the next (1024 bytes); the leading byte offset, the step between 128-byte MN blocks, is never taken at this
+// width (set to 16 KB).
+__device__ __forceinline__ uint64_t smem_desc_mn128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);  // start address
+  d |= static_cast<uint64_t>(16384u >> 4) << 16;             // leading byte offset
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;              // stride byte offset: one 8-row K group
+  d |= static_cast<uint64_t>(1u) << 46;                      // descriptor version for sm_100
+  d |= static_cast<uint64_t>(2u) << 61;                      // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor of a dense tcgen05.mma with both operands K-major. Bit 16 set in addition makes B
+// MN-major (allowed for the 8-bit, 16-bit and tf32 formats).
 //   c_format: 0 f16, 1 f32, 2 s32; a/b format: per kind (i8: 0 u8, 1 s8; f16: 0 f16, 1 bf16; f8: 0 e4m3, 1 e5m2)
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_format, uint32_t a_format, uint32_t b_format,
                                                   uint32_t m, uint32_t n) {

@@ -10,7 +10,10 @@
 //   q_i8  [H][npad][128]   q_scale [H][npad / 32 * 8]   (token t: scale (t / 32) * 8 + t % 8)
 //   k_i8  [H][Lpad][128]   k_scale [H][Lpad / 64 * 4]   (key j: scale (j / 64) * 4 + (j % 8) / 2)
 //   v_f8  [H][128][Lpad]   v_scale [H][128]             (keys contiguous: the K-major B operand of P V)
-// with npad, Lpad multiples of 128 and zero codes in the padding.
+// with npad, Lpad multiples of 128 and zero codes in the padding. wdl_sage_attend instead keeps V as the cache
+// holds it (token_v): E4M3 rows with a scale per (token, head), read in place by the attention kernel's TMA, the
+// keys past rows0 in a scratch of the same row layout, and the scales gathered per head into v_tok_scale
+// [H][Lpad] (see v_token_tile).
 #include "common.cuh"
 #include "sage.h"
 
@@ -142,10 +145,91 @@ struct Source {
 // tile. Warp w reads the 16 tokens 16 w .. 16 w + 15 of the tile, lane l channels 4 l .. 4 l + 3 (one 128-byte row
 // segment per token), all 16 of its loads in flight; the four warps' partials meet in shared memory. K and V in
 // separate CTAs: each has one round of loads to wait for, and twice as many CTAs hide each other's latency.
-__global__ void __launch_bounds__(128) partials_kernel(Source ks, Source vs, float* ksum, float* vmax) {
+// Per-token V of the attention over the cache (PrepArgs::token_v).
+struct VTok {
+  int on, rows0, Lpad;
+  uint8_t* rows;       // scratch rows [rows0, L), pitch H * 128 bytes
+  float* tok_scale;    // [H][Lpad]
+  float* tile_max;     // [tiles][H]: each 64-key tile's largest scale
+};
+
+// Per-token V, per (64-key tile, head): each key's scale (a cached key's from the cache; a chunk key's
+// max(max|v|, 1e-12) / 448 over its 128 channels, the cache's own rule, reference kernels/cache_fp8.py:23-41), into
+// v_tok_scale; the keys from rows0 on written to the scratch rows (a cached key's bytes as the cache holds them, a
+// chunk key's as E4M3(v / scale), the division correctly rounded); the tile's largest scale into tile_max. Keys
+// past L get scale 0. Warp w holds keys 16 w .. 16 w + 15 in four rounds of four; lanes 8 i .. 8 i + 7 share one
+// key, 16 channels each (the key's maximum over its eight lanes by shuffles within the group).
+__device__ __forceinline__ void v_token_tile(const Source& vs, const VTok& vt, int tile, int h, float (&red)[4][128]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane >> 3, seg = lane & 7;
+  const unsigned group = 0xFFu << (sub * 8);
+  float top = 0.f;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int t = tile * 64 + warp * 16 + r * 4 + sub;
+    float sc = 0.f;
+    if (t < vs.L) {
+      uint4 bytes = make_uint4(0u, 0u, 0u, 0u);
+      if (t < vs.at) {
+        const int64_t row = vs.cache_row(t) * vs.cache_H + vs.cache_head(h);
+        sc = __ldg(vs.scale + row);
+        if (t >= vt.rows0) bytes = __ldg(reinterpret_cast<const uint4*>(vs.cache + row * 128 + seg * 16));
+      } else {
+        float x[16];
+        const int64_t off = static_cast<int64_t>(t - vs.at) * vs.ld + h * 128 + seg * 16;
+        if (vs.chunk_bf16) {
+          const uint2* p = reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(vs.chunk) + off);
+          uint2 u[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) u[i] = __ldg(p + i);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[i].x));
+            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[i].y));
+            x[4 * i] = a.x, x[4 * i + 1] = a.y, x[4 * i + 2] = b.x, x[4 * i + 3] = b.y;
+          }
+        } else {
+          const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(vs.chunk) + off);
+          float4 f[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) f[i] = __ldg(p + i);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) x[4 * i] = f[i].x, x[4 * i + 1] = f[i].y, x[4 * i + 2] = f[i].z, x[4 * i + 3] = f[i].w;
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(x[i]));
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(group, amax, o));
+        sc = __fdiv_rn(fmaxf(amax, 1e-12f), 448.f);
+        const float rcp = __frcp_rn(sc);
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i / 4] |= static_cast<uint32_t>(e4m3(div_rn_by(x[i], sc, rcp))) << (8 * (i % 4));
+        bytes = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      if (t >= vt.rows0)
+        *reinterpret_cast<uint4*>(vt.rows + static_cast<int64_t>(t - vt.rows0) * vs.H * 128 + h * 128 + seg * 16) = bytes;
+    }
+    if (seg == 0) vt.tok_scale[static_cast<int64_t>(h) * vt.Lpad + t] = sc;
+    top = fmaxf(top, sc);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
+  if (lane == 0) red[0][warp] = top;
+  __syncthreads();
+  if (threadIdx.x == 0) vt.tile_max[static_cast<int64_t>(tile) * vs.H + h] = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
+}
+
+__global__ void __launch_bounds__(128) partials_kernel(Source ks, Source vs, float* ksum, float* vmax, VTok vt) {
   __shared__ float red[4][128];
   const int tile = blockIdx.x, h = blockIdx.y;
   const bool is_v = blockIdx.z != 0;
+  if (is_v && vt.on) {  // the grid spans Lpad / 64 tiles: the scales of the padding keys are written as 0
+    v_token_tile(vs, vt, tile, h, red);
+    return;
+  }
+  if (tile * 64 >= ks.L) return;
   const Source& src = is_v ? vs : ks;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -179,11 +263,42 @@ __global__ void __launch_bounds__(128) partials_kernel(Source ks, Source vs, flo
 // ---- pass 2: per head: key mean (sum / L) and the V channel scales max(max|V|, 1e-8) / 2.25 (V_MAX, :24). CTA
 // (h, c) holds channels 32 c .. 32 c + 31; its warp w sums tiles w, w + 4, ... (16 loads in flight), and the four
 // warps' sums are added in a fixed order: a short dependent chain instead of one thread walking every tile.
+// With per-token V (vtile_max set), vmax and v_scale are unused and CTA (h, 0) also takes the largest of head h's
+// tile maxima into v_head_max[h].
 __global__ void __launch_bounds__(128) reduce_kernel(const float* ksum, const float* vmax, int tiles, int H, int L,
-                                                     float* kmean, float* v_scale) {
+                                                     float* kmean, float* v_scale, const float* vtile_max,
+                                                     int vtiles, float* v_head_max) {
   __shared__ float red[2][4][32];
   const int h = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int d = blockIdx.y * 32 + lane;
+  if (vtile_max) {
+    if (blockIdx.y == 0) {
+      float top = 0.f;
+      for (int t = threadIdx.x; t < vtiles; t += 128) top = fmaxf(top, vtile_max[static_cast<int64_t>(t) * H + h]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
+      if (lane == 0) red[1][warp][0] = top;
+    }
+    float s = 0.f;
+    int t = warp;
+    for (; t + 28 < tiles; t += 32) {
+      float a[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = ksum[(static_cast<int64_t>(t + 4 * i) * H + h) * 128 + d];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += a[i];
+    }
+    for (; t < tiles; t += 4) s += ksum[(static_cast<int64_t>(t) * H + h) * 128 + d];
+    red[0][warp][lane] = s;
+    __syncthreads();
+    if (warp == 0) {
+      const float sum = (red[0][0][lane] + red[0][1][lane]) + (red[0][2][lane] + red[0][3][lane]);
+      kmean[h * 128 + d] = __fdiv_rn(sum, static_cast<float>(L));
+      if (blockIdx.y == 0 && lane == 0)  // floored: a head whose every scale is 0 keeps log2(vmax) finite
+        v_head_max[h] = fmaxf(fmaxf(fmaxf(red[1][0][0], red[1][1][0]), fmaxf(red[1][2][0], red[1][3][0])), 1e-30f);
+    }
+    return;
+  }
   float s = 0.f, m = 0.f;
   int t = warp;
   for (; t + 28 < tiles; t += 32) {
@@ -348,16 +463,20 @@ void prep_kv_launch(const PrepArgs& a, cudaStream_t s) {
   const int cache_H = a.cache_H > 0 ? a.cache_H : a.H;
   Source ks{a.cache_k, a.cache_ks, a.k_chunk, a.ld_k, a.k_bf16, a.at, L, a.H, cache_H, a.cache_rows, a.hmap, a.tmap,
             a.err};
-  Source vs{a.cache_v, a.cache_vs, a.v_chunk, a.ld_v, a.v_bf16, a.at, L, a.H, cache_H, a.cache_rows, a.hmap, a.tmap,
-            a.err};
+  // no chunk values (per-token V only): the chunk's rows are in the cache already, every key is a cached one
+  Source vs{a.cache_v, a.cache_vs, a.v_chunk, a.ld_v, a.v_bf16, a.v_chunk ? a.at : L, L, a.H, cache_H, a.cache_rows,
+            a.hmap, a.tmap, a.err};
   const int tiles = (L + 63) / 64;
   const int Lpad = (L + 127) / 128 * 128;
   float* ksum = a.work;
-  float* vmax = ksum + static_cast<int64_t>(tiles) * a.H * 128;
+  float* vmax = ksum + static_cast<int64_t>(tiles) * a.H * 128;  // per-token V: the tile maxima [Lpad / 64][H]
   float* kmean = vmax + static_cast<int64_t>(tiles) * a.H * 128;
-  partials_kernel<<<dim3(tiles, a.H, 2), 128, 0, s>>>(ks, vs, ksum, vmax);
-  reduce_kernel<<<dim3(a.H, 4), 128, 0, s>>>(ksum, vmax, tiles, a.H, L, kmean, a.v_scale);
-  quant_kv_kernel<<<dim3(Lpad / 64, a.H, 2), 128, 0, s>>>(ks, vs, kmean, a.v_scale, Lpad, a.k_i8, a.k_scale, a.v_f8);
+  const VTok vt{a.token_v, a.rows0, Lpad, a.v_rows, a.v_tok_scale, vmax};
+  partials_kernel<<<dim3(a.token_v ? Lpad / 64 : tiles, a.H, 2), 128, 0, s>>>(ks, vs, ksum, vmax, vt);
+  reduce_kernel<<<dim3(a.H, 4), 128, 0, s>>>(ksum, vmax, tiles, a.H, L, kmean, a.v_scale, a.token_v ? vmax : nullptr,
+                                             Lpad / 64, a.v_head_max);
+  quant_kv_kernel<<<dim3(Lpad / 64, a.H, a.token_v ? 1 : 2), 128, 0, s>>>(ks, vs, kmean, a.v_scale, Lpad, a.k_i8,
+                                                                         a.k_scale, a.v_f8);
 }
 
 void quant_q_launch(const float* q, int64_t ld_q, int nq, int H, int8_t* q_i8, float* q_scale, cudaStream_t s) {

@@ -44,6 +44,16 @@ struct PrepArgs {
   const int* hmap;
   const int* tmap;
   uint32_t* err;
+  // Per-token V (token_v != 0, wdl_sage_attend): V keeps the cache's E4M3 rows and per-(token, head) scales
+  // instead of v_f8 / v_scale. Keys [0, rows0) are read in place from the cache (rows0 % 128 == 0 or rows0 == L;
+  // rows0 is 0 with maps); keys [rows0, L) go to v_rows (row r = key rows0 + r, pitch H * 128 bytes): cached
+  // rows copied, the chunk's rows quantized per (token, head) by the cache's own rule. v_chunk null: the chunk's
+  // values are already in the cache at rows [at, L) (then rows0 == L).
+  int token_v;
+  int rows0;
+  uint8_t* v_rows;
+  float* v_tok_scale;  // [H][Lpad]: each key's scale, 0 past L
+  float* v_head_max;   // [H]: the largest of a head's key scales
 };
 void prep_launch(const PrepArgs& a, cudaStream_t s);     // K / V then Q
 void prep_kv_launch(const PrepArgs& a, cudaStream_t s);  // K / V only (q fields unused)
@@ -55,8 +65,16 @@ struct AttnArgs {
   const float* q_scale;
   const int8_t* k_i8;
   const float* k_scale;
-  const uint8_t* v_f8;
+  const uint8_t* v_f8;   // per-channel V (token_v 0): [H][128][Lpad] E4M3, scales v_scale [H][128]
   const float* v_scale;
+  int token_v;  // per-token V: E4M3 rows, keys [0, rows0) at v_rows0 (pitch ld_v0 bytes, head h at byte h * 128),
+                // keys [rows0, L) at v_rows1 (pitch H * 128); scales v_tok_scale [H][Lpad], v_head_max [H]
+  const uint8_t* v_rows0;
+  int64_t ld_v0;
+  int rows0;
+  const uint8_t* v_rows1;
+  const float* v_tok_scale;
+  const float* v_head_max;
   int nq, L, H;
   float sm_scale_log2;  // sm_scale * log2(e)
   __nv_bfloat16* out;   // [nq, ld_out] bf16, head h at column h * 128

@@ -11,6 +11,13 @@
 // and finally O * v_scale / (448 l) in bf16. The P scale 448 and the per-channel V scale are SageAttention 2's
 // FP8 P V scheme (sage_kv.py:24 V_MAX = 2.25 keeps |V / v_scale| <= 2.25).
 //
+// Per-token V (kTokenV, the attention over the KV cache): V stays as the FP8 cache holds it, E4M3 rows of 128
+// channels with a scale vs[t] per (key, head). A tile's 128 rows arrive by TMA straight from the cache (the keys
+// past rows0 from a scratch of the same layout) as the MN-major B operand of P V, and the tile's 128 scales by a
+// bulk copy on the same barrier. Each key's scale is folded into P before its E4M3 rounding: with vmax the largest
+// scale of the head, p' = 2^(s - m + log2 448 - log2 vmax) and P = E4M3(p' vs[t]) (<= 448), l sums p', and the
+// output is O / l, no per-channel factor.
+//
 // Warps: 0 TMA producer (Q once, K and V tiles, 2 stages), 1 TMEM owner + MMA issuer, 2-9 softmax: warp w owns
 // TMEM lanes 32 (w % 4) .. +31 (its 32 query rows) and one half of the columns, (w - 2) / 4, so that two threads
 // share a row: each holds 64 scores of a tile, the pair exchanges its row maximum through shared memory (an
@@ -40,6 +47,7 @@ struct __align__(1024) AttnSmem {
   uint8_t k[2][BKV * HD];
   uint8_t v[2][HD * BKV];
   uint8_t p[BQ * BKV];
+  float vsc[2][BKV];  // per-token V: the key scales of each stage's tile
   uint64_t q_full, kv_full[2], kv_empty[2], s_full, s_empty, p_full, o_done;
   uint64_t pair[4];  // per lane quarter: both column halves have published their values (one phase a tile)
   float row_max[2][2][BQ];  // [tile parity][column half][row]: the halves' maxima of a tile's scores
@@ -72,10 +80,11 @@ __device__ __forceinline__ bool pair_exchange(uint64_t* bar, uint32_t phase, int
 // function unit (its pipe is 42 % busy), and the polynomial's nine instructions cost more issue slots than the one
 // ex2 they replace; so the share is 0.
 constexpr int kAttnPolyShare = 0;
-template <int kPoly>
+template <int kPoly, bool kTokenV>
 __global__ void __launch_bounds__(kAttnThreads, 2)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                const __grid_constant__ CUtensorMap map_v, AttnArgs a, uint32_t* err) {
+                const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_v1, AttnArgs a,
+                uint32_t* err) {
   extern __shared__ uint8_t smem_raw[];
   AttnSmem& sm = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -111,15 +120,23 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       prefetch_tensor_map(&map_q);
       prefetch_tensor_map(&map_k);
       prefetch_tensor_map(&map_v);
+      if (kTokenV) prefetch_tensor_map(&map_v1);
+      const int split = (a.rows0 + BKV - 1) / BKV;  // per-token V: tiles [0, split) from the cache rows
       mbar_arrive_expect_tx(&sm.q_full, BQ * HD);
       tma_load_2d(sm.q, &map_q, &sm.q_full, 0, h * npad + qt * BQ);
       int issued = 0;
       for (int j = 0; j < T; ++j) {
         const int st = j & 1;
         if (!mbar_wait(&sm.kv_empty[st], ((j >> 1) & 1) ^ 1, err, kErrWaitEmpty)) break;
-        mbar_arrive_expect_tx(&sm.kv_full[st], 2 * BKV * HD);
+        mbar_arrive_expect_tx(&sm.kv_full[st], 2 * BKV * HD + (kTokenV ? BKV * 4 : 0));
         tma_load_2d(sm.k[st], &map_k, &sm.kv_full[st], 0, h * Lpad + j * BKV);
-        tma_load_2d(sm.v[st], &map_v, &sm.kv_full[st], j * BKV, h * HD);
+        if constexpr (kTokenV) {
+          if (j < split) tma_load_2d(sm.v[st], &map_v, &sm.kv_full[st], h * HD, j * BKV);
+          else tma_load_2d(sm.v[st], &map_v1, &sm.kv_full[st], h * HD, j * BKV - a.rows0);
+          bulk_load(sm.vsc[st], a.v_tok_scale + static_cast<int64_t>(h) * Lpad + j * BKV, BKV * 4, &sm.kv_full[st]);
+        } else {
+          tma_load_2d(sm.v[st], &map_v, &sm.kv_full[st], j * BKV, h * HD);
+        }
         issued = j + 1;
       }
       mbar_wait(&sm.q_full, 0, err, kErrWaitFull);
@@ -128,7 +145,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     }
   } else if (warp == 1) {
     const uint32_t id_qk = make_idesc(2, 1, 1, BQ, BKV);  // s8 x s8 -> s32
-    const uint32_t id_pv = make_idesc(1, 0, 0, BQ, HD);   // e4m3 x e4m3 -> f32
+    // e4m3 x e4m3 -> f32; per-token V: B (the V rows, keys x channels) MN-major
+    const uint32_t id_pv = make_idesc(1, 0, 0, BQ, HD) | (kTokenV ? 1u << 16 : 0u);
     const uint32_t q0 = smem_u32(sm.q), p0 = smem_u32(sm.p);
     bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.q_full, 0, err, kErrWaitFull)) &&
               __all_sync(0xFFFFFFFFu, mbar_wait(&sm.kv_full[0], 0, err, kErrWaitFull));
@@ -166,7 +184,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         const uint32_t v0 = smem_u32(sm.v[j & 1]);
 #pragma unroll
         for (int kk = 0; kk < BKV / 32; ++kk)
-          mma_f8(t_o, smem_desc_k128(p0 + kk * 32), smem_desc_k128(v0 + kk * 32), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_f8(t_o, smem_desc_k128(p0 + kk * 32),
+                 kTokenV ? smem_desc_mn128(v0 + kk * 4096) : smem_desc_k128(v0 + kk * 32), id_pv,
+                 (j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&sm.o_done);
         tc_commit(&sm.kv_empty[j & 1]);
       }
@@ -181,6 +201,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const float qs = a.q_scale[static_cast<int64_t>(h) * (npad / 32) * 8 + (t / 32) * 8 + (t % 8)];
     const float c = qs * a.sm_scale_log2;
+    // per-token V: p' = 2^(s - m) 448 / vmax (P's scale and the head's largest key scale in the exponent)
+    const float log2_vmax = kTokenV ? log2f(__ldg(a.v_head_max + h)) : 0.f;
     // this half's key-scale groups of a tile: columns 64 half .. + 63 hold groups 4 half .. + 3
     const float* ks_head = a.k_scale + static_cast<int64_t>(h) * (Lpad / 64) * 4 + half * 4;
     float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum (of 448 p)
@@ -198,6 +220,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         for (int i = 0; i < 4; ++i) ks_next[i] = __ldg(ks_head + (j + 1) * 8 + i);
       }
       ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.s_full, j & 1, err, kErrWaitAccFull));
+      // per-token V: the tile's key scales landed with its K and V (already complete here: S was computed from
+      // that K); the wait makes the bulk copy's writes visible to this warp. The stage cannot move on to tile
+      // j + 2 before this tile's P is published, so the phase waited for is this tile's.
+      if (kTokenV && ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.kv_full[j & 1], (j >> 1) & 1, err, kErrWaitFull));
       if (!ok) break;
       tc_fence_after();
       uint32_t s[2][32];
@@ -235,7 +261,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         const float m_new = fmaxf(m, fmaxf(mx, sm.row_max[j & 1][half ^ 1][row]));
         alpha = ex2(m - m_new);
         m = m_new;
-        const float base = kLog2PScale - m_new;
+        const float base = kLog2PScale - m_new - log2_vmax;
 #pragma unroll
         for (int col = 0; col < 64; col += 4) {
           float p[4];
@@ -247,6 +273,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
             if (kMasked && c2 >= lim) p[e] = 0.f;
           }
           sum += (p[0] + p[1]) + (p[2] + p[3]);
+          if constexpr (kTokenV) {  // the keys' scales, folded into P before its E4M3 rounding
+            const float4 v4 = *reinterpret_cast<const float4*>(&sm.vsc[j & 1][half * 64 + col]);
+            p[0] *= v4.x, p[1] *= v4.y, p[2] *= v4.z, p[3] *= v4.w;
+          }
           const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(p[0], p[1]), __NV_SATFINITE, __NV_E4M3);
           const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(p[2], p[3]), __NV_SATFINITE, __NV_E4M3);
           pk[col / 4] = lo | (hi << 16);
@@ -293,7 +323,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     l += sm.row_sum[half ^ 1][row];
     if (ok) {
       tc_fence_after();
-      const float inv = 1.f / l;  // l sums 448 p
+      const float inv = 1.f / l;  // l sums 448 p (per-token V: 448 p / vmax)
       const float* vsc = a.v_scale + h * HD;
       __nv_bfloat16* out = a.out + static_cast<int64_t>(t) * a.ld_out + h * HD;
 #pragma unroll
@@ -309,8 +339,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int d = d0 + i + 2 * e;
-              const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o[i + 2 * e]) * __ldg(vsc + d) * inv,
-                                                              __uint_as_float(o[i + 2 * e + 1]) * __ldg(vsc + d + 1) * inv);
+              const float s0 = kTokenV ? inv : __ldg(vsc + d) * inv, s1 = kTokenV ? inv : __ldg(vsc + d + 1) * inv;
+              const __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(o[i + 2 * e]) * s0,
+                                                              __uint_as_float(o[i + 2 * e + 1]) * s1);
               wv[e] = *reinterpret_cast<const uint32_t*>(&b2);
             }
             *reinterpret_cast<uint4*>(out + d0 + i) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
@@ -339,18 +370,29 @@ static bool map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t 
 
 int attn_launch(const AttnArgs& a, uint32_t* err, cudaStream_t s, const char** why) {
   const int npad = (a.nq + BQ - 1) / BQ * BQ, Lpad = (a.L + BKV - 1) / BKV * BKV;
-  CUtensorMap mq, mk, mv;
-  if (!map_2d(&mq, a.q_i8, HD, static_cast<uint64_t>(a.H) * npad, HD) ||
-      !map_2d(&mk, a.k_i8, HD, static_cast<uint64_t>(a.H) * Lpad, HD) ||
-      !map_2d(&mv, a.v_f8, Lpad, static_cast<uint64_t>(a.H) * HD, Lpad)) {
+  CUtensorMap mq, mk, mv, mv1;
+  bool ok = map_2d(&mq, a.q_i8, HD, static_cast<uint64_t>(a.H) * npad, HD) &&
+            map_2d(&mk, a.k_i8, HD, static_cast<uint64_t>(a.H) * Lpad, HD);
+  if (a.token_v) {
+    // keys [0, rows0): the cache rows (rows past rows0 read as zero); [rows0, L): the scratch rows
+    const uint64_t row1 = static_cast<uint64_t>(a.H) * HD;
+    if (a.rows0 > 0) ok = ok && map_2d(&mv, a.v_rows0, a.ld_v0, a.rows0, a.ld_v0);
+    if (a.rows0 < a.L) ok = ok && map_2d(&mv1, a.v_rows1, row1, a.L - a.rows0, row1);
+    if (a.rows0 <= 0) mv = mv1;
+    if (a.rows0 >= a.L) mv1 = mv;
+  } else {
+    ok = ok && map_2d(&mv, a.v_f8, Lpad, static_cast<uint64_t>(a.H) * HD, Lpad);
+    mv1 = mv;
+  }
+  if (!ok) {
     *why = "cuTensorMapEncodeTiled rejected an attention operand";
     return 2;
   }
-  auto kernel = attn_kernel<kAttnPolyShare>;
+  auto kernel = a.token_v ? attn_kernel<kAttnPolyShare, true> : attn_kernel<kAttnPolyShare, false>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(kAttnSmemBytes));
   if (e == cudaSuccess) {
-    kernel<<<dim3(npad / BQ, a.H), kAttnThreads, kAttnSmemBytes, s>>>(mq, mk, mv, a, err);
+    kernel<<<dim3(npad / BQ, a.H), kAttnThreads, kAttnSmemBytes, s>>>(mq, mk, mv, mv1, a, err);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {

@@ -281,7 +281,7 @@ class WanBlockB200:
         if forcing is None:
             _native.check(lib.wdl_sage_attend(
                 buf.q.data_ptr(), dim, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(), at,
-                buf.k.data_ptr(), _native.F32, dim, buf.qkv.data_ptr() + 2 * dim * 2, _native.BF16, 3 * dim, n, H,
+                buf.k.data_ptr(), _native.F32, dim, None, _native.BF16, 3 * dim, n, H,  # V: in the cache (qkv_prep)
                 attention_scale(at + n, entropy_ratio), buf.attn.data_ptr(), dim, buf.sage.data_ptr(), buf.sage.numel(),
                 st))
         else:

@@ -275,7 +275,7 @@ class WanBlockTP:
         if forcing is None:
             _native.check(lib.wdl_sage_attend(
                 buf.q.data_ptr(), d, n, ck.data_ptr(), cks.data_ptr(), cv.data_ptr(), cvs.data_ptr(), at,
-                buf.k.data_ptr(), _native.F32, d, buf.qkv.data_ptr() + 2 * d * 2, _native.BF16, 3 * d, n, H,
+                buf.k.data_ptr(), _native.F32, d, None, _native.BF16, 3 * d, n, H,  # V: in the cache (qkv_prep)
                 attention_scale(at + n, entropy_ratio), buf.attn.data_ptr(), d, buf.sage.data_ptr(), buf.sage.numel(),
                 st))
         else:
