@@ -5,7 +5,9 @@ Reference: src/wan_dit_lab/models/block.py:22-29 (WanBlock.forward), models/mult
 quantization/w4a4.py:248-262 (FusedQKVAttention), :195-204 (gelu_mlp: GELU + 0.171875, unsigned INT4 hidden),
 generation/causal.py:177-220 (KVCache.store / attend with Sage), models/rope.py, models/rms_norm.py,
 models/layer_norm.py. Every linear follows oracle.w4a4.linear on the packed weights given; attention is Sage's
-quantization with P V in FP8 tile by tile (oracle.sage.sage_attention, fp8_p); statistics in float64.
+quantization with P V in FP8 tile by tile (oracle.sage.sage_attention, fp8_p); statistics in float64. With
+token_v the self-attention's P V runs over the cache's per-token V as this build computes it (oracle.sage,
+token_v: V as the cache holds it, each key's scale folded into P) instead of the reference's per-channel V.
 """
 
 import numpy as np
@@ -56,7 +58,8 @@ def whole_blocks(rows, n, block=32):
     return rows
 
 
-def block(X, mod, parts, norms, cache, at, freq, grid, start, text, heads, trace=None, rows=None, x_is_bf16=False):
+def block(X, mod, parts, norms, cache, at, freq, grid, start, text, heads, trace=None, rows=None, x_is_bf16=False,
+          token_v=False):
     """X [n, dim] float32 (updated copy returned), mod [6, dim] float32 (time_in + modulation), parts {layer: packed
     numpy parts}, norms dict(norm_q, norm_k, cross_norm_q, cross_norm_k, norm3_w, norm3_b), cache: dict(k, ks, v, vs)
     numpy FP8 buffers [cap, H, 128] / [cap, H, 1] (written in place at `at`), text [T, dim] bf16 values (the
@@ -87,7 +90,8 @@ def block(X, mod, parts, norms, cache, at, freq, grid, start, text, heads, trace
         rows = whole_blocks(rows, n)
         X = X[rows]
     m = X.shape[0]
-    A = osage.sage_attention(Q, cache["k"], cache["ks"], cache["v"], cache["vs"], at, K, V, fp8_p=True, rows=rows)
+    A = osage.sage_attention(Q, cache["k"], cache["ks"], cache["v"], cache["vs"], at, K, V, fp8_p=True, rows=rows,
+                             token_v=token_v)
     keep("attn", A.reshape(m, dim))
     o = bf16(linear(bf16(A.reshape(m, dim)), parts["self_attn.o"]))
     X = (X + o * g_a).astype(np.float32)

@@ -7,8 +7,11 @@ chunk of 3 frames of 22 x 40 over a full window of 15840 cached keys, attention 
 The north star's tolerances, each stage checked on the GPU's own input to that stage, so that the number is the
 stage's own error and not what it inherited:
 - every linear (qkv, o, cross q / k / v, cross o, the fused MLP): bf16 relative L2 <= 1e-2 (LINEAR_BAR);
-- self- and cross-attention: cosine >= 0.999 (COS_BAR) against the oracle's Sage arithmetic on the same operands
-  and against exact softmax attention;
+- self-attention: cosine >= 0.999 (COS_BAR) against exact softmax attention over the cache's values, no less
+  accurate than the reference's own Sage arithmetic (V re-quantized per channel) measured against the same exact
+  result (within 10 %), and within 5e-3 relative L2 of the oracle's emulation of its own P V over the cache's
+  per-token V; cross-attention: cosine >= 0.999 against the oracle's Sage arithmetic on the same operands and
+  against exact softmax attention;
 - 3D RoPE of q and k: max abs error <= 1e-3 (ROPE_BAR); the RMSNorm before it equal in bf16 but for values on
   the other side of a rounding boundary.
 The whole chain, the oracle run independently from the same input, on the block's residual update: BLOCK_BAR,
@@ -96,7 +99,7 @@ def run(request):
     ot = {}
     ocache = dict(k=ck8.copy(), ks=cks.copy(), v=cv8.copy(), vs=cvs.copy())
     out_rows = ob.block(X.numpy(), mod.cpu().numpy(), parts, norms, ocache, AT, freq, GRID, start, ctx.float().numpy(),
-                        HEADS, trace=ot, rows=ROWS)
+                        HEADS, trace=ot, rows=ROWS, token_v=True)
     gpu = {k: v.float().cpu().numpy() for k, v in gt.items()}
     gpu["out"] = Xd.cpu().numpy()
     return dict(gpu=gpu, oracle=ot, out_rows=out_rows, X=X.numpy(), mod=mod.cpu().numpy(), parts=parts, norms=norms,
@@ -176,10 +179,11 @@ def test_self_attention(run):
     emulated = osage.sage_attention(Q, ck8, cks, cv8, cvs, AT, K, V, fp8_p=True, rows=ROWS,
                                     token_v=True).reshape(len(ROWS), DIM)
     exact = osage.attention(Q[:, ROWS], osage.load(ck8, cks, K, AT), osage.load(cv8, cvs, V, AT)).reshape(len(ROWS), DIM)
-    c_ref, c_exact = cosine(got, reference), cosine(got, exact)
-    print(f"self-attention: cosine {c_ref:.6f} vs the reference's Sage arithmetic, {c_exact:.6f} vs exact; "
-          f"relative L2 {rel(got, emulated):.2e} vs its own P V emulated")
-    assert c_ref >= COS_BAR and c_exact >= COS_BAR
+    c_exact = cosine(got, exact)
+    print(f"self-attention: cosine {c_exact:.6f} vs exact; relative L2 vs exact {rel(got, exact):.4f} (the "
+          f"reference's Sage arithmetic {rel(reference, exact):.4f}); {rel(got, emulated):.2e} vs its own P V emulated")
+    assert c_exact >= COS_BAR
+    assert rel(got, exact) <= 1.1 * rel(reference, exact)  # no less accurate than the reference's arithmetic
     assert rel(got, emulated) < 5e-3  # the kernel's FP8 P V against its emulation
 
 

@@ -7,9 +7,9 @@ The GPU rollout runs eagerly through Stream.next_chunk; every layer of every pas
 leaving it, its modulation, the cache fill and the RoPE table, and the caches are copied after every chunk.
 Checked against the oracle:
 - every layer of the first denoising pass and of the write pass of every chunk, each on its own input and on the
-  cache as it stood before the pass: the oracle block (oracle/block.py, the query rows of the full-size test)
-  updates the stream within the block bar of the full-size test (tests/test_block_full_gpu.py:
-  sqrt(2 (1 - 0.999)) + 1e-2);
+  cache as it stood before the pass: the oracle block (oracle/block.py, the query rows of the full-size test,
+  P V over the cache's per-token V as the kernel computes it) updates the stream within the block bar of the
+  full-size test (tests/test_block_full_gpu.py: sqrt(2 (1 - 0.999)) + 1e-2);
 - the cache's growth and eviction, exactly: the reference's commit (generation/causal.py:298-337, KVCache.commit,
   restated in OracleCache), fed each chunk's keys and values as the write pass stored them, gives the GPU's cache
   byte for byte after every commit, through the fills and the eviction of the ring's oldest chunk.
@@ -126,7 +126,7 @@ def test_rollout_matches_the_oracle_over_a_growing_and_evicting_cache():
     def oracle_block(rec, layer, X, cache, rows):
         return ob.block(X, rec["mods"][layer].cpu().numpy(), parts[layer], norms[layer], cache, rec["at"],
                         rec["freq"].cpu().numpy(), rec["grid"], rec["start"], ctx, HEADS, rows=rows,
-                        x_is_bf16=layer == 0)
+                        x_is_bf16=layer == 0, token_v=True)
 
     report, isolated = [], []
     for chunk in range(CHUNKS):

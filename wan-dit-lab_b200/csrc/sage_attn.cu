@@ -59,7 +59,7 @@ constexpr size_t kAttnSmemBytes = sizeof(AttnSmem) + 1024;
 // The int32 Q K^T sum as a float, exactly, without the conversion unit: |S| <= 128 * 127 * 127 < 2^22, so
 // S + 1.5 * 2^23 is an integer in [2^23, 2^24) whose float bits are those of 0x4B400000 + S; subtracting
 // 1.5 * 2^23 again is exact. An integer add and a float add instead of one conversion on the special function
-// pipe, which the softmax's exponentials already keep busy.
+// pipe, which the softmax's exponentials already keep busy (the exponent arguments skip the float add, see c').
 __device__ __forceinline__ float exact_float(uint32_t s) {
   return __fsub_rn(__uint_as_float(s + 0x4B400000u), 12582912.0f);
 }
@@ -226,13 +226,12 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       if (kTokenV && ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.kv_full[j & 1], (j >> 1) & 1, err, kErrWaitFull));
       if (!ok) break;
       tc_fence_after();
-      uint32_t s[2][32];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) tmem_ld32(t_s + lane_off + half * 64 + q * 32, s[q]);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.s_empty);
+      // This half's 64 scores are read from TMEM twice: both 32-column parts for the row maximum, then the
+      // second part again once the first part's exponentials are done, so that 32 scores are held in registers,
+      // not 64 (the register pressure, not the instruction count, bounds how many exponentials are in flight).
+      // S is released to the next Q K^T after the second read, halfway through this tile's softmax: ample time
+      // for that MMA to finish before the next tile's softmax starts.
+      const uint32_t t_row = t_s + lane_off + half * 64;
       // Row max per scale group over the integer scores: w > 0 and rounding is monotonic, so max(S) * w rounds
       // to max(S * w) (the same m as scaling every score first); the two halves' maxima meet in shared memory.
       // Then one FMA per score gives the exponent argument S * w + log2(448) - m, so that 2^arg = 448 p
@@ -242,16 +241,22 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       uint32_t pk[16];
       auto tile = [&](auto masked) {
         constexpr bool kMasked = decltype(masked)::value;
+        uint32_t s[32];
         int32_t gmax[4];
 #pragma unroll
         for (int g = 0; g < 4; ++g) gmax[g] = INT32_MIN;
-#pragma unroll
-        for (int q = 0; q < 2; ++q)
+        {
+          uint32_t s_hi[32];
+          tmem_ld32(t_row, s);
+          tmem_ld32(t_row + 32, s_hi);
+          tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const int col = q * 32 + i, g = (col % 8) / 2;
-            if (!kMasked || col < lim) gmax[g] = max(gmax[g], static_cast<int32_t>(s[q][i]));
+            const int g = (i % 8) / 2;
+            if (!kMasked || i < lim) gmax[g] = max(gmax[g], static_cast<int32_t>(s[i]));
+            if (!kMasked || 32 + i < lim) gmax[g] = max(gmax[g], static_cast<int32_t>(s_hi[i]));
           }
+        }
         float mx = -INFINITY;
 #pragma unroll
         for (int g = 0; g < 4; ++g)
@@ -262,24 +267,45 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         alpha = ex2(m - m_new);
         m = m_new;
         const float base = kLog2PScale - m_new - log2_vmax;
+        // c' = base - 1.5 * 2^23 w (one rounding: 4e-6 of a log2 unit at most), so that fma(x, w, c') with x the
+        // integer score plus 1.5 * 2^23 read as a float (exactly 1.5 * 2^23 + S, as |S| < 2^22) is S w + base:
+        // an integer add and one FMA per exponent argument
+        float cg[4];
 #pragma unroll
-        for (int col = 0; col < 64; col += 4) {
-          float p[4];
+        for (int g = 0; g < 4; ++g) cg[g] = fmaf(-12582912.f, w[g], base);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c2 = col + e, g = (c2 % 8) / 2;
-            const float arg = fmaf(exact_float(s[c2 / 32][c2 % 32]), w[g], base);
-            p[e] = e >= 4 - kPoly ? exp2_fma(arg) : ex2(arg);
-            if (kMasked && c2 >= lim) p[e] = 0.f;
+        for (int part = 0; part < 2; ++part) {
+          if (part == 1) {  // the second 32 scores, read again; then S is free for the next tile's Q K^T
+            tmem_ld32(t_row + 32, s);
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.s_empty);
           }
-          sum += (p[0] + p[1]) + (p[2] + p[3]);
-          if constexpr (kTokenV) {  // the keys' scales, folded into P before its E4M3 rounding
-            const float4 v4 = *reinterpret_cast<const float4*>(&sm.vsc[j & 1][half * 64 + col]);
-            p[0] *= v4.x, p[1] *= v4.y, p[2] *= v4.z, p[3] *= v4.w;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const int col = part * 32 + i;
+            float p[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int g = ((i + e) % 8) / 2;
+              const float arg = fmaf(__uint_as_float(s[i + e] + 0x4B400000u), w[g], cg[g]);
+              p[e] = e >= 4 - kPoly ? exp2_fma(arg) : ex2(arg);
+              if (kMasked && col + e >= lim) p[e] = 0.f;
+            }
+            sum += (p[0] + p[1]) + (p[2] + p[3]);
+            if constexpr (kTokenV) {  // the keys' scales, folded into P before its E4M3 rounding
+              // read where it is used: a plain load would be hoisted, sixteen float4 held across the loop
+              float4 v4;
+              asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                           : "=f"(v4.x), "=f"(v4.y), "=f"(v4.z), "=f"(v4.w)
+                           : "r"(smem_u32(&sm.vsc[j & 1][half * 64 + col])));
+              p[0] *= v4.x, p[1] *= v4.y, p[2] *= v4.z, p[3] *= v4.w;
+            }
+            const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(p[0], p[1]), __NV_SATFINITE, __NV_E4M3);
+            const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(p[2], p[3]), __NV_SATFINITE, __NV_E4M3);
+            pk[col / 4] = lo | (hi << 16);
           }
-          const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(p[0], p[1]), __NV_SATFINITE, __NV_E4M3);
-          const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(p[2], p[3]), __NV_SATFINITE, __NV_E4M3);
-          pk[col / 4] = lo | (hi << 16);
         }
       };
       const float m_old = m;
@@ -292,24 +318,25 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         ok = __all_sync(0xFFFFFFFFu, mbar_wait(&sm.o_done, (j - 1) & 1, err, kErrWaitAccFull));
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xFFFFFFFFu, m > m_old)) {  // this half of O's columns, rescaled to the new maximum
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            uint32_t o[32];
-            tmem_ld32(t_o + lane_off + half * 64 + q * 32, o);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(t_o + lane_off + half * 64 + q * 32, o);
-          }
-          tmem_st_wait();
-        }
       }
+      // P into shared memory first (its registers free), then O rescaled: both before P V of this tile is issued
 #pragma unroll
       for (int chunk = 0; chunk < 4; ++chunk) {
         const int c16 = half * 4 + chunk;  // this half's 16-byte chunks of the row
         *reinterpret_cast<uint4*>(prow + ((c16 ^ (row & 7)) << 4)) =
             make_uint4(pk[chunk * 4], pk[chunk * 4 + 1], pk[chunk * 4 + 2], pk[chunk * 4 + 3]);
+      }
+      if (j > 0 && __any_sync(0xFFFFFFFFu, m > m_old)) {  // this half of O's columns, rescaled to the new maximum
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          uint32_t o[32];
+          tmem_ld32(t_o + lane_off + half * 64 + q * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_o + lane_off + half * 64 + q * 32, o);
+        }
+        tmem_st_wait();
       }
       fence_proxy_async_smem();
       tc_fence_before();
