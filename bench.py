@@ -411,7 +411,11 @@ def reference_arm(args, rank, world):
         return
     times = []
     if args.workload == "rollout":
-        ref = ReferenceBlockPass()
+        try:
+            ref = ReferenceBlockPass()
+        except (RuntimeError, ImportError) as error:  # the reference package is not installed here
+            print(json.dumps({"impl": "reference", "unavailable": str(error).splitlines()[0]}), flush=True)
+            return
         for _ in range(args.warmup):
             ref()
         times = [ref() for _ in range(args.steps)]
@@ -540,11 +544,14 @@ def main():
         unit, metric = "TOPS", METRIC_LINEAR
 
     cpu = None
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:  # the host baseline is taken at N = 1 only
         if rollout:
-            per_rollout, frames, sample = wl["cpu"]()
-            cpu = {"value": frames / per_rollout, "unit": unit, "cores": torch.get_num_threads(), "kind": "reference",
-                   "sample": sample}
+            try:
+                per_rollout, frames, sample = wl["cpu"]()
+                cpu = {"value": frames / per_rollout, "unit": unit, "cores": torch.get_num_threads(),
+                       "kind": "reference", "sample": sample}
+            except (RuntimeError, ImportError) as error:  # the reference package is not installed here
+                print(f"cpu baseline unavailable: {error}", file=sys.stderr, flush=True)
         else:
             dt, cpu_ops, sample = wl["cpu"]()
             cpu = {"value": cpu_ops / dt / 1e12, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "reference",
