@@ -151,6 +151,32 @@ int wdl_w4a4_gemm_gelu_u4_add(const void* a, const float* a_scales, const void* 
                               uint8_t* codes, int64_t ldc, float* scales, float* gelu_out, int64_t ld_gelu,
                               void* stream);
 
+/* An SVDQuant low-rank branch formed inside the GEMM epilogue (Nunchaku adds lora_act proj_up^T in its GEMM,
+ * native/ops/w4a4_ops.cpp:31-40): act [M, ld_act] f32 = x proj_down (the layer's input times its down-projection,
+ * computed by the caller), up [N, rank] f32 = proj_up, rank a multiple of 4 (<= 1024); every epilogue thread adds
+ * act[m, :] . up[n, :] to its products before the bias, so the [M, N] product is never written to memory. act and
+ * up 16-byte aligned, ld_act a multiple of 4. */
+typedef struct wdl_lowrank {
+  const float* act;
+  int64_t ld_act;
+  const float* up;
+  int rank;
+} wdl_lowrank;
+
+/* The _add entry points above with the branch given as a wdl_lowrank (null: none) instead of its addend. */
+int wdl_w4a4_gemm_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                          const float* bias, const wdl_lowrank* lowrank, int M, int N, int K, uint16_t* y,
+                          int64_t ldy, void* stream);
+int wdl_w4a4_gemm_residual_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                                   int code_format, const float* bias, const wdl_lowrank* lowrank, const float* gate,
+                                   const float* residual, int64_t ldr, int M, int N, int K, float* out, int64_t ldo,
+                                   void* stream);
+int wdl_w4a4_gemm_gelu_u4_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                                  int code_format, const float* bias, const wdl_lowrank* lowrank,
+                                  const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N, int K,
+                                  uint8_t* codes, int64_t ldc, float* scales, float* gelu_out, int64_t ld_gelu,
+                                  void* stream);
+
 /* out [M, ldo] f32 = the GEMM's product (+ addend, + bias when given), not rounded: a tensor-parallel shard's
  * share of a row-parallel layer (its slice of the K input channels), summed across shards (NCCL all-reduce) before
  * wdl_residual_update applies bias, bf16 rounding, gate and residual. Groups of 64 never straddle shards, so each
@@ -160,6 +186,9 @@ int wdl_w4a4_gemm_gelu_u4_add(const void* a, const float* a_scales, const void* 
 int wdl_w4a4_gemm_f32(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                       const float* bias, const float* addend, int64_t ld_add, int M, int N, int K, float* out,
                       int64_t ldo, void* stream);
+int wdl_w4a4_gemm_f32_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                              int code_format, const float* bias, const wdl_lowrank* lowrank, int M, int N, int K,
+                              float* out, int64_t ldo, void* stream);
 
 /* Bytes of scratch wdl_w4a4_linear needs for M tokens of K channels (any code format). */
 size_t wdl_w4a4_linear_workspace(int M, int K);

@@ -35,6 +35,17 @@ int main(void) {
       wdl_w4a4_linear(FAKE, 256, 128, 256, NULL, WDL_BF16, FAKE, FAKE, WDL_CODES_E4M3, NULL, 256, FAKE, 256, FAKE,
                       wdl_w4a4_linear_workspace(128, 256) - 1, NULL),
       "workspace", "linear workspace");
+  /* a low-rank branch formed in the GEMM epilogue takes its rank in fours and a non-null activation */
+  wdl_lowrank lr = {FAKE, 8, FAKE, 6};
+  failures += expect_argument_error(
+      wdl_w4a4_gemm_lowrank(FAKE, FAKE, FAKE, FAKE, WDL_CODES_E4M3, NULL, &lr, 128, 256, 256, FAKE, 256, NULL),
+      "multiple of 4", "low-rank rank");
+  lr.rank = 8;
+  lr.act = NULL;
+  failures += expect_argument_error(
+      wdl_w4a4_gemm_residual_lowrank(FAKE, FAKE, FAKE, FAKE, WDL_CODES_E4M3, NULL, &lr, NULL, FAKE, 256, 128, 256, 256,
+                                     FAKE, 256, NULL),
+      "must not be null", "low-rank null act");
   if (wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, WDL_CODES_E4M3, NULL, 0, 256, 256, FAKE, 256, NULL) != WDL_OK) failures++;
   printf("%s\n", failures ? "FAILED" : "PASSED");
   return failures ? 1 : 0;

@@ -140,6 +140,18 @@ def test_new_entry_points_validate_before_any_launch(native):
     assert st == native.ERR_ARGUMENT and b"addend" in err()
     st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, 128, 200, 256, FAKE, 256, None)
     assert st == native.ERR_ARGUMENT and b"multiple of 128" in err()
+    for rank, ld, act in ((6, 8, FAKE), (0, 8, FAKE), (8, 6, FAKE), (8, 8, None), (8, 8, FAKE + 4)):
+        lr = native.LowRank(act, ld, FAKE, rank)  # rank in fours, rows that hold it, 16-byte aligned, not null
+        st = lib.wdl_w4a4_gemm_lowrank(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, lr, 128, 256, 256, FAKE,
+                                       256, None)
+        assert st == native.ERR_ARGUMENT and b"low-rank" in err(), (rank, ld, act)
+    lr = native.LowRank(FAKE, 8, FAKE, 6)
+    for call in (lambda: lib.wdl_w4a4_gemm_f32_lowrank(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, lr, 128,
+                                                       256, 256, FAKE, 256, None),
+                 lambda: lib.wdl_w4a4_gemm_gelu_u4_lowrank(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, lr,
+                                                           None, 0.171875, native.BF16, 128, 256, 256, FAKE, 256, FAKE,
+                                                           None, 0, None)):
+        assert call() == native.ERR_ARGUMENT and b"multiple of 4" in err()
     assert lib.wdl_rows_sumsq(FAKE, 256, 4, 0, 1, 0, FAKE, None) == native.ERR_ARGUMENT
     st = lib.wdl_residual_update(FAKE, 8, None, None, FAKE, 8, 4, 6, None)
     assert st == native.ERR_ARGUMENT and b"multiple of 4" in err()

@@ -67,8 +67,13 @@ def test_sage_operator_equals_the_kernel_on_its_own_layouts(at, n, H):
     K = (torch.randn(1, n, H, 128, generator=g) + 0.5).cuda()
     V = torch.randn(1, n, H, 128, generator=g).to(torch.bfloat16).cuda()
     Q = torch.randn(1, n, H, 128, generator=g).cuda()
-    want = sage_kv.attend(Q, ck, cks, cv, cvs, at, K, V)
     prepared = sage_kv.prepare(Q, ck, cks, cv, cvs, at, K, V)
+    # the kernel on the prepared per-channel operands in this library's layouts (wdl_sage_attention)
+    want = torch.empty(1, n, H, 128, dtype=torch.bfloat16, device="cuda")
+    lib = _native.lib()
+    _native.check(lib.wdl_sage_attention(*(prepared[x].data_ptr() for x in ("q_i8", "q_scale", "k_i8", "k_scale",
+                                                                            "v_f8", "v_scale")),
+                                         n, at + n, H, 128 ** -0.5, want.data_ptr(), H * 128, _native.stream()))
     args = to_sage_layouts(prepared, n, at + n)
     got = operators.load().sage_sm89(*args, 128 ** -0.5)
     torch.cuda.synchronize()

@@ -1,7 +1,9 @@
 """The SVDQuant low-rank branch and gelu_mlp on the B200 kernels against the CPU oracle (oracle/w4a4.py).
 
 A layer of rank r computes y = INT4 GEMM(x / s) + (x proj_down) proj_up^T + b (reference w4a4.py:141-180,
-native/ops/w4a4_ops.cpp:32-38); the branch's [M, N] product enters the GEMM's epilogue (wdl_w4a4_gemm_add).
+native/ops/w4a4_ops.cpp:32-38); the down-projection is a thin float32 product and the up-projection is formed in the
+GEMM's epilogue (wdl_lowrank: every epilogue thread adds act[m, :] . up[n, :] before the bias), which must equal the
+same branch passed as its float32 [M, N] addend (wdl_w4a4_gemm_add) within float32 rounding.
 gelu_mlp (w4a4_ops.cpp:44-63) keeps GELU's output for the second layer's branch, which reads it without the shift.
 Outputs are bfloat16: relative L2 <= 2e-3 against the float32 oracle (the INT4 codes of the hidden layer may
 differ by one where GELU's output lands on a rounding boundary), and a rank-32 layer must be closer to the
@@ -45,7 +47,7 @@ def oracle_layer(parts):
                 down=f(parts["proj_down"]), up=f(parts["proj_up"]), bias=f(parts["bias"]), smooth=f(parts["smooth"]))
 
 
-@pytest.mark.parametrize("fmt", ["f16fold", "e4m3", "int8"])
+@pytest.mark.parametrize("fmt", ["f16pre", "f16fold", "e4m3", "int8"])
 @pytest.mark.parametrize("M,N,K", [(300, 768, 1024), (37, 256, 512)])
 def test_lowrank_linear_against_oracle(M, N, K, fmt):
     from wan_dit_lab_b200.quantization import w4a4
@@ -142,3 +144,54 @@ def test_gemm_add_rejects_misaligned_addend():
     assert st == 0
     torch.cuda.synchronize()
     assert float(y.float().abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("fmt", ["f16pre", "f16fold", "e4m3", "int8"])
+@pytest.mark.parametrize("rank", [6, 32])
+def test_epilogue_branch_equals_its_addend(fmt, rank):
+    """The branch formed in the GEMM epilogue against the same branch passed as a float32 [M, N] addend, in each
+    output mode: the float32 product (wdl_w4a4_gemm_f32*) within float32 rounding of the sum (the epilogue adds
+    one rank after the other onto the product, the addend is added once), bf16 outputs and the gated residual
+    update at most one bf16 step apart where the two sums straddle a rounding boundary. Rank 6 runs padded to 8
+    with zero columns."""
+    from wan_dit_lab_b200.quantization import w4a4
+    _native = native()
+    lib, st = _native.lib(), _native.stream()
+    M, N, K = 300, 768, 1024
+    x = seeded((M, K), 50).to(torch.bfloat16).cuda()
+    parts = w4a4.quantize(structured_weight(N, K, 51).cuda(), seeded((N,), 52, 0.1).cuda(),
+                          smooth=(seeded((K,), 53).abs() + 0.5).cuda(), rank=rank)
+    layer = w4a4.PreparedW4A4(*(parts[p] for p in w4a4.PARTS), code_format=fmt)
+    assert layer.rank == rank and layer.up.shape[1] == -(-rank // 4) * 4
+    act = layer.lowrank_act(x)
+    add = (act.double() @ layer.up.double().t()).float().contiguous()
+    work = torch.empty(lib.wdl_w4a4_linear_workspace(M, K), dtype=torch.uint8, device="cuda")
+    codes, scales = layer.quantize_input(x, work)
+    args = (codes.data_ptr(), scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), layer.code_format,
+            _native.ptr(layer.bias))
+    f_lr, f_add = (torch.empty(M, N, device="cuda") for _ in range(2))
+    _native.check(lib.wdl_w4a4_gemm_f32_lowrank(*args, layer.lowrank_arg(act), M, N, K, f_lr.data_ptr(), N, st))
+    _native.check(lib.wdl_w4a4_gemm_f32(*args, add.data_ptr(), N, M, N, K, f_add.data_ptr(), N, st))
+    b_lr, b_add = (torch.empty(M, N, dtype=torch.bfloat16, device="cuda") for _ in range(2))
+    _native.check(lib.wdl_w4a4_gemm_lowrank(*args, layer.lowrank_arg(act), M, N, K, b_lr.data_ptr(), N, st))
+    _native.check(lib.wdl_w4a4_gemm_add(*args, add.data_ptr(), N, M, N, K, b_add.data_ptr(), N, st))
+    residual = seeded((M, N), 54).cuda()
+    gate = (seeded((N,), 55, 0.5)).cuda()
+    r_lr, r_add = residual.clone(), residual.clone()
+    _native.check(lib.wdl_w4a4_gemm_residual_lowrank(*args, layer.lowrank_arg(act), gate.data_ptr(),
+                                                     r_lr.data_ptr(), N, M, N, K, r_lr.data_ptr(), N, st))
+    _native.check(lib.wdl_w4a4_gemm_residual_add(*args, add.data_ptr(), N, gate.data_ptr(), r_add.data_ptr(), N, M,
+                                                 N, K, r_add.data_ptr(), N, st))
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    branch = float(add.abs().max())
+    assert branch > 0.1 * float(f_add.abs().max())  # the branch carries a real share of the output
+    tol = 1e-5 * float(f_add.abs().max())  # the two float32 sums: a few ulps of the accumulator apart
+    assert float((f_lr - f_add).abs().max()) <= tol
+    # bf16 outputs: the sums' difference, plus one bf16 step where they straddle a rounding boundary
+    step = lambda a, b: torch.maximum(a.float().abs(), b.float().abs()) * 2.0 ** -7 + tol  # noqa: E731
+    assert bool(((b_lr.float() - b_add.float()).abs() <= step(b_lr, b_add)).all())
+    assert float((b_lr == b_add).float().mean()) > 0.99
+    # the update x + o gate: o as above times the gate, the float32 sum with x rounded once more (|x| < 8)
+    o_lr, o_add = r_lr - residual, r_add - residual
+    assert bool(((r_lr - r_add).abs() <= step(o_lr, o_add) + 2e-6).all())

@@ -221,6 +221,55 @@ static int set_addend(wdl::w4a4::GemmArgs& g, const float* addend, int64_t ld_ad
   return ok();
 }
 
+// The low-rank branch formed in the epilogue (wdl_lowrank), when given.
+static int set_lowrank(wdl::w4a4::GemmArgs& g, const wdl_lowrank* lr) {
+  if (!lr) return ok();
+  if (!lr->act || !lr->up) return fail(WDL_ERR_ARGUMENT, "low-rank act and up must not be null");
+  if (lr->rank <= 0 || lr->rank % 4 != 0 || lr->rank > 1024)
+    return fail(WDL_ERR_ARGUMENT, "low-rank rank must be a positive multiple of 4, at most 1024");
+  if (lr->ld_act < lr->rank || lr->ld_act % 4 != 0 || !aligned(lr->act, 16) || !aligned(lr->up, 16))
+    return fail(WDL_ERR_ARGUMENT, "low-rank act rows must hold rank floats, 16-byte aligned");
+  g.ep.lr_act = lr->act, g.ep.lr_ld = lr->ld_act, g.ep.lr_up = lr->up, g.ep.lr_rank = lr->rank;
+  return ok();
+}
+
+int wdl_w4a4_gemm_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                          const float* bias, const wdl_lowrank* lowrank, int M, int N, int K, uint16_t* y,
+                          int64_t ldy, void* stream) {
+  if (ldy < N || (ldy * 2) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldy must be >= N with 16-byte aligned rows");
+  wdl::w4a4::GemmArgs g{};
+  operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
+  if (set_lowrank(g, lowrank) != WDL_OK) return WDL_ERR_ARGUMENT;
+  g.ep.mode = wdl::w4a4::kEpiBf16, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = ldy;
+  return gemm_common(g, stream);
+}
+
+int wdl_w4a4_gemm_residual_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                                   int code_format, const float* bias, const wdl_lowrank* lowrank, const float* gate,
+                                   const float* residual, int64_t ldr, int M, int N, int K, float* out, int64_t ldo,
+                                   void* stream) {
+  if (!residual) return fail(WDL_ERR_ARGUMENT, "residual must not be null");
+  if (ldr < N || ldo < N || (ldr * 4) % 16 != 0 || (ldo * 4) % 16 != 0)
+    return fail(WDL_ERR_ARGUMENT, "ldr, ldo must be >= N with 16-byte aligned rows");
+  wdl::w4a4::GemmArgs g{};
+  operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
+  if (set_lowrank(g, lowrank) != WDL_OK) return WDL_ERR_ARGUMENT;
+  g.ep.mode = wdl::w4a4::kEpiResidualF32, g.ep.bias = bias, g.ep.gate = gate;
+  g.ep.residual = residual, g.ep.ld_res = ldr, g.ep.out = out, g.ep.ld_out = ldo;
+  return gemm_common(g, stream);
+}
+
+int wdl_w4a4_gemm_f32_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                              int code_format, const float* bias, const wdl_lowrank* lowrank, int M, int N, int K,
+                              float* out, int64_t ldo, void* stream) {
+  if (ldo < N || (ldo * 4) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldo must be >= N with 16-byte aligned rows");
+  wdl::w4a4::GemmArgs g{};
+  operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
+  if (set_lowrank(g, lowrank) != WDL_OK) return WDL_ERR_ARGUMENT;
+  g.ep.mode = wdl::w4a4::kEpiResidualF32, g.ep.bias = bias, g.ep.residual = nullptr, g.ep.out = out, g.ep.ld_out = ldo;
+  return gemm_common(g, stream);
+}
+
 int wdl_w4a4_gemm_add(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                       const float* bias, const float* addend, int64_t ld_add, int M, int N, int K, uint16_t* y,
                       int64_t ldy, void* stream) {
@@ -288,11 +337,35 @@ int wdl_w4a4_gemm_gelu_u4(const void* a, const float* a_scales, const void* w, c
                                    scale_dtype, M, N, K, codes, ldc, scales, nullptr, 0, stream);
 }
 
+static int gelu_u4_impl(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                        const float* bias, const float* addend, int64_t ld_add, const wdl_lowrank* lowrank,
+                        const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N, int K, uint8_t* codes,
+                        int64_t ldc, float* scales, float* gelu_out, int64_t ld_gelu, void* stream);
+
 int wdl_w4a4_gemm_gelu_u4_add(const void* a, const float* a_scales, const void* w, const float* w_scales,
                               int code_format, const float* bias, const float* addend, int64_t ld_add,
                               const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N, int K,
                               uint8_t* codes, int64_t ldc, float* scales, float* gelu_out, int64_t ld_gelu,
                               void* stream) {
+  return gelu_u4_impl(a, a_scales, w, w_scales, code_format, bias, addend, ld_add, nullptr, smooth_next, shift,
+                      scale_dtype, M, N, K, codes, ldc, scales, gelu_out, ld_gelu, stream);
+}
+
+int wdl_w4a4_gemm_gelu_u4_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales,
+                                  int code_format, const float* bias, const wdl_lowrank* lowrank,
+                                  const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N, int K,
+                                  uint8_t* codes, int64_t ldc, float* scales, float* gelu_out, int64_t ld_gelu,
+                                  void* stream) {
+  return gelu_u4_impl(a, a_scales, w, w_scales, code_format, bias, nullptr, 0, lowrank, smooth_next, shift,
+                      scale_dtype, M, N, K, codes, ldc, scales, gelu_out, ld_gelu, stream);
+}
+
+}  // extern "C"
+
+static int gelu_u4_impl(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
+                        const float* bias, const float* addend, int64_t ld_add, const wdl_lowrank* lowrank,
+                        const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N, int K, uint8_t* codes,
+                        int64_t ldc, float* scales, float* gelu_out, int64_t ld_gelu, void* stream) {
   if (gelu_out && (ld_gelu < N || !aligned(gelu_out, 4))) return fail(WDL_ERR_ARGUMENT, "gelu_out rows must hold N floats");
   if (code_format == WDL_CODES_INT8)
     return fail(WDL_ERR_ARGUMENT, "the unsigned hidden codes need an E4M3 or float16 code format");
@@ -302,7 +375,7 @@ int wdl_w4a4_gemm_gelu_u4_add(const void* a, const float* a_scales, const void* 
   if (!scales) return fail(WDL_ERR_ARGUMENT, "null scales");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
-  if (set_addend(g, addend, ld_add, N) != WDL_OK) return WDL_ERR_ARGUMENT;
+  if (set_addend(g, addend, ld_add, N) != WDL_OK || set_lowrank(g, lowrank) != WDL_OK) return WDL_ERR_ARGUMENT;
   g.ep.gelu_out = gelu_out, g.ep.ld_gelu = ld_gelu;
   g.ep.mode = wdl::w4a4::kEpiGeluU4, g.ep.bias = bias, g.ep.out = codes, g.ep.ld_out = ldc, g.ep.out_scales = scales;
   g.ep.out_smooth = reinterpret_cast<const __nv_bfloat16*>(smooth_next), g.ep.out_scale_dtype = scale_dtype;
@@ -310,7 +383,6 @@ int wdl_w4a4_gemm_gelu_u4_add(const void* a, const float* a_scales, const void* 
   return gemm_common(g, stream);
 }
 
-}  // extern "C"
 
 namespace wdl {
 // The bf16-output GEMM of a W4A4 linear over the quantized rows `codes` / `scales`, filled as every GEMM entry

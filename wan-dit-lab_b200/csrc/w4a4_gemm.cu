@@ -91,7 +91,7 @@ __device__ __forceinline__ void promote2(uint64_t& acc, uint32_t p0, uint32_t p1
   }
 }
 
-template <int kMode, bool kFp8, bool kPacked>
+template <int kMode, bool kFp8, bool kPacked, bool kLR>
 __global__ void __launch_bounds__(kThreads, 1)
     w4a4_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      const __grid_constant__ CUtensorMap map_ws, GemmEpilogue ep, int M, int N, int K,
@@ -272,6 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && row_ok) {
       const int n0 = n_tile * BN + h * 128;
       add_addend<128>(ep, m, n0, acc);
+      if constexpr (kLR) add_lowrank<128>(ep, m, n0, acc);  // its own instantiations (registers)
       if constexpr (kMode == kEpiBf16) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.out) + static_cast<size_t>(m) * ep.ld_out + n0;
 #pragma unroll
@@ -413,7 +414,9 @@ int gemm_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
   const bool packed = a.variant == 1;
   switch (a.ep.mode * 4 + (fp8 ? 2 : 0) + (packed ? 1 : 0)) {
 #define WDL_GEMM_CASE(MODE, FP8, PACKED) \
-  case MODE * 4 + (FP8 ? 2 : 0) + (PACKED ? 1 : 0): launch(w4a4_gemm_kernel<MODE, FP8, PACKED>); break;
+  case MODE * 4 + (FP8 ? 2 : 0) + (PACKED ? 1 : 0):                                                         \
+    a.ep.lr_act ? launch(w4a4_gemm_kernel<MODE, FP8, PACKED, true>) : launch(w4a4_gemm_kernel<MODE, FP8, PACKED, false>); \
+    break;
     WDL_GEMM_CASE(kEpiBf16, false, false)
     WDL_GEMM_CASE(kEpiBf16, false, true)
     WDL_GEMM_CASE(kEpiBf16, true, false)

@@ -54,6 +54,12 @@ struct GemmEpilogue {
   int64_t ld_add;
   float* gelu_out;  // kEpiGeluU4: [M, ld_gelu] f32 GELU(y) before shift and smoothing (the next low-rank input), nullable
   int64_t ld_gelu;
+  // The low-rank branch formed in the epilogue instead of an addend: y += lr_act[m, :] . lr_up[n, :] over lr_rank
+  // (a multiple of 4): lr_act [M, lr_ld] f32 = x proj_down, lr_up [N, lr_rank] f32 = proj_up. Nullable.
+  const float* lr_act;
+  int64_t lr_ld;
+  const float* lr_up;
+  int lr_rank;
 };
 
 #ifdef __CUDACC__
@@ -65,6 +71,28 @@ __device__ __forceinline__ void add_addend(const GemmEpilogue& ep, int m, int n0
   const float* p = ep.addend + static_cast<size_t>(m) * ep.ld_add + n0;
 #pragma unroll
   for (int j = 0; j < kCount; ++j) acc[j] += __ldg(p + j);
+}
+
+// Adds row m, columns [n0, n0 + kCount) of the low-rank branch's up-projection into acc (before the bias), when the
+// epilogue has one: acc[j] += sum_r lr_act[m, r] lr_up[n0 + j, r], four ranks at a time (one 16-byte load of the
+// row's activations, then per column one 16-byte load that every lane of the warp shares and four FMAs).
+template <int kCount>
+__device__ __forceinline__ void add_lowrank(const GemmEpilogue& ep, int m, int n0, float* acc) {
+  if (!ep.lr_act) return;
+  const float* act = ep.lr_act + static_cast<size_t>(m) * ep.lr_ld;
+  const float* up = ep.lr_up + static_cast<size_t>(n0) * ep.lr_rank;
+  for (int r = 0; r < ep.lr_rank; r += 4) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(act + r));
+#pragma unroll
+    for (int j = 0; j < kCount; ++j) {
+      // loaded where used: hoisted, the loads of all kCount columns would be held in registers at once
+      float4 u;
+      asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                   : "=f"(u.x), "=f"(u.y), "=f"(u.z), "=f"(u.w)
+                   : "l"(up + static_cast<size_t>(j) * ep.lr_rank + r));
+      acc[j] = fmaf(a.w, u.w, fmaf(a.z, u.z, fmaf(a.y, u.y, fmaf(a.x, u.x, acc[j]))));
+    }
+  }
 }
 #endif
 

@@ -56,9 +56,10 @@ constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // The end of a tile for one epilogue thread: row m_tile * BM + 32 q + lane of the 128 columns n_tile * BN + 128 h
-// .. + 127 in acc (the finished fp32 products): the low-rank addend, then the mode's epilogue. tw: this warp's
+// .. + 127 in acc (the finished fp32 products): the low-rank branch (an addend or its up-projection), then the
+// mode's epilogue. tw: this warp's
 // 32 x 33 floats of shared-memory scratch (residual mode).
-template <int kMode>
+template <int kMode, bool kLR>
 __device__ __forceinline__ void finish_tile(float (&acc)[128], const GemmEpilogue& ep, float* tw, int M, int N,
                                             int m_tile, int n_tile, int q, int h, int lane, bool ok) {
   const int row = q * 32 + lane;
@@ -66,7 +67,10 @@ __device__ __forceinline__ void finish_tile(float (&acc)[128], const GemmEpilogu
   const bool row_ok = m < M;
   // N % 128 == 0: the last column tile may hold only its first half (the TMA zero-fills the missing weight rows)
   const bool col_ok = n_tile * BN + h * 128 < N;
-  if (ok && row_ok && col_ok) add_addend<128>(ep, m, n_tile * BN + h * 128, acc);
+  if (ok && row_ok && col_ok) {
+    add_addend<128>(ep, m, n_tile * BN + h * 128, acc);
+    if constexpr (kLR) add_lowrank<128>(ep, m, n_tile * BN + h * 128, acc);  // its own instantiations (registers)
+  }
 
   if constexpr (kMode == kEpiResidualF32) {
     // Residual update through a per-warp 32 x 32 transpose in shared memory (the pipeline buffers, idle once every
@@ -172,7 +176,7 @@ __device__ __forceinline__ void finish_tile(float (&acc)[128], const GemmEpilogu
   }
 }
 
-template <int kMode>
+template <int kMode, bool kLR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_fold_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                      const float* __restrict__ fold_scale, GemmEpilogue ep, int M, int N, int K, uint32_t* err) {
@@ -302,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     if constexpr (kMode == kEpiResidualF32) fence_proxy_async_smem();  // the scratch is a pipeline buffer
-    finish_tile<kMode>(acc, ep, reinterpret_cast<float*>(sm.a[0]) + (warp - 4) * 32 * 33, M, N, m_tile, n_tile, q,
+    finish_tile<kMode, kLR>(acc, ep, reinterpret_cast<float*>(sm.a[0]) + (warp - 4) * 32 * 33, M, N, m_tile, n_tile, q,
                        h, lane, ok);
   }
 
@@ -336,7 +340,7 @@ struct __align__(1024) SmemP {
 
 constexpr size_t kSmemPBytes = sizeof(SmemP) + 1024;
 
-template <int kMode>
+template <int kMode, bool kLR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pre_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     const float* __restrict__ fold_scale, GemmEpilogue ep, int M, int N, int K, uint32_t* err) {
@@ -458,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[b]);  // every column in registers: the MMA may reuse the buffer
-      finish_tile<kMode>(acc, ep, tw, M, N, m_tile, n_tile, q, h, lane, true);
+      finish_tile<kMode, kLR>(acc, ep, tw, M, N, m_tile, n_tile, q, h, lane, true);
     }
   }
 
@@ -502,7 +506,7 @@ struct __align__(1024) SmemPair {
 constexpr size_t kSmemPairBytes = sizeof(SmemPair) + 1024;
 static_assert(kSmemPairBytes <= 232448, "shared memory of a CTA pair's stage ring");
 
-template <int kMode>
+template <int kMode, bool kLR>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pre_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                          const float* __restrict__ fold_scale, GemmEpilogue ep, int M, int N, int K, uint32_t* err) {
@@ -646,7 +650,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * b);  // every column in registers: the MMA may reuse it
-      finish_tile<kMode>(acc, ep, tw, M, N, m_tile, n_tile, q, h, lane, true);
+      finish_tile<kMode, kLR>(acc, ep, tw, M, N, m_tile, n_tile, q, h, lane, true);
     }
   }
 
@@ -781,9 +785,9 @@ int gemm_fold_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
                                                                                a.K, a.err);
     };
     switch (a.ep.mode) {
-      case kEpiBf16: launch_pair(fold::gemm_pre_pair_kernel<kEpiBf16>); break;
-      case kEpiResidualF32: launch_pair(fold::gemm_pre_pair_kernel<kEpiResidualF32>); break;
-      case kEpiGeluU4: launch_pair(fold::gemm_pre_pair_kernel<kEpiGeluU4>); break;
+      case kEpiBf16: a.ep.lr_act ? launch_pair(fold::gemm_pre_pair_kernel<kEpiBf16, true>) : launch_pair(fold::gemm_pre_pair_kernel<kEpiBf16, false>); break;
+      case kEpiResidualF32: a.ep.lr_act ? launch_pair(fold::gemm_pre_pair_kernel<kEpiResidualF32, true>) : launch_pair(fold::gemm_pre_pair_kernel<kEpiResidualF32, false>); break;
+      case kEpiGeluU4: a.ep.lr_act ? launch_pair(fold::gemm_pre_pair_kernel<kEpiGeluU4, true>) : launch_pair(fold::gemm_pre_pair_kernel<kEpiGeluU4, false>); break;
       default: *why = "unknown epilogue mode"; return 1;
     }
     if (e == cudaSuccess) e = cudaGetLastError();
@@ -804,9 +808,9 @@ int gemm_fold_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
         kernel<<<pgrid, fold::kThreads, fold::kSmemPBytes, stream>>>(ma, mb, a.wscale, a.ep, a.M, a.N, a.K, a.err);
     };
     switch (a.ep.mode) {
-      case kEpiBf16: launch_p(fold::gemm_pre_kernel<kEpiBf16>); break;
-      case kEpiResidualF32: launch_p(fold::gemm_pre_kernel<kEpiResidualF32>); break;
-      case kEpiGeluU4: launch_p(fold::gemm_pre_kernel<kEpiGeluU4>); break;
+      case kEpiBf16: a.ep.lr_act ? launch_p(fold::gemm_pre_kernel<kEpiBf16, true>) : launch_p(fold::gemm_pre_kernel<kEpiBf16, false>); break;
+      case kEpiResidualF32: a.ep.lr_act ? launch_p(fold::gemm_pre_kernel<kEpiResidualF32, true>) : launch_p(fold::gemm_pre_kernel<kEpiResidualF32, false>); break;
+      case kEpiGeluU4: a.ep.lr_act ? launch_p(fold::gemm_pre_kernel<kEpiGeluU4, true>) : launch_p(fold::gemm_pre_kernel<kEpiGeluU4, false>); break;
       default: *why = "unknown epilogue mode"; return 1;
     }
     if (e == cudaSuccess) e = cudaGetLastError();
@@ -822,9 +826,9 @@ int gemm_fold_launch(const GemmArgs& a, cudaStream_t stream, const char** why) {
       kernel<<<grid, fold::kThreads, fold::kSmemBytes, stream>>>(ma, mb, a.wscale, a.ep, a.M, a.N, a.K, a.err);
   };
   switch (a.ep.mode) {
-    case kEpiBf16: launch(fold::gemm_fold_kernel<kEpiBf16>); break;
-    case kEpiResidualF32: launch(fold::gemm_fold_kernel<kEpiResidualF32>); break;
-    case kEpiGeluU4: launch(fold::gemm_fold_kernel<kEpiGeluU4>); break;
+    case kEpiBf16: a.ep.lr_act ? launch(fold::gemm_fold_kernel<kEpiBf16, true>) : launch(fold::gemm_fold_kernel<kEpiBf16, false>); break;
+    case kEpiResidualF32: a.ep.lr_act ? launch(fold::gemm_fold_kernel<kEpiResidualF32, true>) : launch(fold::gemm_fold_kernel<kEpiResidualF32, false>); break;
+    case kEpiGeluU4: a.ep.lr_act ? launch(fold::gemm_fold_kernel<kEpiGeluU4, true>) : launch(fold::gemm_fold_kernel<kEpiGeluU4, false>); break;
     default: *why = "unknown epilogue mode"; return 1;
   }
   if (e == cudaSuccess) e = cudaGetLastError();

@@ -19,6 +19,17 @@ DTYPE_CODE = {torch.bfloat16: BF16, torch.float16: F16, torch.float32: F32}
 
 _P, _I, _I64, _SZ, _U32P = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint32)
 
+
+
+class LowRank(ctypes.Structure):
+    """wdl_lowrank (include/wdl_b200.h): an SVDQuant low-rank branch formed in the GEMM epilogue, act [M, ld_act]
+    float32 = x proj_down, up [N, rank] float32 = proj_up, rank a multiple of 4. Whoever makes one keeps the
+    tensors it points to alive until the GEMM has run (attributes set on the instance do)."""
+    _fields_ = [("act", ctypes.c_void_p), ("ld_act", ctypes.c_int64), ("up", ctypes.c_void_p), ("rank", ctypes.c_int)]
+
+
+_LRP = ctypes.POINTER(LowRank)
+
 # name: (restype, argtypes), in the order of include/wdl_b200.h
 SIGNATURES = {
     "wdl_last_error": (ctypes.c_char_p, []),
@@ -34,7 +45,12 @@ SIGNATURES = {
     "wdl_w4a4_gemm_residual_add": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _P, _P, _I64, _I, _I, _I, _P, _I64, _P]),
     "wdl_w4a4_gemm_gelu_u4_add": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _P, ctypes.c_float, _I, _I, _I, _I, _P,
                                        _I64, _P, _P, _I64, _P]),
+    "wdl_w4a4_gemm_lowrank": (_I, [_P, _P, _P, _P, _I, _P, _LRP, _I, _I, _I, _P, _I64, _P]),
+    "wdl_w4a4_gemm_residual_lowrank": (_I, [_P, _P, _P, _P, _I, _P, _LRP, _P, _P, _I64, _I, _I, _I, _P, _I64, _P]),
+    "wdl_w4a4_gemm_gelu_u4_lowrank": (_I, [_P, _P, _P, _P, _I, _P, _LRP, _P, ctypes.c_float, _I, _I, _I, _I, _P,
+                                           _I64, _P, _P, _I64, _P]),
     "wdl_w4a4_gemm_f32": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _I, _I, _I, _P, _I64, _P]),
+    "wdl_w4a4_gemm_f32_lowrank": (_I, [_P, _P, _P, _P, _I, _P, _LRP, _I, _I, _I, _P, _I64, _P]),
     "wdl_w4a4_linear_workspace": (_SZ, [_I, _I]),
     "wdl_w4a4_linear": (_I, [_P, _I64, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P, _I64, _P, _SZ, _P]),
     "wdl_w4a4_linear_noalloc": (_I, [_P, _I64, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P, _I64, _P]),

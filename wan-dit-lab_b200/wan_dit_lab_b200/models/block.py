@@ -235,22 +235,22 @@ class WanBlockB200:
             timer(e0, e1, 2 * n * layer.N * layer.K)
 
         def lora(layer, x):
-            """The layer's low-rank product [n, N] float32 for its bf16 / float32 input x, or None at rank 0."""
-            return layer.lowrank(x[:n]) if layer.rank else None
+            """The layer's low-rank branch for its bf16 / float32 input x (its down-projection [n, r] here, its
+            up-projection in the GEMM epilogue: a wdl_lowrank), or None at rank 0."""
+            return layer.lowrank_arg(layer.lowrank_act(x[:n])) if layer.rank else None
 
         def gemm(layer, out, add=None):
-            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_add(
+            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_lowrank(
                 buf.codes.data_ptr(), buf.scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), fmt,
-                _native.ptr(layer.bias), _native.ptr(add), layer.N, n, layer.N, layer.K, out.data_ptr(), out.stride(0),
-                st)))
+                _native.ptr(layer.bias), add, n, layer.N, layer.K, out.data_ptr(), out.stride(0), st)))
 
         def gemm_residual(layer, gate_row, codes=None, scales=None, add=None):
             c = buf.codes if codes is None else codes
             s = buf.scales if scales is None else scales
             f = fmt if codes is None else w4a4.hidden_format(fmt)  # the hidden layer's own format
-            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_residual_add(
+            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_residual_lowrank(
                 c.data_ptr(), s.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), f,
-                _native.ptr(layer.bias), _native.ptr(add), layer.N, None if gate_row is None else mod_ptr(gate_row),
+                _native.ptr(layer.bias), add, None if gate_row is None else mod_ptr(gate_row),
                 X.data_ptr(), dim, n, layer.N, layer.K, X.data_ptr(), dim, st)))
 
         def ln_quant(shift_row, scale_row, affine, layer, round_bf16):
@@ -309,10 +309,10 @@ class WanBlockB200:
         fc1, fc2 = L["ffn.0"], L["ffn.2"]
         add = ln_quant(3, 4, False, fc1, False)
         gelu = buf.gelu if fc2.rank else None  # the second layer's branch reads GELU's output without the shift
-        timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4_add(
+        timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4_lowrank(
             buf.codes.data_ptr(), buf.scales.data_ptr(), fc1.codes.data_ptr(), fc1.scales.data_ptr(), fmt,
-            _native.ptr(fc1.bias), _native.ptr(add), fc1.N, _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N,
-            fc1.K, buf.hcodes.data_ptr(), fc1.N, buf.hscales.data_ptr(), _native.ptr(gelu), fc1.N, st)))
+            _native.ptr(fc1.bias), add, _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N, fc1.K,
+            buf.hcodes.data_ptr(), fc1.N, buf.hscales.data_ptr(), _native.ptr(gelu), fc1.N, st)))
         if trace is not None:  # the hidden codes [n, ffn] as float values, whatever their operand format
             raw = buf.hcodes.view(-1)
             if w4a4.hidden_format(fmt) == _native.CODES_F16_FOLD:

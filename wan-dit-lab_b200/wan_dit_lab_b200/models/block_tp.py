@@ -225,20 +225,20 @@ class WanBlockTP:
             timer(e0, e1, 2 * n * layer.N * layer.K)
 
         def lora(layer, x):
-            """The shard's low-rank product (float32, [n, the layer's N]) for its input x, or None at rank 0."""
-            return layer.lowrank(x[:n]) if layer.rank else None
+            """The shard's low-rank branch for its input x (its down-projection here, the up-projection onto the
+            layer's N in the GEMM epilogue: a wdl_lowrank), or None at rank 0."""
+            return layer.lowrank_arg(layer.lowrank_act(x[:n])) if layer.rank else None
 
         def gemm(layer, out, add=None):
-            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_add(
+            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_lowrank(
                 buf.codes.data_ptr(), buf.scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), fmt,
-                _native.ptr(layer.bias), _native.ptr(add), layer.N, n, layer.N, layer.K, out.data_ptr(),
-                out.stride(0), st)))
+                _native.ptr(layer.bias), add, n, layer.N, layer.K, out.data_ptr(), out.stride(0), st)))
 
         def partial(layer, codes, scales, add=None):
             f = w4a4.hidden_format(fmt) if codes is buf.hcodes else fmt  # the hidden layer's own format
-            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_f32(
-                codes.data_ptr(), scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), f, None,
-                _native.ptr(add), dim, n, dim, layer.K, buf.partial.data_ptr(), dim, st)))
+            timed(layer, lambda: _native.check(lib.wdl_w4a4_gemm_f32_lowrank(
+                codes.data_ptr(), scales.data_ptr(), layer.codes.data_ptr(), layer.scales.data_ptr(), f, None, add,
+                n, dim, layer.K, buf.partial.data_ptr(), dim, st)))
 
         def residual(name, gate_row):
             _native.check(lib.wdl_residual_update(buf.partial.data_ptr(), dim, _native.ptr(self.bias[name]),
@@ -305,10 +305,10 @@ class WanBlockTP:
         fc1, fc2 = L["ffn.0"], L["ffn.2"]
         add = ln_quant(3, 4, False, fc1, False)
         gelu = buf.gelu if fc2.rank else None  # the second layer's branch reads GELU's output (its shard's channels)
-        timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4_add(
+        timed(fc1, lambda: _native.check(lib.wdl_w4a4_gemm_gelu_u4_lowrank(
             buf.codes.data_ptr(), buf.scales.data_ptr(), fc1.codes.data_ptr(), fc1.scales.data_ptr(), fmt,
-            _native.ptr(fc1.bias), _native.ptr(add), fc1.N, _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N,
-            fc1.K, buf.hcodes.data_ptr(), fc1.N, buf.hscales.data_ptr(), _native.ptr(gelu), fc1.N, st)))
+            _native.ptr(fc1.bias), add, _native.ptr(fc2.smooth), w4a4.GELU_SHIFT, sd, n, fc1.N, fc1.K,
+            buf.hcodes.data_ptr(), fc1.N, buf.hscales.data_ptr(), _native.ptr(gelu), fc1.N, st)))
         partial(fc2, buf.hcodes, buf.hscales, None if gelu is None else lora(fc2, gelu))
         yield buf.partial
         residual("ffn.2", 5)

@@ -265,13 +265,18 @@ class PreparedW4A4:
             raise ValueError(f"wscales must be [K/64, N] = [{K // GROUP}, {N}], got {tuple(wscales.shape)}")
         self.N, self.K = N, K
         # the SVDQuant low-rank branch (rank r, bf16 factors): proj_down [K, r] (already divided by the smoothing:
-        # the branch reads x itself), proj_up [N, r]; y += (x proj_down) proj_up^T, added in the GEMM epilogue
+        # the branch reads x itself), proj_up [N, r]; y += (x proj_down) proj_up^T: the down-projection a thin
+        # float32 product, the up-projection formed in the GEMM epilogue (wdl_lowrank). The factors are kept in
+        # float32 with the rank padded to a multiple of 4 by zero columns (the epilogue takes four ranks at a time).
         self.rank = 0 if proj_down is None or proj_down.numel() == 0 else int(proj_down.shape[-1])
         if self.rank:
             if proj_down.shape != (K, self.rank) or proj_up is None or proj_up.shape != (N, self.rank):
                 raise ValueError(f"proj_down must be [K, r] = [{K}, r] and proj_up [N, r] = [{N}, r]")
-            self.down = proj_down.float().contiguous()
-            self.up = proj_up.float().contiguous()
+            r4 = -(-self.rank // 4) * 4
+            self.down = torch.zeros(K, r4, dtype=torch.float32, device=proj_down.device)
+            self.up = torch.zeros(N, r4, dtype=torch.float32, device=proj_up.device)
+            self.down[:, :self.rank] = proj_down.float()
+            self.up[:, :self.rank] = proj_up.float()
         self.scale_dtype = wscales.dtype
         self._parts = (qweight, wscales, proj_down, proj_up, smooth, bias)
         fmt = code_format or CODE_FORMAT
@@ -314,11 +319,29 @@ class PreparedW4A4:
 
     def lowrank(self, x):
         """The low-rank branch's contribution (x proj_down) proj_up^T [M, N] float32 for x [M, K] (the layer's
-        input before smoothing), or None at rank 0: two plain float32 GEMMs (cuBLAS); Nunchaku forms the same
-        products in its quantizer and GEMM epilogue (w4a4_ops.cpp:27, 36)."""
+        input before smoothing), or None at rank 0, as two plain float32 products: the addend form that the _add
+        GEMM entry points take (the tensor-parallel shards' partial products use it); the layers themselves form
+        the up-projection in the GEMM epilogue (lowrank_act, lowrank_arg)."""
         if not self.rank:
             return None
         return ((x.float() @ self.down) @ self.up.t()).contiguous()
+
+    def lowrank_act(self, x):
+        """The branch's down-projection x proj_down [M, r] float32 for x [M, K] (the layer's input before
+        smoothing; a thin cuBLAS product, as Nunchaku forms it beside its quantizer, w4a4_ops.cpp:27), or None
+        at rank 0."""
+        if not self.rank:
+            return None
+        return (x.float() @ self.down).contiguous()
+
+    def lowrank_arg(self, act):
+        """The wdl_lowrank that the _lowrank GEMM entry points take for act = lowrank_act(x) (None for None): the
+        epilogue adds act proj_up^T before the bias (w4a4_ops.cpp:36), the [M, N] product never written."""
+        if act is None:
+            return None
+        arg = _native.LowRank(act.data_ptr(), act.stride(0), self.up.data_ptr(), self.up.shape[1])
+        arg.tensors = (act, self.up)  # alive as long as the argument
+        return arg
 
     def quantize_input(self, x, work):
         """x [M, K] bfloat16 -> (codes, scales) of this layer's code format, in the workspace `work`."""
@@ -350,12 +373,12 @@ class PreparedW4A4:
                     self.codes.data_ptr(), self.scales.data_ptr(), self.code_format, _native.ptr(self.bias), self.N,
                     y.data_ptr(), self.N, work.data_ptr(), work.numel(), _native.stream()))
             else:
-                add = self.lowrank(x)
+                branch = self.lowrank_arg(self.lowrank_act(x))
                 codes, scales = self.quantize_input(x, work)
-                _native.check(lib.wdl_w4a4_gemm_add(
+                _native.check(lib.wdl_w4a4_gemm_lowrank(
                     codes.data_ptr(), scales.data_ptr(), self.codes.data_ptr(), self.scales.data_ptr(),
-                    self.code_format, _native.ptr(self.bias), add.data_ptr(), self.N, M, self.N, K, y.data_ptr(),
-                    self.N, _native.stream()))
+                    self.code_format, _native.ptr(self.bias), branch, M, self.N, K, y.data_ptr(), self.N,
+                    _native.stream()))
         return y
 
 
@@ -423,17 +446,16 @@ def w4a4_gelu_mlp(x, *parts):
     gelu = torch.empty(M, l1.N, dtype=torch.float32, device=x.device) if l2.rank else None
     y = torch.empty(M, l2.N, dtype=torch.bfloat16, device=x.device)
     with torch.cuda.device(x.device):
-        add1 = l1.lowrank(x)
+        branch1 = l1.lowrank_arg(l1.lowrank_act(x))
         codes, scales = l1.quantize_input(x, work)
-        _native.check(lib.wdl_w4a4_gemm_gelu_u4_add(
+        _native.check(lib.wdl_w4a4_gemm_gelu_u4_lowrank(
             codes.data_ptr(), scales.data_ptr(), l1.codes.data_ptr(), l1.scales.data_ptr(), l1.code_format,
-            _native.ptr(l1.bias), _native.ptr(add1), l1.N, _native.ptr(l2.smooth), GELU_SHIFT,
-            _scale_code(l2.scale_dtype), M, l1.N, l1.K, hidden.data_ptr(), l1.N, hscales.data_ptr(),
-            _native.ptr(gelu), l1.N, st))
-        add2 = l2.lowrank(gelu) if l2.rank else None
-        _native.check(lib.wdl_w4a4_gemm_add(
+            _native.ptr(l1.bias), branch1, _native.ptr(l2.smooth), GELU_SHIFT, _scale_code(l2.scale_dtype), M, l1.N,
+            l1.K, hidden.data_ptr(), l1.N, hscales.data_ptr(), _native.ptr(gelu), l1.N, st))
+        branch2 = l2.lowrank_arg(l2.lowrank_act(gelu) if l2.rank else None)
+        _native.check(lib.wdl_w4a4_gemm_lowrank(
             hidden.data_ptr(), hscales.data_ptr(), l2.codes.data_ptr(), l2.scales.data_ptr(), hidden_format(l2.code_format),
-            _native.ptr(l2.bias), _native.ptr(add2), l2.N, M, l2.N, l2.K, y.data_ptr(), l2.N, st))
+            _native.ptr(l2.bias), branch2, M, l2.N, l2.K, y.data_ptr(), l2.N, st))
     return y
 
 
