@@ -163,6 +163,13 @@ typedef struct wdl_lowrank {
   int rank;
 } wdl_lowrank;
 
+/* The branch's down-projection: act [M, ld_act] f32 = x [M, ldx] (x_dtype WDL_BF16 or WDL_F32) proj_down [K, rank]
+ * f32 (row-major, rank columns), accumulated in float32 in a fixed order (Nunchaku forms it beside its activation
+ * quantizer, native/ops/w4a4_ops.cpp:27). K a multiple of 32, rank a positive multiple of 4, x and its rows
+ * 16-byte aligned, proj_down 16-byte aligned, ld_act >= rank. */
+int wdl_lowrank_down(const void* x, int x_dtype, int64_t ldx, int M, int K, const float* down, int rank, float* act,
+                     int64_t ld_act, void* stream);
+
 /* The _add entry points above with the branch given as a wdl_lowrank (null: none) instead of its addend. */
 int wdl_w4a4_gemm_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                           const float* bias, const wdl_lowrank* lowrank, int M, int N, int K, uint16_t* y,

@@ -145,6 +145,12 @@ def test_new_entry_points_validate_before_any_launch(native):
         st = lib.wdl_w4a4_gemm_lowrank(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, lr, 128, 256, 256, FAKE,
                                        256, None)
         assert st == native.ERR_ARGUMENT and b"low-rank" in err(), (rank, ld, act)
+    for args, needle in (((FAKE, native.BF16, 64, 4, 48, FAKE, 8, FAKE, 8), b"multiple of 32"),
+                         ((FAKE, native.BF16, 64, 4, 64, FAKE, 6, FAKE, 8), b"multiple of 4"),
+                         ((FAKE, native.F16, 64, 4, 64, FAKE, 8, FAKE, 8), b"bf16 or f32"),
+                         ((FAKE, native.BF16, 60, 4, 64, FAKE, 8, FAKE, 8), b"ldx"),
+                         ((FAKE + 8, native.BF16, 64, 4, 64, FAKE, 8, FAKE, 8), b"misaligned")):
+        assert lib.wdl_lowrank_down(*args, None) == native.ERR_ARGUMENT and needle in err(), needle
     lr = native.LowRank(FAKE, 8, FAKE, 6)
     for call in (lambda: lib.wdl_w4a4_gemm_f32_lowrank(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, lr, 128,
                                                        256, 256, FAKE, 256, None),

@@ -195,3 +195,25 @@ def test_epilogue_branch_equals_its_addend(fmt, rank):
     # the update x + o gate: o as above times the gate, the float32 sum with x rounded once more (|x| < 8)
     o_lr, o_add = r_lr - residual, r_add - residual
     assert bool(((r_lr - r_add).abs() <= step(o_lr, o_add) + 2e-6).all())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("M,K,rank", [(37, 512, 8), (300, 3072, 32), (300, 14336, 32), (64, 1024, 36)])
+def test_lowrank_down_projection(M, K, rank, dtype):
+    """wdl_lowrank_down (x proj_down, K split over a cluster of 1 to 8 CTAs whose sums are added in rank order)
+    against the float64 product: within float32 rounding of the sum, and bit for bit the same on a second call."""
+    _native = native()
+    lib, st = _native.lib(), _native.stream()
+    x = seeded((M, K), 60).to(dtype).cuda()
+    down = seeded((K, rank), 61, 0.05).cuda()
+    acts = []
+    for _ in range(2):
+        act = torch.full((M, rank), float("nan"), device="cuda")
+        _native.check(lib.wdl_lowrank_down(x.data_ptr(), _native.DTYPE_CODE[dtype], K, M, K, down.data_ptr(), rank,
+                                           act.data_ptr(), rank, st))
+        acts.append(act)
+    torch.cuda.synchronize()
+    want = x.double() @ down.double()
+    err = float((acts[0].double() - want).abs().max() / want.abs().max())
+    assert err <= 2e-6, err
+    assert torch.equal(acts[0], acts[1])

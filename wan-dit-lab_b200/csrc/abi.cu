@@ -221,6 +221,21 @@ static int set_addend(wdl::w4a4::GemmArgs& g, const float* addend, int64_t ld_ad
   return ok();
 }
 
+int wdl_lowrank_down(const void* x, int x_dtype, int64_t ldx, int M, int K, const float* down, int rank, float* act,
+                     int64_t ld_act, void* stream) {
+  if (M < 0 || K <= 0 || K % 32 != 0) return fail(WDL_ERR_ARGUMENT, "M >= 0 and K a positive multiple of 32 required");
+  if (rank <= 0 || rank % 4 != 0) return fail(WDL_ERR_ARGUMENT, "rank must be a positive multiple of 4");
+  if (x_dtype != WDL_BF16 && x_dtype != WDL_F32) return fail(WDL_ERR_ARGUMENT, "x must be bf16 or f32");
+  const int esize = x_dtype == WDL_F32 ? 4 : 2;
+  if (ldx < K || (ldx * esize) % 16 != 0 || ld_act < rank)
+    return fail(WDL_ERR_ARGUMENT, "ldx >= K with 16-byte aligned rows and ld_act >= rank required");
+  if (M == 0) return ok();
+  if (!x || !down || !act || !aligned(x, 16) || !aligned(down, 16)) return fail(WDL_ERR_ARGUMENT, "null or misaligned pointer");
+  return cuda_status(wdl::w4a4::lowrank_down_launch(x, x_dtype == WDL_F32, ldx, M, K, down, rank, act, ld_act,
+                                                    static_cast<cudaStream_t>(stream)),
+                     "lowrank_down launch");
+}
+
 // The low-rank branch formed in the epilogue (wdl_lowrank), when given.
 static int set_lowrank(wdl::w4a4::GemmArgs& g, const wdl_lowrank* lr) {
   if (!lr) return ok();

@@ -368,7 +368,14 @@ __device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_add
   asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-// Both CTAs of the cluster reach this point before either goes on (all threads of both).
+// The number of CTAs in this CTA's cluster.
+__device__ __forceinline__ uint32_t cluster_nctas() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+// Every CTA of the cluster reaches this point before any goes on (all threads of all of them).
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }

@@ -20,5 +20,10 @@ void quantize_rows_launch(const void* x, int x_dtype, int64_t ldx, const uint16_
 void unpack_weight_launch(const uint8_t* qweight, const uint16_t* wscales, int scale_dtype, int N, int K,
                           int code_format, int8_t* codes, float* scales, cudaStream_t stream);
 
+// act [M, ld_act] f32 = x [M, ldx] (bf16, or f32 with x_f32) proj_down [K, rank] f32 (lowrank.cu). Requirements
+// (checked by the caller): K % 32 == 0, x and its rows 16-byte aligned, rank % 4 == 0, rank <= ld_act.
+cudaError_t lowrank_down_launch(const void* x, int x_f32, int64_t ldx, int M, int K, const float* down, int rank,
+                                float* act, int64_t ld_act, cudaStream_t s);
+
 }  // namespace w4a4
 }  // namespace wdl

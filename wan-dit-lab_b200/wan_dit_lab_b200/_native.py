@@ -45,6 +45,7 @@ SIGNATURES = {
     "wdl_w4a4_gemm_residual_add": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _P, _P, _I64, _I, _I, _I, _P, _I64, _P]),
     "wdl_w4a4_gemm_gelu_u4_add": (_I, [_P, _P, _P, _P, _I, _P, _P, _I64, _P, ctypes.c_float, _I, _I, _I, _I, _P,
                                        _I64, _P, _P, _I64, _P]),
+    "wdl_lowrank_down": (_I, [_P, _I, _I64, _I, _I, _P, _I, _P, _I64, _P]),
     "wdl_w4a4_gemm_lowrank": (_I, [_P, _P, _P, _P, _I, _P, _LRP, _I, _I, _I, _P, _I64, _P]),
     "wdl_w4a4_gemm_residual_lowrank": (_I, [_P, _P, _P, _P, _I, _P, _LRP, _P, _P, _I64, _I, _I, _I, _P, _I64, _P]),
     "wdl_w4a4_gemm_gelu_u4_lowrank": (_I, [_P, _P, _P, _P, _I, _P, _LRP, _P, ctypes.c_float, _I, _I, _I, _I, _P,

@@ -327,12 +327,22 @@ class PreparedW4A4:
         return ((x.float() @ self.down) @ self.up.t()).contiguous()
 
     def lowrank_act(self, x):
-        """The branch's down-projection x proj_down [M, r] float32 for x [M, K] (the layer's input before
-        smoothing; a thin cuBLAS product, as Nunchaku forms it beside its quantizer, w4a4_ops.cpp:27), or None
-        at rank 0."""
+        """The branch's down-projection x proj_down [M, r] float32 for x [M, K] bfloat16 or float32 (the layer's
+        input before smoothing; Nunchaku forms it beside its quantizer, w4a4_ops.cpp:27), by wdl_lowrank_down, or
+        None at rank 0."""
         if not self.rank:
             return None
-        return (x.float() @ self.down).contiguous()
+        if x.dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError("the low-rank branch reads a bfloat16 or float32 input")
+        if x.stride(1) != 1 or (x.stride(0) * x.element_size()) % 16 or x.data_ptr() % 16:
+            x = x.contiguous()
+        M, r4 = x.shape[0], self.down.shape[1]
+        act = torch.empty(M, r4, dtype=torch.float32, device=x.device)
+        with torch.cuda.device(x.device):
+            _native.check(_native.lib().wdl_lowrank_down(
+                x.data_ptr(), _native.DTYPE_CODE[x.dtype], x.stride(0), M, self.K, self.down.data_ptr(), r4,
+                act.data_ptr(), r4, _native.stream()))
+        return act
 
     def lowrank_arg(self, act):
         """The wdl_lowrank that the _lowrank GEMM entry points take for act = lowrank_act(x) (None for None): the
