@@ -61,6 +61,34 @@ def test_gemm_shapes_rejected_before_any_launch(native):
     assert lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_E4M3, None, 0, 256, 256, FAKE, 256, None) == 0
 
 
+def test_epilogue_strides_above_32_bits_rejected(native):
+    """The GEMM epilogue carries its row strides as 32-bit ints: a stride of 2^31 elements or more is refused
+    before any launch, in each entry point that takes one."""
+    lib = native.lib()
+    wide = 1 << 31
+    lr = native.LowRank(FAKE, wide, FAKE, 8)
+    calls = {
+        b"ldy": lambda: lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, 128, 256, 256, FAKE,
+                                          wide, None),
+        b"ldr": lambda: lib.wdl_w4a4_gemm_residual(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, None, FAKE,
+                                                   wide, 128, 256, 256, FAKE, 256, None),
+        b"ldo": lambda: lib.wdl_w4a4_gemm_f32(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, None, 0, 128, 256,
+                                              256, FAKE, wide, None),
+        b"addend": lambda: lib.wdl_w4a4_gemm_add(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, FAKE, wide, 128,
+                                                 256, 256, FAKE, 256, None),
+        b"low-rank": lambda: lib.wdl_w4a4_gemm_lowrank(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, lr, 128,
+                                                       256, 256, FAKE, 256, None),
+        b"ldc": lambda: lib.wdl_w4a4_gemm_gelu_u4(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, None, 0.171875,
+                                                  native.BF16, 128, 256, 256, FAKE, wide, FAKE, None),
+        b"gelu_out": lambda: lib.wdl_w4a4_gemm_gelu_u4_add(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, None, None,
+                                                           0, None, 0.171875, native.BF16, 128, 256, 256, FAKE, 256,
+                                                           FAKE, FAKE, wide, None),
+    }
+    for needle, call in calls.items():
+        assert call() == native.ERR_ARGUMENT, needle
+        assert needle in lib.wdl_last_error() and b"2^31" in lib.wdl_last_error(), (needle, lib.wdl_last_error())
+
+
 def test_workspace_sizes(native):
     lib = native.lib()
     M, K = 1392, 3072

@@ -213,11 +213,15 @@ static void operands(wdl::w4a4::GemmArgs& g, const void* a, const float* a_scale
   g.ep.ascale = a_scales;
 }
 
+// The GEMM epilogue's leading dimensions reach the kernels as 32-bit ints (GemmEpilogue).
+static bool ld32(int64_t ld) { return ld <= INT32_MAX; }
+
 // The low-rank branch's fp32 addend [M, ld_add], when given.
 static int set_addend(wdl::w4a4::GemmArgs& g, const float* addend, int64_t ld_add, int N) {
   if (!addend) return ok();
-  if (ld_add < N || !aligned(addend, 4)) return fail(WDL_ERR_ARGUMENT, "addend rows must hold N floats");
-  g.ep.addend = addend, g.ep.ld_add = ld_add;
+  if (ld_add < N || !ld32(ld_add) || !aligned(addend, 4))
+    return fail(WDL_ERR_ARGUMENT, "addend rows must hold N floats (ld_add < 2^31)");
+  g.ep.addend = addend, g.ep.ld_add = static_cast<int>(ld_add);
   return ok();
 }
 
@@ -242,20 +246,21 @@ static int set_lowrank(wdl::w4a4::GemmArgs& g, const wdl_lowrank* lr) {
   if (!lr->act || !lr->up) return fail(WDL_ERR_ARGUMENT, "low-rank act and up must not be null");
   if (lr->rank <= 0 || lr->rank % 4 != 0 || lr->rank > 1024)
     return fail(WDL_ERR_ARGUMENT, "low-rank rank must be a positive multiple of 4, at most 1024");
-  if (lr->ld_act < lr->rank || lr->ld_act % 4 != 0 || !aligned(lr->act, 16) || !aligned(lr->up, 16))
-    return fail(WDL_ERR_ARGUMENT, "low-rank act rows must hold rank floats, 16-byte aligned");
-  g.ep.lr_act = lr->act, g.ep.lr_ld = lr->ld_act, g.ep.lr_up = lr->up, g.ep.lr_rank = lr->rank;
+  if (lr->ld_act < lr->rank || lr->ld_act % 4 != 0 || !ld32(lr->ld_act) || !aligned(lr->act, 16) || !aligned(lr->up, 16))
+    return fail(WDL_ERR_ARGUMENT, "low-rank act rows must hold rank floats, 16-byte aligned (ld_act < 2^31)");
+  g.ep.lr_act = lr->act, g.ep.lr_ld = static_cast<int>(lr->ld_act), g.ep.lr_up = lr->up, g.ep.lr_rank = lr->rank;
   return ok();
 }
 
 int wdl_w4a4_gemm_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                           const float* bias, const wdl_lowrank* lowrank, int M, int N, int K, uint16_t* y,
                           int64_t ldy, void* stream) {
-  if (ldy < N || (ldy * 2) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldy must be >= N with 16-byte aligned rows");
+  if (ldy < N || (ldy * 2) % 16 != 0 || !ld32(ldy))
+    return fail(WDL_ERR_ARGUMENT, "ldy must be >= N (and < 2^31) with 16-byte aligned rows");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
   if (set_lowrank(g, lowrank) != WDL_OK) return WDL_ERR_ARGUMENT;
-  g.ep.mode = wdl::w4a4::kEpiBf16, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = ldy;
+  g.ep.mode = wdl::w4a4::kEpiBf16, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = static_cast<int>(ldy);
   return gemm_common(g, stream);
 }
 
@@ -264,35 +269,37 @@ int wdl_w4a4_gemm_residual_lowrank(const void* a, const float* a_scales, const v
                                    const float* residual, int64_t ldr, int M, int N, int K, float* out, int64_t ldo,
                                    void* stream) {
   if (!residual) return fail(WDL_ERR_ARGUMENT, "residual must not be null");
-  if (ldr < N || ldo < N || (ldr * 4) % 16 != 0 || (ldo * 4) % 16 != 0)
-    return fail(WDL_ERR_ARGUMENT, "ldr, ldo must be >= N with 16-byte aligned rows");
+  if (ldr < N || ldo < N || (ldr * 4) % 16 != 0 || (ldo * 4) % 16 != 0 || !ld32(ldr) || !ld32(ldo))
+    return fail(WDL_ERR_ARGUMENT, "ldr, ldo must be >= N (and < 2^31) with 16-byte aligned rows");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
   if (set_lowrank(g, lowrank) != WDL_OK) return WDL_ERR_ARGUMENT;
   g.ep.mode = wdl::w4a4::kEpiResidualF32, g.ep.bias = bias, g.ep.gate = gate;
-  g.ep.residual = residual, g.ep.ld_res = ldr, g.ep.out = out, g.ep.ld_out = ldo;
+  g.ep.residual = residual, g.ep.ld_res = static_cast<int>(ldr), g.ep.out = out, g.ep.ld_out = static_cast<int>(ldo);
   return gemm_common(g, stream);
 }
 
 int wdl_w4a4_gemm_f32_lowrank(const void* a, const float* a_scales, const void* w, const float* w_scales,
                               int code_format, const float* bias, const wdl_lowrank* lowrank, int M, int N, int K,
                               float* out, int64_t ldo, void* stream) {
-  if (ldo < N || (ldo * 4) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldo must be >= N with 16-byte aligned rows");
+  if (ldo < N || (ldo * 4) % 16 != 0 || !ld32(ldo))
+    return fail(WDL_ERR_ARGUMENT, "ldo must be >= N (and < 2^31) with 16-byte aligned rows");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
   if (set_lowrank(g, lowrank) != WDL_OK) return WDL_ERR_ARGUMENT;
-  g.ep.mode = wdl::w4a4::kEpiResidualF32, g.ep.bias = bias, g.ep.residual = nullptr, g.ep.out = out, g.ep.ld_out = ldo;
+  g.ep.mode = wdl::w4a4::kEpiResidualF32, g.ep.bias = bias, g.ep.residual = nullptr, g.ep.out = out, g.ep.ld_out = static_cast<int>(ldo);
   return gemm_common(g, stream);
 }
 
 int wdl_w4a4_gemm_add(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                       const float* bias, const float* addend, int64_t ld_add, int M, int N, int K, uint16_t* y,
                       int64_t ldy, void* stream) {
-  if (ldy < N || (ldy * 2) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldy must be >= N with 16-byte aligned rows");
+  if (ldy < N || (ldy * 2) % 16 != 0 || !ld32(ldy))
+    return fail(WDL_ERR_ARGUMENT, "ldy must be >= N (and < 2^31) with 16-byte aligned rows");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
   if (set_addend(g, addend, ld_add, N) != WDL_OK) return WDL_ERR_ARGUMENT;
-  g.ep.mode = wdl::w4a4::kEpiBf16, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = ldy;
+  g.ep.mode = wdl::w4a4::kEpiBf16, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = static_cast<int>(ldy);
   return gemm_common(g, stream);
 }
 
@@ -313,24 +320,25 @@ int wdl_w4a4_gemm_residual_add(const void* a, const float* a_scales, const void*
                                const float* gate, const float* residual, int64_t ldr, int M, int N, int K, float* out,
                                int64_t ldo, void* stream) {
   if (!residual) return fail(WDL_ERR_ARGUMENT, "residual must not be null");
-  if (ldr < N || ldo < N || (ldr * 4) % 16 != 0 || (ldo * 4) % 16 != 0)
-    return fail(WDL_ERR_ARGUMENT, "ldr, ldo must be >= N with 16-byte aligned rows");
+  if (ldr < N || ldo < N || (ldr * 4) % 16 != 0 || (ldo * 4) % 16 != 0 || !ld32(ldr) || !ld32(ldo))
+    return fail(WDL_ERR_ARGUMENT, "ldr, ldo must be >= N (and < 2^31) with 16-byte aligned rows");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
   if (set_addend(g, addend, ld_add, N) != WDL_OK) return WDL_ERR_ARGUMENT;
   g.ep.mode = wdl::w4a4::kEpiResidualF32, g.ep.bias = bias, g.ep.gate = gate;
-  g.ep.residual = residual, g.ep.ld_res = ldr, g.ep.out = out, g.ep.ld_out = ldo;
+  g.ep.residual = residual, g.ep.ld_res = static_cast<int>(ldr), g.ep.out = out, g.ep.ld_out = static_cast<int>(ldo);
   return gemm_common(g, stream);
 }
 
 int wdl_w4a4_gemm_f32(const void* a, const float* a_scales, const void* w, const float* w_scales, int code_format,
                       const float* bias, const float* addend, int64_t ld_add, int M, int N, int K, float* out,
                       int64_t ldo, void* stream) {
-  if (ldo < N || (ldo * 4) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldo must be >= N with 16-byte aligned rows");
+  if (ldo < N || (ldo * 4) % 16 != 0 || !ld32(ldo))
+    return fail(WDL_ERR_ARGUMENT, "ldo must be >= N (and < 2^31) with 16-byte aligned rows");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
   if (set_addend(g, addend, ld_add, N) != WDL_OK) return WDL_ERR_ARGUMENT;
-  g.ep.mode = wdl::w4a4::kEpiResidualF32, g.ep.bias = bias, g.ep.residual = nullptr, g.ep.out = out, g.ep.ld_out = ldo;
+  g.ep.mode = wdl::w4a4::kEpiResidualF32, g.ep.bias = bias, g.ep.residual = nullptr, g.ep.out = out, g.ep.ld_out = static_cast<int>(ldo);
   return gemm_common(g, stream);
 }
 
@@ -338,10 +346,11 @@ int wdl_w4a4_gemm_group_partials(const void* a, const float* a_scales, const voi
                                  int code_format, int M, int N, int K, int group, int32_t* out, int64_t ldo,
                                  void* stream) {
   if (group < 0 || K <= 0 || group >= K / 64) return fail(WDL_ERR_ARGUMENT, "group out of range");
-  if (ldo < N || (ldo * 4) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldo must be >= N with 16-byte aligned rows");
+  if (ldo < N || (ldo * 4) % 16 != 0 || !ld32(ldo))
+    return fail(WDL_ERR_ARGUMENT, "ldo must be >= N (and < 2^31) with 16-byte aligned rows");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
-  g.ep.mode = wdl::w4a4::kEpiDumpGroup, g.ep.out = out, g.ep.ld_out = ldo, g.ep.dump_group = group;
+  g.ep.mode = wdl::w4a4::kEpiDumpGroup, g.ep.out = out, g.ep.ld_out = static_cast<int>(ldo), g.ep.dump_group = group;
   return gemm_common(g, stream);
 }
 
@@ -381,18 +390,19 @@ static int gelu_u4_impl(const void* a, const float* a_scales, const void* w, con
                         const float* bias, const float* addend, int64_t ld_add, const wdl_lowrank* lowrank,
                         const uint16_t* smooth_next, float shift, int scale_dtype, int M, int N, int K, uint8_t* codes,
                         int64_t ldc, float* scales, float* gelu_out, int64_t ld_gelu, void* stream) {
-  if (gelu_out && (ld_gelu < N || !aligned(gelu_out, 4))) return fail(WDL_ERR_ARGUMENT, "gelu_out rows must hold N floats");
+  if (gelu_out && (ld_gelu < N || !ld32(ld_gelu) || !aligned(gelu_out, 4)))
+    return fail(WDL_ERR_ARGUMENT, "gelu_out rows must hold N floats (ld_gelu < 2^31)");
   if (code_format == WDL_CODES_INT8)
     return fail(WDL_ERR_ARGUMENT, "the unsigned hidden codes need an E4M3 or float16 code format");
   if (scale_dtype != WDL_BF16 && scale_dtype != WDL_F16) return fail(WDL_ERR_ARGUMENT, "scale dtype must be bf16 or f16");
-  if (ldc < N || ldc % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldc must be >= N and a multiple of 16");
+  if (ldc < N || ldc % 16 != 0 || !ld32(ldc)) return fail(WDL_ERR_ARGUMENT, "ldc must be >= N (and < 2^31) and a multiple of 16");
   if (!aligned(codes, 16)) return fail(WDL_ERR_ARGUMENT, "codes must be 16-byte aligned");
   if (!scales) return fail(WDL_ERR_ARGUMENT, "null scales");
   wdl::w4a4::GemmArgs g{};
   operands(g, a, a_scales, w, w_scales, code_format, M, N, K);
   if (set_addend(g, addend, ld_add, N) != WDL_OK || set_lowrank(g, lowrank) != WDL_OK) return WDL_ERR_ARGUMENT;
-  g.ep.gelu_out = gelu_out, g.ep.ld_gelu = ld_gelu;
-  g.ep.mode = wdl::w4a4::kEpiGeluU4, g.ep.bias = bias, g.ep.out = codes, g.ep.ld_out = ldc, g.ep.out_scales = scales;
+  g.ep.gelu_out = gelu_out, g.ep.ld_gelu = static_cast<int>(ld_gelu);
+  g.ep.mode = wdl::w4a4::kEpiGeluU4, g.ep.bias = bias, g.ep.out = codes, g.ep.ld_out = static_cast<int>(ldc), g.ep.out_scales = scales;
   g.ep.out_smooth = reinterpret_cast<const __nv_bfloat16*>(smooth_next), g.ep.out_scale_dtype = scale_dtype;
   g.ep.gelu_shift = shift;
   return gemm_common(g, stream);
@@ -405,8 +415,9 @@ namespace wdl {
 // limits), so that a linear the GEMM would refuse is refused before its quantizer writes anything.
 int linear_gemm_args(w4a4::GemmArgs& g, const void* codes, const float* scales, const void* w, const float* w_scales,
                      int code_format, const float* bias, int M, int N, int K, uint16_t* y, int64_t ldy) {
+  if (ldy > INT32_MAX) return fail(WDL_ERR_ARGUMENT, "ldy must be < 2^31");
   operands(g, codes, scales, w, w_scales, code_format, M, N, K);
-  g.ep.mode = w4a4::kEpiBf16, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = ldy;
+  g.ep.mode = w4a4::kEpiBf16, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = static_cast<int>(ldy);
   if (!codes || !scales || !w || !w_scales || !y) return fail(WDL_ERR_ARGUMENT, "null operand pointer");
   if (!aligned(y, 16)) return fail(WDL_ERR_ARGUMENT, "output must be 16-byte aligned");
   const char* why = "";
@@ -431,7 +442,8 @@ int wdl_w4a4_linear(const uint16_t* x, int64_t ldx, int M, int K, const uint16_t
   if (M < 0) return fail(WDL_ERR_ARGUMENT, "M must be >= 0");
   if (M == 0) return ok();
   if (K % 128 != 0 || N % 256 != 0) return fail(WDL_ERR_ARGUMENT, "K % 128 == 0 and N % 256 == 0 required");
-  if (ldy < N || (ldy * 2) % 16 != 0) return fail(WDL_ERR_ARGUMENT, "ldy must be >= N with 16-byte aligned rows");
+  if (ldy < N || (ldy * 2) % 16 != 0 || !ld32(ldy))
+    return fail(WDL_ERR_ARGUMENT, "ldy must be >= N (and < 2^31) with 16-byte aligned rows");
   if (!valid_codes(code_format)) return fail(WDL_ERR_ARGUMENT, "unknown code format %d", code_format);
   const size_t need = wdl_w4a4_linear_workspace(M, K);
   if (!workspace || workspace_bytes < need)

@@ -36,31 +36,32 @@ enum EpilogueMode : int {
   kEpiGeluU4 = 3,       // out codes [M, N] (E4M3) + out_scales [N / 64, M]: unsigned INT4 of GELU(acc + bias) + shift
 };
 
+// The kernels take this block by value as a launch parameter. It is kept within 128 bytes: on B200 the same
+// kernels with a 160-byte block (the low-rank fields appended to 64-bit strides) ran their epilogues far slower,
+// the GELU-requantizing one 1.5x (FFN-1, M 1392: 176 us against 116 us), with the same registers and no spills;
+// packed to 128 bytes they are back at 116 us. Hence 32-bit leading dimensions, range-checked by the callers.
 struct GemmEpilogue {
   int mode;
+  int dump_group;         // kEpiDumpGroup
   const float* ascale;    // [K / 64, M] activation group scales ([M] row powers of two for kCodesF16Pre)
   const float* bias;      // [N] or null
   const float* gate;      // [N] or null (kEpiResidualF32)
   const float* residual;  // [M, ld_res] f32 (kEpiResidualF32)
-  int64_t ld_res;
-  void* out;  // bf16, f32 or int32 per mode, row stride ld_out elements
-  int64_t ld_out;
-  int dump_group;  // kEpiDumpGroup
+  void* out;              // bf16, f32 or int32 per mode, row stride ld_out elements
   float* out_scales;                // kEpiGeluU4: [N / 64, M] group scales of the hidden codes
   const __nv_bfloat16* out_smooth;  // kEpiGeluU4: [N] the next layer's smoothing (nullable)
-  int out_scale_dtype;              // kEpiGeluU4: 0 bf16, 1 f16 rounding of the stored scales
-  float gelu_shift;                 // kEpiGeluU4: added after GELU (0.171875)
   const float* addend;  // [M, ld_add] f32 added to the product before bias (the low-rank branch), nullable
-  int64_t ld_add;
   float* gelu_out;  // kEpiGeluU4: [M, ld_gelu] f32 GELU(y) before shift and smoothing (the next low-rank input), nullable
-  int64_t ld_gelu;
   // The low-rank branch formed in the epilogue instead of an addend: y += lr_act[m, :] . lr_up[n, :] over lr_rank
   // (a multiple of 4): lr_act [M, lr_ld] f32 = x proj_down, lr_up [N, lr_rank] f32 = proj_up. Nullable.
   const float* lr_act;
-  int64_t lr_ld;
   const float* lr_up;
+  int ld_res, ld_out, ld_add, ld_gelu, lr_ld;  // row strides in elements
+  int out_scale_dtype;  // kEpiGeluU4: 0 bf16, 1 f16 rounding of the stored scales
+  float gelu_shift;     // kEpiGeluU4: added after GELU (0.171875)
   int lr_rank;
 };
+static_assert(sizeof(GemmEpilogue) <= 128, "the epilogue parameter block must stay within 128 bytes");
 
 #ifdef __CUDACC__
 // Adds row m, columns [n0, n0 + kCount) of the low-rank branch's product into acc (before the bias), when the

@@ -98,9 +98,10 @@ __device__ __forceinline__ void finish_tile(float (&acc)[128], const GemmEpilogu
           const float gn = ep.gate ? __ldg(ep.gate + n) : 0.f;
           float* out = reinterpret_cast<float*>(ep.out) + n;
           const float* res = ep.residual + n;
-          float x[32];  // all 32 rows' residuals in flight at once
+          float x[32];  // all 32 rows' residuals in flight at once: unconditional loads (rows past M read the last
+                        // row, their values unused), so that nothing holds one load back behind another
 #pragma unroll
-          for (int r = 0; r < 32; ++r) x[r] = m0 + r < M ? res[static_cast<size_t>(m0 + r) * ep.ld_res] : 0.f;
+          for (int r = 0; r < 32; ++r) x[r] = res[static_cast<size_t>(min(m0 + r, M - 1)) * ep.ld_res];
 #pragma unroll
           for (int r = 0; r < 32; ++r) {
             const float o = bf16_round(tw[r * 33 + lane] + bn);
