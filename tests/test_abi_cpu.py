@@ -56,6 +56,8 @@ def test_gemm_shapes_rejected_before_any_launch(native):
     assert st == native.ERR_ARGUMENT and b"multiple of 128" in lib.wdl_last_error()
     st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE + 8, FAKE, native.CODES_E4M3, None, 128, 256, 256, FAKE, 256, None)
     assert st == native.ERR_ARGUMENT and b"16-byte" in lib.wdl_last_error()
+    st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_F16_PRE, FAKE + 4, 128, 256, 256, FAKE, 256, None)
+    assert st == native.ERR_ARGUMENT and b"bias" in lib.wdl_last_error()  # the epilogue loads it 16 bytes at a time
     st = lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, 7, None, 128, 256, 256, FAKE, 256, None)
     assert st == native.ERR_ARGUMENT and b"code format" in lib.wdl_last_error()
     assert lib.wdl_w4a4_gemm(FAKE, FAKE, FAKE, FAKE, native.CODES_E4M3, None, 0, 256, 256, FAKE, 256, None) == 0

@@ -186,8 +186,8 @@ static int gemm_common(wdl::w4a4::GemmArgs& a, void* stream) {
   if (a.M < 0) return fail(WDL_ERR_ARGUMENT, "M must be >= 0");
   if (a.M == 0) return ok();
   if (!a.a || !a.b || !a.wscale || !a.ep.ascale || !a.ep.out) return fail(WDL_ERR_ARGUMENT, "null operand pointer");
-  if (!aligned(a.ep.out, 16) || (a.ep.residual && !aligned(a.ep.residual, 16)))
-    return fail(WDL_ERR_ARGUMENT, "output and residual must be 16-byte aligned");
+  if (!aligned(a.ep.out, 16) || (a.ep.residual && !aligned(a.ep.residual, 16)) || (a.ep.bias && !aligned(a.ep.bias, 16)))
+    return fail(WDL_ERR_ARGUMENT, "output, residual and bias must be 16-byte aligned");
   const int f = a.code_format;
   const char* why = "";
   const int v = folded(f) ? wdl::w4a4::gemm_fold_validate(a, &why) : wdl::w4a4::gemm_validate(a, &why);
@@ -419,7 +419,7 @@ int linear_gemm_args(w4a4::GemmArgs& g, const void* codes, const float* scales, 
   operands(g, codes, scales, w, w_scales, code_format, M, N, K);
   g.ep.mode = w4a4::kEpiBf16, g.ep.bias = bias, g.ep.out = y, g.ep.ld_out = static_cast<int>(ldy);
   if (!codes || !scales || !w || !w_scales || !y) return fail(WDL_ERR_ARGUMENT, "null operand pointer");
-  if (!aligned(y, 16)) return fail(WDL_ERR_ARGUMENT, "output must be 16-byte aligned");
+  if (!aligned(y, 16) || (bias && !aligned(bias, 16))) return fail(WDL_ERR_ARGUMENT, "output and bias must be 16-byte aligned");
   const char* why = "";
   const int v = folded(code_format) ? w4a4::gemm_fold_validate(g, &why) : w4a4::gemm_validate(g, &why);
   if (v != 0) return fail(WDL_ERR_ARGUMENT, "%s", why);
