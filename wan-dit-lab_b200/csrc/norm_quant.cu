@@ -58,6 +58,27 @@ __device__ __forceinline__ float block_sum128(float v, float* red) {
   return (red[0] + red[1]) + (red[2] + red[3]);
 }
 
+// The CTA's sum (kWarps warps), its warps' sums added pairwise in a fixed order.
+template <int kWarps>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  if constexpr (kWarps == 4) {
+    return block_sum128(v, red);
+  } else {
+    v = warp_sum(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float p[kWarps];
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) p[i] = red[i];
+#pragma unroll
+    for (int w = 1; w < kWarps; w *= 2)
+#pragma unroll
+      for (int i = 0; i + w < kWarps; i += 2 * w) p[i] += p[i + w];
+    return p[0];
+  }
+}
+
 __device__ __forceinline__ uint32_t code_byte(int q, int fmt) {
   return fmt != 0 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(static_cast<float>(q), __NV_SATFINITE, __NV_E4M3))
                   : (static_cast<uint32_t>(q) & 0xFFu);
@@ -66,40 +87,45 @@ __device__ __forceinline__ uint32_t code_byte(int q, int fmt) {
 // kKeep: also write the bf16 layer input to a.x_out. kPre: code format 4, the prescaled float16 activations
 // float16(code * stored scale * 2^-E_m) with the row's 2^E_m in a.scales[m] (E_m from the row's largest stored
 // scale, as quantize_rows_pre_kernel: w4a4_quant.cu); the codes and scales are those of the other formats.
-template <typename TX, bool kKeep, bool kPre>
-__global__ void __launch_bounds__(kRowThreads, kPre ? 4 : 6) ln_quant_kernel(const TX* __restrict__ x, LnQuantArgs a) {
-  __shared__ float red[kRowThreads / 32];
+// kThreads threads per row, kChunks chunks of kThreads * 8 channels (kThreads * 8 * kChunks >= K). The prescaled
+// format with K <= 3072 runs 384 threads, one chunk each: a thread's dependent chain of loads and arithmetic is
+// what bounds these rows, and one chunk a thread shortens it threefold.
+template <typename TX, bool kKeep, bool kPre, int kThreads = kRowThreads, int kChunks = kRowChunks>
+__global__ void __launch_bounds__(kThreads, kThreads == 128 ? (kPre ? 4 : 6) : 3)
+    ln_quant_kernel(const TX* __restrict__ x, LnQuantArgs a) {
+  constexpr int kWarps = kThreads / 32, kStride = kThreads * 8;
+  __shared__ float red[kWarps];
   const int t = threadIdx.x, m = blockIdx.x;
   const int K = a.K;
   const TX* row = x + static_cast<int64_t>(m) * a.ldx;
-  float v[kRowChunks][8];
+  float v[kChunks][8];
   float s = 0.f;
 #pragma unroll
-  for (int c = 0; c < kRowChunks; ++c) {
-    const int k = c * 1024 + t * 8;
+  for (int c = 0; c < kChunks; ++c) {
+    const int k = c * kStride + t * 8;
     if (k < K) {
       load8<TX>(row + k, v[c]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) s += v[c][i];
     }
   }
-  const float mean = __fdiv_rn(block_sum128(s, red), static_cast<float>(K));
+  const float mean = __fdiv_rn(block_sum<kWarps>(s, red), static_cast<float>(K));
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < kRowChunks; ++c)
-    if (c * 1024 + t * 8 < K)
+  for (int c = 0; c < kChunks; ++c)
+    if (c * kStride + t * 8 < K)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float d = v[c][i] - mean;
         ss = fmaf(d, d, ss);
       }
-  const float rstd = __frsqrt_rn(__fadd_rn(__fdiv_rn(block_sum128(ss, red), static_cast<float>(K)), a.eps));
+  const float rstd = __frsqrt_rn(__fadd_rn(__fdiv_rn(block_sum<kWarps>(ss, red), static_cast<float>(K)), a.eps));
   uint8_t* codes = a.codes + static_cast<int64_t>(m) * K;
-  float pre_scale[kRowChunks], pre_stored[kRowChunks];  // kPre: each chunk's group scale and stored scale
+  float pre_scale[kChunks], pre_stored[kChunks];  // kPre: each chunk's group scale and stored scale
 #pragma unroll
-  for (int c = 0; c < kRowChunks; ++c) {
-    if (c * 1024 >= K) break;  // uniform over the CTA
-    const int k = c * 1024 + t * 8;
+  for (int c = 0; c < kChunks; ++c) {
+    if (c * kStride >= K) break;  // uniform over the CTA
+    const int k = c * kStride + t * 8;
     const bool valid = k < K;  // uniform over each group of 8 threads
     float y[8];
     if (valid) {
@@ -181,22 +207,24 @@ __global__ void __launch_bounds__(kRowThreads, kPre ? 4 : 6) ln_quant_kernel(con
   if constexpr (kPre) {
     float top = 0.f;
 #pragma unroll
-    for (int c = 0; c < kRowChunks; ++c)
-      if (c * 1024 < K) top = fmaxf(top, pre_stored[c]);
+    for (int c = 0; c < kChunks; ++c)
+      if (c * kStride < K) top = fmaxf(top, pre_stored[c]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xFFFFFFFFu, top, o));
     __syncthreads();
     if ((t & 31) == 0) red[t >> 5] = top;
     __syncthreads();
-    top = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    top = red[0];
+#pragma unroll
+    for (int i = 1; i < kWarps; ++i) top = fmaxf(top, red[i]);
     const uint32_t e = (__float_as_uint(top) >> 23) & 0xFFu;  // 8 top 2^(138-e) in [2^14, 2^15)
     const float down = __uint_as_float((265u - e) << 23);
     if (t == 0) a.scales[m] = __uint_as_float((e - 11u) << 23);  // 2^(e - 138)
     uint16_t* out = reinterpret_cast<uint16_t*>(a.codes) + static_cast<int64_t>(m) * K;
     bool inexact = false;
 #pragma unroll
-    for (int c = 0; c < kRowChunks; ++c) {
-      const int k = c * 1024 + t * 8;
+    for (int c = 0; c < kChunks; ++c) {
+      const int k = c * kStride + t * 8;
       if (k >= K) continue;
       const float scale = pre_scale[c], stored = pre_stored[c];
       const float r = __frcp_rn(scale);
@@ -225,6 +253,15 @@ void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s) {
   using T_ = std::true_type;
   using F_ = std::false_type;
   const bool pre = a.code_format == 4, keep = a.x_out != nullptr;
+  if (pre && a.K <= 3072) {  // 384 threads a row, one chunk each
+    auto go384 = [&](auto xt, auto kp) {
+      using TX = decltype(xt);
+      ln_quant_kernel<TX, decltype(kp)::value, true, 384, 1><<<a.M, 384, 0, s>>>(static_cast<const TX*>(a.x), a);
+    };
+    if (a.x_f32) keep ? go384(float{}, T_{}) : go384(float{}, F_{});
+    else keep ? go384(__nv_bfloat16{}, T_{}) : go384(__nv_bfloat16{}, F_{});
+    return;
+  }
   if (a.x_f32) {
     if (pre) keep ? go(float{}, T_{}, T_{}) : go(float{}, F_{}, T_{});
     else keep ? go(float{}, T_{}, F_{}) : go(float{}, F_{}, F_{});
