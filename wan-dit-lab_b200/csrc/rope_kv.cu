@@ -189,10 +189,11 @@ void rope_launch(const RopeArgs& a, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------------------------------------
-// qkv_prep: one CTA of 128 threads per token. Row layout: q | k | v, each H * 128 bf16 (dim = H * 128).
-// Thread t holds 8 consecutive channels of each 1024-channel pass; 16 lanes cover one head of 128 channels.
-constexpr int kPrepThreads = 128;
-
+// qkv_prep: one CTA of kThreads threads per token. Row layout: q | k | v, each H * 128 bf16 (dim = H * 128).
+// Thread t holds 8 consecutive channels of each (kThreads * 8)-channel pass; 16 lanes cover one head of 128
+// channels. dim <= 3072 runs 384 threads, one pass: a thread's dependent chain of loads, reductions and stores
+// bounds these rows (128 threads and three passes measured slower).
+template <int kWarps>
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
@@ -202,7 +203,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   __syncthreads();
   float s = 0.f;
 #pragma unroll
-  for (int w = 0; w < kPrepThreads / 32; ++w) s += red[w];
+  for (int w = 0; w < kWarps; ++w) s += red[w];
   return s;
 }
 
@@ -226,12 +227,13 @@ __device__ __forceinline__ uint2 e4m3x8(const float (&y)[8], float scale) {
   return make_uint2(w[0], w[1]);
 }
 
-template <int kPasses>
-__global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
-  __shared__ float red[kPrepThreads / 32];
+template <int kThreads, int kPasses>
+__global__ void __launch_bounds__(kThreads) qkv_prep_kernel(QkvPrepArgs a) {
+  constexpr int kStride = kThreads * 8;
+  __shared__ float red[kThreads / 32];
   const int t = blockIdx.x;  // token of the chunk
   const int tid = threadIdx.x;
-  const int dim = a.dim;  // this call's channels of q (a multiple of 128, at most kPasses * 1024)
+  const int dim = a.dim;  // this call's channels of q (a multiple of 128, at most kPasses * kStride)
   const __nv_bfloat16* row = a.qkv + static_cast<int64_t>(t) * a.ld_qkv;
   const int gh = a.grid_h, gw = a.grid_w;
   const int pos_t = a.start + t / (gh * gw), pos_h = t / gw % gh, pos_w = t % gw;
@@ -246,7 +248,7 @@ __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
     float ss = 0.f;
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
-      const int c0 = p * 1024 + tid * 8;
+      const int c0 = p * kStride + tid * 8;
       if (c0 < dim) {
         load8_bf16(row + part * dim + c0, v[p]);
       } else {
@@ -256,13 +258,13 @@ __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss = fmaf(v[p][i], v[p][i], ss);
     }
-    const float own = block_sum(ss, red);
+    const float own = block_sum<kThreads / 32>(ss, red);
     const float total = a.sumsq ? __ldg(a.sumsq + static_cast<int64_t>(t) * 2 + part) : own;
     const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(a.norm_dim)), a.eps));
     const float* w = part == 0 ? a.norm_q : a.norm_k;
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
-      const int c0 = p * 1024 + tid * 8;  // channel of v[p][0]
+      const int c0 = p * kStride + tid * 8;  // channel of v[p][0]
       const bool act = c0 < dim;
       const int head = c0 >> 7, d0 = c0 & 127;
       float y[8];
@@ -308,7 +310,7 @@ __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
   if (a.cache_v) {
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
-      const int c0 = p * 1024 + tid * 8;
+      const int c0 = p * kStride + tid * 8;
       const bool act = c0 < dim;
       const int head = c0 >> 7, d0 = c0 & 127;
       float y[8];
@@ -335,12 +337,11 @@ __global__ void __launch_bounds__(kPrepThreads) qkv_prep_kernel(QkvPrepArgs a) {
 }
 
 void qkv_prep_launch(const QkvPrepArgs& a, cudaStream_t s) {
-  switch ((a.dim + 1023) / 1024) {
-    case 1: qkv_prep_kernel<1><<<a.n, kPrepThreads, 0, s>>>(a); break;
-    case 2: qkv_prep_kernel<2><<<a.n, kPrepThreads, 0, s>>>(a); break;
-    case 3: qkv_prep_kernel<3><<<a.n, kPrepThreads, 0, s>>>(a); break;
-    default: qkv_prep_kernel<4><<<a.n, kPrepThreads, 0, s>>>(a); break;
+  if (a.dim <= 3072) {
+    qkv_prep_kernel<384, 1><<<a.n, 384, 0, s>>>(a);
+    return;
   }
+  qkv_prep_kernel<128, 4><<<a.n, 128, 0, s>>>(a);
 }
 
 }  // namespace ropekv
