@@ -199,12 +199,13 @@ def test_block_with_lowrank_branches_and_smoothing_matches_oracle(rank):
     d_got, d_exp = Xd.cpu().numpy() - X.numpy(), expected - X.numpy()
     err = float(np.linalg.norm(d_got - d_exp) / np.linalg.norm(d_exp))
     print(f"rank {rank} block: residual update relative L2 vs oracle {err:.4f}")
-    # each linear within the stated bar (bf16 relative L2 <= 1e-2); the block as a whole within 5e-2: the branch's
-    # float32 products are summed in another order by the library GEMM than by numpy, and the few bf16 outputs
-    # that round the other way move INT8 K codes, FP8 P and the hidden INT4 codes across rounding boundaries
-    # downstream (at rank 0 there is no such sum and the block stays within 2e-2)
+    # each linear within the stated bar (bf16 relative L2 <= 1e-2); the block as a whole within BLOCK_BAR, the bar
+    # every block test derives from the attention and linear bars: the branch's float32 products are summed in
+    # another order by the kernels than by numpy, and the few bf16 outputs that round the other way move INT8 K
+    # codes, FP8 P and the hidden INT4 codes across rounding boundaries downstream (measured 0.050 here, the
+    # hidden codes' share the largest; at rank 0 there is no such sum and the block stays within 2e-2)
     assert stages["qkv"] <= 1e-3 and stages["cq"] <= 1e-2
-    assert err <= 5e-2
+    assert err <= BLOCK_BAR
     for name, gpu in (("k", cache[0]), ("v", cache[2])):
         assert (gpu[at:at + n].cpu().numpy() == ocache[name][0, at:at + n]).mean() > 0.99
 

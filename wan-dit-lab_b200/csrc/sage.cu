@@ -221,43 +221,92 @@ __device__ __forceinline__ void v_token_tile(const Source& vs, const VTok& vt, i
   if (threadIdx.x == 0) vt.tile_max[static_cast<int64_t>(tile) * vs.H + h] = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
 }
 
-__global__ void __launch_bounds__(128) partials_kernel(Source ks, Source vs, float* ksum, float* vmax, VTok vt) {
-  __shared__ float red[4][128];
+// Per channel d of head h over the keys of the 64-key tile: their sum (kMax false) or largest |x| (kMax true), into
+// out[d] by thread d. Warp w takes keys 16 w .. 16 w + 15. Cached keys (FP8): lane (sub, seg) = (lane / 8, lane % 8)
+// reads the 16 bytes of channels 16 seg .. + 15 of keys 16 w + 4 r + sub (r = 0..3), one 16-byte load each, and
+// folds them in as they are dequantized; chunk or mixed keys: lane l channels 4 l .. + 3 of the 16 keys in two
+// batches of 8. The CTA then combines its 16 partials per channel (warp-major, sub-group-minor, a fixed order).
+// Few registers a thread, so that many CTAs are resident (at 95 registers five were, and the grid ran in seven
+// waves of long-scoreboard stalls).
+template <bool kMax>
+__device__ __forceinline__ void tile_reduce(const Source& src, int tile, int h, float (&red)[4][4][128], float* out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j0 = tile * 64 + warp * 16;
+  const int where = src.where(j0, min(src.L, j0 + 16));
+  if (where == 1) {
+    const int sub = lane >> 3, seg = lane & 7;
+    const int ch = src.cache_head(h);
+    uint4 w[4];
+    float sc[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int j = j0 + 4 * r + sub;
+      const bool ok = j < src.L;
+      const int64_t row = (ok ? src.cache_row(j) : 0) * src.cache_H + ch;
+      w[r] = ok ? __ldg(reinterpret_cast<const uint4*>(src.cache + row * 128 + seg * 16)) : make_uint4(0u, 0u, 0u, 0u);
+      sc[r] = ok ? __ldg(src.scale + row) : 0.f;
+    }
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const uint32_t u[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __half2 lo(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(u[q] & 0xFFFFu), __NV_E4M3));
+        const __half2 hi(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(u[q] >> 16), __NV_E4M3));
+        const float2 a = __half22float2(lo), b = __half22float2(hi);
+        const float x[4] = {a.x * sc[r], a.y * sc[r], b.x * sc[r], b.y * sc[r]};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[4 * q + c] = kMax ? fmaxf(acc[4 * q + c], fabsf(x[c])) : acc[4 * q + c] + x[c];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) red[warp][sub][seg * 16 + i] = acc[i];
+  } else {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      int j[8];
+      bool valid[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) j[i] = j0 + 8 * half + i, valid[i] = j[i] < src.L;
+      float x[8][4];
+      src.gather4(j, valid, src.where(j[0], min(src.L, j[0] + 8)), h, lane * 4, x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)  // keys in order
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[c] = kMax ? fmaxf(acc[c], fabsf(x[i][c])) : acc[c] + x[i][c];
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      red[warp][0][lane * 4 + c] = acc[c];
+      red[warp][1][lane * 4 + c] = red[warp][2][lane * 4 + c] = red[warp][3][lane * 4 + c] = 0.f;
+    }
+  }
+  __syncthreads();
+  const int d = threadIdx.x;
+  float r = 0.f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int sub = 0; sub < 4; ++sub) r = kMax ? fmaxf(r, red[w][sub][d]) : r + red[w][sub][d];
+  out[d] = r;
+}
+
+__global__ void __launch_bounds__(128, 8) partials_kernel(Source ks, Source vs, float* ksum, float* vmax, VTok vt) {
+  __shared__ float red[4][4][128];
   const int tile = blockIdx.x, h = blockIdx.y;
   const bool is_v = blockIdx.z != 0;
   if (is_v && vt.on) {  // the grid spans Lpad / 64 tiles: the scales of the padding keys are written as 0
-    v_token_tile(vs, vt, tile, h, red);
+    v_token_tile(vs, vt, tile, h, red[0]);
     return;
   }
   if (tile * 64 >= ks.L) return;
-  const Source& src = is_v ? vs : ks;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const int j0 = tile * 64 + warp * 16;
-  int j[16];
-  bool valid[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) j[i] = j0 + i, valid[i] = j[i] < src.L;
-  float x[16][4];
-  src.gather4(j, valid, src.where(j0, min(src.L, j0 + 16)), h, lane * 4, x);
-  if (is_v) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[c] = fmaxf(acc[c], fabsf(x[i][c]));
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i)  // keys in order
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[c] += x[i][c];
-  }
-#pragma unroll
-  for (int c = 0; c < 4; ++c) red[warp][lane * 4 + c] = acc[c];
-  __syncthreads();
-  const int d = threadIdx.x;
-  const int64_t o = (static_cast<int64_t>(tile) * ks.H + h) * 128 + d;
-  if (is_v) vmax[o] = fmaxf(fmaxf(red[0][d], red[1][d]), fmaxf(red[2][d], red[3][d]));
-  else ksum[o] = (red[0][d] + red[1][d]) + (red[2][d] + red[3][d]);
+  const int64_t o = (static_cast<int64_t>(tile) * ks.H + h) * 128;
+  if (is_v) tile_reduce<true>(vs, tile, h, red, vmax + o);
+  else tile_reduce<false>(ks, tile, h, red, ksum + o);
 }
 
 // ---- pass 2: per head: key mean (sum / L) and the V channel scales max(max|V|, 1e-8) / 2.25 (V_MAX, :24). CTA
@@ -331,21 +380,22 @@ __device__ __forceinline__ uint32_t sage_i8(float x, float scale, float rcp) {
   return static_cast<uint32_t>(static_cast<int>(truncf(__fadd_rn(y, y >= 0.f ? 0.5f : -0.5f)))) & 0xFFu;
 }
 
-// ---- pass 3: K - mean to INT8 and V to FP8, per (64-key block, head). 128 threads.
-// K (_quant_k, sage_kv.py:60-85): warp g holds the 16 keys 8 i + 2 g, 8 i + 2 g + 1 (i = 0..7) of the block,
-// lane l channels 4 l .. 4 l + 3; scale = max|x| / 127 + 1e-7 over the 16 x 128 values; code = trunc(x / scale
-// + 0.5 sign(x)). V (_quant_v, :89-105): warp g keys 16 g .. 16 g + 15, lane l channels 4 l .. 4 l + 3, each
+// ---- pass 3: K - mean to INT8 (kV false) or V to FP8 (kV true), per (64-key block, head). 128 threads.
+// K (_quant_k, sage_kv.py:60-85): warp g holds the 16 keys 8 i + 2 g, 8 i + 2 g + 1 (i = 0..7) of the block;
+// scale = max|x| / 127 + 1e-7 over the 16 x 128 values; code = trunc(x / scale + 0.5 sign(x)).
+// V (_quant_v, :89-105): warp g keys 16 g .. 16 g + 15, lane l channels 4 l .. 4 l + 3, each
 // V / v_scale[d] rounded to E4M3; the codes are transposed through shared memory (each lane packs its 16 keys
 // of a channel into one 16-byte store) and leave as one 64-byte row segment per channel.
 constexpr int kVtPitch = 80;  // bytes per channel row of the transpose tile: 16-byte aligned, reads conflict-free
 
+template <bool kV>
 __global__ void __launch_bounds__(128) quant_kv_kernel(Source ks, Source vs, const float* kmean, const float* v_scale,
                                                        int Lpad, int8_t* k_i8, float* k_scale, uint8_t* v_f8) {
-  __shared__ __align__(16) uint8_t vt[128 * kVtPitch];
+  __shared__ __align__(16) uint8_t vt[kV ? 128 * kVtPitch : 16];
   const int blk = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int L = ks.L;
-  if (blockIdx.z == 0) {  // K and V in separate CTAs (one round of loads each)
+  if constexpr (!kV) {
     const int g = warp;
     const float4 mean = *reinterpret_cast<const float4*>(kmean + h * 128 + lane * 4);
     float x[16][4];
@@ -475,8 +525,9 @@ void prep_kv_launch(const PrepArgs& a, cudaStream_t s) {
   partials_kernel<<<dim3(a.token_v ? Lpad / 64 : tiles, a.H, 2), 128, 0, s>>>(ks, vs, ksum, vmax, vt);
   reduce_kernel<<<dim3(a.H, 4), 128, 0, s>>>(ksum, vmax, tiles, a.H, L, kmean, a.v_scale, a.token_v ? vmax : nullptr,
                                              Lpad / 64, a.v_head_max);
-  quant_kv_kernel<<<dim3(Lpad / 64, a.H, a.token_v ? 1 : 2), 128, 0, s>>>(ks, vs, kmean, a.v_scale, Lpad, a.k_i8,
-                                                                         a.k_scale, a.v_f8);
+  quant_kv_kernel<false><<<dim3(Lpad / 64, a.H), 128, 0, s>>>(ks, vs, kmean, a.v_scale, Lpad, a.k_i8, a.k_scale, a.v_f8);
+  if (!a.token_v)  // V per channel, in its own kernel (its registers would hold the K kernel to fewer CTAs)
+    quant_kv_kernel<true><<<dim3(Lpad / 64, a.H), 128, 0, s>>>(ks, vs, kmean, a.v_scale, Lpad, a.k_i8, a.k_scale, a.v_f8);
 }
 
 void quant_q_launch(const float* q, int64_t ld_q, int nq, int H, int8_t* q_i8, float* q_scale, cudaStream_t s) {
