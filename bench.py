@@ -228,9 +228,10 @@ def cpu_linear_sample(x, W, repeats=3):
         f"{torch.get_num_threads()} threads, mean of {repeats} calls")
 
 
-def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True, height=512, width=928):
+def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True, height=512, width=928, svd_rank=0):
     """tp = (world, reduce): one stream split across the ranks (tensor parallelism), else one stream per rank.
-    height x width pixels: 512 x 928 (464 tokens a frame) or 704 x 1280 (config 5, 880)."""
+    height x width pixels: 512 x 928 (464 tokens a frame) or 704 x 1280 (config 5, 880).
+    svd_rank: every layer's SVDQuant low-rank branch (0: none, BASELINE's configs; 32: the LongLive packs')."""
     from wan_dit_lab_b200.generation import causal
     from wan_dit_lab_b200.models.block import WanBlockB200
     from wan_dit_lab_b200.models.block_tp import WanBlockTP
@@ -239,7 +240,8 @@ def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True, 
     torch.manual_seed(0)
     world = 1 if tp is None else tp[0]
     model = causal.random_model(seed=6, device=device, num_layers=layers,
-                                shard=None if tp is None else (rank, world), reduce=None if tp is None else tp[1])
+                                shard=None if tp is None else (rank, world), reduce=None if tp is None else tp[1],
+                                svd_rank=svd_rank)
     block_cls = WanBlockB200 if tp is None else WanBlockTP
     seed_rank = rank if tp is None else 0  # the ranks of a split stream share its noise
     g = torch.Generator().manual_seed(8 + 1000 * seed_rank)  # one independent seeded stream per rank
@@ -296,7 +298,8 @@ def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True, 
                 launches_per_step=chunks * 5 * (1 + layers * (20 if tp is None else 25)),
                 h2d=noise.numel() * 4, d2h=noise.numel() * 4,
                 config={"workload": name,
-                        "model": "Wan2.2-TI2V-5B shape, random init N(0,0.02), W4A4 (INT4 g64, bf16 scales, rank 0)",
+                        "model": "Wan2.2-TI2V-5B shape, random init N(0,0.02), W4A4 (INT4 g64, bf16 scales, "
+                                 f"SVD rank {svd_rank})",
                         "tokens_per_chunk": tokens, "keys_per_chunk": [min(tokens * (c + 1), window) for c in range(chunks)],
                         "chunks": chunks, "layers": layers, **({} if tp is None else {"tensor_parallel": world}),
                         "cuda_graphs": bool(graphs and tp is None),
@@ -469,6 +472,9 @@ def main():
     parser.add_argument("--tp", action="store_true",
                         help="BASELINE config 5b: one stream split across the ranks (heads / hidden channels, NCCL "
                              "all-reduce after O, cross-O and FFN-2) instead of one independent stream per rank")
+    parser.add_argument("--svd-rank", type=int, default=0,
+                        help="rank of every layer's SVDQuant low-rank branch (BASELINE's configs: 0; the LongLive "
+                             "W4A4 packs: 32)")
     args = parser.parse_args()
     global CODES
     CODES = args.codes
@@ -495,7 +501,8 @@ def main():
     if args.tp and not rollout:
         parser.error("--tp splits the rollout")
     tp = (world, (lambda t: dist.all_reduce(t)) if dist is not None else (lambda t: None)) if args.tp else None
-    wl = (WORKLOADS[args.workload](device, rank, args.chunks, args.layers, tp, not args.eager, args.height, args.width)
+    wl = (WORKLOADS[args.workload](device, rank, args.chunks, args.layers, tp, not args.eager, args.height, args.width,
+                                   args.svd_rank)
           if rollout else WORKLOADS[args.workload](device))
     stream = torch.cuda.current_stream(device)
     flush_buf = torch.empty(512 << 20, dtype=torch.uint8, device=device)

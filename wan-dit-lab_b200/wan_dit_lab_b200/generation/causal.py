@@ -410,17 +410,20 @@ def random_block_state(g, dim, ffn_dim, device):
 
 
 def random_model(dim=3072, ffn_dim=14336, freq_dim=256, in_dim=48, out_dim=48, num_heads=24, num_layers=30,
-                 text_dim=4096, seed=6, device="cuda", shard=None, reduce=None):
+                 text_dim=4096, seed=6, device="cuda", shard=None, reduce=None, svd_rank=0):
     """A WanModelB200 of the Wan2.2-TI2V-5B shape with random-init weights (N(0, 0.02)),
     generated on `device` from one seed, one block at a time (each block's float weights are dropped once it
     is quantized to W4A4). shard = (rank, world): this rank's tensor-parallel shard of every block (every rank
     generates the same weights from the seed and keeps its heads and hidden channels); reduce: the in-place sum
-    across ranks (torch.distributed.all_reduce)."""
+    across ranks (torch.distributed.all_reduce). svd_rank: every layer's SVDQuant low-rank branch (0: none; the
+    LongLive W4A4 packs carry rank 32), one stream per GPU only."""
+    if svd_rank and shard is not None:
+        raise ValueError("svd_rank applies to one stream per GPU (the tensor-parallel blocks quantize at rank 0)")
     g = torch.Generator(device=device).manual_seed(seed)
     edges = random_state(dim, freq_dim=freq_dim, in_dim=in_dim, out_dim=out_dim, num_layers=0, text_dim=text_dim,
                          generator=g, device=device)
     if shard is None:
-        make = lambda st: WanBlockB200(st, dim, ffn_dim, num_heads, device=device)  # noqa: E731
+        make = lambda st: WanBlockB200(st, dim, ffn_dim, num_heads, device=device, svd_rank=svd_rank)  # noqa: E731
     else:
         from wan_dit_lab_b200.models.block_tp import WanBlockTP
         make = lambda st: WanBlockTP(st, dim, ffn_dim, num_heads, shard[0], shard[1], device=device,  # noqa: E731

@@ -70,17 +70,18 @@ class Buffers:
             self.gelu = torch.empty(n, ffn_dim, **f32)  # GELU's output in the feed forward (before the shift)
 
 
-def quantize_block(p, scale_dtype=torch.bfloat16):
-    """The W4A4 parts {layer: quantize() tensors} of a block's float weights p (the reference's names; rank 0; q, k
-    and v of self-attention as one qkv layer, FusedQKVAttention; ffn.2 made for gelu_mlp's shifted input)."""
+def quantize_block(p, scale_dtype=torch.bfloat16, rank=0):
+    """The W4A4 parts {layer: quantize() tensors} of a block's float weights p (the reference's names; SVDQuant
+    low-rank branches of `rank`, 0 for none; q, k and v of self-attention as one qkv layer, FusedQKVAttention; ffn.2
+    made for gelu_mlp's shifted input)."""
     parts = {}
     cat = lambda *names: torch.cat([p[n] for n in names])  # noqa: E731
     parts["self_attn.qkv"] = w4a4.quantize(cat("self_attn.q.weight", "self_attn.k.weight", "self_attn.v.weight"),
                                            cat("self_attn.q.bias", "self_attn.k.bias", "self_attn.v.bias"),
-                                           rank=0, scale_dtype=scale_dtype)
+                                           rank=rank, scale_dtype=scale_dtype)
     for name in ("self_attn.o", "cross_attn.q", "cross_attn.k", "cross_attn.v", "cross_attn.o", "ffn.0"):
-        parts[name] = w4a4.quantize(p[f"{name}.weight"], p[f"{name}.bias"], rank=0, scale_dtype=scale_dtype)
-    parts["ffn.2"] = w4a4.quantize(p["ffn.2.weight"], p["ffn.2.bias"], rank=0, shift=w4a4.GELU_SHIFT,
+        parts[name] = w4a4.quantize(p[f"{name}.weight"], p[f"{name}.bias"], rank=rank, scale_dtype=scale_dtype)
+    parts["ffn.2"] = w4a4.quantize(p["ffn.2.weight"], p["ffn.2.bias"], rank=rank, shift=w4a4.GELU_SHIFT,
                                    scale_dtype=scale_dtype)
     return parts
 
@@ -134,19 +135,19 @@ class CrossKV:
 class WanBlockB200:
     """One Wan block with its weights in the kernels' layouts, made from a WanBlock state dict (the reference's
     parameter names: self_attn.{q,k,v,o}, cross_attn.{q,k,v,o}, ffn.{0,2}, norm3, *.norm_q / norm_k, modulation).
-    Every linear layer is W4A4 (INT4 groups of 64): quantized here from float weights at rank 0, or given as
-    `parts` {layer: quantize() tensors} of a converted pack, with SVDQuant low-rank branches of any rank and
-    smoothing vectors."""
+    Every linear layer is W4A4 (INT4 groups of 64): quantized here from float weights (with SVDQuant low-rank
+    branches of svd_rank, 0 for none), or given as `parts` {layer: quantize() tensors} of a converted pack, with
+    low-rank branches of any rank and smoothing vectors."""
 
     def __init__(self, state, dim, ffn_dim, heads, eps=1e-6, device="cuda", parts=None, scale_dtype=torch.bfloat16,
-                 code_format=None):
+                 code_format=None, svd_rank=0):
         self.dim, self.ffn_dim, self.heads, self.eps = dim, ffn_dim, heads, eps
         self.kv_heads = heads  # the heads of this process's KV cache and attention
         if dim != heads * HEAD_DIM:
             raise ValueError("head_dim must be 128")
         p = {k: v.to(device) for k, v in state.items()}
         if parts is None:
-            parts = quantize_block(p, scale_dtype)
+            parts = quantize_block(p, scale_dtype, rank=svd_rank)
         self.parts = parts
         self.layers = {name: w4a4.PreparedW4A4(*(t[k] for k in w4a4.PARTS), code_format=code_format)
                        for name, t in parts.items()}
