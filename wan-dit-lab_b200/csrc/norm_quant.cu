@@ -275,30 +275,32 @@ void ln_quant_launch(const LnQuantArgs& a, cudaStream_t s) {
 // Same thread layout as ln_quant: one CTA of 128 threads per row.
 // sumsq (nullable): the sum of squares of each row over all norm_dim channels, when this call holds only a slice
 // of them (a tensor-parallel shard: the slices' sums added across shards); else the row's own sum over K = norm_dim.
-__global__ void __launch_bounds__(kRowThreads, 8) rms_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
-                                                               int K, const float* __restrict__ w, float eps,
-                                                               const float* __restrict__ sumsq, int norm_dim,
-                                                               float* __restrict__ out, int64_t ldo) {
-  __shared__ float red[kRowThreads / 32];
+// kThreads threads a row, kChunks chunks of kThreads * 8 channels; K <= 3072 runs 384 threads, one chunk each.
+template <int kThreads = kRowThreads, int kChunks = kRowChunks>
+__global__ void __launch_bounds__(kThreads, kThreads == kRowThreads ? 8 : 4)
+    rms_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int K, const float* __restrict__ w, float eps,
+                    const float* __restrict__ sumsq, int norm_dim, float* __restrict__ out, int64_t ldo) {
+  constexpr int kStride = kThreads * 8;
+  __shared__ float red[kThreads / 32];
   const int t = threadIdx.x, m = blockIdx.x;
   const __nv_bfloat16* row = x + static_cast<int64_t>(m) * ldx;
-  float v[kRowChunks][8];
+  float v[kChunks][8];
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < kRowChunks; ++c) {
-    const int k = c * 1024 + t * 8;
+  for (int c = 0; c < kChunks; ++c) {
+    const int k = c * kStride + t * 8;
     if (k < K) {
       load8<__nv_bfloat16>(row + k, v[c]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss = fmaf(v[c][i], v[c][i], ss);
     }
   }
-  const float total = block_sum128(ss, red);
+  const float total = block_sum<kThreads / 32>(ss, red);
   const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(sumsq ? __ldg(sumsq + m) : total, static_cast<float>(norm_dim)), eps));
   float* o = out + static_cast<int64_t>(m) * ldo;
 #pragma unroll
-  for (int c = 0; c < kRowChunks; ++c) {
-    const int k = c * 1024 + t * 8;
+  for (int c = 0; c < kChunks; ++c) {
+    const int k = c * kStride + t * 8;
     if (k < K) {
       float wk[8], y[8];
       load8<float>(w + k, wk);
@@ -313,7 +315,8 @@ __global__ void __launch_bounds__(kRowThreads, 8) rms_rows_kernel(const __nv_bfl
 void rms_rows_launch(const __nv_bfloat16* x, int64_t ldx, int M, int K, const float* w, float eps, const float* sumsq,
                      int norm_dim, float* out, int64_t ldo, cudaStream_t s) {
   if (M == 0) return;
-  rms_rows_kernel<<<M, kRowThreads, 0, s>>>(x, ldx, K, w, eps, sumsq, norm_dim, out, ldo);
+  if (K <= 3072) rms_rows_kernel<384, 1><<<M, 384, 0, s>>>(x, ldx, K, w, eps, sumsq, norm_dim, out, ldo);
+  else rms_rows_kernel<><<<M, kRowThreads, 0, s>>>(x, ldx, K, w, eps, sumsq, norm_dim, out, ldo);
 }
 
 // Sums of squares of `parts` slices of K channels of each bf16 row (slice p starts at channel p * part_stride):
