@@ -30,6 +30,7 @@ is imported, unmodified, from baseline/_ref (baseline/install_reference.sh).
 """
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -251,7 +252,7 @@ def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True, 
     text = torch.randn(1, 512, 4096, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
     stream = causal.Stream(model, text.to(device), height, width,
                            torch.Generator(device=device).manual_seed(10 + seed_rank), vae_stride=16,
-                           cuda_graph=graphs and tp is None)  # passes replayed from CUDA graphs
+                           cuda_graph=graphs)  # passes replayed from CUDA graphs (a split's all-reduces with them)
     noise_d = noise.to(device)
     out = torch.empty_like(noise_d)
 
@@ -302,7 +303,7 @@ def rollout_workload(device, rank=0, chunks=7, layers=30, tp=None, graphs=True, 
                                  f"SVD rank {svd_rank})",
                         "tokens_per_chunk": tokens, "keys_per_chunk": [min(tokens * (c + 1), window) for c in range(chunks)],
                         "chunks": chunks, "layers": layers, **({} if tp is None else {"tensor_parallel": world}),
-                        "cuda_graphs": bool(graphs and tp is None),
+                        "cuda_graphs": bool(graphs),
                         "codes": CODES, "l2": "inputs larger than L2 (5 GB of weights per pass)"},
                 algorithmic={"gemm_int_ops_per_block_pass": per_block, "gemm_launches_per_block_pass": 6},
                 cpu=lambda: cpu_block_sample(tokens=tokens, grid=(3, lat_h // 2, lat_w // 2)), dtype="W4A4 (int4 x int4 exact on int8 tensor cores) + INT8/FP8 Sage "
@@ -595,6 +596,9 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
+        wl.clear()  # the passes' CUDA graphs (a split's hold NCCL calls) released before the process group
+        gc.collect()
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -1,7 +1,8 @@
 """The tensor-parallel block across GPUs: one process per GPU, NCCL all-reduce as the reduce callable
 (WanBlockTP.forward). Every rank ends with the same residual stream, equal bit for bit to what the shards give in
 lock step on one GPU (the same sums: NCCL adds two ranks' values in one order) and within relative L2 1e-3 of the
-whole block's update. Needs two GPUs; skipped otherwise."""
+whole block's update; the same forward captured in a CUDA graph (its all-reduces with it, as the rollout's passes
+are) and replayed gives the eager result bit for bit. Needs two GPUs; skipped otherwise."""
 
 import datetime
 import os
@@ -68,10 +69,23 @@ def _rank(rank, world, port, out):
         hl = heads // world
         c = [t[:, rank * hl:(rank + 1) * hl].contiguous().to(dev) for t in cache]
         Xd = X.to(dev)
-        blk.forward(Xd, blk.modulation_of(time_in.to(dev)), (*c, cap), at, freq.to(dev), (frames, h, w),
-                    at // (h * w), blk.cross_kv(ctx.to(dev)), blk.buffers(n, at + n, text, dev))
+        args = (blk.modulation_of(time_in.to(dev)), (*c, cap), at, freq.to(dev), (frames, h, w), at // (h * w),
+                blk.cross_kv(ctx.to(dev)), blk.buffers(n, at + n, text, dev))
+        blk.forward(Xd, *args)
         torch.cuda.synchronize()
-        out[rank] = (Xd.cpu().numpy(), _native.device_error())
+        # the same pass captured with its all-reduces (every rank captures and replays the same collectives in the
+        # same order) and replayed from the same input: it writes the same cache rows with the same values
+        Xg = X.to(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            blk.forward(Xg, *args)
+        Xg.copy_(X.to(dev))
+        graph.replay()
+        torch.cuda.synchronize()
+        replay_equal = bool(torch.equal(Xg, Xd))
+        del graph  # released before the process group (it holds NCCL calls)
+        torch.cuda.synchronize()
+        out[rank] = (Xd.cpu().numpy(), _native.device_error(), replay_equal)
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -84,9 +98,10 @@ def test_tp_block_over_nccl_matches_lockstep_and_whole_block():
     world, port = 2, free_port()
     out = mp.get_context("spawn").Manager().dict()
     mp.spawn(_rank, args=(world, port, out), nprocs=world, join=True)
-    x0, err0 = out[0]
-    x1, err1 = out[1]
+    x0, err0, replay0 = out[0]
+    x1, err1, replay1 = out[1]
     assert err0 == 0 and err1 == 0
+    assert replay0 and replay1  # graph replay with the all-reduces captured equals the eager pass
     np.testing.assert_array_equal(x0, x1)
     # the same split in lock step on this GPU, and the whole block
     dim, heads, ffn, frames, h, w, at, text = CASE
