@@ -9,6 +9,10 @@
  *
  * Dtype codes: WDL_BF16 = 0, WDL_F16 = 1, WDL_F32 = 2.
  *
+ * The W4A4 GEMM entry points (wdl_w4a4_gemm*, wdl_w4a4_linear*) take their bias 16-byte aligned, like every
+ * other pointer they take, and row strides (ldy, ldo, ldr, ldc, ld_add, ld_gelu, wdl_lowrank.ld_act) below 2^31
+ * elements; other values return WDL_ERR_ARGUMENT.
+ *
  * Each declaration names the reference interface it replaces, by file:line of the wan-dit-lab repository.
  */
 #ifndef WDL_B200_H

@@ -207,3 +207,12 @@ def test_row_parallel_partials_all_reduced_over_gloo():
     for name in ("self_attn.o", "cross_attn.o"):
         assert out[0][name + ".rel"] <= 1e-6
         np.testing.assert_array_equal(out[0][name], out[1][name])  # every rank holds the same sums
+
+
+def test_random_model_refuses_lowrank_branches_on_shards():
+    """svd_rank applies to one stream per GPU: with a tensor-parallel shard the model refuses it before making
+    anything (the split's blocks quantize at rank 0)."""
+    import pytest
+    from wan_dit_lab_b200.generation.causal import random_model
+    with pytest.raises(ValueError, match="svd_rank"):
+        random_model(num_layers=1, device="cpu", shard=(0, 2), svd_rank=32)
