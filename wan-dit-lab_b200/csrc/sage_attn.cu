@@ -250,21 +250,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
           tmem_ld32(t_row, s);
           tmem_ld32(t_row + 32, s_hi);
           tmem_ld_wait();
-          if constexpr (!kMasked) {
-            // group g holds columns 8 k + 2 g and 8 k + 2 g + 1: two scores a three-input max
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              const int g = (i % 8) / 2;
-              gmax[g] = __vimax3_s32(gmax[g], static_cast<int32_t>(s[i]), static_cast<int32_t>(s[i + 1]));
-              gmax[g] = __vimax3_s32(gmax[g], static_cast<int32_t>(s_hi[i]), static_cast<int32_t>(s_hi[i + 1]));
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int g = (i % 8) / 2;
-              if (i < lim) gmax[g] = max(gmax[g], static_cast<int32_t>(s[i]));
-              if (32 + i < lim) gmax[g] = max(gmax[g], static_cast<int32_t>(s_hi[i]));
-            }
+          for (int i = 0; i < 32; ++i) {
+            const int g = (i % 8) / 2;
+            if (!kMasked || i < lim) gmax[g] = max(gmax[g], static_cast<int32_t>(s[i]));
+            if (!kMasked || 32 + i < lim) gmax[g] = max(gmax[g], static_cast<int32_t>(s_hi[i]));
           }
         }
         float mx = -INFINITY;
